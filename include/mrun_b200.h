@@ -1,0 +1,155 @@
+/*
+ * mrun-b200 C ABI: the drop-in boundary for mrun's quantized decode hot path.
+ *
+ * Every function is `extern "C"`, takes plain device pointers, element counts and a
+ * `void *stream` (a cudaStream_t, or NULL for the legacy default stream), enqueues its
+ * kernels on that stream without synchronising, and returns an int status:
+ *
+ *   MRB_OK (0)            success
+ *   MRB_ERR_ARG (1)       an argument failed validation (the Python mirror raises ValueError)
+ *   MRB_ERR_CUDA (2)      a CUDA launch or runtime call failed (RuntimeError)
+ *   MRB_ERR_UNSUPPORTED (3) a valid request outside this build's kernels (RuntimeError)
+ *
+ * mrb_last_error() returns the message of the last failing call on the calling thread.
+ * Layouts follow the reference QStore: a "qrow" matrix is int8 codes [rows, cols] row-major
+ * with one fp32 scale per row (weight = code * scale), exactly as written by
+ * `_quant_row_int8` (mrun engine/kernels/qstore_build.py:496-501).
+ *
+ * The reference is pure Python; the ctypes binding a maintainer would add on its side is
+ * shown in INTEGRATION.md. Each entry point names the reference function it replaces.
+ */
+#ifndef MRUN_B200_H
+#define MRUN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MRB_OK = 0,
+  MRB_ERR_ARG = 1,
+  MRB_ERR_CUDA = 2,
+  MRB_ERR_UNSUPPORTED = 3,
+};
+
+/* Element types of activation/output buffers. */
+enum {
+  MRB_F32 = 0,
+  MRB_BF16 = 1,
+  MRB_F16 = 2,
+};
+
+/* ---------------------------------------------------------------- library */
+
+/* ABI revision of this header; bumps on any signature change. */
+int mrb_abi_version(void);
+
+/* Message for the last non-zero status returned on this host thread ("" if none). */
+const char *mrb_last_error(void);
+
+/* ---------------------------------------------------------------- (a) QStore int8 linear */
+
+/* Per-output-channel symmetric int8 quantisation of an fp32 [rows, cols] matrix:
+ * scale = max|w_row| / 127 (1 for an all-zero row), code = round_half_even(w / scale)
+ * clipped to [-127, 127].
+ * Replaces `_quant_row_int8` (engine/kernels/qstore_build.py:496-501). */
+int mrb_quant_row_int8(const float *weight, int64_t rows, int64_t cols, int8_t *codes,
+                       float *scales, void *stream);
+
+/* Dequantised row gather: out[i, :] = codes[ids[i], :] * scales[ids[i]] in fp32, stored
+ * as out_dtype. ids outside [0, rows) produce a zero row and set *bad_ids (device int32,
+ * may be NULL) to 1.
+ * Replaces `QStore.embed_rows` (engine/kernels/qstore.py:1099-1128). */
+int mrb_qrow_embed_rows(const int8_t *codes, const float *scales, int64_t rows, int64_t cols,
+                        const int64_t *ids, int64_t n_ids, void *out, int out_dtype,
+                        int32_t *bad_ids, void *stream);
+
+/* y[m, n] = sum_k x[m, k] * codes[n, k] * scales[n] (+ bias[n]), fp32 accumulation.
+ * x_dtype in {F32, BF16, F16}; y_dtype = x_dtype (the reference returns x's dtype).
+ * bias (fp32 [n], may be NULL) is added after rounding to y's dtype, as the reference adds
+ * a compute-dtype bias to the projection output.
+ * Requires k % 16 == 0 and 16-byte aligned codes.
+ * Replaces `fused_qrow_matmul` (engine/kernels/dense_qstore_cuda.py:1105-1152) for
+ * bf16/fp16 rows and `QStore.matmul` (engine/kernels/qstore.py:1082-1092) for fp32 rows. */
+int mrb_qrow_matmul(const void *x, int x_dtype, int64_t m, int64_t k, const int8_t *codes,
+                    const float *scales, int64_t n, const float *bias, void *y, int y_dtype,
+                    void *stream);
+
+/* Paired gate/up W8A16 projection with the reference's BF16 SwiGLU boundaries:
+ * g = bf16(x.Wg), u = bf16(x.Wu), s = bf16(g * sigmoid(g)), y = bf16(s * u).
+ * Replaces `fused_qrow_swiglu` (engine/kernels/dense_qstore_cuda.py:1052-1102). */
+int mrb_qrow_swiglu(const void *x_bf16, int64_t m, int64_t k, const int8_t *gate_codes,
+                    const float *gate_scales, const int8_t *up_codes, const float *up_scales,
+                    int64_t n, void *y_bf16, void *stream);
+
+/* Greedy language head: logits[m, v] = x[m].W[v] * scale[v] in fp32 over the first
+ * `semantic_rows` rows, then the first maximal index per row (lowest index on ties).
+ * out_index: int64 [m]; out_value: fp32 [m] (may be NULL); logits: fp32 [m, n] workspace
+ * that also receives the full logits (n = all rows).
+ * Replaces the streamed exact head `_head` (engine/dense_qstore_cuda.py:800-896). */
+int mrb_qrow_argmax(const void *x, int x_dtype, int64_t m, int64_t k, const int8_t *codes,
+                    const float *scales, int64_t n, int64_t semantic_rows, float *logits,
+                    int64_t *out_index, float *out_value, void *stream);
+
+/* Row RMSNorm in fp32: y = x * rsqrt(mean(x^2) + eps) * w, stored in x's dtype.
+ * Replaces `stable_rms_norm` (engine/kernels/dense_qstore_cuda.py:1473-1511). */
+int mrb_rms_norm(const void *x, int dtype, int64_t rows, int64_t width, const float *weight,
+                 float eps, void *y, void *stream);
+
+/* r = bf16(residual + update); normed = bf16(RMSNorm(r) * w).
+ * Replaces `fused_residual_rms_norm` (engine/kernels/dense_qstore_cuda.py:1411-1459). */
+int mrb_residual_rms_norm(const void *residual_bf16, const void *update_bf16, int64_t rows,
+                          int64_t width, const float *weight, float eps, void *residual_out,
+                          void *normed_out, void *stream);
+
+
+/* ---------------------------------------------------------------- (c) paged-KV decode attention */
+
+/* RoPE (rotate-half, fp32 products rounded separately, then bf16) for the queries and keys of
+ * `tokens` new positions, and the K/V append into a paged cache.
+ * Token t reads q/k/v rows at q_in/k_in/v_in + t * in_row_stride (bf16 elements), sits at
+ * absolute position positions[t] of block-table row token_rows[t] (NULL: row 0), and is
+ * written to page block_table[row * block_table_stride + pos / page_size], slot
+ * pos % page_size, of K/V caches addressed as page*stride_page + head*stride_head +
+ * slot*stride_tok + d. rope_cos/rope_sin: fp32 [rope_len, head_dim/2] tables (NULL: no
+ * rotation, a plain scatter). q_out: bf16 [tokens, hq, head_dim] rotated queries (may be
+ * NULL). Invalid positions/pages are skipped and set *error_flag (device int32, may be NULL).
+ * Replaces `_rope` (engine/dense_qstore_cuda.py:689-704) and `scatter_segmented_decode_kv`
+ * (engine/kernels/segmented_gqa_decode.py:458-524). */
+int mrb_rope_kv_append(const void *q_in, const void *k_in, const void *v_in, int64_t in_row_stride,
+                       int64_t tokens, int64_t hq, int64_t hkv, int64_t head_dim,
+                       const int32_t *positions, const int32_t *token_rows, const float *rope_cos,
+                       const float *rope_sin, int64_t rope_len, void *q_out, void *k_cache,
+                       void *v_cache, int64_t stride_page, int64_t stride_head, int64_t stride_tok,
+                       int64_t page_size, const int32_t *block_table, int64_t block_table_stride,
+                       int64_t num_pages, int32_t *error_flag, void *stream);
+
+/* Workspace bytes mrb_paged_attention needs for these sizes (0 when no split is used). */
+size_t mrb_paged_attention_workspace(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
+                                     int64_t max_total_tokens);
+
+/* One-token grouped-query attention per query row over a paged KV cache, split-K over
+ * 16-token tiles with a deterministic merge. q/out: bf16 [rows, hq, head_dim]; row r attends
+ * to tokens [0, row_len[r]) of block-table row row_seq[r] (NULL: r), plus, when k_new/v_new
+ * (bf16 [rows, hkv, head_dim]) are given, one provisional token at position row_len[r].
+ * max_total_tokens bounds row_len (+1 with k_new) and fixes the split plan. The workspace
+ * (mrb_paged_attention_workspace bytes) must be zero-filled before its first use; calls
+ * leave it ready for the next call. head_dim in {64, 128}; hq / hkv <= 16.
+ * Replaces `segmented_decode_attention` (engine/kernels/dense_qstore_cuda.py:1763-1854) and
+ * `segmented_gqa_decode` (engine/kernels/segmented_gqa_decode.py:526-607). */
+int mrb_paged_attention(const void *q, int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
+                        const void *k_cache, const void *v_cache, int64_t stride_page,
+                        int64_t stride_head, int64_t stride_tok, int64_t page_size,
+                        const int32_t *block_table, int64_t block_table_stride,
+                        const int32_t *row_seq, const int32_t *row_len, const void *k_new,
+                        const void *v_new, float scale, int64_t max_total_tokens, void *out,
+                        void *workspace, size_t workspace_size, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MRUN_B200_H */

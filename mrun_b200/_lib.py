@@ -1,0 +1,150 @@
+"""ctypes binding of the in-tree CUDA library ``libmrun_b200.so`` (the C ABI boundary).
+
+Loading is strict: if the library is missing or lacks a declared symbol, importing any
+operator raises instead of falling back to another implementation. Status codes follow
+``include/mrun_b200.h``: argument errors raise ``ValueError`` (the reference's validation
+errors), CUDA and unsupported-shape errors raise ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from ctypes import c_float, c_int, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+import torch
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "libmrun_b200.so"
+
+MRB_OK = 0
+MRB_ERR_ARG = 1
+MRB_ERR_CUDA = 2
+MRB_ERR_UNSUPPORTED = 3
+
+MRB_F32 = 0
+MRB_BF16 = 1
+MRB_F16 = 2
+
+_P = c_void_p
+_I64 = c_int64
+
+# name -> argtypes (all functions return int unless listed in _RESTYPES)
+SIGNATURES: dict[str, list] = {
+    "mrb_abi_version": [],
+    "mrb_last_error": [],
+    "mrb_quant_row_int8": [_P, _I64, _I64, _P, _P, _P],
+    "mrb_qrow_embed_rows": [_P, _P, _I64, _I64, _P, _I64, _P, c_int, _P, _P],
+    "mrb_qrow_matmul": [_P, c_int, _I64, _I64, _P, _P, _I64, _P, _P, c_int, _P],
+    "mrb_qrow_swiglu": [_P, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P],
+    "mrb_qrow_argmax": [_P, c_int, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P, _P],
+    "mrb_rms_norm": [_P, c_int, _I64, _I64, _P, c_float, _P, _P],
+    "mrb_residual_rms_norm": [_P, _P, _I64, _I64, _P, c_float, _P, _P, _P],
+    "mrb_rope_kv_append": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P, _P,
+                           _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P],
+    "mrb_paged_attention_workspace": [_I64, _I64, _I64, _I64, _I64],
+    "mrb_paged_attention": [_P, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P,
+                            _P, _P, c_float, _I64, _P, _P, c_size_t, _P],
+}
+_RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class MrbError(RuntimeError):
+    """A CUDA or unsupported-shape failure reported by the native library."""
+
+
+def load() -> ctypes.CDLL:
+    """Load the native library once; raise if it is absent (no fallback path exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIBRARY_PATH.exists():
+            raise ImportError(
+                f"mrun_b200 native library not built: {LIBRARY_PATH} is missing "
+                "(run `python -c 'import __graft_entry__ as g; g.build()'`)"
+            )
+        lib = ctypes.CDLL(str(LIBRARY_PATH))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)  # AttributeError if a declared symbol is missing
+            fn.argtypes = argtypes
+            fn.restype = _RESTYPES.get(name, c_int)
+        _lib = lib
+        return lib
+
+
+def check(status: int, what: str) -> None:
+    if status == MRB_OK:
+        return
+    message = load().mrb_last_error().decode("utf-8", "replace")
+    text = f"{what}: {message}" if message else f"{what}: status {status}"
+    if status == MRB_ERR_ARG:
+        raise ValueError(text)
+    raise MrbError(text)
+
+
+def call(name: str, *args) -> None:
+    """Invoke a C-ABI entry point and raise on a non-zero status."""
+    check(getattr(load(), name)(*args), name)
+
+
+def ptr(tensor: torch.Tensor | None) -> int | None:
+    return None if tensor is None else tensor.data_ptr()
+
+
+def stream_handle(device: torch.device | None = None) -> int:
+    """Raw cudaStream_t of torch's current stream on ``device``."""
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype is torch.float32:
+        return MRB_F32
+    if dtype is torch.bfloat16:
+        return MRB_BF16
+    if dtype is torch.float16:
+        return MRB_F16
+    raise ValueError(f"unsupported activation dtype {dtype}")
+
+
+def require_cuda(*tensors: torch.Tensor, what: str) -> torch.device:
+    """Every hot-path operator runs on CUDA only; CPU tensors are a caller error."""
+    device = None
+    for tensor in tensors:
+        if tensor is None:
+            continue
+        if tensor.device.type != "cuda":
+            raise RuntimeError(f"{what} requires CUDA tensors (got {tensor.device}); there is no CPU path")
+        if device is None:
+            device = tensor.device
+        elif tensor.device != device:
+            raise ValueError(f"{what}: tensors must share one device")
+    if device is None:
+        raise ValueError(f"{what}: no tensor given")
+    return device
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+__all__ = [
+    "LIBRARY_PATH",
+    "MRB_BF16",
+    "MRB_F16",
+    "MRB_F32",
+    "MrbError",
+    "c_size_t",
+    "call",
+    "check",
+    "dtype_code",
+    "exported_symbols",
+    "load",
+    "ptr",
+    "require_cuda",
+    "stream_handle",
+]

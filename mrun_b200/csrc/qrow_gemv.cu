@@ -1,0 +1,496 @@
+// Decode-size W8A16 projection: an HBM-bound int8 GEMV on the tensor pipe.
+//
+// y[m, n] = scale[n] * sum_k x[m, k] * code[n, k] for m <= 16 rows of activations.
+//
+// Design (B200, sm_100a):
+//  * Weights stream once from HBM with 128-bit L1-bypassing loads. A CTA (8 warps) owns a
+//    16-row weight tile; its warps split K in 64-byte blocks, interleaved so the CTA reads
+//    each row as one contiguous stream, and reduce the partial sums through shared memory
+//    in a fixed order (deterministic).
+//  * Dequantisation is exact and costs ~1.25 integer/half instructions per weight byte:
+//    int8 -> biased byte -> f16 (0x6400 | byte) - 1152 gives the code as an exact f16.
+//  * The dot product runs on mma.sync m16n8k16 (f16 x f16 -> f32). Activations are staged
+//    once per CTA in shared memory as f16 scaled by a per-row power of two so every bf16
+//    value is represented exactly (8 significant bits fit f16's 11); fp32 activations are
+//    split into hi + lo f16 halves (22 significant bits) occupying two mma columns.
+//    Products are therefore exact and accumulate in fp32, the contract of the reference's
+//    `tl.dot(..., fp32 acc)`; the row scale is applied once in fp32 after the reduction.
+//  * The k order inside each 64-element block is permuted identically for weights and
+//    activations (each lane consumes 4 consecutive bytes per mma), so every lane issues one
+//    16-byte load per weight row per block and no shuffles are needed.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace mrb {
+
+constexpr int GV_WARPS = 8;
+constexpr int GV_THREADS = GV_WARPS * 32;
+constexpr int GV_ROWS = 16;   // weight rows per CTA tile (mma M)
+constexpr int GV_KB = 64;     // k elements per lane-group block
+constexpr int GV_UNROLL = 4;  // k blocks in flight per warp
+
+enum { EPI_STORE = 0, EPI_SWIGLU = 1 };
+
+struct GemvArgs {
+  const void* x;
+  int64_t m;
+  int64_t k;
+  const int8_t* codes0;
+  const float* scales0;
+  const int8_t* codes1;  // up projection for EPI_SWIGLU
+  const float* scales1;
+  const float* bias;
+  int64_t n;
+  void* y;
+};
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Four signed int8 codes -> f16x2 of bytes (0,1) and f16x2 of bytes (2,3), exactly.
+__device__ __forceinline__ void i8x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;  // q + 128 as an unsigned byte
+  lo = hsub2(prmt(u, 0x64646464u, 0x4140u), 0x64806480u);  // (1024 + q + 128) - 1152
+  hi = hsub2(prmt(u, 0x64646464u, 0x4342u), 0x64806480u);
+}
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// SiLU as the reference writes it: g * sigmoid(g), sigmoid = 1 / (1 + exp(-g)).
+__device__ __forceinline__ float silu_f32(float g) { return g * (1.0f / (1.0f + expf(-g))); }
+
+// Shared-memory plan of one CTA.
+__host__ __device__ inline int gv_kpad(int64_t k) { return (int)(((k + GV_KB - 1) / GV_KB) * GV_KB); }
+__host__ __device__ inline int gv_xstride(int64_t k) { return gv_kpad(k) + 8; }  // f16 elems, +16 B
+__host__ inline size_t gv_smem_bytes(int ncols, int64_t k, int nt, int nstream) {
+  size_t xs = (size_t)ncols * gv_xstride(k) * 2;
+  xs = (xs + 15) & ~size_t(15);
+  size_t red = (size_t)GV_WARPS * nstream * GV_ROWS * 8 * nt * 4;
+  return xs + red + 64 * 4;  // + per-row power-of-two factors and row maxima
+}
+
+// XT: activation element type. SPLIT: fp32 activations as hi/lo f16 pairs.
+// NT: number of n8 mma column tiles (columns = 8 * NT >= rows * (SPLIT ? 2 : 1)).
+template <typename XT, typename YT, bool SPLIT, int NT, int EPI>
+__global__ void __launch_bounds__(GV_THREADS, 2) qrow_gemv_kernel(GemvArgs a) {
+  constexpr int NSTREAM = (EPI == EPI_SWIGLU) ? 2 : 1;
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int M = (int)a.m;
+  const int64_t K = a.k;
+  const int ncols = SPLIT ? 2 * M : M;
+  const int kpad = gv_kpad(K);
+  const int xstride = gv_xstride(K);
+  const int nkb = kpad / GV_KB;
+  __half* xs = reinterpret_cast<__half*>(smem);
+  size_t xs_bytes = ((size_t)ncols * xstride * 2 + 15) & ~size_t(15);
+  float* red = reinterpret_cast<float*>(smem + xs_bytes);
+  float* colscale = red + GV_WARPS * NSTREAM * GV_ROWS * 8 * NT;  // 2^-e per activation row
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int g = lane >> 2;  // mma group id: weight row (and +8), activation column
+  const int c = lane & 3;   // thread in group: 16-element slice of a 64-element k block
+
+  // ---- stage activations: per-row power-of-two scale, exact f16 (or hi/lo f16) copy.
+  // Two fully parallel passes of 16-byte vector loads (the second hits L1).
+  constexpr int VEC = 16 / sizeof(XT);  // elements per 16-byte vector
+  unsigned* colmax = reinterpret_cast<unsigned*>(colscale + 32);
+  if (tid < 16) colmax[tid] = 0u;
+  __syncthreads();
+  const int vpr = (int)(K / VEC);  // vectors per activation row (K % 16 == 0)
+  const int nvec = M * vpr;
+  const uint4* xv = reinterpret_cast<const uint4*>(a.x);
+  {
+    int cur = -1;
+    float mx = 0.f;
+    for (int v = tid; v < nvec; v += GV_THREADS) {
+      const int mi = v / vpr;
+      if (mi != cur) {
+        if (cur >= 0) atomicMax(&colmax[cur], __float_as_uint(mx));
+        cur = mi;
+        mx = 0.f;
+      }
+      const uint4 raw = __ldg(xv + v);
+      const XT* e = reinterpret_cast<const XT*>(&raw);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) mx = fmaxf(mx, fabsf(io<XT>::load(e + i)));
+    }
+    if (cur >= 0) atomicMax(&colmax[cur], __float_as_uint(mx));
+  }
+  __syncthreads();
+  if (tid < M) {
+    const float mx = __uint_as_float(colmax[tid]);
+    int e = 0;
+    if (mx > 0.f && isfinite(mx)) {
+      int ex;
+      frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
+      e = max(-100, min(100, 15 - ex));  // mx * 2^e in [2^14, 2^15)
+    }
+    colscale[tid] = ldexpf(1.0f, -e);
+    colscale[16 + tid] = ldexpf(1.0f, e);
+  }
+  __syncthreads();
+  for (int v = tid; v < nvec; v += GV_THREADS) {
+    const int mi = v / vpr;
+    const int kk = (v - mi * vpr) * VEC;
+    const uint4 raw = __ldg(xv + v);
+    const XT* e = reinterpret_cast<const XT*>(&raw);
+    const float f = colscale[16 + mi];
+    if (SPLIT) {
+      __half hi[VEC], lo[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const float val = io<XT>::load(e + i) * f;  // exact power-of-two scaling
+        hi[i] = __float2half_rn(val);
+        lo[i] = __float2half_rn((val - __half2float(hi[i])) * 2048.0f);
+      }
+      *reinterpret_cast<uint2*>(xs + (2 * mi) * xstride + kk) = *reinterpret_cast<const uint2*>(hi);
+      *reinterpret_cast<uint2*>(xs + (2 * mi + 1) * xstride + kk) = *reinterpret_cast<const uint2*>(lo);
+    } else {
+      __align__(16) __half h[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) h[i] = __float2half_rn(io<XT>::load(e + i) * f);
+      *reinterpret_cast<uint4*>(xs + mi * xstride + kk) = *reinterpret_cast<const uint4*>(h);
+    }
+  }
+  // zero padding up to the 64-element block boundary
+  const int padw = kpad - (int)K;
+  for (int idx = tid; idx < ncols * padw; idx += GV_THREADS) {
+    const int col = idx / padw;
+    xs[col * xstride + (int)K + (idx - col * padw)] = __float2half_rn(0.f);
+  }
+  __syncthreads();
+
+  const int64_t n = a.n;
+  const int64_t ntiles = (n + GV_ROWS - 1) / GV_ROWS;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int64_t r0 = min(tile * GV_ROWS + g, n - 1);
+    const int64_t r1 = min(tile * GV_ROWS + g + 8, n - 1);
+    const int8_t* w00 = a.codes0 + r0 * K + 16 * c;
+    const int8_t* w01 = a.codes0 + r1 * K + 16 * c;
+    const int8_t* w10 = nullptr;
+    const int8_t* w11 = nullptr;
+    if (EPI == EPI_SWIGLU) {
+      w10 = a.codes1 + r0 * K + 16 * c;
+      w11 = a.codes1 + r1 * K + 16 * c;
+    }
+    float acc[NSTREAM][NT][4];
+#pragma unroll
+    for (int s = 0; s < NSTREAM; ++s)
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[s][t][i] = 0.f;
+
+    for (int kb0 = warp; kb0 < nkb; kb0 += GV_WARPS * GV_UNROLL) {
+      uint4 wa[GV_UNROLL][NSTREAM], wb[GV_UNROLL][NSTREAM];
+#pragma unroll
+      for (int u = 0; u < GV_UNROLL; ++u) {
+        const int kb = kb0 + u * GV_WARPS;
+        const int64_t koff = (int64_t)kb * GV_KB;
+        const bool ok = kb < nkb && koff + 16 * c < K;
+#pragma unroll
+        for (int s = 0; s < NSTREAM; ++s) {
+          const int8_t* pa = s == 0 ? w00 : w10;
+          const int8_t* pb = s == 0 ? w01 : w11;
+          wa[u][s] = ok ? ld_stream_u4(pa + koff) : make_uint4(0, 0, 0, 0);
+          wb[u][s] = ok ? ld_stream_u4(pb + koff) : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < GV_UNROLL; ++u) {
+        const int kb = kb0 + u * GV_WARPS;
+        if (kb >= nkb) break;  // warp-uniform
+        uint32_t xb[NT][8];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const int col = t * 8 + g;
+          if (col < ncols) {
+            const uint4* p = reinterpret_cast<const uint4*>(xs + col * xstride + kb * GV_KB + 16 * c);
+            const uint4 v0 = p[0], v1 = p[1];
+            xb[t][0] = v0.x; xb[t][1] = v0.y; xb[t][2] = v0.z; xb[t][3] = v0.w;
+            xb[t][4] = v1.x; xb[t][5] = v1.y; xb[t][6] = v1.z; xb[t][7] = v1.w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) xb[t][i] = 0u;
+          }
+        }
+#pragma unroll
+        for (int s = 0; s < NSTREAM; ++s) {
+          const uint32_t ra[4] = {wa[u][s].x, wa[u][s].y, wa[u][s].z, wa[u][s].w};
+          const uint32_t rb[4] = {wb[u][s].x, wb[u][s].y, wb[u][s].z, wb[u][s].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t a_lo, a_hi, b_lo, b_hi;
+            i8x4_to_f16x2(ra[j], a_lo, a_hi);
+            i8x4_to_f16x2(rb[j], b_lo, b_hi);
+#pragma unroll
+            for (int t = 0; t < NT; ++t) mma_f16(acc[s][t], a_lo, b_lo, a_hi, b_hi, xb[t][2 * j], xb[t][2 * j + 1]);
+          }
+        }
+      }
+    }
+
+    // ---- cross-warp reduction in a fixed order.
+#pragma unroll
+    for (int s = 0; s < NSTREAM; ++s)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        float* base = red + ((warp * NSTREAM + s) * GV_ROWS) * (8 * NT);
+        const int col = t * 8 + 2 * c;
+        base[g * (8 * NT) + col] = acc[s][t][0];
+        base[g * (8 * NT) + col + 1] = acc[s][t][1];
+        base[(g + 8) * (8 * NT) + col] = acc[s][t][2];
+        base[(g + 8) * (8 * NT) + col + 1] = acc[s][t][3];
+      }
+    __syncthreads();
+    for (int idx = tid; idx < GV_ROWS * M; idx += GV_THREADS) {
+      const int row = idx % GV_ROWS;
+      const int mi = idx / GV_ROWS;
+      const int64_t nrow = tile * GV_ROWS + row;
+      if (nrow < n) {
+        float v[NSTREAM];
+#pragma unroll
+        for (int s = 0; s < NSTREAM; ++s) {
+          float hi = 0.f, lo = 0.f;
+#pragma unroll
+          for (int w = 0; w < GV_WARPS; ++w) {
+            const float* base = red + ((w * NSTREAM + s) * GV_ROWS + row) * (8 * NT);
+            if (SPLIT) {
+              hi += base[2 * mi];
+              lo += base[2 * mi + 1];
+            } else {
+              hi += base[mi];
+            }
+          }
+          const float tot = SPLIT ? hi + lo * (1.0f / 2048.0f) : hi;
+          const float* sc = s == 0 ? a.scales0 : a.scales1;
+          v[s] = tot * colscale[mi] * sc[nrow];
+        }
+        YT* y = reinterpret_cast<YT*>(a.y) + (int64_t)mi * n + nrow;
+        if (EPI == EPI_SWIGLU) {
+          const float gt = round_bf16(v[0]);
+          const float up = round_bf16(v[NSTREAM - 1]);
+          const float sl = round_bf16(silu_f32(gt));
+          io<YT>::store(y, sl * up);
+        } else {
+          float out = v[0];
+          if (a.bias) {
+            // The reference adds a compute-dtype bias to the compute-dtype projection.
+            YT tmp;
+            io<YT>::store(&tmp, out);
+            YT b;
+            io<YT>::store(&b, a.bias[nrow]);
+            out = io<YT>::load(&tmp) + io<YT>::load(&b);
+          }
+          io<YT>::store(y, out);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ argmax over logits
+
+// First maximal index per row over the first `semantic` columns (lowest index on ties).
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ logits, int64_t n,
+                                                           int64_t semantic, int64_t* __restrict__ out_index,
+                                                           float* __restrict__ out_value) {
+  const int64_t row = blockIdx.x;
+  const float* p = logits + row * n;
+  float best = -INFINITY;
+  int64_t bi = 0x7fffffffffffffffLL;
+  for (int64_t i = threadIdx.x; i < semantic; i += blockDim.x) {
+    const float v = p[i];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int64_t si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sv[w] = best;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int nw = blockDim.x >> 5;
+    best = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
+    bi = threadIdx.x < nw ? si[threadIdx.x] : 0x7fffffffffffffffLL;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (threadIdx.x == 0) {
+      out_index[row] = bi == 0x7fffffffffffffffLL ? 0 : bi;
+      if (out_value) out_value[row] = best;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host dispatch
+
+template <typename XT, typename YT, bool SPLIT, int NT, int EPI>
+static int launch_gemv(const GemvArgs& a, cudaStream_t s) {
+  const int ncols = SPLIT ? 2 * (int)a.m : (int)a.m;
+  const size_t smem = gv_smem_bytes(ncols, a.k, NT, EPI == EPI_SWIGLU ? 2 : 1);
+  if (smem > 200 * 1024)
+    return fail(MRB_ERR_UNSUPPORTED, "qrow gemv: activation block %lld x %lld too large for one CTA",
+                (long long)a.m, (long long)a.k);
+  auto kern = qrow_gemv_kernel<XT, YT, SPLIT, NT, EPI>;
+  static size_t configured = 0;  // per instantiation
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "qrow gemv: smem attribute: %s", cudaGetErrorString(e));
+    configured = smem;
+  }
+  // Residency: two CTAs per SM by the register bound, fewer when shared memory limits it.
+  int per_sm = (int)std::min<size_t>(2, (227 * 1024) / (smem + 1024));
+  if (per_sm < 1) per_sm = 1;
+  const int64_t ntiles = (a.n + GV_ROWS - 1) / GV_ROWS;
+  const int64_t grid = std::min<int64_t>(ntiles, (int64_t)num_sms() * per_sm);
+  kern<<<(unsigned)grid, GV_THREADS, smem, s>>>(a);
+  return launch_status("qrow gemv");
+}
+
+template <typename XT, typename YT, bool SPLIT, int EPI>
+static int dispatch_nt(const GemvArgs& a, cudaStream_t s) {
+  // Activation rows per launch: at most 16 mma columns, and a staged f16 copy that fits
+  // one CTA's shared memory; wider requests re-stream the weights once per chunk.
+  const int per_col = gv_xstride(a.k) * 2;
+  int max_rows = std::min<int>((int)((160 * 1024) / per_col), 16) / (SPLIT ? 2 : 1);
+  if (max_rows < 1) return fail(MRB_ERR_UNSUPPORTED, "qrow gemv: in_features %lld too large", (long long)a.k);
+  for (int64_t r0 = 0; r0 < a.m; r0 += max_rows) {
+    GemvArgs part = a;
+    part.m = std::min<int64_t>(max_rows, a.m - r0);
+    part.x = reinterpret_cast<const XT*>(a.x) + r0 * a.k;
+    part.y = reinterpret_cast<YT*>(a.y) + r0 * a.n;
+    const int pcols = SPLIT ? 2 * (int)part.m : (int)part.m;
+    const int st = pcols <= 8 ? launch_gemv<XT, YT, SPLIT, 1, EPI>(part, s) : launch_gemv<XT, YT, SPLIT, 2, EPI>(part, s);
+    if (st) return st;
+  }
+  return MRB_OK;
+}
+
+static int check_common(const void* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
+                        int64_t n, const void* y, const char* what) {
+  if (m < 0 || k <= 0 || n <= 0) return fail(MRB_ERR_ARG, "%s: bad shape m=%lld k=%lld n=%lld", what,
+                                             (long long)m, (long long)k, (long long)n);
+  if (!codes || !scales) return fail(MRB_ERR_ARG, "%s: null pointer", what);
+  if (m > 0 && (!x || !y)) return fail(MRB_ERR_ARG, "%s: null pointer", what);
+  if (k % 16 != 0) return fail(MRB_ERR_UNSUPPORTED, "%s: in_features %lld is not a multiple of 16", what,
+                               (long long)k);
+  if (!aligned(codes, 16)) return fail(MRB_ERR_ARG, "%s: codes must be 16-byte aligned", what);
+  if (m > 0 && !aligned(x, 16)) return fail(MRB_ERR_ARG, "%s: activations must be 16-byte aligned", what);
+  return MRB_OK;
+}
+
+int qrow_gemm_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
+                   int64_t n, const float* bias, __nv_bfloat16* y, cudaStream_t s);
+int qrow_gemm_swiglu_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* gate_codes,
+                          const float* gate_scales, const int8_t* up_codes, const float* up_scales, int64_t n,
+                          __nv_bfloat16* y, cudaStream_t s);
+
+// Activation rows above which bf16 projections use the tensor-core GEMM.
+constexpr int64_t GEMV_MAX_ROWS = 16;
+
+int qrow_gemv_dispatch(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* codes,
+                       const float* scales, int64_t n, const float* bias, void* y, cudaStream_t s) {
+  GemvArgs a{x, m, k, codes, scales, nullptr, nullptr, bias, n, y};
+  switch (x_dtype) {
+    case MRB_BF16:
+      if (m > GEMV_MAX_ROWS)
+        return qrow_gemm_bf16((const __nv_bfloat16*)x, m, k, codes, scales, n, bias, (__nv_bfloat16*)y, s);
+      return dispatch_nt<__nv_bfloat16, __nv_bfloat16, false, EPI_STORE>(a, s);
+    case MRB_F16: return dispatch_nt<__half, __half, false, EPI_STORE>(a, s);
+    case MRB_F32: return dispatch_nt<float, float, true, EPI_STORE>(a, s);
+    default: return fail(MRB_ERR_ARG, "qrow_matmul: bad x_dtype %d", x_dtype);
+  }
+}
+
+}  // namespace mrb
+
+using namespace mrb;
+
+extern "C" int mrb_qrow_matmul(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* codes,
+                               const float* scales, int64_t n, const float* bias, void* y, int y_dtype,
+                               void* stream) {
+  int st = check_common(x, m, k, codes, scales, n, y, "qrow_matmul");
+  if (st) return st;
+  if (y_dtype != x_dtype) return fail(MRB_ERR_ARG, "qrow_matmul: output dtype must equal activation dtype");
+  if (m == 0) return MRB_OK;
+  return qrow_gemv_dispatch(x, x_dtype, m, k, codes, scales, n, bias, y, (cudaStream_t)stream);
+}
+
+extern "C" int mrb_qrow_swiglu(const void* x_bf16, int64_t m, int64_t k, const int8_t* gate_codes,
+                               const float* gate_scales, const int8_t* up_codes, const float* up_scales,
+                               int64_t n, void* y_bf16, void* stream) {
+  int st = check_common(x_bf16, m, k, gate_codes, gate_scales, n, y_bf16, "qrow_swiglu");
+  if (st) return st;
+  if (!up_codes || !up_scales) return fail(MRB_ERR_ARG, "qrow_swiglu: null up page");
+  if (!aligned(up_codes, 16)) return fail(MRB_ERR_ARG, "qrow_swiglu: codes must be 16-byte aligned");
+  if (m == 0) return MRB_OK;
+  if (m > GEMV_MAX_ROWS)
+    return qrow_gemm_swiglu_bf16((const __nv_bfloat16*)x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales,
+                                 n, (__nv_bfloat16*)y_bf16, (cudaStream_t)stream);
+  GemvArgs a{x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales, nullptr, n, y_bf16};
+  return dispatch_nt<__nv_bfloat16, __nv_bfloat16, false, EPI_SWIGLU>(a, (cudaStream_t)stream);
+}
+
+extern "C" int mrb_qrow_argmax(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* codes,
+                               const float* scales, int64_t n, int64_t semantic_rows, float* logits,
+                               int64_t* out_index, float* out_value, void* stream) {
+  int st = check_common(x, m, k, codes, scales, n, logits, "qrow_argmax");
+  if (st) return st;
+  if (!out_index) return fail(MRB_ERR_ARG, "qrow_argmax: null out_index");
+  if (semantic_rows < 1 || semantic_rows > n)
+    return fail(MRB_ERR_ARG, "qrow_argmax: semantic_rows %lld outside [1, %lld]", (long long)semantic_rows,
+                (long long)n);
+  if (m == 0) return MRB_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  GemvArgs a{x, m, k, codes, scales, nullptr, nullptr, nullptr, n, logits};
+  switch (x_dtype) {
+    case MRB_BF16: st = dispatch_nt<__nv_bfloat16, float, false, EPI_STORE>(a, s); break;
+    case MRB_F16: st = dispatch_nt<__half, float, false, EPI_STORE>(a, s); break;
+    case MRB_F32: st = dispatch_nt<float, float, true, EPI_STORE>(a, s); break;
+    default: return fail(MRB_ERR_ARG, "qrow_argmax: bad x_dtype %d", x_dtype);
+  }
+  if (st) return st;
+  argmax_rows_kernel<<<(unsigned)m, 1024, 0, s>>>(logits, n, semantic_rows, out_index, out_value);
+  return launch_status("qrow_argmax");
+}

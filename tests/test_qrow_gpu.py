@@ -1,0 +1,206 @@
+"""Parity of the B200 int8 QStore linear kernels against the CPU oracle and the reference's
+golden vectors. Tolerances: fp32 outputs max relative error 1e-4, bf16 outputs 1e-2
+(norm-wise: max|a-b| / max|b|); integer results bit-exact."""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import qrow as oq
+from oracle.numerics import bf16_round, max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 1e-2
+FP32_TOL = 1e-4
+
+
+def _sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def _dev(a, dtype=None, device="cuda"):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(device)
+    return t if dtype is None else t.to(dtype)
+
+
+def test_quantiser_bit_exact(golden, cuda):
+    from mrun_b200.qstore_build import quant_row_int8
+
+    g = golden("qrow")
+    q, s = quant_row_int8(_dev(g["quant_w"]))
+    np.testing.assert_array_equal(q.cpu().numpy(), g["quant_q"])
+    np.testing.assert_array_equal(s.cpu().numpy(), g["quant_s"])
+
+
+def test_config1_w8a16_fp32_against_reference(golden, cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+    from mrun_b200.qstore_build import quant_row_int8
+
+    g = golden("config1")
+    torch.manual_seed(0)
+    x = torch.randn(8, 2048)
+    w = torch.randn(2048, 2048) * 0.02
+    q, s = quant_row_int8(w.to(cuda))
+    assert _sha(q.cpu().numpy()) == str(g["codes_sha"])
+    assert _sha(s.cpu().numpy()) == str(g["scales_sha"])
+    y = qrow_linear(q, s, x.to(cuda))
+    assert y.dtype == torch.float32
+    assert max_rel_err(y.cpu().numpy(), g["y_w8a16"]) < FP32_TOL
+
+
+def test_fp32_rows_against_golden(golden, cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+
+    g = golden("qrow")
+    y = qrow_linear(_dev(g["quant_q"]), _dev(g["quant_s"]), _dev(g["mm32_x"]))
+    assert max_rel_err(y.cpu().numpy(), g["mm32_y"]) < FP32_TOL
+
+
+def test_w8a16_bf16_against_golden(golden, cuda):
+    from mrun_b200.dense_qstore_cuda import CompactQRowPage, fused_qrow_matmul
+
+    g = golden("qrow")
+    page = CompactQRowPage("p", 0, 96, 256, _dev(g["w16_q"]), _dev(g["w16_s"]))
+    y, impl = fused_qrow_matmul(page, _dev(g["w16_x"], torch.bfloat16))
+    assert impl.startswith("b200-")
+    assert y.dtype == torch.bfloat16
+    assert max_rel_err(y.float().cpu().numpy(), g["w16_y"]) < BF16_TOL
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 9, 16])
+@pytest.mark.parametrize("n,k", [(1, 16), (17, 80), (512, 3584), (4608, 3584), (96, 18944)])
+def test_w8a16_shapes(m, n, k, cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+    from mrun_b200.qstore_build import quant_row_int8
+
+    gen = torch.Generator(device="cpu").manual_seed(m * 1000 + n + k)
+    w = torch.randn(n, k, generator=gen) * 0.02
+    x = (torch.randn(m, k, generator=gen) * 3).to(torch.bfloat16)
+    q, s = quant_row_int8(w.to(cuda))
+    y = qrow_linear(q, s, x.to(cuda)).float().cpu().numpy()
+    exact = oq.qrow_matmul_exact(x.float().numpy(), q.cpu().numpy(), s.cpu().numpy())
+    assert max_rel_err(y, exact) < 4e-3  # one bf16 rounding of the output
+    ref = oq.qrow_matmul_w8a16(x.float().numpy(), q.cpu().numpy(), s.cpu().numpy())
+    assert max_rel_err(y, ref) < BF16_TOL
+
+
+@pytest.mark.parametrize("m", [1, 4, 5, 8])
+def test_fp32_rows_shapes(m, cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+
+    gen = torch.Generator(device="cpu").manual_seed(m)
+    q = torch.randint(-127, 128, (300, 1024), generator=gen, dtype=torch.int8)
+    s = torch.rand(300, generator=gen) * 0.01 + 1e-4
+    x = torch.randn(m, 1024, generator=gen) * torch.logspace(-3, 3, 1024)[None, :]
+    y = qrow_linear(q.to(cuda), s.to(cuda), x.to(cuda)).cpu().numpy()
+    exact = oq.qrow_matmul_exact(x.numpy(), q.numpy(), s.numpy())
+    assert max_rel_err(y, exact) < 1e-5
+
+
+def test_bias_added_in_compute_dtype(cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+
+    gen = torch.Generator(device="cpu").manual_seed(11)
+    q = torch.randint(-127, 128, (64, 128), generator=gen, dtype=torch.int8)
+    s = torch.rand(64, generator=gen) * 0.01
+    x = torch.randn(2, 128, generator=gen).to(torch.bfloat16)
+    bias = torch.randn(64, generator=gen)
+    y = qrow_linear(q.to(cuda), s.to(cuda), x.to(cuda), bias=bias.to(cuda)).float().cpu().numpy()
+    base = bf16_round(oq.qrow_matmul_exact(x.float().numpy(), q.numpy(), s.numpy()))
+    expected = bf16_round(base + bf16_round(bias.numpy())[None, :])
+    assert max_rel_err(y, expected) < BF16_TOL
+
+
+def test_swiglu_against_golden_and_oracle(golden, cuda):
+    from mrun_b200.dense_qstore_cuda import CompactQRowPage, fused_qrow_swiglu
+
+    g = golden("qrow")
+    gp = CompactQRowPage("g", 0, 64, 128, _dev(g["sw_gq"]), _dev(g["sw_gs"]))
+    up = CompactQRowPage("u", 0, 64, 128, _dev(g["sw_uq"]), _dev(g["sw_us"]))
+    y, _ = fused_qrow_swiglu(gp, up, _dev(g["sw_x"], torch.bfloat16))
+    assert max_rel_err(y.float().cpu().numpy(), g["sw_y"]) < BF16_TOL
+    # larger shape against the oracle
+    gen = torch.Generator(device="cpu").manual_seed(3)
+    x = torch.randn(1, 3584, generator=gen).to(torch.bfloat16)
+    wg = torch.randn(1000, 3584, generator=gen) * 0.02
+    wu = torch.randn(1000, 3584, generator=gen) * 0.02
+    gq, gs = oq.quant_row_int8(wg.numpy())
+    uq, us = oq.quant_row_int8(wu.numpy())
+    gp = CompactQRowPage("g", 0, 1000, 3584, _dev(gq), _dev(gs))
+    up = CompactQRowPage("u", 0, 1000, 3584, _dev(uq), _dev(us))
+    y, _ = fused_qrow_swiglu(gp, up, x.to(cuda))
+    ref = oq.swiglu_w8a16(x.float().numpy(), gq, gs, uq, us)
+    assert max_rel_err(y.float().cpu().numpy(), ref) < BF16_TOL
+
+
+def test_residual_rms_norm_against_golden(golden, cuda):
+    from mrun_b200.dense_qstore_cuda import fused_residual_rms_norm
+
+    g = golden("qrow")
+    r, n, _ = fused_residual_rms_norm(_dev(g["rr_res"], torch.bfloat16), _dev(g["rr_upd"], torch.bfloat16),
+                                      _dev(g["rr_w"]), 1e-6)
+    np.testing.assert_array_equal(r.float().cpu().numpy(), g["rr_r"])
+    assert max_rel_err(n.float().cpu().numpy(), g["rr_n"]) < BF16_TOL
+
+
+def test_rms_norm_against_golden(golden, cuda):
+    from mrun_b200.dense_qstore_cuda import stable_rms_norm
+
+    g = golden("qrow")
+    y, _ = stable_rms_norm(_dev(g["rn_x"], torch.bfloat16), _dev(g["rr_w"]), 1e-6)
+    assert max_rel_err(y.float().cpu().numpy(), g["rn_y"]) < BF16_TOL
+
+
+def test_exact_argmax_head(golden, cuda):
+    from mrun_b200.dense_qstore_cuda import CompactQRowPage, fused_qrow_exact_argmax
+
+    g = golden("qrow")
+    page = CompactQRowPage("lm_head", 0, 300, 64, _dev(g["hd_q"]), _dev(g["hd_s"]))
+    best, val, _ = fused_qrow_exact_argmax(page, _dev(g["hd_x"], torch.bfloat16), semantic_row_count=290)
+    np.testing.assert_array_equal(best.cpu().numpy(), g["hd_best"])
+
+
+def test_argmax_ties_pick_lowest_index(cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_argmax
+
+    q = torch.zeros(4000, 64, dtype=torch.int8)
+    q[[7, 1234, 3999], 0] = 100  # three identical maximal rows
+    s = torch.ones(4000)
+    x = torch.zeros(2, 64, dtype=torch.bfloat16)
+    x[:, 0] = 1.0
+    idx, val, _ = qrow_argmax(q.to(cuda), s.to(cuda), x.to(cuda))
+    assert idx.cpu().tolist() == [7, 7]
+    idx, _, _ = qrow_argmax(q.to(cuda), s.to(cuda), x.to(cuda), semantic_rows=5)
+    assert idx.cpu().tolist() == [0, 0]
+
+
+def test_embed_rows_bit_exact(cuda):
+    from mrun_b200.qstore_build import embed_rows
+
+    gen = torch.Generator(device="cpu").manual_seed(5)
+    q = torch.randint(-127, 128, (500, 256), generator=gen, dtype=torch.int8)
+    s = torch.rand(500, generator=gen) * 0.02
+    ids = torch.tensor([0, 499, 17, 17, 250])
+    out = embed_rows(q.to(cuda), s.to(cuda), ids.to(cuda), dtype=torch.float32).cpu().numpy()
+    np.testing.assert_array_equal(out, oq.embed_rows(q.numpy(), s.numpy(), ids.numpy()))
+    bad = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = embed_rows(q.to(cuda), s.to(cuda), torch.tensor([3, 600], device=cuda), bad_ids=bad)
+    assert int(bad.item()) == 1 and float(out[1].abs().sum()) == 0.0
+
+
+def test_edge_cases(cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+
+    q = torch.ones(32, 64, dtype=torch.int8, device=cuda)
+    s = torch.ones(32, device=cuda)
+    empty = qrow_linear(q, s, torch.empty(0, 64, dtype=torch.bfloat16, device=cuda))
+    assert empty.shape == (0, 32)
+    with pytest.raises(RuntimeError, match="multiple of 16"):
+        qrow_linear(torch.ones(8, 24, dtype=torch.int8, device=cuda), torch.ones(8, device=cuda),
+                    torch.ones(1, 24, dtype=torch.bfloat16, device=cuda))
+    with pytest.raises(ValueError):
+        qrow_linear(q, s, torch.ones(1, 32, dtype=torch.bfloat16, device=cuda))
