@@ -1,0 +1,403 @@
+"""Benchmark: greedy decode tokens/s of the Qwen2.5-7B-shape int8 QStore decoder (BASELINE
+config 2) and its int8-weight HBM bandwidth, on N GPUs (independent replicas).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one greedy decode token (batch 1, after a 512-token prompt), i.e. one pass of the
+hot path over all 28 layers and the head. `value` is device-timed (CUDA events around K
+CUDA-graph replays, inputs resident in HBM); `e2e` is the same loop through the public
+per-token path with the token id copied host->device and the chosen id device->host every
+step. The reference arm (`--impl reference`) times the reference's CPU decode path
+(restated in oracle/: fp32 dequantise-then-matmul, engine/kernels/paged_forward.py) on the
+host cores. Prints exactly one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+METRIC = "decode tokens/s and int8-weight HBM GB/s vs ~8 TB/s peak at 1/2/4/8 B200"
+PROMPT_LEN = 512
+WORKLOAD = "config2: Qwen2.5-7B-shape dense int8-QStore decoder, batch 1, 512-token prompt, greedy decode"
+
+
+def _peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _traffic_from_profiles() -> float | None:
+    """Per-launch DRAM bytes of the roofline kernel from the committed ncu summary."""
+    path = REPO / "profiles" / "qrow_gemv_swiglu_m1.md"
+    if not path.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist_setup(n_gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def _max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------- CPU arm
+
+
+CPU_CONTEXT = 512
+
+
+def _cpu_decoder(threads: int):
+    import torch
+
+    from oracle.cpu_path import CpuPathDecoder
+
+    torch.set_num_threads(threads)
+    dec = CpuPathDecoder.synthetic_qwen25_7b(seed=0)
+    dec.prepare_context(CPU_CONTEXT)
+    return dec
+
+
+def _cpu_units(dec, units) -> float:
+    """Seconds to run the given decode units (layers / head blocks) once."""
+    import torch
+
+    x = torch.randn(1, dec.hidden) * 0.5
+    t0 = time.perf_counter()
+    for u in units:
+        y = dec.run_unit(u, x)
+        if u < dec.num_layers:
+            x = y
+    return time.perf_counter() - t0
+
+
+def _cpu_decode_sample(tokens: int, threads: int) -> dict:
+    """The reference's CPU decode path on the host cores: fp32 dequantise-then-matmul per
+    projection (engine/kernels/qstore.py:385-399, 1082-1092 via paged_forward_kv), timed on
+    `tokens` full decode steps (28 layers + head) of the config-2 model at context 512."""
+    dec = _cpu_decoder(threads)
+    _cpu_units(dec, [0, dec.num_layers])  # warm-up: allocator and thread pool
+    dt = _cpu_units(dec, list(range(dec.units())) * tokens)
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{tokens} full decode tokens (28 layers + 19 head blocks) of the config-2 model at context "
+                      f"{CPU_CONTEXT}, fp32 dequantise-then-matmul (the reference CPU path), {dt:.1f} s"}
+
+
+def run_reference(args) -> None:
+    # CPU-only arm: rank 0 alone runs; other torchrun ranks exit without work or collectives.
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    threads = os.cpu_count() or 1
+    dec = _cpu_decoder(threads)
+    total = dec.units()
+    per_step_units = 3  # each bench step is 3 of the token's 47 units, rotating
+    times = []
+    cursor = 0
+    budget_end = time.perf_counter() + 150.0  # bound the arm to a few minutes at any --steps
+    for i in range(args.warmup + args.steps):
+        if times and time.perf_counter() > budget_end:
+            break
+        units = [(cursor + j) % total for j in range(per_step_units)]
+        cursor = (cursor + per_step_units) % total
+        dt = _cpu_units(dec, units)
+        if i >= args.warmup:
+            times.append(dt)
+    step_s = sum(times) / len(times)
+    token_s = step_s * total / per_step_units
+    value = 1.0 / token_s
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": token_s * 1000.0, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": 1, "cpu_threads": threads, "context": CPU_CONTEXT},
+        "cpu_baseline": {
+            "value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"each step runs {per_step_units} of the {total} units of one decode token (28 layers + 19 "
+                      f"head blocks, rotating); token time = mean step time x {total}/{per_step_units}; "
+                      f"{len(times)} steps timed",
+        },
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- GPU arm
+
+
+def _time_gemv(weights, iters: int = 56) -> dict:
+    """Average device duration of the dominant kernel (paired gate/up SwiGLU GEMV, M=1) over
+    all layers in turn, so every launch streams its weights from HBM."""
+    import torch
+
+    from mrun_b200.dense_qstore_cuda import qrow_swiglu
+
+    cfg = weights.cfg
+    x = torch.randn(1, cfg.hidden, device="cuda").to(torch.bfloat16)
+    out = torch.empty(1, cfg.ffn, device="cuda", dtype=torch.bfloat16)
+    layers = weights.layers
+
+    def launch(i):
+        layer = layers[i % len(layers)]
+        qrow_swiglu(layer.gate.codes, layer.gate.scales, layer.up.codes, layer.up.scales, x, out=out)
+
+    for i in range(len(layers)):
+        launch(i)
+    stream = torch.cuda.current_stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(iters):
+            launch(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    avg_s = e0.elapsed_time(e1) / 1000.0 / iters
+    bytes_per_launch = 2 * cfg.ffn * cfg.hidden + 2 * cfg.ffn * 4 + cfg.hidden * 2 + cfg.ffn * 2
+    del graph
+    return {"avg_s": avg_s, "bytes": bytes_per_launch}
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+
+    from mrun_b200.dense_engine import DenseConfig, DenseDecoder, DenseWeights
+
+    world, rank, local = _dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    cfg = DenseConfig.qwen25_7b()
+    weights = DenseWeights.synthetic(cfg, device, seed=0)
+    total_steps = args.warmup + args.steps
+    dec = DenseDecoder(weights, max_batch=1, max_seq_len=PROMPT_LEN + 2 * total_steps + 32, device=device,
+                       max_prefill_tokens=PROMPT_LEN)
+    prompt = torch.from_numpy(np.random.default_rng(rank).integers(0, cfg.vocab, PROMPT_LEN))
+
+    # ---- device-timed decode: K graph replays, inputs resident in HBM
+    first = dec.prefill(0, prompt)
+    length = dec.kv.lengths[0]
+    dec.kv.reserve(0, length + 2 * total_steps + 1)
+    dec.begin_decode(1, first.reshape(1), [length])
+    dec.capture(1)
+    dec.begin_decode(1, first.reshape(1), [length])
+    for _ in range(args.warmup):
+        dec.step()
+    stream = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            dec.step()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+    _barrier(world)
+    step_s = _max_over_ranks(e0.elapsed_time(e1) / 1000.0 / args.steps, world)
+    dec.check_errors()
+
+    # ---- end-to-end: host token in, host token out, every step (the public generate path)
+    pin_in = torch.empty(1, dtype=torch.int64, pin_memory=True)
+    pin_out = torch.empty(1, dtype=torch.int64, pin_memory=True)
+    pin_in[0] = int(dec.next_ids[0].item())
+
+    def e2e_step():
+        dec.in_ids[:1].copy_(pin_in, non_blocking=True)
+        dec.step()
+        pin_out.copy_(dec.next_ids[:1], non_blocking=True)
+        stream.synchronize()
+        pin_in[0] = pin_out[0]
+
+    for _ in range(min(args.warmup, 3)):
+        e2e_step()
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = _max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+    dec.check_errors()
+
+    # ---- dominant-kernel roofline (timed alone, burst HBM peak)
+    g = _time_gemv(weights)
+    peaks = _peaks()
+    achieved_gbs = g["bytes"] / g["avg_s"] / 1e9
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+    wb = cfg.weight_bytes()
+    step_weight_bytes = wb["body"] + wb["head"] + wb["scales"]
+    value = world / step_s
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_s * 1000.0,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "weights": "int8 per-channel (QStore qrow)",
+        "data": "synthetic: random-init N(0,0.02) int8-quantised weights, uniform random prompt ids (seeded)",
+        "config": {
+            "workload": WORKLOAD,
+            "batch": 1,
+            "prompt_len": PROMPT_LEN,
+            "context_during_timing": [PROMPT_LEN + args.warmup, PROMPT_LEN + args.warmup + args.steps],
+            "kv_page_tokens": 16,
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "no flush: each step streams 7.08 GB of weights, far above the 126 MB L2",
+        },
+        "int8_weight_gbs": step_weight_bytes / step_s / 1e9,
+        "int8_weight_frac_of_measured_hbm": step_weight_bytes / step_s / 1e9 / peaks["hbm_gbs"],
+        "int8_weight_frac_of_8tbs_spec": step_weight_bytes / step_s / 1e9 / 8000.0,
+        "roofline": {
+            "kernel": "qrow_gemv_kernel (paired gate/up SwiGLU, M=1, 18944x3584 x2)",
+            "bound": "hbm",
+            "achieved": achieved_gbs,
+            "peak": peaks["hbm_gbs"],
+            "peak_source": f"{peaks['source']} hbm_gbs (burst copy)",
+            "unit": "GB/s",
+            "frac": achieved_gbs / peaks["hbm_gbs"],
+            "traffic": _traffic_from_profiles(),
+            "bytes_per_launch": g["bytes"],
+        },
+        "e2e": {"value": world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+        "gpu_launches": dec.launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = _cpu_decode_sample(args.cpu_tokens, os.cpu_count() or 1)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-tokens", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

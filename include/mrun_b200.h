@@ -148,6 +148,12 @@ int mrb_paged_attention(const void *q, int64_t rows, int64_t hq, int64_t hkv, in
                         const void *v_new, float scale, int64_t max_total_tokens, void *out,
                         void *workspace, size_t workspace_size, void *stream);
 
+/* Greedy decode bookkeeping: input_ids[i] = next_ids[i]; positions[i] += 1; row_len[i] += 1
+ * for i < rows. Lets a captured decode step feed itself (the reference's engine does this on
+ * the host after `token.cpu()`, engine/dense_qstore_cuda.py:2389-2416). */
+int mrb_decode_advance(const int64_t *next_ids, int64_t *input_ids, int32_t *positions,
+                       int32_t *row_len, int64_t rows, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -323,12 +323,16 @@ static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total) {
   return SplitPlan{(int)ns, (int)tps};
 }
 
+// Workspace layout: AT_MAX_COUNTERS merge counters at offset 0 (fixed, so that a buffer
+// reused across different shapes never finds stale partials where counters live), then the
+// fp32 partials. Splitting only happens for fewer than 2 * SMs (row, head) groups.
+constexpr int64_t AT_MAX_COUNTERS = 4096;
+constexpr size_t AT_COUNTER_BYTES = AT_MAX_COUNTERS * sizeof(unsigned);
+
 static size_t workspace_bytes(int64_t rows, int64_t hq, int64_t hkv, int64_t d, const SplitPlan& p) {
   if (p.nsplit <= 1) return 0;
   const int64_t group = hq / hkv;
-  size_t part = (size_t)rows * hkv * p.nsplit * group * (2 + d) * sizeof(float);
-  part = (part + 255) & ~size_t(255);
-  return part + (size_t)rows * hkv * sizeof(unsigned);
+  return AT_COUNTER_BYTES + (size_t)rows * hkv * p.nsplit * group * (2 + d) * sizeof(float);
 }
 
 }  // namespace mrb
@@ -396,10 +400,9 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
              (const __nv_bfloat16*)k_new, (const __nv_bfloat16*)v_new, scale, plan.nsplit, plan.tiles_per_split,
              (__nv_bfloat16*)out, nullptr, nullptr};
   if (need > 0) {
-    size_t part = (size_t)rows * hkv * plan.nsplit * (hq / hkv) * (2 + head_dim) * sizeof(float);
-    part = (part + 255) & ~size_t(255);
-    a.part = (float*)workspace;
-    a.counters = (unsigned*)((char*)workspace + part);
+    if (rows * hkv > AT_MAX_COUNTERS) return fail(MRB_ERR_UNSUPPORTED, "paged_attention: too many split groups");
+    a.counters = (unsigned*)workspace;
+    a.part = (float*)((char*)workspace + AT_COUNTER_BYTES);
   }
   dim3 grid((unsigned)(rows * hkv), (unsigned)plan.nsplit);
   if (head_dim == 128)
@@ -407,4 +410,29 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
   else
     paged_attention_kernel<64><<<grid, AT_THREADS, 0, (cudaStream_t)stream>>>(a);
   return launch_status("paged_attention");
+}
+
+// ------------------------------------------------------------------ decode-step bookkeeping
+
+// After a greedy decode step: the chosen token becomes the next input, every row advances
+// one position. Runs inside the captured decode graph so replays need no host writes.
+__global__ void decode_advance_kernel(const int64_t* __restrict__ next_ids, int64_t* __restrict__ input_ids,
+                                      int32_t* __restrict__ positions, int32_t* __restrict__ row_len,
+                                      int64_t rows) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < rows) {
+    input_ids[i] = next_ids[i];
+    positions[i] += 1;
+    row_len[i] += 1;
+  }
+}
+
+extern "C" int mrb_decode_advance(const int64_t* next_ids, int64_t* input_ids, int32_t* positions,
+                                  int32_t* row_len, int64_t rows, void* stream) {
+  if (rows < 0) return fail(MRB_ERR_ARG, "decode_advance: bad rows");
+  if (rows == 0) return MRB_OK;
+  if (!next_ids || !input_ids || !positions || !row_len) return fail(MRB_ERR_ARG, "decode_advance: null pointer");
+  decode_advance_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, (cudaStream_t)stream>>>(next_ids, input_ids,
+                                                                                           positions, row_len, rows);
+  return launch_status("decode_advance");
 }

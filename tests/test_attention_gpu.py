@@ -104,7 +104,7 @@ def test_rope_kv_append_bit_exact_and_gather(cuda):
     cache.append(
         1, qkv_dev[:, hq * d:], qkv_dev[:, (hq + hkv) * d:], torch.from_numpy(positions).to(cuda),
         torch.ones(tokens, dtype=torch.int32, device=cuda), q_rows=qkv_dev, q_out=q_out,
-        rope=(torch.from_numpy(cos).to(cuda), torch.from_numpy(sin).to(cuda)), in_row_stride=(hq + 2 * hkv) * d,
+        rope=(torch.from_numpy(cos[:, : d // 2].copy()).to(cuda), torch.from_numpy(sin[:, : d // 2].copy()).to(cuda)), in_row_stride=(hq + 2 * hkv) * d,
         num_heads=hq, error_flag=err,
     )
     assert int(err.item()) == 0

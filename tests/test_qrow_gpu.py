@@ -204,3 +204,39 @@ def test_edge_cases(cuda):
                     torch.ones(1, 24, dtype=torch.bfloat16, device=cuda))
     with pytest.raises(ValueError):
         qrow_linear(q, s, torch.ones(1, 32, dtype=torch.bfloat16, device=cuda))
+
+
+@pytest.mark.parametrize("m,n,k", [(17, 64, 128), (100, 300, 512), (512, 512, 3584), (130, 200, 80)])
+def test_w8a16_gemm_path(m, n, k, cuda):
+    """Prefill-size rows take the tensor-core GEMM; same contract as the GEMV."""
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+
+    gen = torch.Generator(device="cpu").manual_seed(m + n + k)
+    q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    s = torch.rand(n, generator=gen) * 0.01 + 1e-4
+    x = (torch.randn(m, k, generator=gen) * 2).to(torch.bfloat16)
+    bias = torch.randn(n, generator=gen)
+    y = qrow_linear(q.to(cuda), s.to(cuda), x.to(cuda)).float().cpu().numpy()
+    exact = oq.qrow_matmul_exact(x.float().numpy(), q.numpy(), s.numpy())
+    assert max_rel_err(y, exact) < 4e-3
+    yb = qrow_linear(q.to(cuda), s.to(cuda), x.to(cuda), bias=bias.to(cuda)).float().cpu().numpy()
+    expected = bf16_round(bf16_round(exact) + bf16_round(bias.numpy())[None, :])
+    assert max_rel_err(yb, expected) < BF16_TOL
+
+
+@pytest.mark.parametrize("m,n,k", [(17, 64, 128), (200, 300, 512), (512, 256, 3584)])
+def test_swiglu_gemm_path(m, n, k, cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_swiglu
+
+    gen = torch.Generator(device="cpu").manual_seed(m * 7 + n)
+    gq = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    uq = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    gs = torch.rand(n, generator=gen) * 0.002
+    us = torch.rand(n, generator=gen) * 0.002
+    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    y = qrow_swiglu(gq.to(cuda), gs.to(cuda), uq.to(cuda), us.to(cuda), x.to(cuda)).float().cpu().numpy()
+    ref = oq.swiglu_w8a16(x.float().numpy(), gq.numpy(), gs.numpy(), uq.numpy(), us.numpy())
+    assert max_rel_err(y, ref) < BF16_TOL
+    # the GEMV and GEMM paths agree on the rows they share
+    y_small = qrow_swiglu(gq.to(cuda), gs.to(cuda), uq.to(cuda), us.to(cuda), x[:4].to(cuda)).float().cpu().numpy()
+    assert max_rel_err(y_small, y[:4]) < BF16_TOL
