@@ -17,9 +17,9 @@
 
 namespace mrb {
 
-constexpr int AT_THREADS = 128;
 constexpr int AT_TILE = 16;
 constexpr int AT_MAX_GROUP = 16;
+constexpr int AT_MAX_SPLIT = 128;  // splits per (row, head); merge stats live in wacc
 
 // ------------------------------------------------------------------ RoPE + KV append
 
@@ -47,11 +47,28 @@ struct RopeArgs {
 // Rotate-half RoPE exactly as the reference evaluates it in fp32
 // (engine/dense_qstore_cuda.py:689-704): out = bf16(v*cos + rot(v)*sin), with separately
 // rounded products (no fused multiply-add) and rot(v) = cat(-v[h:], v[:h]).
-__device__ __forceinline__ float rope_elem(const __nv_bfloat16* v, int i, int half, const float* c, const float* s) {
-  const int j = i < half ? i : i - half;
-  const float x = __bfloat162float(v[i]);
-  const float r = i < half ? -__bfloat162float(v[i + half]) : __bfloat162float(v[i - half]);
-  return __fadd_rn(__fmul_rn(x, c[j]), __fmul_rn(r, s[j]));
+// One CTA per token, one warp per head (queries, then keys, then values). Lane j handles
+// the rotation pairs (2j, 2j+1) of the first half and their partners in the second half.
+__device__ __forceinline__ void rope_head(const __nv_bfloat16* src, __nv_bfloat16* dst, int half, const float* c,
+                                          const float* s, int lane) {
+  for (int j = 2 * lane; j < half; j += 64) {
+    const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j));
+    const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + half + j));
+    float2 o_lo, o_hi;
+    if (c) {
+      const float2 cc = *reinterpret_cast<const float2*>(c + j);
+      const float2 ss = *reinterpret_cast<const float2*>(s + j);
+      o_lo.x = __fadd_rn(__fmul_rn(lo.x, cc.x), __fmul_rn(-hi.x, ss.x));
+      o_lo.y = __fadd_rn(__fmul_rn(lo.y, cc.y), __fmul_rn(-hi.y, ss.y));
+      o_hi.x = __fadd_rn(__fmul_rn(hi.x, cc.x), __fmul_rn(lo.x, ss.x));
+      o_hi.y = __fadd_rn(__fmul_rn(hi.y, cc.y), __fmul_rn(lo.y, ss.y));
+    } else {
+      o_lo = lo;
+      o_hi = hi;
+    }
+    *reinterpret_cast<__nv_bfloat162*>(dst + j) = __floats2bfloat162_rn(o_lo.x, o_lo.y);
+    *reinterpret_cast<__nv_bfloat162*>(dst + half + j) = __floats2bfloat162_rn(o_hi.x, o_hi.y);
+  }
 }
 
 __global__ void __launch_bounds__(256) rope_kv_append_kernel(RopeArgs a) {
@@ -78,25 +95,21 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(RopeArgs a) {
     return;
   }
   const int64_t slot = pos % a.page_size;
-  // queries
-  if (a.q_out) {
-    const __nv_bfloat16* qi = a.q_in + t * a.in_stride;
-    for (int64_t e = threadIdx.x; e < a.hq * a.d; e += blockDim.x) {
-      const int64_t h = e / a.d;
-      const int i = (int)(e - h * a.d);
-      const float v = c ? rope_elem(qi + h * a.d, i, half, c, s) : __bfloat162float(qi[e]);
-      a.q_out[t * a.hq * a.d + e] = __float2bfloat16_rn(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int64_t nq = a.q_out ? a.hq : 0;
+  for (int64_t h = warp; h < nq + 2 * a.hkv; h += nwarps) {
+    if (h < nq) {
+      rope_head(a.q_in + t * a.in_stride + h * a.d, a.q_out + (t * a.hq + h) * a.d, half, c, s, lane);
+    } else if (h < nq + a.hkv) {
+      const int64_t kh = h - nq;
+      rope_head(a.k_in + t * a.in_stride + kh * a.d,
+                a.k_cache + page * a.stride_page + kh * a.stride_head + slot * a.stride_tok, half, c, s, lane);
+    } else {
+      const int64_t vh = h - nq - a.hkv;
+      rope_head(a.v_in + t * a.in_stride + vh * a.d,
+                a.v_cache + page * a.stride_page + vh * a.stride_head + slot * a.stride_tok, half, nullptr, nullptr,
+                lane);
     }
-  }
-  const __nv_bfloat16* ki = a.k_in + t * a.in_stride;
-  const __nv_bfloat16* vi = a.v_in + t * a.in_stride;
-  for (int64_t e = threadIdx.x; e < a.hkv * a.d; e += blockDim.x) {
-    const int64_t h = e / a.d;
-    const int i = (int)(e - h * a.d);
-    const int64_t dst = page * a.stride_page + h * a.stride_head + slot * a.stride_tok + i;
-    const float kv = c ? rope_elem(ki + h * a.d, i, half, c, s) : __bfloat162float(ki[e]);
-    a.k_cache[dst] = __float2bfloat16_rn(kv);
-    a.v_cache[dst] = vi[e];
   }
 }
 
@@ -122,35 +135,36 @@ struct AttnArgs {
   unsigned* counters;  // [rows*hkv]
 };
 
+__device__ __forceinline__ int64_t kv_offset(const AttnArgs& a, int64_t seq, int64_t tok, int64_t khead) {
+  const unsigned t = (unsigned)tok, ps = (unsigned)a.page_size;  // positions < 2^31
+  const unsigned lp = t / ps;
+  const int64_t page = a.block_table[seq * a.bt_stride + lp];
+  return page * a.stride_page + khead + (int64_t)(t - lp * ps) * a.stride_tok;
+}
+
+// Decode attention, one warp per query head of the GQA group (blockDim = 32 * group).
+// The CTA owns (query row, KV head, split) and walks the split's 16-token tiles: all threads
+// stage the tile's K and V in shared memory (K XOR-swizzled so the score reads are
+// conflict-free), then every warp runs an fp32 online softmax for its head. Score phase:
+// lane = (token, half of the head dim); value phase: lane owns D/32 consecutive dims.
+// Splits publish (max, sum, acc) partials; the last CTA of the (row, head) group merges them
+// in split order (deterministic), each warp merging its own head.
 template <int D>
-__global__ void __launch_bounds__(AT_THREADS) paged_attention_kernel(AttnArgs a) {
-  static_assert(D <= AT_THREADS && D % 64 == 0, "one thread per head dimension");
-  constexpr int PARTS = 8;          // threads cooperating on one (token, head) dot product
-  constexpr int DPP = D / PARTS;    // dims per part
-  const int group = (int)(a.hq / a.hkv);
+__global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(AttnArgs a) {
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+  constexpr int HALF = D / 2;     // dims per lane in the score phase
+  constexpr int VD = D / 32;      // dims per lane in the value phase
+  constexpr int CH = D / 8;       // 16-byte chunks per K/V row
+  const int group = blockDim.x >> 5;
   const int64_t rh = blockIdx.x;  // row * hkv + kv head
   const int split = blockIdx.y;
   const int64_t r = rh / a.hkv;
   const int kvh = (int)(rh - r * a.hkv);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, g = tid >> 5, lane = tid & 31;
 
-  __shared__ float qs[AT_MAX_GROUP][D];
-  __shared__ float ps[AT_MAX_GROUP][AT_TILE];
-  __shared__ float m_s[AT_MAX_GROUP], l_s[AT_MAX_GROUP], alpha_s[AT_MAX_GROUP];
+  __shared__ __align__(16) __nv_bfloat16 ks[AT_TILE][D];
+  __shared__ __align__(16) __nv_bfloat16 vs[AT_TILE][D];
   __shared__ bool is_last;
-
-  for (int e = tid; e < group * D; e += AT_THREADS) {
-    const int g = e / D, dd = e - g * D;
-    qs[g][dd] = __bfloat162float(a.q[(r * a.hq + (int64_t)kvh * group + g) * D + dd]);
-  }
-  if (tid < group) {
-    m_s[tid] = -INFINITY;
-    l_s[tid] = 0.f;
-  }
-  float acc[AT_MAX_GROUP];
-#pragma unroll
-  for (int g = 0; g < AT_MAX_GROUP; ++g) acc[g] = 0.f;
-  __syncthreads();
 
   const int64_t seq = a.row_seq ? a.row_seq[r] : r;
   const int64_t len = a.row_len[r];
@@ -159,126 +173,114 @@ __global__ void __launch_bounds__(AT_THREADS) paged_attention_kernel(AttnArgs a)
   const int64_t t_begin = (int64_t)split * a.tiles_per_split * AT_TILE;
   const int64_t t_end = min(total, t_begin + (int64_t)a.tiles_per_split * AT_TILE);
   const int64_t khead = (int64_t)kvh * a.stride_head;
+  const int my_tok = lane & 15, half = lane >> 4;
 
-  const int my_tok = tid / PARTS;  // token within the tile for the score phase
-  const int part = tid % PARTS;
+  // this warp's query head, pre-scaled, for this lane's half of the dims
+  float qreg[HALF];
+  {
+    const __nv_bfloat16* qp = a.q + (r * a.hq + (int64_t)kvh * group + g) * D + half * HALF;
+#pragma unroll
+    for (int i = 0; i < HALF; i += 8) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(qp + i);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h2[j]);
+        qreg[i + 2 * j] = f.x * a.scale;
+        qreg[i + 2 * j + 1] = f.y * a.scale;
+      }
+    }
+  }
+  float m = -INFINITY, l = 0.f, acc[VD];
+#pragma unroll
+  for (int i = 0; i < VD; ++i) acc[i] = 0.f;
+
   for (int64_t t0 = t_begin; t0 < t_end; t0 += AT_TILE) {
-    // ---- scores: 16 tokens x group heads, 8 threads per (token) dot product
-    const int64_t tok = t0 + my_tok;
-    float kreg[DPP];
-    const bool valid = tok < t_end;
-    if (valid) {
-      const __nv_bfloat16* kp;
-      if (has_new && tok == len) {
-        kp = a.k_new + (r * a.hkv + kvh) * D;
-      } else {
-        const int64_t page = a.block_table[seq * a.bt_stride + tok / a.page_size];
-        kp = a.k_cache + page * a.stride_page + khead + (tok % a.page_size) * a.stride_tok;
-      }
-      const uint4* kv = reinterpret_cast<const uint4*>(kp + part * DPP);
-#pragma unroll
-      for (int v = 0; v < DPP / 8; ++v) {
-        const uint4 raw = __ldg(kv + v);
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) kreg[v * 8 + i] = __bfloat162float(e[i]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < DPP; ++i) kreg[i] = 0.f;
-    }
-    for (int g = 0; g < group; ++g) {
-      float sdot = 0.f;
-#pragma unroll
-      for (int i = 0; i < DPP; ++i) sdot = fmaf(qs[g][part * DPP + i], kreg[i], sdot);
-      sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
-      sdot += __shfl_xor_sync(0xffffffffu, sdot, 2);
-      sdot += __shfl_xor_sync(0xffffffffu, sdot, 4);
-      if (part == 0) ps[g][my_tok] = valid ? sdot * a.scale : -INFINITY;
-    }
-    __syncthreads();
-    // ---- online softmax update, 16 lanes per head (all lanes take part in the shuffles)
-    {
-      const bool active = tid < group * AT_TILE;
-      const int g = active ? tid / AT_TILE : 0;
-      const int j = tid % AT_TILE;
-      const float sc = active ? ps[g][j] : -INFINITY;
-      float mx = sc;
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_old = active ? m_s[g] : -INFINITY;
-      const float m_new = fmaxf(m_old, mx);
-      const float p = (m_new == -INFINITY) ? 0.f : expf(sc - m_new);
-      float sum = p;
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (active) {
-        ps[g][j] = p;
-        if (j == 0) {
-          const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-          alpha_s[g] = alpha;
-          l_s[g] = l_s[g] * alpha + sum;
-          m_s[g] = m_new;
-        }
-      }
-    }
-    __syncthreads();
-    // ---- acc[g][d] = acc * alpha + sum_j p[g][j] * V[j][d]
-    if (tid < D) {
-      const int dd = tid;
-      float vv[AT_TILE];
-#pragma unroll
-      for (int j = 0; j < AT_TILE; ++j) {
-        const int64_t tj = t0 + j;
-        if (tj < t_end) {
-          const __nv_bfloat16* vp;
-          if (has_new && tj == len) {
-            vp = a.v_new + (r * a.hkv + kvh) * D;
-          } else {
-            const int64_t page = a.block_table[seq * a.bt_stride + tj / a.page_size];
-            vp = a.v_cache + page * a.stride_page + khead + (tj % a.page_size) * a.stride_tok;
-          }
-          vv[j] = __bfloat162float(vp[dd]);
+    // ---- stage K (swizzled) and V of 16 tokens
+    for (int e = tid; e < AT_TILE * CH; e += blockDim.x) {
+      const int t = e / CH, c = e - t * CH;
+      const int64_t tok = t0 + t;
+      uint4 kraw = make_uint4(0, 0, 0, 0), vraw = make_uint4(0, 0, 0, 0);
+      if (tok < t_end) {
+        const __nv_bfloat16 *kp, *vp;
+        if (has_new && tok == len) {
+          kp = a.k_new + (r * a.hkv + kvh) * D;
+          vp = a.v_new + (r * a.hkv + kvh) * D;
         } else {
-          vv[j] = 0.f;
+          const int64_t off = kv_offset(a, seq, tok, khead);
+          kp = a.k_cache + off;
+          vp = a.v_cache + off;
         }
+        kraw = __ldg(reinterpret_cast<const uint4*>(kp) + c);
+        vraw = __ldg(reinterpret_cast<const uint4*>(vp) + c);
       }
+      reinterpret_cast<uint4*>(&ks[t][0])[c ^ (t & 7)] = kraw;
+      reinterpret_cast<uint4*>(&vs[t][0])[c] = vraw;
+    }
+    __syncthreads();
+    // ---- score of this lane's token for this warp's head
+    float sc = 0.f;
 #pragma unroll
-      for (int g = 0; g < AT_MAX_GROUP; ++g) {
-        if (g < group) {
-          float s = acc[g] * alpha_s[g];
+    for (int i = 0; i < HALF / 8; ++i) {
+      const int c = half * (HALF / 8) + i;
+      const uint4 raw = reinterpret_cast<const uint4*>(&ks[my_tok][0])[c ^ (my_tok & 7)];
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-          for (int j = 0; j < AT_TILE; ++j) s = fmaf(ps[g][j], vv[j], s);
-          acc[g] = s;
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h2[j]);
+        sc = fmaf(qreg[i * 8 + 2 * j], f.x, sc);
+        sc = fmaf(qreg[i * 8 + 2 * j + 1], f.y, sc);
+      }
+    }
+    sc += __shfl_xor_sync(0xffffffffu, sc, 16);
+    if (t0 + my_tok >= t_end) sc = -INFINITY;
+    float mx = sc;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float m_new = fmaxf(m, mx);
+    const float p = (m_new == -INFINITY) ? 0.f : expf(sc - m_new);
+    float sum = p;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float alpha = (m == -INFINITY) ? 0.f : expf(m - m_new);
+    l = l * alpha + sum;
+    m = m_new;
+#pragma unroll
+    for (int i = 0; i < VD; ++i) acc[i] *= alpha;
+    // ---- acc += sum_t p_t * V[t][lane dims]
+#pragma unroll
+    for (int t = 0; t < AT_TILE; ++t) {
+      const float pt = __shfl_sync(0xffffffffu, p, t);
+      if (VD == 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(&vs[t][lane * 4]);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
+        acc[0] = fmaf(pt, f0.x, acc[0]);
+        acc[1 % VD] = fmaf(pt, f0.y, acc[1 % VD]);
+        acc[2 % VD] = fmaf(pt, f1.x, acc[2 % VD]);
+        acc[3 % VD] = fmaf(pt, f1.y, acc[3 % VD]);
+      } else {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vs[t][lane * 2]));
+        acc[0] = fmaf(pt, f.x, acc[0]);
+        acc[1 % VD] = fmaf(pt, f.y, acc[1 % VD]);
       }
     }
     __syncthreads();
   }
 
-  // ---- finish: direct store, or publish a partial and let the last split merge
+  __nv_bfloat16* out = a.out + (r * a.hq + (int64_t)kvh * group + g) * D + lane * VD;
   if (a.nsplit == 1) {
-    if (tid < D) {
 #pragma unroll
-      for (int g = 0; g < AT_MAX_GROUP; ++g) {
-        if (g < group) {
-          const float l = l_s[g];
-          const float v = l > 0.f ? acc[g] / l : 0.f;
-          a.out[(r * a.hq + (int64_t)kvh * group + g) * D + tid] = __float2bfloat16_rn(v);
-        }
-      }
-    }
+    for (int i = 0; i < VD; ++i) out[i] = __float2bfloat16_rn(l > 0.f ? acc[i] / l : 0.f);
     return;
   }
-  float* my = a.part + ((rh * a.nsplit + split) * group) * (2 + D);
-  if (tid < D) {
+  // ---- publish this split's partial for the warp's head
+  float* mine = a.part + ((rh * a.nsplit + split) * group + g) * (2 + D);
 #pragma unroll
-    for (int g = 0; g < AT_MAX_GROUP; ++g)
-      if (g < group) my[g * (2 + D) + 2 + tid] = acc[g];
-  }
-  if (tid < group) {
-    my[tid * (2 + D)] = m_s[tid];
-    my[tid * (2 + D) + 1] = l_s[tid];
+  for (int i = 0; i < VD; ++i) mine[2 + lane * VD + i] = acc[i];
+  if (lane == 0) {
+    mine[0] = m;
+    mine[1] = l;
   }
   __threadfence();
   __syncthreads();
@@ -289,22 +291,37 @@ __global__ void __launch_bounds__(AT_THREADS) paged_attention_kernel(AttnArgs a)
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  const float* base = a.part + (rh * a.nsplit) * group * (2 + D);
-  for (int dd = tid; dd < D; dd += AT_THREADS) {
-    for (int g = 0; g < group; ++g) {
-      float mx = -INFINITY;
-      for (int s = 0; s < a.nsplit; ++s) mx = fmaxf(mx, __ldcg(base + (s * group + g) * (2 + D)));
-      float l = 0.f, o = 0.f;
-      for (int s = 0; s < a.nsplit; ++s) {
-        const float* p = base + (s * group + g) * (2 + D);
-        const float ms = __ldcg(p);
-        const float w = (ms == -INFINITY) ? 0.f : expf(ms - mx);
-        l = fmaf(__ldcg(p + 1), w, l);
-        o = fmaf(__ldcg(p + 2 + dd), w, o);
-      }
-      a.out[(r * a.hq + (int64_t)kvh * group + g) * D + dd] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+  // ---- last split: each warp merges its head over all splits, in split order
+  const float* base = a.part + (rh * a.nsplit * group + g) * (2 + D);
+  const int64_t sstride = (int64_t)group * (2 + D);
+  float mx_all = -INFINITY;
+  for (int s0 = lane; s0 < a.nsplit; s0 += 32) mx_all = fmaxf(mx_all, __ldcg(base + s0 * sstride));
+  mx_all = warp_max(mx_all);
+  float lsum = 0.f, o[VD];
+#pragma unroll
+  for (int i = 0; i < VD; ++i) o[i] = 0.f;
+  for (int s0 = 0; s0 < a.nsplit; s0 += 8) {
+    float ms[8], ls[8], av[8][VD];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool ok = s0 + j < a.nsplit;
+      const float* p = base + (s0 + j) * sstride;
+      ms[j] = ok ? __ldcg(p) : -INFINITY;
+      ls[j] = ok ? __ldcg(p + 1) : 0.f;
+#pragma unroll
+      for (int i = 0; i < VD; ++i) av[j][i] = ok ? __ldcg(p + 2 + lane * VD + i) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float wt = (ms[j] == -INFINITY) ? 0.f : expf(ms[j] - mx_all);
+      lsum = fmaf(ls[j], wt, lsum);
+#pragma unroll
+      for (int i = 0; i < VD; ++i) o[i] = fmaf(av[j][i], wt, o[i]);
     }
   }
+#pragma unroll
+  for (int i = 0; i < VD; ++i) out[i] = __float2bfloat16_rn(lsum > 0.f ? o[i] / lsum : 0.f);
+  __syncthreads();
   if (tid == 0) a.counters[rh] = 0u;  // ready for the next launch (graph replays)
 }
 
@@ -319,6 +336,7 @@ static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total) {
   const int64_t target = (2LL * num_sms() + groups - 1) / groups;  // splits wanted per group
   int64_t tps = std::max<int64_t>(2, (tiles + target - 1) / target);
   tps = std::min<int64_t>(tps, tiles);
+  tps = std::max<int64_t>(tps, (tiles + AT_MAX_SPLIT - 1) / AT_MAX_SPLIT);
   const int64_t ns = (tiles + tps - 1) / tps;
   return SplitPlan{(int)ns, (int)tps};
 }
@@ -346,13 +364,17 @@ extern "C" int mrb_rope_kv_append(const void* q_in, const void* k_in, const void
                                   void* v_cache, int64_t stride_page, int64_t stride_head, int64_t stride_tok,
                                   int64_t page_size, const int32_t* block_table, int64_t block_table_stride,
                                   int64_t num_pages, int32_t* error_flag, void* stream) {
-  if (tokens < 0 || hkv <= 0 || head_dim <= 0 || head_dim % 2 || page_size <= 0 || num_pages <= 0)
+  if (tokens < 0 || hkv <= 0 || head_dim <= 0 || head_dim % 4 || page_size <= 0 || num_pages <= 0)
     return fail(MRB_ERR_ARG, "rope_kv_append: bad shape");
   if (tokens == 0) return MRB_OK;
   if (!k_in || !v_in || !positions || !k_cache || !v_cache || !block_table)
     return fail(MRB_ERR_ARG, "rope_kv_append: null pointer");
   if (q_out && (!q_in || hq <= 0)) return fail(MRB_ERR_ARG, "rope_kv_append: q_out needs q_in and hq");
   if ((rope_cos == nullptr) != (rope_sin == nullptr)) return fail(MRB_ERR_ARG, "rope_kv_append: cos/sin mismatch");
+  if ((in_row_stride % 2) || (stride_page % 2) || (stride_head % 2) || (stride_tok % 2) || !aligned(k_in, 4) ||
+      !aligned(v_in, 4) || (q_in && !aligned(q_in, 4)) || !aligned(k_cache, 4) || !aligned(v_cache, 4) ||
+      (q_out && !aligned(q_out, 4)) || (rope_cos && (!aligned(rope_cos, 8) || !aligned(rope_sin, 8) || (head_dim % 4))))
+    return fail(MRB_ERR_ARG, "rope_kv_append: rows must be 4-byte aligned (8-byte tables, head_dim % 4 == 0)");
   if (tokens > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "rope_kv_append: too many tokens");
   RopeArgs a{(const __nv_bfloat16*)q_in, (const __nv_bfloat16*)k_in, (const __nv_bfloat16*)v_in, in_row_stride,
              tokens, hq, hkv, head_dim, positions, token_rows, rope_cos, rope_sin, rope_len,
@@ -405,10 +427,11 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
     a.part = (float*)((char*)workspace + AT_COUNTER_BYTES);
   }
   dim3 grid((unsigned)(rows * hkv), (unsigned)plan.nsplit);
+  const unsigned threads = (unsigned)(32 * (hq / hkv));
   if (head_dim == 128)
-    paged_attention_kernel<128><<<grid, AT_THREADS, 0, (cudaStream_t)stream>>>(a);
+    paged_attention_kernel<128><<<grid, threads, 0, (cudaStream_t)stream>>>(a);
   else
-    paged_attention_kernel<64><<<grid, AT_THREADS, 0, (cudaStream_t)stream>>>(a);
+    paged_attention_kernel<64><<<grid, threads, 0, (cudaStream_t)stream>>>(a);
   return launch_status("paged_attention");
 }
 

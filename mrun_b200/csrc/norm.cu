@@ -45,6 +45,55 @@ __global__ void __launch_bounds__(NORM_THREADS) rms_norm_kernel(const T* __restr
 
 // r = bf16(residual + update) (fp32 add), normed = bf16(RMSNorm(r) * w).
 // Follows `fused_residual_rms_norm_reference` (engine/kernels/dense_qstore_cuda.py:1390-1408).
+// One pass: each thread keeps its (up to NORM_VPT) 8-element vectors in registers.
+constexpr int NORM_VPT = 4;
+
+__global__ void __launch_bounds__(NORM_THREADS) residual_rms_norm_vec_kernel(
+    const __nv_bfloat16* res, const __nv_bfloat16* __restrict__ upd, int64_t width,
+    const float* __restrict__ w, float eps, __nv_bfloat16* res_out,  // res_out may alias res
+    __nv_bfloat16* __restrict__ normed) {
+  __shared__ float red[33];
+  const int64_t base = blockIdx.x * width;
+  const int nvec = (int)(width / 8);
+  float r[NORM_VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NORM_VPT; ++j) {
+    const int v = threadIdx.x + j * NORM_THREADS;
+    if (v < nvec) {
+      const uint4 a = *reinterpret_cast<const uint4*>(res + base + v * 8);
+      const uint4 b = *reinterpret_cast<const uint4*>(upd + base + v * 8);
+      const __nv_bfloat16* ae = reinterpret_cast<const __nv_bfloat16*>(&a);
+      const __nv_bfloat16* be = reinterpret_cast<const __nv_bfloat16*>(&b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        r[j][i] = round_bf16(__fadd_rn(__bfloat162float(ae[i]), __bfloat162float(be[i])));
+        ss = fmaf(r[j][i], r[j][i], ss);
+      }
+    }
+  }
+  const float tot = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(tot / (float)width + eps);
+#pragma unroll
+  for (int j = 0; j < NORM_VPT; ++j) {
+    const int v = threadIdx.x + j * NORM_THREADS;
+    if (v < nvec) {
+      __align__(16) __nv_bfloat16 ro[8], no[8];
+      const float4 w0 = *reinterpret_cast<const float4*>(w + v * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(w + v * 8 + 4);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ro[i] = __float2bfloat16_rn(r[j][i]);
+        no[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(r[j][i], inv), wv[i]));
+      }
+      *reinterpret_cast<uint4*>(res_out + base + v * 8) = *reinterpret_cast<const uint4*>(ro);
+      *reinterpret_cast<uint4*>(normed + base + v * 8) = *reinterpret_cast<const uint4*>(no);
+    }
+  }
+}
+
+// Scalar fallback for widths that are not a multiple of 8 or exceed the register plan.
 __global__ void __launch_bounds__(NORM_THREADS) residual_rms_norm_kernel(
     const __nv_bfloat16* res, const __nv_bfloat16* __restrict__ upd, int64_t width,
     const float* __restrict__ w, float eps, __nv_bfloat16* res_out,  // res_out may alias res
@@ -101,8 +150,15 @@ extern "C" int mrb_residual_rms_norm(const void* residual, const void* update, i
     return fail(MRB_ERR_ARG, "residual_rms_norm: null pointer");
   if (rows < 0 || width <= 0) return fail(MRB_ERR_ARG, "residual_rms_norm: bad shape");
   if (rows == 0) return MRB_OK;
-  residual_rms_norm_kernel<<<(unsigned)rows, NORM_THREADS, 0, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)residual, (const __nv_bfloat16*)update, width, weight, eps,
-      (__nv_bfloat16*)residual_out, (__nv_bfloat16*)normed_out);
+  const bool vec = width % 8 == 0 && width / 8 <= (int64_t)NORM_THREADS * NORM_VPT && aligned(residual, 16) &&
+                   aligned(update, 16) && aligned(weight, 16) && aligned(residual_out, 16) && aligned(normed_out, 16);
+  if (vec)
+    residual_rms_norm_vec_kernel<<<(unsigned)rows, NORM_THREADS, 0, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16*)residual, (const __nv_bfloat16*)update, width, weight, eps,
+        (__nv_bfloat16*)residual_out, (__nv_bfloat16*)normed_out);
+  else
+    residual_rms_norm_kernel<<<(unsigned)rows, NORM_THREADS, 0, (cudaStream_t)stream>>>(
+        (const __nv_bfloat16*)residual, (const __nv_bfloat16*)update, width, weight, eps,
+        (__nv_bfloat16*)residual_out, (__nv_bfloat16*)normed_out);
   return launch_status("residual_rms_norm");
 }

@@ -30,7 +30,7 @@ constexpr int GV_ROWS = 16;   // weight rows per CTA tile (mma M)
 constexpr int GV_KB = 64;     // k elements per lane-group block
 constexpr int GV_UNROLL = 4;  // k blocks in flight per warp
 
-enum { EPI_STORE = 0, EPI_SWIGLU = 1 };
+enum { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ARGMAX = 2 };
 
 struct GemvArgs {
   const void* x;
@@ -42,8 +42,17 @@ struct GemvArgs {
   const float* scales1;
   const float* bias;
   int64_t n;
-  void* y;
+  void* y;                       // EPI_ARGMAX: fp32 logits or null
+  int64_t semantic;              // EPI_ARGMAX: rows eligible for the argmax
+  unsigned long long* packed;    // EPI_ARGMAX: per activation row, max of pack(logit, row)
 };
+
+// Order-preserving key: larger logit -> larger key; equal logits -> the lower row wins.
+__device__ __forceinline__ unsigned long long pack_argmax(float v, int64_t row) {
+  const unsigned u = __float_as_uint(v);
+  const unsigned hi = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)hi << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)row);
+}
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
@@ -181,6 +190,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qrow_gemv_kernel(GemvArgs a) {
 
   const int64_t n = a.n;
   const int64_t ntiles = (n + GV_ROWS - 1) / GV_ROWS;
+  unsigned long long best_key = 0ull;  // EPI_ARGMAX: running max over this CTA's tiles
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const int64_t r0 = min(tile * GV_ROWS + g, n - 1);
     const int64_t r1 = min(tile * GV_ROWS + g + 8, n - 1);
@@ -262,51 +272,95 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qrow_gemv_kernel(GemvArgs a) {
         base[(g + 8) * (8 * NT) + col + 1] = acc[s][t][3];
       }
     __syncthreads();
-    for (int idx = tid; idx < GV_ROWS * M; idx += GV_THREADS) {
-      const int row = idx % GV_ROWS;
-      const int mi = idx / GV_ROWS;
+    if (EPI == EPI_ARGMAX) {
+      // all threads take part so the 16-lane shuffles are converged
+      const int row = tid % GV_ROWS, mi = tid / GV_ROWS;
       const int64_t nrow = tile * GV_ROWS + row;
-      if (nrow < n) {
-        float v[NSTREAM];
+      unsigned long long key = 0ull;
+      if (mi < M && nrow < n) {
+        float hi = 0.f, lo = 0.f;
 #pragma unroll
-        for (int s = 0; s < NSTREAM; ++s) {
-          float hi = 0.f, lo = 0.f;
-#pragma unroll
-          for (int w = 0; w < GV_WARPS; ++w) {
-            const float* base = red + ((w * NSTREAM + s) * GV_ROWS + row) * (8 * NT);
-            if (SPLIT) {
-              hi += base[2 * mi];
-              lo += base[2 * mi + 1];
-            } else {
-              hi += base[mi];
-            }
+        for (int w = 0; w < GV_WARPS; ++w) {
+          const float* base = red + (w * GV_ROWS + row) * (8 * NT);
+          if (SPLIT) {
+            hi += base[2 * mi];
+            lo += base[2 * mi + 1];
+          } else {
+            hi += base[mi];
           }
-          const float tot = SPLIT ? hi + lo * (1.0f / 2048.0f) : hi;
-          const float* sc = s == 0 ? a.scales0 : a.scales1;
-          v[s] = tot * colscale[mi] * sc[nrow];
         }
-        YT* y = reinterpret_cast<YT*>(a.y) + (int64_t)mi * n + nrow;
-        if (EPI == EPI_SWIGLU) {
-          const float gt = round_bf16(v[0]);
-          const float up = round_bf16(v[NSTREAM - 1]);
-          const float sl = round_bf16(silu_f32(gt));
-          io<YT>::store(y, sl * up);
-        } else {
-          float out = v[0];
-          if (a.bias) {
-            // The reference adds a compute-dtype bias to the compute-dtype projection.
-            YT tmp;
-            io<YT>::store(&tmp, out);
-            YT b;
-            io<YT>::store(&b, a.bias[nrow]);
-            out = io<YT>::load(&tmp) + io<YT>::load(&b);
+        const float tot = SPLIT ? hi + lo * (1.0f / 2048.0f) : hi;
+        const float v = tot * colscale[mi] * a.scales0[nrow];
+        if (a.y) reinterpret_cast<float*>(a.y)[(int64_t)mi * n + nrow] = v;
+        if (nrow < a.semantic) key = pack_argmax(v, nrow);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+      }
+      if (key > best_key) best_key = key;
+    } else {
+      for (int idx = tid; idx < GV_ROWS * M; idx += GV_THREADS) {
+        const int row = idx % GV_ROWS;
+        const int mi = idx / GV_ROWS;
+        const int64_t nrow = tile * GV_ROWS + row;
+        if (nrow < n) {
+          float v[NSTREAM];
+  #pragma unroll
+          for (int s = 0; s < NSTREAM; ++s) {
+            float hi = 0.f, lo = 0.f;
+  #pragma unroll
+            for (int w = 0; w < GV_WARPS; ++w) {
+              const float* base = red + ((w * NSTREAM + s) * GV_ROWS + row) * (8 * NT);
+              if (SPLIT) {
+                hi += base[2 * mi];
+                lo += base[2 * mi + 1];
+              } else {
+                hi += base[mi];
+              }
+            }
+            const float tot = SPLIT ? hi + lo * (1.0f / 2048.0f) : hi;
+            const float* sc = s == 0 ? a.scales0 : a.scales1;
+            v[s] = tot * colscale[mi] * sc[nrow];
           }
-          io<YT>::store(y, out);
+          YT* y = reinterpret_cast<YT*>(a.y) + (int64_t)mi * n + nrow;
+          if (EPI == EPI_SWIGLU) {
+            const float gt = round_bf16(v[0]);
+            const float up = round_bf16(v[NSTREAM - 1]);
+            const float sl = round_bf16(silu_f32(gt));
+            io<YT>::store(y, sl * up);
+          } else {
+            float out = v[0];
+            if (a.bias) {
+              // The reference adds a compute-dtype bias to the compute-dtype projection.
+              YT tmp;
+              io<YT>::store(&tmp, out);
+              YT b;
+              io<YT>::store(&b, a.bias[nrow]);
+              out = io<YT>::load(&tmp) + io<YT>::load(&b);
+            }
+            io<YT>::store(y, out);
+          }
         }
       }
     }
     __syncthreads();
   }
+  if (EPI == EPI_ARGMAX && (tid % GV_ROWS) == 0 && tid / GV_ROWS < M && best_key != 0ull)
+    atomicMax(a.packed + tid / GV_ROWS, best_key);
+}
+
+// Unpack the argmax keys into indices (int64) and logit values, in place.
+__global__ void argmax_unpack_kernel(unsigned long long* packed, float* out_value, int64_t m) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= m) return;
+  const unsigned long long key = packed[i];
+  const unsigned hi = (unsigned)(key >> 32);
+  const unsigned u = (hi & 0x80000000u) ? (hi & 0x7FFFFFFFu) : ~hi;
+  const int64_t row = (int64_t)(0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull));
+  reinterpret_cast<int64_t*>(packed)[i] = row;
+  if (out_value) out_value[i] = __uint_as_float(u);
 }
 
 // ------------------------------------------------------------------ argmax over logits
@@ -399,7 +453,8 @@ static int dispatch_nt(const GemvArgs& a, cudaStream_t s) {
     GemvArgs part = a;
     part.m = std::min<int64_t>(max_rows, a.m - r0);
     part.x = reinterpret_cast<const XT*>(a.x) + r0 * a.k;
-    part.y = reinterpret_cast<YT*>(a.y) + r0 * a.n;
+    part.y = a.y ? reinterpret_cast<YT*>(a.y) + r0 * a.n : nullptr;
+    if (a.packed) part.packed = a.packed + r0;
     const int pcols = SPLIT ? 2 * (int)part.m : (int)part.m;
     const int st = pcols <= 8 ? launch_gemv<XT, YT, SPLIT, 1, EPI>(part, s) : launch_gemv<XT, YT, SPLIT, 2, EPI>(part, s);
     if (st) return st;
@@ -431,7 +486,7 @@ constexpr int64_t GEMV_MAX_ROWS = 16;
 
 int qrow_gemv_dispatch(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* codes,
                        const float* scales, int64_t n, const float* bias, void* y, cudaStream_t s) {
-  GemvArgs a{x, m, k, codes, scales, nullptr, nullptr, bias, n, y};
+  GemvArgs a{x, m, k, codes, scales, nullptr, nullptr, bias, n, y, 0, nullptr};
   switch (x_dtype) {
     case MRB_BF16:
       if (m > GEMV_MAX_ROWS)
@@ -468,29 +523,33 @@ extern "C" int mrb_qrow_swiglu(const void* x_bf16, int64_t m, int64_t k, const i
   if (m > GEMV_MAX_ROWS)
     return qrow_gemm_swiglu_bf16((const __nv_bfloat16*)x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales,
                                  n, (__nv_bfloat16*)y_bf16, (cudaStream_t)stream);
-  GemvArgs a{x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales, nullptr, n, y_bf16};
+  GemvArgs a{x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales, nullptr, n, y_bf16, 0, nullptr};
   return dispatch_nt<__nv_bfloat16, __nv_bfloat16, false, EPI_SWIGLU>(a, (cudaStream_t)stream);
 }
 
 extern "C" int mrb_qrow_argmax(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* codes,
                                const float* scales, int64_t n, int64_t semantic_rows, float* logits,
                                int64_t* out_index, float* out_value, void* stream) {
-  int st = check_common(x, m, k, codes, scales, n, logits, "qrow_argmax");
+  int st = check_common(x, m, k, codes, scales, n, out_index, "qrow_argmax");
   if (st) return st;
-  if (!out_index) return fail(MRB_ERR_ARG, "qrow_argmax: null out_index");
   if (semantic_rows < 1 || semantic_rows > n)
     return fail(MRB_ERR_ARG, "qrow_argmax: semantic_rows %lld outside [1, %lld]", (long long)semantic_rows,
                 (long long)n);
+  if (n > 0xFFFFFFFFLL) return fail(MRB_ERR_UNSUPPORTED, "qrow_argmax: more than 2^32 rows");
   if (m == 0) return MRB_OK;
   cudaStream_t s = (cudaStream_t)stream;
-  GemvArgs a{x, m, k, codes, scales, nullptr, nullptr, nullptr, n, logits};
+  cudaError_t e = cudaMemsetAsync(out_index, 0, (size_t)m * sizeof(int64_t), s);
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "qrow_argmax: memset: %s", cudaGetErrorString(e));
+  GemvArgs a{x, m, k, codes, scales, nullptr, nullptr, nullptr, n, logits, semantic_rows,
+             reinterpret_cast<unsigned long long*>(out_index)};
   switch (x_dtype) {
-    case MRB_BF16: st = dispatch_nt<__nv_bfloat16, float, false, EPI_STORE>(a, s); break;
-    case MRB_F16: st = dispatch_nt<__half, float, false, EPI_STORE>(a, s); break;
-    case MRB_F32: st = dispatch_nt<float, float, true, EPI_STORE>(a, s); break;
+    case MRB_BF16: st = dispatch_nt<__nv_bfloat16, float, false, EPI_ARGMAX>(a, s); break;
+    case MRB_F16: st = dispatch_nt<__half, float, false, EPI_ARGMAX>(a, s); break;
+    case MRB_F32: st = dispatch_nt<float, float, true, EPI_ARGMAX>(a, s); break;
     default: return fail(MRB_ERR_ARG, "qrow_argmax: bad x_dtype %d", x_dtype);
   }
   if (st) return st;
-  argmax_rows_kernel<<<(unsigned)m, 1024, 0, s>>>(logits, n, semantic_rows, out_index, out_value);
+  argmax_unpack_kernel<<<(unsigned)((m + 127) / 128), 128, 0, s>>>(reinterpret_cast<unsigned long long*>(out_index),
+                                                                    out_value, m);
   return launch_status("qrow_argmax");
 }

@@ -213,7 +213,6 @@ class DenseDecoder:
             "mlp": torch.empty(rows, cfg.ffn, dtype=bf, device=device),
         }
         b = self.max_batch
-        self.logits = torch.empty(b, cfg.vocab, dtype=torch.float32, device=device)
         self.next_ids = torch.zeros(b, dtype=torch.int64, device=device)
         self.next_val = torch.zeros(b, dtype=torch.float32, device=device)
         # decode-step state (device-resident so a captured graph can advance itself)
@@ -280,8 +279,8 @@ class DenseDecoder:
         normed = self._layers(n, positions, token_rows, row_len, start + n, last_only=True)
         self.kv.lengths[seq] = start + n
         idx, _, _ = qrow_argmax(self.w.head.codes, self.w.head.scales, normed[n - 1 : n],
-                                logits=self.logits[:1], out_index=self.next_ids[seq : seq + 1],
-                                out_value=self.next_val[seq : seq + 1])
+                                out_index=self.next_ids[seq : seq + 1], out_value=self.next_val[seq : seq + 1],
+                                store_logits=False)
         return idx[0]
 
     # ------------------------------------------------------------------ decode
@@ -292,8 +291,8 @@ class DenseDecoder:
         embed_rows(self.w.embed.codes, self.w.embed.scales, self.in_ids[:rows], out=self.buf["hidden"][:rows])
         normed = self._layers(rows, self.positions[:rows], self.row_seq[:rows], self.row_len[:rows],
                               self.max_seq_len, last_only=False)
-        qrow_argmax(self.w.head.codes, self.w.head.scales, normed, logits=self.logits[:rows],
-                    out_index=self.next_ids[:rows], out_value=self.next_val[:rows])
+        qrow_argmax(self.w.head.codes, self.w.head.scales, normed, out_index=self.next_ids[:rows],
+                    out_value=self.next_val[:rows], store_logits=False)
         _lib.call("mrb_decode_advance", self.next_ids.data_ptr(), self.in_ids.data_ptr(),
                   self.positions.data_ptr(), self.row_len.data_ptr(), rows, _lib.stream_handle(self.device))
         del cfg
@@ -325,7 +324,8 @@ class DenseDecoder:
             self._decode_body(rows)
         self.graph = graph
         self.graph_rows = rows
-        self.launches_per_step = 3 + 8 * self.cfg.num_layers + 2  # embed, norm, 8/layer, head x2, advance
+        # embed, norm, 8 per layer, head (memset + GEMV + unpack), advance
+        self.launches_per_step = 2 + 8 * self.cfg.num_layers + 3 + 1
 
     def step(self) -> None:
         """Advance every captured row by one greedy token (graph replay, no host sync)."""

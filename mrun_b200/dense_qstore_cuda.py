@@ -325,14 +325,18 @@ def qrow_argmax(
     logits: torch.Tensor | None = None,
     out_index: torch.Tensor | None = None,
     out_value: torch.Tensor | None = None,
-) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Exact fp32 head logits and their first maximal index (lowest index on ties)."""
+    store_logits: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """Exact fp32 head logits and their first maximal index (lowest index on ties).
+
+    The argmax is fused into the head GEMV (no logits pass); ``store_logits=False`` also
+    skips writing the logits."""
     vocab, in_features = (int(v) for v in codes.shape)
     device = _lib.require_cuda(codes, scales, activations, what="qrow argmax head")
     flat = _rows(activations, in_features)
     rows = int(flat.shape[0])
     semantic = vocab if semantic_rows is None else int(semantic_rows)
-    if logits is None:
+    if logits is None and store_logits:
         logits = torch.empty((rows, vocab), device=device, dtype=torch.float32)
     if out_index is None:
         out_index = torch.empty((rows,), device=device, dtype=torch.int64)
@@ -348,12 +352,12 @@ def qrow_argmax(
         scales.data_ptr(),
         vocab,
         semantic,
-        logits.data_ptr(),
+        _lib.ptr(logits if store_logits else None),
         out_index.data_ptr(),
         out_value.data_ptr(),
         _lib.stream_handle(device),
     )
-    return out_index, out_value, logits
+    return out_index, out_value, logits if store_logits else None
 
 
 @torch.inference_mode()
