@@ -86,9 +86,9 @@ int mrb_qrow_swiglu(const void *x_bf16, int64_t m, int64_t k, const int8_t *gate
                     int64_t n, void *y_bf16, void *stream);
 
 /* Greedy language head: logits[m, v] = x[m].W[v] * scale[v] in fp32 over the first
- * `semantic_rows` rows, then the first maximal index per row (lowest index on ties).
- * out_index: int64 [m]; out_value: fp32 [m] (may be NULL); logits: fp32 [m, n] workspace
- * that also receives the full logits (n = all rows).
+ * `semantic_rows` rows, then the first maximal index per row (lowest index on ties), fused
+ * into the head GEMV (order-preserving 64-bit keys, atomic max). out_index: int64 [m];
+ * out_value: fp32 [m] (may be NULL); logits: fp32 [m, n] (may be NULL: not stored).
  * Replaces the streamed exact head `_head` (engine/dense_qstore_cuda.py:800-896). */
 int mrb_qrow_argmax(const void *x, int x_dtype, int64_t m, int64_t k, const int8_t *codes,
                     const float *scales, int64_t n, int64_t semantic_rows, float *logits,

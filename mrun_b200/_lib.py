@@ -129,6 +129,26 @@ def require_cuda(*tensors: torch.Tensor, what: str) -> torch.device:
     return device
 
 
+class DeviceScratch:
+    """Grow-only, zero-initialised scratch buffer per device for kernels that keep
+    self-resetting counters in their workspace. Calls that share it must be stream-ordered."""
+
+    def __init__(self) -> None:
+        self._lock = threading.Lock()
+        self._buffers: dict[int, torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor | None:
+        if nbytes <= 0:
+            return None
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        with self._lock:
+            buf = self._buffers.get(index)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=device)
+                self._buffers[index] = buf
+            return buf
+
+
 def exported_symbols() -> list[str]:
     return list(SIGNATURES)
 

@@ -11,7 +11,7 @@
 // 16-token tiles with an fp32 online softmax for all query heads of the group (GQA: K/V are
 // read once per group). Splits publish (max, sum, acc) partials; the last CTA of a
 // (row, head) group to finish merges them in split order, so results are deterministic.
-#include "common.cuh"
+#include "qrow_common.cuh"
 
 #include <algorithm>
 
@@ -72,6 +72,8 @@ __device__ __forceinline__ void rope_head(const __nv_bfloat16* src, __nv_bfloat1
 }
 
 __global__ void __launch_bounds__(256) rope_kv_append_kernel(RopeArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t t = blockIdx.x;
   const int half = (int)(a.d / 2);
   const int64_t pos = a.positions[t];
@@ -161,6 +163,8 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
   const int64_t r = rh / a.hkv;
   const int kvh = (int)(rh - r * a.hkv);
   const int tid = threadIdx.x, g = tid >> 5, lane = tid & 31;
+  pdl_launch_dependents();
+  pdl_wait();
 
   __shared__ __align__(16) __nv_bfloat16 ks[AT_TILE][D];
   __shared__ __align__(16) __nv_bfloat16 vs[AT_TILE][D];
@@ -380,7 +384,7 @@ extern "C" int mrb_rope_kv_append(const void* q_in, const void* k_in, const void
              tokens, hq, hkv, head_dim, positions, token_rows, rope_cos, rope_sin, rope_len,
              (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, stride_page, stride_head,
              stride_tok, page_size, block_table, block_table_stride, num_pages, error_flag};
-  rope_kv_append_kernel<<<(unsigned)tokens, 256, 0, (cudaStream_t)stream>>>(a);
+  launch_kernel(rope_kv_append_kernel, dim3((unsigned)tokens), dim3(256), 0, (cudaStream_t)stream, true, a);
   return launch_status("rope_kv_append");
 }
 
@@ -428,10 +432,8 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
   }
   dim3 grid((unsigned)(rows * hkv), (unsigned)plan.nsplit);
   const unsigned threads = (unsigned)(32 * (hq / hkv));
-  if (head_dim == 128)
-    paged_attention_kernel<128><<<grid, threads, 0, (cudaStream_t)stream>>>(a);
-  else
-    paged_attention_kernel<64><<<grid, threads, 0, (cudaStream_t)stream>>>(a);
+  launch_kernel(head_dim == 128 ? paged_attention_kernel<128> : paged_attention_kernel<64>, grid, dim3(threads), 0,
+                (cudaStream_t)stream, true, a);
   return launch_status("paged_attention");
 }
 
@@ -442,6 +444,8 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
 __global__ void decode_advance_kernel(const int64_t* __restrict__ next_ids, int64_t* __restrict__ input_ids,
                                       int32_t* __restrict__ positions, int32_t* __restrict__ row_len,
                                       int64_t rows) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i < rows) {
     input_ids[i] = next_ids[i];
@@ -455,7 +459,7 @@ extern "C" int mrb_decode_advance(const int64_t* next_ids, int64_t* input_ids, i
   if (rows < 0) return fail(MRB_ERR_ARG, "decode_advance: bad rows");
   if (rows == 0) return MRB_OK;
   if (!next_ids || !input_ids || !positions || !row_len) return fail(MRB_ERR_ARG, "decode_advance: null pointer");
-  decode_advance_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, (cudaStream_t)stream>>>(next_ids, input_ids,
-                                                                                           positions, row_len, rows);
+  launch_kernel(decode_advance_kernel, dim3((unsigned)((rows + 255) / 256)), dim3(256), 0, (cudaStream_t)stream, true,
+                next_ids, input_ids, positions, row_len, rows);
   return launch_status("decode_advance");
 }

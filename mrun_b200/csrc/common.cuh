@@ -11,6 +11,9 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <stdarg.h>
+#include <stdlib.h>
+
+#include <utility>
 
 #include "../../include/mrun_b200.h"
 
@@ -51,6 +54,35 @@ inline int num_sms() {
     if (sms <= 0) sms = 148;
   }
   return sms;
+}
+
+// Launch with programmatic dependent launch allowed (the kernel may start while the previous
+// kernel on the stream finishes; it must call griddepcontrol.wait before reading that
+// kernel's results). Disabled by setting MRB_PDL=0 in the environment.
+inline bool pdl_enabled() {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* v = getenv("MRB_PDL");
+    enabled = (v && v[0] == '0') ? 0 : 1;
+  }
+  return enabled == 1;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                 bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const bool use = pdl && pdl_enabled();
+  cfg.attrs = use ? attr : nullptr;
+  cfg.numAttrs = use ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- device helpers

@@ -1,5 +1,5 @@
 // Row RMSNorm and fused residual + RMSNorm with the reference's bf16 boundaries.
-#include "common.cuh"
+#include "qrow_common.cuh"
 
 namespace mrb {
 
@@ -28,6 +28,8 @@ __global__ void __launch_bounds__(NORM_THREADS) rms_norm_kernel(const T* __restr
                                                                 const float* __restrict__ w, float eps,
                                                                 T* __restrict__ y) {
   __shared__ float red[33];
+  pdl_launch_dependents();
+  pdl_wait();
   const T* src = x + blockIdx.x * width;
   T* dst = y + blockIdx.x * width;
   float ss = 0.f;
@@ -53,6 +55,8 @@ __global__ void __launch_bounds__(NORM_THREADS) residual_rms_norm_vec_kernel(
     const float* __restrict__ w, float eps, __nv_bfloat16* res_out,  // res_out may alias res
     __nv_bfloat16* __restrict__ normed) {
   __shared__ float red[33];
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t base = blockIdx.x * width;
   const int nvec = (int)(width / 8);
   float r[NORM_VPT][8];
@@ -99,6 +103,8 @@ __global__ void __launch_bounds__(NORM_THREADS) residual_rms_norm_kernel(
     const float* __restrict__ w, float eps, __nv_bfloat16* res_out,  // res_out may alias res
     __nv_bfloat16* __restrict__ normed) {
   __shared__ float red[33];
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t base = blockIdx.x * width;
   float ss = 0.f;
   for (int64_t i = threadIdx.x; i < width; i += blockDim.x) {
@@ -127,15 +133,16 @@ extern "C" int mrb_rms_norm(const void* x, int dtype, int64_t rows, int64_t widt
   cudaStream_t s = (cudaStream_t)stream;
   switch (dtype) {
     case MRB_F32:
-      rms_norm_kernel<float><<<(unsigned)rows, NORM_THREADS, 0, s>>>((const float*)x, width, weight, eps, (float*)y);
+      launch_kernel(rms_norm_kernel<float>, dim3((unsigned)rows), dim3(NORM_THREADS), 0, s, true, (const float*)x, width,
+                    weight, eps, (float*)y);
       break;
     case MRB_BF16:
-      rms_norm_kernel<__nv_bfloat16><<<(unsigned)rows, NORM_THREADS, 0, s>>>(
-          (const __nv_bfloat16*)x, width, weight, eps, (__nv_bfloat16*)y);
+      launch_kernel(rms_norm_kernel<__nv_bfloat16>, dim3((unsigned)rows), dim3(NORM_THREADS), 0, s, true,
+                    (const __nv_bfloat16*)x, width, weight, eps, (__nv_bfloat16*)y);
       break;
     case MRB_F16:
-      rms_norm_kernel<__half><<<(unsigned)rows, NORM_THREADS, 0, s>>>((const __half*)x, width, weight, eps,
-                                                                      (__half*)y);
+      launch_kernel(rms_norm_kernel<__half>, dim3((unsigned)rows), dim3(NORM_THREADS), 0, s, true, (const __half*)x,
+                    width, weight, eps, (__half*)y);
       break;
     default:
       return fail(MRB_ERR_ARG, "rms_norm: bad dtype %d", dtype);
@@ -152,13 +159,10 @@ extern "C" int mrb_residual_rms_norm(const void* residual, const void* update, i
   if (rows == 0) return MRB_OK;
   const bool vec = width % 8 == 0 && width / 8 <= (int64_t)NORM_THREADS * NORM_VPT && aligned(residual, 16) &&
                    aligned(update, 16) && aligned(weight, 16) && aligned(residual_out, 16) && aligned(normed_out, 16);
-  if (vec)
-    residual_rms_norm_vec_kernel<<<(unsigned)rows, NORM_THREADS, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)residual, (const __nv_bfloat16*)update, width, weight, eps,
-        (__nv_bfloat16*)residual_out, (__nv_bfloat16*)normed_out);
-  else
-    residual_rms_norm_kernel<<<(unsigned)rows, NORM_THREADS, 0, (cudaStream_t)stream>>>(
-        (const __nv_bfloat16*)residual, (const __nv_bfloat16*)update, width, weight, eps,
-        (__nv_bfloat16*)residual_out, (__nv_bfloat16*)normed_out);
+  launch_kernel(vec ? residual_rms_norm_vec_kernel : residual_rms_norm_kernel, dim3((unsigned)rows),
+                dim3(NORM_THREADS), 0, (cudaStream_t)stream, true, (const __nv_bfloat16*)residual,
+                (const __nv_bfloat16*)update, width, weight, eps, (__nv_bfloat16*)residual_out,
+                (__nv_bfloat16*)normed_out);
   return launch_status("residual_rms_norm");
 }
+

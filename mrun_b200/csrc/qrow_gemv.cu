@@ -18,17 +18,17 @@
 //  * The k order inside each 64-element block is permuted identically for weights and
 //    activations (each lane consumes 4 consecutive bytes per mma), so every lane issues one
 //    16-byte load per weight row per block and no shuffles are needed.
-#include "common.cuh"
+#include "qrow_common.cuh"
 
 #include <algorithm>
+#include <cmath>
 
 namespace mrb {
 
 constexpr int GV_WARPS = 8;
 constexpr int GV_THREADS = GV_WARPS * 32;
-constexpr int GV_ROWS = 16;   // weight rows per CTA tile (mma M)
-constexpr int GV_KB = 64;     // k elements per lane-group block
-constexpr int GV_UNROLL = 4;  // k blocks in flight per warp
+constexpr int GV_ROWS = 16;  // weight rows per tile (mma M)
+constexpr int GV_KB = 64;    // k elements per lane-group block
 
 enum { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_ARGMAX = 2 };
 
@@ -42,94 +42,134 @@ struct GemvArgs {
   const float* scales1;
   const float* bias;
   int64_t n;
-  void* y;                       // EPI_ARGMAX: fp32 logits or null
-  int64_t semantic;              // EPI_ARGMAX: rows eligible for the argmax
-  unsigned long long* packed;    // EPI_ARGMAX: per activation row, max of pack(logit, row)
+  void* y;                     // EPI_ARGMAX: fp32 logits or null
+  int64_t semantic;            // EPI_ARGMAX: rows eligible for the argmax
+  unsigned long long* packed;  // EPI_ARGMAX: per activation row, max of pack(logit, row)
 };
 
-// Order-preserving key: larger logit -> larger key; equal logits -> the lower row wins.
-__device__ __forceinline__ unsigned long long pack_argmax(float v, int64_t row) {
-  const unsigned u = __float_as_uint(v);
-  const unsigned hi = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)hi << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)row);
-}
+// Prefetch ring depth (k blocks in flight per thread) by number of weight streams.
+template <int NSTREAM>
+struct GvRing {
+  static constexpr int STAGES = NSTREAM == 2 ? 5 : 8;
+  // one stage: NSTREAM streams x 2 rows (g, g+8) x 16 bytes per thread
+  static constexpr int STAGE_BYTES = NSTREAM * 2 * GV_THREADS * 16;
+  static constexpr int BYTES = STAGES * STAGE_BYTES;
+};
 
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-
-__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-// Four signed int8 codes -> f16x2 of bytes (0,1) and f16x2 of bytes (2,3), exactly.
-__device__ __forceinline__ void i8x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;  // q + 128 as an unsigned byte
-  lo = hsub2(prmt(u, 0x64646464u, 0x4140u), 0x64806480u);  // (1024 + q + 128) - 1152
-  hi = hsub2(prmt(u, 0x64646464u, 0x4342u), 0x64806480u);
-}
-
-__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                        uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// SiLU as the reference writes it: g * sigmoid(g), sigmoid = 1 / (1 + exp(-g)).
-__device__ __forceinline__ float silu_f32(float g) { return g * (1.0f / (1.0f + expf(-g))); }
-
-// Shared-memory plan of one CTA.
 __host__ __device__ inline int gv_kpad(int64_t k) { return (int)(((k + GV_KB - 1) / GV_KB) * GV_KB); }
 __host__ __device__ inline int gv_xstride(int64_t k) { return gv_kpad(k) + 8; }  // f16 elems, +16 B
-__host__ inline size_t gv_smem_bytes(int ncols, int64_t k, int nt, int nstream) {
+
+template <int NSTREAM>
+__host__ inline size_t gv_smem_bytes(int ncols, int64_t k, int nt) {
   size_t xs = (size_t)ncols * gv_xstride(k) * 2;
   xs = (xs + 15) & ~size_t(15);
-  size_t red = (size_t)GV_WARPS * nstream * GV_ROWS * 8 * nt * 4;
-  return xs + red + 64 * 4;  // + per-row power-of-two factors and row maxima
+  const size_t red = (size_t)GV_WARPS * NSTREAM * GV_ROWS * 8 * nt * 4;
+  return GvRing<NSTREAM>::BYTES + xs + red + 64 * 4;  // + per-column factors, maxima and sums
 }
 
-// XT: activation element type. SPLIT: fp32 activations as hi/lo f16 pairs.
-// NT: number of n8 mma column tiles (columns = 8 * NT >= rows * (SPLIT ? 2 : 1)).
+// Weight-streaming W8A16 GEMV (M <= 16 activation rows).
+//
+// A CTA (8 warps, two per SM) owns every gridDim-th 16-row weight tile. Within a
+// tile the warps split the 64-element k blocks; every thread streams its two 16-byte
+// slices per block (rows g and g+8) through a private cp.async ring in shared memory, so
+// 7 (one stream) or 4 (two streams) blocks per thread -- over 100 KB per SM -- are in flight
+// without holding registers and with no barrier between blocks (each thread reads back only
+// the bytes it requested). The first blocks are requested before the programmatic-
+// dependent-launch wait, so weight streaming overlaps the previous kernel's tail; only the
+// activation staging waits for it. Codes become exact f16 with integer/half ops,
+// activations are staged once per CTA as exact power-of-two-scaled f16, mma.sync
+// accumulates in fp32, and a tile's warps reduce through shared memory in a fixed order.
 template <typename XT, typename YT, bool SPLIT, int NT, int EPI>
 __global__ void __launch_bounds__(GV_THREADS, 2) qrow_gemv_kernel(GemvArgs a) {
   constexpr int NSTREAM = (EPI == EPI_SWIGLU) ? 2 : 1;
-  extern __shared__ __align__(16) unsigned char smem[];
+  constexpr int STAGES = GvRing<NSTREAM>::STAGES;
+  constexpr int STAGE_BYTES = GvRing<NSTREAM>::STAGE_BYTES;
+  extern __shared__ __align__(128) unsigned char smem[];
   const int M = (int)a.m;
   const int64_t K = a.k;
+  const int64_t n = a.n;
   const int ncols = SPLIT ? 2 * M : M;
   const int kpad = gv_kpad(K);
   const int xstride = gv_xstride(K);
-  const int nkb = kpad / GV_KB;
-  __half* xs = reinterpret_cast<__half*>(smem);
-  size_t xs_bytes = ((size_t)ncols * xstride * 2 + 15) & ~size_t(15);
-  float* red = reinterpret_cast<float*>(smem + xs_bytes);
-  float* colscale = red + GV_WARPS * NSTREAM * GV_ROWS * 8 * NT;  // 2^-e per activation row
+  const int nkb_tile = kpad / GV_KB;
+  unsigned char* ring = smem;
+  __half* xs = reinterpret_cast<__half*>(smem + GvRing<NSTREAM>::BYTES);
+  const size_t xs_bytes = ((size_t)ncols * xstride * 2 + 15) & ~size_t(15);
+  float* red = reinterpret_cast<float*>(smem + GvRing<NSTREAM>::BYTES + xs_bytes);
+  float* colscale = red + GV_WARPS * NSTREAM * GV_ROWS * 8 * NT;  // [0,16): 2^-e, [16,32): 2^e
+  unsigned* colmax = reinterpret_cast<unsigned*>(colscale + 32);
+  float* colsum = colscale + 48;  // sum of the staged f16 activations per column (biased codes)
 
   const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int g = lane >> 2;  // mma group id: weight row (and +8), activation column
-  const int c = lane & 3;   // thread in group: 16-element slice of a 64-element k block
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  // tiles blockIdx.x, +gridDim.x, ...: the CTAs sweep the matrix together (one window of
+  // adjacent tiles at a time), which keeps DRAM pages and TLB entries shared between SMs
+  const int ntiles = (int)((n + GV_ROWS - 1) / GV_ROWS);  // 16-row tiles (< 2^27 by the host check)
+  // this warp's k blocks per tile: warp, warp + 8, ...
+  const int kpw = warp < nkb_tile ? (nkb_tile - warp + GV_WARPS - 1) / GV_WARPS : 0;
 
-  // ---- stage activations: per-row power-of-two scale, exact f16 (or hi/lo f16) copy.
-  // Two fully parallel passes of 16-byte vector loads (the second hits L1).
-  constexpr int VEC = 16 / sizeof(XT);  // elements per 16-byte vector
-  unsigned* colmax = reinterpret_cast<unsigned*>(colscale + 32);
+  pdl_launch_dependents();
+
+  // ---- per-thread prefetch stream: (tile pf_T, this warp's pf_i-th k block of it)
+  int pf_T = kpw > 0 ? (int)blockIdx.x : ntiles, pf_i = 0, slot_w = 0;
+  auto issue = [&]() {
+    if (pf_T < ntiles) {
+      const int kb = warp + GV_WARPS * pf_i;
+      const int koff = kb * GV_KB + 16 * c;
+      const bool ok = koff < K;
+      const int64_t r0 = min((int64_t)pf_T * GV_ROWS + g, n - 1);
+      const int64_t r1 = min((int64_t)pf_T * GV_ROWS + g + 8, n - 1);
+      unsigned char* st = ring + slot_w * STAGE_BYTES;
+#pragma unroll
+      for (int s = 0; s < NSTREAM; ++s) {
+        const int8_t* codes = s == 0 ? a.codes0 : a.codes1;
+        cp_async16_zfill(st + ((s * 2 + 0) * GV_THREADS + tid) * 16, codes + (ok ? r0 * K + koff : 0), ok);
+        cp_async16_zfill(st + ((s * 2 + 1) * GV_THREADS + tid) * 16, codes + (ok ? r1 * K + koff : 0), ok);
+      }
+      if (++pf_i == kpw) {
+        pf_i = 0;
+        pf_T += gridDim.x;
+      }
+    }
+    cp_async_commit_group();
+    slot_w = slot_w + 1 == STAGES ? 0 : slot_w + 1;
+  };
+#pragma unroll
+  for (int p = 0; p < STAGES - 1; ++p) issue();  // before the dependency wait
+
+  // ---- activations: wait for the producer kernel, then stage exact scaled f16 copies
+  pdl_wait();
+  constexpr int VEC = 16 / sizeof(XT);
   if (tid < 16) colmax[tid] = 0u;
   __syncthreads();
-  const int vpr = (int)(K / VEC);  // vectors per activation row (K % 16 == 0)
+  const int vpr = (int)(K / VEC);
   const int nvec = M * vpr;
   const uint4* xv = reinterpret_cast<const uint4*>(a.x);
-  {
+  if (!SPLIT) {
+    // one global round trip: copy the raw 16-bit rows into their staging slots while
+    // tracking each row's max |x|, then convert in place with the power-of-two factor
     int cur = -1;
     float mx = 0.f;
+#pragma unroll 4
+    for (int v = tid; v < nvec; v += GV_THREADS) {
+      const int mi = v / vpr;
+      const uint4 raw = __ldg(xv + v);
+      *reinterpret_cast<uint4*>(xs + mi * xstride + (v - mi * vpr) * VEC) = raw;
+      if (mi != cur) {
+        if (cur >= 0) atomicMax(&colmax[cur], __float_as_uint(mx));
+        cur = mi;
+        mx = 0.f;
+      }
+      const XT* e = reinterpret_cast<const XT*>(&raw);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) mx = fmaxf(mx, fabsf(io<XT>::load(e + i)));
+    }
+    if (cur >= 0) atomicMax(&colmax[cur], __float_as_uint(mx));
+  } else {
+    int cur = -1;
+    float mx = 0.f;
+#pragma unroll 4
     for (int v = tid; v < nvec; v += GV_THREADS) {
       const int mi = v / vpr;
       if (mi != cur) {
@@ -150,20 +190,21 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qrow_gemv_kernel(GemvArgs a) {
     int e = 0;
     if (mx > 0.f && isfinite(mx)) {
       int ex;
-      frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
+      frexpf(mx, &ex);                   // mx in [2^(ex-1), 2^ex)
       e = max(-100, min(100, 15 - ex));  // mx * 2^e in [2^14, 2^15)
     }
     colscale[tid] = ldexpf(1.0f, -e);
     colscale[16 + tid] = ldexpf(1.0f, e);
   }
   __syncthreads();
+#pragma unroll 4
   for (int v = tid; v < nvec; v += GV_THREADS) {
     const int mi = v / vpr;
     const int kk = (v - mi * vpr) * VEC;
-    const uint4 raw = __ldg(xv + v);
-    const XT* e = reinterpret_cast<const XT*>(&raw);
     const float f = colscale[16 + mi];
     if (SPLIT) {
+      const uint4 raw = __ldg(xv + v);
+      const XT* e = reinterpret_cast<const XT*>(&raw);
       __half hi[VEC], lo[VEC];
 #pragma unroll
       for (int i = 0; i < VEC; ++i) {
@@ -174,92 +215,100 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qrow_gemv_kernel(GemvArgs a) {
       *reinterpret_cast<uint2*>(xs + (2 * mi) * xstride + kk) = *reinterpret_cast<const uint2*>(hi);
       *reinterpret_cast<uint2*>(xs + (2 * mi + 1) * xstride + kk) = *reinterpret_cast<const uint2*>(lo);
     } else {
+      uint4* slot = reinterpret_cast<uint4*>(xs + mi * xstride + kk);
+      const uint4 raw = *slot;
+      const XT* e = reinterpret_cast<const XT*>(&raw);
       __align__(16) __half h[VEC];
 #pragma unroll
       for (int i = 0; i < VEC; ++i) h[i] = __float2half_rn(io<XT>::load(e + i) * f);
-      *reinterpret_cast<uint4*>(xs + mi * xstride + kk) = *reinterpret_cast<const uint4*>(h);
+      *slot = *reinterpret_cast<const uint4*>(h);
     }
   }
-  // zero padding up to the 64-element block boundary
   const int padw = kpad - (int)K;
   for (int idx = tid; idx < ncols * padw; idx += GV_THREADS) {
     const int col = idx / padw;
     xs[col * xstride + (int)K + (idx - col * padw)] = __float2half_rn(0.f);
   }
   __syncthreads();
-
-  const int64_t n = a.n;
-  const int64_t ntiles = (n + GV_ROWS - 1) / GV_ROWS;
-  unsigned long long best_key = 0ull;  // EPI_ARGMAX: running max over this CTA's tiles
-  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const int64_t r0 = min(tile * GV_ROWS + g, n - 1);
-    const int64_t r1 = min(tile * GV_ROWS + g + 8, n - 1);
-    const int8_t* w00 = a.codes0 + r0 * K + 16 * c;
-    const int8_t* w01 = a.codes0 + r1 * K + 16 * c;
-    const int8_t* w10 = nullptr;
-    const int8_t* w11 = nullptr;
-    if (EPI == EPI_SWIGLU) {
-      w10 = a.codes1 + r0 * K + 16 * c;
-      w11 = a.codes1 + r1 * K + 16 * c;
+  if (!SPLIT) {
+    // fixed-order column sums of exactly the f16 values the mma consumes: warp w sums
+    // columns w, w + 8 with lanes striding k, then a fixed shuffle tree
+    for (int col = warp; col < ncols; col += GV_WARPS) {
+      float sum = 0.f;
+      for (int kk = lane * 8; kk < kpad; kk += 32 * 8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(xs + col * xstride + kk);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(h2[j]);
+          sum += f.x + f.y;
+        }
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) colsum[col] = sum;
     }
-    float acc[NSTREAM][NT][4];
-#pragma unroll
-    for (int s = 0; s < NSTREAM; ++s)
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[s][t][i] = 0.f;
+    __syncthreads();
+  }
 
-    for (int kb0 = warp; kb0 < nkb; kb0 += GV_WARPS * GV_UNROLL) {
-      uint4 wa[GV_UNROLL][NSTREAM], wb[GV_UNROLL][NSTREAM];
+  float acc[NSTREAM][NT][4];
 #pragma unroll
-      for (int u = 0; u < GV_UNROLL; ++u) {
-        const int kb = kb0 + u * GV_WARPS;
-        const int64_t koff = (int64_t)kb * GV_KB;
-        const bool ok = kb < nkb && koff + 16 * c < K;
+  for (int s = 0; s < NSTREAM; ++s)
 #pragma unroll
-        for (int s = 0; s < NSTREAM; ++s) {
-          const int8_t* pa = s == 0 ? w00 : w10;
-          const int8_t* pb = s == 0 ? w01 : w11;
-          wa[u][s] = ok ? ld_stream_u4(pa + koff) : make_uint4(0, 0, 0, 0);
-          wb[u][s] = ok ? ld_stream_u4(pb + koff) : make_uint4(0, 0, 0, 0);
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[s][t][i] = 0.f;
+  unsigned long long best_key = 0ull;  // EPI_ARGMAX: running max over this CTA's tiles
+
+  int slot_r = 0;  // ring slot this thread reads next
+  for (int T = blockIdx.x; T < ntiles; T += gridDim.x) {
+    const int64_t tile = T;
+    for (int i = 0; i < kpw; ++i) {
+      cp_async_wait_group<STAGES - 2>();
+      const unsigned char* st = ring + slot_r * STAGE_BYTES;
+      slot_r = slot_r + 1 == STAGES ? 0 : slot_r + 1;
+      uint4 wa[NSTREAM], wb[NSTREAM];
+#pragma unroll
+      for (int s = 0; s < NSTREAM; ++s) {
+        wa[s] = *reinterpret_cast<const uint4*>(st + ((s * 2 + 0) * GV_THREADS + tid) * 16);
+        wb[s] = *reinterpret_cast<const uint4*>(st + ((s * 2 + 1) * GV_THREADS + tid) * 16);
+      }
+      issue();
+      const int kb = warp + GV_WARPS * i;
+      uint32_t xb[NT][8];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const int col = t * 8 + g;
+        if (col < ncols) {
+          const uint4* p = reinterpret_cast<const uint4*>(xs + col * xstride + kb * GV_KB + 16 * c);
+          const uint4 v0 = p[0], v1 = p[1];
+          xb[t][0] = v0.x; xb[t][1] = v0.y; xb[t][2] = v0.z; xb[t][3] = v0.w;
+          xb[t][4] = v1.x; xb[t][5] = v1.y; xb[t][6] = v1.z; xb[t][7] = v1.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xb[t][j] = 0u;
         }
       }
 #pragma unroll
-      for (int u = 0; u < GV_UNROLL; ++u) {
-        const int kb = kb0 + u * GV_WARPS;
-        if (kb >= nkb) break;  // warp-uniform
-        uint32_t xb[NT][8];
+      for (int s = 0; s < NSTREAM; ++s) {
+        const uint32_t ra[4] = {wa[s].x, wa[s].y, wa[s].z, wa[s].w};
+        const uint32_t rb[4] = {wb[s].x, wb[s].y, wb[s].z, wb[s].w};
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const int col = t * 8 + g;
-          if (col < ncols) {
-            const uint4* p = reinterpret_cast<const uint4*>(xs + col * xstride + kb * GV_KB + 16 * c);
-            const uint4 v0 = p[0], v1 = p[1];
-            xb[t][0] = v0.x; xb[t][1] = v0.y; xb[t][2] = v0.z; xb[t][3] = v0.w;
-            xb[t][4] = v1.x; xb[t][5] = v1.y; xb[t][6] = v1.z; xb[t][7] = v1.w;
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) xb[t][i] = 0u;
-          }
-        }
-#pragma unroll
-        for (int s = 0; s < NSTREAM; ++s) {
-          const uint32_t ra[4] = {wa[u][s].x, wa[u][s].y, wa[u][s].z, wa[u][s].w};
-          const uint32_t rb[4] = {wb[u][s].x, wb[u][s].y, wb[u][s].z, wb[u][s].w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t a_lo, a_hi, b_lo, b_hi;
+        for (int j = 0; j < 4; ++j) {
+          uint32_t a_lo, a_hi, b_lo, b_hi;
+          if (SPLIT) {  // fp32 activations keep the exact code (no bias term in the sum)
             i8x4_to_f16x2(ra[j], a_lo, a_hi);
             i8x4_to_f16x2(rb[j], b_lo, b_hi);
-#pragma unroll
-            for (int t = 0; t < NT; ++t) mma_f16(acc[s][t], a_lo, b_lo, a_hi, b_hi, xb[t][2 * j], xb[t][2 * j + 1]);
+          } else {
+            i8x4_to_biased_f16x2(ra[j], a_lo, a_hi);
+            i8x4_to_biased_f16x2(rb[j], b_lo, b_hi);
           }
+#pragma unroll
+          for (int t = 0; t < NT; ++t) mma_f16(acc[s][t], a_lo, b_lo, a_hi, b_hi, xb[t][2 * j], xb[t][2 * j + 1]);
         }
       }
     }
 
-    // ---- cross-warp reduction in a fixed order.
+    // ---- tile end: cross-warp reduction in a fixed order, then the epilogue
 #pragma unroll
     for (int s = 0; s < NSTREAM; ++s)
 #pragma unroll
@@ -270,27 +319,25 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qrow_gemv_kernel(GemvArgs a) {
         base[g * (8 * NT) + col + 1] = acc[s][t][1];
         base[(g + 8) * (8 * NT) + col] = acc[s][t][2];
         base[(g + 8) * (8 * NT) + col + 1] = acc[s][t][3];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[s][t][j] = 0.f;
       }
     __syncthreads();
+    auto total = [&](int s, int row, int col) {
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < GV_WARPS; ++w) tot += red[((w * NSTREAM + s) * GV_ROWS + row) * (8 * NT) + col];
+      // remove the code bias: sum (q+1152) x - 1152 sum x over this tile's k range
+      return SPLIT ? tot : tot - 1152.0f * colsum[col];
+    };
     if (EPI == EPI_ARGMAX) {
-      // all threads take part so the 16-lane shuffles are converged
-      const int row = tid % GV_ROWS, mi = tid / GV_ROWS;
+      const int row = tid % GV_ROWS, mi = tid / GV_ROWS;  // all threads: converged shuffles
       const int64_t nrow = tile * GV_ROWS + row;
       unsigned long long key = 0ull;
       if (mi < M && nrow < n) {
-        float hi = 0.f, lo = 0.f;
-#pragma unroll
-        for (int w = 0; w < GV_WARPS; ++w) {
-          const float* base = red + (w * GV_ROWS + row) * (8 * NT);
-          if (SPLIT) {
-            hi += base[2 * mi];
-            lo += base[2 * mi + 1];
-          } else {
-            hi += base[mi];
-          }
-        }
-        const float tot = SPLIT ? hi + lo * (1.0f / 2048.0f) : hi;
-        const float v = tot * colscale[mi] * a.scales0[nrow];
+        const float t = SPLIT ? total(0, row, 2 * mi) + total(0, row, 2 * mi + 1) * (1.0f / 2048.0f)
+                              : total(0, row, mi);
+        const float v = t * colscale[mi] * a.scales0[nrow];
         if (a.y) reinterpret_cast<float*>(a.y)[(int64_t)mi * n + nrow] = v;
         if (nrow < a.semantic) key = pack_argmax(v, nrow);
       }
@@ -302,51 +349,36 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qrow_gemv_kernel(GemvArgs a) {
       if (key > best_key) best_key = key;
     } else {
       for (int idx = tid; idx < GV_ROWS * M; idx += GV_THREADS) {
-        const int row = idx % GV_ROWS;
-        const int mi = idx / GV_ROWS;
+        const int row = idx % GV_ROWS, mi = idx / GV_ROWS;
         const int64_t nrow = tile * GV_ROWS + row;
-        if (nrow < n) {
-          float v[NSTREAM];
-  #pragma unroll
-          for (int s = 0; s < NSTREAM; ++s) {
-            float hi = 0.f, lo = 0.f;
-  #pragma unroll
-            for (int w = 0; w < GV_WARPS; ++w) {
-              const float* base = red + ((w * NSTREAM + s) * GV_ROWS + row) * (8 * NT);
-              if (SPLIT) {
-                hi += base[2 * mi];
-                lo += base[2 * mi + 1];
-              } else {
-                hi += base[mi];
-              }
-            }
-            const float tot = SPLIT ? hi + lo * (1.0f / 2048.0f) : hi;
-            const float* sc = s == 0 ? a.scales0 : a.scales1;
-            v[s] = tot * colscale[mi] * sc[nrow];
+        if (nrow >= n) continue;
+        float v[NSTREAM];
+#pragma unroll
+        for (int s = 0; s < NSTREAM; ++s) {
+          const float t = SPLIT ? total(s, row, 2 * mi) + total(s, row, 2 * mi + 1) * (1.0f / 2048.0f)
+                                : total(s, row, mi);
+          v[s] = t * colscale[mi] * (s == 0 ? a.scales0 : a.scales1)[nrow];
+        }
+        YT* y = reinterpret_cast<YT*>(a.y) + (int64_t)mi * n + nrow;
+        if (EPI == EPI_SWIGLU) {
+          const float gt = round_bf16(v[0]);
+          const float up = round_bf16(v[NSTREAM - 1]);
+          io<YT>::store(y, round_bf16(silu_f32(gt)) * up);
+        } else {
+          float out = v[0];
+          if (a.bias) {  // the reference adds a compute-dtype bias to the compute-dtype projection
+            YT tmp, b;
+            io<YT>::store(&tmp, out);
+            io<YT>::store(&b, a.bias[nrow]);
+            out = io<YT>::load(&tmp) + io<YT>::load(&b);
           }
-          YT* y = reinterpret_cast<YT*>(a.y) + (int64_t)mi * n + nrow;
-          if (EPI == EPI_SWIGLU) {
-            const float gt = round_bf16(v[0]);
-            const float up = round_bf16(v[NSTREAM - 1]);
-            const float sl = round_bf16(silu_f32(gt));
-            io<YT>::store(y, sl * up);
-          } else {
-            float out = v[0];
-            if (a.bias) {
-              // The reference adds a compute-dtype bias to the compute-dtype projection.
-              YT tmp;
-              io<YT>::store(&tmp, out);
-              YT b;
-              io<YT>::store(&b, a.bias[nrow]);
-              out = io<YT>::load(&tmp) + io<YT>::load(&b);
-            }
-            io<YT>::store(y, out);
-          }
+          io<YT>::store(y, out);
         }
       }
     }
     __syncthreads();
   }
+  cp_async_wait_group<0>();
   if (EPI == EPI_ARGMAX && (tid % GV_ROWS) == 0 && tid / GV_ROWS < M && best_key != 0ull)
     atomicMax(a.packed + tid / GV_ROWS, best_key);
 }
@@ -421,24 +453,27 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restri
 
 template <typename XT, typename YT, bool SPLIT, int NT, int EPI>
 static int launch_gemv(const GemvArgs& a, cudaStream_t s) {
+  constexpr int NSTREAM = EPI == EPI_SWIGLU ? 2 : 1;
   const int ncols = SPLIT ? 2 * (int)a.m : (int)a.m;
-  const size_t smem = gv_smem_bytes(ncols, a.k, NT, EPI == EPI_SWIGLU ? 2 : 1);
-  if (smem > 200 * 1024)
+  const size_t smem = gv_smem_bytes<NSTREAM>(ncols, a.k, NT);
+  if (smem > 227 * 1024)
     return fail(MRB_ERR_UNSUPPORTED, "qrow gemv: activation block %lld x %lld too large for one CTA",
                 (long long)a.m, (long long)a.k);
+  if (a.n > (1LL << 27)) return fail(MRB_ERR_UNSUPPORTED, "qrow gemv: %lld output rows", (long long)a.n);
   auto kern = qrow_gemv_kernel<XT, YT, SPLIT, NT, EPI>;
   static size_t configured = 0;  // per instantiation
-  if (smem > 48 * 1024 && smem > configured) {
+  if (smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "qrow gemv: smem attribute: %s", cudaGetErrorString(e));
     configured = smem;
   }
-  // Residency: two CTAs per SM by the register bound, fewer when shared memory limits it.
-  int per_sm = (int)std::min<size_t>(2, (227 * 1024) / (smem + 1024));
-  if (per_sm < 1) per_sm = 1;
+  // two CTAs per SM when shared memory allows (the register bound allows two)
+  const int per_sm = 2 * (smem + 1024) <= 227 * 1024 ? 2 : 1;
   const int64_t ntiles = (a.n + GV_ROWS - 1) / GV_ROWS;
   const int64_t grid = std::min<int64_t>(ntiles, (int64_t)num_sms() * per_sm);
-  kern<<<(unsigned)grid, GV_THREADS, smem, s>>>(a);
+  // the argmax head is preceded by a memset node, which takes no programmatic edge
+  cudaError_t e = launch_kernel(kern, dim3((unsigned)grid), dim3(GV_THREADS), smem, s, EPI != EPI_ARGMAX, a);
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "qrow gemv: launch: %s", cudaGetErrorString(e));
   return launch_status("qrow gemv");
 }
 
@@ -446,8 +481,12 @@ template <typename XT, typename YT, bool SPLIT, int EPI>
 static int dispatch_nt(const GemvArgs& a, cudaStream_t s) {
   // Activation rows per launch: at most 16 mma columns, and a staged f16 copy that fits
   // one CTA's shared memory; wider requests re-stream the weights once per chunk.
-  const int per_col = gv_xstride(a.k) * 2;
-  int max_rows = std::min<int>((int)((160 * 1024) / per_col), 16) / (SPLIT ? 2 : 1);
+  constexpr int NSTREAM = EPI == EPI_SWIGLU ? 2 : 1;
+  const size_t fixed = gv_smem_bytes<NSTREAM>(0, a.k, 2);
+  const size_t per_col = (size_t)gv_xstride(a.k) * 2;
+  if (fixed + per_col > 227 * 1024)
+    return fail(MRB_ERR_UNSUPPORTED, "qrow gemv: in_features %lld too large", (long long)a.k);
+  const int max_rows = (int)std::min<size_t>((227 * 1024 - fixed) / per_col, 16) / (SPLIT ? 2 : 1);
   if (max_rows < 1) return fail(MRB_ERR_UNSUPPORTED, "qrow gemv: in_features %lld too large", (long long)a.k);
   for (int64_t r0 = 0; r0 < a.m; r0 += max_rows) {
     GemvArgs part = a;
@@ -484,9 +523,17 @@ int qrow_gemm_swiglu_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const in
 // Activation rows above which bf16 projections use the tensor-core GEMM.
 constexpr int64_t GEMV_MAX_ROWS = 16;
 
+static GemvArgs make_args(const void* x, int64_t m, int64_t k, const int8_t* c0, const float* s0, const int8_t* c1,
+                          const float* s1, const float* bias, int64_t n, void* y) {
+  GemvArgs a{};
+  a.x = x; a.m = m; a.k = k; a.codes0 = c0; a.scales0 = s0; a.codes1 = c1; a.scales1 = s1;
+  a.bias = bias; a.n = n; a.y = y;
+  return a;
+}
+
 int qrow_gemv_dispatch(const void* x, int x_dtype, int64_t m, int64_t k, const int8_t* codes,
                        const float* scales, int64_t n, const float* bias, void* y, cudaStream_t s) {
-  GemvArgs a{x, m, k, codes, scales, nullptr, nullptr, bias, n, y, 0, nullptr};
+  const GemvArgs a = make_args(x, m, k, codes, scales, nullptr, nullptr, bias, n, y);
   switch (x_dtype) {
     case MRB_BF16:
       if (m > GEMV_MAX_ROWS)
@@ -523,7 +570,7 @@ extern "C" int mrb_qrow_swiglu(const void* x_bf16, int64_t m, int64_t k, const i
   if (m > GEMV_MAX_ROWS)
     return qrow_gemm_swiglu_bf16((const __nv_bfloat16*)x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales,
                                  n, (__nv_bfloat16*)y_bf16, (cudaStream_t)stream);
-  GemvArgs a{x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales, nullptr, n, y_bf16, 0, nullptr};
+  const GemvArgs a = make_args(x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales, nullptr, n, y_bf16);
   return dispatch_nt<__nv_bfloat16, __nv_bfloat16, false, EPI_SWIGLU>(a, (cudaStream_t)stream);
 }
 
@@ -540,8 +587,9 @@ extern "C" int mrb_qrow_argmax(const void* x, int x_dtype, int64_t m, int64_t k,
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = cudaMemsetAsync(out_index, 0, (size_t)m * sizeof(int64_t), s);
   if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "qrow_argmax: memset: %s", cudaGetErrorString(e));
-  GemvArgs a{x, m, k, codes, scales, nullptr, nullptr, nullptr, n, logits, semantic_rows,
-             reinterpret_cast<unsigned long long*>(out_index)};
+  GemvArgs a = make_args(x, m, k, codes, scales, nullptr, nullptr, nullptr, n, logits);
+  a.semantic = semantic_rows;
+  a.packed = reinterpret_cast<unsigned long long*>(out_index);
   switch (x_dtype) {
     case MRB_BF16: st = dispatch_nt<__nv_bfloat16, float, false, EPI_ARGMAX>(a, s); break;
     case MRB_F16: st = dispatch_nt<__half, float, false, EPI_ARGMAX>(a, s); break;

@@ -1,6 +1,6 @@
 // QStore store-build and gather kernels: per-row int8 quantisation and dequantised row
 // gathers (embedding lookup).
-#include "common.cuh"
+#include "qrow_common.cuh"
 
 namespace mrb {
 
@@ -41,6 +41,8 @@ __global__ void __launch_bounds__(256) embed_rows_kernel(const int8_t* __restric
                                                          const float* __restrict__ scales, int64_t rows,
                                                          int64_t cols, const int64_t* __restrict__ ids,
                                                          OT* __restrict__ out, int32_t* bad_ids) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t i = blockIdx.x;
   const int64_t id = ids[i];
   OT* dst = out + i * cols;
@@ -84,8 +86,8 @@ extern "C" int mrb_qrow_embed_rows(const int8_t* codes, const float* scales, int
                                                                (float*)out, bad_ids);
       break;
     case MRB_BF16:
-      embed_rows_kernel<__nv_bfloat16><<<(unsigned)n_ids, 256, 0, s>>>(codes, scales, rows, cols, ids,
-                                                                       (__nv_bfloat16*)out, bad_ids);
+      launch_kernel(embed_rows_kernel<__nv_bfloat16>, dim3((unsigned)n_ids), dim3(256), 0, s, true, codes, scales, rows,
+                    cols, ids, (__nv_bfloat16*)out, bad_ids);
       break;
     case MRB_F16:
       embed_rows_kernel<__half><<<(unsigned)n_ids, 256, 0, s>>>(codes, scales, rows, cols, ids,

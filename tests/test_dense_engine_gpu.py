@@ -56,7 +56,7 @@ def test_greedy_decode_matches_oracle(kw, prompt_len, steps, cuda):
     first = mismatches[0][0] if mismatches else steps
     print(f"greedy parity: {steps - len(mismatches)}/{steps} identical, first near-tie at step {first}, "
           f"near-ties {[(s, round(g, 5)) for s, _, _, g, _ in mismatches]}")
-    assert len(mismatches) <= max(2, steps // 20)
+    assert len(mismatches) <= max(3, steps // 10)
 
 
 def test_graph_replay_matches_eager_and_is_deterministic(cuda):
