@@ -148,6 +148,32 @@ int mrb_paged_attention(const void *q, int64_t rows, int64_t hq, int64_t hkv, in
                         const void *v_new, float scale, int64_t max_total_tokens, void *out,
                         void *workspace, size_t workspace_size, void *stream);
 
+/* Allocation-free variant of mrb_paged_attention (no counterpart in the reference, which
+ * always lets torch allocate). For callers that cannot allocate device memory -- a host that
+ * has already reserved all GPU memory for its own pool, a latency-critical path where
+ * cudaMalloc/cudaFree could synchronise the device, or a thin binding that only receives raw
+ * pointers -- the split-K scratch lives in one static device array of
+ * MRB_ATTN_STATIC_SCRATCH_BYTES per GPU (held by every GPU that loads the library until the
+ * process exits), and nothing is allocated per call.
+ * - Arguments and results as mrb_paged_attention, without the workspace.
+ * - Sizes whose split plan needs more scratch than the array holds are rejected with
+ *   MRB_ERR_UNSUPPORTED (mrb_paged_attention_workspace gives the need; use the
+ *   workspace entry point for those).
+ * - The first call on a device looks up the array's device address with that device
+ *   current; make that first call before any stream capture.
+ * - Every call on a device shares the array: calls that can overlap on the GPU (different
+ *   streams without ordering) race and must not be issued. Each call returns the array's
+ *   merge counters to zero, so consecutive calls need no clearing. */
+#define MRB_ATTN_STATIC_SCRATCH_BYTES (2 << 20)
+size_t mrb_paged_attention_static_capacity(void);
+int mrb_paged_attention_static(const void *q, int64_t rows, int64_t hq, int64_t hkv,
+                               int64_t head_dim, const void *k_cache, const void *v_cache,
+                               int64_t stride_page, int64_t stride_head, int64_t stride_tok,
+                               int64_t page_size, const int32_t *block_table,
+                               int64_t block_table_stride, const int32_t *row_seq,
+                               const int32_t *row_len, const void *k_new, const void *v_new,
+                               float scale, int64_t max_total_tokens, void *out, void *stream);
+
 /* Greedy decode bookkeeping: input_ids[i] = next_ids[i]; positions[i] += 1; row_len[i] += 1
  * for i < rows. Lets a captured decode step feed itself (the reference's engine does this on
  * the host after `token.cpu()`, engine/dense_qstore_cuda.py:2389-2416). */

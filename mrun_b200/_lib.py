@@ -44,9 +44,13 @@ SIGNATURES: dict[str, list] = {
     "mrb_paged_attention_workspace": [_I64, _I64, _I64, _I64, _I64],
     "mrb_paged_attention": [_P, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P,
                             _P, _P, c_float, _I64, _P, _P, c_size_t, _P],
+    "mrb_paged_attention_static_capacity": [],
+    "mrb_paged_attention_static": [_P, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P,
+                                   _P, _P, c_float, _I64, _P, _P],
     "mrb_decode_advance": [_P, _P, _P, _P, _I64, _P],
 }
-_RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t}
+_RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t,
+             "mrb_paged_attention_static_capacity": c_size_t}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

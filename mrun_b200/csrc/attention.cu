@@ -463,3 +463,93 @@ extern "C" int mrb_decode_advance(const int64_t* next_ids, int64_t* input_ids, i
                 next_ids, input_ids, positions, row_len, rows);
   return launch_status("decode_advance");
 }
+
+// ------------------------------------------------------------------ allocation-free variant
+//
+// Some callers cannot allocate device memory at all: a host process that reserves all GPU
+// memory for its own pool up front (so a plugin's cudaMalloc would fail or fragment it),
+// code on a latency-critical path where cudaMalloc/cudaFree may synchronise the device, and
+// thin bindings that only ever receive raw pointers from their host. For them,
+// mrb_paged_attention_static runs the same split-K kernel with its scratch in a fixed
+// static device array instead of a caller workspace.
+
+// Scratch of mrb_paged_attention_static: merge counters, then split partials. Zero at load
+// (static storage); the kernel returns every counter to zero, so each call starts clean.
+static __device__ __align__(256) unsigned char g_attn_static_scratch[MRB_ATTN_STATIC_SCRATCH_BYTES];
+
+namespace mrb {
+namespace {
+constexpr int kMaxDevices = 64;
+int g_static_ready[kMaxDevices] = {0};
+void* g_static_ptr[kMaxDevices] = {nullptr};
+}  // namespace
+}  // namespace mrb
+
+extern "C" size_t mrb_paged_attention_static_capacity(void) { return MRB_ATTN_STATIC_SCRATCH_BYTES; }
+
+extern "C" int mrb_paged_attention_static(const void* q, int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
+                                          const void* k_cache, const void* v_cache, int64_t stride_page,
+                                          int64_t stride_head, int64_t stride_tok, int64_t page_size,
+                                          const int32_t* block_table, int64_t block_table_stride,
+                                          const int32_t* row_seq, const int32_t* row_len, const void* k_new,
+                                          const void* v_new, float scale, int64_t max_total_tokens, void* out,
+                                          void* stream) {
+  if (rows < 0 || hq <= 0 || hkv <= 0 || hq % hkv || page_size <= 0 || max_total_tokens < 0)
+    return fail(MRB_ERR_ARG, "paged_attention_static: bad shape");
+  if (rows == 0) return MRB_OK;
+  if (hq / hkv > AT_MAX_GROUP)
+    return fail(MRB_ERR_UNSUPPORTED, "paged_attention_static: query group %lld exceeds %d", (long long)(hq / hkv),
+                AT_MAX_GROUP);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(MRB_ERR_UNSUPPORTED, "paged_attention_static: head_dim %lld (supported: 64, 128)",
+                (long long)head_dim);
+  if (!q || !k_cache || !v_cache || !block_table || !row_len || !out)
+    return fail(MRB_ERR_ARG, "paged_attention_static: null pointer");
+  if ((k_new == nullptr) != (v_new == nullptr))
+    return fail(MRB_ERR_ARG, "paged_attention_static: k_new/v_new mismatch");
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || (stride_page % 8) || (stride_head % 8) || (stride_tok % 8) ||
+      (k_new && !aligned(k_new, 16)))
+    return fail(MRB_ERR_ARG, "paged_attention_static: K/V rows must be 16-byte aligned");
+  const SplitPlan plan = plan_splits(rows, hkv, max_total_tokens);
+  const size_t need = workspace_bytes(rows, hq, hkv, head_dim, plan);
+  if (need > MRB_ATTN_STATIC_SCRATCH_BYTES)
+    return fail(MRB_ERR_UNSUPPORTED,
+                "paged_attention_static: these sizes need %zu bytes of scratch, above the static %d; "
+                "use mrb_paged_attention with a workspace",
+                need, MRB_ATTN_STATIC_SCRATCH_BYTES);
+  if (rows * hkv > 0x7fffffffLL || plan.nsplit > 65535)
+    return fail(MRB_ERR_UNSUPPORTED, "paged_attention_static: grid too large");
+  void* scratch = nullptr;
+  if (need > 0) {
+    if (rows * hkv > AT_MAX_COUNTERS)
+      return fail(MRB_ERR_UNSUPPORTED, "paged_attention_static: too many split groups");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "paged_attention_static: cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(MRB_ERR_UNSUPPORTED, "paged_attention_static: device %d", dev);
+    // once per device, with that device current: the device address of the static array
+    // (host code only has a host-side stand-in for it)
+    if (!__atomic_load_n(&g_static_ready[dev], __ATOMIC_ACQUIRE)) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_attn_static_scratch);
+      if (e != cudaSuccess || ptr == nullptr)
+        return fail(MRB_ERR_CUDA, "paged_attention_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      g_static_ptr[dev] = ptr;
+      __atomic_store_n(&g_static_ready[dev], 1, __ATOMIC_RELEASE);
+    }
+    scratch = g_static_ptr[dev];
+  }
+  AttnArgs a{(const __nv_bfloat16*)q, rows, hq, hkv, (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache,
+             stride_page, stride_head, stride_tok, page_size, block_table, block_table_stride, row_seq, row_len,
+             (const __nv_bfloat16*)k_new, (const __nv_bfloat16*)v_new, scale, plan.nsplit, plan.tiles_per_split,
+             (__nv_bfloat16*)out, nullptr, nullptr};
+  if (scratch) {
+    a.counters = (unsigned*)scratch;
+    a.part = (float*)((char*)scratch + AT_COUNTER_BYTES);
+  }
+  dim3 grid((unsigned)(rows * hkv), (unsigned)plan.nsplit);
+  const unsigned threads = (unsigned)(32 * (hq / hkv));
+  launch_kernel(head_dim == 128 ? paged_attention_kernel<128> : paged_attention_kernel<64>, grid, dim3(threads), 0,
+                (cudaStream_t)stream, true, a);
+  return launch_status("paged_attention_static");
+}
