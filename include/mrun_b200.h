@@ -106,6 +106,40 @@ int mrb_residual_rms_norm(const void *residual_bf16, const void *update_bf16, in
                           void *normed_out, void *stream);
 
 
+/* ---------------------------------------------------------------- (a) W8A8 */
+
+/* Per-token dynamic int8 activations exactly as the reference quantises them:
+ * act_scale[r] = max|x[r] * keep| / 127 (fp32 division, 0 -> 1),
+ * qx = clamp(round_half_even(x * keep / act_scale), -127, 127). keep (fp32 [k]) may be NULL.
+ * Replaces the activation step of `w8a8_matmul` (engine/kernels/w8a8.py:117-121). */
+int mrb_w8a8_quantize(const void *x, int x_dtype, int64_t m, int64_t k, const float *keep,
+                      int8_t *qx, float *act_scale, void *stream);
+
+/* acc[m, n] = sum_k qx[m, k] * qw[n, k] in int32, exact (k % 16 == 0, k <= 133000).
+ * Replaces `_int8_gemm` (engine/kernels/w8a8.py:33-64). */
+int mrb_int8_gemm(const int8_t *qx, const int8_t *qw, int64_t m, int64_t n, int64_t k,
+                  int32_t *acc, void *stream);
+
+/* Outlier columns: the `topk` columns with the largest max|x| over all rows (ties -> lower
+ * column), written to idx_out, with keep[col] = 0 for them and 1 elsewhere.
+ * Replaces the protect_k selection of `w8a8_matmul` (engine/kernels/w8a8.py:98-105). */
+int mrb_w8a8_protect_topk(const void *x, int x_dtype, int64_t m, int64_t k, int topk,
+                          int64_t *idx_out, float *keep, void *stream);
+
+/* y[m, n] = side + (float(acc) * act_scale[m]) * w_scale[n] with acc the exact int32 dot of
+ * the quantised activations and codes; side is the fp32 path of the `nprotect` protected
+ * columns (0 when nprotect == 0, making y bit-identical to the reference). keep: the mask
+ * from mrb_w8a8_protect_topk (or any 0/1 mask matching protect_idx). acc_out (int32 [m, n])
+ * may be NULL. Workspaces: qx_ws int8 [m, k] and scale_ws fp32 [m] (needed unless the
+ * decode GEMV takes the call: m <= 16 and the int8 row block fits one CTA; scale_ws also
+ * receives the activation scales there when given), side_ws fp32 [m, n]
+ * (needed when nprotect > 0).
+ * Replaces `w8a8_matmul` (engine/kernels/w8a8.py:67-125). */
+int mrb_w8a8_matmul(const void *x, int x_dtype, int64_t m, int64_t k, const int8_t *qw,
+                    const float *w_scale, int64_t n, const int64_t *protect_idx, int nprotect,
+                    const float *keep, float *y, int32_t *acc_out, int8_t *qx_ws, float *scale_ws,
+                    float *side_ws, void *stream);
+
 /* ---------------------------------------------------------------- (c) paged-KV decode attention */
 
 /* RoPE (rotate-half, fp32 products rounded separately, then bf16) for the queries and keys of

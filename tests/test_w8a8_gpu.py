@@ -1,0 +1,84 @@
+"""W8A8 parity: int32 accumulators and activation codes bit-exact, outputs bit-identical to
+the reference (no protected columns) and within 1e-4 (fp32) with protected columns."""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import w8a8 as ow8
+from oracle.numerics import max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_config1_w8a8_bit_exact(golden, cuda):
+    from mrun_b200.qstore_build import quant_row_int8
+    from mrun_b200.w8a8 import quantize_activations, w8a8_matmul
+
+    g = golden("config1")
+    torch.manual_seed(0)
+    x = torch.randn(8, 2048)
+    w = torch.randn(2048, 2048) * 0.02
+    q, s = quant_row_int8(w.to(cuda))
+    qx, scale = quantize_activations(x.to(cuda))
+    np.testing.assert_array_equal(qx.cpu().numpy(), g["qx"])
+    np.testing.assert_array_equal(scale.cpu().numpy(), g["act_scale"])
+    acc = torch.empty(8, 2048, dtype=torch.int32, device=cuda)
+    y = w8a8_matmul(q, s, x.to(cuda), acc_out=acc)
+    assert _sha(acc.cpu().numpy()) == str(g["acc_sha"])
+    np.testing.assert_array_equal(y.cpu().numpy(), g["y_w8a8"])
+
+
+def test_reference_w8a8_fixture(golden, cuda):
+    from mrun_b200.w8a8 import _int8_gemm, w8a8_matmul
+
+    g = golden("w8a8")
+    qw = torch.from_numpy(g["q_w"]).to(cuda)
+    sw = torch.from_numpy(g["sc_w"]).to(cuda)
+    x = torch.from_numpy(g["x"]).to(cuda)
+    np.testing.assert_array_equal(w8a8_matmul(qw, sw, x, protect_k=0).cpu().numpy(), g["y_k0"])
+    y4 = w8a8_matmul(qw, sw, x, protect_k=4).cpu().numpy()
+    assert max_rel_err(y4, g["y_k4"]) < 1e-4
+    np.testing.assert_array_equal(_int8_gemm(torch.from_numpy(g["gemm_qx"]).to(cuda), qw).cpu().numpy(), g["gemm_acc"])
+
+
+@pytest.mark.parametrize("m", [1, 5, 16, 17, 64, 300])
+@pytest.mark.parametrize("n,k", [(512, 3584), (4608, 3584), (3584, 18944)])
+def test_w8a8_gemv_and_gemm_bit_exact(m, n, k, cuda):
+    from mrun_b200.w8a8 import w8a8_matmul
+
+    if m == 300 and k == 18944:
+        pytest.skip("oracle int64 matmul too slow at this size")
+    gen = torch.Generator().manual_seed(m + n + k)
+    qw = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    sw = torch.rand(n, generator=gen) * 0.01
+    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    acc = torch.empty(m, n, dtype=torch.int32, device=cuda)
+    y = w8a8_matmul(qw.to(cuda), sw.to(cuda), x.to(cuda), acc_out=acc).cpu().numpy()
+    xf = x.float().numpy()
+    qx, act = ow8.quantize_activations(xf)
+    ref_acc = ow8.int8_gemm(qx, qw.numpy())
+    np.testing.assert_array_equal(acc.cpu().numpy(), ref_acc)
+    np.testing.assert_array_equal(y, ow8.w8a8_matmul(qw.numpy(), sw.numpy(), xf))
+
+
+def test_protect_topk_matches_oracle(cuda):
+    from mrun_b200.w8a8 import w8a8_matmul
+
+    gen = torch.Generator().manual_seed(9)
+    qw = torch.randint(-127, 128, (128, 256), generator=gen, dtype=torch.int8)
+    sw = torch.rand(128, generator=gen) * 0.02 + 1e-3
+    x = torch.randn(8, 256, generator=gen)
+    x[:, torch.randperm(256, generator=gen)[:4]] *= 300.0
+    y = w8a8_matmul(qw.to(cuda), sw.to(cuda), x.to(cuda), protect_k=8).cpu().numpy()
+    ref = ow8.w8a8_matmul(qw.numpy(), sw.numpy(), x.numpy(), protect_k=8)
+    assert max_rel_err(y, ref) < 1e-5
+    exact = x.numpy().astype(np.float64) @ (qw.numpy().astype(np.float64) * sw.numpy()[:, None]).T
+    assert np.array_equal(y.argmax(-1), exact.argmax(-1))
