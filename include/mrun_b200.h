@@ -140,6 +140,47 @@ int mrb_w8a8_matmul(const void *x, int x_dtype, int64_t m, int64_t k, const int8
                     const float *keep, float *y, int32_t *acc_out, int8_t *qx_ws, float *scale_ws,
                     float *side_ws, void *stream);
 
+/* ---------------------------------------------------------------- (b) routed MoE */
+
+/* Router: probabilities = softmax(fp32(logits)) per token (max-subtracted, divided by the
+ * sum), the k largest (ties -> lower expert) in descending order, optionally renormalised
+ * by their fp32 sum; weights also rounded to bf16 (top_w_f32 / top_w_bf16 may be NULL).
+ * logits_dtype in {F32, BF16}; experts <= 256; k <= 16.
+ * Replaces the router of `Qwen3MoeDecodeRuntime.forward` (engine/qwen3_moe_cuda.py:3700-3707). */
+int mrb_router_topk(const void *logits, int logits_dtype, int64_t tokens, int64_t experts, int64_t k,
+                    int renorm, int64_t *top_idx, float *top_w_f32, void *top_w_bf16, void *stream);
+
+/* Route plan: counts/starts per expert (exclusive scan), expert-major token_ids and
+ * coefficients in the stable order of the reference's CPU branch (argsort by expert,
+ * stable: flat (token, rank) order inside each expert), and inverse[token*k + rank] = the
+ * assignment's expert-major position. Deterministic: no atomic decides a position.
+ * Expert ids outside [0, experts) set *error_flag (may be NULL) and are skipped.
+ * experts <= 512. Replaces `grouped_route_tensors_with_inverse` (engine/olmoe_cuda.py:989-1135). */
+int mrb_route_compile(const int64_t *top_idx, const float *top_w, int64_t tokens, int64_t k,
+                      int64_t experts, int32_t *counts, int32_t *starts, int64_t *token_ids,
+                      float *coef, int64_t *inverse, int32_t *error_flag, void *stream);
+
+/* Grouped W8A16 expert projection over ragged per-expert row groups: for expert e, rows
+ * [starts[e], starts[e] + counts[e]) of the output are x[row_ids[a]] (row_ids NULL: a) times
+ * the expert's int8 codes (slot slot_of[e], NULL: e, at codes + slot * codes_stride bytes;
+ * fp32 row scales at scales + slot * scales_stride floats), fp32 accumulation, bf16 output
+ * [A, n]. swiglu: the page's rows [0, n) are gate rows and [up_rows, up_rows + n) up rows,
+ * and the output is bf16(bf16(silu(bf16 g)) * bf16 u) as the reference forms it.
+ * Replaces the grouped expert GEMMs of `PagedFP8ExpertBackend.moe`
+ * (engine/qwen3_moe_cuda.py:2740-2761), with the int8 qrow codec. */
+int mrb_grouped_qrow(const void *x_bf16, const int64_t *row_ids, const int32_t *starts,
+                     const int32_t *counts, int64_t experts, const int8_t *codes,
+                     int64_t codes_stride, const float *scales, int64_t scales_stride,
+                     const int32_t *slot_of, int64_t n, int64_t k, int64_t up_rows, int swiglu,
+                     void *y_bf16, void *stream);
+
+/* Weighted combine in route-rank order: out[t] = sum_r coef[p] * expert_out[p] with
+ * p = inverse[t*k + r], fp32 products summed left to right; fp32 and/or bf16 outputs.
+ * Replaces `stable_route_reduce` (engine/qwen3_moe_cuda.py:2561-2664). */
+int mrb_stable_route_reduce(const void *expert_out_bf16, const float *coef, const int64_t *inverse,
+                            int64_t tokens, int64_t k, int64_t hidden, float *out_f32,
+                            void *out_bf16, void *stream);
+
 /* ---------------------------------------------------------------- (c) paged-KV decode attention */
 
 /* RoPE (rotate-half, fp32 products rounded separately, then bf16) for the queries and keys of

@@ -1,0 +1,321 @@
+"""Routed-MoE chain on B200: router top-k, route compiler, grouped int8 expert MLP, stable
+combine, and the ``.moe`` backend protocol of mrun's Qwen3-MoE engine.
+
+Reference interfaces mirrored here (same names and argument meaning):
+  * ``grouped_route_tensors`` / ``grouped_route_tensors_with_inverse`` (engine/olmoe_cuda.py:1092-1135)
+  * ``stable_route_reduce`` (engine/qwen3_moe_cuda.py:2561-2664)
+  * ``ExpertPageLayout`` (engine/qwen3_moe_cuda.py:187-231)
+  * backend ``.moe(layer, source, top_indices, top_weights, *, prefill)`` / ``.report()`` /
+    ``.reset_stats(clear_pages=)`` (engine/qwen3_moe_cuda.py:2698-2822)
+Expert weights use the int8 qrow codec (per-output-channel scales) instead of the
+reference's FP8/int4 pages; every computation runs in libmrun_b200.so.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+from . import _lib
+
+PAGE_ALIGNMENT = 4096
+
+
+def align_up(value: int, alignment: int = PAGE_ALIGNMENT) -> int:
+    return (value + alignment - 1) // alignment * alignment
+
+
+@dataclass(frozen=True)
+class ExpertPageLayout:
+    """One expert's page: gate_up codes [2F, H] | gate_up scales [2F] fp32 | down codes
+    [H, F] | down scales [H] fp32, padded to 4 KiB (the reference's page layout with the
+    int8 qrow codec)."""
+
+    hidden_size: int
+    intermediate_size: int
+    gate_up_codes_offset: int
+    gate_up_codes_bytes: int
+    gate_up_scales_offset: int
+    gate_up_scales_bytes: int
+    down_codes_offset: int
+    down_codes_bytes: int
+    down_scales_offset: int
+    down_scales_bytes: int
+    page_stride: int
+
+    @classmethod
+    def create(cls, hidden_size: int, intermediate_size: int) -> "ExpertPageLayout":
+        gate_up_rows = 2 * intermediate_size
+        gu_codes = gate_up_rows * hidden_size
+        gu_scales_off = align_up(gu_codes, 16)
+        gu_scales = gate_up_rows * 4
+        down_off = align_up(gu_scales_off + gu_scales, 16)
+        down_codes = hidden_size * intermediate_size
+        down_scales_off = align_up(down_off + down_codes, 16)
+        down_scales = hidden_size * 4
+        return cls(
+            hidden_size=hidden_size,
+            intermediate_size=intermediate_size,
+            gate_up_codes_offset=0,
+            gate_up_codes_bytes=gu_codes,
+            gate_up_scales_offset=gu_scales_off,
+            gate_up_scales_bytes=gu_scales,
+            down_codes_offset=down_off,
+            down_codes_bytes=down_codes,
+            down_scales_offset=down_scales_off,
+            down_scales_bytes=down_scales,
+            page_stride=align_up(down_scales_off + down_scales),
+        )
+
+    def as_dict(self) -> dict[str, int]:
+        return {name: int(getattr(self, name)) for name in self.__dataclass_fields__}
+
+
+def pack_expert_page(layout: ExpertPageLayout, gate_up_codes, gate_up_scales, down_codes, down_scales,
+                     out: torch.Tensor) -> None:
+    """Write one expert's tensors into a uint8 page (device or pinned host)."""
+    ly = layout
+
+    def put(offset: int, tensor: torch.Tensor) -> None:
+        raw = tensor.contiguous().view(torch.uint8).reshape(-1)
+        out[offset : offset + raw.numel()].copy_(raw)
+
+    put(ly.gate_up_codes_offset, gate_up_codes)
+    put(ly.gate_up_scales_offset, gate_up_scales)
+    put(ly.down_codes_offset, down_codes)
+    put(ly.down_scales_offset, down_scales)
+
+
+def expert_page_views(layout: ExpertPageLayout, page: torch.Tensor):
+    """(gate_up codes, gate_up scales, down codes, down scales) views of one page."""
+    ly = layout
+    f, h = ly.intermediate_size, ly.hidden_size
+    gu = page[ly.gate_up_codes_offset : ly.gate_up_codes_offset + ly.gate_up_codes_bytes].view(torch.int8)
+    gus = page[ly.gate_up_scales_offset : ly.gate_up_scales_offset + ly.gate_up_scales_bytes].view(torch.float32)
+    dn = page[ly.down_codes_offset : ly.down_codes_offset + ly.down_codes_bytes].view(torch.int8)
+    dns = page[ly.down_scales_offset : ly.down_scales_offset + ly.down_scales_bytes].view(torch.float32)
+    return gu.view(2 * f, h), gus, dn.view(h, f), dns
+
+
+# ------------------------------------------------------------------ router
+
+
+def router_topk(logits: torch.Tensor, k: int, *, renorm: bool = True) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """softmax(fp32) -> top-k (ties -> lower expert) -> optional renorm -> bf16 weights.
+
+    Returns (indices int64 [T, k], weights bf16 [T, k], weights fp32 [T, k])."""
+    device = _lib.require_cuda(logits, what="router top-k")
+    lg = logits.reshape(-1, logits.shape[-1])
+    if lg.dtype not in (torch.float32, torch.bfloat16):
+        lg = lg.float()
+    lg = lg.contiguous()
+    t, e = (int(v) for v in lg.shape)
+    idx = torch.empty((t, k), dtype=torch.int64, device=device)
+    w32 = torch.empty((t, k), dtype=torch.float32, device=device)
+    w16 = torch.empty((t, k), dtype=torch.bfloat16, device=device)
+    _lib.call("mrb_router_topk", lg.data_ptr(), _lib.dtype_code(lg.dtype), t, e, int(k), int(bool(renorm)),
+              idx.data_ptr(), w32.data_ptr(), w16.data_ptr(), _lib.stream_handle(device))
+    return idx, w16, w32
+
+
+# ------------------------------------------------------------------ route compiler
+
+
+def _grouped_route_tensors_impl(top_indices, top_weights, *, num_experts, include_inverse):
+    started = time.perf_counter()
+    device = _lib.require_cuda(top_indices, top_weights, what="route compiler")
+    idx = top_indices.to(torch.int64).contiguous()
+    rows, top_k = (int(v) for v in idx.shape)
+    w = top_weights.to(torch.float32).reshape(-1).contiguous()
+    a = rows * top_k
+    counts = torch.empty(num_experts, dtype=torch.int32, device=device)
+    starts = torch.empty(num_experts, dtype=torch.int32, device=device)
+    token_ids = torch.empty(a, dtype=torch.int64, device=device)
+    coefficients = torch.empty(a, dtype=torch.float32, device=device)
+    inverse = torch.empty(a, dtype=torch.int64, device=device)
+    _lib.call("mrb_route_compile", idx.data_ptr(), w.data_ptr(), rows, top_k, int(num_experts), counts.data_ptr(),
+              starts.data_ptr(), token_ids.data_ptr(), coefficients.data_ptr(), inverse.data_ptr(), None,
+              _lib.stream_handle(device))
+    if top_weights.dtype != torch.float32:
+        coefficients = coefficients.to(top_weights.dtype)
+    return token_ids, coefficients, starts, counts, (inverse if include_inverse else None), time.perf_counter() - started
+
+
+def grouped_route_tensors(top_indices, top_weights, *, num_experts):
+    """Expert-major route plan without a host sync (reference: engine/olmoe_cuda.py:1092)."""
+    token_ids, coefficients, starts, counts, _, metadata_s = _grouped_route_tensors_impl(
+        top_indices, top_weights, num_experts=num_experts, include_inverse=False)
+    return token_ids, coefficients, starts, counts, metadata_s
+
+
+def grouped_route_tensors_with_inverse(top_indices, top_weights, *, num_experts):
+    """Route plan plus the original-rank -> expert-major-row bijection (engine/olmoe_cuda.py:1108)."""
+    return _grouped_route_tensors_impl(top_indices, top_weights, num_experts=num_experts, include_inverse=True)
+
+
+# ------------------------------------------------------------------ combine
+
+
+def stable_route_reduce(
+    expert_output: torch.Tensor,
+    coefficients: torch.Tensor,
+    token_ids: torch.Tensor,
+    counts: torch.Tensor,
+    top_indices: torch.Tensor,
+    selected_experts: torch.Tensor,
+    *,
+    inverse_assignments: torch.Tensor | None = None,
+    out_bf16: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """fp32 [rows, hidden] combine in original route-rank order (engine/qwen3_moe_cuda.py:2561)."""
+    if top_indices.ndim != 2:
+        raise ValueError("stable route reduction requires [rows, top_k] indices")
+    rows, top_k = map(int, top_indices.shape)
+    assignments = rows * top_k
+    if expert_output.ndim != 2 or int(expert_output.shape[0]) != assignments:
+        raise ValueError("expert output rows must equal rows * top_k")
+    if token_ids.ndim != 1 or int(token_ids.numel()) != assignments:
+        raise ValueError("stable route token IDs must cover every assignment")
+    if coefficients.ndim != 1 or int(coefficients.numel()) != assignments:
+        raise ValueError("stable route coefficients must cover every assignment")
+    if counts.ndim != 1 or int(counts.numel()) != int(selected_experts.numel()):
+        raise ValueError("stable route counts must match selected experts")
+    device = _lib.require_cuda(expert_output, coefficients, token_ids, counts, top_indices, what="stable route reduce")
+    inverse = inverse_assignments
+    if inverse is None:
+        compact = torch.searchsorted(selected_experts.to(device), top_indices)
+        _, _, _, _, inverse, _ = _grouped_route_tensors_impl(
+            compact, torch.zeros(top_indices.shape, dtype=torch.float32, device=device),
+            num_experts=int(selected_experts.numel()), include_inverse=True)
+    elif inverse.ndim != 1 or int(inverse.numel()) != assignments:
+        raise ValueError("stable route inverse must cover every assignment")
+    eo = expert_output if expert_output.dtype == torch.bfloat16 else expert_output.to(torch.bfloat16)
+    eo = eo.contiguous()
+    hidden = int(eo.shape[1])
+    out = torch.empty((rows, hidden), dtype=torch.float32, device=device)
+    _lib.call("mrb_stable_route_reduce", eo.data_ptr(), coefficients.float().contiguous().data_ptr(),
+              inverse.to(torch.int64).contiguous().data_ptr(), rows, top_k, hidden, out.data_ptr(), _lib.ptr(out_bf16),
+              _lib.stream_handle(device))
+    return out
+
+
+# ------------------------------------------------------------------ grouped expert MLP
+
+
+def grouped_expert_mlp(
+    source: torch.Tensor,
+    token_ids: torch.Tensor,
+    starts: torch.Tensor,
+    counts: torch.Tensor,
+    pages: torch.Tensor,
+    layout: ExpertPageLayout,
+    *,
+    slot_of: torch.Tensor | None = None,
+    act_out: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Expert-major rows -> bf16 expert outputs [A, H]: gate/up (SwiGLU fused) then down.
+
+    ``pages`` is a uint8 buffer of expert pages ``[slots, page_stride]``; expert ``e`` uses
+    slot ``slot_of[e]`` (identity when None)."""
+    device = _lib.require_cuda(source, token_ids, starts, counts, pages, what="grouped expert MLP")
+    ly = layout
+    f, h = ly.intermediate_size, ly.hidden_size
+    a = int(token_ids.numel())
+    e = int(counts.numel())
+    base = pages.data_ptr()
+    stride = ly.page_stride
+    act = act_out if act_out is not None else torch.empty((a, f), dtype=torch.bfloat16, device=device)
+    y = out if out is not None else torch.empty((a, h), dtype=torch.bfloat16, device=device)
+    if a == 0:
+        return y
+    stream = _lib.stream_handle(device)
+    src = source.contiguous()
+    _lib.call("mrb_grouped_qrow", src.data_ptr(), token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
+              base + ly.gate_up_codes_offset, stride, base + ly.gate_up_scales_offset, stride // 4,
+              _lib.ptr(slot_of), f, h, f, 1, act.data_ptr(), stream)
+    _lib.call("mrb_grouped_qrow", act.data_ptr(), None, starts.data_ptr(), counts.data_ptr(), e,
+              base + ly.down_codes_offset, stride, base + ly.down_scales_offset, stride // 4,
+              _lib.ptr(slot_of), h, f, 0, 0, y.data_ptr(), stream)
+    return y
+
+
+# ------------------------------------------------------------------ backends
+
+
+@dataclass
+class ExpertBackendStats:
+    grouped_kernel_calls: int = 0
+    route_compiler_calls: int = 0
+    expert_assignments: int = 0
+    addressed_source_bytes: int = 0
+
+    def as_dict(self) -> dict[str, int]:
+        return dict(self.__dict__)
+
+
+class ResidentInt8ExpertPages:
+    """All experts of every layer resident in HBM: pages[layer] is [experts, page_stride]."""
+
+    def __init__(self, layout: ExpertPageLayout, pages: list[torch.Tensor]) -> None:
+        self.layout = layout
+        self.pages = pages
+
+    def layer_pages(self, layer: int, top_indices: torch.Tensor, *, prefill: bool):
+        return self.pages[layer], None
+
+    def reset(self, *, clear_pages: bool) -> None:
+        del clear_pages
+
+    def report(self) -> dict[str, Any]:
+        return {"kind": "resident", "layers": len(self.pages)}
+
+
+@dataclass
+class PagedInt8ExpertBackend:
+    """The reference's `.moe` protocol over int8 expert pages (engine/qwen3_moe_cuda.py:2698)."""
+
+    cache: Any
+    dtype: torch.dtype = torch.bfloat16
+    num_experts: int = 0
+    stats: ExpertBackendStats = field(default_factory=ExpertBackendStats)
+
+    def reset_stats(self, *, clear_pages: bool) -> None:
+        self.stats = ExpertBackendStats()
+        self.cache.reset(clear_pages=clear_pages)
+
+    def moe(self, layer: int, source: torch.Tensor, top_indices: torch.Tensor, top_weights: torch.Tensor, *,
+            prefill: bool = False) -> torch.Tensor:
+        pages, slot_of = self.cache.layer_pages(layer, top_indices, prefill=prefill)
+        token_ids, coefficients, starts, counts, inverse, _ = grouped_route_tensors_with_inverse(
+            top_indices, top_weights.float(), num_experts=self.num_experts)
+        expert_output = grouped_expert_mlp(source, token_ids, starts, counts, pages, self.cache.layout,
+                                           slot_of=slot_of)
+        out = torch.empty((source.shape[0], source.shape[1]), dtype=torch.bfloat16, device=source.device)
+        _lib.call("mrb_stable_route_reduce", expert_output.data_ptr(), coefficients.data_ptr(), inverse.data_ptr(),
+                  int(top_indices.shape[0]), int(top_indices.shape[1]), int(source.shape[1]), None, out.data_ptr(),
+                  _lib.stream_handle(source.device))
+        self.stats.grouped_kernel_calls += 2
+        self.stats.route_compiler_calls += 1
+        self.stats.expert_assignments += int(top_indices.numel())
+        return out if self.dtype == torch.bfloat16 else out.to(self.dtype)
+
+    def report(self) -> dict[str, Any]:
+        return {"kind": "paged-int8-qstore", "kernel": "b200-grouped-int8-qrow", "backend": self.stats.as_dict(),
+                "page_cache": self.cache.report(), "page_stride": self.cache.layout.page_stride}
+
+
+__all__ = [
+    "ExpertPageLayout",
+    "PagedInt8ExpertBackend",
+    "ResidentInt8ExpertPages",
+    "expert_page_views",
+    "grouped_expert_mlp",
+    "grouped_route_tensors",
+    "grouped_route_tensors_with_inverse",
+    "pack_expert_page",
+    "router_topk",
+    "stable_route_reduce",
+]

@@ -1,0 +1,114 @@
+"""Routed-MoE chain parity: router indices/weights, route plans (counts, starts, token order,
+coefficients, inverse) and the stable combine bit-exact against the reference's golden
+vectors; grouped int8 expert projections within the bf16 tolerance of the oracle, and
+bit-identical per row whatever the group composition (the property expert parallelism
+relies on)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as omoe
+from oracle import qrow as oq
+from oracle.numerics import bf16_round, max_rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+def test_router_topk_golden(golden, cuda):
+    from mrun_b200.moe import router_topk
+
+    g = golden("moe")
+    idx, w16, _ = router_topk(torch.from_numpy(g["router_logits"]).to(cuda), 8, renorm=True)
+    np.testing.assert_array_equal(idx.cpu().numpy(), g["router_idx"])
+    np.testing.assert_array_equal(w16.float().cpu().numpy(), g["router_w"])
+
+
+def test_route_compile_golden_and_kat(golden, cuda):
+    from mrun_b200.moe import grouped_route_tensors, grouped_route_tensors_with_inverse
+
+    g = golden("moe")
+    tok, coef, starts, counts, inv, _ = grouped_route_tensors_with_inverse(
+        torch.from_numpy(g["router_idx"]).to(cuda), torch.from_numpy(g["router_w"]).to(cuda), num_experts=128)
+    np.testing.assert_array_equal(tok.cpu().numpy(), g["route_tok"])
+    np.testing.assert_array_equal(coef.cpu().numpy(), g["route_coef"])
+    np.testing.assert_array_equal(starts.cpu().numpy(), g["route_starts"])
+    np.testing.assert_array_equal(counts.cpu().numpy(), g["route_counts"])
+    np.testing.assert_array_equal(inv.cpu().numpy(), g["route_inv"])
+    # tests/test_olmoe_cuda.py:73-90 of the reference
+    idx = torch.tensor([[3, 1], [1, 2], [3, 2]], device=cuda)
+    w = torch.tensor([[0.7, 0.3], [0.6, 0.4], [0.8, 0.2]], device=cuda)
+    tok, coef, starts, counts, _ = grouped_route_tensors(idx, w, num_experts=5)
+    assert counts.tolist() == [0, 2, 2, 2, 0]
+    assert starts.tolist() == [0, 0, 2, 4, 6]
+    assert tok.tolist() == [0, 1, 1, 2, 0, 2]
+    torch.testing.assert_close(coef, torch.tensor([0.3, 0.6, 0.4, 0.2, 0.7, 0.8], device=cuda))
+
+
+@pytest.mark.parametrize("tokens,k,experts", [(32, 8, 128), (2048, 8, 128), (256, 2, 8), (5000, 4, 64)])
+def test_route_compile_random_bit_exact(tokens, k, experts, cuda):
+    from mrun_b200.moe import grouped_route_tensors_with_inverse
+
+    rng = np.random.default_rng(tokens)
+    idx = np.stack([rng.permutation(experts)[:k] for _ in range(tokens)]).astype(np.int64)
+    w = rng.random((tokens, k)).astype(np.float32)
+    got = grouped_route_tensors_with_inverse(torch.from_numpy(idx).to(cuda), torch.from_numpy(w).to(cuda),
+                                             num_experts=experts)
+    ref = omoe.route_tensors(idx, w, experts)
+    for a, b in zip(got[:5], (ref[0], ref[1], ref[2], ref[3], ref[4])):
+        np.testing.assert_array_equal(a.cpu().numpy(), b)
+
+
+def test_stable_reduce_golden(golden, cuda):
+    from mrun_b200.moe import stable_route_reduce
+
+    g = golden("moe")
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
+    out = stable_route_reduce(dev(g["reduce_eo"]).to(torch.bfloat16), dev(g["route_coef"]), dev(g["route_tok"]),
+                              dev(g["route_counts"]), dev(g["router_idx"]), torch.arange(128, device=cuda),
+                              inverse_assignments=dev(g["route_inv"]))
+    np.testing.assert_array_equal(out.cpu().numpy(), g["reduce_out"])
+
+
+def _expert_pages(rng, experts, hidden, ffn, dev):
+    from mrun_b200.moe import ExpertPageLayout, pack_expert_page
+
+    ly = ExpertPageLayout.create(hidden, ffn)
+    pages = torch.zeros((experts, ly.page_stride), dtype=torch.uint8, device=dev)
+    host = []
+    for e in range(experts):
+        gu_q, gu_s = oq.quant_row_int8((rng.standard_normal((2 * ffn, hidden)) * 0.02).astype(np.float32))
+        dn_q, dn_s = oq.quant_row_int8((rng.standard_normal((hidden, ffn)) * 0.02).astype(np.float32))
+        pack_expert_page(ly, torch.from_numpy(gu_q), torch.from_numpy(gu_s), torch.from_numpy(dn_q),
+                         torch.from_numpy(dn_s), pages[e])
+        host.append((gu_q, gu_s, dn_q, dn_s))
+    return ly, pages, host
+
+
+@pytest.mark.parametrize("tokens,k,experts,hidden,ffn", [(32, 8, 16, 256, 128), (7, 2, 8, 512, 384), (64, 4, 8, 2048, 768)])
+def test_moe_backend_vs_oracle_and_row_independence(tokens, k, experts, hidden, ffn, cuda):
+    from mrun_b200.moe import PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_topk
+
+    rng = np.random.default_rng(tokens + experts)
+    ly, pages, host = _expert_pages(rng, experts, hidden, ffn, cuda)
+    backend = PagedInt8ExpertBackend(ResidentInt8ExpertPages(ly, [pages]), num_experts=experts)
+    x = torch.from_numpy(bf16_round(rng.standard_normal((tokens, hidden)).astype(np.float32))).to(cuda).to(torch.bfloat16)
+    logits = torch.from_numpy(rng.standard_normal((tokens, experts)).astype(np.float32)).to(cuda)
+    idx, w16, _ = router_topk(logits, k)
+    out = backend.moe(0, x, idx, w16)
+    # oracle: route, per-expert exact projections with the same bf16 boundaries, stable combine
+    idx_np, w_np = idx.cpu().numpy(), w16.float().cpu().numpy()
+    tok, coef, starts, counts, inv = omoe.route_tensors(idx_np, w_np, experts)
+    xf = x.float().cpu().numpy()
+    eo = np.zeros((tok.size, hidden), np.float32)
+    for e in range(experts):
+        s, c = int(starts[e]), int(counts[e])
+        if c:
+            eo[s:s + c] = omoe.expert_swiglu_exact(xf[tok[s:s + c]], *host[e])
+    ref = bf16_round(omoe.stable_route_reduce(eo, coef, inv, tokens, k))
+    assert max_rel_err(out.float().cpu().numpy(), ref) < TOL
+    # each token's result is independent of which other tokens share its experts
+    single = torch.stack([backend.moe(0, x[i:i + 1], idx[i:i + 1], w16[i:i + 1])[0] for i in range(min(tokens, 6))])
+    assert torch.equal(single, out[: single.shape[0]])
