@@ -1,0 +1,166 @@
+"""Expert parallelism for the routed-MoE layer: experts sharded over the GPUs of one box,
+tokens exchanged with NCCL all-to-all over NVLink.
+
+The reference runs every expert on one device (engine/qwen3_moe_cuda.py:2698-2788); this
+module spreads the same computation. Expert ``e`` lives on rank ``e // (E / world)``; each
+rank routes its own tokens (data-parallel attention), then per layer:
+
+1. assignments are ordered by destination rank (stable, so the order is the same on every
+   run) and the per-destination counts are exchanged (``all_to_all_single`` of counts);
+2. each assignment's activation row and its destination-local expert id are sent
+   (``all_to_all_single`` with split sizes);
+3. the owner runs the grouped int8 expert MLP on what it received;
+4. the outputs travel back by the reverse all-to-all;
+5. the source combines every token's k outputs in route-rank order.
+
+Each expert output row depends only on its own activation row and the combine order is
+fixed, so the layer's result is bit-identical for every world size. The collectives and
+the planners are injected, so the host-side logic is testable on CPU with the gloo
+backend; on GPUs the planner is the native route compiler and compute is the grouped
+int8 MLP.
+"""
+from __future__ import annotations
+
+from collections.abc import Callable
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+# planner(keys int64 [n], num_groups) -> (order int64 [n], counts int64 [num_groups], inverse int64 [n])
+# with order = stable argsort of keys and inverse[order] = arange(n).
+Planner = Callable[[torch.Tensor, int], tuple[torch.Tensor, torch.Tensor, torch.Tensor]]
+
+
+def torch_stable_planner(keys: torch.Tensor, groups: int):
+    """Reference planner (any device): stable argsort, bincount, inverse bijection."""
+    order = torch.argsort(keys, stable=True)
+    counts = torch.bincount(keys, minlength=groups).to(torch.int64)
+    inverse = torch.empty_like(order)
+    inverse[order] = torch.arange(order.numel(), device=order.device)
+    return order, counts, inverse
+
+
+def native_planner(keys: torch.Tensor, groups: int):
+    """The native deterministic route compiler with k = 1 (same order as the reference)."""
+    from .moe import grouped_route_tensors_with_inverse
+
+    token_ids, _, _, counts, inverse, _ = grouped_route_tensors_with_inverse(
+        keys.reshape(-1, 1), torch.zeros((keys.numel(), 1), device=keys.device), num_experts=groups)
+    return token_ids, counts.to(torch.int64), inverse
+
+
+@dataclass
+class ExpertShard:
+    """Rank ``rank`` of ``world`` owns experts [first, first + count)."""
+
+    world: int
+    rank: int
+    num_experts: int
+
+    @property
+    def per_rank(self) -> int:
+        if self.num_experts % self.world:
+            raise ValueError("expert count must divide evenly over the ranks")
+        return self.num_experts // self.world
+
+    @property
+    def first(self) -> int:
+        return self.rank * self.per_rank
+
+
+class ExpertParallelMoE:
+    """Dispatch / local compute / return / combine for one MoE layer on one rank.
+
+    ``local_mlp(rows bf16 [n, H], local_expert int64 [n]) -> bf16 [n, H]`` computes the
+    owned experts' outputs for received rows (any row order)."""
+
+    def __init__(self, shard: ExpertShard, local_mlp, *, group=None, planner: Planner = torch_stable_planner,
+                 combine=None) -> None:
+        self.shard = shard
+        self.local_mlp = local_mlp
+        self.group = group
+        self.planner = planner
+        self.combine = combine or torch_combine
+        self.last_stats: dict[str, int] = {}
+
+    def _all_to_all(self, out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits) -> None:
+        dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits, group=self.group)
+
+    def forward(self, source: torch.Tensor, top_indices: torch.Tensor, top_weights: torch.Tensor) -> torch.Tensor:
+        """source [T, H] bf16, top_indices [T, k], top_weights [T, k] -> bf16 [T, H]."""
+        sh = self.shard
+        t, k = (int(v) for v in top_indices.shape)
+        hidden = int(source.shape[1])
+        device = source.device
+        flat_e = top_indices.reshape(-1).to(torch.int64)
+        dest = torch.div(flat_e, sh.per_rank, rounding_mode="floor")
+        order, send_counts, inverse = self.planner(dest, sh.world)
+        # 1. counts
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        send_split = [int(v) for v in send_counts.tolist()]
+        recv_split = [int(v) for v in recv_counts.tolist()]
+        n_recv = sum(recv_split)
+        # 2. rows and destination-local expert ids, in destination order
+        token_of = torch.div(order, k, rounding_mode="floor")
+        send_rows = source.index_select(0, token_of)
+        send_expert = (flat_e.index_select(0, order) - dest.index_select(0, order) * sh.per_rank).contiguous()
+        recv_rows = torch.empty((n_recv, hidden), dtype=source.dtype, device=device)
+        recv_expert = torch.empty((n_recv,), dtype=torch.int64, device=device)
+        self._all_to_all(recv_rows, send_rows.contiguous(), recv_split, send_split)
+        self._all_to_all(recv_expert, send_expert, recv_split, send_split)
+        # 3. owned experts
+        recv_out = self.local_mlp(recv_rows, recv_expert) if n_recv else recv_rows
+        # 4. return
+        back = torch.empty((t * k, hidden), dtype=source.dtype, device=device)
+        self._all_to_all(back, recv_out.contiguous(), send_split, recv_split)
+        # 5. combine in route-rank order: assignment a's output sits at back[inverse[a]]
+        coef = top_weights.reshape(-1).float().index_select(0, order).contiguous()
+        self.last_stats = {"sent_rows": t * k, "received_rows": n_recv}
+        return self.combine(back, coef, inverse, t, k)
+
+
+def torch_combine(rows: torch.Tensor, coef: torch.Tensor, inverse: torch.Tensor, t: int, k: int) -> torch.Tensor:
+    """out[t] = sum_r coef[p] * rows[p], p = inverse[t*k + r]: fp32 products added in rank order."""
+    per = rows.index_select(0, inverse).reshape(t, k, -1).float()
+    c = coef.index_select(0, inverse).reshape(t, k, 1)
+    out = per[:, 0] * c[:, 0]
+    for r in range(1, k):
+        out = out + per[:, r] * c[:, r]
+    return out.to(rows.dtype)
+
+
+def native_combine(rows: torch.Tensor, coef: torch.Tensor, inverse: torch.Tensor, t: int, k: int) -> torch.Tensor:
+    """The same combine on the native fixed-rank kernel (bf16 output)."""
+    from . import _lib
+
+    out = torch.empty((t, rows.shape[1]), dtype=torch.bfloat16, device=rows.device)
+    _lib.call("mrb_stable_route_reduce", rows.contiguous().data_ptr(), coef.data_ptr(), inverse.contiguous().data_ptr(),
+              t, k, int(rows.shape[1]), None, out.data_ptr(), _lib.stream_handle(rows.device))
+    return out
+
+
+def local_expert_mlp_fn(pages: torch.Tensor, layout, experts_per_rank: int):
+    """local_mlp for ExpertParallelMoE over this rank's resident expert pages."""
+    from .moe import grouped_expert_mlp, grouped_route_tensors_with_inverse
+
+    def run(rows: torch.Tensor, local_expert: torch.Tensor) -> torch.Tensor:
+        token_ids, _, starts, counts, inverse, _ = grouped_route_tensors_with_inverse(
+            local_expert.reshape(-1, 1), torch.zeros((local_expert.numel(), 1), device=rows.device),
+            num_experts=experts_per_rank)
+        eo = grouped_expert_mlp(rows, token_ids, starts, counts, pages, layout)
+        return eo.index_select(0, inverse)  # back to received-row order
+
+    return run
+
+
+__all__ = [
+    "ExpertParallelMoE",
+    "ExpertShard",
+    "local_expert_mlp_fn",
+    "native_combine",
+    "native_planner",
+    "torch_combine",
+    "torch_stable_planner",
+]

@@ -1,0 +1,80 @@
+"""Expert parallelism on 2+ GPUs (NCCL all-to-all over NVLink): each rank's MoE output must
+be bit-identical to the single-GPU backend over all experts. Skipped with fewer than 2 GPUs."""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+E, K, H, F, T = 16, 4, 512, 256, 24
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from mrun_b200.expert_parallel import (
+        ExpertParallelMoE, ExpertShard, local_expert_mlp_fn, native_combine, native_planner,
+    )
+    from mrun_b200.moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, pack_expert_page, router_topk
+    from oracle import qrow as oq
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        rng = np.random.default_rng(7)  # same experts on every rank
+        ly = ExpertPageLayout.create(H, F)
+        pages = torch.zeros((E, ly.page_stride), dtype=torch.uint8, device=dev)
+        for e in range(E):
+            gu = oq.quant_row_int8((rng.standard_normal((2 * F, H)) * 0.02).astype(np.float32))
+            dn = oq.quant_row_int8((rng.standard_normal((H, F)) * 0.02).astype(np.float32))
+            pack_expert_page(ly, torch.from_numpy(gu[0]), torch.from_numpy(gu[1]), torch.from_numpy(dn[0]),
+                             torch.from_numpy(dn[1]), pages[e])
+        trng = np.random.default_rng(100 + rank)  # this rank's own tokens
+        x = torch.from_numpy(trng.standard_normal((T, H)).astype(np.float32)).to(dev).to(torch.bfloat16)
+        idx, w, _ = router_topk(torch.from_numpy(trng.standard_normal((T, E)).astype(np.float32)).to(dev), K)
+        single = PagedInt8ExpertBackend(ResidentInt8ExpertPages(ly, [pages]), num_experts=E).moe(0, x, idx, w)
+        shard = ExpertShard(world, rank, E)
+        mine = pages[shard.first : shard.first + shard.per_rank].contiguous()
+        ep = ExpertParallelMoE(shard, local_expert_mlp_fn(mine, ly, shard.per_rank), planner=native_planner,
+                               combine=native_combine)
+        out = ep.forward(x, idx, w)
+        torch.cuda.synchronize()
+        q.put((rank, bool(torch.equal(out, single)), ep.last_stats))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_bit_identical_to_single_gpu():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs at least 2 GPUs")
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _ in results), results
