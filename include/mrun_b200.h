@@ -255,6 +255,18 @@ int mrb_paged_attention_static(const void *q, int64_t rows, int64_t hq, int64_t 
 int mrb_decode_advance(const int64_t *next_ids, int64_t *input_ids, int32_t *positions,
                        int32_t *row_len, int64_t rows, void *stream);
 
+/* ---------------------------------------------------------------- (d) weight-page streaming */
+
+/* Host->device page copies on `stream`: page src_pages[i] (at src_base + page * src_stride,
+ * pinned host memory for asynchronous copies) to slot dst_slots[i] (dst_base + slot *
+ * dst_stride), one cudaMemcpyAsync per page, then records `done` (a cudaEvent_t, may be
+ * NULL) on the stream. dst_slots/src_pages are host arrays of `count` entries.
+ * Replaces the side-stream page staging of `_RingPrefetch` (engine/kernels/qstore.py:622-660)
+ * and of the expert page cache (engine/qwen3_moe_cuda.py:1533-1546). */
+int mrb_copy_pages(void *dst_base, int64_t dst_stride, const void *src_base, int64_t src_stride,
+                   const int32_t *dst_slots, const int32_t *src_pages, int64_t count,
+                   int64_t page_bytes, void *stream, void *done);
+
 #ifdef __cplusplus
 }
 #endif

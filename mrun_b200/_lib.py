@@ -56,6 +56,7 @@ SIGNATURES: dict[str, list] = {
     "mrb_paged_attention_static": [_P, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P,
                                    _P, _P, c_float, _I64, _P, _P],
     "mrb_decode_advance": [_P, _P, _P, _P, _I64, _P],
+    "mrb_copy_pages": [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P],
 }
 _RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t,
              "mrb_paged_attention_static_capacity": c_size_t}

@@ -297,6 +297,9 @@ class PagedInt8ExpertBackend:
         _lib.call("mrb_stable_route_reduce", expert_output.data_ptr(), coefficients.data_ptr(), inverse.data_ptr(),
                   int(top_indices.shape[0]), int(top_indices.shape[1]), int(source.shape[1]), None, out.data_ptr(),
                   _lib.stream_handle(source.device))
+        release = getattr(self.cache, "release_layer", None)
+        if release is not None:  # streamed pages: slots may be reused after these kernels
+            release()
         self.stats.grouped_kernel_calls += 2
         self.stats.route_compiler_calls += 1
         self.stats.expert_assignments += int(top_indices.numel())
