@@ -257,6 +257,57 @@ def _time_gemv(weights, iters: int = 56) -> dict:
     return {"avg_s": avg_s, "bytes": bytes_per_launch}
 
 
+GEMV_CASES = {
+    # name: (rows n, depth k, paired gate/up SwiGLU) at the config-2 shapes
+    "gemv-swiglu": (18944, 3584, True),
+    "gemv-down": (3584, 18944, False),
+    "gemv-qkv": (4608, 3584, False),
+}
+
+
+def run_gemv_case(args) -> None:
+    """Small case for kernel captures: one decode GEMV (M=1) at a config-2 shape over 4
+    weight sets in turn (272 to 543 MB, above L2). Prints one JSON line with the
+    device-timed average; not the bench metric."""
+    import torch
+
+    from mrun_b200.dense_qstore_cuda import qrow_linear, qrow_swiglu
+
+    n, k, paired = GEMV_CASES[args.case]
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device).manual_seed(0)
+    sets = 4
+    per = 2 if paired else 1
+    codes = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=gen)
+             for _ in range(sets * per)]
+    scales = [torch.rand(n, device=device, generator=gen) * 0.01 for _ in range(sets * per)]
+    x = torch.randn(1, k, device=device, generator=gen).to(torch.bfloat16)
+    out = torch.empty(1, n, device=device, dtype=torch.bfloat16)
+
+    def launch(i):
+        j = per * (i % sets)
+        if paired:
+            qrow_swiglu(codes[j], scales[j], codes[j + 1], scales[j + 1], x, out=out)
+        else:
+            qrow_linear(codes[j], scales[j], x, out=out)
+
+    for i in range(args.warmup):
+        launch(i)
+    stream = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    for i in range(args.steps):
+        launch(i)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    avg_s = e0.elapsed_time(e1) / 1000.0 / args.steps
+    nbytes = per * (n * k + n * 4) + 2 * k + 2 * n
+    print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "bytes_per_launch": nbytes,
+                      "gbs": nbytes / avg_s / 1e9, "launches": args.steps}), flush=True)
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -287,11 +338,14 @@ def run_ours(args) -> None:
     _barrier(world)
     torch.cuda.synchronize(device)
     with ClockSampler(local) as clocks:
+        # the profiler bracket lets `ncu --profile-from-start off` list exactly the timed launches
+        torch.cuda.cudart().cudaProfilerStart()
         e0.record(stream)
         for _ in range(args.steps):
             dec.step()
         e1.record(stream)
         torch.cuda.synchronize(device)
+        torch.cuda.cudart().cudaProfilerStop()
     _barrier(world)
     step_s = _max_over_ranks(e0.elapsed_time(e1) / 1000.0 / args.steps, world)
     dec.check_errors()
@@ -390,10 +444,14 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", choices=["decode", *GEMV_CASES], default="decode",
+                    help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.case in GEMV_CASES:
+        run_gemv_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -324,8 +324,9 @@ class DenseDecoder:
             self._decode_body(rows)
         self.graph = graph
         self.graph_rows = rows
-        # embed, norm, 8 per layer, head (memset + GEMV + unpack), advance
-        self.launches_per_step = 2 + 8 * self.cfg.num_layers + 3 + 1
+        # kernels: embed, final norm, 8 per layer, head GEMV + argmax unpack, advance (the
+        # argmax key reset is a memset node, not a kernel)
+        self.launches_per_step = 2 + 8 * self.cfg.num_layers + 2 + 1
 
     def step(self) -> None:
         """Advance every captured row by one greedy token (graph replay, no host sync)."""
