@@ -72,18 +72,31 @@ int mrb_qrow_embed_rows(const int8_t *codes, const float *scales, int64_t rows, 
  * bias (fp32 [n], may be NULL) is added after rounding to y's dtype, as the reference adds
  * a compute-dtype bias to the projection output.
  * Requires k % 16 == 0 and 16-byte aligned codes.
+ * workspace (may be NULL): zero-initialised device memory of mrb_qrow_workspace(n) bytes,
+ * 256-byte aligned. With it, decode-size calls (m <= 16) whose 16-row tiles do not spread
+ * evenly over the SMs split tiles along k (stream-K) so every CTA streams the same number
+ * of weight bytes; a split tile is finished by its last CTA, adding partial sums in a fixed
+ * order. Its counters reset themselves, so one workspace serves any number of calls that
+ * are ordered on one stream; calls that may run concurrently need separate workspaces.
+ * With NULL every CTA owns whole tiles.
  * Replaces `fused_qrow_matmul` (engine/kernels/dense_qstore_cuda.py:1105-1152) for
  * bf16/fp16 rows and `QStore.matmul` (engine/kernels/qstore.py:1082-1092) for fp32 rows. */
 int mrb_qrow_matmul(const void *x, int x_dtype, int64_t m, int64_t k, const int8_t *codes,
                     const float *scales, int64_t n, const float *bias, void *y, int y_dtype,
-                    void *stream);
+                    void *workspace, size_t workspace_bytes, void *stream);
+
+/* Bytes of the optional mrb_qrow_matmul / mrb_qrow_swiglu workspace for n output rows on
+ * the current device (any m, k and dtype). */
+size_t mrb_qrow_workspace(int64_t n);
 
 /* Paired gate/up W8A16 projection with the reference's BF16 SwiGLU boundaries:
  * g = bf16(x.Wg), u = bf16(x.Wu), s = bf16(g * sigmoid(g)), y = bf16(s * u).
+ * workspace: as for mrb_qrow_matmul.
  * Replaces `fused_qrow_swiglu` (engine/kernels/dense_qstore_cuda.py:1052-1102). */
 int mrb_qrow_swiglu(const void *x_bf16, int64_t m, int64_t k, const int8_t *gate_codes,
                     const float *gate_scales, const int8_t *up_codes, const float *up_scales,
-                    int64_t n, void *y_bf16, void *stream);
+                    int64_t n, void *y_bf16, void *workspace, size_t workspace_bytes,
+                    void *stream);
 
 /* Greedy language head: logits[m, v] = x[m].W[v] * scale[v] in fp32 over the first
  * `semantic_rows` rows, then the first maximal index per row (lowest index on ties), fused

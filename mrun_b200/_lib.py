@@ -34,8 +34,9 @@ SIGNATURES: dict[str, list] = {
     "mrb_last_error": [],
     "mrb_quant_row_int8": [_P, _I64, _I64, _P, _P, _P],
     "mrb_qrow_embed_rows": [_P, _P, _I64, _I64, _P, _I64, _P, c_int, _P, _P],
-    "mrb_qrow_matmul": [_P, c_int, _I64, _I64, _P, _P, _I64, _P, _P, c_int, _P],
-    "mrb_qrow_swiglu": [_P, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P],
+    "mrb_qrow_matmul": [_P, c_int, _I64, _I64, _P, _P, _I64, _P, _P, c_int, _P, c_size_t, _P],
+    "mrb_qrow_workspace": [_I64],
+    "mrb_qrow_swiglu": [_P, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P, c_size_t, _P],
     "mrb_qrow_argmax": [_P, c_int, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P, _P],
     "mrb_rms_norm": [_P, c_int, _I64, _I64, _P, c_float, _P, _P],
     "mrb_residual_rms_norm": [_P, _P, _I64, _I64, _P, c_float, _P, _P, _P],
@@ -59,7 +60,7 @@ SIGNATURES: dict[str, list] = {
     "mrb_copy_pages": [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P],
 }
 _RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t,
-             "mrb_paged_attention_static_capacity": c_size_t}
+             "mrb_paged_attention_static_capacity": c_size_t, "mrb_qrow_workspace": c_size_t}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -159,6 +160,32 @@ class DeviceScratch:
             if buf is None or buf.numel() < nbytes:
                 buf = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=device)
                 self._buffers[index] = buf
+            return buf
+
+
+class StreamScratch:
+    """Zero-initialised workspace per (device, CUDA stream) for kernels whose workspace
+    holds self-resetting counters: calls ordered on one stream may share it, calls on
+    different streams never do. While the current stream is being captured only an
+    existing buffer is handed out (None otherwise), so a CUDA graph never owns one."""
+
+    def __init__(self) -> None:
+        self._lock = threading.Lock()
+        self._buffers: dict[tuple[int, int], torch.Tensor] = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor | None:
+        if nbytes <= 0:
+            return None
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        key = (index, torch.cuda.current_stream(device).cuda_stream)
+        with self._lock:
+            buf = self._buffers.get(key)
+            if buf is not None and buf.numel() >= nbytes:
+                return buf
+            if torch.cuda.is_current_stream_capturing():
+                return None
+            buf = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=device)
+            self._buffers[key] = buf
             return buf
 
 

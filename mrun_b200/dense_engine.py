@@ -20,7 +20,8 @@ import numpy as np
 import torch
 
 from . import _lib
-from .dense_qstore_cuda import qrow_argmax, qrow_linear, qrow_swiglu, residual_rms_norm_into, rms_norm_into
+from .dense_qstore_cuda import (qrow_argmax, qrow_linear, qrow_swiglu, qrow_workspace_bytes, residual_rms_norm_into,
+                                rms_norm_into)
 from .paged_kv import PagedKVCache
 from .qstore_build import embed_rows, quant_row_int8
 
@@ -200,6 +201,9 @@ class DenseDecoder:
         # the split plan depends on the row count: size for the worst row count we will run
         ws = max(self.kv.workspace_bytes(r, cfg.heads, self.max_seq_len) for r in range(1, rows + 1))
         self.workspace = torch.zeros(max(ws, 256), dtype=torch.uint8, device=device)
+        # GEMV stream-K workspace shared by every projection (all ordered on one stream)
+        gemv_ws = max(qrow_workspace_bytes(device, n) for n in (cfg.qkv_rows, cfg.hidden, cfg.ffn))
+        self.gemv_workspace = torch.zeros(gemv_ws, dtype=torch.uint8, device=device)
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=device)
         bf = torch.bfloat16
         h = cfg.hidden
@@ -238,9 +242,10 @@ class DenseDecoder:
         proj = buf["proj"][:rows]
         mlp = buf["mlp"][:rows]
         qd, kd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        gws = self.gemv_workspace
         rms_norm_into(hidden, w.layers[0].ln1, cfg.eps, normed)
         for i, layer in enumerate(w.layers):
-            qrow_linear(layer.qkv.codes, layer.qkv.scales, normed, bias=layer.qkv_bias, out=qkv)
+            qrow_linear(layer.qkv.codes, layer.qkv.scales, normed, bias=layer.qkv_bias, out=qkv, workspace=gws)
             self.kv.append(
                 i, qkv[:, qd:], qkv[:, qd + kd:], positions, token_rows, q_rows=qkv, q_out=q,
                 rope=(self.cos, self.sin), in_row_stride=cfg.qkv_rows, num_heads=cfg.heads,
@@ -248,10 +253,11 @@ class DenseDecoder:
             )
             self.kv.attend(i, q, row_len, max_total_tokens=max_total, row_seq=token_rows, out=ctx,
                            workspace=self.workspace, scale=self.scale)
-            qrow_linear(layer.o.codes, layer.o.scales, ctx.view(rows, qd), out=proj)
+            qrow_linear(layer.o.codes, layer.o.scales, ctx.view(rows, qd), out=proj, workspace=gws)
             residual_rms_norm_into(hidden, proj, layer.ln2, cfg.eps, hidden, normed)
-            qrow_swiglu(layer.gate.codes, layer.gate.scales, layer.up.codes, layer.up.scales, normed, out=mlp)
-            qrow_linear(layer.down.codes, layer.down.scales, mlp, out=proj)
+            qrow_swiglu(layer.gate.codes, layer.gate.scales, layer.up.codes, layer.up.scales, normed, out=mlp,
+                        workspace=gws)
+            qrow_linear(layer.down.codes, layer.down.scales, mlp, out=proj, workspace=gws)
             nxt = w.layers[i + 1].ln1 if i + 1 < len(w.layers) else w.final_norm
             residual_rms_norm_into(hidden, proj, nxt, cfg.eps, hidden, normed)
         return normed

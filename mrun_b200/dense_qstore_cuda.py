@@ -76,6 +76,33 @@ def _check_page(page: CompactQRowPage) -> None:
         raise ValueError("compact qrow page codes do not match its row range")
 
 
+_GEMV_SCRATCH = _lib.StreamScratch()
+_GEMV_WS_BYTES: dict[tuple[int, int], int] = {}
+
+
+def qrow_workspace_bytes(device: torch.device, out_features: int) -> int:
+    """Bytes of the optional GEMV workspace (stream-K tile splitting) for ``out_features``."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (index, int(out_features))
+    nbytes = _GEMV_WS_BYTES.get(key)
+    if nbytes is None:
+        with torch.cuda.device(index):
+            nbytes = int(_lib.load().mrb_qrow_workspace(int(out_features)))
+        _GEMV_WS_BYTES[key] = nbytes
+    return nbytes
+
+
+def _gemv_workspace(device: torch.device, out_features: int, workspace: torch.Tensor | None):
+    """(pointer, bytes) of the workspace for one GEMV call: the caller's, else this stream's."""
+    if workspace is None:
+        workspace = _GEMV_SCRATCH.get(device, qrow_workspace_bytes(device, out_features))
+        if workspace is None:
+            return None, 0
+    elif workspace.device != device or workspace.dtype != torch.uint8 or not workspace.is_contiguous():
+        raise ValueError("workspace must be a contiguous uint8 tensor on the activations' device")
+    return workspace.data_ptr(), workspace.numel()
+
+
 def qrow_linear(
     codes: torch.Tensor,
     scales: torch.Tensor,
@@ -83,8 +110,12 @@ def qrow_linear(
     *,
     bias: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """``activations @ (codes * scales[:, None]).T (+ bias)`` in the activation dtype."""
+    """``activations @ (codes * scales[:, None]).T (+ bias)`` in the activation dtype.
+
+    ``workspace`` (zeroed uint8, ``qrow_workspace_bytes`` long) lets decode-size calls
+    split uneven tiles over all SMs; by default a per-stream workspace is used."""
     out_features, in_features = (int(v) for v in codes.shape)
     if activations.shape[-1] != in_features:
         raise ValueError("activation width does not match compact qrow page")
@@ -98,6 +129,7 @@ def qrow_linear(
     if bias is not None and (bias.dtype != torch.float32 or bias.numel() != out_features):
         raise ValueError("bias must be fp32 [out_features]")
     code = _lib.dtype_code(flat.dtype)
+    ws_ptr, ws_bytes = _gemv_workspace(device, out_features, workspace) if rows <= 16 else (None, 0)
     _lib.call(
         "mrb_qrow_matmul",
         flat.data_ptr(),
@@ -110,6 +142,8 @@ def qrow_linear(
         _lib.ptr(bias),
         out.data_ptr(),
         code,
+        ws_ptr,
+        ws_bytes,
         _lib.stream_handle(device),
     )
     return out.reshape(*activations.shape[:-1], out_features)
@@ -174,6 +208,7 @@ def qrow_swiglu(
     activations: torch.Tensor,
     *,
     out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
     out_features, in_features = (int(v) for v in gate_codes.shape)
     device = _lib.require_cuda(gate_codes, up_codes, activations, what="paired SwiGLU")
@@ -181,6 +216,7 @@ def qrow_swiglu(
     rows = int(flat.shape[0])
     if out is None:
         out = torch.empty((rows, out_features), device=device, dtype=torch.bfloat16)
+    ws_ptr, ws_bytes = _gemv_workspace(device, out_features, workspace) if rows <= 16 else (None, 0)
     _lib.call(
         "mrb_qrow_swiglu",
         flat.data_ptr(),
@@ -192,6 +228,8 @@ def qrow_swiglu(
         up_scales.data_ptr(),
         out_features,
         out.data_ptr(),
+        ws_ptr,
+        ws_bytes,
         _lib.stream_handle(device),
     )
     return out.reshape(*activations.shape[:-1], out_features)
@@ -387,6 +425,7 @@ __all__ = [
     "qrow_argmax",
     "qrow_linear",
     "qrow_swiglu",
+    "qrow_workspace_bytes",
     "residual_rms_norm_into",
     "rms_norm_into",
     "stable_rms_norm",

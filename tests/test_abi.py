@@ -44,7 +44,7 @@ def test_abi_version_and_error_text_without_gpu():
     lib = _lib.load()
     assert lib.mrb_abi_version() >= 1
     # argument validation runs on the host and needs no device
-    status = lib.mrb_qrow_matmul(None, 1, 1, 64, None, None, 8, None, None, 1, None)
+    status = lib.mrb_qrow_matmul(None, 1, 1, 64, None, None, 8, None, None, 1, None, 0, None)
     assert status == _lib.MRB_ERR_ARG
     assert b"null" in lib.mrb_last_error()
     with pytest.raises(ValueError):

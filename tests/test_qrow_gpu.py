@@ -240,3 +240,76 @@ def test_swiglu_gemm_path(m, n, k, cuda):
     # the GEMV and GEMM paths agree on the rows they share
     y_small = qrow_swiglu(gq.to(cuda), gs.to(cuda), uq.to(cuda), us.to(cuda), x[:4].to(cuda)).float().cpu().numpy()
     assert max_rel_err(y_small, y[:4]) < BF16_TOL
+
+
+def _abi_matmul(x, q, s, workspace):
+    """mrb_qrow_matmul through the C ABI with an explicit workspace (None: whole tiles)."""
+    from mrun_b200 import _lib
+
+    m, k = x.shape
+    n = q.shape[0]
+    y = torch.empty((m, n), dtype=x.dtype, device=x.device)
+    code = _lib.dtype_code(x.dtype)
+    _lib.call("mrb_qrow_matmul", x.data_ptr(), code, m, k, q.data_ptr(), s.data_ptr(), n, None, y.data_ptr(), code,
+              _lib.ptr(workspace), 0 if workspace is None else workspace.numel(), _lib.stream_handle(x.device))
+    return y
+
+
+@pytest.mark.parametrize("m,n,k,dtype", [
+    (1, 3584, 3584, torch.bfloat16),    # 224 tiles on 296 CTA slots: tiles split along k
+    (1, 3584, 18944, torch.bfloat16),
+    (3, 3584, 128, torch.bfloat16),     # 2 k blocks per tile: CTAs of 1 or 2 units
+    (16, 3584, 3584, torch.bfloat16),
+    (2, 200, 1024, torch.float16),      # 13 tiles over many CTAs: every tile split
+    (4, 3584, 1024, torch.float32),     # fp32 rows (hi/lo split columns)
+])
+def test_stream_k_matches_whole_tiles_and_oracle(m, n, k, dtype, cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_workspace_bytes
+
+    gen = torch.Generator(device="cpu").manual_seed(n + k + m)
+    q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    s = torch.rand(n, generator=gen) * 0.01 + 1e-4
+    x = (torch.randn(m, k, generator=gen) * 2).to(dtype)
+    qd, sd, xd = q.to(cuda), s.to(cuda), x.to(cuda)
+    ws = torch.zeros(qrow_workspace_bytes(xd.device, n), dtype=torch.uint8, device=cuda)
+    split = _abi_matmul(xd, qd, sd, ws)
+    again = _abi_matmul(xd, qd, sd, ws)  # counters reset themselves: same bits on reuse
+    whole = _abi_matmul(xd, qd, sd, None)
+    torch.testing.assert_close(split, again, rtol=0, atol=0)
+    exact = oq.qrow_matmul_exact(x.float().numpy(), q.numpy(), s.numpy())
+    tol = FP32_TOL if dtype is torch.float32 else 4e-3
+    assert max_rel_err(split.float().cpu().numpy(), exact) < tol
+    assert max_rel_err(whole.float().cpu().numpy(), exact) < tol
+
+
+def test_stream_k_swiglu_matches_oracle(cuda):
+    from mrun_b200.dense_qstore_cuda import qrow_swiglu, qrow_workspace_bytes
+
+    n, k = 3584, 2048  # 224 tiles: the stream-K schedule
+    gen = torch.Generator(device="cpu").manual_seed(7)
+    qg = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    qu = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    sg = torch.rand(n, generator=gen) * 0.002
+    su = torch.rand(n, generator=gen) * 0.002
+    x = torch.randn(2, k, generator=gen).to(torch.bfloat16)
+    ws = torch.zeros(qrow_workspace_bytes(torch.device(cuda), n), dtype=torch.uint8, device=cuda)
+    y = qrow_swiglu(qg.to(cuda), sg.to(cuda), qu.to(cuda), su.to(cuda), x.to(cuda), workspace=ws)
+    ref = oq.swiglu_w8a16(x.float().numpy(), qg.numpy(), sg.numpy(), qu.numpy(), su.numpy())
+    assert max_rel_err(y.float().cpu().numpy(), ref) < BF16_TOL
+
+
+def test_stream_k_workspace_shared_across_widths(cuda):
+    """One workspace serves a chain of projections of different widths (the decoder's
+    qkv -> o -> down order); every call must equal the same call on a fresh workspace."""
+    from mrun_b200.dense_qstore_cuda import qrow_workspace_bytes
+
+    gen = torch.Generator(device="cpu").manual_seed(11)
+    shapes = [(1536, 512), (512, 1024), (1024, 512), (512, 1024), (1536, 512)]
+    size = max(qrow_workspace_bytes(torch.device(cuda), n) for n, _ in shapes)
+    shared = torch.zeros(size, dtype=torch.uint8, device=cuda)
+    for n, k in shapes * 2:
+        q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8).to(cuda)
+        s = (torch.rand(n, generator=gen) * 0.01).to(cuda)
+        x = torch.randn(1, k, generator=gen).to(torch.bfloat16).to(cuda)
+        fresh = torch.zeros(size, dtype=torch.uint8, device=cuda)
+        torch.testing.assert_close(_abi_matmul(x, q, s, shared), _abi_matmul(x, q, s, fresh), rtol=0, atol=0)
