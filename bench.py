@@ -308,6 +308,47 @@ def run_gemv_case(args) -> None:
                       "gbs": nbytes / avg_s / 1e9, "launches": args.steps}), flush=True)
 
 
+TC_CASES = {
+    # name: (m, n, k) of the tcgen05 int8 GEMM (W8A8 prefill at the config-2 shapes)
+    "int8-gemm-gateup": (512, 18944, 3584),
+    "int8-gemm-down": (512, 3584, 18944),
+}
+
+
+def run_tc_case(args) -> None:
+    """Small case for kernel captures: the tcgen05 int8 GEMM (exact int32 accumulators) at a
+    config-2 prefill shape, alternating two weight matrices. Prints one JSON line with the
+    device-timed average and the int8 tensor throughput; not the bench metric."""
+    import torch
+
+    from mrun_b200 import _lib
+
+    m, n, k = TC_CASES[args.case]
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device).manual_seed(0)
+    qx = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=device, generator=gen)
+    qws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=gen) for _ in range(2)]
+    acc = torch.empty(m, n, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def launch(i):
+        _lib.call("mrb_int8_gemm", qx.data_ptr(), qws[i % 2].data_ptr(), m, n, k, acc.data_ptr(), stream.cuda_stream)
+
+    for i in range(args.warmup):
+        launch(i)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    for i in range(args.steps):
+        launch(i)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    avg_s = e0.elapsed_time(e1) / 1000.0 / args.steps
+    print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "tops": 2 * m * n * k / avg_s / 1e12,
+                      "launches": args.steps}), flush=True)
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -444,13 +485,15 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=["decode", *GEMV_CASES], default="decode",
+    ap.add_argument("--case", choices=["decode", *GEMV_CASES, *TC_CASES], default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.case in GEMV_CASES:
         run_gemv_case(args)
+    elif args.case in TC_CASES:
+        run_tc_case(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

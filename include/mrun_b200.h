@@ -121,6 +121,11 @@ int mrb_residual_rms_norm(const void *residual_bf16, const void *update_bf16, in
 
 /* ---------------------------------------------------------------- (a) W8A8 */
 
+/* Number of bounded waits of the tensor-core (tcgen05) GEMMs that timed out since the last
+ * call, then reset; 0 in normal operation (non-zero: those launches' outputs are invalid).
+ * Synchronises the current device. No counterpart in the reference. */
+int mrb_tc_status(unsigned *timeouts);
+
 /* Per-token dynamic int8 activations exactly as the reference quantises them:
  * act_scale[r] = max|x[r] * keep| / 127 (fp32 division, 0 -> 1),
  * qx = clamp(round_half_even(x * keep / act_scale), -127, 127). keep (fp32 [k]) may be NULL.

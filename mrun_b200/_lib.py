@@ -42,6 +42,7 @@ SIGNATURES: dict[str, list] = {
     "mrb_residual_rms_norm": [_P, _P, _I64, _I64, _P, c_float, _P, _P, _P],
     "mrb_w8a8_quantize": [_P, c_int, _I64, _I64, _P, _P, _P, _P],
     "mrb_int8_gemm": [_P, _P, _I64, _I64, _I64, _P, _P],
+    "mrb_tc_status": [_P],
     "mrb_w8a8_protect_topk": [_P, c_int, _I64, _I64, c_int, _P, _P, _P],
     "mrb_w8a8_matmul": [_P, c_int, _I64, _I64, _P, _P, _I64, _P, c_int, _P, _P, _P, _P, _P, _P, _P],
     "mrb_router_topk": [_P, c_int, _I64, _I64, _I64, c_int, _P, _P, _P, _P],

@@ -406,7 +406,14 @@ __global__ void __launch_bounds__(I8_THREADS, 1) int8_gemm_kernel(I8GemmArgs a) 
     }
 }
 
+int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64_t k, const float* act_scale,
+                 const float* sw, const float* side, float* y, int32_t* acc_out, cudaStream_t s);
+
 static int launch_int8_gemm(const I8GemmArgs& a, cudaStream_t s) {
+  return tc_int8_gemm(a.qx, a.qw, a.m, a.n, a.k, a.act_scale, a.sw, a.side, a.y, a.acc_out, s);
+}
+
+[[maybe_unused]] static int launch_int8_gemm_mma_sync(const I8GemmArgs& a, cudaStream_t s) {
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(int8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, I8_SMEM);

@@ -82,3 +82,32 @@ def test_protect_topk_matches_oracle(cuda):
     assert max_rel_err(y, ref) < 1e-5
     exact = x.numpy().astype(np.float64) @ (qw.numpy().astype(np.float64) * sw.numpy()[:, None]).T
     assert np.array_equal(y.argmax(-1), exact.argmax(-1))
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (1, 256, 64),        # single row, one tile, k inside one 128-byte stage
+    (17, 300, 160),      # ragged m, n and k (zero-filled tile edges)
+    (128, 256, 128),     # exactly one tile and one stage
+    (200, 700, 1040),
+    (512, 3584, 3584),   # config-2 prefill o projection: many tiles per CTA, both accumulators
+])
+def test_tensor_core_int8_gemm_exact(m, n, k, cuda):
+    """The tcgen05 int8 GEMM (TMA + TMEM accumulators) equals exact integer matmul."""
+    from mrun_b200.w8a8 import _int8_gemm
+
+    gen = torch.Generator(device="cpu").manual_seed(m * 7 + n + k)
+    qx = torch.randint(-127, 128, (m, k), generator=gen, dtype=torch.int8)
+    qw = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    acc = _int8_gemm(qx.to(cuda), qw.to(cuda)).cpu().numpy()
+    exact = qx.numpy().astype(np.int64) @ qw.numpy().astype(np.int64).T
+    np.testing.assert_array_equal(acc.astype(np.int64), exact)
+
+
+def test_tensor_core_waits_never_timed_out(cuda):
+    import ctypes
+
+    from mrun_b200 import _lib
+
+    count = ctypes.c_uint(99)
+    _lib.call("mrb_tc_status", ctypes.addressof(count))
+    assert count.value == 0
