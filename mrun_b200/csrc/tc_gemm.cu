@@ -5,16 +5,20 @@
 // which is the reference's W8A8 rescale (engine/kernels/w8a8.py:67-125), bit-identical for
 // every accumulator because the accumulation is exact.
 //
-// Design: one persistent CTA per SM walks 128 x 256 output tiles (M x N) with the M tiles of
-// one N tile adjacent in the walk, so CTAs running together share the weight tile in L2.
-//  * warp 0, one thread: TMA producer. Each stage is a [128 x 128 B] activation box and a
-//    [256 x 128 B] weight box with the 128-byte swizzle, 4 stages in flight (192 KB).
-//  * warp 1: allocates 512 TMEM columns (two 128 x 256 int32 accumulators); one thread issues
-//    tcgen05.mma (M=128, N=256, K=32; four per stage) and commits each stage back to the
-//    producer and each finished accumulator to the epilogue.
+// Design: one persistent CTA per SM walks output tiles with the M tiles of one N tile
+// adjacent in the walk, so CTAs running together share the weight tile in L2. A tile is
+// HALVES 128-row accumulators x BN weight rows (256x256, 128x256 or 128x128, chosen by how
+// well the tiles fill the SMs): two halves share every weight stage, which halves the weight
+// bytes each CTA pulls from L2 per multiply-add (large problems are L2-bandwidth-bound with
+// 128-row tiles); smaller tiles keep more SMs busy on small problems.
+//  * warp 0, one thread: TMA producer. Each stage is a [BM x 128 B] activation box and a
+//    [BN x 128 B] weight box with the 128-byte swizzle; 3 to 6 stages (192 KB) in flight.
+//  * warp 1: allocates the TMEM accumulators (double-buffered for single-half tiles); one
+//    thread issues tcgen05.mma (M=128, N=BN, K=32) and commits each stage back to the
+//    producer and each finished tile to the epilogue.
 //  * warps 2-5: epilogue. Each warp owns the 32 TMEM lanes (tile rows) its index selects,
-//    loads 32 columns at a time with tcgen05.ld, rescales and stores; the accumulator is
-//    released to the MMA thread, which meanwhile fills the other one.
+//    loads 32 columns at a time with tcgen05.ld, rescales and stores, then releases the
+//    accumulators to the MMA thread.
 // Every wait is bounded: on a timeout the CTA records the failure, stops, and still frees
 // its TMEM. No load uses cluster multicast.
 #include "qrow_common.cuh"
@@ -24,23 +28,29 @@
 
 namespace mrb {
 
-constexpr int TC_BM = 128;             // tile rows (activation rows), MMA M
-constexpr int TC_BN = 256;             // tile columns (weight rows), MMA N
+constexpr int TC_HM = 128;             // MMA M (rows of one accumulator)
 constexpr int TC_BK = 128;             // bytes of k per stage: one 128-byte swizzle row
 constexpr int TC_UK = 32;              // k per MMA (kind::i8)
-constexpr int TC_STAGES = 4;
-constexpr int TC_A_BYTES = TC_BM * TC_BK;
-constexpr int TC_B_BYTES = TC_BN * TC_BK;
-constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
-constexpr int TC_ACC_COLS = TC_BN;               // int32 columns per accumulator
-constexpr unsigned TC_TMEM_COLS = 2 * TC_ACC_COLS;  // double-buffered
-constexpr int TC_THREADS = 192;
+constexpr int TC_THREADS = 192;        // warp 0 TMA, warp 1 MMA + TMEM owner, warps 2-5 epilogue
 constexpr int TC_EPI_THREADS = 128;
-constexpr size_t TC_SMEM = 1024 + (size_t)TC_STAGES * TC_STAGE_BYTES + 256;
+constexpr size_t TC_RING_BUDGET = 192 * 1024;
+
+// Tile shape: HALVES 128-row accumulators (sharing each weight stage) x BN weight rows.
+template <int HALVES, int BN>
+struct TcTile {
+  static constexpr int BM = TC_HM * HALVES;
+  static constexpr int A_BYTES = BM * TC_BK;
+  static constexpr int B_BYTES = BN * TC_BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (int)(TC_RING_BUDGET / STAGE_BYTES) < 6 ? (int)(TC_RING_BUDGET / STAGE_BYTES) : 6;
+  static constexpr int NBUF = HALVES == 1 ? 2 : 1;  // accumulator sets (double-buffered when they fit)
+  static constexpr unsigned TMEM_COLS = HALVES * BN * NBUF <= 256 ? 256u : 512u;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+};
 
 struct TcGemmArgs {
-  CUtensorMap map_x;  // qx [m, k] int8, box [128 rows, 128 B], 128-byte swizzle
-  CUtensorMap map_w;  // qw [n, k] int8, box [256 rows, 128 B], 128-byte swizzle
+  CUtensorMap map_x;  // qx [m, k] int8, box [BM rows, 128 B], 128-byte swizzle
+  CUtensorMap map_w;  // qw [n, k] int8, box [BN rows, 128 B], 128-byte swizzle
   int64_t m, n, k;
   int tiles_m, tiles_n, kblocks;
   const float* act_scale;  // [m] or null (then y is not written)
@@ -54,31 +64,34 @@ struct TcGemmArgs {
 // Timed-out waits of the tensor-core GEMM since the last status read (0 in normal operation).
 __device__ unsigned g_tc_timeouts = 0;
 
+template <int HALVES, int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __grid_constant__ TcGemmArgs a) {
+  using Tile = TcTile<HALVES, BN>;
+  constexpr int STAGES = Tile::STAGES, NBUF = Tile::NBUF, BM = Tile::BM;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
-  uint64_t* empty = full + TC_STAGES;
-  uint64_t* acc_full = empty + TC_STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Tile::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + NBUF;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NBUF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(acc_full + b, 1);
       mbar_init(acc_empty + b, TC_EPI_THREADS);
     }
     *abort_flag = 0;
     fence_proxy_async_smem();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, TC_TMEM_COLS);
+  if (warp == 1) tmem_alloc(tmem_slot, Tile::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -90,6 +103,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
     *abort_flag = 1;
     atomicAdd(&g_tc_timeouts, 1u);
   };
+  // accumulator of half h in buffer b
+  auto acc_col = [&](int b, int h) { return (uint32_t)((b * HALVES + h) * BN); };
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -104,11 +119,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
             fail_wait();
             break;
           }
-          unsigned char* st = smem + stage * TC_STAGE_BYTES;
-          mbar_arrive_expect_tx(full + stage, TC_STAGE_BYTES);
-          tma_load_2d(st, &a.map_x, kb * TC_BK, tm * TC_BM, full + stage);
-          tma_load_2d(st + TC_A_BYTES, &a.map_w, kb * TC_BK, tn * TC_BN, full + stage);
-          if (++stage == TC_STAGES) {
+          unsigned char* st = smem + stage * Tile::STAGE_BYTES;
+          mbar_arrive_expect_tx(full + stage, Tile::STAGE_BYTES);
+          tma_load_2d(st, &a.map_x, kb * TC_BK, tm * BM, full + stage);
+          tma_load_2d(st + Tile::A_BYTES, &a.map_w, kb * TC_BK, tn * BN, full + stage);
+          if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
@@ -118,7 +133,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc(UMMA_D_S32, UMMA_S8, UMMA_S8, TC_BM, TC_BN);
+      constexpr uint32_t idesc = umma_idesc(UMMA_D_S32, UMMA_S8, UMMA_S8, TC_HM, BN);
       int stage = 0, buf = 0;
       unsigned phase = 0, acc_phase = 0;
       for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
@@ -127,7 +142,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * TC_ACC_COLS);
+        // halves beyond the last activation row are skipped (their rows are all zero)
+        int halves = HALVES;
+        while (halves > 1 && (int64_t)(t % a.tiles_m) * BM + (halves - 1) * TC_HM >= a.m) --halves;
         bool ok = true;
         for (int kb = 0; kb < a.kblocks; ++kb) {
           if (!mbar_wait_bounded(full + stage, phase)) {
@@ -136,21 +153,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * TC_STAGE_BYTES);
-          const uint32_t sb = sa + TC_A_BYTES;
+          const uint32_t sa = smem_u32(smem + stage * Tile::STAGE_BYTES);
+          const uint32_t sb = sa + Tile::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < TC_BK / TC_UK; ++kk)
-            umma_i8(d, umma_desc_k_sw128(sa + kk * TC_UK), umma_desc_k_sw128(sb + kk * TC_UK), idesc,
-                    kb > 0 || kk > 0);
+          for (int kk = 0; kk < TC_BK / TC_UK; ++kk) {
+            const uint64_t db = umma_desc_k_sw128(sb + kk * TC_UK);
+#pragma unroll
+            for (int h = 0; h < HALVES; ++h)
+              if (h < halves)
+                umma_i8(tmem + acc_col(buf, h), umma_desc_k_sw128(sa + h * TC_HM * TC_BK + kk * TC_UK), db, idesc,
+                        kb > 0 || kk > 0);
+          }
           umma_commit(empty + stage);  // the stage is free once these MMAs have read it
-          if (++stage == TC_STAGES) {
+          if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(acc_full + buf);  // accumulator complete
-        if (++buf == 2) {
+        umma_commit(acc_full + buf);  // accumulators complete
+        if (++buf == NBUF) {
           buf = 0;
           acc_phase ^= 1u;
         }
@@ -173,49 +195,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
       }
       tc_fence_after();
       const int tm = t % a.tiles_m, tn = t / a.tiles_m;
-      const int64_t row = (int64_t)tm * TC_BM + q * 32 + lane;
-      const bool row_ok = row < a.m;
-      const float as = (row_ok && a.act_scale) ? a.act_scale[row] : 0.f;
-      for (int c0 = 0; c0 < TC_BN; c0 += 32) {
-        uint32_t v[32];
-        __syncwarp();
-        tmem_ld_32cols(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TC_ACC_COLS + c0), v);
-        const int64_t col0 = (int64_t)tn * TC_BN + c0;
-        if (!row_ok || col0 >= a.n) continue;
-        const int64_t o0 = row * a.n + col0;
-        const bool full_run = vec && col0 + 32 <= a.n;
-        if (a.acc_out) {
-          if (full_run) {
+      for (int h = 0; h < HALVES; ++h) {
+        if ((int64_t)tm * BM + h * TC_HM >= a.m) break;  // uniform: an empty half
+        const int64_t row = (int64_t)tm * BM + h * TC_HM + q * 32 + lane;
+        const bool row_ok = row < a.m;
+        const float as = (row_ok && a.act_scale) ? a.act_scale[row] : 0.f;
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld_32cols(tmem + ((uint32_t)(q * 32) << 16) + acc_col(buf, h) + (uint32_t)c0, v);
+          const int64_t col0 = (int64_t)tn * BN + c0;
+          if (!row_ok || col0 >= a.n) continue;
+          const int64_t o0 = row * a.n + col0;
+          const bool full_run = vec && col0 + 32 <= a.n;
+          if (a.acc_out) {
+            if (full_run) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<int4*>(a.acc_out + o0 + j) =
-                  make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
-          } else {
-            for (int j = 0; j < 32 && col0 + j < a.n; ++j) a.acc_out[o0 + j] = (int)v[j];
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<int4*>(a.acc_out + o0 + j) =
+                    make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
+            } else {
+              for (int j = 0; j < 32 && col0 + j < a.n; ++j) a.acc_out[o0 + j] = (int)v[j];
+            }
           }
-        }
-        if (a.y && a.act_scale) {
-          float out[32];
+          if (a.y && a.act_scale) {
+            float out[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int64_t col = col0 + j;
-            const float wsc = col < a.n ? a.sw[col] : 0.f;
-            float r = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), wsc);
-            if (a.side && col < a.n) r = __fadd_rn(a.side[o0 + j], r);
-            out[j] = r;
-          }
-          if (full_run) {
+            for (int j = 0; j < 32; ++j) {
+              const int64_t col = col0 + j;
+              const float wsc = col < a.n ? a.sw[col] : 0.f;
+              float r = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), wsc);
+              if (a.side && col < a.n) r = __fadd_rn(a.side[o0 + j], r);
+              out[j] = r;
+            }
+            if (full_run) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(a.y + o0 + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
-          } else {
-            for (int j = 0; j < 32 && col0 + j < a.n; ++j) a.y[o0 + j] = out[j];
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(a.y + o0 + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
+            } else {
+              for (int j = 0; j < 32 && col0 + j < a.n; ++j) a.y[o0 + j] = out[j];
+            }
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(acc_empty + buf);  // accumulator drained
-      if (++buf == 2) {
+      mbar_arrive(acc_empty + buf);  // accumulators drained
+      if (++buf == NBUF) {
         buf = 0;
         acc_phase ^= 1u;
       }
@@ -225,30 +250,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, TC_TMEM_COLS);
+  if (warp == 1) tmem_dealloc(tmem, Tile::TMEM_COLS);
 }
 
-// Launch the tensor-core W8A8 GEMM (see the file comment); arguments are checked by callers.
-int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64_t k, const float* act_scale,
-                 const float* sw, const float* side, float* y, int32_t* acc_out, cudaStream_t s) {
+template <int HALVES, int BN>
+static int tc_launch(TcGemmArgs& a, const int8_t* qx, const int8_t* qw, cudaStream_t s) {
+  using Tile = TcTile<HALVES, BN>;
+  auto kern = tc_int8_gemm_kernel<HALVES, BN>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(tc_int8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)TC_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile::SMEM);
     if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc int8 gemm: smem attribute: %s", cudaGetErrorString(e));
     configured = true;
   }
-  TcGemmArgs a{};
-  int st = encode_map_2d(&a.map_x, qx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, m, k, TC_BM, TC_BK,
+  int st = encode_map_2d(&a.map_x, qx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m, a.k, Tile::BM, TC_BK,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (!st)
-    st = encode_map_2d(&a.map_w, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, n, k, TC_BN, TC_BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    st = encode_map_2d(&a.map_w, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.n, a.k, BN, TC_BK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
+  a.tiles_m = (int)((a.m + Tile::BM - 1) / Tile::BM);
+  a.tiles_n = (int)((a.n + BN - 1) / BN);
+  const int64_t ntiles = (int64_t)a.tiles_m * a.tiles_n;
+  if (ntiles > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "tc int8 gemm: too many tiles");
+  const int grid = (int)std::min<int64_t>(ntiles, num_sms());
+  cudaError_t e = launch_kernel(kern, dim3(grid), dim3(TC_THREADS), Tile::SMEM, s, true, a);
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc int8 gemm: launch: %s", cudaGetErrorString(e));
+  return launch_status("tc int8 gemm");
+}
+
+// Launch the tensor-core W8A8 GEMM (see the file comment); arguments are checked by callers.
+// Tile shape by SM fill: 256-row tiles when they give every SM at least two, else 128 x 256
+// double-buffered tiles when those fill the SMs, else 128 x 128.
+int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64_t k, const float* act_scale,
+                 const float* sw, const float* side, float* y, int32_t* acc_out, cudaStream_t s) {
+  TcGemmArgs a{};
   a.m = m;
   a.n = n;
   a.k = k;
-  a.tiles_m = (int)((m + TC_BM - 1) / TC_BM);
-  a.tiles_n = (int)((n + TC_BN - 1) / TC_BN);
   a.kblocks = (int)((k + TC_BK - 1) / TC_BK);
   a.act_scale = act_scale;
   a.sw = sw;
@@ -256,12 +294,11 @@ int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64
   a.y = y;
   a.acc_out = acc_out;
   a.vec_store = (n % 4) == 0 && (!y || aligned(y, 16)) && (!acc_out || aligned(acc_out, 16));
-  const int64_t ntiles = (int64_t)a.tiles_m * a.tiles_n;
-  if (ntiles > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "tc int8 gemm: too many tiles");
-  const int grid = (int)std::min<int64_t>(ntiles, num_sms());
-  cudaError_t e = launch_kernel(tc_int8_gemm_kernel, dim3(grid), dim3(TC_THREADS), TC_SMEM, s, true, a);
-  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc int8 gemm: launch: %s", cudaGetErrorString(e));
-  return launch_status("tc int8 gemm");
+  const int64_t sms = num_sms();
+  auto tiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n + bn - 1) / bn); };
+  if (tiles(256, 256) >= 2 * sms) return tc_launch<2, 256>(a, qx, qw, s);
+  if (tiles(128, 256) >= sms) return tc_launch<1, 256>(a, qx, qw, s);
+  return tc_launch<1, 128>(a, qx, qw, s);
 }
 
 // Read and reset the count of timed-out waits (synchronises the device).
