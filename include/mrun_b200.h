@@ -210,6 +210,10 @@ int mrb_stable_route_reduce(const void *expert_out_bf16, const float *coef, cons
  * slot*stride_tok + d. rope_cos/rope_sin: fp32 [rope_len, head_dim/2] tables (NULL: no
  * rotation, a plain scatter). q_out: bf16 [tokens, hq, head_dim] rotated queries (may be
  * NULL). Invalid positions/pages are skipped and set *error_flag (device int32, may be NULL).
+ * q_norm / k_norm (bf16 [head_dim], may be NULL): per-head RMSNorm applied to each query /
+ * key head before the rotation, as the reference's Qwen3 q/k norm (fp32 mean of squares +
+ * norm_eps, normalised value rounded to bf16, times the weight rounded to bf16;
+ * engine/qwen3_moe_cuda.py:3282-3285, 3903-3904).
  * Replaces `_rope` (engine/dense_qstore_cuda.py:689-704) and `scatter_segmented_decode_kv`
  * (engine/kernels/segmented_gqa_decode.py:458-524). */
 int mrb_rope_kv_append(const void *q_in, const void *k_in, const void *v_in, int64_t in_row_stride,
@@ -218,7 +222,8 @@ int mrb_rope_kv_append(const void *q_in, const void *k_in, const void *v_in, int
                        const float *rope_sin, int64_t rope_len, void *q_out, void *k_cache,
                        void *v_cache, int64_t stride_page, int64_t stride_head, int64_t stride_tok,
                        int64_t page_size, const int32_t *block_table, int64_t block_table_stride,
-                       int64_t num_pages, int32_t *error_flag, void *stream);
+                       int64_t num_pages, int32_t *error_flag, const void *q_norm,
+                       const void *k_norm, float norm_eps, void *stream);
 
 /* Workspace bytes mrb_paged_attention needs for these sizes (0 when no split is used). */
 size_t mrb_paged_attention_workspace(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,

@@ -50,7 +50,7 @@ SIGNATURES: dict[str, list] = {
     "mrb_grouped_qrow": [_P, _P, _P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, c_int, _P, _P],
     "mrb_stable_route_reduce": [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
     "mrb_rope_kv_append": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P, _P,
-                           _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P],
+                           _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P, c_float, _P],
     "mrb_paged_attention_workspace": [_I64, _I64, _I64, _I64, _I64],
     "mrb_paged_attention": [_P, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P,
                             _P, _P, c_float, _I64, _P, _P, c_size_t, _P],

@@ -42,18 +42,44 @@ struct RopeArgs {
   int64_t bt_stride;
   int64_t num_pages;
   int32_t* error_flag;
+  const __nv_bfloat16* q_norm;  // [d] per-head RMSNorm weight for queries, or null
+  const __nv_bfloat16* k_norm;  // [d] for keys, or null
+  float norm_eps;
 };
 
 // Rotate-half RoPE exactly as the reference evaluates it in fp32
 // (engine/dense_qstore_cuda.py:689-704): out = bf16(v*cos + rot(v)*sin), with separately
 // rounded products (no fused multiply-add) and rot(v) = cat(-v[h:], v[:h]).
+// With a norm weight the head is first RMS-normalised as the reference's per-head q/k norm
+// (engine/qwen3_moe_cuda.py:3282-3285, 3903-3904): fp32 mean of squares, normalised value
+// rounded to bf16, times the bf16 weight rounded to bf16.
 // One CTA per token, one warp per head (queries, then keys, then values). Lane j handles
 // the rotation pairs (2j, 2j+1) of the first half and their partners in the second half.
 __device__ __forceinline__ void rope_head(const __nv_bfloat16* src, __nv_bfloat16* dst, int half, const float* c,
-                                          const float* s, int lane) {
+                                          const float* s, int lane, const __nv_bfloat16* nw = nullptr,
+                                          float eps = 0.f) {
+  float rs = 1.f;
+  if (nw) {
+    float ss = 0.f;
+    for (int j = 2 * lane; j < half; j += 64) {
+      const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j));
+      const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + half + j));
+      ss += lo.x * lo.x + lo.y * lo.y + hi.x * hi.x + hi.y * hi.y;
+    }
+    ss = warp_sum(ss);
+    rs = rsqrtf(ss / (float)(2 * half) + eps);
+  }
   for (int j = 2 * lane; j < half; j += 64) {
-    const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j));
-    const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + half + j));
+    float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + j));
+    float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + half + j));
+    if (nw) {
+      const float2 wl = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(nw + j));
+      const float2 wh = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(nw + half + j));
+      lo.x = round_bf16(round_bf16(lo.x * rs) * wl.x);
+      lo.y = round_bf16(round_bf16(lo.y * rs) * wl.y);
+      hi.x = round_bf16(round_bf16(hi.x * rs) * wh.x);
+      hi.y = round_bf16(round_bf16(hi.y * rs) * wh.y);
+    }
     float2 o_lo, o_hi;
     if (c) {
       const float2 cc = *reinterpret_cast<const float2*>(c + j);
@@ -101,11 +127,13 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(RopeArgs a) {
   const int64_t nq = a.q_out ? a.hq : 0;
   for (int64_t h = warp; h < nq + 2 * a.hkv; h += nwarps) {
     if (h < nq) {
-      rope_head(a.q_in + t * a.in_stride + h * a.d, a.q_out + (t * a.hq + h) * a.d, half, c, s, lane);
+      rope_head(a.q_in + t * a.in_stride + h * a.d, a.q_out + (t * a.hq + h) * a.d, half, c, s, lane, a.q_norm,
+                a.norm_eps);
     } else if (h < nq + a.hkv) {
       const int64_t kh = h - nq;
       rope_head(a.k_in + t * a.in_stride + kh * a.d,
-                a.k_cache + page * a.stride_page + kh * a.stride_head + slot * a.stride_tok, half, c, s, lane);
+                a.k_cache + page * a.stride_page + kh * a.stride_head + slot * a.stride_tok, half, c, s, lane,
+                a.k_norm, a.norm_eps);
     } else {
       const int64_t vh = h - nq - a.hkv;
       rope_head(a.v_in + t * a.in_stride + vh * a.d,
@@ -367,9 +395,12 @@ extern "C" int mrb_rope_kv_append(const void* q_in, const void* k_in, const void
                                   const float* rope_sin, int64_t rope_len, void* q_out, void* k_cache,
                                   void* v_cache, int64_t stride_page, int64_t stride_head, int64_t stride_tok,
                                   int64_t page_size, const int32_t* block_table, int64_t block_table_stride,
-                                  int64_t num_pages, int32_t* error_flag, void* stream) {
+                                  int64_t num_pages, int32_t* error_flag, const void* q_norm, const void* k_norm,
+                                  float norm_eps, void* stream) {
   if (tokens < 0 || hkv <= 0 || head_dim <= 0 || head_dim % 4 || page_size <= 0 || num_pages <= 0)
     return fail(MRB_ERR_ARG, "rope_kv_append: bad shape");
+  if ((q_norm && !aligned(q_norm, 4)) || (k_norm && !aligned(k_norm, 4)))
+    return fail(MRB_ERR_ARG, "rope_kv_append: norm weights must be 4-byte aligned");
   if (tokens == 0) return MRB_OK;
   if (!k_in || !v_in || !positions || !k_cache || !v_cache || !block_table)
     return fail(MRB_ERR_ARG, "rope_kv_append: null pointer");
@@ -383,7 +414,8 @@ extern "C" int mrb_rope_kv_append(const void* q_in, const void* k_in, const void
   RopeArgs a{(const __nv_bfloat16*)q_in, (const __nv_bfloat16*)k_in, (const __nv_bfloat16*)v_in, in_row_stride,
              tokens, hq, hkv, head_dim, positions, token_rows, rope_cos, rope_sin, rope_len,
              (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, stride_page, stride_head,
-             stride_tok, page_size, block_table, block_table_stride, num_pages, error_flag};
+             stride_tok, page_size, block_table, block_table_stride, num_pages, error_flag,
+             (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, norm_eps};
   launch_kernel(rope_kv_append_kernel, dim3((unsigned)tokens), dim3(256), 0, (cudaStream_t)stream, true, a);
   return launch_status("rope_kv_append");
 }

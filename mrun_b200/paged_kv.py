@@ -99,11 +99,14 @@ class PagedKVCache:
         in_row_stride: int | None = None,
         num_heads: int = 0,
         error_flag: torch.Tensor | None = None,
+        qk_norm: tuple[torch.Tensor, torch.Tensor] | None = None,
+        norm_eps: float = 1e-6,
     ) -> None:
         rope_kv_append(
             k_rows, v_rows, self.k[layer], self.v[layer], strides=self.strides, page_size=self.page_size,
             block_table=self.block_table, positions=positions, token_rows=token_rows, q_in=q_rows, q_out=q_out,
-            rope=rope, in_row_stride=in_row_stride, num_heads=num_heads, error_flag=error_flag,
+            rope=rope, in_row_stride=in_row_stride, num_heads=num_heads, error_flag=error_flag, qk_norm=qk_norm,
+            norm_eps=norm_eps,
         )
 
     def workspace_bytes(self, rows: int, num_heads: int, max_total_tokens: int) -> int:

@@ -119,8 +119,13 @@ def rope_kv_append(
     in_row_stride: int | None = None,
     num_heads: int = 0,
     error_flag: torch.Tensor | None = None,
+    qk_norm: tuple[torch.Tensor, torch.Tensor] | None = None,
+    norm_eps: float = 1e-6,
 ) -> None:
-    """Rotate (optional) and append one K/V position per token into a paged cache."""
+    """Rotate (optional) and append one K/V position per token into a paged cache.
+
+    ``qk_norm`` = (q weight, k weight), bf16 [head_dim]: per-head RMSNorm of queries and keys
+    before the rotation (the Qwen3 q/k norm)."""
     tokens = int(positions.numel())
     hkv, d = int(k_cache.shape[1]), int(k_cache.shape[-1])
     device = _lib.require_cuda(k_in, v_in, k_cache, v_cache, block_table, positions, what="KV append")
@@ -133,7 +138,8 @@ def rope_kv_append(
         0 if cos is None else int(cos.shape[0]), _lib.ptr(q_out), k_cache.data_ptr(), v_cache.data_ptr(),
         strides[0], strides[1], strides[2], page_size, block_table.data_ptr(),
         int(block_table.stride(0)) if block_table.ndim > 1 else 1, int(k_cache.shape[0]),
-        _lib.ptr(error_flag), _lib.stream_handle(device),
+        _lib.ptr(error_flag), _lib.ptr(qk_norm[0] if qk_norm else None), _lib.ptr(qk_norm[1] if qk_norm else None),
+        float(norm_eps), _lib.stream_handle(device),
     )
 
 

@@ -1,0 +1,102 @@
+"""Ragged MoE decode steps (Qwen3-MoE family) against the CPU step oracle.
+
+Each step is checked on its own: the oracle gets the same committed K/V the device step saw
+(gathered from the paged cache) and recomputes the step with the reference's bf16
+boundaries (engine/qwen3_moe_cuda.py:3790-3960). The device's greedy token must be the
+oracle's argmax unless the oracle's logits put it within bf16 noise of the best (a near
+tie), and the device's chosen-logit value must track the oracle's. Routes (top-k expert
+indices) must match wherever the oracle's k-th/k+1-th router margin is not a near tie.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.moe_decoder import moe_decode_step
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_GAP_TOL = 2e-2
+
+
+def _tiny():
+    from mrun_b200.moe_engine import MoeConfig
+
+    return MoeConfig(num_layers=2, hidden=256, heads=4, kv_heads=2, head_dim=64, experts=8, top_k=2,
+                     expert_ffn=128, vocab=500)
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_moe_decode_steps_match_oracle(graph, cuda):
+    from mrun_b200.moe_engine import MoeDecoder, MoeWeights
+
+    cfg = _tiny()
+    w = MoeWeights.synthetic(cfg, cuda, seed=3)
+    lengths = [5, 17, 33, 1, 64]
+    rows = len(lengths)
+    steps = 4
+    dec = MoeDecoder(w, max_rows=8, max_seq_len=96, device=cuda)
+    first = torch.tensor([7, 123, 42, 499, 0])
+    dec.load_synthetic_context(lengths, first, steps=steps, seed=1)
+    host = w.to_host()
+    if graph:
+        dec.capture(rows)
+    ids = first.numpy()
+    pos = np.array(lengths)
+    near_ties = 0
+    for _ in range(steps):
+        ctx_k = [[dec.gather_kv(li, r, int(pos[r]))[0] for r in range(rows)] for li in range(cfg.num_layers)]
+        ctx_v = [[dec.gather_kv(li, r, int(pos[r]))[1] for r in range(rows)] for li in range(cfg.num_layers)]
+        logits, _ = moe_decode_step(host, cfg, ids, pos, ctx_k, ctx_v)
+        dec.routes = []
+        if graph:
+            dec.routes = None
+        dec.step(rows)
+        torch.cuda.synchronize()
+        got = dec.next_ids[:rows].cpu().numpy()
+        val = dec.next_val[:rows].cpu().numpy()
+        for r in range(rows):
+            best = float(logits[r].max())
+            gap = best - float(logits[r, got[r]])
+            assert gap <= LOGIT_GAP_TOL, f"row {r}: token {got[r]} is {gap:.4g} below the oracle's best"
+            near_ties += int(got[r] != int(np.argmax(logits[r])))
+            assert abs(val[r] - float(logits[r, got[r]])) <= LOGIT_GAP_TOL + 1e-2 * abs(best)
+        ids = got
+        pos = pos + 1
+    dec.check_errors()
+    assert near_ties <= 2
+
+
+def test_moe_routes_match_oracle_first_layer(cuda):
+    """Layer-0 top-k expert indices equal the oracle's wherever the router margin is clear."""
+    from mrun_b200.moe_engine import MoeDecoder, MoeWeights
+    from oracle.moe import softmax_f32
+
+    cfg = _tiny()
+    w = MoeWeights.synthetic(cfg, cuda, seed=5)
+    lengths = [3, 9, 20]
+    dec = MoeDecoder(w, max_rows=4, max_seq_len=40, device=cuda)
+    first = torch.tensor([1, 2, 3])
+    dec.load_synthetic_context(lengths, first, steps=1, seed=2)
+    host = w.to_host()
+    ctx_k = [[dec.gather_kv(li, r, lengths[r])[0] for r in range(3)] for li in range(cfg.num_layers)]
+    ctx_v = [[dec.gather_kv(li, r, lengths[r])[1] for r in range(3)] for li in range(cfg.num_layers)]
+    _, routes = moe_decode_step(host, cfg, first.numpy(), np.array(lengths), ctx_k, ctx_v)
+    dec.routes = []
+    dec.step(3)
+    got = dec.routes[0].cpu().numpy()
+    assert np.array_equal(np.sort(got, axis=1), np.sort(routes[0], axis=1))
+
+
+def test_expert_parallel_shards_hold_the_same_experts(cuda):
+    """A sharded model materialises exactly the unsharded model's experts."""
+    from mrun_b200.expert_parallel import ExpertShard
+    from mrun_b200.moe_engine import MoeWeights
+
+    cfg = _tiny()
+    full = MoeWeights.synthetic(cfg, cuda, seed=9)
+    part = MoeWeights.synthetic(cfg, cuda, seed=9, shard=ExpertShard(4, 2, cfg.experts))
+    for a, b in zip(full.layers, part.layers):
+        assert torch.equal(a.pages[4:6], b.pages)
+        assert torch.equal(a.qkv.codes, b.qkv.codes)
