@@ -349,6 +349,81 @@ def run_tc_case(args) -> None:
                       "launches": args.steps}), flush=True)
 
 
+MOE_ROWS = 32
+
+
+def run_moe_case(args) -> None:
+    """Config 4: Qwen3-30B-A3B-shape MoE decoder, 32 ragged rows per GPU with contexts drawn
+    uniformly from [256, 4096] (seeded per rank; K/V pages hold random bf16 values instead of a
+    prefill), greedy decode. One GPU: CUDA-graph steps. N GPUs (torchrun): experts sharded
+    over the ranks with NCCL all-to-all dispatch/return, each rank decoding its own rows
+    (weak scaling). Prints one JSON line on rank 0; not the headline metric."""
+    import numpy as np
+    import torch
+
+    from mrun_b200.expert_parallel import ExpertShard
+    from mrun_b200.moe_engine import MoeConfig, MoeDecoder, MoeWeights
+
+    world, rank, local = _dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    cfg = MoeConfig.qwen3_30b_a3b()
+    shard = ExpertShard(world, rank, cfg.experts) if world > 1 else None
+    weights = MoeWeights.synthetic(cfg, device, seed=0, shard=shard)
+    rng = np.random.default_rng(rank)
+    lengths = [int(v) for v in rng.integers(256, 4097, MOE_ROWS)]
+    total = args.warmup + args.steps
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        group = dist.group.WORLD
+    dec = MoeDecoder(weights, max_rows=MOE_ROWS, max_seq_len=4096 + total + 16, device=device, group=group,
+                     world=world)
+    first = torch.from_numpy(rng.integers(0, cfg.vocab, MOE_ROWS))
+    dec.load_synthetic_context(lengths, first, steps=total, seed=rank)
+    if world == 1:
+        dec.capture(MOE_ROWS)
+    for _ in range(args.warmup):
+        dec.step(MOE_ROWS)
+    stream = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        torch.cuda.cudart().cudaProfilerStart()
+        e0.record(stream)
+        for _ in range(args.steps):
+            dec.step(MOE_ROWS)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        torch.cuda.cudart().cudaProfilerStop()
+    _barrier(world)
+    step_s = _max_over_ranks(e0.elapsed_time(e1) / 1000.0 / args.steps, world)
+    dec.check_errors()
+    if rank == 0:
+        # expected distinct experts per layer for 32 rows x top-8 of 128
+        distinct = cfg.experts * (1.0 - (1.0 - cfg.top_k / cfg.experts) ** MOE_ROWS)
+        expert_bytes = distinct * weights.layout.page_stride * cfg.num_layers
+        kv_bytes = sum(lengths) * 2 * cfg.num_layers * cfg.kv_heads * cfg.head_dim * 2
+        line = {
+            "case": "moe-decode", "metric": "MoE decode tokens/s (config 4)", "unit": "tokens/s",
+            "value": MOE_ROWS * world / step_s, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_s * 1000.0, "scaling": "weak",
+            "config": {"workload": "config4: Qwen3-30B-A3B-shape MoE, 48 layers, 128 experts top-8, "
+                                   "32 ragged rows per GPU, contexts U[256,4096]",
+                       "rows_per_gpu": MOE_ROWS, "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                       "graph": world == 1, "mean_context": float(np.mean(lengths))},
+            "algorithmic_bytes_per_step_per_gpu": {"experts": expert_bytes / world, "kv": kv_bytes},
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -485,7 +560,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=["decode", *GEMV_CASES, *TC_CASES], default="decode",
+    ap.add_argument("--case", choices=["decode", "moe-decode", *GEMV_CASES, *TC_CASES], default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -494,6 +569,8 @@ def main() -> None:
         run_gemv_case(args)
     elif args.case in TC_CASES:
         run_tc_case(args)
+    elif args.case == "moe-decode":
+        run_moe_case(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -20,6 +20,13 @@ namespace mrb {
 constexpr int AT_TILE = 16;
 constexpr int AT_MAX_GROUP = 16;
 constexpr int AT_MAX_SPLIT = 128;  // splits per (row, head); merge stats live in wacc
+constexpr int AT_STAGES = 4;       // K/V tiles per CTA in shared memory (cp.async ring)
+#ifndef AT_CTAS_PER_SM
+#define AT_CTAS_PER_SM 8  // split-K target: CTAs per SM
+#endif
+#ifndef AT_MIN_TILES
+#define AT_MIN_TILES 4  // split-K: fewest 16-token tiles per split
+#endif
 
 // ------------------------------------------------------------------ RoPE + KV append
 
@@ -173,9 +180,10 @@ __device__ __forceinline__ int64_t kv_offset(const AttnArgs& a, int64_t seq, int
 }
 
 // Decode attention, one warp per query head of the GQA group (blockDim = 32 * group).
-// The CTA owns (query row, KV head, split) and walks the split's 16-token tiles: all threads
-// stage the tile's K and V in shared memory (K XOR-swizzled so the score reads are
-// conflict-free), then every warp runs an fp32 online softmax for its head. Score phase:
+// The CTA owns (query row, KV head, split) and walks the split's 16-token tiles through a
+// 4-stage cp.async ring in shared memory (K XOR-swizzled so the score reads are
+// conflict-free; three tiles in flight while one is scored, one barrier per tile), and every
+// warp runs an fp32 online softmax for its head. Score phase:
 // lane = (token, half of the head dim); value phase: lane owns D/32 consecutive dims.
 // Splits publish (max, sum, acc) partials; the last CTA of the (row, head) group merges them
 // in split order (deterministic), each warp merging its own head.
@@ -194,8 +202,8 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
   pdl_launch_dependents();
   pdl_wait();
 
-  __shared__ __align__(16) __nv_bfloat16 ks[AT_TILE][D];
-  __shared__ __align__(16) __nv_bfloat16 vs[AT_TILE][D];
+  __shared__ __align__(16) __nv_bfloat16 ks[AT_STAGES][AT_TILE][D];
+  __shared__ __align__(16) __nv_bfloat16 vs[AT_STAGES][AT_TILE][D];
   __shared__ bool is_last;
 
   const int64_t seq = a.row_seq ? a.row_seq[r] : r;
@@ -204,8 +212,41 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
   const int64_t total = len + (has_new ? 1 : 0);
   const int64_t t_begin = (int64_t)split * a.tiles_per_split * AT_TILE;
   const int64_t t_end = min(total, t_begin + (int64_t)a.tiles_per_split * AT_TILE);
+  const int ntile = t_end > t_begin ? (int)((t_end - t_begin + AT_TILE - 1) / AT_TILE) : 0;
   const int64_t khead = (int64_t)kvh * a.stride_head;
   const int my_tok = lane & 15, half = lane >> 4;
+
+  // ---- K/V tile ring: tile i of this split lands in stage i % AT_STAGES (cp.async, zero fill
+  // past the split's end); AT_STAGES - 1 tiles are in flight while one is scored
+  auto issue = [&](int i) {
+    if (i < ntile) {
+      const int st = i % AT_STAGES;
+      const int64_t t0 = t_begin + (int64_t)i * AT_TILE;
+      for (int e = tid; e < AT_TILE * CH; e += blockDim.x) {
+        const int t = e / CH, c = e - t * CH;
+        const int64_t tok = t0 + t;
+        const bool ok = tok < t_end;
+        const __nv_bfloat16 *kp = a.k_cache, *vp = a.v_cache;
+        if (ok) {
+          if (has_new && tok == len) {
+            kp = a.k_new + (r * a.hkv + kvh) * D;
+            vp = a.v_new + (r * a.hkv + kvh) * D;
+          } else {
+            const int64_t off = kv_offset(a, seq, tok, khead);
+            kp = a.k_cache + off;
+            vp = a.v_cache + off;
+          }
+        }
+        cp_async16_zfill(reinterpret_cast<uint4*>(&ks[st][t][0]) + (c ^ (t & 7)),
+                         reinterpret_cast<const uint4*>(kp) + (ok ? c : 0), ok);
+        cp_async16_zfill(reinterpret_cast<uint4*>(&vs[st][t][0]) + c, reinterpret_cast<const uint4*>(vp) + (ok ? c : 0),
+                         ok);
+      }
+    }
+    cp_async_commit_group();
+  };
+#pragma unroll
+  for (int i = 0; i < AT_STAGES - 1; ++i) issue(i);
 
   // this warp's query head, pre-scaled, for this lane's half of the dims
   float qreg[HALF];
@@ -227,41 +268,24 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
 #pragma unroll
   for (int i = 0; i < VD; ++i) acc[i] = 0.f;
 
-  for (int64_t t0 = t_begin; t0 < t_end; t0 += AT_TILE) {
-    // ---- stage K (swizzled) and V of 16 tokens
-    for (int e = tid; e < AT_TILE * CH; e += blockDim.x) {
-      const int t = e / CH, c = e - t * CH;
-      const int64_t tok = t0 + t;
-      uint4 kraw = make_uint4(0, 0, 0, 0), vraw = make_uint4(0, 0, 0, 0);
-      if (tok < t_end) {
-        const __nv_bfloat16 *kp, *vp;
-        if (has_new && tok == len) {
-          kp = a.k_new + (r * a.hkv + kvh) * D;
-          vp = a.v_new + (r * a.hkv + kvh) * D;
-        } else {
-          const int64_t off = kv_offset(a, seq, tok, khead);
-          kp = a.k_cache + off;
-          vp = a.v_cache + off;
-        }
-        kraw = __ldg(reinterpret_cast<const uint4*>(kp) + c);
-        vraw = __ldg(reinterpret_cast<const uint4*>(vp) + c);
-      }
-      reinterpret_cast<uint4*>(&ks[t][0])[c ^ (t & 7)] = kraw;
-      reinterpret_cast<uint4*>(&vs[t][0])[c] = vraw;
-    }
-    __syncthreads();
+  for (int i = 0; i < ntile; ++i) {
+    cp_async_wait_group<AT_STAGES - 2>();
+    __syncthreads();  // tile i is in shared memory; every warp is done with tile i - 1
+    issue(i + AT_STAGES - 1);  // refills the stage tile i - 1 used
+    const int st = i % AT_STAGES;
+    const int64_t t0 = t_begin + (int64_t)i * AT_TILE;
     // ---- score of this lane's token for this warp's head
     float sc = 0.f;
 #pragma unroll
-    for (int i = 0; i < HALF / 8; ++i) {
-      const int c = half * (HALF / 8) + i;
-      const uint4 raw = reinterpret_cast<const uint4*>(&ks[my_tok][0])[c ^ (my_tok & 7)];
+    for (int c8 = 0; c8 < HALF / 8; ++c8) {
+      const int c = half * (HALF / 8) + c8;
+      const uint4 raw = reinterpret_cast<const uint4*>(&ks[st][my_tok][0])[c ^ (my_tok & 7)];
       const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __bfloat1622float2(h2[j]);
-        sc = fmaf(qreg[i * 8 + 2 * j], f.x, sc);
-        sc = fmaf(qreg[i * 8 + 2 * j + 1], f.y, sc);
+        sc = fmaf(qreg[c8 * 8 + 2 * j], f.x, sc);
+        sc = fmaf(qreg[c8 * 8 + 2 * j + 1], f.y, sc);
       }
     }
     sc += __shfl_xor_sync(0xffffffffu, sc, 16);
@@ -278,13 +302,13 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
     l = l * alpha + sum;
     m = m_new;
 #pragma unroll
-    for (int i = 0; i < VD; ++i) acc[i] *= alpha;
+    for (int k = 0; k < VD; ++k) acc[k] *= alpha;
     // ---- acc += sum_t p_t * V[t][lane dims]
 #pragma unroll
     for (int t = 0; t < AT_TILE; ++t) {
       const float pt = __shfl_sync(0xffffffffu, p, t);
       if (VD == 4) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(&vs[t][lane * 4]);
+        const uint2 raw = *reinterpret_cast<const uint2*>(&vs[st][t][lane * 4]);
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
         const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
         acc[0] = fmaf(pt, f0.x, acc[0]);
@@ -292,13 +316,13 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
         acc[2 % VD] = fmaf(pt, f1.x, acc[2 % VD]);
         acc[3 % VD] = fmaf(pt, f1.y, acc[3 % VD]);
       } else {
-        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vs[t][lane * 2]));
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vs[st][t][lane * 2]));
         acc[0] = fmaf(pt, f.x, acc[0]);
         acc[1 % VD] = fmaf(pt, f.y, acc[1 % VD]);
       }
     }
-    __syncthreads();
   }
+  cp_async_wait_group<0>();
 
   __nv_bfloat16* out = a.out + (r * a.hq + (int64_t)kvh * group + g) * D + lane * VD;
   if (a.nsplit == 1) {
@@ -362,11 +386,16 @@ struct SplitPlan {
   int tiles_per_split;
 };
 
+// Splits per (row, head): enough CTAs for about 8 per SM (the kernel is latency-bound per
+// CTA; its 32 KB tile ring and 32-512 threads let several share an SM), each split at least
+// 4 tiles (2 for contexts up to 64 tiles) so the ring has tiles to overlap, at most
+// AT_MAX_SPLIT splits.
 static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total) {
   const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
   const int64_t groups = std::max<int64_t>(1, rows * hkv);
-  const int64_t target = (2LL * num_sms() + groups - 1) / groups;  // splits wanted per group
-  int64_t tps = std::max<int64_t>(2, (tiles + target - 1) / target);
+  const int64_t target = ((int64_t)AT_CTAS_PER_SM * num_sms() + groups - 1) / groups;  // splits per group
+  const int64_t min_tiles = tiles <= 64 ? 2 : AT_MIN_TILES;  // short contexts: more, shorter splits
+  int64_t tps = std::max<int64_t>(min_tiles, (tiles + target - 1) / target);
   tps = std::min<int64_t>(tps, tiles);
   tps = std::max<int64_t>(tps, (tiles + AT_MAX_SPLIT - 1) / AT_MAX_SPLIT);
   const int64_t ns = (tiles + tps - 1) / tps;
@@ -375,7 +404,7 @@ static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total) {
 
 // Workspace layout: AT_MAX_COUNTERS merge counters at offset 0 (fixed, so that a buffer
 // reused across different shapes never finds stale partials where counters live), then the
-// fp32 partials. Splitting only happens for fewer than 2 * SMs (row, head) groups.
+// fp32 partials. Splitting only happens for fewer than 8 * SMs (row, head) groups.
 constexpr int64_t AT_MAX_COUNTERS = 4096;
 constexpr size_t AT_COUNTER_BYTES = AT_MAX_COUNTERS * sizeof(unsigned);
 

@@ -180,10 +180,11 @@ __global__ void __launch_bounds__(RC_THREADS) route_compile_kernel(
 
 constexpr int GX_WARPS = 8;
 constexpr int GX_THREADS = GX_WARPS * 32;
-constexpr int GX_ROWS = 16;
-constexpr int GX_KB = 64;
-constexpr int GX_UNROLL = 4;
-constexpr int GX_MAXR = 8;  // activation rows per pass (one n8 mma tile)
+constexpr int GX_ROWS = 16;       // weight rows per warp tile (mma M)
+constexpr int GX_KB = 64;         // k elements per step and stream
+constexpr int GX_MAXR = 8;        // activation rows per pass (one n8 mma tile)
+constexpr int GX_STAGES = 4;      // cp.async ring depth per thread
+constexpr int GX_STAGE_BYTES = 2 * 2 * GX_THREADS * 16;  // 2 streams x rows (g, g+8) x 16 B per thread
 
 struct GroupedArgs {
   const __nv_bfloat16* x;    // activation rows
@@ -199,49 +200,141 @@ struct GroupedArgs {
   int64_t n, k;              // per-expert output rows (gate rows for SwiGLU) and in_features
   int64_t up_rows;           // SwiGLU: up rows start at this row offset inside the page
   __nv_bfloat16* y;          // [A, n]
+  int chunks;                // tile chunks per expert (work items per expert)
+  int chunk_tiles;           // 16-row tiles per chunk
 };
 
-// Work item = (expert, 16-row tile). A CTA streams the tile's weights with 8 warps
-// splitting k (L1-bypassing 16-byte loads, 4 blocks in flight per warp) and applies them to
-// the expert's rows in passes of 8 (activations staged as exact power-of-two-scaled f16).
-// Each output row depends only on its own activation row, so results do not depend on how
-// many rows an expert received (bit-identical across expert-parallel world sizes).
+__host__ __device__ inline int gx_steps(int64_t k, bool halves) {
+  const int nkb = (int)((k + GX_KB - 1) / GX_KB);
+  return halves ? (nkb + 1) / 2 : nkb;
+}
+__host__ __device__ inline int gx_xlen(int64_t k, bool halves) { return gx_steps(k, halves) * GX_KB * (halves ? 2 : 1); }
+__host__ __device__ inline size_t gx_xs_bytes(int64_t k, bool halves) {
+  return ((size_t)GX_MAXR * (gx_xlen(k, halves) + 8) * 2 + 15) & ~size_t(15);
+}
+__host__ inline size_t gx_smem_bytes(int64_t k, bool halves) {
+  return (size_t)GX_STAGES * GX_STAGE_BYTES + gx_xs_bytes(k, halves) + 32 * 4;
+}
+
+// Grouped int8 expert projection over ragged per-expert row counts.
+//
+// Work item = (expert, chunk of 16-row tiles); a CTA walks items blockIdx.x, +gridDim.x, ...
+// (experts without rows are skipped). Per item and pass of up to 8 rows it stages the
+// expert's activation rows once (gathered through row_ids, exact power-of-two-scaled f16),
+// then each warp owns whole tiles of the chunk: it streams the tile's weights over the full
+// k through a per-thread cp.async ring (rows g and g+8, two streams per step: the gate and
+// up rows for SwiGLU, the two k halves otherwise), accumulates on mma.sync in fp32 and
+// writes its outputs directly -- no cross-warp reduction, no barrier inside an item. The
+// ring prefetches across tiles, passes and items. Codes convert to exact f16, so each output
+// row depends only on its own activation row (bit-identical for any row grouping, hence
+// across expert-parallel world sizes).
 template <bool SWIGLU>
 __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs a) {
-  constexpr int NSTREAM = SWIGLU ? 2 : 1;
+  constexpr bool HALVES = !SWIGLU;
   extern __shared__ __align__(16) unsigned char smem[];
   const int64_t K = a.k;
-  const int kpad = (int)((K + GX_KB - 1) / GX_KB) * GX_KB;
-  const int xstride = kpad + 8;
-  const int nkb = kpad / GX_KB;
-  __half* xs = reinterpret_cast<__half*>(smem);
-  float* red = reinterpret_cast<float*>(smem + (((size_t)GX_MAXR * xstride * 2 + 15) & ~size_t(15)));
-  float* rscale = red + GX_WARPS * NSTREAM * GX_ROWS * 8;  // [8] 2^-e, [8..16) 2^e
-  unsigned* rmax = reinterpret_cast<unsigned*>(rscale + 16);
+  const int nks = gx_steps(K, HALVES);    // k steps per tile
+  const int xlen = gx_xlen(K, HALVES);
+  const int xstride = xlen + 8;
+  const int kspan = HALVES ? nks * GX_KB : 0;
+  unsigned char* ring = smem;
+  __half* xs = reinterpret_cast<__half*>(smem + (size_t)GX_STAGES * GX_STAGE_BYTES);
+  float* rscale = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + gx_xs_bytes(K, HALVES));
+  unsigned* rmax = reinterpret_cast<unsigned*>(rscale + 16);  // [8]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int64_t rtiles = (a.n + GX_ROWS - 1) / GX_ROWS;
-  const int64_t items = (int64_t)a.E * rtiles;
+  const int rtiles = (int)((a.n + GX_ROWS - 1) / GX_ROWS);
+  const int items = a.E * a.chunks;
+  const bool k_check = (int64_t)xlen != K;
+
   pdl_launch_dependents();
-  pdl_wait();
-  for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
-    const int e = (int)(item / rtiles);
-    const int64_t tile = item - (int64_t)e * rtiles;
-    const int cnt = a.counts[e];
-    if (cnt == 0) continue;  // uniform across the CTA
-    const int st = a.starts[e];
+  pdl_wait();  // routes and activations come from the previous kernels
+
+  auto item_expert = [&](int item) { return item / a.chunks; };
+  auto item_t0 = [&](int item) { return (item - item_expert(item) * a.chunks) * a.chunk_tiles; };
+  auto item_t1 = [&](int item) { return min(rtiles, item_t0(item) + a.chunk_tiles); };
+  auto item_passes = [&](int item) { return (a.counts[item_expert(item)] + GX_MAXR - 1) / GX_MAXR; };
+
+  // ---- per-thread prefetch cursor over (item, pass, this warp's tile, k step)
+  int pf_item = blockIdx.x, pf_pass = 0, pf_tile = 0, pf_step = 0, pf_koff = 0, slot_w = 0;
+  const int8_t* pf_row0 = nullptr;
+  const int8_t* pf_row1 = nullptr;
+  int64_t pf_delta = 0;
+  auto pf_load_tile = [&]() {  // pointers of (pf_item, pf_tile) at step 0
+    const int e = item_expert(pf_item);
     const int slot = a.slot_of ? a.slot_of[e] : e;
     const int8_t* codes = a.codes + (int64_t)slot * a.codes_stride;
+    const int64_t r0 = min((int64_t)pf_tile * GX_ROWS + g, a.n - 1);
+    const int64_t r1 = min((int64_t)pf_tile * GX_ROWS + g + 8, a.n - 1);
+    pf_koff = 16 * c;
+    pf_row0 = codes + r0 * K + pf_koff;
+    pf_row1 = codes + r1 * K + pf_koff;
+    pf_delta = SWIGLU ? a.up_rows * K : (int64_t)kspan;
+    pf_step = 0;
+  };
+  // settle on the next (item, pass, tile) that holds work for this warp, from pf_item/pf_pass/pf_tile
+  auto pf_settle = [&](bool fresh_item) {
+    for (; pf_item < items; pf_item += gridDim.x, fresh_item = true) {
+      if (fresh_item) {
+        if (a.counts[item_expert(pf_item)] == 0) continue;
+        pf_pass = 0;
+        pf_tile = item_t0(pf_item) + warp;
+      }
+      const int t1 = item_t1(pf_item), passes = item_passes(pf_item);
+      while (pf_pass < passes) {
+        if (pf_tile < t1 && nks > 0) {
+          pf_load_tile();
+          return;
+        }
+        ++pf_pass;
+        pf_tile = item_t0(pf_item) + warp;
+      }
+    }
+  };
+  pf_settle(true);
+  auto issue = [&]() {
+    if (pf_item < items) {
+      unsigned char* st = ring + slot_w * GX_STAGE_BYTES + tid * 16;
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const int64_t d = s == 0 ? 0 : pf_delta;
+        const bool ok = !k_check || pf_koff + (HALVES ? s * kspan : 0) < K;
+        cp_async16_zfill(st + (s * 2 + 0) * GX_THREADS * 16, ok ? pf_row0 + d : a.codes, ok);
+        cp_async16_zfill(st + (s * 2 + 1) * GX_THREADS * 16, ok ? pf_row1 + d : a.codes, ok);
+      }
+      pf_row0 += GX_KB;
+      pf_row1 += GX_KB;
+      pf_koff += GX_KB;
+      if (++pf_step == nks) {
+        pf_tile += GX_WARPS;
+        pf_settle(false);
+      }
+    }
+    cp_async_commit_group();
+    slot_w = slot_w + 1 == GX_STAGES ? 0 : slot_w + 1;
+  };
+#pragma unroll
+  for (int p = 0; p < GX_STAGES - 1; ++p) issue();
+
+  int slot_r = 0;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int e = item_expert(item);
+    const int cnt = a.counts[e];
+    if (cnt == 0) continue;  // uniform across the CTA
+    const int st0 = a.starts[e];
+    const int slot = a.slot_of ? a.slot_of[e] : e;
     const float* scales = a.scales + (int64_t)slot * a.scales_stride;
-    const int64_t r0 = min(tile * GX_ROWS + g, a.n - 1), r1 = min(tile * GX_ROWS + g + 8, a.n - 1);
+    const int t0 = item_t0(item), t1 = item_t1(item);
     for (int p0 = 0; p0 < cnt; p0 += GX_MAXR) {
       const int rows = min(GX_MAXR, cnt - p0);
-      // ---- stage this pass's activation rows
+      // ---- stage this pass's activation rows (raw copy + row max, then exact scaled f16)
+      __syncthreads();  // every warp is done with the previous pass's rows
       if (tid < GX_MAXR) rmax[tid] = 0u;
       __syncthreads();
-      for (int idx = tid; idx < rows * (int)(K / 8); idx += GX_THREADS) {
-        const int r = idx / (int)(K / 8), v = idx - r * (int)(K / 8);
-        const int64_t arow = st + p0 + r;
+      const int vpr = (int)(K / 8);
+      for (int idx = tid; idx < rows * vpr; idx += GX_THREADS) {
+        const int r = idx / vpr, v = idx - r * vpr;
+        const int64_t arow = st0 + p0 + r;
         const int64_t src = a.row_ids ? a.row_ids[arow] : arow;
         const uint4 raw = __ldg(reinterpret_cast<const uint4*>(a.x + src * K) + v);
         *reinterpret_cast<uint4*>(xs + r * xstride + v * 8) = raw;
@@ -257,18 +350,18 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
         int ex = 0, e2 = 0;
         if (mx > 0.f && isfinite(mx)) {
           frexpf(mx, &ex);
-          e2 = max(-100, min(100, 15 - ex));
+          e2 = max(-100, min(100, 15 - ex));  // max * 2^e2 in [2^14, 2^15): exact in f16
         }
         rscale[tid] = ldexpf(1.0f, -e2);
         rscale[8 + tid] = ldexpf(1.0f, e2);
       }
       __syncthreads();
-      for (int idx = tid; idx < GX_MAXR * (kpad / 8); idx += GX_THREADS) {
-        const int r = idx / (kpad / 8), v = idx - r * (kpad / 8);
-        uint4* slotp = reinterpret_cast<uint4*>(xs + r * xstride + v * 8);
+      for (int idx = tid; idx < GX_MAXR * (xlen / 8); idx += GX_THREADS) {
+        const int r = idx / (xlen / 8), v = idx - r * (xlen / 8);
+        uint4* sp = reinterpret_cast<uint4*>(xs + r * xstride + v * 8);
         __align__(16) __half hv[8];
         if (r < rows && v * 8 < K) {
-          const uint4 raw = *slotp;
+          const uint4 raw = *sp;
           const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
           for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(__bfloat162float(h[i]) * rscale[8 + r]);
@@ -276,44 +369,35 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
 #pragma unroll
           for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(0.f);
         }
-        *slotp = *reinterpret_cast<const uint4*>(hv);
+        *sp = *reinterpret_cast<const uint4*>(hv);
       }
       __syncthreads();
-      // ---- stream the tile's weights
-      float acc[NSTREAM][4];
+      // ---- this warp's tiles of the chunk
+      for (int tile = t0 + warp; tile < t1; tile += GX_WARPS) {
+        float acc[2][4];
 #pragma unroll
-      for (int s = 0; s < NSTREAM; ++s)
+        for (int s = 0; s < 2; ++s)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[s][i] = 0.f;
-      for (int kb0 = warp; kb0 < nkb; kb0 += GX_WARPS * GX_UNROLL) {
-        uint4 wa[GX_UNROLL][NSTREAM], wb[GX_UNROLL][NSTREAM];
+          for (int i = 0; i < 4; ++i) acc[s][i] = 0.f;
+        const __half* xp = xs + g * xstride + 16 * c;  // activation row g of the pass
+        for (int ks = 0; ks < nks; ++ks, xp += GX_KB) {
+          cp_async_wait_group<GX_STAGES - 2>();
+          const unsigned char* st = ring + slot_r * GX_STAGE_BYTES + tid * 16;
+          slot_r = slot_r + 1 == GX_STAGES ? 0 : slot_r + 1;
+          uint4 wa[2], wb[2];
 #pragma unroll
-        for (int u = 0; u < GX_UNROLL; ++u) {
-          const int kb = kb0 + u * GX_WARPS;
-          const int64_t koff = (int64_t)kb * GX_KB + 16 * c;
-          const bool ok = kb < nkb && koff < K;
-#pragma unroll
-          for (int s = 0; s < NSTREAM; ++s) {
-            const int64_t roff = s == 0 ? 0 : a.up_rows;
-            wa[u][s] = ok ? ld_stream_u4(codes + (roff + r0) * K + koff) : make_uint4(0, 0, 0, 0);
-            wb[u][s] = ok ? ld_stream_u4(codes + (roff + r1) * K + koff) : make_uint4(0, 0, 0, 0);
+          for (int s = 0; s < 2; ++s) {
+            wa[s] = *reinterpret_cast<const uint4*>(st + (s * 2 + 0) * GX_THREADS * 16);
+            wb[s] = *reinterpret_cast<const uint4*>(st + (s * 2 + 1) * GX_THREADS * 16);
           }
-        }
+          issue();
 #pragma unroll
-        for (int u = 0; u < GX_UNROLL; ++u) {
-          const int kb = kb0 + u * GX_WARPS;
-          if (kb >= nkb) break;
-          uint32_t xb[8];
-          if (g < GX_MAXR) {
-            const uint4* p = reinterpret_cast<const uint4*>(xs + g * xstride + kb * GX_KB + 16 * c);
+          for (int s = 0; s < 2; ++s) {
+            const uint4* p = reinterpret_cast<const uint4*>(xp + (HALVES ? s * kspan : 0));
             const uint4 v0 = p[0], v1 = p[1];
-            xb[0] = v0.x; xb[1] = v0.y; xb[2] = v0.z; xb[3] = v0.w;
-            xb[4] = v1.x; xb[5] = v1.y; xb[6] = v1.z; xb[7] = v1.w;
-          }
-#pragma unroll
-          for (int s = 0; s < NSTREAM; ++s) {
-            const uint32_t ra[4] = {wa[u][s].x, wa[u][s].y, wa[u][s].z, wa[u][s].w};
-            const uint32_t rb[4] = {wb[u][s].x, wb[u][s].y, wb[u][s].z, wb[u][s].w};
+            const uint32_t xb[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+            const uint32_t ra[4] = {wa[s].x, wa[s].y, wa[s].z, wa[s].w};
+            const uint32_t rb[4] = {wb[s].x, wb[s].y, wb[s].z, wb[s].w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               uint32_t a_lo, a_hi, b_lo, b_hi;
@@ -323,41 +407,25 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
             }
           }
         }
-      }
-      // ---- reduce over warps and write this pass's rows
+        // ---- epilogue: lane holds weight rows (g, g+8) x activation rows (2c, 2c+1)
 #pragma unroll
-      for (int s = 0; s < NSTREAM; ++s) {
-        float* base = red + ((warp * NSTREAM + s) * GX_ROWS) * 8;
-        base[g * 8 + 2 * c] = acc[s][0];
-        base[g * 8 + 2 * c + 1] = acc[s][1];
-        base[(g + 8) * 8 + 2 * c] = acc[s][2];
-        base[(g + 8) * 8 + 2 * c + 1] = acc[s][3];
-      }
-      __syncthreads();
-      for (int idx = tid; idx < GX_ROWS * rows; idx += GX_THREADS) {
-        const int row = idx % GX_ROWS, r = idx / GX_ROWS;
-        const int64_t nrow = tile * GX_ROWS + row;
-        if (nrow >= a.n) continue;
-        float v[NSTREAM];
-#pragma unroll
-        for (int s = 0; s < NSTREAM; ++s) {
-          float tot = 0.f;
-#pragma unroll
-          for (int w = 0; w < GX_WARPS; ++w) tot += red[((w * NSTREAM + s) * GX_ROWS + row) * 8 + r];
-          v[s] = tot * rscale[r] * scales[(s == 0 ? 0 : a.up_rows) + nrow];
-        }
-        __nv_bfloat16* out = a.y + (int64_t)(st + p0 + r) * a.n + nrow;
-        if (SWIGLU) {
-          const float gt = round_bf16(v[0]);
-          const float up = round_bf16(v[NSTREAM - 1]);
-          *out = __float2bfloat16_rn(round_bf16(silu_f32(gt)) * up);
-        } else {
-          *out = __float2bfloat16_rn(v[0]);
+        for (int i = 0; i < 4; ++i) {
+          const int r = 2 * c + (i & 1);
+          const int64_t nrow = (int64_t)tile * GX_ROWS + g + (i >> 1) * 8;
+          if (r >= rows || nrow >= a.n) continue;
+          __nv_bfloat16* out = a.y + (int64_t)(st0 + p0 + r) * a.n + nrow;
+          if (SWIGLU) {
+            const float gt = round_bf16(acc[0][i] * rscale[r] * scales[nrow]);
+            const float up = round_bf16(acc[1][i] * rscale[r] * scales[a.up_rows + nrow]);
+            *out = __float2bfloat16_rn(round_bf16(silu_f32(gt)) * up);
+          } else {
+            *out = __float2bfloat16_rn((acc[0][i] + acc[1][i]) * rscale[r] * scales[nrow]);
+          }
         }
       }
-      __syncthreads();
     }
   }
+  cp_async_wait_group<0>();
 }
 
 // ------------------------------------------------------------------ fixed-rank combine
@@ -435,26 +503,31 @@ extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, cons
   if (!aligned(codes, 16) || (codes_stride % 16) || !aligned(x_bf16, 16))
     return fail(MRB_ERR_ARG, "grouped_qrow: codes and activation rows must be 16-byte aligned");
   if (swiglu && up_rows < n) return fail(MRB_ERR_ARG, "grouped_qrow: up rows overlap the gate rows");
-  const int kpad = (int)((k + GX_KB - 1) / GX_KB) * GX_KB;
-  const size_t xs = (((size_t)GX_MAXR * (kpad + 8) * 2) + 15) & ~size_t(15);
-  const size_t smem = xs + (size_t)GX_WARPS * (swiglu ? 2 : 1) * GX_ROWS * 8 * 4 + 32 * 4;
-  if (smem > 200 * 1024) return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: in_features %lld too large", (long long)k);
+  const size_t smem = gx_smem_bytes(k, !swiglu);
+  if (smem > 227 * 1024) return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: in_features %lld too large", (long long)k);
+  if (experts * ((n + GX_ROWS - 1) / GX_ROWS) > 0x7fffffffLL)
+    return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: too many expert tiles");
   GroupedArgs a{(const __nv_bfloat16*)x_bf16, row_ids, starts, counts, (int)experts, codes, codes_stride, scales,
-                scales_stride, slot_of, n, k, up_rows, (__nv_bfloat16*)y_bf16};
-  const int64_t items = experts * ((n + GX_ROWS - 1) / GX_ROWS);
-  const int64_t grid = std::min<int64_t>(items, (int64_t)num_sms() * 2);
+                scales_stride, slot_of, n, k, up_rows, (__nv_bfloat16*)y_bf16, 1, 1};
+  // two CTAs per SM; chunks of whole tiles per warp sized for about two work items per CTA
+  const int64_t slots = (int64_t)num_sms() * 2;
+  const int64_t rtiles = (n + GX_ROWS - 1) / GX_ROWS;
+  const int64_t per_warp = std::max<int64_t>(1, experts * rtiles / (GX_WARPS * 2 * slots));
+  a.chunk_tiles = (int)std::min<int64_t>(rtiles, per_warp * GX_WARPS);
+  a.chunks = (int)((rtiles + a.chunk_tiles - 1) / a.chunk_tiles);
+  const int64_t grid = std::min<int64_t>(experts * a.chunks, slots);
   cudaStream_t s = (cudaStream_t)stream;
-  auto run = [&](auto kern) -> int {
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
+  static size_t configured[2] = {0, 0};  // per kernel instantiation
+  auto run = [&](auto kern, int which) -> int {
+    if (smem > 48 * 1024 && smem > configured[which]) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "grouped_qrow: smem attribute: %s", cudaGetErrorString(e));
-      configured = smem;
+      configured[which] = smem;
     }
     launch_kernel(kern, dim3((unsigned)grid), dim3(GX_THREADS), smem, s, true, a);
     return launch_status("grouped_qrow");
   };
-  return swiglu ? run(grouped_qrow_kernel<true>) : run(grouped_qrow_kernel<false>);
+  return swiglu ? run(grouped_qrow_kernel<true>, 1) : run(grouped_qrow_kernel<false>, 0);
 }
 
 extern "C" int mrb_stable_route_reduce(const void* expert_out_bf16, const float* coef, const int64_t* inverse,

@@ -698,8 +698,12 @@ int qrow_gemm_swiglu_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const in
                           const float* gate_scales, const int8_t* up_codes, const float* up_scales, int64_t n,
                           __nv_bfloat16* y, cudaStream_t s);
 
-// Activation rows above which bf16 projections use the tensor-core GEMM.
-constexpr int64_t GEMV_MAX_ROWS = 16;
+// Activation rows above which bf16 projections use the tile GEMM (below it, 16-row GEMV
+// launches stream the weights once per chunk, the second pass mostly from L2).
+#ifndef MRB_GEMV_MAX_ROWS
+#define MRB_GEMV_MAX_ROWS 32
+#endif
+constexpr int64_t GEMV_MAX_ROWS = MRB_GEMV_MAX_ROWS;
 
 static GemvArgs make_args(const void* x, int64_t m, int64_t k, const int8_t* c0, const float* s0, const int8_t* c1,
                           const float* s1, const float* bias, int64_t n, void* y) {

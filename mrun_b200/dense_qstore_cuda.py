@@ -129,7 +129,7 @@ def qrow_linear(
     if bias is not None and (bias.dtype != torch.float32 or bias.numel() != out_features):
         raise ValueError("bias must be fp32 [out_features]")
     code = _lib.dtype_code(flat.dtype)
-    ws_ptr, ws_bytes = _gemv_workspace(device, out_features, workspace) if rows <= 16 else (None, 0)
+    ws_ptr, ws_bytes = _gemv_workspace(device, out_features, workspace) if rows <= 32 else (None, 0)
     _lib.call(
         "mrb_qrow_matmul",
         flat.data_ptr(),
@@ -216,7 +216,7 @@ def qrow_swiglu(
     rows = int(flat.shape[0])
     if out is None:
         out = torch.empty((rows, out_features), device=device, dtype=torch.bfloat16)
-    ws_ptr, ws_bytes = _gemv_workspace(device, out_features, workspace) if rows <= 16 else (None, 0)
+    ws_ptr, ws_bytes = _gemv_workspace(device, out_features, workspace) if rows <= 32 else (None, 0)
     _lib.call(
         "mrb_qrow_swiglu",
         flat.data_ptr(),

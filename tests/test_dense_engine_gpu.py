@@ -70,11 +70,17 @@ def test_graph_replay_matches_eager_and_is_deterministic(cuda):
         dec = DenseDecoder(weights, max_batch=1, max_seq_len=128, device=cuda, max_prefill_tokens=64)
         runs.append(dec.generate(prompt, 40))
     assert runs[0] == runs[1]
-    # eager: prefill the generated prefix and compare the next token with the graph's
+    # eager: prefill the generated prefix and compare the next token with the graph's. The
+    # prefill runs other kernels (tile GEMM, other attention splits), so the two may differ
+    # only at a near tie: then both tokens score within bf16 noise in the oracle's logits.
     dec = DenseDecoder(weights, max_batch=1, max_seq_len=128, device=cuda, max_prefill_tokens=128)
     seq = torch.cat([prompt, torch.tensor(runs[0][:-1])])
     nxt = int(dec.prefill(0, seq).item())
-    assert nxt == runs[0][-1]
+    if nxt != runs[0][-1]:
+        logits = _oracle(cfg, weights).forward(seq.numpy())[-1]
+        gap = abs(float(logits[nxt]) - float(logits[runs[0][-1]]))
+        assert gap <= 2e-2, f"graph token {runs[0][-1]} vs eager {nxt}: oracle logit gap {gap:.4g}"
+        print(f"graph/eager near tie: tokens {runs[0][-1]} / {nxt}, oracle gap {gap:.4g}")
 
 
 @pytest.mark.slow
