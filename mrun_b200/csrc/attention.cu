@@ -381,6 +381,309 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
   if (tid == 0) a.counters[rh] = 0u;  // ready for the next launch (graph replays)
 }
 
+// ------------------------------------------------------------------ tensor-core decode attention
+
+constexpr int AM_STAGES = 3;                          // K/V tiles in flight per warp
+constexpr int AM_ROW = 128 + 8;                       // padded smem row (bf16): conflict-free fragments
+constexpr int AM_TILE_ELEMS = AT_TILE * AM_ROW;       // one K or V tile
+constexpr int AM_STAGE_ELEMS = 2 * AM_TILE_ELEMS;     // K and V
+constexpr int AM_MAX_WARPS = 4;
+
+__host__ __device__ inline size_t am_smem_bytes(int warps) {
+  const size_t ring = (size_t)warps * AM_STAGES * AM_STAGE_ELEMS * sizeof(__nv_bfloat16);
+  const size_t merge = (size_t)warps * 16 * (2 + 128) * sizeof(float);
+  return ring > merge ? ring : merge;
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& b0, uint32_t& b1, const void* p) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(s));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Decode attention on the tensor pipe (head_dim 128, GQA group <= 16).
+//
+// The CTA owns (query row, KV head, split) like the scalar kernel, with W <= 4 warps that
+// take the split's 16-token tiles in turn (warp w: tiles w, w + W, ...), each through its
+// own 3-stage cp.async ring of K and V tiles (rows padded to 272 B so fragment reads are
+// conflict-free). Per tile a warp computes S = Q K^T for all query heads of the group at
+// once -- heads are the 16 rows of mma.sync m16n8k16 (bf16 inputs, fp32 accumulation), two
+// 8-token column blocks, eight 16-dim k steps -- scales it in fp32, runs the online softmax
+// per head row in fp32, and accumulates O += P V on the tensor pipe with P (rounded to
+// bf16) reused straight from the score fragments and V fragments from ldmatrix.trans. The
+// W partial states are merged through shared memory in warp order, then published and
+// merged across splits exactly as the scalar kernel does (deterministic).
+__global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(AttnArgs a) {
+  constexpr int D = 128;
+  const int W = blockDim.x >> 5;
+  const int group = (int)(a.hq / a.hkv);
+  const int64_t rh = blockIdx.x;  // row * hkv + kv head
+  const int split = blockIdx.y;
+  const int64_t r = rh / a.hkv;
+  const int kvh = (int)(rh - r * a.hkv);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  extern __shared__ __align__(16) unsigned char am_smem[];
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(am_smem) + (size_t)warp * AM_STAGES * AM_STAGE_ELEMS;
+  __shared__ bool is_last;
+
+  const int64_t seq = a.row_seq ? a.row_seq[r] : r;
+  const int64_t len = a.row_len[r];
+  const bool has_new = a.k_new != nullptr;
+  const int64_t total = len + (has_new ? 1 : 0);
+  const int64_t t_begin = (int64_t)split * a.tiles_per_split * AT_TILE;
+  const int64_t t_end = min(total, t_begin + (int64_t)a.tiles_per_split * AT_TILE);
+  const int ntile = t_end > t_begin ? (int)((t_end - t_begin + AT_TILE - 1) / AT_TILE) : 0;
+  const int nmine = warp < ntile ? (ntile - warp + W - 1) / W : 0;
+  const int64_t khead = (int64_t)kvh * a.stride_head;
+
+  // ---- this warp's K/V ring: its j-th tile (split tile warp + j*W) in stage j % AM_STAGES
+  auto issue = [&](int j) {
+    if (j < nmine) {
+      __nv_bfloat16* kst = ring + (j % AM_STAGES) * AM_STAGE_ELEMS;
+      __nv_bfloat16* vst = kst + AM_TILE_ELEMS;
+      const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
+#pragma unroll 4
+      for (int e = lane; e < AT_TILE * (D / 8); e += 32) {
+        const int t = e >> 4, ch = e & 15;
+        const int64_t tok = t0 + t;
+        const bool ok = tok < t_end;
+        const __nv_bfloat16 *kp = a.k_cache, *vp = a.v_cache;
+        if (ok) {
+          if (has_new && tok == len) {
+            kp = a.k_new + (r * a.hkv + kvh) * D;
+            vp = a.v_new + (r * a.hkv + kvh) * D;
+          } else {
+            const int64_t off = kv_offset(a, seq, tok, khead);
+            kp = a.k_cache + off;
+            vp = a.v_cache + off;
+          }
+        }
+        cp_async16_zfill(kst + t * AM_ROW + ch * 8, kp + (ok ? ch * 8 : 0), ok);
+        cp_async16_zfill(vst + t * AM_ROW + ch * 8, vp + (ok ? ch * 8 : 0), ok);
+      }
+    }
+    cp_async_commit_group();
+  };
+#pragma unroll
+  for (int j = 0; j < AM_STAGES - 1; ++j) issue(j);
+
+  // ---- Q of the group as the mma A operand: rows g and g + 8 are query heads (zero beyond
+  // the group), eight 16-dim k steps
+  uint32_t qa[D / 16][4];
+  {
+    const __nv_bfloat16* q0 = a.q + (r * a.hq + (int64_t)kvh * group) * D;
+    const bool v0 = g < group, v1 = g + 8 < group;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int d0 = ks * 16 + 2 * c;
+      qa[ks][0] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + g * D + d0) : 0u;
+      qa[ks][1] = v1 ? *reinterpret_cast<const uint32_t*>(q0 + (g + 8) * D + d0) : 0u;
+      qa[ks][2] = v0 ? *reinterpret_cast<const uint32_t*>(q0 + g * D + d0 + 8) : 0u;
+      qa[ks][3] = v1 ? *reinterpret_cast<const uint32_t*>(q0 + (g + 8) * D + d0 + 8) : 0u;
+    }
+  }
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  for (int j = 0; j < nmine; ++j) {
+    cp_async_wait_group<AM_STAGES - 2>();
+    __syncwarp();  // the whole tile is in shared memory; the stage of tile j - 1 is free
+    issue(j + AM_STAGES - 1);
+    const __nv_bfloat16* kst = ring + (j % AM_STAGES) * AM_STAGE_ELEMS;
+    const __nv_bfloat16* vst = kst + AM_TILE_ELEMS;
+    const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
+    // ---- scores: s[nt] = (head g | g+8) x (tokens nt*8 + 2c, +1)
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      const __nv_bfloat16* kr = kst + (nt * 8 + g) * AM_ROW + 2 * c;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + ks * 16);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + 8);
+        mma_bf16_16816(s[nt], qa[ks], b0, b1);
+      }
+    }
+    // ---- online softmax per head row (rows g and g + 8), fp32
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t tok = t0 + nt * 8 + 2 * c + (i & 1);
+        s[nt][i] = tok < t_end ? s[nt][i] * a.scale : -INFINITY;
+      }
+    float alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float mx = fmaxf(fmaxf(s[0][2 * h], s[0][2 * h + 1]), fmaxf(s[1][2 * h], s[1][2 * h + 1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(mrow[h], mx);
+      alpha[h] = (mrow[h] == -INFINITY) ? 0.f : expf(mrow[h] - m_new);
+      float sum = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float p = (m_new == -INFINITY) ? 0.f : expf(s[nt][2 * h + i] - m_new);
+          s[nt][2 * h + i] = p;
+          sum += p;
+        }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      lrow[h] = lrow[h] * alpha[h] + sum;
+      mrow[h] = m_new;
+    }
+    // ---- O = O * alpha + P V (P in bf16 as the A operand, V via ldmatrix.trans)
+    const uint32_t pa[4] = {pack_bf16x2(s[0][0], s[0][1]), pack_bf16x2(s[0][2], s[0][3]),
+                            pack_bf16x2(s[1][0], s[1][1]), pack_bf16x2(s[1][2], s[1][3])};
+    const __nv_bfloat16* vrow = vst + (lane & 15) * AM_ROW;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt) {
+      o[dt][0] *= alpha[0];
+      o[dt][1] *= alpha[0];
+      o[dt][2] *= alpha[1];
+      o[dt][3] *= alpha[1];
+      uint32_t b0, b1;
+      ldmatrix_x2_trans(b0, b1, vrow + dt * 8);
+      mma_bf16_16816(o[dt], pa, b0, b1);
+    }
+  }
+  cp_async_wait_group<0>();
+  __syncthreads();  // every warp is done with its ring: the space becomes the merge area
+
+  // ---- merge the W warp states per head row in warp order
+  float* mb = reinterpret_cast<float*>(am_smem);  // [W][16 rows][2 + D]
+  {
+    float* mine = mb + (size_t)warp * 16 * (2 + D);
+    if (c == 0) {
+      mine[g * (2 + D)] = mrow[0];
+      mine[g * (2 + D) + 1] = lrow[0];
+      mine[(g + 8) * (2 + D)] = mrow[1];
+      mine[(g + 8) * (2 + D) + 1] = lrow[1];
+    }
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt) {
+      mine[g * (2 + D) + 2 + dt * 8 + 2 * c] = o[dt][0];
+      mine[g * (2 + D) + 2 + dt * 8 + 2 * c + 1] = o[dt][1];
+      mine[(g + 8) * (2 + D) + 2 + dt * 8 + 2 * c] = o[dt][2];
+      mine[(g + 8) * (2 + D) + 2 + dt * 8 + 2 * c + 1] = o[dt][3];
+    }
+  }
+  __syncthreads();
+  float* part_base = a.nsplit > 1 ? a.part + (rh * a.nsplit + split) * (int64_t)group * (2 + D) : nullptr;
+  for (int idx = tid; idx < group * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx - h * D;
+    float mx = -INFINITY;
+    for (int w = 0; w < W; ++w) mx = fmaxf(mx, mb[((size_t)w * 16 + h) * (2 + D)]);
+    float l = 0.f, acc = 0.f;
+    for (int w = 0; w < W; ++w) {
+      const float* st = mb + ((size_t)w * 16 + h) * (2 + D);
+      const float wt = (st[0] == -INFINITY) ? 0.f : expf(st[0] - mx);
+      l = fmaf(st[1], wt, l);
+      acc = fmaf(st[2 + d], wt, acc);
+    }
+    if (a.nsplit == 1) {
+      a.out[(r * a.hq + (int64_t)kvh * group + h) * D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+    } else {
+      float* p = part_base + (int64_t)h * (2 + D);
+      p[2 + d] = acc;
+      if (d == 0) {
+        p[0] = mx;
+        p[1] = l;
+      }
+    }
+  }
+  if (a.nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&a.counters[rh], 1u);
+    is_last = prev == (unsigned)(a.nsplit - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // ---- last split: warps merge the heads over all splits, in split order
+  constexpr int VD = D / 32;
+  const int64_t sstride = (int64_t)group * (2 + D);
+  for (int h = warp; h < group; h += W) {
+    const float* base = a.part + (rh * a.nsplit * group + h) * (2 + D);
+    float mx_all = -INFINITY;
+    for (int s0 = lane; s0 < a.nsplit; s0 += 32) mx_all = fmaxf(mx_all, __ldcg(base + s0 * sstride));
+    mx_all = warp_max(mx_all);
+    float lsum = 0.f, ov[VD];
+#pragma unroll
+    for (int i = 0; i < VD; ++i) ov[i] = 0.f;
+    for (int s0 = 0; s0 < a.nsplit; s0 += 8) {  // 8 splits' loads in flight at a time
+      float ms[8], ls[8], av[8][VD];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const bool ok = s0 + jj < a.nsplit;
+        const float* p = base + (s0 + jj) * sstride;
+        ms[jj] = ok ? __ldcg(p) : -INFINITY;
+        ls[jj] = ok ? __ldcg(p + 1) : 0.f;
+#pragma unroll
+        for (int i = 0; i < VD; ++i) av[jj][i] = ok ? __ldcg(p + 2 + lane * VD + i) : 0.f;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const float wt = (ms[jj] == -INFINITY) ? 0.f : expf(ms[jj] - mx_all);
+        lsum = fmaf(ls[jj], wt, lsum);
+#pragma unroll
+        for (int i = 0; i < VD; ++i) ov[i] = fmaf(av[jj][i], wt, ov[i]);
+      }
+    }
+    __nv_bfloat16* out = a.out + (r * a.hq + (int64_t)kvh * group + h) * D + lane * VD;
+#pragma unroll
+    for (int i = 0; i < VD; ++i) out[i] = __float2bfloat16_rn(lsum > 0.f ? ov[i] / lsum : 0.f);
+  }
+  __syncthreads();
+  if (tid == 0) a.counters[rh] = 0u;  // ready for the next launch (graph replays)
+}
+
+static bool use_mma(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_dim);
+
+// Launch the decode attention for a checked AttnArgs planned with plan_splits: the
+// tensor-core kernel when use_mma selects it, else the scalar kernel.
+static int launch_attention(const AttnArgs& a, int64_t head_dim, int64_t max_total, cudaStream_t s) {
+  dim3 grid((unsigned)(a.rows * a.hkv), (unsigned)a.nsplit);
+  if (use_mma(a.rows, a.hkv, max_total, head_dim)) {
+    const int warps = std::min(AM_MAX_WARPS, std::max(1, a.tiles_per_split));
+    const size_t smem = am_smem_bytes(warps);
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+      cudaError_t e = cudaFuncSetAttribute(paged_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)am_smem_bytes(AM_MAX_WARPS));
+      if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "paged_attention: smem attribute: %s", cudaGetErrorString(e));
+      configured = am_smem_bytes(AM_MAX_WARPS);
+    }
+    launch_kernel(paged_attention_mma_kernel, grid, dim3(32 * warps), smem, s, true, a);
+  } else {
+    launch_kernel(head_dim == 128 ? paged_attention_kernel<128> : paged_attention_kernel<64>, grid,
+                  dim3((unsigned)(32 * (a.hq / a.hkv))), 0, s, true, a);
+  }
+  return launch_status("paged_attention");
+}
+
 struct SplitPlan {
   int nsplit;
   int tiles_per_split;
@@ -390,11 +693,23 @@ struct SplitPlan {
 // CTA; its 32 KB tile ring and 32-512 threads let several share an SM), each split at least
 // 4 tiles (2 for contexts up to 64 tiles) so the ring has tiles to overlap, at most
 // AT_MAX_SPLIT splits.
-static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total) {
+// Kernel choice: the tensor-core kernel (head_dim 128) once the (row, head) groups times
+// the context tiles reach 4096 -- long contexts or many rows, where the scalar kernel is
+// instruction-bound; short decode batches keep the scalar kernel, whose fixed latency is
+// lower.
+static bool use_mma(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_dim) {
+  const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
+  return head_dim == 128 && rows * hkv * tiles >= 4096;
+}
+
+// The tensor-core kernel wants at least 8 tiles per split: its 4 warps take 2 each, and
+// fewer, longer splits keep the final merge (dependent L2 round trips) short.
+static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_dim) {
   const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
   const int64_t groups = std::max<int64_t>(1, rows * hkv);
   const int64_t target = ((int64_t)AT_CTAS_PER_SM * num_sms() + groups - 1) / groups;  // splits per group
-  const int64_t min_tiles = tiles <= 64 ? 2 : AT_MIN_TILES;  // short contexts: more, shorter splits
+  const int64_t min_tiles =
+      use_mma(rows, hkv, max_total, head_dim) ? 2 * AM_MAX_WARPS : (tiles <= 64 ? 2 : AT_MIN_TILES);
   int64_t tps = std::max<int64_t>(min_tiles, (tiles + target - 1) / target);
   tps = std::min<int64_t>(tps, tiles);
   tps = std::max<int64_t>(tps, (tiles + AT_MAX_SPLIT - 1) / AT_MAX_SPLIT);
@@ -452,7 +767,7 @@ extern "C" int mrb_rope_kv_append(const void* q_in, const void* k_in, const void
 extern "C" size_t mrb_paged_attention_workspace(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
                                                 int64_t max_total_tokens) {
   if (rows <= 0 || hkv <= 0 || hq % hkv) return 0;
-  return workspace_bytes(rows, hq, hkv, head_dim, plan_splits(rows, hkv, max_total_tokens));
+  return workspace_bytes(rows, hq, hkv, head_dim, plan_splits(rows, hkv, max_total_tokens, head_dim));
 }
 
 extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
@@ -476,7 +791,7 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || (stride_page % 8) || (stride_head % 8) || (stride_tok % 8) ||
       (k_new && !aligned(k_new, 16)))
     return fail(MRB_ERR_ARG, "paged_attention: K/V rows must be 16-byte aligned");
-  const SplitPlan plan = plan_splits(rows, hkv, max_total_tokens);
+  const SplitPlan plan = plan_splits(rows, hkv, max_total_tokens, head_dim);
   const size_t need = workspace_bytes(rows, hq, hkv, head_dim, plan);
   if (need > 0 && (workspace == nullptr || workspace_size < need))
     return fail(MRB_ERR_ARG, "paged_attention: workspace of %zu bytes required (got %zu)", need, workspace_size);
@@ -491,11 +806,7 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
     a.counters = (unsigned*)workspace;
     a.part = (float*)((char*)workspace + AT_COUNTER_BYTES);
   }
-  dim3 grid((unsigned)(rows * hkv), (unsigned)plan.nsplit);
-  const unsigned threads = (unsigned)(32 * (hq / hkv));
-  launch_kernel(head_dim == 128 ? paged_attention_kernel<128> : paged_attention_kernel<64>, grid, dim3(threads), 0,
-                (cudaStream_t)stream, true, a);
-  return launch_status("paged_attention");
+  return launch_attention(a, head_dim, max_total_tokens, (cudaStream_t)stream);
 }
 
 // ------------------------------------------------------------------ decode-step bookkeeping
@@ -571,7 +882,7 @@ extern "C" int mrb_paged_attention_static(const void* q, int64_t rows, int64_t h
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || (stride_page % 8) || (stride_head % 8) || (stride_tok % 8) ||
       (k_new && !aligned(k_new, 16)))
     return fail(MRB_ERR_ARG, "paged_attention_static: K/V rows must be 16-byte aligned");
-  const SplitPlan plan = plan_splits(rows, hkv, max_total_tokens);
+  const SplitPlan plan = plan_splits(rows, hkv, max_total_tokens, head_dim);
   const size_t need = workspace_bytes(rows, hq, hkv, head_dim, plan);
   if (need > MRB_ATTN_STATIC_SCRATCH_BYTES)
     return fail(MRB_ERR_UNSUPPORTED,
@@ -608,9 +919,5 @@ extern "C" int mrb_paged_attention_static(const void* q, int64_t rows, int64_t h
     a.counters = (unsigned*)scratch;
     a.part = (float*)((char*)scratch + AT_COUNTER_BYTES);
   }
-  dim3 grid((unsigned)(rows * hkv), (unsigned)plan.nsplit);
-  const unsigned threads = (unsigned)(32 * (hq / hkv));
-  launch_kernel(head_dim == 128 ? paged_attention_kernel<128> : paged_attention_kernel<64>, grid, dim3(threads), 0,
-                (cudaStream_t)stream, true, a);
-  return launch_status("paged_attention_static");
+  return launch_attention(a, head_dim, max_total_tokens, (cudaStream_t)stream);
 }

@@ -62,6 +62,10 @@ def _random_paged(rng, rows, hkv, d, lengths, num_pages):
     (3, 32, 4, [17, 256, 4096]),
     (4, 8, 8, [16, 15, 33, 100]),
     (2, 32, 8, [1024, 2047]),
+    # (row, head) groups x context tiles >= 4096: the tensor-core kernel, ragged lengths,
+    # query groups of 8 and 7
+    (8, 32, 4, [1, 300, 777, 1024, 1500, 1999, 2048, 64]),
+    (6, 28, 4, [4000, 3333, 2500, 17, 1024, 3100]),
 ])
 def test_paged_attention_vs_oracle(rows, hq, hkv, lengths, cuda):
     from mrun_b200.segmented_gqa_decode import paged_attention

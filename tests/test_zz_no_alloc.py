@@ -57,7 +57,8 @@ def _args(c, out, max_total):
 @pytest.mark.parametrize("rows,hq,hkv,lengths,max_total", [
     (1, 28, 4, [700], 1024),          # decode shape: split-K with a cross-split merge
     (3, 32, 4, [17, 256, 1500], 2048),
-    (2, 8, 8, [33, 90], 128),
+    (2, 8, 8, [33, 300], 512),
+    (4, 8, 4, [100, 1000, 2500, 4000], 4096),  # long contexts: the tensor-core kernel
 ])
 def test_static_scratch_matches_workspace_entry_point(rows, hq, hkv, lengths, max_total, cuda):
     c = _case(rows, hq, hkv, lengths, rows * 7 + hq, cuda)
