@@ -381,8 +381,7 @@ def run_moe_case(args) -> None:
                      world=world)
     first = torch.from_numpy(rng.integers(0, cfg.vocab, MOE_ROWS))
     dec.load_synthetic_context(lengths, first, steps=total, seed=rank)
-    if world == 1:
-        dec.capture(MOE_ROWS)
+    dec.capture(MOE_ROWS)
     for _ in range(args.warmup):
         dec.step(MOE_ROWS)
     stream = torch.cuda.current_stream(device)
@@ -413,11 +412,14 @@ def run_moe_case(args) -> None:
             "config": {"workload": "config4: Qwen3-30B-A3B-shape MoE, 48 layers, 128 experts top-8, "
                                    "32 ragged rows per GPU, contexts U[256,4096]",
                        "rows_per_gpu": MOE_ROWS, "parallelism": f"ep{world}" if world > 1 else "single GPU",
-                       "graph": world == 1, "mean_context": float(np.mean(lengths))},
+                       "graph": True, "exchange": "fixed-capacity NCCL all-to-all" if world > 1 else None,
+                       "mean_context": float(np.mean(lengths))},
             "algorithmic_bytes_per_step_per_gpu": {"experts": expert_bytes / world, "kv": kv_bytes},
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
+    dec.graph = None  # a graph holding NCCL calls must go before the process group
+    torch.cuda.synchronize(device)
     if world > 1:
         import torch.distributed as dist
 

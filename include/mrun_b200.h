@@ -192,6 +192,26 @@ int mrb_grouped_qrow(const void *x_bf16, const int64_t *row_ids, const int32_t *
                      const int32_t *slot_of, int64_t n, int64_t k, int64_t up_rows, int swiglu,
                      void *y_bf16, void *stream);
 
+/* Fixed-capacity expert-parallel dispatch plan (no reference counterpart: the reference
+ * runs every expert on one device). Expert e lives on rank e / experts_per_rank. Each
+ * (source, destination) block has `capacity` >= tokens * k slots, so the plan never
+ * overflows and every exchange has a size known on the host (CUDA-graph friendly).
+ * Assignment a = t * k + r goes to slot dst * capacity + pos (pos: its rank among the
+ * assignments to dst, in route order). Outputs (device): send_expert int32 [world *
+ * capacity] (destination-local expert id; unused slots: experts_per_rank), coef_slot fp32
+ * (top_w of the slot's assignment, 0 if unused), slot_of_assign int64 [tokens * k],
+ * slot_src int32 (source token, -1 if unused). An expert id outside [0, world *
+ * experts_per_rank) sets *error_flag (device int32, may be NULL). */
+int mrb_ep_pack(const int64_t *top_idx, const float *top_w, int64_t tokens, int64_t k,
+                int64_t experts_per_rank, int64_t world, int64_t capacity, int32_t *send_expert,
+                float *coef_slot, int64_t *slot_of_assign, int32_t *slot_src, int32_t *error_flag,
+                void *stream);
+
+/* send_rows[s] = source[slot_src[s]] (bf16 rows of `hidden`) for every used slot of a
+ * dispatch plan; unused slots are left as they are. No reference counterpart. */
+int mrb_ep_gather_rows(const void *source_bf16, int64_t hidden, const int32_t *slot_src, int64_t slots,
+                       void *send_rows_bf16, void *stream);
+
 /* Weighted combine in route-rank order: out[t] = sum_r coef[p] * expert_out[p] with
  * p = inverse[t*k + r], fp32 products summed left to right; fp32 and/or bf16 outputs.
  * Replaces `stable_route_reduce` (engine/qwen3_moe_cuda.py:2561-2664). */

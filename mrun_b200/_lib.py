@@ -49,6 +49,8 @@ SIGNATURES: dict[str, list] = {
     "mrb_route_compile": [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P],
     "mrb_grouped_qrow": [_P, _P, _P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, c_int, _P, _P],
     "mrb_stable_route_reduce": [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
+    "mrb_ep_pack": [_P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P],
+    "mrb_ep_gather_rows": [_P, _I64, _P, _I64, _P, _P],
     "mrb_rope_kv_append": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P, _P,
                            _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P, c_float, _P],
     "mrb_paged_attention_workspace": [_I64, _I64, _I64, _I64, _I64],

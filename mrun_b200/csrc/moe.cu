@@ -450,6 +450,68 @@ __global__ void stable_route_reduce_kernel(const __nv_bfloat16* __restrict__ eo,
   }
 }
 
+
+// ------------------------------------------------------------------ expert-parallel dispatch
+
+// Fixed-capacity dispatch plan for expert parallelism (expert e on rank e / experts_per_rank).
+// Every (source, destination) block has `capacity` slots (>= tokens * k, so nothing can
+// overflow); assignment a goes to slot dst * capacity + pos, pos = its rank among the
+// assignments to dst in route order (stable). Unused slots carry the dummy local expert id
+// experts_per_rank, coefficient 0 and source -1. One CTA: the plan is tiny.
+__global__ void __launch_bounds__(1024) ep_pack_kernel(const int64_t* __restrict__ top_idx,
+                                                       const float* __restrict__ top_w, int assignments,
+                                                       int experts_per_rank, int world, int capacity, int k,
+                                                       int32_t* __restrict__ send_expert, float* __restrict__ coef_slot,
+                                                       int64_t* __restrict__ slot_of_assign,
+                                                       int32_t* __restrict__ slot_src, int32_t* __restrict__ error_flag) {
+  pdl_launch_dependents();
+  pdl_wait();
+  extern __shared__ int32_t ep_dst[];
+  const int slots = world * capacity;
+  for (int i = threadIdx.x; i < slots; i += blockDim.x) {
+    send_expert[i] = experts_per_rank;
+    coef_slot[i] = 0.f;
+    slot_src[i] = -1;
+  }
+  for (int a = threadIdx.x; a < assignments; a += blockDim.x) {
+    const int64_t e = top_idx[a];
+    int d = (int)(e / experts_per_rank);
+    if (e < 0 || d >= world) {
+      if (error_flag) atomicExch(error_flag, 1);
+      d = -1;
+    }
+    ep_dst[a] = d;
+  }
+  __syncthreads();
+  for (int a = threadIdx.x; a < assignments; a += blockDim.x) {
+    const int d = ep_dst[a];
+    if (d < 0) {
+      slot_of_assign[a] = 0;
+      continue;
+    }
+    int pos = 0;
+    for (int b = 0; b < a; ++b) pos += ep_dst[b] == d;
+    const int slot = d * capacity + pos;
+    slot_of_assign[a] = slot;
+    send_expert[slot] = (int)(top_idx[a] - (int64_t)d * experts_per_rank);
+    coef_slot[slot] = top_w[a];
+    slot_src[slot] = a / k;
+  }
+}
+
+// send_rows[s, :] = source[slot_src[s], :] for used slots (one CTA per slot).
+__global__ void ep_gather_rows_kernel(const __nv_bfloat16* __restrict__ source, int64_t hidden,
+                                      const int32_t* __restrict__ slot_src, __nv_bfloat16* __restrict__ send_rows) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t s = blockIdx.x;
+  const int src = slot_src[s];
+  if (src < 0) return;
+  const uint4* in = reinterpret_cast<const uint4*>(source + (int64_t)src * hidden);
+  uint4* out = reinterpret_cast<uint4*>(send_rows + s * hidden);
+  for (int64_t i = threadIdx.x; i < hidden / 8; i += blockDim.x) out[i] = __ldg(in + i);
+}
+
 }  // namespace mrb
 
 using namespace mrb;
@@ -543,4 +605,33 @@ extern "C" int mrb_stable_route_reduce(const void* expert_out_bf16, const float*
                 (const __nv_bfloat16*)expert_out_bf16, coef, inverse, tokens, (int)k, hidden, out_f32,
                 (__nv_bfloat16*)out_bf16);
   return launch_status("stable_route_reduce");
+}
+
+extern "C" int mrb_ep_pack(const int64_t* top_idx, const float* top_w, int64_t tokens, int64_t k,
+                           int64_t experts_per_rank, int64_t world, int64_t capacity, int32_t* send_expert,
+                           float* coef_slot, int64_t* slot_of_assign, int32_t* slot_src, int32_t* error_flag,
+                           void* stream) {
+  const int64_t a = tokens * k;
+  if (tokens < 0 || k <= 0 || experts_per_rank <= 0 || world <= 0 || capacity < a)
+    return fail(MRB_ERR_ARG, "ep_pack: bad shape (capacity must hold tokens * k)");
+  if (a > 8192 || world * capacity > (1LL << 24)) return fail(MRB_ERR_UNSUPPORTED, "ep_pack: too many assignments");
+  if (!top_idx || !top_w || !send_expert || !coef_slot || !slot_of_assign || !slot_src)
+    return fail(MRB_ERR_ARG, "ep_pack: null pointer");
+  launch_kernel(ep_pack_kernel, dim3(1), dim3(1024), (size_t)std::max<int64_t>(a, 1) * sizeof(int32_t),
+                (cudaStream_t)stream, true, top_idx, top_w, (int)a, (int)experts_per_rank, (int)world, (int)capacity,
+                (int)k, send_expert, coef_slot, slot_of_assign, slot_src, error_flag);
+  return launch_status("ep_pack");
+}
+
+extern "C" int mrb_ep_gather_rows(const void* source_bf16, int64_t hidden, const int32_t* slot_src, int64_t slots,
+                                  void* send_rows_bf16, void* stream) {
+  if (hidden <= 0 || hidden % 8 || slots < 0) return fail(MRB_ERR_ARG, "ep_gather_rows: bad shape");
+  if (slots == 0) return MRB_OK;
+  if (!source_bf16 || !slot_src || !send_rows_bf16) return fail(MRB_ERR_ARG, "ep_gather_rows: null pointer");
+  if (!aligned(source_bf16, 16) || !aligned(send_rows_bf16, 16))
+    return fail(MRB_ERR_ARG, "ep_gather_rows: rows must be 16-byte aligned");
+  if (slots > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "ep_gather_rows: too many slots");
+  launch_kernel(ep_gather_rows_kernel, dim3((unsigned)slots), dim3(128), 0, (cudaStream_t)stream, true,
+                (const __nv_bfloat16*)source_bf16, hidden, slot_src, (__nv_bfloat16*)send_rows_bf16);
+  return launch_status("ep_gather_rows");
 }

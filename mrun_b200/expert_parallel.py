@@ -121,6 +121,63 @@ class ExpertParallelMoE:
         return self.combine(back, coef, inverse, t, k)
 
 
+class FixedCapacityExpertParallelMoE:
+    """The same exchange with sizes fixed on the host, so a decode step can be captured in a
+    CUDA graph (no device-to-host synchronisation): every (source, destination) block holds
+    T*k rows (the worst case, so nothing overflows). ``mrb_ep_pack`` plans the slots on the
+    device (padding slots carry a dummy local expert), rows and destination-local expert ids
+    travel by equal-split ``all_to_all_single``, the owner runs the grouped int8 MLP over the
+    real experts only, outputs come back the same way, and the fixed-rank combine reads each
+    assignment's slot. Results are bit-identical to one GPU (row-independent experts, combine
+    in route-rank order). Exchange cost: world * T*k rows each way per layer."""
+
+    def __init__(self, shard: ExpertShard, pages: torch.Tensor, layout, *, group=None) -> None:
+        self.shard = shard
+        self.pages = pages
+        self.layout = layout
+        self.group = group
+
+    def forward(self, source: torch.Tensor, top_indices: torch.Tensor, top_weights: torch.Tensor) -> torch.Tensor:
+        from . import _lib
+        from .moe import grouped_expert_mlp, grouped_route_tensors_with_inverse
+
+        sh = self.shard
+        t, k = (int(v) for v in top_indices.shape)
+        hidden = int(source.shape[1])
+        device = source.device
+        world, per = sh.world, sh.per_rank
+        cap = t * k
+        slots = world * cap
+        stream = _lib.stream_handle(device)
+        idx = top_indices.to(torch.int64).contiguous()
+        w32 = top_weights.float().contiguous()
+        send_expert = torch.empty(slots, dtype=torch.int32, device=device)
+        coef_slot = torch.empty(slots, dtype=torch.float32, device=device)
+        slot_of_assign = torch.empty(cap, dtype=torch.int64, device=device)
+        slot_src = torch.empty(slots, dtype=torch.int32, device=device)
+        _lib.call("mrb_ep_pack", idx.data_ptr(), w32.data_ptr(), t, k, per, world, cap, send_expert.data_ptr(),
+                  coef_slot.data_ptr(), slot_of_assign.data_ptr(), slot_src.data_ptr(), None, stream)
+        send_rows = torch.empty((slots, hidden), dtype=torch.bfloat16, device=device)
+        src = source.contiguous()
+        _lib.call("mrb_ep_gather_rows", src.data_ptr(), hidden, slot_src.data_ptr(), slots, send_rows.data_ptr(),
+                  stream)
+        recv_rows = torch.empty_like(send_rows)
+        recv_expert = torch.empty_like(send_expert)
+        dist.all_to_all_single(recv_rows, send_rows, group=self.group)
+        dist.all_to_all_single(recv_expert, send_expert, group=self.group)
+        # padding slots route to the dummy expert `per`, which the grouped MLP never runs
+        token_ids, _, starts, counts, inverse, _ = grouped_route_tensors_with_inverse(
+            recv_expert.view(-1, 1).to(torch.int64), torch.zeros((slots, 1), device=device), num_experts=per + 1)
+        eo = grouped_expert_mlp(recv_rows, token_ids, starts[:per], counts[:per], self.pages, self.layout)
+        back_local = eo.index_select(0, inverse)  # received-slot order
+        back = torch.empty_like(back_local)
+        dist.all_to_all_single(back, back_local, group=self.group)
+        out = torch.empty((t, hidden), dtype=torch.bfloat16, device=device)
+        _lib.call("mrb_stable_route_reduce", back.data_ptr(), coef_slot.data_ptr(), slot_of_assign.data_ptr(), t, k,
+                  hidden, None, out.data_ptr(), stream)
+        return out
+
+
 def torch_combine(rows: torch.Tensor, coef: torch.Tensor, inverse: torch.Tensor, t: int, k: int) -> torch.Tensor:
     """out[t] = sum_r coef[p] * rows[p], p = inverse[t*k + r]: fp32 products added in rank order."""
     per = rows.index_select(0, inverse).reshape(t, k, -1).float()
@@ -157,6 +214,7 @@ def local_expert_mlp_fn(pages: torch.Tensor, layout, experts_per_rank: int):
 
 __all__ = [
     "ExpertParallelMoE",
+    "FixedCapacityExpertParallelMoE",
     "ExpertShard",
     "local_expert_mlp_fn",
     "native_combine",

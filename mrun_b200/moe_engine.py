@@ -8,10 +8,11 @@ the ``.moe`` backend (route compiler, grouped int8 expert SwiGLU MLP, fixed-orde
 residual; then the final norm and a greedy head. Every dense projection (qkv, o, router,
 head, embedding) is an int8 qrow matrix; expert weights are int8 qrow pages.
 
-On one GPU the whole step is captured in a CUDA graph (no host synchronisation inside). With
-a process group of N ranks the experts are sharded (rank r owns experts [r*E/N, (r+1)*E/N))
-and each layer's MoE runs through ``ExpertParallelMoE`` (NCCL all-to-all); every rank decodes
-its own rows (data-parallel attention), so per-GPU work stays fixed as N grows.
+The whole step is captured in a CUDA graph (no host synchronisation inside). With a process
+group of N ranks the experts are sharded (rank r owns experts [r*E/N, (r+1)*E/N)) and each
+layer's MoE runs through ``FixedCapacityExpertParallelMoE`` (fixed-size NCCL all-to-all, so
+the exchange is captured with the rest of the step); every rank decodes its own rows
+(data-parallel attention), so per-GPU work stays fixed as N grows.
 """
 from __future__ import annotations
 
@@ -24,7 +25,7 @@ import torch
 from . import _lib
 from .dense_engine import QRow, rope_tables
 from .dense_qstore_cuda import qrow_argmax, qrow_linear, qrow_workspace_bytes, residual_rms_norm_into, rms_norm_into
-from .expert_parallel import ExpertParallelMoE, ExpertShard, local_expert_mlp_fn, native_combine, native_planner
+from .expert_parallel import ExpertShard, FixedCapacityExpertParallelMoE
 from .moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_topk
 from .paged_kv import PagedKVCache
 from .qstore_build import embed_rows
@@ -195,8 +196,7 @@ class MoeDecoder:
         self.group = group
         if self.world > 1:
             shard = ExpertShard(self.world, torch.distributed.get_rank(group), cfg.experts)
-            self.ep = [ExpertParallelMoE(shard, local_expert_mlp_fn(L.pages, weights.layout, shard.per_rank),
-                                         group=group, planner=native_planner, combine=native_combine)
+            self.ep = [FixedCapacityExpertParallelMoE(shard, L.pages, weights.layout, group=group)
                        for L in weights.layers]
             self.backend = None
         else:
@@ -271,9 +271,8 @@ class MoeDecoder:
 
     @torch.inference_mode()
     def capture(self, rows: int) -> None:
-        """Capture one decode step for `rows` rows in a CUDA graph (one GPU only)."""
-        if self.ep is not None:
-            raise RuntimeError("expert-parallel steps exchange split sizes on the host; run them eagerly")
+        """Capture one decode step for `rows` rows in a CUDA graph (with expert parallelism the
+        NCCL exchanges are captured too; every rank must capture)."""
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
         saved = (self.in_ids.clone(), self.positions.clone(), self.row_len.clone())

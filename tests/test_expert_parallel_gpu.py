@@ -1,5 +1,7 @@
 """Expert parallelism on 2+ GPUs (NCCL all-to-all over NVLink): each rank's MoE output must
-be bit-identical to the single-GPU backend over all experts. Skipped with fewer than 2 GPUs."""
+be bit-identical to the single-GPU backend over all experts, for the host-sized exchange and
+for the fixed-capacity exchange both eagerly and replayed from a CUDA graph. Skipped with
+fewer than 2 GPUs."""
 from __future__ import annotations
 
 import datetime
@@ -25,7 +27,8 @@ def _worker(rank, world, port, q):
     import torch.distributed as dist
 
     from mrun_b200.expert_parallel import (
-        ExpertParallelMoE, ExpertShard, local_expert_mlp_fn, native_combine, native_planner,
+        ExpertParallelMoE, ExpertShard, FixedCapacityExpertParallelMoE, local_expert_mlp_fn, native_combine,
+        native_planner,
     )
     from mrun_b200.moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, pack_expert_page, router_topk
     from oracle import qrow as oq
@@ -53,8 +56,23 @@ def _worker(rank, world, port, q):
         ep = ExpertParallelMoE(shard, local_expert_mlp_fn(mine, ly, shard.per_rank), planner=native_planner,
                                combine=native_combine)
         out = ep.forward(x, idx, w)
+        # the fixed-capacity exchange, eager and captured in a CUDA graph with its NCCL calls
+        fixed = FixedCapacityExpertParallelMoE(shard, mine, ly)
+        out_fixed = fixed.forward(x, idx, w)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fixed.forward(x, idx, w)  # warm-up outside the graph
+        torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(out, single)), ep.last_stats))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            out_graph = fixed.forward(x, idx, w)
+        graph.replay()
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(out, single) and torch.equal(out_fixed, single) and torch.equal(out_graph, single))
+        del graph  # before the process group goes away
+        q.put((rank, ok, ep.last_stats))
         dist.barrier()
     finally:
         dist.destroy_process_group()
