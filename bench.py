@@ -426,6 +426,107 @@ def run_moe_case(args) -> None:
         dist.destroy_process_group()
 
 
+def run_stream_case(args) -> None:
+    """Config 5: Mixtral-8x7B-shape expert pages (H 4096, F 14336, 8 experts, top-2; 176 MB
+    int8 per page) held in pinned host memory and streamed into an HBM slot cache of 25 % of
+    the expert bytes, for 256 decode rows (every expert is hit in every layer). A slice of
+    8 MoE layers is timed: streamed steps (next-layer prefetch on the copy stream, overlapped
+    with the current layer's grouped expert MLP), a copy-only pass over the same pages, and
+    the same steps on resident pages. Prints one JSON line; not the headline metric."""
+    import numpy as np
+    import torch
+
+    from mrun_b200.moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_topk
+    from mrun_b200.moe_engine import MoeConfig, MoeWeights
+    from mrun_b200.streaming import ExpertPageCache, HostPageTier
+
+    hidden, ffn, experts, top_k, rows, layers = 4096, 14336, 8, 2, 256, 8
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    layout = ExpertPageLayout.create(hidden, ffn)
+    cfg = MoeConfig(num_layers=1, hidden=hidden, heads=32, kv_heads=8, head_dim=128, experts=experts, top_k=top_k,
+                    expert_ffn=ffn, vocab=32000)
+    gen = torch.Generator(device=device).manual_seed(0)
+    page_set = MoeWeights._expert_pages(cfg, layout, gen, device, 0, experts)  # one layer's 8 pages
+    host = HostPageTier(layout, layers, experts)
+    for layer in range(layers):
+        host.pages[layer].copy_(page_set)
+    torch.cuda.synchronize(device)
+    budget = int(0.25 * layers * experts * layout.page_stride)
+    cache = ExpertPageCache(host, budget_bytes=budget, device=device)
+    streamed = PagedInt8ExpertBackend(cache, num_experts=experts)
+    resident = PagedInt8ExpertBackend(ResidentInt8ExpertPages(layout, [page_set] * layers), num_experts=experts)
+    rng = np.random.default_rng(0)
+    x = torch.from_numpy(rng.standard_normal((rows, hidden)).astype(np.float32) * 0.1).to(device).to(torch.bfloat16)
+    routes = [router_topk(torch.from_numpy(rng.standard_normal((rows, experts)).astype(np.float32)).to(device), top_k)
+              for _ in range(layers)]
+    everyone = list(range(experts))
+
+    def step(backend, streaming: bool):
+        h = x
+        for layer in range(layers):
+            if streaming:  # predicted experts of the next layer (all of them at 256 rows)
+                cache.prefetch((layer + 1) % layers, everyone, protect_layer=layer)
+            idx, w, _ = routes[layer]
+            h = backend.moe(layer, h, idx, w)
+        return h
+
+    def timed(fn, n):
+        stream = torch.cuda.current_stream(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / 1000.0 / n
+
+    for _ in range(args.warmup):
+        step(streamed, True)
+    cache.reset(clear_pages=False)
+    with ClockSampler(0) as clocks:
+        stream_s = timed(lambda: step(streamed, True), args.steps)
+    h2d = cache.stats.bytes_h2d / args.steps
+    for _ in range(2):
+        step(resident, False)
+    compute_s = timed(lambda: step(resident, False), args.steps)
+    # copy-only: the same number of page copies into the slot pool, back to back on one stream
+    from mrun_b200 import _lib
+
+    n_pages = max(1, int(round(h2d / layout.page_stride)))
+    slot_ids = torch.tensor([i % cache.capacity for i in range(n_pages)], dtype=torch.int32)
+    page_ids = torch.tensor([i % (layers * experts) for i in range(n_pages)], dtype=torch.int32)
+
+    def copy_only():
+        _lib.call("mrb_copy_pages", cache.slots.data_ptr(), layout.page_stride, host.pages.data_ptr(),
+                  layout.page_stride, slot_ids.data_ptr(), page_ids.data_ptr(), n_pages, layout.page_stride,
+                  torch.cuda.current_stream(device).cuda_stream, None)
+
+    copy_only()
+    copy_s = timed(copy_only, 2)
+    overlap = (copy_s + compute_s - stream_s) / max(1e-9, min(copy_s, compute_s))
+    line = {
+        "case": "stream-decode", "metric": "MoE decode with host-paged experts (config 5)",
+        "unit": "tokens/s", "value": rows / (stream_s * 32 / layers), "steps": args.steps, "warmup": args.warmup,
+        "config": {"workload": "config5: Mixtral-8x7B-shape experts (8 x 176 MB int8 pages per layer, top-2), "
+                               "256 decode rows, pinned host tier, HBM slot cache = 25% of expert bytes",
+                   "layers_timed": layers, "value_scaled_to_layers": 32, "page_bytes": layout.page_stride,
+                   "cache_slots": cache.capacity},
+        "ms_per_slice_step": stream_s * 1000.0,
+        "h2d_bytes_per_slice_step": h2d,
+        "h2d_gbs_streamed": h2d / stream_s / 1e9,
+        "h2d_gbs_copy_only": n_pages * layout.page_stride / copy_s / 1e9,
+        "ms_copy_only": copy_s * 1000.0,
+        "ms_compute_resident": compute_s * 1000.0,
+        "overlap_fraction": overlap,
+        "cache": cache.report(),
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -562,7 +663,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=["decode", "moe-decode", *GEMV_CASES, *TC_CASES], default="decode",
+    ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", *GEMV_CASES, *TC_CASES],
+                    default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -573,6 +675,8 @@ def main() -> None:
         run_tc_case(args)
     elif args.case == "moe-decode":
         run_moe_case(args)
+    elif args.case == "stream-decode":
+        run_stream_case(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -202,6 +202,7 @@ struct GroupedArgs {
   __nv_bfloat16* y;          // [A, n]
   int chunks;                // tile chunks per expert (work items per expert)
   int chunk_tiles;           // 16-row tiles per chunk
+  int maxr;                  // activation rows per pass (<= GX_MAXR; fewer when k is large)
 };
 
 __host__ __device__ inline int gx_steps(int64_t k, bool halves) {
@@ -209,17 +210,18 @@ __host__ __device__ inline int gx_steps(int64_t k, bool halves) {
   return halves ? (nkb + 1) / 2 : nkb;
 }
 __host__ __device__ inline int gx_xlen(int64_t k, bool halves) { return gx_steps(k, halves) * GX_KB * (halves ? 2 : 1); }
-__host__ __device__ inline size_t gx_xs_bytes(int64_t k, bool halves) {
-  return ((size_t)GX_MAXR * (gx_xlen(k, halves) + 8) * 2 + 15) & ~size_t(15);
+__host__ __device__ inline size_t gx_xs_bytes(int64_t k, bool halves, int maxr) {
+  return ((size_t)maxr * (gx_xlen(k, halves) + 8) * 2 + 15) & ~size_t(15);
 }
-__host__ inline size_t gx_smem_bytes(int64_t k, bool halves) {
-  return (size_t)GX_STAGES * GX_STAGE_BYTES + gx_xs_bytes(k, halves) + 32 * 4;
+__host__ inline size_t gx_smem_bytes(int64_t k, bool halves, int maxr) {
+  return (size_t)GX_STAGES * GX_STAGE_BYTES + gx_xs_bytes(k, halves, maxr) + 32 * 4;
 }
 
 // Grouped int8 expert projection over ragged per-expert row counts.
 //
 // Work item = (expert, chunk of 16-row tiles); a CTA walks items blockIdx.x, +gridDim.x, ...
-// (experts without rows are skipped). Per item and pass of up to 8 rows it stages the
+// (experts without rows are skipped). Per item and pass of up to maxr rows (8, or fewer when
+// 8 rows of in_features do not fit in shared memory) it stages the
 // expert's activation rows once (gathered through row_ids, exact power-of-two-scaled f16),
 // then each warp owns whole tiles of the chunk: it streams the tile's weights over the full
 // k through a per-thread cp.async ring (rows g and g+8, two streams per step: the gate and
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
   const int kspan = HALVES ? nks * GX_KB : 0;
   unsigned char* ring = smem;
   __half* xs = reinterpret_cast<__half*>(smem + (size_t)GX_STAGES * GX_STAGE_BYTES);
-  float* rscale = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + gx_xs_bytes(K, HALVES));
+  float* rscale = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + gx_xs_bytes(K, HALVES, a.maxr));
   unsigned* rmax = reinterpret_cast<unsigned*>(rscale + 16);  // [8]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -253,7 +255,8 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
   auto item_expert = [&](int item) { return item / a.chunks; };
   auto item_t0 = [&](int item) { return (item - item_expert(item) * a.chunks) * a.chunk_tiles; };
   auto item_t1 = [&](int item) { return min(rtiles, item_t0(item) + a.chunk_tiles); };
-  auto item_passes = [&](int item) { return (a.counts[item_expert(item)] + GX_MAXR - 1) / GX_MAXR; };
+  const int maxr = a.maxr;
+  auto item_passes = [&](int item) { return (a.counts[item_expert(item)] + maxr - 1) / maxr; };
 
   // ---- per-thread prefetch cursor over (item, pass, this warp's tile, k step)
   int pf_item = blockIdx.x, pf_pass = 0, pf_tile = 0, pf_step = 0, pf_koff = 0, slot_w = 0;
@@ -325,8 +328,8 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
     const int slot = a.slot_of ? a.slot_of[e] : e;
     const float* scales = a.scales + (int64_t)slot * a.scales_stride;
     const int t0 = item_t0(item), t1 = item_t1(item);
-    for (int p0 = 0; p0 < cnt; p0 += GX_MAXR) {
-      const int rows = min(GX_MAXR, cnt - p0);
+    for (int p0 = 0; p0 < cnt; p0 += maxr) {
+      const int rows = min(maxr, cnt - p0);
       // ---- stage this pass's activation rows (raw copy + row max, then exact scaled f16)
       __syncthreads();  // every warp is done with the previous pass's rows
       if (tid < GX_MAXR) rmax[tid] = 0u;
@@ -356,7 +359,7 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
         rscale[8 + tid] = ldexpf(1.0f, e2);
       }
       __syncthreads();
-      for (int idx = tid; idx < GX_MAXR * (xlen / 8); idx += GX_THREADS) {
+      for (int idx = tid; idx < maxr * (xlen / 8); idx += GX_THREADS) {
         const int r = idx / (xlen / 8), v = idx - r * (xlen / 8);
         uint4* sp = reinterpret_cast<uint4*>(xs + r * xstride + v * 8);
         __align__(16) __half hv[8];
@@ -379,7 +382,9 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
         for (int s = 0; s < 2; ++s)
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[s][i] = 0.f;
-        const __half* xp = xs + g * xstride + 16 * c;  // activation row g of the pass
+        // activation row g of the pass (mma column g); columns at or past maxr read the last
+        // staged row and their outputs are dropped in the epilogue
+        const __half* xp = xs + min(g, maxr - 1) * xstride + 16 * c;
         for (int ks = 0; ks < nks; ++ks, xp += GX_KB) {
           cp_async_wait_group<GX_STAGES - 2>();
           const unsigned char* st = ring + slot_r * GX_STAGE_BYTES + tid * 16;
@@ -565,14 +570,17 @@ extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, cons
   if (!aligned(codes, 16) || (codes_stride % 16) || !aligned(x_bf16, 16))
     return fail(MRB_ERR_ARG, "grouped_qrow: codes and activation rows must be 16-byte aligned");
   if (swiglu && up_rows < n) return fail(MRB_ERR_ARG, "grouped_qrow: up rows overlap the gate rows");
-  const size_t smem = gx_smem_bytes(k, !swiglu);
+  int maxr = GX_MAXR;  // rows per pass: the most whose staged activations fit next to the ring
+  while (maxr > 1 && gx_smem_bytes(k, !swiglu, maxr) > 227 * 1024) maxr /= 2;
+  const size_t smem = gx_smem_bytes(k, !swiglu, maxr);
   if (smem > 227 * 1024) return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: in_features %lld too large", (long long)k);
   if (experts * ((n + GX_ROWS - 1) / GX_ROWS) > 0x7fffffffLL)
     return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: too many expert tiles");
   GroupedArgs a{(const __nv_bfloat16*)x_bf16, row_ids, starts, counts, (int)experts, codes, codes_stride, scales,
-                scales_stride, slot_of, n, k, up_rows, (__nv_bfloat16*)y_bf16, 1, 1};
-  // two CTAs per SM; chunks of whole tiles per warp sized for about two work items per CTA
-  const int64_t slots = (int64_t)num_sms() * 2;
+                scales_stride, slot_of, n, k, up_rows, (__nv_bfloat16*)y_bf16, 1, 1, maxr};
+  // two CTAs per SM when two fit; chunks of whole tiles per warp sized for about two work
+  // items per CTA
+  const int64_t slots = (int64_t)num_sms() * (2 * (smem + 1024) <= 228 * 1024 ? 2 : 1);
   const int64_t rtiles = (n + GX_ROWS - 1) / GX_ROWS;
   const int64_t per_warp = std::max<int64_t>(1, experts * rtiles / (GX_WARPS * 2 * slots));
   a.chunk_tiles = (int)std::min<int64_t>(rtiles, per_warp * GX_WARPS);

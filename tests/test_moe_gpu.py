@@ -87,7 +87,11 @@ def _expert_pages(rng, experts, hidden, ffn, dev):
     return ly, pages, host
 
 
-@pytest.mark.parametrize("tokens,k,experts,hidden,ffn", [(32, 8, 16, 256, 128), (7, 2, 8, 512, 384), (64, 4, 8, 2048, 768)])
+@pytest.mark.parametrize("tokens,k,experts,hidden,ffn", [
+    (32, 8, 16, 256, 128), (7, 2, 8, 512, 384), (64, 4, 8, 2048, 768),
+    # Mixtral's expert ffn: the down projection's 14336 in_features stage 4 rows per pass
+    (24, 2, 2, 1024, 14336),
+])
 def test_moe_backend_vs_oracle_and_row_independence(tokens, k, experts, hidden, ffn, cuda):
     from mrun_b200.moe import PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_topk
 
