@@ -312,13 +312,18 @@ TC_CASES = {
     # name: (m, n, k) of the tcgen05 int8 GEMM (W8A8 prefill at the config-2 shapes)
     "int8-gemm-gateup": (512, 18944, 3584),
     "int8-gemm-down": (512, 3584, 18944),
+    # the tcgen05 W8A16 GEMM (bf16 activations, int8 weights): paired gate/up with the SwiGLU
+    # epilogue (n = output columns; 2n weight rows) and the down projection
+    "w8a16-gemm-gateup": (512, 18944, 3584),
+    "w8a16-gemm-down": (512, 3584, 18944),
 }
 
 
 def run_tc_case(args) -> None:
-    """Small case for kernel captures: the tcgen05 int8 GEMM (exact int32 accumulators) at a
-    config-2 prefill shape, alternating two weight matrices. Prints one JSON line with the
-    device-timed average and the int8 tensor throughput; not the bench metric."""
+    """Small case for kernel captures: a tcgen05 GEMM at a config-2 prefill shape (the int8
+    GEMM with exact int32 accumulators, or the W8A16 GEMM with bf16 activations), alternating
+    two weight matrices. Prints one JSON line with the device-timed average and the tensor
+    throughput; not the bench metric."""
     import torch
 
     from mrun_b200 import _lib
@@ -326,13 +331,32 @@ def run_tc_case(args) -> None:
     m, n, k = TC_CASES[args.case]
     device = torch.device("cuda", 0)
     gen = torch.Generator(device=device).manual_seed(0)
-    qx = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=device, generator=gen)
-    qws = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=gen) for _ in range(2)]
-    acc = torch.empty(m, n, dtype=torch.int32, device=device)
     stream = torch.cuda.current_stream(device)
+    w8a16 = args.case.startswith("w8a16")
+    paired = args.case == "w8a16-gemm-gateup"
+    wrows = 2 * n if paired else n  # weight rows the GEMM multiplies
+    qws = [torch.randint(-127, 128, (wrows, k), dtype=torch.int8, device=device, generator=gen) for _ in range(2)]
+    if w8a16:
+        x = (torch.randn(m, k, device=device, generator=gen)).to(torch.bfloat16)
+        scales = torch.rand(wrows, device=device, generator=gen) * 1e-3
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
 
-    def launch(i):
-        _lib.call("mrb_int8_gemm", qx.data_ptr(), qws[i % 2].data_ptr(), m, n, k, acc.data_ptr(), stream.cuda_stream)
+        def launch(i):
+            w = qws[i % 2]
+            if paired:
+                _lib.call("mrb_qrow_swiglu", x.data_ptr(), m, k, w.data_ptr(), scales.data_ptr(), w[n:].data_ptr(),
+                          scales[n:].data_ptr(), n, y.data_ptr(), None, 0, stream.cuda_stream)
+            else:
+                code = _lib.dtype_code(torch.bfloat16)
+                _lib.call("mrb_qrow_matmul", x.data_ptr(), code, m, k, w.data_ptr(), scales.data_ptr(), n, None,
+                          y.data_ptr(), code, None, 0, stream.cuda_stream)
+    else:
+        qx = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=device, generator=gen)
+        acc = torch.empty(m, n, dtype=torch.int32, device=device)
+
+        def launch(i):
+            _lib.call("mrb_int8_gemm", qx.data_ptr(), qws[i % 2].data_ptr(), m, n, k, acc.data_ptr(),
+                      stream.cuda_stream)
 
     for i in range(args.warmup):
         launch(i)
@@ -345,7 +369,8 @@ def run_tc_case(args) -> None:
     e1.record(stream)
     torch.cuda.synchronize(device)
     avg_s = e0.elapsed_time(e1) / 1000.0 / args.steps
-    print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "tops": 2 * m * n * k / avg_s / 1e12,
+    print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "tops": 2 * m * wrows * k / avg_s / 1e12,
+                      "kind": "bf16 x bf16 (int8 weights)" if w8a16 else "int8 x int8",
                       "launches": args.steps}), flush=True)
 
 

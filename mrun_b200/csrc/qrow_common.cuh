@@ -25,6 +25,19 @@ __device__ __forceinline__ void i8x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t
   hi = hsub2(prmt(u, 0x64646464u, 0x4342u), 0x64806480u);
 }
 
+// Four signed int8 codes -> bf16x2 of bytes (0,1) and bf16x2 of bytes (2,3), exactly: the
+// biased byte under the fp32 exponent of 2^23 minus (2^23 + 128) is the code as an fp32
+// integer, whose high half is its exact bf16.
+__device__ __forceinline__ void i8x4_to_bf16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const float f0 = __uint_as_float(prmt(u, 0x4B000000u, 0x7540u)) - 8388736.0f;
+  const float f1 = __uint_as_float(prmt(u, 0x4B000000u, 0x7541u)) - 8388736.0f;
+  const float f2 = __uint_as_float(prmt(u, 0x4B000000u, 0x7542u)) - 8388736.0f;
+  const float f3 = __uint_as_float(prmt(u, 0x4B000000u, 0x7543u)) - 8388736.0f;
+  lo = prmt(__float_as_uint(f0), __float_as_uint(f1), 0x7632u);
+  hi = prmt(__float_as_uint(f2), __float_as_uint(f3), 0x7632u);
+}
+
 // Four signed int8 codes -> f16x2 holding (q + 1152) for bytes (0,1) and (2,3), exactly:
 // one xor and two byte permutes; the constant 1152 is removed after the dot product as
 // 1152 * sum(x) (see the biased-code GEMV path).

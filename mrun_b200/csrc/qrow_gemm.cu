@@ -7,7 +7,7 @@
 // activation tile is XOR-swizzled in shared memory so fragment loads are conflict-free.
 // Within each 64-element k block the k order is permuted identically for both operands so
 // every lane reads 16 contiguous bytes per row. The fp32 accumulator is scaled once per row.
-#include "common.cuh"
+#include "qrow_common.cuh"
 
 #include <algorithm>
 
@@ -21,24 +21,6 @@ constexpr int GM_THREADS = 256;
 constexpr int GM_W_STAGE = GM_BN * GM_BK;      // int8 bytes
 constexpr int GM_X_STAGE = GM_BM * GM_BK * 2;  // bf16 bytes
 constexpr int GM_SMEM = GM_STAGES * (GM_W_STAGE + GM_X_STAGE);
-
-__device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t d;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-  return d;
-}
-
-// Four signed int8 codes -> bf16x2 of bytes (0,1) and bf16x2 of bytes (2,3), exactly.
-__device__ __forceinline__ void i8x4_to_bf16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  const float f0 = __uint_as_float(prmt_b32(u, 0x4B000000u, 0x7540u)) - 8388736.0f;
-  const float f1 = __uint_as_float(prmt_b32(u, 0x4B000000u, 0x7541u)) - 8388736.0f;
-  const float f2 = __uint_as_float(prmt_b32(u, 0x4B000000u, 0x7542u)) - 8388736.0f;
-  const float f3 = __uint_as_float(prmt_b32(u, 0x4B000000u, 0x7543u)) - 8388736.0f;
-  // small integers are exact in bf16: keep the high half of each fp32
-  lo = prmt_b32(__float_as_uint(f0), __float_as_uint(f1), 0x7632u);
-  hi = prmt_b32(__float_as_uint(f2), __float_as_uint(f3), 0x7632u);
-}
 
 __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {

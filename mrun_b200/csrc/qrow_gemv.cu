@@ -692,6 +692,10 @@ static int check_common(const void* x, int64_t m, int64_t k, const int8_t* codes
   return MRB_OK;
 }
 
+bool tc_w8a16_supported(const void* x, int64_t k, const int8_t* codes, const int8_t* up_codes);
+int tc_w8a16_gemm(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
+                  const int8_t* up_codes, const float* up_scales, int64_t n, const float* bias, __nv_bfloat16* y,
+                  cudaStream_t s);
 int qrow_gemm_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
                    int64_t n, const float* bias, __nv_bfloat16* y, cudaStream_t s);
 int qrow_gemm_swiglu_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* gate_codes,
@@ -719,8 +723,12 @@ static int qrow_gemv_dispatch(const void* x, int x_dtype, int64_t m, int64_t k, 
   const GemvArgs a = make_args(x, m, k, codes, scales, nullptr, nullptr, bias, n, y);
   switch (x_dtype) {
     case MRB_BF16:
-      if (m > GEMV_MAX_ROWS)
+      if (m > GEMV_MAX_ROWS) {
+        if (tc_w8a16_supported(x, k, codes, nullptr))
+          return tc_w8a16_gemm((const __nv_bfloat16*)x, m, k, codes, scales, nullptr, nullptr, n, bias,
+                               (__nv_bfloat16*)y, s);
         return qrow_gemm_bf16((const __nv_bfloat16*)x, m, k, codes, scales, n, bias, (__nv_bfloat16*)y, s);
+      }
       return dispatch_nt<__nv_bfloat16, __nv_bfloat16, false, EPI_STORE>(a, ws, s);
     case MRB_F16: return dispatch_nt<__half, __half, false, EPI_STORE>(a, ws, s);
     case MRB_F32: return dispatch_nt<float, float, true, EPI_STORE>(a, ws, s);
@@ -764,9 +772,13 @@ extern "C" int mrb_qrow_swiglu(const void* x_bf16, int64_t m, int64_t k, const i
   if (!up_codes || !up_scales) return fail(MRB_ERR_ARG, "qrow_swiglu: null up page");
   if (!aligned(up_codes, 16)) return fail(MRB_ERR_ARG, "qrow_swiglu: codes must be 16-byte aligned");
   if (m == 0) return MRB_OK;
-  if (m > GEMV_MAX_ROWS)
+  if (m > GEMV_MAX_ROWS) {
+    if (tc_w8a16_supported(x_bf16, k, gate_codes, up_codes))
+      return tc_w8a16_gemm((const __nv_bfloat16*)x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales, n,
+                           nullptr, (__nv_bfloat16*)y_bf16, (cudaStream_t)stream);
     return qrow_gemm_swiglu_bf16((const __nv_bfloat16*)x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales,
                                  n, (__nv_bfloat16*)y_bf16, (cudaStream_t)stream);
+  }
   const GemvArgs a = make_args(x_bf16, m, k, gate_codes, gate_scales, up_codes, up_scales, nullptr, n, y_bf16);
   return dispatch_nt<__nv_bfloat16, __nv_bfloat16, false, EPI_SWIGLU>(a, GvWorkspace{workspace, workspace_bytes},
                                                                       (cudaStream_t)stream);

@@ -19,6 +19,14 @@
 //  * warps 2-5: epilogue. Each warp owns the 32 TMEM lanes (tile rows) its index selects,
 //    loads 32 columns at a time with tcgen05.ld, rescales and stores, then releases the
 //    accumulators to the MMA thread.
+// Engine outputs: y_bf16 = bf16((float(acc)·s_x)·s_w + bias), or, with paired gate/up weight
+// pages (a B tile of BN/2 gate rows then the same BN/2 up rows), the SwiGLU
+// bf16(bf16(silu(bf16 g))·bf16 u) of the two rescaled accumulators.
+// Split-K (skinny activation blocks, e.g. 64-row W8A8 decode, whose output tiles fill few
+// SMs): a work item is (tile, k range); each warp stores its 32 rows' int32 partial
+// accumulators to a workspace and the last warp to arrive for those rows (a per-(tile,
+// quarter) counter) sums the partials and writes the outputs. int32 addition is exact, so
+// the result does not depend on the split or the arrival order.
 // Every wait is bounded: on a timeout the CTA records the failure, stops, and still frees
 // its TMEM. No load uses cluster multicast.
 #include "qrow_common.cuh"
@@ -50,15 +58,23 @@ struct TcTile {
 
 struct TcGemmArgs {
   CUtensorMap map_x;  // qx [m, k] int8, box [BM rows, 128 B], 128-byte swizzle
-  CUtensorMap map_w;  // qw [n, k] int8, box [BN rows, 128 B], 128-byte swizzle
-  int64_t m, n, k;
+  CUtensorMap map_w;  // qw [n, k] int8, box [BN (paired: BN/2) rows, 128 B], 128-byte swizzle
+  CUtensorMap map_u;  // paired: up codes [n, k] int8, box [BN/2 rows, 128 B]
+  int64_t m, n, k;    // n: output columns
   int tiles_m, tiles_n, kblocks;
-  const float* act_scale;  // [m] or null (then y is not written)
+  bool paired;
+  const float* act_scale;  // [m] or null (then y / y_bf16 are not written)
   const float* sw;         // [n]
-  const float* side;       // [m, n] or null
+  const float* sw_up;      // [n] (paired)
+  const float* side;       // [m, n] or null (fp32 output only)
+  const float* bias;       // [n] or null (bf16 output only), added in fp32
   float* y;                // [m, n] or null
-  int32_t* acc_out;        // [m, n] or null
-  bool vec_store;          // n % 4 == 0 and 16-byte aligned outputs: 16-byte stores
+  __nv_bfloat16* y_bf16;   // [m, n] or null
+  int32_t* acc_out;        // [m, n] or null (not paired)
+  bool vec_store;          // 16-byte aligned outputs with n % 4 == 0 (n % 8 for bf16)
+  int splits, kb_per;      // split-K: k blocks [split * kb_per, +kb_per) per work item
+  unsigned* counters;      // [tiles * 4] arrivals per (tile, TMEM lane quarter); zero between launches
+  int32_t* parts;          // [splits, m, tiles_n * BN] int32 partial accumulators
 };
 
 // Timed-out waits of the tensor-core GEMM since the last status read (0 in normal operation).
@@ -99,6 +115,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
   pdl_launch_dependents();
 
   const int ntiles = a.tiles_m * a.tiles_n;
+  const int items = ntiles * a.splits;
   auto fail_wait = [&]() {
     *abort_flag = 1;
     atomicAdd(&g_tc_timeouts, 1u);
@@ -112,9 +129,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
       pdl_wait();  // the quantised activations come from the previous kernel
       int stage = 0;
       unsigned phase = 0;
-      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+        const int t = it / a.splits;
         const int tm = t % a.tiles_m, tn = t / a.tiles_m;
-        for (int kb = 0; kb < a.kblocks; ++kb) {
+        const int kb0 = (it % a.splits) * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(empty + stage, phase ^ 1u)) {
             fail_wait();
             break;
@@ -122,7 +141,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
           unsigned char* st = smem + stage * Tile::STAGE_BYTES;
           mbar_arrive_expect_tx(full + stage, Tile::STAGE_BYTES);
           tma_load_2d(st, &a.map_x, kb * TC_BK, tm * BM, full + stage);
-          tma_load_2d(st + Tile::A_BYTES, &a.map_w, kb * TC_BK, tn * BN, full + stage);
+          if (a.paired) {
+            tma_load_2d(st + Tile::A_BYTES, &a.map_w, kb * TC_BK, tn * (BN / 2), full + stage);
+            tma_load_2d(st + Tile::A_BYTES + (BN / 2) * TC_BK, &a.map_u, kb * TC_BK, tn * (BN / 2), full + stage);
+          } else {
+            tma_load_2d(st + Tile::A_BYTES, &a.map_w, kb * TC_BK, tn * BN, full + stage);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -136,7 +160,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
       constexpr uint32_t idesc = umma_idesc(UMMA_D_S32, UMMA_S8, UMMA_S8, TC_HM, BN);
       int stage = 0, buf = 0;
       unsigned phase = 0, acc_phase = 0;
-      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+        const int t = it / a.splits;
+        const int kb0 = (it % a.splits) * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
         if (!mbar_wait_bounded(acc_empty + buf, acc_phase ^ 1u)) {
           fail_wait();
           break;
@@ -146,7 +172,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
         int halves = HALVES;
         while (halves > 1 && (int64_t)(t % a.tiles_m) * BM + (halves - 1) * TC_HM >= a.m) --halves;
         bool ok = true;
-        for (int kb = 0; kb < a.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(full + stage, phase)) {
             fail_wait();
             ok = false;
@@ -162,7 +188,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
             for (int h = 0; h < HALVES; ++h)
               if (h < halves)
                 umma_i8(tmem + acc_col(buf, h), umma_desc_k_sw128(sa + h * TC_HM * TC_BK + kk * TC_UK), db, idesc,
-                        kb > 0 || kk > 0);
+                        kb > kb0 || kk > 0);
           }
           umma_commit(empty + stage);  // the stage is free once these MMAs have read it
           if (++stage == STAGES) {
@@ -185,7 +211,68 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
     int buf = 0;
     unsigned acc_phase = 0;
     const bool vec = a.vec_store;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int out_cols = a.paired ? BN / 2 : BN;
+    const int64_t pstride = (int64_t)a.tiles_n * BN;  // partial-accumulator row stride
+    // 32 output columns [col0, col0 + 32) of one row from int32 accumulators v (gate or
+    // plain) and u (up, paired)
+    auto emit = [&](int64_t row, float as, int64_t col0, const uint32_t (&v)[32], const uint32_t (&u)[32]) {
+      const int64_t o0 = row * a.n + col0;
+      const bool full_run = vec && col0 + 32 <= a.n;
+      if (a.acc_out) {
+        if (full_run) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<int4*>(a.acc_out + o0 + j) =
+                make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
+        } else {
+          for (int j = 0; j < 32 && col0 + j < a.n; ++j) a.acc_out[o0 + j] = (int)v[j];
+        }
+      }
+      if (!a.act_scale) return;
+      if (a.y) {
+        float out[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int64_t col = col0 + j;
+          const float wsc = col < a.n ? a.sw[col] : 0.f;
+          float r = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), wsc);
+          if (a.side && col < a.n) r = __fadd_rn(a.side[o0 + j], r);
+          out[j] = r;
+        }
+        if (full_run) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(a.y + o0 + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
+        } else {
+          for (int j = 0; j < 32 && col0 + j < a.n; ++j) a.y[o0 + j] = out[j];
+        }
+      }
+      if (a.y_bf16) {
+        __align__(16) __nv_bfloat16 out[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int64_t col = col0 + j < a.n ? col0 + j : a.n - 1;
+          const float g = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), a.sw[col]);
+          if (a.paired) {
+            const float up = __fmul_rn(__fmul_rn(__int2float_rn((int)u[j]), as), a.sw_up[col]);
+            const float gv = round_bf16(g), uv = round_bf16(up);
+            out[j] = __float2bfloat16_rn(round_bf16(silu_f32(gv)) * uv);
+          } else {
+            out[j] = __float2bfloat16_rn(a.bias ? __fadd_rn(g, a.bias[col]) : g);
+          }
+        }
+        __nv_bfloat16* dst = a.y_bf16 + o0;
+        if (full_run) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8)
+            *reinterpret_cast<uint4*>(dst + j) = *reinterpret_cast<const uint4*>(out + j);
+        } else {
+          for (int j = 0; j < 32 && col0 + j < a.n; ++j) dst[j] = out[j];
+        }
+      }
+    };
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+      const int t = it / a.splits, split = it % a.splits;
       // warp-uniform: tcgen05.ld below is a whole-warp instruction
       bool ok = !*abort_flag && mbar_wait_bounded(acc_full + buf, acc_phase);
       ok = __all_sync(0xffffffffu, ok);
@@ -195,51 +282,75 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
       }
       tc_fence_after();
       const int tm = t % a.tiles_m, tn = t / a.tiles_m;
-      for (int h = 0; h < HALVES; ++h) {
-        if ((int64_t)tm * BM + h * TC_HM >= a.m) break;  // uniform: an empty half
-        const int64_t row = (int64_t)tm * BM + h * TC_HM + q * 32 + lane;
+      if (a.splits == 1) {
+        for (int h = 0; h < HALVES; ++h) {
+          if ((int64_t)tm * BM + h * TC_HM >= a.m) break;  // uniform: an empty half
+          const int64_t row = (int64_t)tm * BM + h * TC_HM + q * 32 + lane;
+          const bool row_ok = row < a.m;
+          const float as = (row_ok && a.act_scale) ? a.act_scale[row] : 0.f;
+          const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + acc_col(buf, h);
+          for (int c0 = 0; c0 < out_cols; c0 += 32) {
+            uint32_t v[32], u[32];
+            __syncwarp();
+            tmem_ld_32cols(tbase + (uint32_t)c0, v);
+            if (a.paired) tmem_ld_32cols(tbase + (uint32_t)(BN / 2 + c0), u);
+            const int64_t col0 = (int64_t)tn * out_cols + c0;
+            if (!row_ok || col0 >= a.n) continue;
+            emit(row, as, col0, v, u);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(acc_empty + buf);  // accumulators drained
+      } else {
+        // split-K (single-half tiles): store this k range's partials, release TMEM, and let
+        // the last warp to arrive for these 32 rows sum every split's partials
+        const int64_t row = (int64_t)tm * BM + q * 32 + lane;
         const bool row_ok = row < a.m;
-        const float as = (row_ok && a.act_scale) ? a.act_scale[row] : 0.f;
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + acc_col(buf, 0);
+        int32_t* mine = a.parts + ((int64_t)split * a.m + (row_ok ? row : 0)) * pstride + (int64_t)tn * BN;
         for (int c0 = 0; c0 < BN; c0 += 32) {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_32cols(tmem + ((uint32_t)(q * 32) << 16) + acc_col(buf, h) + (uint32_t)c0, v);
-          const int64_t col0 = (int64_t)tn * BN + c0;
-          if (!row_ok || col0 >= a.n) continue;
-          const int64_t o0 = row * a.n + col0;
-          const bool full_run = vec && col0 + 32 <= a.n;
-          if (a.acc_out) {
-            if (full_run) {
+          tmem_ld_32cols(tbase + (uint32_t)c0, v);
+          if (row_ok) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<int4*>(a.acc_out + o0 + j) =
-                    make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
-            } else {
-              for (int j = 0; j < 32 && col0 + j < a.n; ++j) a.acc_out[o0 + j] = (int)v[j];
-            }
-          }
-          if (a.y && a.act_scale) {
-            float out[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int64_t col = col0 + j;
-              const float wsc = col < a.n ? a.sw[col] : 0.f;
-              float r = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), wsc);
-              if (a.side && col < a.n) r = __fadd_rn(a.side[o0 + j], r);
-              out[j] = r;
-            }
-            if (full_run) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(a.y + o0 + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
-            } else {
-              for (int j = 0; j < 32 && col0 + j < a.n; ++j) a.y[o0 + j] = out[j];
-            }
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<int4*>(mine + c0 + j) = make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
           }
         }
+        tc_fence_before();
+        mbar_arrive(acc_empty + buf);
+        __threadfence();
+        __syncwarp();
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(a.counters + (int64_t)t * 4 + q, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == (unsigned)a.splits - 1u) {
+          __threadfence();
+          const float as = (row_ok && a.act_scale) ? a.act_scale[row] : 0.f;
+          for (int c0 = 0; c0 < out_cols; c0 += 32) {
+            const int64_t col0 = (int64_t)tn * out_cols + c0;
+            if (!row_ok || col0 >= a.n) continue;
+            uint32_t v[32], u[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = u[j] = 0u;
+            for (int sp = 0; sp < a.splits; ++sp) {
+              const int32_t* src = a.parts + ((int64_t)sp * a.m + row) * pstride + (int64_t)tn * BN + c0;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const int4 pv = __ldcg(reinterpret_cast<const int4*>(src + j));
+                v[j] += (uint32_t)pv.x; v[j + 1] += (uint32_t)pv.y; v[j + 2] += (uint32_t)pv.z; v[j + 3] += (uint32_t)pv.w;
+                if (a.paired) {
+                  const int4 pu = __ldcg(reinterpret_cast<const int4*>(src + BN / 2 + j));
+                  u[j] += (uint32_t)pu.x; u[j + 1] += (uint32_t)pu.y; u[j + 2] += (uint32_t)pu.z; u[j + 3] += (uint32_t)pu.w;
+                }
+              }
+            }
+            emit(row, as, col0, v, u);
+          }
+          if (lane == 0) a.counters[(int64_t)t * 4 + q] = 0u;  // ready for the next launch
+        }
       }
-      tc_fence_before();
-      mbar_arrive(acc_empty + buf);  // accumulators drained
       if (++buf == NBUF) {
         buf = 0;
         acc_phase ^= 1u;
@@ -254,7 +365,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
 }
 
 template <int HALVES, int BN>
-static int tc_launch(TcGemmArgs& a, const int8_t* qx, const int8_t* qw, cudaStream_t s) {
+static int tc_launch(TcGemmArgs& a, const int8_t* qx, const int8_t* qw, const int8_t* qw_up, cudaStream_t s) {
   using Tile = TcTile<HALVES, BN>;
   auto kern = tc_int8_gemm_kernel<HALVES, BN>;
   static bool configured = false;
@@ -265,40 +376,95 @@ static int tc_launch(TcGemmArgs& a, const int8_t* qx, const int8_t* qw, cudaStre
   }
   int st = encode_map_2d(&a.map_x, qx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m, a.k, Tile::BM, TC_BK,
                          CU_TENSOR_MAP_SWIZZLE_128B);
+  const int wrows = a.paired ? BN / 2 : BN;
   if (!st)
-    st = encode_map_2d(&a.map_w, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.n, a.k, BN, TC_BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    st = encode_map_2d(&a.map_w, qw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.n, a.k, wrows, TC_BK,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!st && a.paired)
+    st = encode_map_2d(&a.map_u, qw_up, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.n, a.k, wrows, TC_BK,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
   a.tiles_m = (int)((a.m + Tile::BM - 1) / Tile::BM);
-  a.tiles_n = (int)((a.n + BN - 1) / BN);
-  const int64_t ntiles = (int64_t)a.tiles_m * a.tiles_n;
-  if (ntiles > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "tc int8 gemm: too many tiles");
-  const int grid = (int)std::min<int64_t>(ntiles, num_sms());
+  a.tiles_n = (int)((a.n + wrows - 1) / wrows);
+  const int64_t items = (int64_t)a.tiles_m * a.tiles_n * a.splits;
+  if (items > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "tc int8 gemm: too many tiles");
+  const int grid = (int)std::min<int64_t>(items, num_sms());
   cudaError_t e = launch_kernel(kern, dim3(grid), dim3(TC_THREADS), Tile::SMEM, s, true, a);
   if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc int8 gemm: launch: %s", cudaGetErrorString(e));
   return launch_status("tc int8 gemm");
 }
 
+// Split-K plan for a problem whose 128 x 128 output tiles leave most SMs idle: about one
+// work item per SM with at least 4 k blocks each. 1 = no split.
+static int tc_split_plan(int64_t m, int64_t n, int64_t k, bool paired, int64_t* tiles_out) {
+  const int64_t out_cols = paired ? 64 : 128;
+  const int64_t tiles = ((m + 127) / 128) * ((n + out_cols - 1) / out_cols);
+  const int64_t kblocks = (k + TC_BK - 1) / TC_BK;
+  *tiles_out = tiles;
+  const int64_t sms = num_sms();
+  if (2 * tiles > sms || kblocks < 8) return 1;
+  const int64_t by_sm = (sms + tiles - 1) / tiles;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(by_sm, kblocks / 4));
+}
+
+size_t tc_int8_workspace_bytes(int64_t m, int64_t n, int64_t k, bool paired) {
+  int64_t tiles = 0;
+  const int splits = tc_split_plan(m, n, k, paired, &tiles);
+  if (splits <= 1) return 0;
+  const int64_t tiles_n = (n + (paired ? 64 : 128) - 1) / (paired ? 64 : 128);
+  const size_t counters = (((size_t)tiles * 4 * sizeof(unsigned)) + 255) & ~size_t(255);
+  return counters + (size_t)splits * (size_t)m * (size_t)tiles_n * 128 * sizeof(int32_t);
+}
+
 // Launch the tensor-core W8A8 GEMM (see the file comment); arguments are checked by callers.
 // Tile shape by SM fill: 256-row tiles when they give every SM at least two, else 128 x 256
-// double-buffered tiles when those fill the SMs, else 128 x 128.
-int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64_t k, const float* act_scale,
-                 const float* sw, const float* side, float* y, int32_t* acc_out, cudaStream_t s) {
+// double-buffered tiles when those fill the SMs, else 128 x 128 — split over k when those
+// leave most SMs idle and the caller gave a workspace of tc_int8_workspace_bytes().
+// qw_up non-null: paired gate/up pages (n outputs, SwiGLU epilogue, y_bf16 only).
+int tc_int8_gemm_ex(const int8_t* qx, const int8_t* qw, const int8_t* qw_up, int64_t m, int64_t n, int64_t k,
+                    const float* act_scale, const float* sw, const float* sw_up, const float* side,
+                    const float* bias, float* y, __nv_bfloat16* y_bf16, int32_t* acc_out, void* workspace,
+                    size_t workspace_bytes, cudaStream_t s) {
   TcGemmArgs a{};
   a.m = m;
   a.n = n;
   a.k = k;
   a.kblocks = (int)((k + TC_BK - 1) / TC_BK);
+  a.paired = qw_up != nullptr;
   a.act_scale = act_scale;
   a.sw = sw;
+  a.sw_up = sw_up;
   a.side = side;
+  a.bias = bias;
   a.y = y;
+  a.y_bf16 = y_bf16;
   a.acc_out = acc_out;
-  a.vec_store = (n % 4) == 0 && (!y || aligned(y, 16)) && (!acc_out || aligned(acc_out, 16));
+  a.vec_store = (n % 8) == 0 && (!y || aligned(y, 16)) && (!acc_out || aligned(acc_out, 16)) &&
+                (!y_bf16 || aligned(y_bf16, 16));
+  a.splits = 1;
+  a.kb_per = a.kblocks;
+  int64_t tiles = 0;
+  const int splits = tc_split_plan(m, n, k, a.paired, &tiles);
+  if (splits > 1 && workspace && workspace_bytes >= tc_int8_workspace_bytes(m, n, k, a.paired)) {
+    a.kb_per = (a.kblocks + splits - 1) / splits;
+    a.splits = (a.kblocks + a.kb_per - 1) / a.kb_per;  // no empty split
+    a.counters = reinterpret_cast<unsigned*>(workspace);
+    a.parts = reinterpret_cast<int32_t*>(reinterpret_cast<unsigned char*>(workspace) +
+                                         ((((size_t)tiles * 4 * sizeof(unsigned)) + 255) & ~size_t(255)));
+    return tc_launch<1, 128>(a, qx, qw, qw_up, s);
+  }
   const int64_t sms = num_sms();
-  auto tiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n + bn - 1) / bn); };
-  if (tiles(256, 256) >= 2 * sms) return tc_launch<2, 256>(a, qx, qw, s);
-  if (tiles(128, 256) >= sms) return tc_launch<1, 256>(a, qx, qw, s);
-  return tc_launch<1, 128>(a, qx, qw, s);
+  const int64_t wr = a.paired ? 2 : 1;  // weight rows per output column
+  auto ntiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n * wr + bn - 1) / bn); };
+  if (ntiles(256, 256) >= 2 * sms) return tc_launch<2, 256>(a, qx, qw, qw_up, s);
+  if (ntiles(128, 256) >= sms) return tc_launch<1, 256>(a, qx, qw, qw_up, s);
+  return tc_launch<1, 128>(a, qx, qw, qw_up, s);
+}
+
+int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64_t k, const float* act_scale,
+                 const float* sw, const float* side, float* y, int32_t* acc_out, cudaStream_t s) {
+  return tc_int8_gemm_ex(qx, qw, nullptr, m, n, k, act_scale, sw, nullptr, side, nullptr, y, nullptr, acc_out,
+                         nullptr, 0, s);
 }
 
 // Read and reset the count of timed-out waits (synchronises the device).
@@ -316,7 +482,16 @@ int tc_gemm_timeouts(unsigned* out) {
 
 }  // namespace mrb
 
+namespace mrb {
+int tc_w8a16_timeouts(unsigned* out);
+}
+
 extern "C" int mrb_tc_status(unsigned* timeouts) {
   if (!timeouts) return mrb::fail(MRB_ERR_ARG, "tc_status: null pointer");
-  return mrb::tc_gemm_timeouts(timeouts);
+  unsigned a = 0, b = 0;
+  int st = mrb::tc_gemm_timeouts(&a);
+  if (!st) st = mrb::tc_w8a16_timeouts(&b);
+  if (st) return st;
+  *timeouts = a + b;
+  return MRB_OK;
 }

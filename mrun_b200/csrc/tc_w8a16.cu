@@ -1,0 +1,396 @@
+// Prefill / large-batch W8A16 projection on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+//   y[m, j] = bf16(acc[m, j] * scale[j])                      (plain; + bf16 bias, rounded again)
+//   y[m, j] = bf16(bf16(silu(bf16(g * sg[j]))) * bf16(u * su[j]))   (paired gate/up, SwiGLU)
+// with acc[m, j] = sum_k x[m, k] * codes[j, k], bf16 x bf16 products accumulated in fp32
+// (kind::f16). int8 codes convert to bf16 exactly, so this is the W8A16 contract of the
+// reference's QStore linear (engine/kernels/qstore.py:95-128) with the per-row scale applied
+// once to the accumulator.
+//
+// The tensor core reads both operands from shared memory, but the weights arrive as int8:
+//  * warp 0, one thread: TMA producer of the raw int8 weight boxes ([BN x 64 B], no swizzle;
+//    the gate and up halves as two boxes when paired) into a ring of its own, running ahead
+//    of the conversion;
+//  * warps 6-13 (256 threads): converters. Per stage they wait for the stage to be free,
+//    one elected thread issues the activation TMA ([BM x 64 bf16], 128-byte swizzle), and
+//    all of them turn the raw int8 box into bf16 rows in the 128-byte-swizzled K-major
+//    layout the MMA descriptor reads (chunk c of row r at c ^ (r & 7)), fence the writes to
+//    the async proxy and arrive on the stage barrier;
+//  * warp 1: TMEM owner; one thread issues tcgen05.mma (M=128 per accumulator half, N=BN,
+//    K=16) and commits stages and finished tiles;
+//  * warps 2-5: epilogue, TMEM -> registers -> bf16 rows.
+// Tiles are HALVES 128-row activation accumulators x BN weight rows, chosen by SM fill like
+// the int8 GEMM; persistent CTAs walk tiles with the M tiles of one weight tile adjacent.
+// Every wait is bounded; on a timeout the CTA records it, stops, and still frees its TMEM.
+// No load uses cluster multicast.
+#include "qrow_common.cuh"
+#include "tc_common.cuh"
+
+#include <algorithm>
+
+namespace mrb {
+
+constexpr int TW_HM = 128;            // MMA M (activation rows of one accumulator)
+constexpr int TW_BKE = 64;            // k elements per stage: one 128-byte bf16 swizzle row
+constexpr int TW_UK_BYTES = 32;       // k bytes per MMA (16 bf16)
+constexpr int TW_CVT_WARP0 = 6;       // first converter warp
+constexpr int TW_CVT_THREADS = 256;   // 8 converter warps
+constexpr int TW_EPI_THREADS = 128;
+constexpr int TW_THREADS = TW_CVT_WARP0 * 32 + TW_CVT_THREADS;
+constexpr size_t TW_SMEM_LIMIT = 227 * 1024;
+
+template <int HALVES, int BN>
+struct TwTile {
+  static constexpr int BM = TW_HM * HALVES;
+  static constexpr int A_BYTES = BM * 128;   // bf16 activations [BM x 64]
+  static constexpr int B_BYTES = BN * 128;   // converted bf16 weights [BN x 64]
+  static constexpr int RAW_BYTES = BN * 64;  // int8 weights [BN x 64]
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int RAW_STAGES = HALVES == 2 ? 2 : 4;
+  static constexpr size_t FIXED = 1024 + 512 + (size_t)RAW_STAGES * RAW_BYTES;
+  static constexpr int STAGES_FIT = (int)((TW_SMEM_LIMIT - FIXED) / STAGE_BYTES);
+  static constexpr int STAGES = STAGES_FIT < 6 ? STAGES_FIT : 6;
+  static constexpr int NBUF = HALVES == 1 ? 2 : 1;
+  static constexpr unsigned TMEM_COLS = HALVES * BN * NBUF <= 256 ? 256u : 512u;
+  static constexpr size_t SMEM = FIXED + (size_t)STAGES * STAGE_BYTES;
+  static_assert(STAGES >= 2, "tile does not fit in shared memory");
+  static_assert(SMEM <= TW_SMEM_LIMIT, "tile does not fit in shared memory");
+  static_assert(HALVES * BN * NBUF <= 512, "accumulators exceed TMEM");
+};
+
+struct TwGemmArgs {
+  CUtensorMap map_x;   // x [m, k] bf16, box [BM rows, 64], 128-byte swizzle
+  CUtensorMap map_w;   // codes [n, k] int8, box [BN (paired: BN/2) rows, 64 B]
+  CUtensorMap map_u;   // paired: up codes [n, k] int8, box [BN/2 rows, 64 B]
+  int64_t m, n, k;     // n: output columns
+  int tiles_m, tiles_n, kblocks;
+  bool paired;
+  const float* scales;     // [n]
+  const float* scales_up;  // [n] (paired)
+  const float* bias;       // [n] or null (plain only)
+  __nv_bfloat16* y;        // [m, n]
+  bool vec_store;          // n % 8 == 0 and y 16-byte aligned
+};
+
+__device__ unsigned g_tw_timeouts = 0;
+
+template <int HALVES, int BN>
+__global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __grid_constant__ TwGemmArgs a) {
+  using Tile = TwTile<HALVES, BN>;
+  constexpr int STAGES = Tile::STAGES, RAW_STAGES = Tile::RAW_STAGES, NBUF = Tile::NBUF, BM = Tile::BM;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* raw_base = smem + STAGES * Tile::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(raw_base + RAW_STAGES * Tile::RAW_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* raw_full = empty + STAGES;
+  uint64_t* raw_empty = raw_full + RAW_STAGES;
+  uint64_t* acc_full = raw_empty + RAW_STAGES;
+  uint64_t* acc_empty = acc_full + NBUF;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NBUF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1 + TW_CVT_THREADS);  // activation TMA (expect_tx) + every converter
+      mbar_init(empty + s, 1);
+    }
+    for (int s = 0; s < RAW_STAGES; ++s) {
+      mbar_init(raw_full + s, 1);
+      mbar_init(raw_empty + s, TW_CVT_THREADS);
+    }
+    for (int b = 0; b < NBUF; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, TW_EPI_THREADS);
+    }
+    *abort_flag = 0;
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Tile::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+
+  const int ntiles = a.tiles_m * a.tiles_n;
+  auto fail_wait = [&]() {
+    *abort_flag = 1;
+    atomicAdd(&g_tw_timeouts, 1u);
+  };
+  auto acc_col = [&](int b, int h) { return (uint32_t)((b * HALVES + h) * BN); };
+  const int out_cols = a.paired ? BN / 2 : BN;
+
+  if (warp == 0) {
+    // ---------------- raw int8 weight producer
+    if (lane == 0) {
+      pdl_wait();
+      int rs = 0;
+      unsigned rphase = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+        const int tn = t / a.tiles_m;
+        for (int kb = 0; kb < a.kblocks; ++kb) {
+          if (!mbar_wait_bounded(raw_empty + rs, rphase ^ 1u)) {
+            fail_wait();
+            break;
+          }
+          unsigned char* dst = raw_base + rs * Tile::RAW_BYTES;
+          mbar_arrive_expect_tx(raw_full + rs, Tile::RAW_BYTES);
+          if (a.paired) {
+            tma_load_2d(dst, &a.map_w, kb * TW_BKE, tn * (BN / 2), raw_full + rs);
+            tma_load_2d(dst + Tile::RAW_BYTES / 2, &a.map_u, kb * TW_BKE, tn * (BN / 2), raw_full + rs);
+          } else {
+            tma_load_2d(dst, &a.map_w, kb * TW_BKE, tn * BN, raw_full + rs);
+          }
+          if (++rs == RAW_STAGES) {
+            rs = 0;
+            rphase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(UMMA_D_F32, UMMA_BF16, UMMA_BF16, TW_HM, BN);
+      int stage = 0, buf = 0;
+      unsigned phase = 0, acc_phase = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+        if (!mbar_wait_bounded(acc_empty + buf, acc_phase ^ 1u)) {
+          fail_wait();
+          break;
+        }
+        tc_fence_after();
+        int halves = HALVES;
+        while (halves > 1 && (int64_t)(t % a.tiles_m) * BM + (halves - 1) * TW_HM >= a.m) --halves;
+        bool ok = true;
+        for (int kb = 0; kb < a.kblocks; ++kb) {
+          if (!mbar_wait_bounded(full + stage, phase)) {
+            fail_wait();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Tile::STAGE_BYTES);
+          const uint32_t sb = sa + Tile::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 128 / TW_UK_BYTES; ++kk) {
+            const uint64_t db = umma_desc_k_sw128(sb + kk * TW_UK_BYTES);
+#pragma unroll
+            for (int h = 0; h < HALVES; ++h)
+              if (h < halves)
+                umma_f16(tmem + acc_col(buf, h), umma_desc_k_sw128(sa + h * TW_HM * 128 + kk * TW_UK_BYTES), db,
+                         idesc, kb > 0 || kk > 0);
+          }
+          umma_commit(empty + stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(acc_full + buf);
+        if (++buf == NBUF) {
+          buf = 0;
+          acc_phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp < TW_CVT_WARP0) {
+    // ---------------- epilogue
+    pdl_wait();
+    const int q = warp & 3;
+    int buf = 0;
+    unsigned acc_phase = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      bool ok = !*abort_flag && mbar_wait_bounded(acc_full + buf, acc_phase);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0 && !*abort_flag) fail_wait();
+        break;
+      }
+      tc_fence_after();
+      const int tm = t % a.tiles_m, tn = t / a.tiles_m;
+      for (int h = 0; h < HALVES; ++h) {
+        if ((int64_t)tm * BM + h * TW_HM >= a.m) break;
+        const int64_t row = (int64_t)tm * BM + h * TW_HM + q * 32 + lane;
+        const bool row_ok = row < a.m;
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + acc_col(buf, h);
+        for (int c0 = 0; c0 < out_cols; c0 += 32) {
+          uint32_t v[32], u[32];
+          __syncwarp();
+          tmem_ld_32cols(tbase + (uint32_t)c0, v);
+          if (a.paired) tmem_ld_32cols(tbase + (uint32_t)(BN / 2 + c0), u);
+          const int64_t col0 = (int64_t)tn * out_cols + c0;
+          if (!row_ok || col0 >= a.n) continue;
+          __align__(16) __nv_bfloat16 out[32];
+          if (a.paired) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int64_t col = col0 + j < a.n ? col0 + j : a.n - 1;
+              const float gv = round_bf16(__uint_as_float(v[j]) * a.scales[col]);
+              const float uv = round_bf16(__uint_as_float(u[j]) * a.scales_up[col]);
+              out[j] = __float2bfloat16_rn(round_bf16(silu_f32(gv)) * uv);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int64_t col = col0 + j < a.n ? col0 + j : a.n - 1;
+              float r = __uint_as_float(v[j]) * a.scales[col];
+              if (a.bias) r = round_bf16(r) + round_bf16(a.bias[col]);
+              out[j] = __float2bfloat16_rn(r);
+            }
+          }
+          __nv_bfloat16* dst = a.y + row * a.n + col0;
+          if (a.vec_store && col0 + 32 <= a.n) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8)
+              *reinterpret_cast<uint4*>(dst + j) = *reinterpret_cast<const uint4*>(out + j);
+          } else {
+            for (int j = 0; j < 32 && col0 + j < a.n; ++j) dst[j] = out[j];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty + buf);
+      if (++buf == NBUF) {
+        buf = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------- converters: int8 raw box -> swizzled bf16 B operand
+    const int ct = tid - TW_CVT_WARP0 * 32;
+    const bool leader = ct == 0;
+    if (leader) pdl_wait();  // the activations come from the previous kernel
+    int stage = 0, rs = 0;
+    unsigned phase = 0, rphase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      const int tm = t % a.tiles_m;
+      for (int kb = 0; kb < a.kblocks; ++kb) {
+        ok = !*abort_flag && mbar_wait_bounded(empty + stage, phase ^ 1u);
+        if (ok && leader) {
+          unsigned char* st = smem + stage * Tile::STAGE_BYTES;
+          mbar_arrive_expect_tx(full + stage, Tile::A_BYTES);
+          tma_load_2d(st, &a.map_x, kb * TW_BKE, tm * BM, full + stage);
+        }
+        ok = ok && mbar_wait_bounded(raw_full + rs, rphase);
+        if (!ok) {
+          if (!*abort_flag) fail_wait();
+          break;
+        }
+        const unsigned char* raw = raw_base + rs * Tile::RAW_BYTES;
+        unsigned char* dst = smem + stage * Tile::STAGE_BYTES + Tile::A_BYTES;
+#pragma unroll
+        for (int j = 0; j < BN * 4 / TW_CVT_THREADS; ++j) {
+          const int i = ct + j * TW_CVT_THREADS;  // 16-byte chunk of the raw box
+          const int r = i >> 2, qk = i & 3;       // weight row, k quarter (16 codes)
+          const uint4 w = *reinterpret_cast<const uint4*>(raw + r * 64 + qk * 16);
+          uint4 lo, hi;
+          i8x4_to_bf16x2(w.x, lo.x, lo.y);
+          i8x4_to_bf16x2(w.y, lo.z, lo.w);
+          i8x4_to_bf16x2(w.z, hi.x, hi.y);
+          i8x4_to_bf16x2(w.w, hi.z, hi.w);
+          unsigned char* row = dst + r * 128;
+          *reinterpret_cast<uint4*>(row + (((2 * qk) ^ (r & 7)) << 4)) = lo;
+          *reinterpret_cast<uint4*>(row + (((2 * qk + 1) ^ (r & 7)) << 4)) = hi;
+        }
+        fence_proxy_async_smem();  // make the converted rows visible to the tensor core
+        mbar_arrive(raw_empty + rs);
+        mbar_arrive(full + stage);
+        if (++rs == RAW_STAGES) {
+          rs = 0;
+          rphase ^= 1u;
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, Tile::TMEM_COLS);
+}
+
+template <int HALVES, int BN>
+static int tw_launch(TwGemmArgs& a, const __nv_bfloat16* x, const int8_t* codes, const int8_t* up_codes,
+                     cudaStream_t s) {
+  using Tile = TwTile<HALVES, BN>;
+  auto kern = tc_w8a16_gemm_kernel<HALVES, BN>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile::SMEM);
+    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc w8a16 gemm: smem attribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  const int wrows = a.paired ? BN / 2 : BN;
+  int st = encode_map_2d(&a.map_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.m, a.k, Tile::BM, TW_BKE,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!st)
+    st = encode_map_2d(&a.map_w, codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.n, a.k, wrows, TW_BKE,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!st && a.paired)
+    st = encode_map_2d(&a.map_u, up_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.n, a.k, wrows, TW_BKE,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (st) return st;
+  a.tiles_m = (int)((a.m + Tile::BM - 1) / Tile::BM);
+  a.tiles_n = (int)((a.n + wrows - 1) / wrows);
+  const int64_t ntiles = (int64_t)a.tiles_m * a.tiles_n;
+  if (ntiles > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "tc w8a16 gemm: too many tiles");
+  const int grid = (int)std::min<int64_t>(ntiles, num_sms());
+  cudaError_t e = launch_kernel(kern, dim3(grid), dim3(TW_THREADS), Tile::SMEM, s, true, a);
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc w8a16 gemm: launch: %s", cudaGetErrorString(e));
+  return launch_status("tc w8a16 gemm");
+}
+
+// Whether the tensor-core path takes this problem: TMA needs 16-byte aligned bases and row
+// strides (k % 16 for the int8 codes, which also covers the bf16 activations).
+bool tc_w8a16_supported(const void* x, int64_t k, const int8_t* codes, const int8_t* up_codes) {
+  return k % 16 == 0 && aligned(x, 16) && aligned(codes, 16) && (!up_codes || aligned(up_codes, 16));
+}
+
+// Launch the tensor-core W8A16 GEMM (see the file comment); the caller checked the shapes and
+// tc_w8a16_supported(). up_codes non-null selects the paired SwiGLU epilogue (n outputs from
+// n gate rows and n up rows).
+int tc_w8a16_gemm(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
+                  const int8_t* up_codes, const float* up_scales, int64_t n, const float* bias, __nv_bfloat16* y,
+                  cudaStream_t s) {
+  TwGemmArgs a{};
+  a.m = m;
+  a.n = n;
+  a.k = k;
+  a.kblocks = (int)((k + TW_BKE - 1) / TW_BKE);
+  a.paired = up_codes != nullptr;
+  a.scales = scales;
+  a.scales_up = up_scales;
+  a.bias = a.paired ? nullptr : bias;
+  a.y = y;
+  a.vec_store = (n % 8) == 0 && aligned(y, 16);
+  const int64_t sms = num_sms();
+  const int64_t per_tile = a.paired ? 2 : 1;  // weight rows per output column
+  auto tiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n * per_tile + bn - 1) / bn); };
+  if (tiles(256, 256) >= 2 * sms) return tw_launch<2, 256>(a, x, codes, up_codes, s);
+  if (tiles(128, 256) >= sms) return tw_launch<1, 256>(a, x, codes, up_codes, s);
+  return tw_launch<1, 128>(a, x, codes, up_codes, s);
+}
+
+int tc_w8a16_timeouts(unsigned* out) {
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tw_timeouts, sizeof(v));
+  if (e == cudaSuccess && v) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_tw_timeouts, &zero, sizeof(zero));
+  }
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tensor-core status: %s", cudaGetErrorString(e));
+  *out = v;
+  return MRB_OK;
+}
+
+}  // namespace mrb

@@ -408,6 +408,11 @@ __global__ void __launch_bounds__(I8_THREADS, 1) int8_gemm_kernel(I8GemmArgs a) 
 
 int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64_t k, const float* act_scale,
                  const float* sw, const float* side, float* y, int32_t* acc_out, cudaStream_t s);
+int tc_int8_gemm_ex(const int8_t* qx, const int8_t* qw, const int8_t* qw_up, int64_t m, int64_t n, int64_t k,
+                    const float* act_scale, const float* sw, const float* sw_up, const float* side,
+                    const float* bias, float* y, __nv_bfloat16* y_bf16, int32_t* acc_out, void* workspace,
+                    size_t workspace_bytes, cudaStream_t s);
+size_t tc_int8_workspace_bytes(int64_t m, int64_t n, int64_t k, bool paired);
 
 static int launch_int8_gemm(const I8GemmArgs& a, cudaStream_t s) {
   return tc_int8_gemm(a.qx, a.qw, a.m, a.n, a.k, a.act_scale, a.sw, a.side, a.y, a.acc_out, s);
@@ -542,6 +547,34 @@ extern "C" int mrb_w8a8_matmul(const void* x, int x_dtype, int64_t m, int64_t k,
   if (st) return st;
   I8GemmArgs a{qx_ws, qw, m, n, k, scale_ws, sw, side, y, acc_out};
   return launch_int8_gemm(a, s);
+}
+
+extern "C" size_t mrb_w8a8_workspace(int64_t m, int64_t n, int64_t k, int paired) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  return tc_int8_workspace_bytes(m, n, k, paired != 0);
+}
+
+extern "C" int mrb_w8a8_linear_bf16(const void* x_bf16, int64_t m, int64_t k, const int8_t* codes,
+                                    const float* scales, const int8_t* up_codes, const float* up_scales,
+                                    const float* bias, int64_t n, void* y_bf16, int8_t* qx_ws, float* scale_ws,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (m < 0 || k <= 0 || n <= 0) return fail(MRB_ERR_ARG, "w8a8_linear: bad shape");
+  if (m == 0) return MRB_OK;
+  if (!x_bf16 || !codes || !scales || !y_bf16 || !qx_ws || !scale_ws)
+    return fail(MRB_ERR_ARG, "w8a8_linear: null pointer");
+  if ((up_codes == nullptr) != (up_scales == nullptr))
+    return fail(MRB_ERR_ARG, "w8a8_linear: up codes and up scales go together");
+  if (up_codes && bias) return fail(MRB_ERR_ARG, "w8a8_linear: the paired SwiGLU takes no bias");
+  if (k % 16) return fail(MRB_ERR_UNSUPPORTED, "w8a8_linear: k %lld is not a multiple of 16", (long long)k);
+  if (k > 133000) return fail(MRB_ERR_UNSUPPORTED, "w8a8_linear: k %lld could overflow int32", (long long)k);
+  if (!aligned(codes, 16) || !aligned(qx_ws, 16) || (up_codes && !aligned(up_codes, 16)))
+    return fail(MRB_ERR_ARG, "w8a8_linear: codes and the qx workspace must be 16-byte aligned");
+  if (workspace && !aligned(workspace, 256)) return fail(MRB_ERR_ARG, "w8a8_linear: workspace must be 256-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = quantize_dispatch(x_bf16, MRB_BF16, m, k, nullptr, qx_ws, scale_ws, s);
+  if (st) return st;
+  return tc_int8_gemm_ex(qx_ws, codes, up_codes, m, n, k, scale_ws, scales, up_scales, nullptr, bias, nullptr,
+                         (__nv_bfloat16*)y_bf16, nullptr, workspace, workspace_bytes, s);
 }
 
 // ------------------------------------------------------------------ outlier column selection

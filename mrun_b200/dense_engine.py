@@ -10,6 +10,12 @@ the first maximal index on the device.
 
 Weights live in HBM as int8 codes + fp32 row scales (the QStore ``qrow`` layout); q/k/v are
 stored as one concatenated page so one GEMV streams all three.
+
+``mode="w8a8"`` runs every body projection as the W8A8 store matmul of ``enable_w8a8``
+(engine/kernels/w8a8.py:145-177): per-token int8 activations, exact int32 accumulation on the
+tensor cores (split over k for skinny row blocks), fp32 rescale (+ fp32 bias), one bf16
+rounding; gate/up stay paired with the SwiGLU epilogue. The greedy head keeps the exact fp32
+head of ``_head`` (engine/dense_qstore_cuda.py:800-896).
 """
 from __future__ import annotations
 
@@ -24,6 +30,7 @@ from .dense_qstore_cuda import (qrow_argmax, qrow_linear, qrow_swiglu, qrow_work
                                 rms_norm_into)
 from .paged_kv import PagedKVCache
 from .qstore_build import embed_rows, quant_row_int8
+from .w8a8 import w8a8_linear_bf16, w8a8_workspace_bytes
 
 
 @dataclass(frozen=True)
@@ -178,7 +185,11 @@ class DenseDecoder:
         device: torch.device,
         num_pages: int | None = None,
         max_prefill_tokens: int = 2048,
+        mode: str = "w8a16",
     ) -> None:
+        if mode not in ("w8a16", "w8a8"):
+            raise ValueError(f"unknown projection mode {mode!r}")
+        self.mode = mode
         self.w = weights
         self.cfg = cfg = weights.cfg
         self.device = device
@@ -204,6 +215,17 @@ class DenseDecoder:
         # GEMV stream-K workspace shared by every projection (all ordered on one stream)
         gemv_ws = max(qrow_workspace_bytes(device, n) for n in (cfg.qkv_rows, cfg.hidden, cfg.ffn))
         self.gemv_workspace = torch.zeros(gemv_ws, dtype=torch.uint8, device=device)
+        if mode == "w8a8":
+            # per-token int8 activations and the split-K workspace of the tensor-core GEMM,
+            # shared by every projection (all ordered on one stream)
+            shapes = [(cfg.qkv_rows, cfg.hidden, False), (cfg.hidden, cfg.heads * cfg.head_dim, False),
+                      (cfg.ffn, cfg.hidden, True), (cfg.hidden, cfg.ffn, False)]
+            split_ws = max(w8a8_workspace_bytes(device, r, n, k, paired=pd)
+                           for r in {1, self.max_batch, self.max_prefill_tokens} for n, k, pd in shapes)
+            self.w8_workspace = torch.zeros(max(split_ws, 256), dtype=torch.uint8, device=device)
+            self.w8_qx = torch.empty(rows, max(cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim), dtype=torch.int8,
+                                     device=device)
+            self.w8_scale = torch.empty(rows, dtype=torch.float32, device=device)
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=device)
         bf = torch.bfloat16
         h = cfg.hidden
@@ -243,9 +265,27 @@ class DenseDecoder:
         mlp = buf["mlp"][:rows]
         qd, kd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
         gws = self.gemv_workspace
+        if self.mode == "w8a8":
+            def linear(page, x, out, bias=None):
+                k = int(x.shape[1])
+                return w8a8_linear_bf16(page.codes, page.scales, x, bias=bias, out=out,
+                                        qx_ws=self.w8_qx[:rows, :k], scale_ws=self.w8_scale[:rows],
+                                        workspace=self.w8_workspace)
+
+            def swiglu(gate, up, x, out):
+                k = int(x.shape[1])
+                return w8a8_linear_bf16(gate.codes, gate.scales, x, up=(up.codes, up.scales), out=out,
+                                        qx_ws=self.w8_qx[:rows, :k], scale_ws=self.w8_scale[:rows],
+                                        workspace=self.w8_workspace)
+        else:
+            def linear(page, x, out, bias=None):
+                return qrow_linear(page.codes, page.scales, x, bias=bias, out=out, workspace=gws)
+
+            def swiglu(gate, up, x, out):
+                return qrow_swiglu(gate.codes, gate.scales, up.codes, up.scales, x, out=out, workspace=gws)
         rms_norm_into(hidden, w.layers[0].ln1, cfg.eps, normed)
         for i, layer in enumerate(w.layers):
-            qrow_linear(layer.qkv.codes, layer.qkv.scales, normed, bias=layer.qkv_bias, out=qkv, workspace=gws)
+            linear(layer.qkv, normed, qkv, bias=layer.qkv_bias)
             self.kv.append(
                 i, qkv[:, qd:], qkv[:, qd + kd:], positions, token_rows, q_rows=qkv, q_out=q,
                 rope=(self.cos, self.sin), in_row_stride=cfg.qkv_rows, num_heads=cfg.heads,
@@ -253,11 +293,10 @@ class DenseDecoder:
             )
             self.kv.attend(i, q, row_len, max_total_tokens=max_total, row_seq=token_rows, out=ctx,
                            workspace=self.workspace, scale=self.scale)
-            qrow_linear(layer.o.codes, layer.o.scales, ctx.view(rows, qd), out=proj, workspace=gws)
+            linear(layer.o, ctx.view(rows, qd), proj)
             residual_rms_norm_into(hidden, proj, layer.ln2, cfg.eps, hidden, normed)
-            qrow_swiglu(layer.gate.codes, layer.gate.scales, layer.up.codes, layer.up.scales, normed, out=mlp,
-                        workspace=gws)
-            qrow_linear(layer.down.codes, layer.down.scales, mlp, out=proj, workspace=gws)
+            swiglu(layer.gate, layer.up, normed, mlp)
+            linear(layer.down, mlp, proj)
             nxt = w.layers[i + 1].ln1 if i + 1 < len(w.layers) else w.final_norm
             residual_rms_norm_into(hidden, proj, nxt, cfg.eps, hidden, normed)
         return normed
@@ -330,9 +369,10 @@ class DenseDecoder:
             self._decode_body(rows)
         self.graph = graph
         self.graph_rows = rows
-        # kernels: embed, final norm, 8 per layer, head GEMV + argmax unpack, advance (the
-        # argmax key reset is a memset node, not a kernel)
-        self.launches_per_step = 2 + 8 * self.cfg.num_layers + 2 + 1
+        # kernels: embed, final norm, 8 per layer (W8A8: + 4 activation quantisers), head
+        # GEMV + argmax unpack, advance (the argmax key reset is a memset node, not a kernel)
+        per_layer = 8 + (4 if self.mode == "w8a8" else 0)
+        self.launches_per_step = 2 + per_layer * self.cfg.num_layers + 2 + 1
 
     def step(self) -> None:
         """Advance every captured row by one greedy token (graph replay, no host sync)."""

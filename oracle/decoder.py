@@ -11,6 +11,9 @@ Restates the fused-body forward of ``DenseQStoreTarget._forward_impl``
   * residual + RMSNorm and paired SwiGLU with the reference's bf16 boundaries
   * head: the streamed exact head — fp32 hidden @ fp32 dequantised rows, first maximal
     index (:838-896)
+``mode="w8a8"``: every body projection is the W8A8 store matmul of ``enable_w8a8``
+(engine/kernels/w8a8.py:67-125, 145-177) — per-token int8 activations, exact int32
+accumulation, ``(acc * s_x) * s_w`` in fp32, + fp32 bias, then the engine's bf16 boundary.
 Torch on the CPU does the dense fp32 arithmetic, as the reference's CPU path does.
 Weights come as a dict in QStore naming (``embed``, ``L{i}.q`` ... ``lm_head``), each a
 ``.codes`` int8 / ``.scales`` fp32 pair, plus fp32 ``L{i}.ln1``/``ln2``/``norm.final`` and
@@ -43,9 +46,11 @@ class OracleConfig:
 
 
 class OracleDecoder:
-    def __init__(self, cfg: OracleConfig, weights: dict[str, np.ndarray], *, threads: int | None = None) -> None:
+    def __init__(self, cfg: OracleConfig, weights: dict[str, np.ndarray], *, threads: int | None = None,
+                 mode: str = "w8a16") -> None:
         self.cfg = cfg
         self.w = weights
+        self.mode = mode
         if threads:
             torch.set_num_threads(int(threads))
         self.k_cache: list[torch.Tensor] = []
@@ -59,7 +64,17 @@ class OracleDecoder:
         return q.mul_(torch.from_numpy(self.w[name + ".scales"])[:, None])
 
     def _linear(self, name: str, x: torch.Tensor) -> torch.Tensor:
-        """bf16-valued x [T, in] -> bf16-valued [T, out] (the W8A16 contract)."""
+        """bf16-valued x [T, in] -> bf16-valued [T, out] (the W8A16 contract, or W8A8)."""
+        if self.mode == "w8a8":
+            from .w8a8 import int8_gemm, quantize_activations
+
+            qx, sx = quantize_activations(x.numpy())
+            acc = int8_gemm(qx, self.w[name + ".codes"])
+            y = (acc.astype(np.float32) * sx).astype(np.float32) * self.w[name + ".scales"][None, :]
+            bias = self.w.get(name + ".bias")
+            if bias is not None:
+                y = (y + np.asarray(bias, np.float32)[None, :]).astype(np.float32)
+            return _bf16(torch.from_numpy(np.ascontiguousarray(y, np.float32)))
         w = _bf16(self._dequant(name))
         y = _bf16(x @ w.T)
         bias = self.w.get(name + ".bias")

@@ -24,10 +24,10 @@ def _tiny(**kw):
     return DenseConfig(**base)
 
 
-def _oracle(cfg, weights):
+def _oracle(cfg, weights, mode="w8a16"):
     ocfg = OracleConfig(cfg.num_layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab,
                         cfg.rope_theta, cfg.eps)
-    return OracleDecoder(ocfg, weights.to_host())
+    return OracleDecoder(ocfg, weights.to_host(), mode=mode)
 
 
 @pytest.mark.parametrize("kw,prompt_len,steps", [
@@ -81,6 +81,42 @@ def test_graph_replay_matches_eager_and_is_deterministic(cuda):
         gap = abs(float(logits[nxt]) - float(logits[runs[0][-1]]))
         assert gap <= 2e-2, f"graph token {runs[0][-1]} vs eager {nxt}: oracle logit gap {gap:.4g}"
         print(f"graph/eager near tie: tokens {runs[0][-1]} / {nxt}, oracle gap {gap:.4g}")
+
+
+def test_w8a8_batched_decode_matches_oracle(cuda):
+    """W8A8 mode (per-token int8 activations, exact int32 tensor-core accumulation, split-K at
+    decode row counts) over ragged prefills then a captured batched decode; each row's tokens
+    are scored by the W8A8 oracle teacher-forced, differing only at near-ties."""
+    from mrun_b200.dense_engine import DenseDecoder, DenseWeights
+
+    cfg = _tiny(hidden=512, heads=8, kv_heads=2, head_dim=64, ffn=1024, vocab=2000)
+    weights = DenseWeights.synthetic(cfg, cuda, seed=3)
+    rows, steps = 5, 12
+    rng = np.random.default_rng(5)
+    prompts = [torch.from_numpy(rng.integers(0, cfg.vocab, int(n))) for n in rng.integers(3, 60, rows)]
+    dec = DenseDecoder(weights, max_batch=rows, max_seq_len=128, device=cuda, max_prefill_tokens=64, mode="w8a8")
+    firsts = [int(dec.prefill(i, p).item()) for i, p in enumerate(prompts)]
+    lengths = [dec.kv.lengths[i] for i in range(rows)]
+    for i in range(rows):
+        dec.kv.reserve(i, lengths[i] + steps)
+    dec.begin_decode(rows, torch.tensor(firsts), lengths)
+    dec.capture(rows)
+    out = [[f] for f in firsts]
+    for _ in range(steps - 1):
+        dec.step()
+        ids = dec.next_ids[:rows].cpu().tolist()
+        for i in range(rows):
+            out[i].append(int(ids[i]))
+    dec.check_errors()
+    oracle = _oracle(cfg, weights, mode="w8a8")
+    total = 0
+    for i in range(rows):
+        picks, gaps, margins = oracle.teacher_forced(prompts[i].numpy(), out[i])
+        for step, (tok, pick, gap) in enumerate(zip(out[i], picks, gaps)):
+            if tok != pick:
+                total += 1
+                assert gap <= 2e-2, f"row {i} step {step}: gpu {tok} vs oracle {pick}, gap {gap:.4g}"
+    assert total <= max(3, rows * steps // 10)
 
 
 @pytest.mark.slow

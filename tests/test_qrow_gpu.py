@@ -242,6 +242,62 @@ def test_swiglu_gemm_path(m, n, k, cuda):
     assert max_rel_err(y_small, y[:4]) < BF16_TOL
 
 
+def _tc_timeouts() -> int:
+    import ctypes
+
+    from mrun_b200 import _lib
+
+    out = ctypes.c_uint(0)
+    _lib.call("mrb_tc_status", ctypes.addressof(out))
+    return out.value
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (64, 300, 512),      # 128 x 128 tiles, one k tail-free tile row
+    (300, 1001, 80),     # ragged rows / columns (scalar stores), k tail inside a 64-wide stage
+    (1024, 4736, 512),   # 128 x 256 double-buffered tiles
+    (4096, 9472, 64),    # 256 x 256 tiles (two accumulator halves), one k stage
+    (33, 4096, 3584),    # smallest GEMM row count
+])
+def test_tcgen05_w8a16_gemm(m, n, k, cuda):
+    """The tcgen05 W8A16 GEMM (int8 weights converted to bf16 in shared memory, fp32 TMEM
+    accumulators) against the float64 product, plus the bias epilogue; no wait timed out."""
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+
+    gen = torch.Generator(device="cpu").manual_seed(m * 3 + n + k)
+    q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    s = torch.rand(n, generator=gen) * 0.01 + 1e-4
+    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    y = qrow_linear(q.to(cuda), s.to(cuda), x.to(cuda)).float().cpu().numpy()
+    exact = oq.qrow_matmul_exact(x.float().numpy(), q.numpy(), s.numpy())
+    # fp32 accumulation of exact bf16 products, one bf16 rounding at the end
+    assert max_rel_err(y, exact) < 4e-3
+    bias = torch.randn(n, generator=gen)
+    yb = qrow_linear(q.to(cuda), s.to(cuda), x.to(cuda), bias=bias.to(cuda)).float().cpu().numpy()
+    assert max_rel_err(yb, bf16_round(bf16_round(exact) + bf16_round(bias.numpy())[None, :])) < BF16_TOL
+    # deterministic
+    y2 = qrow_linear(q.to(cuda), s.to(cuda), x.to(cuda)).float().cpu().numpy()
+    assert np.array_equal(y, y2)
+    assert _tc_timeouts() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 18944, 512), (100, 700, 256), (1024, 2368, 128)])
+def test_tcgen05_w8a16_swiglu(m, n, k, cuda):
+    """Paired gate/up tiles (gate rows then up rows in one B operand) with the SwiGLU epilogue."""
+    from mrun_b200.dense_qstore_cuda import qrow_swiglu
+
+    gen = torch.Generator(device="cpu").manual_seed(m + 5 * n + k)
+    gq = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    uq = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    gs = torch.rand(n, generator=gen) * 0.004
+    us = torch.rand(n, generator=gen) * 0.004
+    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    y = qrow_swiglu(gq.to(cuda), gs.to(cuda), uq.to(cuda), us.to(cuda), x.to(cuda)).float().cpu().numpy()
+    ref = oq.swiglu_w8a16(x.float().numpy(), gq.numpy(), gs.numpy(), uq.numpy(), us.numpy())
+    assert max_rel_err(y, ref) < BF16_TOL
+    assert _tc_timeouts() == 0
+
+
 def _abi_matmul(x, q, s, workspace):
     """mrb_qrow_matmul through the C ABI with an explicit workspace (None: whole tiles)."""
     from mrun_b200 import _lib

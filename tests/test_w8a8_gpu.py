@@ -2,14 +2,16 @@
 the reference (no protected columns) and within 1e-4 (fp32) with protected columns."""
 from __future__ import annotations
 
+import ctypes
 import hashlib
 
 import numpy as np
 import pytest
 import torch
 
+from oracle import qrow as oq
 from oracle import w8a8 as ow8
-from oracle.numerics import max_rel_err
+from oracle.numerics import bf16_round, max_rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -114,3 +116,53 @@ def test_tensor_core_waits_never_timed_out(cuda):
     count = ctypes.c_uint(99)
     _lib.call("mrb_tc_status", ctypes.addressof(count))
     assert count.value == 0
+
+
+@pytest.mark.parametrize("m,n,k,paired,with_bias", [
+    (64, 3584, 3584, False, False),    # o projection at 64 decode rows: split over k
+    (64, 4608, 3584, False, True),     # qkv with bias, split
+    (64, 3584, 18944, False, False),   # down projection, split
+    (64, 18944, 3584, True, False),    # paired gate/up, 296 tiles: no split
+    (64, 1000, 1024, True, False),     # paired, split, ragged output columns
+    (300, 1000, 512, False, True),     # several row tiles
+    (1, 256, 128, False, False),
+])
+def test_w8a8_linear_bf16_exact_and_split_invariant(m, n, k, paired, with_bias, cuda):
+    """bf16 W8A8 projection: int32 accumulation exact, so the split-K result equals the
+    unsplit one bit for bit and the plain epilogue equals the oracle's fp32 rescale rounded
+    once to bf16."""
+    from mrun_b200.w8a8 import w8a8_linear_bf16, w8a8_workspace_bytes
+
+    gen = torch.Generator(device="cpu").manual_seed(m + n + k)
+    q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    s = torch.rand(n, generator=gen) * 1e-3 + 1e-5
+    qu = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    su = torch.rand(n, generator=gen) * 1e-3 + 1e-5
+    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    bias = torch.randn(n, generator=gen) * 0.1 if with_bias else None
+    dev = lambda t: None if t is None else t.to(cuda)  # noqa: E731
+    up = (dev(qu), dev(su)) if paired else None
+    nbytes = w8a8_workspace_bytes(cuda, m, n, k, paired=paired)
+    ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=cuda)
+    y_split = w8a8_linear_bf16(dev(q), dev(s), dev(x), bias=dev(bias), up=up, workspace=ws)
+    y_split2 = w8a8_linear_bf16(dev(q), dev(s), dev(x), bias=dev(bias), up=up, workspace=ws)  # reused workspace
+    y_whole = w8a8_linear_bf16(dev(q), dev(s), dev(x), bias=dev(bias), up=up)
+    assert torch.equal(y_split, y_whole) and torch.equal(y_split2, y_whole)
+
+    qx, sx = ow8.quantize_activations(x.float().numpy())
+    acc = ow8.int8_gemm(qx, q.numpy())
+    g = (acc.astype(np.float32) * sx).astype(np.float32) * s.numpy()[None, :]
+    if paired:
+        u = (ow8.int8_gemm(qx, qu.numpy()).astype(np.float32) * sx).astype(np.float32) * su.numpy()[None, :]
+        gv, uv = bf16_round(g), bf16_round(u)
+        ref = bf16_round(bf16_round(gv * oq.sigmoid_f32(gv)) * uv)
+        assert max_rel_err(y_whole.float().cpu().numpy(), ref) < 1e-2
+    else:
+        if bias is not None:
+            g = (g + bias.numpy()[None, :]).astype(np.float32)
+        np.testing.assert_array_equal(y_whole.float().cpu().numpy(), bf16_round(g))
+    out = ctypes.c_uint(0)
+    from mrun_b200 import _lib
+
+    _lib.call("mrb_tc_status", ctypes.addressof(out))
+    assert out.value == 0
