@@ -312,10 +312,18 @@ TC_CASES = {
     # name: (m, n, k) of the tcgen05 int8 GEMM (W8A8 prefill at the config-2 shapes)
     "int8-gemm-gateup": (512, 18944, 3584),
     "int8-gemm-down": (512, 3584, 18944),
+    # the same GEMM at decode row counts (int32 accumulators out, no split)
+    "int8-gemm-wide64": (64, 37888, 3584),
+    "int8-gemm-wide128": (128, 37888, 3584),
     # the tcgen05 W8A16 GEMM (bf16 activations, int8 weights): paired gate/up with the SwiGLU
     # epilogue (n = output columns; 2n weight rows) and the down projection
     "w8a16-gemm-gateup": (512, 18944, 3584),
     "w8a16-gemm-down": (512, 3584, 18944),
+    # W8A8 projections of the config-3 decode step (64 rows: split-K for the narrow ones,
+    # paired gate/up), through mrb_w8a8_linear_bf16 with its workspace
+    "w8a8-linear-o64": (64, 3584, 3584),
+    "w8a8-linear-down64": (64, 3584, 18944),
+    "w8a8-linear-gateup64": (64, 18944, 3584),
 }
 
 
@@ -333,10 +341,24 @@ def run_tc_case(args) -> None:
     gen = torch.Generator(device=device).manual_seed(0)
     stream = torch.cuda.current_stream(device)
     w8a16 = args.case.startswith("w8a16")
-    paired = args.case == "w8a16-gemm-gateup"
+    w8a8_linear = args.case.startswith("w8a8-linear")
+    paired = args.case in ("w8a16-gemm-gateup", "w8a8-linear-gateup64")
     wrows = 2 * n if paired else n  # weight rows the GEMM multiplies
     qws = [torch.randint(-127, 128, (wrows, k), dtype=torch.int8, device=device, generator=gen) for _ in range(2)]
-    if w8a16:
+    if w8a8_linear:
+        from mrun_b200.w8a8 import w8a8_linear_bf16
+
+        x = torch.randn(m, k, device=device, generator=gen).to(torch.bfloat16)
+        scales = torch.rand(wrows, device=device, generator=gen) * 1e-3
+        y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+        qx = torch.empty(m, k, dtype=torch.int8, device=device)
+        sx = torch.empty(m, dtype=torch.float32, device=device)
+
+        def launch(i):
+            w = qws[i % 2]
+            up = (w[n:], scales[n:]) if paired else None
+            w8a8_linear_bf16(w[:n], scales[:n], x, up=up, out=y, qx_ws=qx, scale_ws=sx)
+    elif w8a16:
         x = (torch.randn(m, k, device=device, generator=gen)).to(torch.bfloat16)
         scales = torch.rand(wrows, device=device, generator=gen) * 1e-3
         y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
@@ -370,6 +392,7 @@ def run_tc_case(args) -> None:
     torch.cuda.synchronize(device)
     avg_s = e0.elapsed_time(e1) / 1000.0 / args.steps
     print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "tops": 2 * m * wrows * k / avg_s / 1e12,
+                      "weight_gbs": wrows * k / avg_s / 1e9,
                       "kind": "bf16 x bf16 (int8 weights)" if w8a16 else "int8 x int8",
                       "launches": args.steps}), flush=True)
 
@@ -552,6 +575,97 @@ def run_stream_case(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+BATCH_SEQS = 64
+BATCH_NEW_TOKENS = 128
+
+
+def run_batch_case(args) -> None:
+    """Config 3: the Qwen2.5-7B-shape decoder in W8A8 mode (per-token int8 activations, exact
+    int32 tensor-core accumulation), 64 sequences with prompt lengths drawn from U[128, 2048]
+    (numpy seed 0, per rank), each prefilled on its own (tensor-core GEMMs at M = prompt
+    length) and then decoded together, 64 rows per CUDA-graph step, for up to 128 new tokens
+    each. Reports decode tokens/s (whole job), prefill tokens/s and the decode step's
+    algorithmic HBM bytes (weights once + every row's KV) per second. N GPUs: replicas over
+    disjoint sequences (the dense path does not shard). Prints one JSON line on rank 0; not
+    the headline metric."""
+    import numpy as np
+    import torch
+
+    from mrun_b200.dense_engine import DenseConfig, DenseDecoder, DenseWeights
+
+    world, rank, local = _dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    cfg = DenseConfig.qwen25_7b()
+    weights = DenseWeights.synthetic(cfg, device, seed=0)
+    rng = np.random.default_rng(rank)
+    lengths = [int(v) for v in rng.integers(128, 2049, BATCH_SEQS)]
+    prompts = [torch.from_numpy(rng.integers(0, cfg.vocab, n)) for n in lengths]
+    dec = DenseDecoder(weights, max_batch=BATCH_SEQS, max_seq_len=2048 + BATCH_NEW_TOKENS + 16, device=device,
+                       max_prefill_tokens=2048, mode="w8a8")
+    stream = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    dec.prefill(0, prompts[0][:128])  # warm-up of the prefill kernels
+    dec.kv.release(0)
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    firsts = [dec.prefill(i, p) for i, p in enumerate(prompts)]
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    prefill_s = _max_over_ranks(e0.elapsed_time(e1) / 1000.0, world)
+    for i, n in enumerate(lengths):
+        dec.kv.reserve(i, n + BATCH_NEW_TOKENS)
+    dec.begin_decode(BATCH_SEQS, torch.stack(firsts), lengths)
+    dec.capture(BATCH_SEQS)
+    steps = max(1, min(args.steps, BATCH_NEW_TOKENS - 1 - args.warmup))
+    for _ in range(args.warmup):
+        dec.step()
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        torch.cuda.cudart().cudaProfilerStart()  # launch lists cover the timed steps only
+        e0.record(stream)
+        for _ in range(steps):
+            dec.step()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        torch.cuda.cudart().cudaProfilerStop()
+    _barrier(world)
+    step_s = _max_over_ranks(e0.elapsed_time(e1) / 1000.0 / steps, world)
+    dec.check_errors()
+    if rank == 0:
+        wb = cfg.weight_bytes()
+        weight_bytes = float(sum(wb.values()))
+        kv_per_token = 2 * cfg.num_layers * cfg.kv_heads * cfg.head_dim * 2
+        mean_ctx = float(np.mean(lengths)) + args.warmup + steps / 2.0
+        kv_bytes = BATCH_SEQS * mean_ctx * kv_per_token
+        peaks = _peaks()
+        line = {
+            "case": "w8a8-batch", "metric": "W8A8 continuous-batching decode tokens/s (config 3)",
+            "unit": "tokens/s", "value": BATCH_SEQS * world / step_s, "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1000.0, "scaling": "weak",
+            "config": {"workload": "config3: Qwen2.5-7B-shape dense int8-QStore decoder, W8A8, 64 sequences, "
+                                   "prompts U[128,2048], 128 new tokens each",
+                       "sequences_per_gpu": BATCH_SEQS, "parallelism": f"replicas{world}" if world > 1 else "single GPU",
+                       "graph": True, "mean_prompt": float(np.mean(lengths))},
+            "prefill_tokens_per_s": sum(lengths) * world / prefill_s,
+            "prefill_s": prefill_s,
+            "decode_bytes_per_step": weight_bytes + kv_bytes,
+            "decode_gbs": (weight_bytes + kv_bytes) / step_s / 1e9,
+            "decode_frac_of_hbm": (weight_bytes + kv_bytes) / step_s / 1e9 / peaks["hbm_gbs"],
+            "peak_source": peaks["source"],
+            "gpu_launches_per_step": dec.launches_per_step,
+            "data": "synthetic", "dtype": "int8 x int8 -> int32 (bf16 activations between layers)",
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dec.graph = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -688,7 +802,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", *GEMV_CASES, *TC_CASES],
+    ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
+                                       *TC_CASES],
                     default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
@@ -702,6 +817,8 @@ def main() -> None:
         run_moe_case(args)
     elif args.case == "stream-decode":
         run_stream_case(args)
+    elif args.case == "w8a8-batch":
+        run_batch_case(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

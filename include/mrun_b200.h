@@ -163,17 +163,15 @@ int mrb_w8a8_matmul(const void *x, int x_dtype, int64_t m, int64_t k, const int8
  * tensor cores, then y = bf16((float(acc) * act_scale) * w_scale + bias) (bias fp32 [n] or
  * NULL). With up_codes/up_scales (paired gate/up pages, each [n, k]) y is the SwiGLU
  * bf16(bf16(silu(bf16 g)) * bf16 u) of the two rescaled projections and bias must be NULL.
- * workspace: zero-initialised device memory of mrb_w8a8_workspace(m, n, k, paired) bytes
- * for split-K over skinny row blocks (its arrival counters return to zero, so it is reused
- * without clearing; NULL, 0: no split). The int32 accumulators are exact, so y does not
- * depend on the split.
+ * Skinny row blocks (decode batches) split k over the CTAs of a thread-block cluster and
+ * reduce the exact int32 partials through distributed shared memory, so y does not depend
+ * on the split and no workspace is needed.
  * Replaces `store.matmul` under `enable_w8a8` (engine/kernels/w8a8.py:145-177) for the
  * dense engine's projections and its paired gate/up (engine/dense_qstore_cuda.py:661-687). */
 int mrb_w8a8_linear_bf16(const void *x_bf16, int64_t m, int64_t k, const int8_t *codes,
                          const float *scales, const int8_t *up_codes, const float *up_scales,
                          const float *bias, int64_t n, void *y_bf16, int8_t *qx_ws, float *scale_ws,
-                         void *workspace, size_t workspace_bytes, void *stream);
-size_t mrb_w8a8_workspace(int64_t m, int64_t n, int64_t k, int paired);
+                         void *stream);
 
 /* ---------------------------------------------------------------- (b) routed MoE */
 

@@ -61,12 +61,10 @@ SIGNATURES: dict[str, list] = {
                                    _P, _P, c_float, _I64, _P, _P],
     "mrb_decode_advance": [_P, _P, _P, _P, _I64, _P],
     "mrb_copy_pages": [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P],
-    "mrb_w8a8_linear_bf16": [_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, c_size_t, _P],
-    "mrb_w8a8_workspace": [_I64, _I64, _I64, c_int],
+    "mrb_w8a8_linear_bf16": [_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P],
 }
 _RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t,
-             "mrb_paged_attention_static_capacity": c_size_t, "mrb_qrow_workspace": c_size_t,
-             "mrb_w8a8_workspace": c_size_t}
+             "mrb_paged_attention_static_capacity": c_size_t, "mrb_qrow_workspace": c_size_t}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -23,10 +23,12 @@
 // pages (a B tile of BN/2 gate rows then the same BN/2 up rows), the SwiGLU
 // bf16(bf16(silu(bf16 g))·bf16 u) of the two rescaled accumulators.
 // Split-K (skinny activation blocks, e.g. 64-row W8A8 decode, whose output tiles fill few
-// SMs): a work item is (tile, k range); each warp stores its 32 rows' int32 partial
-// accumulators to a workspace and the last warp to arrive for those rows (a per-(tile,
-// quarter) counter) sums the partials and writes the outputs. int32 addition is exact, so
-// the result does not depend on the split or the arrival order.
+// SMs; bf16 outputs): the k ranges of one output tile run as the CTAs of one thread-block
+// cluster. Each parks its int32 partial tile in its own shared memory (the stage ring is idle
+// by then); after a cluster barrier every CTA sums one column slice of the tile over all the
+// cluster's partials through distributed shared memory and writes those outputs; a second
+// barrier keeps the partials alive until every peer has read them. int32 addition is exact,
+// so the result does not depend on the split.
 // Every wait is bounded: on a timeout the CTA records the failure, stops, and still frees
 // its TMEM. No load uses cluster multicast.
 #include "qrow_common.cuh"
@@ -53,8 +55,12 @@ struct TcTile {
   static constexpr int STAGES = (int)(TC_RING_BUDGET / STAGE_BYTES) < 6 ? (int)(TC_RING_BUDGET / STAGE_BYTES) : 6;
   static constexpr int NBUF = HALVES == 1 ? 2 : 1;  // accumulator sets (double-buffered when they fit)
   static constexpr unsigned TMEM_COLS = HALVES * BN * NBUF <= 256 ? 256u : 512u;
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  static constexpr size_t SCALE_BYTES = 4 * 2 * BN * sizeof(float);  // per epilogue warp: [BN] + [BN]
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256 + SCALE_BYTES;
+  static constexpr int PSTRIDE = BN + 4;  // int32 row stride of a parked partial (bank spread)
+  static_assert((size_t)TC_HM * PSTRIDE * 4 <= (size_t)STAGES * STAGE_BYTES, "partial tile exceeds the ring");
 };
+constexpr int TC_MAX_CLUSTER = 8;
 
 struct TcGemmArgs {
   CUtensorMap map_x;  // qx [m, k] int8, box [BM rows, 128 B], 128-byte swizzle
@@ -72,9 +78,7 @@ struct TcGemmArgs {
   __nv_bfloat16* y_bf16;   // [m, n] or null
   int32_t* acc_out;        // [m, n] or null (not paired)
   bool vec_store;          // 16-byte aligned outputs with n % 4 == 0 (n % 8 for bf16)
-  int splits, kb_per;      // split-K: k blocks [split * kb_per, +kb_per) per work item
-  unsigned* counters;      // [tiles * 4] arrivals per (tile, TMEM lane quarter); zero between launches
-  int32_t* parts;          // [splits, m, tiles_n * BN] int32 partial accumulators
+  int splits, kb_per;      // split-K: k blocks [split * kb_per, +kb_per); splits > 1 = cluster of splits CTAs
 };
 
 // Timed-out waits of the tensor-core GEMM since the last status read (0 in normal operation).
@@ -93,6 +97,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
   uint64_t* acc_empty = acc_full + NBUF;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + NBUF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* scale_smem = reinterpret_cast<float*>(smem + STAGES * Tile::STAGE_BYTES + 256);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -212,10 +217,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
     unsigned acc_phase = 0;
     const bool vec = a.vec_store;
     const int out_cols = a.paired ? BN / 2 : BN;
-    const int64_t pstride = (int64_t)a.tiles_n * BN;  // partial-accumulator row stride
-    // 32 output columns [col0, col0 + 32) of one row from int32 accumulators v (gate or
-    // plain) and u (up, paired)
-    auto emit = [&](int64_t row, float as, int64_t col0, const uint32_t (&v)[32], const uint32_t (&u)[32]) {
+    // this warp's copy of the tile's column scales: [BN] weight scales, [BN] up scales (paired)
+    // or bias; loaded in one batch per tile so the epilogue never waits on them one by one
+    float* sc = scale_smem + q * 2 * BN;
+    auto stage_scales = [&](int tn) {
+      float g[BN / 32], u[BN / 32];
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) {
+        const int c = lane + 32 * i;
+        const int64_t col = (int64_t)tn * out_cols + c;
+        const bool ok = c < out_cols && col < a.n;
+        g[i] = (ok && a.sw) ? __ldg(a.sw + col) : 0.f;
+        u[i] = !ok ? 0.f : a.paired ? __ldg(a.sw_up + col) : (a.bias ? __ldg(a.bias + col) : 0.f);
+      }
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) {
+        sc[lane + 32 * i] = g[i];
+        sc[BN + lane + 32 * i] = u[i];
+      }
+      __syncwarp();
+    };
+    // 32 output columns from int32 accumulators v (gate or plain) and u (up, paired); c0 is
+    // the tile-local output column, col0 the global one
+    auto emit = [&](int64_t row, float as, int c0, int64_t col0, const uint32_t (&v)[32], const uint32_t (&u)[32]) {
       const int64_t o0 = row * a.n + col0;
       const bool full_run = vec && col0 + 32 <= a.n;
       if (a.acc_out) {
@@ -233,10 +258,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
         float out[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int64_t col = col0 + j;
-          const float wsc = col < a.n ? a.sw[col] : 0.f;
-          float r = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), wsc);
-          if (a.side && col < a.n) r = __fadd_rn(a.side[o0 + j], r);
+          float r = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), sc[c0 + j]);
+          if (a.side && col0 + j < a.n) r = __fadd_rn(a.side[o0 + j], r);
           out[j] = r;
         }
         if (full_run) {
@@ -251,14 +274,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
         __align__(16) __nv_bfloat16 out[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int64_t col = col0 + j < a.n ? col0 + j : a.n - 1;
-          const float g = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), a.sw[col]);
+          const float g = __fmul_rn(__fmul_rn(__int2float_rn((int)v[j]), as), sc[c0 + j]);
           if (a.paired) {
-            const float up = __fmul_rn(__fmul_rn(__int2float_rn((int)u[j]), as), a.sw_up[col]);
+            const float up = __fmul_rn(__fmul_rn(__int2float_rn((int)u[j]), as), sc[BN + c0 + j]);
             const float gv = round_bf16(g), uv = round_bf16(up);
             out[j] = __float2bfloat16_rn(round_bf16(silu_f32(gv)) * uv);
           } else {
-            out[j] = __float2bfloat16_rn(a.bias ? __fadd_rn(g, a.bias[col]) : g);
+            out[j] = __float2bfloat16_rn(a.bias ? __fadd_rn(g, sc[BN + c0 + j]) : g);
           }
         }
         __nv_bfloat16* dst = a.y_bf16 + o0;
@@ -272,7 +294,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
       }
     };
     for (int it = blockIdx.x; it < items; it += gridDim.x) {
-      const int t = it / a.splits, split = it % a.splits;
+      const int t = it / a.splits;
       // warp-uniform: tcgen05.ld below is a whole-warp instruction
       bool ok = !*abort_flag && mbar_wait_bounded(acc_full + buf, acc_phase);
       ok = __all_sync(0xffffffffu, ok);
@@ -283,6 +305,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
       tc_fence_after();
       const int tm = t % a.tiles_m, tn = t / a.tiles_m;
       if (a.splits == 1) {
+        stage_scales(tn);
         for (int h = 0; h < HALVES; ++h) {
           if ((int64_t)tm * BM + h * TC_HM >= a.m) break;  // uniform: an empty half
           const int64_t row = (int64_t)tm * BM + h * TC_HM + q * 32 + lane;
@@ -296,66 +319,88 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_int8_gemm_kernel(const __gri
             if (a.paired) tmem_ld_32cols(tbase + (uint32_t)(BN / 2 + c0), u);
             const int64_t col0 = (int64_t)tn * out_cols + c0;
             if (!row_ok || col0 >= a.n) continue;
-            emit(row, as, col0, v, u);
+            emit(row, as, c0, col0, v, u);
           }
         }
-        tc_fence_before();
-        mbar_arrive(acc_empty + buf);  // accumulators drained
       } else {
-        // split-K (single-half tiles): store this k range's partials, release TMEM, and let
-        // the last warp to arrive for these 32 rows sum every split's partials
-        const int64_t row = (int64_t)tm * BM + q * 32 + lane;
-        const bool row_ok = row < a.m;
+        // cluster split-K (one work item per CTA, single-half tiles): park this k range's
+        // int32 partial in shared memory for the reduction after the role loops
+        int32_t* part = reinterpret_cast<int32_t*>(smem) + (q * 32 + lane) * Tile::PSTRIDE;
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + acc_col(buf, 0);
-        int32_t* mine = a.parts + ((int64_t)split * a.m + (row_ok ? row : 0)) * pstride + (int64_t)tn * BN;
         for (int c0 = 0; c0 < BN; c0 += 32) {
           uint32_t v[32];
           __syncwarp();
           tmem_ld_32cols(tbase + (uint32_t)c0, v);
-          if (row_ok) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<int4*>(mine + c0 + j) = make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(acc_empty + buf);
-        __threadfence();
-        __syncwarp();
-        unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(a.counters + (int64_t)t * 4 + q, 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == (unsigned)a.splits - 1u) {
-          __threadfence();
-          const float as = (row_ok && a.act_scale) ? a.act_scale[row] : 0.f;
-          for (int c0 = 0; c0 < out_cols; c0 += 32) {
-            const int64_t col0 = (int64_t)tn * out_cols + c0;
-            if (!row_ok || col0 >= a.n) continue;
-            uint32_t v[32], u[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = u[j] = 0u;
-            for (int sp = 0; sp < a.splits; ++sp) {
-              const int32_t* src = a.parts + ((int64_t)sp * a.m + row) * pstride + (int64_t)tn * BN + c0;
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const int4 pv = __ldcg(reinterpret_cast<const int4*>(src + j));
-                v[j] += (uint32_t)pv.x; v[j + 1] += (uint32_t)pv.y; v[j + 2] += (uint32_t)pv.z; v[j + 3] += (uint32_t)pv.w;
-                if (a.paired) {
-                  const int4 pu = __ldcg(reinterpret_cast<const int4*>(src + BN / 2 + j));
-                  u[j] += (uint32_t)pu.x; u[j + 1] += (uint32_t)pu.y; u[j + 2] += (uint32_t)pu.z; u[j + 3] += (uint32_t)pu.w;
-                }
-              }
-            }
-            emit(row, as, col0, v, u);
-          }
-          if (lane == 0) a.counters[(int64_t)t * 4 + q] = 0u;  // ready for the next launch
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<int4*>(part + c0 + j) = make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
         }
       }
+      tc_fence_before();
+      mbar_arrive(acc_empty + buf);  // accumulators drained
       if (++buf == NBUF) {
         buf = 0;
         acc_phase ^= 1u;
       }
     }
+  }
+
+  if (a.splits > 1) {
+    // ---------------- cluster split-K reduction (every thread takes part in both barriers)
+    __syncwarp();
+    cluster_sync_all();  // every CTA of the cluster has parked its partial tile
+    if (warp >= 2 && a.act_scale && a.y_bf16) {
+      const unsigned nsplit = (unsigned)a.splits, rank = cluster_ctarank();
+      const int t = blockIdx.x / a.splits;
+      const int tm = t % a.tiles_m, tn = t / a.tiles_m;
+      const int out_cols = a.paired ? BN / 2 : BN;
+      const int groups = out_cols / 4;  // 4-column output groups; this CTA reduces [g0, g1)
+      const int g0 = (int)(rank * groups / nsplit), g1 = (int)((rank + 1) * groups / nsplit), ng = g1 - g0;
+      const int64_t rows_left = a.m - (int64_t)tm * BM;
+      const int rows = rows_left < BM ? (int)rows_left : BM;
+      const uint32_t base = smem_u32(smem);
+      for (int unit = tid - 64; unit < rows * ng; unit += TC_EPI_THREADS) {
+        const int r = unit / ng, c = (g0 + unit % ng) * 4;  // tile row, tile-local output column
+        int4 sg = make_int4(0, 0, 0, 0), su = make_int4(0, 0, 0, 0);
+#pragma unroll
+        for (unsigned p = 0; p < (unsigned)TC_MAX_CLUSTER; ++p) {
+          if (p < nsplit) {
+            const int4 g = ld_shared_cluster_v4(mapa_shared(base + (uint32_t)(r * Tile::PSTRIDE + c) * 4u, p));
+            sg.x += g.x; sg.y += g.y; sg.z += g.z; sg.w += g.w;
+            if (a.paired) {
+              const int4 w =
+                  ld_shared_cluster_v4(mapa_shared(base + (uint32_t)(r * Tile::PSTRIDE + BN / 2 + c) * 4u, p));
+              su.x += w.x; su.y += w.y; su.z += w.z; su.w += w.w;
+            }
+          }
+        }
+        const int64_t row = (int64_t)tm * BM + r, col0 = (int64_t)tn * out_cols + c;
+        if (col0 >= a.n) continue;
+        const float as = a.act_scale[row];
+        const int gv4[4] = {sg.x, sg.y, sg.z, sg.w}, uv4[4] = {su.x, su.y, su.z, su.w};
+        __align__(8) __nv_bfloat16 out[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t col = col0 + j < a.n ? col0 + j : a.n - 1;
+          const float g = __fmul_rn(__fmul_rn(__int2float_rn(gv4[j]), as), __ldg(a.sw + col));
+          if (a.paired) {
+            const float up = __fmul_rn(__fmul_rn(__int2float_rn(uv4[j]), as), __ldg(a.sw_up + col));
+            const float gr = round_bf16(g), ur = round_bf16(up);
+            out[j] = __float2bfloat16_rn(round_bf16(silu_f32(gr)) * ur);
+          } else {
+            out[j] = __float2bfloat16_rn(a.bias ? __fadd_rn(g, __ldg(a.bias + col)) : g);
+          }
+        }
+        __nv_bfloat16* dst = a.y_bf16 + row * a.n + col0;
+        if (a.vec_store && col0 + 4 <= a.n) {
+          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(out);
+        } else {
+          for (int j = 0; j < 4 && col0 + j < a.n; ++j) dst[j] = out[j];
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // every peer has read this CTA's partial
   }
 
   tc_fence_before();
@@ -388,43 +433,85 @@ static int tc_launch(TcGemmArgs& a, const int8_t* qx, const int8_t* qw, const in
   a.tiles_n = (int)((a.n + wrows - 1) / wrows);
   const int64_t items = (int64_t)a.tiles_m * a.tiles_n * a.splits;
   if (items > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "tc int8 gemm: too many tiles");
-  const int grid = (int)std::min<int64_t>(items, num_sms());
-  cudaError_t e = launch_kernel(kern, dim3(grid), dim3(TC_THREADS), Tile::SMEM, s, true, a);
+  cudaError_t e;
+  if (a.splits > 1) {
+    // one work item per CTA, the splits of a tile as one cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)items);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = Tile::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)a.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a);
+  } else {
+    const int grid = (int)std::min<int64_t>(items, num_sms());
+    e = launch_kernel(kern, dim3(grid), dim3(TC_THREADS), Tile::SMEM, s, true, a);
+  }
   if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc int8 gemm: launch: %s", cudaGetErrorString(e));
   return launch_status("tc int8 gemm");
 }
 
-// Split-K plan for a problem whose 128 x 128 output tiles leave most SMs idle: about one
-// work item per SM with at least 4 k blocks each. 1 = no split.
-static int tc_split_plan(int64_t m, int64_t n, int64_t k, bool paired, int64_t* tiles_out) {
+// Clusters of `size` 128 x 128-tile CTAs that can be resident at once (0 if none).
+static int tc_cluster_capacity(int size) {
+  static int cached[TC_MAX_CLUSTER + 1] = {};
+  static bool done[TC_MAX_CLUSTER + 1] = {};
+  if (size < 2 || size > TC_MAX_CLUSTER) return 0;
+  if (!done[size]) {
+    using Tile = TcTile<1, 128>;
+    auto kern = tc_int8_gemm_kernel<1, 128>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile::SMEM);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(size * 64));
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = Tile::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    cached[size] = n;
+    done[size] = true;
+  }
+  return cached[size];
+}
+
+// Split-K plan for a problem whose 128 x 128 output tiles leave most SMs idle: the largest
+// cluster size (k ranges per tile, at least 4 k blocks each) whose clusters all fit on the
+// GPU at once. 1 = no split.
+static int tc_split_plan(int64_t m, int64_t n, int64_t k, bool paired) {
   const int64_t out_cols = paired ? 64 : 128;
   const int64_t tiles = ((m + 127) / 128) * ((n + out_cols - 1) / out_cols);
   const int64_t kblocks = (k + TC_BK - 1) / TC_BK;
-  *tiles_out = tiles;
-  const int64_t sms = num_sms();
-  if (2 * tiles > sms || kblocks < 8) return 1;
-  const int64_t by_sm = (sms + tiles - 1) / tiles;
-  return (int)std::max<int64_t>(1, std::min<int64_t>(by_sm, kblocks / 4));
-}
-
-size_t tc_int8_workspace_bytes(int64_t m, int64_t n, int64_t k, bool paired) {
-  int64_t tiles = 0;
-  const int splits = tc_split_plan(m, n, k, paired, &tiles);
-  if (splits <= 1) return 0;
-  const int64_t tiles_n = (n + (paired ? 64 : 128) - 1) / (paired ? 64 : 128);
-  const size_t counters = (((size_t)tiles * 4 * sizeof(unsigned)) + 255) & ~size_t(255);
-  return counters + (size_t)splits * (size_t)m * (size_t)tiles_n * 128 * sizeof(int32_t);
+  if (2 * tiles > num_sms() || kblocks < 8) return 1;
+  int best = 1;
+  for (int size = 2; size <= TC_MAX_CLUSTER && 4 * size <= kblocks; ++size)
+    if (tiles <= tc_cluster_capacity(size)) best = size;
+  return best;
 }
 
 // Launch the tensor-core W8A8 GEMM (see the file comment); arguments are checked by callers.
 // Tile shape by SM fill: 256-row tiles when they give every SM at least two, else 128 x 256
-// double-buffered tiles when those fill the SMs, else 128 x 128 — split over k when those
-// leave most SMs idle and the caller gave a workspace of tc_int8_workspace_bytes().
+// double-buffered tiles when those fill the SMs, else 128 x 128 — split over k in clusters
+// when those leave most SMs idle and the only output is y_bf16.
 // qw_up non-null: paired gate/up pages (n outputs, SwiGLU epilogue, y_bf16 only).
 int tc_int8_gemm_ex(const int8_t* qx, const int8_t* qw, const int8_t* qw_up, int64_t m, int64_t n, int64_t k,
                     const float* act_scale, const float* sw, const float* sw_up, const float* side,
-                    const float* bias, float* y, __nv_bfloat16* y_bf16, int32_t* acc_out, void* workspace,
-                    size_t workspace_bytes, cudaStream_t s) {
+                    const float* bias, float* y, __nv_bfloat16* y_bf16, int32_t* acc_out, cudaStream_t s) {
   TcGemmArgs a{};
   a.m = m;
   a.n = n;
@@ -443,15 +530,12 @@ int tc_int8_gemm_ex(const int8_t* qx, const int8_t* qw, const int8_t* qw_up, int
                 (!y_bf16 || aligned(y_bf16, 16));
   a.splits = 1;
   a.kb_per = a.kblocks;
-  int64_t tiles = 0;
-  const int splits = tc_split_plan(m, n, k, a.paired, &tiles);
-  if (splits > 1 && workspace && workspace_bytes >= tc_int8_workspace_bytes(m, n, k, a.paired)) {
+  const int splits = (y_bf16 && act_scale && !y && !acc_out) ? tc_split_plan(m, n, k, a.paired) : 1;
+  if (splits > 1) {
     a.kb_per = (a.kblocks + splits - 1) / splits;
-    a.splits = (a.kblocks + a.kb_per - 1) / a.kb_per;  // no empty split
-    a.counters = reinterpret_cast<unsigned*>(workspace);
-    a.parts = reinterpret_cast<int32_t*>(reinterpret_cast<unsigned char*>(workspace) +
-                                         ((((size_t)tiles * 4 * sizeof(unsigned)) + 255) & ~size_t(255)));
-    return tc_launch<1, 128>(a, qx, qw, qw_up, s);
+    a.splits = (a.kblocks + a.kb_per - 1) / a.kb_per;  // no empty k range
+    if (a.splits > 1) return tc_launch<1, 128>(a, qx, qw, qw_up, s);
+    a.kb_per = a.kblocks;
   }
   const int64_t sms = num_sms();
   const int64_t wr = a.paired ? 2 : 1;  // weight rows per output column
@@ -463,8 +547,7 @@ int tc_int8_gemm_ex(const int8_t* qx, const int8_t* qw, const int8_t* qw_up, int
 
 int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64_t k, const float* act_scale,
                  const float* sw, const float* side, float* y, int32_t* acc_out, cudaStream_t s) {
-  return tc_int8_gemm_ex(qx, qw, nullptr, m, n, k, act_scale, sw, nullptr, side, nullptr, y, nullptr, acc_out,
-                         nullptr, 0, s);
+  return tc_int8_gemm_ex(qx, qw, nullptr, m, n, k, act_scale, sw, nullptr, side, nullptr, y, nullptr, acc_out, s);
 }
 
 // Read and reset the count of timed-out waits (synchronises the device).

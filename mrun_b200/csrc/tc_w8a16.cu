@@ -15,7 +15,7 @@
 //    one elected thread issues the activation TMA ([BM x 64 bf16], 128-byte swizzle), and
 //    all of them turn the raw int8 box into bf16 rows in the 128-byte-swizzled K-major
 //    layout the MMA descriptor reads (chunk c of row r at c ^ (r & 7)), fence the writes to
-//    the async proxy and arrive on the stage barrier;
+//    the async proxy and arrive on the stage barrier (one arrival per warp);
 //  * warp 1: TMEM owner; one thread issues tcgen05.mma (M=128 per accumulator half, N=BN,
 //    K=16) and commits stages and finished tiles;
 //  * warps 2-5: epilogue, TMEM -> registers -> bf16 rows.
@@ -35,6 +35,7 @@ constexpr int TW_BKE = 64;            // k elements per stage: one 128-byte bf16
 constexpr int TW_UK_BYTES = 32;       // k bytes per MMA (16 bf16)
 constexpr int TW_CVT_WARP0 = 6;       // first converter warp
 constexpr int TW_CVT_THREADS = 256;   // 8 converter warps
+constexpr int TW_CVT_WARPS = TW_CVT_THREADS / 32;
 constexpr int TW_EPI_THREADS = 128;
 constexpr int TW_THREADS = TW_CVT_WARP0 * 32 + TW_CVT_THREADS;
 constexpr size_t TW_SMEM_LIMIT = 227 * 1024;
@@ -94,12 +95,12 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full + s, 1 + TW_CVT_THREADS);  // activation TMA (expect_tx) + every converter
+      mbar_init(full + s, 1 + TW_CVT_WARPS);  // activation TMA (expect_tx) + one per converter warp
       mbar_init(empty + s, 1);
     }
     for (int s = 0; s < RAW_STAGES; ++s) {
       mbar_init(raw_full + s, 1);
-      mbar_init(raw_empty + s, TW_CVT_THREADS);
+      mbar_init(raw_empty + s, TW_CVT_WARPS);
     }
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(acc_full + b, 1);
@@ -271,15 +272,16 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
     for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
       const int tm = t % a.tiles_m;
       for (int kb = 0; kb < a.kblocks; ++kb) {
-        ok = !*abort_flag && mbar_wait_bounded(empty + stage, phase ^ 1u);
+        // waits are made warp-uniform: the warp signals with one lane after __syncwarp
+        ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait_bounded(empty + stage, phase ^ 1u));
         if (ok && leader) {
           unsigned char* st = smem + stage * Tile::STAGE_BYTES;
           mbar_arrive_expect_tx(full + stage, Tile::A_BYTES);
           tma_load_2d(st, &a.map_x, kb * TW_BKE, tm * BM, full + stage);
         }
-        ok = ok && mbar_wait_bounded(raw_full + rs, rphase);
+        ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(raw_full + rs, rphase));
         if (!ok) {
-          if (!*abort_flag) fail_wait();
+          if (lane == 0 && !*abort_flag) fail_wait();
           break;
         }
         const unsigned char* raw = raw_base + rs * Tile::RAW_BYTES;
@@ -298,9 +300,14 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
           *reinterpret_cast<uint4*>(row + (((2 * qk) ^ (r & 7)) << 4)) = lo;
           *reinterpret_cast<uint4*>(row + (((2 * qk + 1) ^ (r & 7)) << 4)) = hi;
         }
-        fence_proxy_async_smem();  // make the converted rows visible to the tensor core
-        mbar_arrive(raw_empty + rs);
-        mbar_arrive(full + stage);
+        // every writer fences its rows to the async proxy; one lane per warp then signals
+        // (one arrival per warp keeps the barrier traffic off the shared-memory atomics)
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(raw_empty + rs);
+          mbar_arrive(full + stage);
+        }
         if (++rs == RAW_STAGES) {
           rs = 0;
           rphase ^= 1u;

@@ -17,6 +17,7 @@
 #include "qrow_common.cuh"
 
 #include <algorithm>
+#include <type_traits>
 
 namespace mrb {
 
@@ -82,6 +83,57 @@ __global__ void __launch_bounds__(256) w8a8_quantize_kernel(const XT* __restrict
     dst[c] = quant_act(v, scale);
   }
 }
+
+// bf16 rows without a keep mask, k % 8 == 0, k <= 256 * 8 * MAXV: the row is read once with
+// 16-byte loads and held in registers between the max and the quantise pass; 8-byte stores.
+// Same arithmetic as w8a8_quantize_kernel, element for element.
+template <int MAXV>
+__global__ void __launch_bounds__(256) w8a8_quantize_bf16_vec_kernel(const __nv_bfloat16* __restrict__ x, int64_t k,
+                                                                     int8_t* __restrict__ qx,
+                                                                     float* __restrict__ act_scale) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  const int nv = (int)(k / 8);
+  const uint4* src = reinterpret_cast<const uint4*>(x + row * k);
+  uint4 v[MAXV];
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int idx = threadIdx.x + i * 256;
+    if (idx < nv) {
+      v[i] = __ldg(src + idx);
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(__bfloat162float(h[j])));
+    }
+  }
+  __shared__ float red[8];
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    t = warp_max(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float scale = act_scale_of(red[0]);
+  if (threadIdx.x == 0) act_scale[row] = scale;
+  uint2* dst = reinterpret_cast<uint2*>(qx + row * k);
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int idx = threadIdx.x + i * 256;
+    if (idx < nv) {
+      const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v[i]);
+      __align__(8) int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = quant_act(__bfloat162float(h[j]), scale);
+      dst[idx] = *reinterpret_cast<const uint2*>(q);
+    }
+  }
+}
+constexpr int QV_MAXV = 10;  // k <= 20480 on the vector path
 
 // ------------------------------------------------------------------ protected side path
 
@@ -410,9 +462,7 @@ int tc_int8_gemm(const int8_t* qx, const int8_t* qw, int64_t m, int64_t n, int64
                  const float* sw, const float* side, float* y, int32_t* acc_out, cudaStream_t s);
 int tc_int8_gemm_ex(const int8_t* qx, const int8_t* qw, const int8_t* qw_up, int64_t m, int64_t n, int64_t k,
                     const float* act_scale, const float* sw, const float* sw_up, const float* side,
-                    const float* bias, float* y, __nv_bfloat16* y_bf16, int32_t* acc_out, void* workspace,
-                    size_t workspace_bytes, cudaStream_t s);
-size_t tc_int8_workspace_bytes(int64_t m, int64_t n, int64_t k, bool paired);
+                    const float* bias, float* y, __nv_bfloat16* y_bf16, int32_t* acc_out, cudaStream_t s);
 
 static int launch_int8_gemm(const I8GemmArgs& a, cudaStream_t s) {
   return tc_int8_gemm(a.qx, a.qw, a.m, a.n, a.k, a.act_scale, a.sw, a.side, a.y, a.acc_out, s);
@@ -457,6 +507,12 @@ static int launch_a8_gemv(const A8Args& a, cudaStream_t s) {
 template <typename XT>
 static int launch_quantize(const void* x, int64_t m, int64_t k, const float* keep, int8_t* qx, float* scale,
                            cudaStream_t s) {
+  if (std::is_same<XT, __nv_bfloat16>::value && !keep && k % 8 == 0 && k <= 256 * 8 * QV_MAXV &&
+      aligned(x, 16) && aligned(qx, 8)) {
+    launch_kernel(w8a8_quantize_bf16_vec_kernel<QV_MAXV>, dim3((unsigned)m), dim3(256), 0, s, true,
+                  (const __nv_bfloat16*)x, k, qx, scale);
+    return launch_status("w8a8 quantize");
+  }
   launch_kernel(w8a8_quantize_kernel<XT>, dim3((unsigned)m), dim3(256), 0, s, true, (const XT*)x, k, keep, qx, scale);
   return launch_status("w8a8 quantize");
 }
@@ -549,15 +605,10 @@ extern "C" int mrb_w8a8_matmul(const void* x, int x_dtype, int64_t m, int64_t k,
   return launch_int8_gemm(a, s);
 }
 
-extern "C" size_t mrb_w8a8_workspace(int64_t m, int64_t n, int64_t k, int paired) {
-  if (m <= 0 || n <= 0 || k <= 0) return 0;
-  return tc_int8_workspace_bytes(m, n, k, paired != 0);
-}
-
 extern "C" int mrb_w8a8_linear_bf16(const void* x_bf16, int64_t m, int64_t k, const int8_t* codes,
                                     const float* scales, const int8_t* up_codes, const float* up_scales,
                                     const float* bias, int64_t n, void* y_bf16, int8_t* qx_ws, float* scale_ws,
-                                    void* workspace, size_t workspace_bytes, void* stream) {
+                                    void* stream) {
   if (m < 0 || k <= 0 || n <= 0) return fail(MRB_ERR_ARG, "w8a8_linear: bad shape");
   if (m == 0) return MRB_OK;
   if (!x_bf16 || !codes || !scales || !y_bf16 || !qx_ws || !scale_ws)
@@ -569,12 +620,11 @@ extern "C" int mrb_w8a8_linear_bf16(const void* x_bf16, int64_t m, int64_t k, co
   if (k > 133000) return fail(MRB_ERR_UNSUPPORTED, "w8a8_linear: k %lld could overflow int32", (long long)k);
   if (!aligned(codes, 16) || !aligned(qx_ws, 16) || (up_codes && !aligned(up_codes, 16)))
     return fail(MRB_ERR_ARG, "w8a8_linear: codes and the qx workspace must be 16-byte aligned");
-  if (workspace && !aligned(workspace, 256)) return fail(MRB_ERR_ARG, "w8a8_linear: workspace must be 256-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
   int st = quantize_dispatch(x_bf16, MRB_BF16, m, k, nullptr, qx_ws, scale_ws, s);
   if (st) return st;
   return tc_int8_gemm_ex(qx_ws, codes, up_codes, m, n, k, scale_ws, scales, up_scales, nullptr, bias, nullptr,
-                         (__nv_bfloat16*)y_bf16, nullptr, workspace, workspace_bytes, s);
+                         (__nv_bfloat16*)y_bf16, nullptr, s);
 }
 
 // ------------------------------------------------------------------ outlier column selection

@@ -13,7 +13,7 @@ stored as one concatenated page so one GEMV streams all three.
 
 ``mode="w8a8"`` runs every body projection as the W8A8 store matmul of ``enable_w8a8``
 (engine/kernels/w8a8.py:145-177): per-token int8 activations, exact int32 accumulation on the
-tensor cores (split over k for skinny row blocks), fp32 rescale (+ fp32 bias), one bf16
+tensor cores (split over k in clusters for skinny row blocks), fp32 rescale (+ fp32 bias), one bf16
 rounding; gate/up stay paired with the SwiGLU epilogue. The greedy head keeps the exact fp32
 head of ``_head`` (engine/dense_qstore_cuda.py:800-896).
 """
@@ -30,7 +30,7 @@ from .dense_qstore_cuda import (qrow_argmax, qrow_linear, qrow_swiglu, qrow_work
                                 rms_norm_into)
 from .paged_kv import PagedKVCache
 from .qstore_build import embed_rows, quant_row_int8
-from .w8a8 import w8a8_linear_bf16, w8a8_workspace_bytes
+from .w8a8 import w8a8_linear_bf16
 
 
 @dataclass(frozen=True)
@@ -216,13 +216,7 @@ class DenseDecoder:
         gemv_ws = max(qrow_workspace_bytes(device, n) for n in (cfg.qkv_rows, cfg.hidden, cfg.ffn))
         self.gemv_workspace = torch.zeros(gemv_ws, dtype=torch.uint8, device=device)
         if mode == "w8a8":
-            # per-token int8 activations and the split-K workspace of the tensor-core GEMM,
-            # shared by every projection (all ordered on one stream)
-            shapes = [(cfg.qkv_rows, cfg.hidden, False), (cfg.hidden, cfg.heads * cfg.head_dim, False),
-                      (cfg.ffn, cfg.hidden, True), (cfg.hidden, cfg.ffn, False)]
-            split_ws = max(w8a8_workspace_bytes(device, r, n, k, paired=pd)
-                           for r in {1, self.max_batch, self.max_prefill_tokens} for n, k, pd in shapes)
-            self.w8_workspace = torch.zeros(max(split_ws, 256), dtype=torch.uint8, device=device)
+            # per-token int8 activations of the projection being run (all ordered on one stream)
             self.w8_qx = torch.empty(rows, max(cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim), dtype=torch.int8,
                                      device=device)
             self.w8_scale = torch.empty(rows, dtype=torch.float32, device=device)
@@ -269,14 +263,12 @@ class DenseDecoder:
             def linear(page, x, out, bias=None):
                 k = int(x.shape[1])
                 return w8a8_linear_bf16(page.codes, page.scales, x, bias=bias, out=out,
-                                        qx_ws=self.w8_qx[:rows, :k], scale_ws=self.w8_scale[:rows],
-                                        workspace=self.w8_workspace)
+                                        qx_ws=self.w8_qx[:rows, :k], scale_ws=self.w8_scale[:rows])
 
             def swiglu(gate, up, x, out):
                 k = int(x.shape[1])
                 return w8a8_linear_bf16(gate.codes, gate.scales, x, up=(up.codes, up.scales), out=out,
-                                        qx_ws=self.w8_qx[:rows, :k], scale_ws=self.w8_scale[:rows],
-                                        workspace=self.w8_workspace)
+                                        qx_ws=self.w8_qx[:rows, :k], scale_ws=self.w8_scale[:rows])
         else:
             def linear(page, x, out, bias=None):
                 return qrow_linear(page.codes, page.scales, x, bias=bias, out=out, workspace=gws)

@@ -100,12 +100,6 @@ def w8a8_matmul(
     return y.reshape(*x.shape[:-1], out_features)
 
 
-def w8a8_workspace_bytes(device: torch.device, m: int, n: int, k: int, *, paired: bool = False) -> int:
-    """Bytes of the zeroed split-K workspace ``w8a8_linear_bf16`` can use (0: never splits)."""
-    del device
-    return int(_lib.load().mrb_w8a8_workspace(int(m), int(n), int(k), int(bool(paired))))
-
-
 def w8a8_linear_bf16(
     codes: torch.Tensor,
     scales: torch.Tensor,
@@ -116,13 +110,12 @@ def w8a8_linear_bf16(
     out: torch.Tensor | None = None,
     qx_ws: torch.Tensor | None = None,
     scale_ws: torch.Tensor | None = None,
-    workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """W8A8 projection for a bf16 decoder: ``bf16((acc * s_x) * s_w + bias)`` with per-token
     int8 activations and exact int32 accumulation (the ``enable_w8a8`` store matmul,
     engine/kernels/w8a8.py:145-177, at the dense engine's bf16 boundary). ``up=(codes, scales)``
-    gives the paired gate/up SwiGLU instead. ``workspace``: zeroed uint8 buffer of
-    ``w8a8_workspace_bytes`` for split-K over skinny row blocks."""
+    gives the paired gate/up SwiGLU instead. ``qx_ws`` / ``scale_ws``: optional int8 [m, k]
+    and fp32 [m] buffers for the quantised activations."""
     device = _lib.require_cuda(codes, scales, x, what="W8A8 linear")
     if x.dtype != torch.bfloat16:
         raise ValueError("W8A8 linear takes bf16 activations")
@@ -138,11 +131,9 @@ def w8a8_linear_bf16(
     y = out if out is not None else torch.empty((m, n), dtype=torch.bfloat16, device=device)
     qx = qx_ws if qx_ws is not None else torch.empty((m, k), dtype=torch.int8, device=device)
     sx = scale_ws if scale_ws is not None else torch.empty((m,), dtype=torch.float32, device=device)
-    ws_ptr, ws_bytes = (workspace.data_ptr(), workspace.numel()) if workspace is not None else (None, 0)
     _lib.call("mrb_w8a8_linear_bf16", x2.data_ptr(), m, k, codes.data_ptr(), scales.data_ptr(),
               _lib.ptr(up[0] if up is not None else None), _lib.ptr(up[1] if up is not None else None),
-              _lib.ptr(bias), n, y.data_ptr(), qx.data_ptr(), sx.data_ptr(), ws_ptr, ws_bytes,
-              _lib.stream_handle(device))
+              _lib.ptr(bias), n, y.data_ptr(), qx.data_ptr(), sx.data_ptr(), _lib.stream_handle(device))
     return y
 
 
@@ -183,5 +174,4 @@ def disable_w8a8(store: Any) -> Any:
     return store
 
 
-__all__ = ["_int8_gemm", "disable_w8a8", "enable_w8a8", "quantize_activations", "w8a8_linear_bf16", "w8a8_matmul",
-           "w8a8_workspace_bytes"]
+__all__ = ["_int8_gemm", "disable_w8a8", "enable_w8a8", "quantize_activations", "w8a8_linear_bf16", "w8a8_matmul"]

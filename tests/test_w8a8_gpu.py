@@ -119,35 +119,36 @@ def test_tensor_core_waits_never_timed_out(cuda):
 
 
 @pytest.mark.parametrize("m,n,k,paired,with_bias", [
-    (64, 3584, 3584, False, False),    # o projection at 64 decode rows: split over k
+    (64, 3584, 3584, False, False),    # o projection at 64 decode rows: k split over a cluster
     (64, 4608, 3584, False, True),     # qkv with bias, split
     (64, 3584, 18944, False, False),   # down projection, split
     (64, 18944, 3584, True, False),    # paired gate/up, 296 tiles: no split
     (64, 1000, 1024, True, False),     # paired, split, ragged output columns
+    (100, 1000, 512, False, True),     # split with a ragged row tile
     (300, 1000, 512, False, True),     # several row tiles
     (1, 256, 128, False, False),
 ])
 def test_w8a8_linear_bf16_exact_and_split_invariant(m, n, k, paired, with_bias, cuda):
-    """bf16 W8A8 projection: int32 accumulation exact, so the split-K result equals the
-    unsplit one bit for bit and the plain epilogue equals the oracle's fp32 rescale rounded
-    once to bf16."""
-    from mrun_b200.w8a8 import w8a8_linear_bf16, w8a8_workspace_bytes
+    """bf16 W8A8 projection: int32 accumulation is exact, so rows computed in a skinny batch
+    (k split over a cluster) equal the same rows computed inside a tall batch (no split) bit
+    for bit, and the plain epilogue equals the oracle's fp32 rescale rounded once to bf16."""
+    from mrun_b200.w8a8 import w8a8_linear_bf16
 
     gen = torch.Generator(device="cpu").manual_seed(m + n + k)
     q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
     s = torch.rand(n, generator=gen) * 1e-3 + 1e-5
     qu = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
     su = torch.rand(n, generator=gen) * 1e-3 + 1e-5
-    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    tall = 2048  # enough 128-row tiles that nothing splits
+    x_all = torch.randn(tall, k, generator=gen).to(torch.bfloat16)
+    x = x_all[:m].contiguous()
     bias = torch.randn(n, generator=gen) * 0.1 if with_bias else None
     dev = lambda t: None if t is None else t.to(cuda)  # noqa: E731
     up = (dev(qu), dev(su)) if paired else None
-    nbytes = w8a8_workspace_bytes(cuda, m, n, k, paired=paired)
-    ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=cuda)
-    y_split = w8a8_linear_bf16(dev(q), dev(s), dev(x), bias=dev(bias), up=up, workspace=ws)
-    y_split2 = w8a8_linear_bf16(dev(q), dev(s), dev(x), bias=dev(bias), up=up, workspace=ws)  # reused workspace
-    y_whole = w8a8_linear_bf16(dev(q), dev(s), dev(x), bias=dev(bias), up=up)
-    assert torch.equal(y_split, y_whole) and torch.equal(y_split2, y_whole)
+    y = w8a8_linear_bf16(dev(q), dev(s), dev(x), bias=dev(bias), up=up)
+    y_again = w8a8_linear_bf16(dev(q), dev(s), dev(x), bias=dev(bias), up=up)
+    y_tall = w8a8_linear_bf16(dev(q), dev(s), dev(x_all), bias=dev(bias), up=up)
+    assert torch.equal(y, y_again) and torch.equal(y, y_tall[:m])
 
     qx, sx = ow8.quantize_activations(x.float().numpy())
     acc = ow8.int8_gemm(qx, q.numpy())
@@ -156,13 +157,30 @@ def test_w8a8_linear_bf16_exact_and_split_invariant(m, n, k, paired, with_bias, 
         u = (ow8.int8_gemm(qx, qu.numpy()).astype(np.float32) * sx).astype(np.float32) * su.numpy()[None, :]
         gv, uv = bf16_round(g), bf16_round(u)
         ref = bf16_round(bf16_round(gv * oq.sigmoid_f32(gv)) * uv)
-        assert max_rel_err(y_whole.float().cpu().numpy(), ref) < 1e-2
+        assert max_rel_err(y.float().cpu().numpy(), ref) < 1e-2
     else:
         if bias is not None:
             g = (g + bias.numpy()[None, :]).astype(np.float32)
-        np.testing.assert_array_equal(y_whole.float().cpu().numpy(), bf16_round(g))
+        np.testing.assert_array_equal(y.float().cpu().numpy(), bf16_round(g))
     out = ctypes.c_uint(0)
     from mrun_b200 import _lib
 
     _lib.call("mrb_tc_status", ctypes.addressof(out))
     assert out.value == 0
+
+
+@pytest.mark.parametrize("m,k", [(64, 3584), (3, 18944), (5, 20480), (2, 20496), (7, 40)])
+def test_bf16_activation_quantiser_bit_exact(m, k, cuda):
+    """bf16 rows (the vector path up to 20480 columns, the generic one beyond): codes and
+    scales bit-identical to the oracle quantiser."""
+    from mrun_b200.w8a8 import quantize_activations
+
+    gen = torch.Generator(device="cpu").manual_seed(m * k)
+    x = (torch.randn(m, k, generator=gen) * 3).to(torch.bfloat16)
+    x[0, 5] = 0.0
+    if m > 2:
+        x[2] = 0.0  # an all-zero row takes scale 1
+    qx, sx = quantize_activations(x.to(cuda))
+    rq, rs = ow8.quantize_activations(x.float().numpy())
+    np.testing.assert_array_equal(qx.cpu().numpy(), rq)
+    np.testing.assert_array_equal(sx.cpu().numpy().reshape(-1), rs.reshape(-1))
