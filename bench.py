@@ -575,6 +575,63 @@ def run_stream_case(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+ATTN_CASES = {
+    # name: (rows, query heads, kv heads, context low, context high) of one layer's decode
+    # attention: config 3's 64 rows and config 4's 32 rows
+    "attn-batch64": (64, 28, 4, 128, 2048),
+    "attn-moe32": (32, 32, 4, 256, 4096),
+}
+
+
+def run_attn_case(args) -> None:
+    """Small case for kernel captures: one layer's paged decode attention at a config-3 or
+    config-4 shape (random bf16 K/V pages, ragged contexts from numpy seed 0), timed over
+    back-to-back launches. Prints the device-timed average and the KV bytes read per second;
+    not the bench metric."""
+    import numpy as np
+    import torch
+
+    from mrun_b200.paged_kv import PagedKVCache
+
+    rows, hq, hkv, lo, hi = ATTN_CASES[args.case]
+    d = 128
+    device = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    lengths = [int(v) for v in rng.integers(lo, hi + 1, rows)]
+    cap = hi + 16
+    kv = PagedKVCache(num_layers=1, num_pages=rows * ((cap + 15) // 16), kv_heads=hkv, head_dim=d, max_seqs=rows,
+                      max_pages_per_seq=(cap + 15) // 16, device=device)
+    for i, n in enumerate(lengths):
+        kv.reserve(i, n)
+    gen = torch.Generator(device=device).manual_seed(0)
+    kv.k[0].normal_(0.0, 1.0, generator=gen)
+    kv.v[0].normal_(0.0, 1.0, generator=gen)
+    q = torch.randn(rows, hq, d, device=device, generator=gen).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    row_len = torch.tensor(lengths, dtype=torch.int32, device=device)
+    row_seq = torch.arange(rows, dtype=torch.int32, device=device)
+    ws = torch.zeros(max(256, kv.workspace_bytes(rows, hq, cap)), dtype=torch.uint8, device=device)
+
+    def launch():
+        kv.attend(0, q, row_len, max_total_tokens=cap, row_seq=row_seq, out=out, workspace=ws, scale=d ** -0.5)
+
+    for _ in range(args.warmup):
+        launch()
+    stream = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    for _ in range(args.steps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    avg_s = e0.elapsed_time(e1) / 1000.0 / args.steps
+    kv_bytes = sum(lengths) * 2 * hkv * d * 2
+    print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "kv_bytes": kv_bytes,
+                      "kv_gbs": kv_bytes / avg_s / 1e9, "launches": args.steps}), flush=True)
+
+
 BATCH_SEQS = 64
 BATCH_NEW_TOKENS = 128
 
@@ -803,7 +860,7 @@ def main() -> None:
     ap.add_argument("--cpu-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
-                                       *TC_CASES],
+                                       *TC_CASES, *ATTN_CASES],
                     default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
@@ -811,6 +868,8 @@ def main() -> None:
         args.warmup = 3
     if args.case in GEMV_CASES:
         run_gemv_case(args)
+    elif args.case in ATTN_CASES:
+        run_attn_case(args)
     elif args.case in TC_CASES:
         run_tc_case(args)
     elif args.case == "moe-decode":

@@ -451,9 +451,37 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
   const int nmine = warp < ntile ? (ntile - warp + W - 1) / W : 0;
   const int64_t khead = (int64_t)kvh * a.stride_head;
 
+  // a 16-token tile (tiles start at multiples of 16) lies inside one page when the page size
+  // is a multiple of 16: one block-table lookup per tile, then affine addresses
+  const bool tile_in_page = (a.page_size % AT_TILE) == 0;
   // ---- this warp's K/V ring: its j-th tile (split tile warp + j*W) in stage j % AM_STAGES
   auto issue = [&](int j) {
-    if (j < nmine) {
+    if (j < nmine && tile_in_page) {
+      __nv_bfloat16* kst = ring + (j % AM_STAGES) * AM_STAGE_ELEMS;
+      __nv_bfloat16* vst = kst + AM_TILE_ELEMS;
+      const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
+      const int64_t base = t0 < len ? kv_offset(a, seq, t0, khead) : 0;  // committed tokens only
+      const int lim = (int)(t_end - t0), newt = has_new ? (int)(len - t0) : -1;
+#pragma unroll
+      for (int i = 0; i < AT_TILE * (D / 8) / 32; ++i) {
+        const int e = lane + 32 * i;
+        const int t = e >> 4, ch = e & 15;
+        const bool ok = t < lim;
+        const __nv_bfloat16 *kp = a.k_cache, *vp = a.v_cache;
+        if (ok) {
+          if (t == newt) {
+            kp = a.k_new + (r * a.hkv + kvh) * D;
+            vp = a.v_new + (r * a.hkv + kvh) * D;
+          } else {
+            const int64_t off = base + (int64_t)t * a.stride_tok;
+            kp = a.k_cache + off;
+            vp = a.v_cache + off;
+          }
+        }
+        cp_async16_zfill(kst + t * AM_ROW + ch * 8, kp + (ok ? ch * 8 : 0), ok);
+        cp_async16_zfill(vst + t * AM_ROW + ch * 8, vp + (ok ? ch * 8 : 0), ok);
+      }
+    } else if (j < nmine) {
       __nv_bfloat16* kst = ring + (j % AM_STAGES) * AM_STAGE_ELEMS;
       __nv_bfloat16* vst = kst + AM_TILE_ELEMS;
       const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
@@ -523,13 +551,11 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
       }
     }
     // ---- online softmax per head row (rows g and g + 8), fp32
+    const int lim = (int)(t_end - t0);  // tokens of this tile inside the split
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int64_t tok = t0 + nt * 8 + 2 * c + (i & 1);
-        s[nt][i] = tok < t_end ? s[nt][i] * a.scale : -INFINITY;
-      }
+      for (int i = 0; i < 4; ++i) s[nt][i] = nt * 8 + 2 * c + (i & 1) < lim ? s[nt][i] * a.scale : -INFINITY;
     float alpha[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -556,12 +582,18 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
     const uint32_t pa[4] = {pack_bf16x2(s[0][0], s[0][1]), pack_bf16x2(s[0][2], s[0][3]),
                             pack_bf16x2(s[1][0], s[1][1]), pack_bf16x2(s[1][2], s[1][3])};
     const __nv_bfloat16* vrow = vst + (lane & 15) * AM_ROW;
+    // rescale only when some row's running max moved (alpha is exactly 1 otherwise)
+    if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt) {
+        o[dt][0] *= alpha[0];
+        o[dt][1] *= alpha[0];
+        o[dt][2] *= alpha[1];
+        o[dt][3] *= alpha[1];
+      }
+    }
 #pragma unroll
     for (int dt = 0; dt < D / 8; ++dt) {
-      o[dt][0] *= alpha[0];
-      o[dt][1] *= alpha[0];
-      o[dt][2] *= alpha[1];
-      o[dt][3] *= alpha[1];
       uint32_t b0, b1;
       ldmatrix_x2_trans(b0, b1, vrow + dt * 8);
       mma_bf16_16816(o[dt], pa, b0, b1);
