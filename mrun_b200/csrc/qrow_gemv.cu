@@ -693,6 +693,8 @@ static int check_common(const void* x, int64_t m, int64_t k, const int8_t* codes
 }
 
 bool tc_w8a16_supported(const void* x, int64_t k, const int8_t* codes, const int8_t* up_codes);
+int tc_w8a16_argmax(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
+                    int64_t n, int64_t semantic, float* logits, unsigned long long* packed, cudaStream_t s);
 int tc_w8a16_gemm(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
                   const int8_t* up_codes, const float* up_scales, int64_t n, const float* bias, __nv_bfloat16* y,
                   cudaStream_t s);
@@ -801,7 +803,13 @@ extern "C" int mrb_qrow_argmax(const void* x, int x_dtype, int64_t m, int64_t k,
   a.semantic = semantic_rows;
   a.packed = reinterpret_cast<unsigned long long*>(out_index);
   switch (x_dtype) {
-    case MRB_BF16: st = dispatch_nt<__nv_bfloat16, float, false, EPI_ARGMAX>(a, GvWorkspace{}, s); break;
+    case MRB_BF16:
+      // many rows: one tensor-core pass over the head instead of one GEMV pass per 16 rows
+      if (m > GEMV_MAX_ROWS && tc_w8a16_supported(x, k, codes, nullptr))
+        st = tc_w8a16_argmax((const __nv_bfloat16*)x, m, k, codes, scales, n, semantic_rows, logits, a.packed, s);
+      else
+        st = dispatch_nt<__nv_bfloat16, float, false, EPI_ARGMAX>(a, GvWorkspace{}, s);
+      break;
     case MRB_F16: st = dispatch_nt<__half, float, false, EPI_ARGMAX>(a, GvWorkspace{}, s); break;
     case MRB_F32: st = dispatch_nt<float, float, true, EPI_ARGMAX>(a, GvWorkspace{}, s); break;
     default: return fail(MRB_ERR_ARG, "qrow_argmax: bad x_dtype %d", x_dtype);

@@ -540,7 +540,7 @@ int tc_int8_gemm_ex(const int8_t* qx, const int8_t* qw, const int8_t* qw_up, int
   const int64_t sms = num_sms();
   const int64_t wr = a.paired ? 2 : 1;  // weight rows per output column
   auto ntiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n * wr + bn - 1) / bn); };
-  if (ntiles(256, 256) >= 2 * sms) return tc_launch<2, 256>(a, qx, qw, qw_up, s);
+  if (m > 128 && ntiles(256, 256) >= 2 * sms) return tc_launch<2, 256>(a, qx, qw, qw_up, s);
   if (ntiles(128, 256) >= sms) return tc_launch<1, 256>(a, qx, qw, qw_up, s);
   return tc_launch<1, 128>(a, qx, qw, qw_up, s);
 }

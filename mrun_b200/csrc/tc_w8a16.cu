@@ -69,8 +69,13 @@ struct TwGemmArgs {
   const float* scales;     // [n]
   const float* scales_up;  // [n] (paired)
   const float* bias;       // [n] or null (plain only)
-  __nv_bfloat16* y;        // [m, n]
+  __nv_bfloat16* y;        // [m, n] (null in argmax mode)
   bool vec_store;          // n % 8 == 0 and y 16-byte aligned
+  // greedy-head mode (packed non-null): per activation row, atomicMax of pack(logit, col)
+  // over columns < semantic; logits (fp32 [m, n]) optionally written
+  unsigned long long* packed;
+  float* logits;
+  int64_t semantic;
 };
 
 __device__ unsigned g_tw_timeouts = 0;
@@ -219,6 +224,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
         const int64_t row = (int64_t)tm * BM + h * TW_HM + q * 32 + lane;
         const bool row_ok = row < a.m;
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + acc_col(buf, h);
+        unsigned long long best = 0ull;  // argmax mode: this row's best key over the tile
         for (int c0 = 0; c0 < out_cols; c0 += 32) {
           uint32_t v[32], u[32];
           __syncwarp();
@@ -226,21 +232,34 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
           if (a.paired) tmem_ld_32cols(tbase + (uint32_t)(BN / 2 + c0), u);
           const int64_t col0 = (int64_t)tn * out_cols + c0;
           if (!row_ok || col0 >= a.n) continue;
+          if (a.packed) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int64_t col = col0 + j;
+              const float val = __uint_as_float(v[j]) * __ldg(a.scales + (col < a.n ? col : a.n - 1));
+              if (col < a.n && a.logits) a.logits[row * a.n + col] = val;
+              if (col < a.semantic) {
+                const unsigned long long key = pack_argmax(val, col);
+                best = key > best ? key : best;
+              }
+            }
+            continue;
+          }
           __align__(16) __nv_bfloat16 out[32];
           if (a.paired) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int64_t col = col0 + j < a.n ? col0 + j : a.n - 1;
-              const float gv = round_bf16(__uint_as_float(v[j]) * a.scales[col]);
-              const float uv = round_bf16(__uint_as_float(u[j]) * a.scales_up[col]);
+              const float gv = round_bf16(__uint_as_float(v[j]) * __ldg(a.scales + col));
+              const float uv = round_bf16(__uint_as_float(u[j]) * __ldg(a.scales_up + col));
               out[j] = __float2bfloat16_rn(round_bf16(silu_f32(gv)) * uv);
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int64_t col = col0 + j < a.n ? col0 + j : a.n - 1;
-              float r = __uint_as_float(v[j]) * a.scales[col];
-              if (a.bias) r = round_bf16(r) + round_bf16(a.bias[col]);
+              float r = __uint_as_float(v[j]) * __ldg(a.scales + col);
+              if (a.bias) r = round_bf16(r) + round_bf16(__ldg(a.bias + col));
               out[j] = __float2bfloat16_rn(r);
             }
           }
@@ -253,6 +272,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
             for (int j = 0; j < 32 && col0 + j < a.n; ++j) dst[j] = out[j];
           }
         }
+        if (a.packed && row_ok && best != 0ull) atomicMax(a.packed + row, best);
       }
       tc_fence_before();
       mbar_arrive(acc_empty + buf);
@@ -383,9 +403,31 @@ int tc_w8a16_gemm(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* co
   const int64_t sms = num_sms();
   const int64_t per_tile = a.paired ? 2 : 1;  // weight rows per output column
   auto tiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n * per_tile + bn - 1) / bn); };
-  if (tiles(256, 256) >= 2 * sms) return tw_launch<2, 256>(a, x, codes, up_codes, s);
+  if (m > 128 && tiles(256, 256) >= 2 * sms) return tw_launch<2, 256>(a, x, codes, up_codes, s);
   if (tiles(128, 256) >= sms) return tw_launch<1, 256>(a, x, codes, up_codes, s);
   return tw_launch<1, 128>(a, x, codes, up_codes, s);
+}
+
+// Greedy head on the tensor cores: packed[r] = max over columns < semantic of
+// pack_argmax(x[r] . codes[col] * scales[col], col) (packed must start at 0; atomicMax), fp32
+// logits optionally written. Same requirements as tc_w8a16_gemm.
+int tc_w8a16_argmax(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
+                    int64_t n, int64_t semantic, float* logits, unsigned long long* packed, cudaStream_t s) {
+  TwGemmArgs a{};
+  a.m = m;
+  a.n = n;
+  a.k = k;
+  a.kblocks = (int)((k + TW_BKE - 1) / TW_BKE);
+  a.paired = false;
+  a.scales = scales;
+  a.packed = packed;
+  a.logits = logits;
+  a.semantic = semantic;
+  const int64_t sms = num_sms();
+  auto tiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n + bn - 1) / bn); };
+  if (m > 128 && tiles(256, 256) >= 2 * sms) return tw_launch<2, 256>(a, x, codes, nullptr, s);
+  if (tiles(128, 256) >= sms) return tw_launch<1, 256>(a, x, codes, nullptr, s);
+  return tw_launch<1, 128>(a, x, codes, nullptr, s);
 }
 
 int tc_w8a16_timeouts(unsigned* out) {

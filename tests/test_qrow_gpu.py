@@ -178,6 +178,31 @@ def test_argmax_ties_pick_lowest_index(cuda):
     assert idx.cpu().tolist() == [0, 0]
 
 
+@pytest.mark.parametrize("m,n,k,semantic", [(64, 152064, 512, 152000), (40, 3001, 256, 3001), (300, 9000, 128, 8999)])
+def test_greedy_head_many_rows(m, n, k, semantic, cuda):
+    """Above 32 rows the greedy head runs on the tcgen05 W8A16 GEMM with the argmax fused
+    into its epilogue: fp32 logits within 1e-4 of the float64 product and every pick the
+    float64 argmax unless the top two are within that error (reported near-tie)."""
+    from mrun_b200.dense_qstore_cuda import qrow_argmax
+
+    gen = torch.Generator(device="cpu").manual_seed(m + n)
+    q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    s = torch.rand(n, generator=gen) * 1e-3 + 1e-4
+    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    idx, val, logits = qrow_argmax(q.to(cuda), s.to(cuda), x.to(cuda), semantic_rows=semantic)
+    exact = oq.qrow_matmul_exact(x.float().numpy(), q.numpy(), s.numpy())
+    got = logits.cpu().numpy()
+    assert max_rel_err(got, exact) < FP32_TOL
+    e = exact[:, :semantic]
+    best = e.argmax(axis=1)
+    picks = idx.cpu().numpy()
+    for r in range(m):
+        if picks[r] != best[r]:
+            assert e[r, best[r]] - e[r, picks[r]] <= 1e-4 * np.abs(e[r]).max(), (r, picks[r], best[r])
+    np.testing.assert_array_equal(val.cpu().numpy(), got[np.arange(m), picks])
+    assert _tc_timeouts() == 0
+
+
 def test_embed_rows_bit_exact(cuda):
     from mrun_b200.qstore_build import embed_rows
 
