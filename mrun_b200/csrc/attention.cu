@@ -27,6 +27,9 @@ constexpr int AT_STAGES = 4;       // K/V tiles per CTA in shared memory (cp.asy
 #ifndef AT_MIN_TILES
 #define AT_MIN_TILES 4  // split-K: fewest 16-token tiles per split
 #endif
+#ifndef AT_MMA_CTAS_PER_SM
+#define AT_MMA_CTAS_PER_SM 2  // split-K target of the tensor-core kernel
+#endif
 
 // ------------------------------------------------------------------ RoPE + KV append
 
@@ -391,7 +394,8 @@ constexpr int AM_MAX_WARPS = 4;
 
 __host__ __device__ inline size_t am_smem_bytes(int warps) {
   const size_t ring = (size_t)warps * AM_STAGES * AM_STAGE_ELEMS * sizeof(__nv_bfloat16);
-  const size_t merge = (size_t)warps * 16 * (2 + 128) * sizeof(float);
+  // merge area: per-warp states [W][16][2 + D], then weights [W][16] and per-head (max, sum)
+  const size_t merge = ((size_t)warps * 16 * (2 + 128) + (size_t)warps * 16 + 2 * 16) * sizeof(float);
   return ring > merge ? ring : merge;
 }
 
@@ -402,9 +406,18 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& b0, uint32_t& b1, const void* p) {
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* p) {
   const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(p));
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(s));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* p) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -512,6 +525,7 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
 
   // ---- Q of the group as the mma A operand: rows g and g + 8 are query heads (zero beyond
   // the group), eight 16-dim k steps
+  const bool two_halves = group > 8;
   uint32_t qa[D / 16][4];
   {
     const __nv_bfloat16* q0 = a.q + (r * a.hq + (int64_t)kvh * group) * D;
@@ -538,16 +552,19 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
     const __nv_bfloat16* vst = kst + AM_TILE_ELEMS;
     const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
     // ---- scores: s[nt] = (head g | g+8) x (tokens nt*8 + 2c, +1)
+    // K fragments by ldmatrix.x4: lane l addresses token nt*8 + (l & 7), dims
+    // ks*16 + (l >> 3)*8, so the four matrices are (b0, b1) of k steps ks and ks + 1
     float s[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      const __nv_bfloat16* kr = kst + (nt * 8 + g) * AM_ROW + 2 * c;
+      const __nv_bfloat16* kr = kst + (nt * 8 + (lane & 7)) * AM_ROW + (lane >> 3) * 8;
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + ks * 16);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + ks * 16 + 8);
-        mma_bf16_16816(s[nt], qa[ks], b0, b1);
+      for (int ks = 0; ks < D / 16; ks += 2) {
+        uint32_t kb[4];
+        ldmatrix_x4(kb, kr + ks * 16);
+        mma_bf16_16816(s[nt], qa[ks], kb[0], kb[1]);
+        mma_bf16_16816(s[nt], qa[ks + 1], kb[2], kb[3]);
       }
     }
     // ---- online softmax per head row (rows g and g + 8), fp32
@@ -556,9 +573,12 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) s[nt][i] = nt * 8 + 2 * c + (i & 1) < lim ? s[nt][i] * a.scale : -INFINITY;
-    float alpha[2];
+    // rows g + 8 hold query heads only for groups above 8; otherwise they stay empty
+    float alpha[2] = {1.f, 1.f};
+    if (!two_halves) s[0][2] = s[0][3] = s[1][2] = s[1][3] = 0.f;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
+      if (h == 1 && !two_halves) break;
       float mx = fmaxf(fmaxf(s[0][2 * h], s[0][2 * h + 1]), fmaxf(s[1][2 * h], s[1][2 * h + 1]));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
@@ -581,7 +601,9 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
     // ---- O = O * alpha + P V (P in bf16 as the A operand, V via ldmatrix.trans)
     const uint32_t pa[4] = {pack_bf16x2(s[0][0], s[0][1]), pack_bf16x2(s[0][2], s[0][3]),
                             pack_bf16x2(s[1][0], s[1][1]), pack_bf16x2(s[1][2], s[1][3])};
-    const __nv_bfloat16* vrow = vst + (lane & 15) * AM_ROW;
+    // V fragments by ldmatrix.x4.trans: lanes 0-15 address tokens 0-15 at dims dt*8, lanes
+    // 16-31 the same tokens at dims (dt+1)*8
+    const __nv_bfloat16* vrow = vst + (lane & 15) * AM_ROW + (lane >> 4) * 8;
     // rescale only when some row's running max moved (alpha is exactly 1 otherwise)
     if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
@@ -593,10 +615,11 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
       }
     }
 #pragma unroll
-    for (int dt = 0; dt < D / 8; ++dt) {
-      uint32_t b0, b1;
-      ldmatrix_x2_trans(b0, b1, vrow + dt * 8);
-      mma_bf16_16816(o[dt], pa, b0, b1);
+    for (int dt = 0; dt < D / 8; dt += 2) {
+      uint32_t vb[4];
+      ldmatrix_x4_trans(vb, vrow + dt * 8);
+      mma_bf16_16816(o[dt], pa, vb[0], vb[1]);
+      mma_bf16_16816(o[dt + 1], pa, vb[2], vb[3]);
     }
   }
   cp_async_wait_group<0>();
@@ -621,18 +644,31 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
     }
   }
   __syncthreads();
-  float* part_base = a.nsplit > 1 ? a.part + (rh * a.nsplit + split) * (int64_t)group * (2 + D) : nullptr;
-  for (int idx = tid; idx < group * D; idx += blockDim.x) {
-    const int h = idx / D, d = idx - h * D;
+  // per head: the combined max and sum, and one weight per warp state (expf once per (warp,
+  // head) instead of once per element)
+  float* wts = mb + (size_t)W * 16 * (2 + D);  // [W][16]
+  float* hstat = wts + (size_t)W * 16;         // [16] max, [16] sum
+  if (tid < group) {
+    const int h = tid;
     float mx = -INFINITY;
     for (int w = 0; w < W; ++w) mx = fmaxf(mx, mb[((size_t)w * 16 + h) * (2 + D)]);
-    float l = 0.f, acc = 0.f;
+    float l = 0.f;
     for (int w = 0; w < W; ++w) {
       const float* st = mb + ((size_t)w * 16 + h) * (2 + D);
       const float wt = (st[0] == -INFINITY) ? 0.f : expf(st[0] - mx);
+      wts[w * 16 + h] = wt;
       l = fmaf(st[1], wt, l);
-      acc = fmaf(st[2 + d], wt, acc);
     }
+    hstat[h] = mx;
+    hstat[16 + h] = l;
+  }
+  __syncthreads();
+  float* part_base = a.nsplit > 1 ? a.part + (rh * a.nsplit + split) * (int64_t)group * (2 + D) : nullptr;
+  for (int idx = tid; idx < group * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx - h * D;
+    const float mx = hstat[h], l = hstat[16 + h];
+    float acc = 0.f;
+    for (int w = 0; w < W; ++w) acc = fmaf(mb[((size_t)w * 16 + h) * (2 + D) + 2 + d], wts[w * 16 + h], acc);
     if (a.nsplit == 1) {
       a.out[(r * a.hq + (int64_t)kvh * group + h) * D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
     } else {
@@ -739,9 +775,12 @@ static bool use_mma(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_d
 static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_dim) {
   const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
   const int64_t groups = std::max<int64_t>(1, rows * hkv);
-  const int64_t target = ((int64_t)AT_CTAS_PER_SM * num_sms() + groups - 1) / groups;  // splits per group
-  const int64_t min_tiles =
-      use_mma(rows, hkv, max_total, head_dim) ? 2 * AM_MAX_WARPS : (tiles <= 64 ? 2 : AT_MIN_TILES);
+  const bool mma = use_mma(rows, hkv, max_total, head_dim);
+  // the tensor-core kernel holds 2 CTAs per SM: aim at one resident wave, so each warp has
+  // enough tiles to amortise its prologue and merge (measured best of 2, 3, 4, 6 per SM)
+  const int64_t per_sm = mma ? AT_MMA_CTAS_PER_SM : AT_CTAS_PER_SM;
+  const int64_t target = (per_sm * num_sms() + groups - 1) / groups;  // splits per group
+  const int64_t min_tiles = mma ? 2 * AM_MAX_WARPS : (tiles <= 64 ? 2 : AT_MIN_TILES);
   int64_t tps = std::max<int64_t>(min_tiles, (tiles + target - 1) / target);
   tps = std::min<int64_t>(tps, tiles);
   tps = std::max<int64_t>(tps, (tiles + AT_MAX_SPLIT - 1) / AT_MAX_SPLIT);

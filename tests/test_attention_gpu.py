@@ -66,6 +66,8 @@ def _random_paged(rng, rows, hkv, d, lengths, num_pages):
     # query groups of 8 and 7
     (8, 32, 4, [1, 300, 777, 1024, 1500, 1999, 2048, 64]),
     (6, 28, 4, [4000, 3333, 2500, 17, 1024, 3100]),
+    # tensor-core kernel with a 16-head group (both 8-row halves of the mma tile in use)
+    (4, 64, 4, [3000, 100, 2048, 4096]),
 ])
 def test_paged_attention_vs_oracle(rows, hq, hkv, lengths, cuda):
     from mrun_b200.segmented_gqa_decode import paged_attention
