@@ -257,53 +257,75 @@ def _time_gemv(weights, iters: int = 56) -> dict:
     return {"avg_s": avg_s, "bytes": bytes_per_launch}
 
 
+def _graph_avg_seconds(launch, steps: int, warmup: int, device) -> float:
+    """Average device time of launch(i) for i in range(steps), captured in one CUDA graph (so
+    host call overhead is not timed) and replayed once untimed, then once between CUDA events
+    on the replay stream."""
+    import torch
+
+    for i in range(warmup):
+        launch(i)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for i in range(steps):
+            launch(i)
+    graph.replay()
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(side):
+        e0.record(side)
+        graph.replay()
+        e1.record(side)
+    torch.cuda.synchronize(device)
+    del graph
+    return e0.elapsed_time(e1) / 1000.0 / steps
+
+
 GEMV_CASES = {
-    # name: (rows n, depth k, paired gate/up SwiGLU) at the config-2 shapes
-    "gemv-swiglu": (18944, 3584, True),
-    "gemv-down": (3584, 18944, False),
-    "gemv-qkv": (4608, 3584, False),
+    # name: (rows n, depth k, paired gate/up SwiGLU, activation rows, stream-K workspace):
+    # config-2 shapes at M=1, config-4 dense projections at M=32 (as the MoE decoder calls them)
+    "gemv-swiglu": (18944, 3584, True, 1, False),
+    "gemv-down": (3584, 18944, False, 1, False),
+    "gemv-qkv": (4608, 3584, False, 1, False),
+    "gemv-o32": (2048, 4096, False, 32, True),
+    "gemv-qkv32": (5120, 2048, False, 32, True),
+    "gemv-o32-whole": (2048, 4096, False, 32, False),
 }
 
 
 def run_gemv_case(args) -> None:
-    """Small case for kernel captures: one decode GEMV (M=1) at a config-2 shape over 4
-    weight sets in turn (272 to 543 MB, above L2). Prints one JSON line with the
-    device-timed average; not the bench metric."""
+    """Small case for kernel captures: one decode GEMV at a config-2 (M=1) or config-4 (M=32)
+    shape over enough weight sets in turn to exceed L2 (>= 256 MB). Prints one JSON line with
+    the device-timed average; not the bench metric."""
     import torch
 
-    from mrun_b200.dense_qstore_cuda import qrow_linear, qrow_swiglu
+    from mrun_b200.dense_qstore_cuda import qrow_linear, qrow_swiglu, qrow_workspace_bytes
 
-    n, k, paired = GEMV_CASES[args.case]
+    n, k, paired, rows, use_ws = GEMV_CASES[args.case]
     device = torch.device("cuda", 0)
     gen = torch.Generator(device=device).manual_seed(0)
-    sets = 4
     per = 2 if paired else 1
+    sets = max(4, -(-(256 << 20) // (per * n * k)))
     codes = [torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=gen)
              for _ in range(sets * per)]
     scales = [torch.rand(n, device=device, generator=gen) * 0.01 for _ in range(sets * per)]
-    x = torch.randn(1, k, device=device, generator=gen).to(torch.bfloat16)
-    out = torch.empty(1, n, device=device, dtype=torch.bfloat16)
+    x = torch.randn(rows, k, device=device, generator=gen).to(torch.bfloat16)
+    out = torch.empty(rows, n, device=device, dtype=torch.bfloat16)
+    ws = torch.zeros(max(256, qrow_workspace_bytes(device, n)), dtype=torch.uint8, device=device) if use_ws else None
 
     def launch(i):
         j = per * (i % sets)
         if paired:
-            qrow_swiglu(codes[j], scales[j], codes[j + 1], scales[j + 1], x, out=out)
+            qrow_swiglu(codes[j], scales[j], codes[j + 1], scales[j + 1], x, out=out, workspace=ws)
         else:
-            qrow_linear(codes[j], scales[j], x, out=out)
+            qrow_linear(codes[j], scales[j], x, out=out, workspace=ws)
 
-    for i in range(args.warmup):
-        launch(i)
-    stream = torch.cuda.current_stream(device)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(device)
-    e0.record(stream)
-    for i in range(args.steps):
-        launch(i)
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    avg_s = e0.elapsed_time(e1) / 1000.0 / args.steps
-    nbytes = per * (n * k + n * 4) + 2 * k + 2 * n
+    avg_s = _graph_avg_seconds(launch, args.steps, args.warmup, device)
+    nbytes = per * (n * k + n * 4) + rows * (2 * k + 2 * n)
     print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "bytes_per_launch": nbytes,
                       "gbs": nbytes / avg_s / 1e9, "launches": args.steps}), flush=True)
 
@@ -329,9 +351,10 @@ TC_CASES = {
 
 def run_tc_case(args) -> None:
     """Small case for kernel captures: a tcgen05 GEMM at a config-2 prefill shape (the int8
-    GEMM with exact int32 accumulators, or the W8A16 GEMM with bf16 activations), alternating
-    two weight matrices. Prints one JSON line with the device-timed average and the tensor
-    throughput; not the bench metric."""
+    GEMM with exact int32 accumulators, or the W8A16 GEMM with bf16 activations) or a 64-row
+    W8A8 projection, cycling weight matrices (enough to exceed L2), timed in a CUDA graph.
+    Prints one JSON line with the device-timed average and the tensor throughput; not the
+    bench metric."""
     import torch
 
     from mrun_b200 import _lib
@@ -339,12 +362,12 @@ def run_tc_case(args) -> None:
     m, n, k = TC_CASES[args.case]
     device = torch.device("cuda", 0)
     gen = torch.Generator(device=device).manual_seed(0)
-    stream = torch.cuda.current_stream(device)
     w8a16 = args.case.startswith("w8a16")
     w8a8_linear = args.case.startswith("w8a8-linear")
     paired = args.case in ("w8a16-gemm-gateup", "w8a8-linear-gateup64")
     wrows = 2 * n if paired else n  # weight rows the GEMM multiplies
-    qws = [torch.randint(-127, 128, (wrows, k), dtype=torch.int8, device=device, generator=gen) for _ in range(2)]
+    nsets = max(2, -(-(256 << 20) // (wrows * k)))  # weight sets cycled so they exceed L2
+    qws = [torch.randint(-127, 128, (wrows, k), dtype=torch.int8, device=device, generator=gen) for _ in range(nsets)]
     if w8a8_linear:
         from mrun_b200.w8a8 import w8a8_linear_bf16
 
@@ -355,7 +378,7 @@ def run_tc_case(args) -> None:
         sx = torch.empty(m, dtype=torch.float32, device=device)
 
         def launch(i):
-            w = qws[i % 2]
+            w = qws[i % nsets]
             up = (w[n:], scales[n:]) if paired else None
             w8a8_linear_bf16(w[:n], scales[:n], x, up=up, out=y, qx_ws=qx, scale_ws=sx)
     elif w8a16:
@@ -364,33 +387,23 @@ def run_tc_case(args) -> None:
         y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
 
         def launch(i):
-            w = qws[i % 2]
+            w = qws[i % nsets]
             if paired:
                 _lib.call("mrb_qrow_swiglu", x.data_ptr(), m, k, w.data_ptr(), scales.data_ptr(), w[n:].data_ptr(),
-                          scales[n:].data_ptr(), n, y.data_ptr(), None, 0, stream.cuda_stream)
+                          scales[n:].data_ptr(), n, y.data_ptr(), None, 0, _lib.stream_handle(device))
             else:
                 code = _lib.dtype_code(torch.bfloat16)
                 _lib.call("mrb_qrow_matmul", x.data_ptr(), code, m, k, w.data_ptr(), scales.data_ptr(), n, None,
-                          y.data_ptr(), code, None, 0, stream.cuda_stream)
+                          y.data_ptr(), code, None, 0, _lib.stream_handle(device))
     else:
         qx = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=device, generator=gen)
         acc = torch.empty(m, n, dtype=torch.int32, device=device)
 
         def launch(i):
-            _lib.call("mrb_int8_gemm", qx.data_ptr(), qws[i % 2].data_ptr(), m, n, k, acc.data_ptr(),
-                      stream.cuda_stream)
+            _lib.call("mrb_int8_gemm", qx.data_ptr(), qws[i % nsets].data_ptr(), m, n, k, acc.data_ptr(),
+                      _lib.stream_handle(device))
 
-    for i in range(args.warmup):
-        launch(i)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(device)
-    e0.record(stream)
-    for i in range(args.steps):
-        launch(i)
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    avg_s = e0.elapsed_time(e1) / 1000.0 / args.steps
+    avg_s = _graph_avg_seconds(launch, args.steps, args.warmup, device)
     print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "tops": 2 * m * wrows * k / avg_s / 1e12,
                       "weight_gbs": wrows * k / avg_s / 1e9,
                       "kind": "bf16 x bf16 (int8 weights)" if w8a16 else "int8 x int8",
@@ -586,8 +599,8 @@ ATTN_CASES = {
 def run_attn_case(args) -> None:
     """Small case for kernel captures: one layer's paged decode attention at a config-3 or
     config-4 shape (random bf16 K/V pages, ragged contexts from numpy seed 0), timed over
-    back-to-back launches. Prints the device-timed average and the KV bytes read per second;
-    not the bench metric."""
+    back-to-back launches in a CUDA graph. Prints the device-timed average and the KV bytes
+    read per second; not the bench metric."""
     import numpy as np
     import torch
 
@@ -612,21 +625,11 @@ def run_attn_case(args) -> None:
     row_seq = torch.arange(rows, dtype=torch.int32, device=device)
     ws = torch.zeros(max(256, kv.workspace_bytes(rows, hq, cap)), dtype=torch.uint8, device=device)
 
-    def launch():
+    def launch(i):
+        del i
         kv.attend(0, q, row_len, max_total_tokens=cap, row_seq=row_seq, out=out, workspace=ws, scale=d ** -0.5)
 
-    for _ in range(args.warmup):
-        launch()
-    stream = torch.cuda.current_stream(device)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(device)
-    e0.record(stream)
-    for _ in range(args.steps):
-        launch()
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    avg_s = e0.elapsed_time(e1) / 1000.0 / args.steps
+    avg_s = _graph_avg_seconds(launch, args.steps, args.warmup, device)
     kv_bytes = sum(lengths) * 2 * hkv * d * 2
     print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "kv_bytes": kv_bytes,
                       "kv_gbs": kv_bytes / avg_s / 1e9, "launches": args.steps}), flush=True)

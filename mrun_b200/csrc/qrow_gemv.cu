@@ -704,10 +704,11 @@ int qrow_gemm_swiglu_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const in
                           const float* gate_scales, const int8_t* up_codes, const float* up_scales, int64_t n,
                           __nv_bfloat16* y, cudaStream_t s);
 
-// Activation rows above which bf16 projections use the tile GEMM (below it, 16-row GEMV
-// launches stream the weights once per chunk, the second pass mostly from L2).
+// Activation rows above which bf16 projections (and the greedy head) use the tensor-core
+// GEMM: one GEMV launch stages at most 16 activation rows per CTA, and a wider block makes
+// that staging cost more than the weight stream it serves.
 #ifndef MRB_GEMV_MAX_ROWS
-#define MRB_GEMV_MAX_ROWS 32
+#define MRB_GEMV_MAX_ROWS 16
 #endif
 constexpr int64_t GEMV_MAX_ROWS = MRB_GEMV_MAX_ROWS;
 

@@ -21,6 +21,10 @@
 //  * warps 2-5: epilogue, TMEM -> registers -> bf16 rows.
 // Tiles are HALVES 128-row activation accumulators x BN weight rows, chosen by SM fill like
 // the int8 GEMM; persistent CTAs walk tiles with the M tiles of one weight tile adjacent.
+// Skinny activation blocks (17-128 rows) whose tiles fill few SMs split k over the CTAs of a
+// thread-block cluster: each parks its fp32 partial tile in its own shared memory, and after
+// a cluster barrier every CTA sums one column slice over the cluster's partials in rank order
+// through distributed shared memory (deterministic for a given shape) and writes it.
 // Every wait is bounded; on a timeout the CTA records it, stops, and still frees its TMEM.
 // No load uses cluster multicast.
 #include "qrow_common.cuh"
@@ -57,7 +61,10 @@ struct TwTile {
   static_assert(STAGES >= 2, "tile does not fit in shared memory");
   static_assert(SMEM <= TW_SMEM_LIMIT, "tile does not fit in shared memory");
   static_assert(HALVES * BN * NBUF <= 512, "accumulators exceed TMEM");
+  static constexpr int PSTRIDE = BN + 4;  // fp32 row stride of a parked partial (bank spread)
+  static_assert((size_t)TW_HM * PSTRIDE * 4 <= (size_t)STAGES * STAGE_BYTES, "partial tile exceeds the ring");
 };
+constexpr int TW_MAX_CLUSTER = 8;
 
 struct TwGemmArgs {
   CUtensorMap map_x;   // x [m, k] bf16, box [BM rows, 64], 128-byte swizzle
@@ -76,6 +83,7 @@ struct TwGemmArgs {
   unsigned long long* packed;
   float* logits;
   int64_t semantic;
+  int splits, kb_per;  // split-K: k blocks [split * kb_per, +kb_per); splits > 1 = cluster of splits CTAs
 };
 
 __device__ unsigned g_tw_timeouts = 0;
@@ -122,6 +130,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
   pdl_launch_dependents();
 
   const int ntiles = a.tiles_m * a.tiles_n;
+  const int items = ntiles * a.splits;
   auto fail_wait = [&]() {
     *abort_flag = 1;
     atomicAdd(&g_tw_timeouts, 1u);
@@ -135,9 +144,10 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
       pdl_wait();
       int rs = 0;
       unsigned rphase = 0;
-      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
-        const int tn = t / a.tiles_m;
-        for (int kb = 0; kb < a.kblocks; ++kb) {
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+        const int tn = (it / a.splits) / a.tiles_m;
+        const int kb0 = (it % a.splits) * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(raw_empty + rs, rphase ^ 1u)) {
             fail_wait();
             break;
@@ -163,7 +173,9 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
       constexpr uint32_t idesc = umma_idesc(UMMA_D_F32, UMMA_BF16, UMMA_BF16, TW_HM, BN);
       int stage = 0, buf = 0;
       unsigned phase = 0, acc_phase = 0;
-      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+        const int t = it / a.splits;
+        const int kb0 = (it % a.splits) * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
         if (!mbar_wait_bounded(acc_empty + buf, acc_phase ^ 1u)) {
           fail_wait();
           break;
@@ -172,7 +184,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
         int halves = HALVES;
         while (halves > 1 && (int64_t)(t % a.tiles_m) * BM + (halves - 1) * TW_HM >= a.m) --halves;
         bool ok = true;
-        for (int kb = 0; kb < a.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(full + stage, phase)) {
             fail_wait();
             ok = false;
@@ -188,7 +200,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
             for (int h = 0; h < HALVES; ++h)
               if (h < halves)
                 umma_f16(tmem + acc_col(buf, h), umma_desc_k_sw128(sa + h * TW_HM * 128 + kk * TW_UK_BYTES), db,
-                         idesc, kb > 0 || kk > 0);
+                         idesc, kb > kb0 || kk > 0);
           }
           umma_commit(empty + stage);
           if (++stage == STAGES) {
@@ -210,7 +222,8 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
     const int q = warp & 3;
     int buf = 0;
     unsigned acc_phase = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+      const int t = it / a.splits;
       bool ok = !*abort_flag && mbar_wait_bounded(acc_full + buf, acc_phase);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
@@ -219,7 +232,21 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
       }
       tc_fence_after();
       const int tm = t % a.tiles_m, tn = t / a.tiles_m;
-      for (int h = 0; h < HALVES; ++h) {
+      if (a.splits > 1) {
+        // cluster split-K (one work item per CTA, single-half tiles): park this k range's
+        // fp32 partial in shared memory for the reduction after the role loops
+        float* part = reinterpret_cast<float*>(smem) + (q * 32 + lane) * Tile::PSTRIDE;
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + acc_col(buf, 0);
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld_32cols(tbase + (uint32_t)c0, v);
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<uint4*>(part + c0 + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+      }
+      for (int h = 0; h < HALVES && a.splits == 1; ++h) {
         if ((int64_t)tm * BM + h * TW_HM >= a.m) break;
         const int64_t row = (int64_t)tm * BM + h * TW_HM + q * 32 + lane;
         const bool row_ok = row < a.m;
@@ -289,9 +316,10 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
     int stage = 0, rs = 0;
     unsigned phase = 0, rphase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-      const int tm = t % a.tiles_m;
-      for (int kb = 0; kb < a.kblocks; ++kb) {
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      const int tm = (it / a.splits) % a.tiles_m;
+      const int kb0 = (it % a.splits) * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
+      for (int kb = kb0; kb < kb1; ++kb) {
         // waits are made warp-uniform: the warp signals with one lane after __syncwarp
         ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait_bounded(empty + stage, phase ^ 1u));
         if (ok && leader) {
@@ -340,6 +368,64 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
     }
   }
 
+  if (a.splits > 1) {
+    // ---------------- cluster split-K reduction (every thread takes part in both barriers)
+    __syncwarp();
+    cluster_sync_all();  // every CTA of the cluster has parked its partial tile
+    if (warp >= 2 && warp < TW_CVT_WARP0) {
+      const unsigned nsplit = (unsigned)a.splits, rank = cluster_ctarank();
+      const int t = blockIdx.x / a.splits;
+      const int tm = t % a.tiles_m, tn = t / a.tiles_m;
+      const int groups = out_cols / 4;  // 4-column output groups; this CTA reduces [g0, g1)
+      const int g0 = (int)(rank * groups / nsplit), g1 = (int)((rank + 1) * groups / nsplit), ng = g1 - g0;
+      const int64_t rows_left = a.m - (int64_t)tm * BM;
+      const int rows = rows_left < BM ? (int)rows_left : BM;
+      const uint32_t base = smem_u32(smem);
+      for (int unit = tid - 64; unit < rows * ng; unit += TW_EPI_THREADS) {
+        const int r = unit / ng, c = (g0 + unit % ng) * 4;  // tile row, tile-local output column
+        float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (unsigned p = 0; p < (unsigned)TW_MAX_CLUSTER; ++p) {
+          if (p < nsplit) {  // rank order: the same sum on every run
+            const int4 g = ld_shared_cluster_v4(mapa_shared(base + (uint32_t)(r * Tile::PSTRIDE + c) * 4u, p));
+            sg[0] += __int_as_float(g.x); sg[1] += __int_as_float(g.y);
+            sg[2] += __int_as_float(g.z); sg[3] += __int_as_float(g.w);
+            if (a.paired) {
+              const int4 w =
+                  ld_shared_cluster_v4(mapa_shared(base + (uint32_t)(r * Tile::PSTRIDE + BN / 2 + c) * 4u, p));
+              su[0] += __int_as_float(w.x); su[1] += __int_as_float(w.y);
+              su[2] += __int_as_float(w.z); su[3] += __int_as_float(w.w);
+            }
+          }
+        }
+        const int64_t row = (int64_t)tm * BM + r, col0 = (int64_t)tn * out_cols + c;
+        if (col0 >= a.n) continue;
+        __align__(8) __nv_bfloat16 out[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int64_t col = col0 + j < a.n ? col0 + j : a.n - 1;
+          if (a.paired) {
+            const float gv = round_bf16(sg[j] * __ldg(a.scales + col));
+            const float uv = round_bf16(su[j] * __ldg(a.scales_up + col));
+            out[j] = __float2bfloat16_rn(round_bf16(silu_f32(gv)) * uv);
+          } else {
+            float v = sg[j] * __ldg(a.scales + col);
+            if (a.bias) v = round_bf16(v) + round_bf16(__ldg(a.bias + col));
+            out[j] = __float2bfloat16_rn(v);
+          }
+        }
+        __nv_bfloat16* dst = a.y + row * a.n + col0;
+        if (a.vec_store && col0 + 4 <= a.n) {
+          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(out);
+        } else {
+          for (int j = 0; j < 4 && col0 + j < a.n; ++j) dst[j] = out[j];
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // every peer has read this CTA's partial
+  }
+
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -369,12 +455,76 @@ static int tw_launch(TwGemmArgs& a, const __nv_bfloat16* x, const int8_t* codes,
   if (st) return st;
   a.tiles_m = (int)((a.m + Tile::BM - 1) / Tile::BM);
   a.tiles_n = (int)((a.n + wrows - 1) / wrows);
-  const int64_t ntiles = (int64_t)a.tiles_m * a.tiles_n;
-  if (ntiles > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "tc w8a16 gemm: too many tiles");
-  const int grid = (int)std::min<int64_t>(ntiles, num_sms());
-  cudaError_t e = launch_kernel(kern, dim3(grid), dim3(TW_THREADS), Tile::SMEM, s, true, a);
+  const int64_t items = (int64_t)a.tiles_m * a.tiles_n * a.splits;
+  if (items > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "tc w8a16 gemm: too many tiles");
+  cudaError_t e;
+  if (a.splits > 1) {
+    // one work item per CTA, the splits of a tile as one cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)items);
+    cfg.blockDim = dim3(TW_THREADS);
+    cfg.dynamicSmemBytes = Tile::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)a.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a);
+  } else {
+    const int grid = (int)std::min<int64_t>(items, num_sms());
+    e = launch_kernel(kern, dim3(grid), dim3(TW_THREADS), Tile::SMEM, s, true, a);
+  }
   if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc w8a16 gemm: launch: %s", cudaGetErrorString(e));
   return launch_status("tc w8a16 gemm");
+}
+
+// Clusters of `size` 128 x 128-tile CTAs that can be resident at once (0 if none).
+static int tw_cluster_capacity(int size) {
+  static int cached[TW_MAX_CLUSTER + 1] = {};
+  static bool done[TW_MAX_CLUSTER + 1] = {};
+  if (size < 2 || size > TW_MAX_CLUSTER) return 0;
+  if (!done[size]) {
+    using Tile = TwTile<1, 128>;
+    auto kern = tc_w8a16_gemm_kernel<1, 128>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile::SMEM);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(size * 64));
+    cfg.blockDim = dim3(TW_THREADS);
+    cfg.dynamicSmemBytes = Tile::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    cached[size] = n;
+    done[size] = true;
+  }
+  return cached[size];
+}
+
+// Split-K plan for 128 x 128 tiles that leave most SMs idle: the largest cluster size (k
+// ranges of at least 4 k blocks) whose clusters all fit on the GPU at once. 1 = no split.
+static int tw_split_plan(int64_t m, int64_t n, int64_t k, bool paired) {
+  const int64_t out_cols = paired ? 64 : 128;
+  const int64_t tiles = ((m + 127) / 128) * ((n + out_cols - 1) / out_cols);
+  const int64_t kblocks = (k + TW_BKE - 1) / TW_BKE;
+  if (2 * tiles > num_sms() || kblocks < 8) return 1;
+  int best = 1;
+  for (int size = 2; size <= TW_MAX_CLUSTER && 4 * size <= kblocks; ++size)
+    if (tiles <= tw_cluster_capacity(size)) best = size;
+  return best;
 }
 
 // Whether the tensor-core path takes this problem: TMA needs 16-byte aligned bases and row
@@ -400,6 +550,15 @@ int tc_w8a16_gemm(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* co
   a.bias = a.paired ? nullptr : bias;
   a.y = y;
   a.vec_store = (n % 8) == 0 && aligned(y, 16);
+  a.splits = 1;
+  a.kb_per = a.kblocks;
+  const int splits = tw_split_plan(m, n, k, a.paired);
+  if (splits > 1) {
+    a.kb_per = (a.kblocks + splits - 1) / splits;
+    a.splits = (a.kblocks + a.kb_per - 1) / a.kb_per;  // no empty k range
+    if (a.splits > 1) return tw_launch<1, 128>(a, x, codes, up_codes, s);
+    a.kb_per = a.kblocks;
+  }
   const int64_t sms = num_sms();
   const int64_t per_tile = a.paired ? 2 : 1;  // weight rows per output column
   auto tiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n * per_tile + bn - 1) / bn); };
@@ -423,6 +582,8 @@ int tc_w8a16_argmax(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* 
   a.packed = packed;
   a.logits = logits;
   a.semantic = semantic;
+  a.splits = 1;
+  a.kb_per = a.kblocks;
   const int64_t sms = num_sms();
   auto tiles = [&](int bm, int bn) { return ((m + bm - 1) / bm) * ((n + bn - 1) / bn); };
   if (m > 128 && tiles(256, 256) >= 2 * sms) return tw_launch<2, 256>(a, x, codes, nullptr, s);

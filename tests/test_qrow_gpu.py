@@ -178,9 +178,10 @@ def test_argmax_ties_pick_lowest_index(cuda):
     assert idx.cpu().tolist() == [0, 0]
 
 
-@pytest.mark.parametrize("m,n,k,semantic", [(64, 152064, 512, 152000), (40, 3001, 256, 3001), (300, 9000, 128, 8999)])
+@pytest.mark.parametrize("m,n,k,semantic", [(64, 152064, 512, 152000), (40, 3001, 256, 3001), (300, 9000, 128, 8999),
+                                             (32, 151936, 256, 151936)])
 def test_greedy_head_many_rows(m, n, k, semantic, cuda):
-    """Above 32 rows the greedy head runs on the tcgen05 W8A16 GEMM with the argmax fused
+    """Above 16 rows the greedy head runs on the tcgen05 W8A16 GEMM with the argmax fused
     into its epilogue: fp32 logits within 1e-4 of the float64 product and every pick the
     float64 argmax unless the top two are within that error (reported near-tie)."""
     from mrun_b200.dense_qstore_cuda import qrow_argmax
@@ -282,7 +283,13 @@ def _tc_timeouts() -> int:
     (300, 1001, 80),     # ragged rows / columns (scalar stores), k tail inside a 64-wide stage
     (1024, 4736, 512),   # 128 x 256 double-buffered tiles
     (4096, 9472, 64),    # 256 x 256 tiles (two accumulator halves), one k stage
-    (33, 4096, 3584),    # smallest GEMM row count
+    (33, 4096, 3584),
+    # 17-32 rows: k split over a thread-block cluster, partials reduced through distributed
+    # shared memory (config-4 o, qkv and router shapes)
+    (32, 2048, 4096),
+    (32, 5120, 2048),
+    (17, 128, 2048),
+    (24, 1000, 1024),
 ])
 def test_tcgen05_w8a16_gemm(m, n, k, cuda):
     """The tcgen05 W8A16 GEMM (int8 weights converted to bf16 in shared memory, fp32 TMEM
@@ -306,7 +313,7 @@ def test_tcgen05_w8a16_gemm(m, n, k, cuda):
     assert _tc_timeouts() == 0
 
 
-@pytest.mark.parametrize("m,n,k", [(512, 18944, 512), (100, 700, 256), (1024, 2368, 128)])
+@pytest.mark.parametrize("m,n,k", [(512, 18944, 512), (100, 700, 256), (1024, 2368, 128), (32, 700, 1024)])
 def test_tcgen05_w8a16_swiglu(m, n, k, cuda):
     """Paired gate/up tiles (gate rows then up rows in one B operand) with the SwiGLU epilogue."""
     from mrun_b200.dense_qstore_cuda import qrow_swiglu
