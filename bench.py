@@ -635,6 +635,54 @@ def run_attn_case(args) -> None:
                       "kv_gbs": kv_bytes / avg_s / 1e9, "launches": args.steps}), flush=True)
 
 
+EXPERT_CASES = {
+    # name: (experts on this GPU, tokens, top-k) of one config-4 MoE layer's grouped expert
+    # MLP: one GPU (32 tokens x top-8 over 128 experts, ~2 rows per expert) and an EP8 shard
+    # (16 experts receiving 256 assignments, ~16 rows per expert)
+    "experts-ep1": (128, 32, 8),
+    "experts-ep8": (16, 32, 8),
+}
+
+
+def run_expert_case(args) -> None:
+    """Small case for kernel captures: the grouped int8 expert SwiGLU MLP (gate/up then down,
+    two launches) of one config-4 layer, routes from seeded random router logits, several
+    page sets cycled to exceed L2, timed in a CUDA graph. Reports the bytes of the experts
+    that received rows per second; not the bench metric."""
+    import torch
+
+    from mrun_b200.moe import ExpertPageLayout, grouped_expert_mlp, grouped_route_tensors_with_inverse, router_topk
+
+    experts, tokens, k = EXPERT_CASES[args.case]
+    h, f = 2048, 768
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device).manual_seed(0)
+    ly = ExpertPageLayout.create(h, f)
+    sets = max(2, -(-(256 << 20) // (experts * ly.page_stride)))
+    pages = [torch.randint(-127, 128, (experts, ly.page_stride), dtype=torch.int8, device=device,
+                           generator=gen).view(torch.uint8) for _ in range(sets)]
+    for pg in pages:  # sane scales
+        pg.view(torch.uint8)[:, ly.gate_up_scales_offset:ly.gate_up_scales_offset + ly.gate_up_scales_bytes].copy_(
+            torch.full((experts, 2 * f), 1e-3, device=device).view(torch.uint8))
+        pg.view(torch.uint8)[:, ly.down_scales_offset:ly.down_scales_offset + ly.down_scales_bytes].copy_(
+            torch.full((experts, h), 1e-3, device=device).view(torch.uint8))
+    x = torch.randn(tokens, h, device=device, generator=gen).to(torch.bfloat16)
+    idx, w16, _ = router_topk(torch.randn(tokens, experts, device=device, generator=gen), min(k, experts))
+    token_ids, _, starts, counts, _, _ = grouped_route_tensors_with_inverse(idx, w16, num_experts=experts)
+    act = torch.empty(token_ids.numel(), f, dtype=torch.bfloat16, device=device)
+    y = torch.empty(token_ids.numel(), h, dtype=torch.bfloat16, device=device)
+
+    def launch(i):
+        grouped_expert_mlp(x, token_ids, starts, counts, pages[i % sets], ly, act_out=act, out=y)
+
+    avg_s = _graph_avg_seconds(launch, args.steps, args.warmup, device)
+    active = int((counts > 0).sum().item())
+    nbytes = active * ly.page_stride
+    print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "experts_with_rows": active,
+                      "rows": int(token_ids.numel()), "expert_bytes": nbytes, "gbs": nbytes / avg_s / 1e9,
+                      "launches": 2 * args.steps}), flush=True)
+
+
 BATCH_SEQS = 64
 BATCH_NEW_TOKENS = 128
 
@@ -863,7 +911,7 @@ def main() -> None:
     ap.add_argument("--cpu-tokens", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
-                                       *TC_CASES, *ATTN_CASES],
+                                       *TC_CASES, *ATTN_CASES, *EXPERT_CASES],
                     default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
@@ -873,6 +921,8 @@ def main() -> None:
         run_gemv_case(args)
     elif args.case in ATTN_CASES:
         run_attn_case(args)
+    elif args.case in EXPERT_CASES:
+        run_expert_case(args)
     elif args.case in TC_CASES:
         run_tc_case(args)
     elif args.case == "moe-decode":

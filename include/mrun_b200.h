@@ -199,13 +199,15 @@ int mrb_route_compile(const int64_t *top_idx, const float *top_w, int64_t tokens
  * fp32 row scales at scales + slot * scales_stride floats), fp32 accumulation, bf16 output
  * [A, n]. swiglu: the page's rows [0, n) are gate rows and [up_rows, up_rows + n) up rows,
  * and the output is bf16(bf16(silu(bf16 g)) * bf16 u) as the reference forms it.
+ * rows_hint: the total row count A (0 if unknown); with 8 or more rows per expert on
+ * average the kernel stages 16 rows per pass instead of 8 (results are the same either way).
  * Replaces the grouped expert GEMMs of `PagedFP8ExpertBackend.moe`
  * (engine/qwen3_moe_cuda.py:2740-2761), with the int8 qrow codec. */
 int mrb_grouped_qrow(const void *x_bf16, const int64_t *row_ids, const int32_t *starts,
                      const int32_t *counts, int64_t experts, const int8_t *codes,
                      int64_t codes_stride, const float *scales, int64_t scales_stride,
                      const int32_t *slot_of, int64_t n, int64_t k, int64_t up_rows, int swiglu,
-                     void *y_bf16, void *stream);
+                     int64_t rows_hint, void *y_bf16, void *stream);
 
 /* Fixed-capacity expert-parallel dispatch plan (no reference counterpart: the reference
  * runs every expert on one device). Expert e lives on rank e / experts_per_rank. Each

@@ -182,7 +182,7 @@ constexpr int GX_WARPS = 8;
 constexpr int GX_THREADS = GX_WARPS * 32;
 constexpr int GX_ROWS = 16;       // weight rows per warp tile (mma M)
 constexpr int GX_KB = 64;         // k elements per step and stream
-constexpr int GX_MAXR = 8;        // activation rows per pass (one n8 mma tile)
+constexpr int GX_MAXR = 16;       // activation rows per pass (up to two n8 mma tiles)
 constexpr int GX_STAGES = 4;      // cp.async ring depth per thread
 constexpr int GX_STAGE_BYTES = 2 * 2 * GX_THREADS * 16;  // 2 streams x rows (g, g+8) x 16 B per thread
 
@@ -214,14 +214,15 @@ __host__ __device__ inline size_t gx_xs_bytes(int64_t k, bool halves, int maxr) 
   return ((size_t)maxr * (gx_xlen(k, halves) + 8) * 2 + 15) & ~size_t(15);
 }
 __host__ inline size_t gx_smem_bytes(int64_t k, bool halves, int maxr) {
-  return (size_t)GX_STAGES * GX_STAGE_BYTES + gx_xs_bytes(k, halves, maxr) + 32 * 4;
+  return (size_t)GX_STAGES * GX_STAGE_BYTES + gx_xs_bytes(k, halves, maxr) + 64 * 4;  // + rscale[32], rmax[16]
 }
 
 // Grouped int8 expert projection over ragged per-expert row counts.
 //
 // Work item = (expert, chunk of 16-row tiles); a CTA walks items blockIdx.x, +gridDim.x, ...
-// (experts without rows are skipped). Per item and pass of up to maxr rows (8, or fewer when
-// 8 rows of in_features do not fit in shared memory) it stages the
+// (experts without rows are skipped). Per item and pass of up to maxr rows (16 -- two n8 mma
+// tiles sharing every weight fragment, one tile when the pass has 8 rows or fewer -- or fewer
+// rows when they do not fit in shared memory) it stages the
 // expert's activation rows once (gathered through row_ids, exact power-of-two-scaled f16),
 // then each warp owns whole tiles of the chunk: it streams the tile's weights over the full
 // k through a per-thread cp.async ring (rows g and g+8, two streams per step: the gate and
@@ -230,7 +231,7 @@ __host__ inline size_t gx_smem_bytes(int64_t k, bool halves, int maxr) {
 // ring prefetches across tiles, passes and items. Codes convert to exact f16, so each output
 // row depends only on its own activation row (bit-identical for any row grouping, hence
 // across expert-parallel world sizes).
-template <bool SWIGLU>
+template <bool SWIGLU, int NT>  // NT: n8 mma tiles per pass (16-row passes when 2)
 __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs a) {
   constexpr bool HALVES = !SWIGLU;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
   unsigned char* ring = smem;
   __half* xs = reinterpret_cast<__half*>(smem + (size_t)GX_STAGES * GX_STAGE_BYTES);
   float* rscale = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + gx_xs_bytes(K, HALVES, a.maxr));
-  unsigned* rmax = reinterpret_cast<unsigned*>(rscale + 16);  // [8]
+  unsigned* rmax = reinterpret_cast<unsigned*>(rscale + 32);  // [16]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int rtiles = (int)((a.n + GX_ROWS - 1) / GX_ROWS);
@@ -356,10 +357,13 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
           e2 = max(-100, min(100, 15 - ex));  // max * 2^e2 in [2^14, 2^15): exact in f16
         }
         rscale[tid] = ldexpf(1.0f, -e2);
-        rscale[8 + tid] = ldexpf(1.0f, e2);
+        rscale[16 + tid] = ldexpf(1.0f, e2);
       }
       __syncthreads();
-      for (int idx = tid; idx < maxr * (xlen / 8); idx += GX_THREADS) {
+      // pass width: one n8 tile for up to 8 rows, two above (staged rows beyond `rows` are 0)
+      const bool two = NT == 2 && rows > 8;
+      const int prow = two ? maxr : min(8, maxr);
+      for (int idx = tid; idx < prow * (xlen / 8); idx += GX_THREADS) {
         const int r = idx / (xlen / 8), v = idx - r * (xlen / 8);
         uint4* sp = reinterpret_cast<uint4*>(xs + r * xstride + v * 8);
         __align__(16) __half hv[8];
@@ -367,7 +371,7 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
           const uint4 raw = *sp;
           const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(__bfloat162float(h[i]) * rscale[8 + r]);
+          for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(__bfloat162float(h[i]) * rscale[16 + r]);
         } else {
 #pragma unroll
           for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(0.f);
@@ -377,14 +381,17 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
       __syncthreads();
       // ---- this warp's tiles of the chunk
       for (int tile = t0 + warp; tile < t1; tile += GX_WARPS) {
-        float acc[2][4];
+        float acc[2][NT][4];  // [stream][n8 tile][fragment]
 #pragma unroll
         for (int s = 0; s < 2; ++s)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[s][i] = 0.f;
-        // activation row g of the pass (mma column g); columns at or past maxr read the last
-        // staged row and their outputs are dropped in the epilogue
-        const __half* xp = xs + min(g, maxr - 1) * xstride + 16 * c;
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[s][nt][i] = 0.f;
+        // activation rows g and g + 8 of the pass (mma column g of tiles 0 and 1); columns at
+        // or past the staged width read the last staged row and are dropped in the epilogue
+        const __half* xp = xs + min(g, prow - 1) * xstride + 16 * c;
+        const int64_t x1off = (int64_t)(min(g + 8, prow - 1) - min(g, prow - 1)) * xstride;
         for (int ks = 0; ks < nks; ++ks, xp += GX_KB) {
           cp_async_wait_group<GX_STAGES - 2>();
           const unsigned char* st = ring + slot_r * GX_STAGE_BYTES + tid * 16;
@@ -401,6 +408,13 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
             const uint4* p = reinterpret_cast<const uint4*>(xp + (HALVES ? s * kspan : 0));
             const uint4 v0 = p[0], v1 = p[1];
             const uint32_t xb[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+            uint32_t xc[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+            if (NT == 2 && two) {
+              const uint4* p1 = reinterpret_cast<const uint4*>(xp + x1off + (HALVES ? s * kspan : 0));
+              const uint4 u0 = p1[0], u1 = p1[1];
+              xc[0] = u0.x; xc[1] = u0.y; xc[2] = u0.z; xc[3] = u0.w;
+              xc[4] = u1.x; xc[5] = u1.y; xc[6] = u1.z; xc[7] = u1.w;
+            }
             const uint32_t ra[4] = {wa[s].x, wa[s].y, wa[s].z, wa[s].w};
             const uint32_t rb[4] = {wb[s].x, wb[s].y, wb[s].z, wb[s].w};
 #pragma unroll
@@ -408,23 +422,28 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
               uint32_t a_lo, a_hi, b_lo, b_hi;
               i8x4_to_f16x2(ra[j], a_lo, a_hi);
               i8x4_to_f16x2(rb[j], b_lo, b_hi);
-              mma_f16(acc[s], a_lo, b_lo, a_hi, b_hi, xb[2 * j], xb[2 * j + 1]);
+              mma_f16(acc[s][0], a_lo, b_lo, a_hi, b_hi, xb[2 * j], xb[2 * j + 1]);
+              if (NT == 2 && two) mma_f16(acc[s][NT - 1], a_lo, b_lo, a_hi, b_hi, xc[2 * j], xc[2 * j + 1]);
             }
           }
         }
-        // ---- epilogue: lane holds weight rows (g, g+8) x activation rows (2c, 2c+1)
+        // ---- epilogue: lane holds weight rows (g, g+8) x activation rows (nt*8 + 2c, +1)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = 2 * c + (i & 1);
-          const int64_t nrow = (int64_t)tile * GX_ROWS + g + (i >> 1) * 8;
-          if (r >= rows || nrow >= a.n) continue;
-          __nv_bfloat16* out = a.y + (int64_t)(st0 + p0 + r) * a.n + nrow;
-          if (SWIGLU) {
-            const float gt = round_bf16(acc[0][i] * rscale[r] * scales[nrow]);
-            const float up = round_bf16(acc[1][i] * rscale[r] * scales[a.up_rows + nrow]);
-            *out = __float2bfloat16_rn(round_bf16(silu_f32(gt)) * up);
-          } else {
-            *out = __float2bfloat16_rn((acc[0][i] + acc[1][i]) * rscale[r] * scales[nrow]);
+        for (int nt = 0; nt < NT; ++nt) {
+          if (nt == 1 && !two) break;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = nt * 8 + 2 * c + (i & 1);
+            const int64_t nrow = (int64_t)tile * GX_ROWS + g + (i >> 1) * 8;
+            if (r >= rows || nrow >= a.n) continue;
+            __nv_bfloat16* out = a.y + (int64_t)(st0 + p0 + r) * a.n + nrow;
+            if (SWIGLU) {
+              const float gt = round_bf16(acc[0][nt][i] * rscale[r] * scales[nrow]);
+              const float up = round_bf16(acc[1][nt][i] * rscale[r] * scales[a.up_rows + nrow]);
+              *out = __float2bfloat16_rn(round_bf16(silu_f32(gt)) * up);
+            } else {
+              *out = __float2bfloat16_rn((acc[0][nt][i] + acc[1][nt][i]) * rscale[r] * scales[nrow]);
+            }
           }
         }
       }
@@ -563,14 +582,17 @@ extern "C" int mrb_route_compile(const int64_t* top_idx, const float* top_w, int
 extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, const int32_t* starts,
                                 const int32_t* counts, int64_t experts, const int8_t* codes, int64_t codes_stride,
                                 const float* scales, int64_t scales_stride, const int32_t* slot_of, int64_t n,
-                                int64_t k, int64_t up_rows, int swiglu, void* y_bf16, void* stream) {
+                                int64_t k, int64_t up_rows, int swiglu, int64_t rows_hint, void* y_bf16,
+                                void* stream) {
   if (experts <= 0 || n <= 0 || k <= 0) return fail(MRB_ERR_ARG, "grouped_qrow: bad shape");
   if (!x_bf16 || !starts || !counts || !codes || !scales || !y_bf16) return fail(MRB_ERR_ARG, "grouped_qrow: null pointer");
   if (k % 16) return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: in_features %lld is not a multiple of 16", (long long)k);
   if (!aligned(codes, 16) || (codes_stride % 16) || !aligned(x_bf16, 16))
     return fail(MRB_ERR_ARG, "grouped_qrow: codes and activation rows must be 16-byte aligned");
   if (swiglu && up_rows < n) return fail(MRB_ERR_ARG, "grouped_qrow: up rows overlap the gate rows");
-  int maxr = GX_MAXR;  // rows per pass: the most whose staged activations fit next to the ring
+  // rows per pass: 16 (two n8 tiles) when experts average 8 rows or more, else 8, then the
+  // most whose staged activations fit next to the ring
+  int maxr = (rows_hint >= 8 * experts) ? GX_MAXR : GX_MAXR / 2;
   while (maxr > 1 && gx_smem_bytes(k, !swiglu, maxr) > 227 * 1024) maxr /= 2;
   const size_t smem = gx_smem_bytes(k, !swiglu, maxr);
   if (smem > 227 * 1024) return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: in_features %lld too large", (long long)k);
@@ -583,11 +605,14 @@ extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, cons
   const int64_t slots = (int64_t)num_sms() * (2 * (smem + 1024) <= 228 * 1024 ? 2 : 1);
   const int64_t rtiles = (n + GX_ROWS - 1) / GX_ROWS;
   const int64_t per_warp = std::max<int64_t>(1, experts * rtiles / (GX_WARPS * 2 * slots));
-  a.chunk_tiles = (int)std::min<int64_t>(rtiles, per_warp * GX_WARPS);
+  // few experts (an expert-parallel shard): smaller chunks so the items still cover every
+  // CTA slot -- some warps of a CTA idle, but every SM streams weights
+  const int64_t fill = std::max<int64_t>(1, (experts * rtiles + slots - 1) / slots);
+  a.chunk_tiles = (int)std::min<int64_t>(rtiles, std::min<int64_t>(per_warp * GX_WARPS, fill));
   a.chunks = (int)((rtiles + a.chunk_tiles - 1) / a.chunk_tiles);
   const int64_t grid = std::min<int64_t>(experts * a.chunks, slots);
   cudaStream_t s = (cudaStream_t)stream;
-  static size_t configured[2] = {0, 0};  // per kernel instantiation
+  static size_t configured[4] = {0, 0, 0, 0};  // per kernel instantiation
   auto run = [&](auto kern, int which) -> int {
     if (smem > 48 * 1024 && smem > configured[which]) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -597,7 +622,8 @@ extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, cons
     launch_kernel(kern, dim3((unsigned)grid), dim3(GX_THREADS), smem, s, true, a);
     return launch_status("grouped_qrow");
   };
-  return swiglu ? run(grouped_qrow_kernel<true>, 1) : run(grouped_qrow_kernel<false>, 0);
+  if (maxr > 8) return swiglu ? run(grouped_qrow_kernel<true, 2>, 3) : run(grouped_qrow_kernel<false, 2>, 2);
+  return swiglu ? run(grouped_qrow_kernel<true, 1>, 1) : run(grouped_qrow_kernel<false, 1>, 0);
 }
 
 extern "C" int mrb_stable_route_reduce(const void* expert_out_bf16, const float* coef, const int64_t* inverse,

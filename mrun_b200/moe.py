@@ -235,10 +235,10 @@ def grouped_expert_mlp(
     src = source.contiguous()
     _lib.call("mrb_grouped_qrow", src.data_ptr(), token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
               base + ly.gate_up_codes_offset, stride, base + ly.gate_up_scales_offset, stride // 4,
-              _lib.ptr(slot_of), f, h, f, 1, act.data_ptr(), stream)
+              _lib.ptr(slot_of), f, h, f, 1, a, act.data_ptr(), stream)
     _lib.call("mrb_grouped_qrow", act.data_ptr(), None, starts.data_ptr(), counts.data_ptr(), e,
               base + ly.down_codes_offset, stride, base + ly.down_scales_offset, stride // 4,
-              _lib.ptr(slot_of), h, f, 0, 0, y.data_ptr(), stream)
+              _lib.ptr(slot_of), h, f, 0, 0, a, y.data_ptr(), stream)
     return y
 
 
