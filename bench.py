@@ -439,7 +439,7 @@ def run_moe_case(args) -> None:
 
         group = dist.group.WORLD
     dec = MoeDecoder(weights, max_rows=MOE_ROWS, max_seq_len=4096 + total + 16, device=device, group=group,
-                     world=world)
+                     world=world, exchange=args.exchange)
     first = torch.from_numpy(rng.integers(0, cfg.vocab, MOE_ROWS))
     dec.load_synthetic_context(lengths, first, steps=total, seed=rank)
     dec.capture(MOE_ROWS)
@@ -473,13 +473,16 @@ def run_moe_case(args) -> None:
             "config": {"workload": "config4: Qwen3-30B-A3B-shape MoE, 48 layers, 128 experts top-8, "
                                    "32 ragged rows per GPU, contexts U[256,4096]",
                        "rows_per_gpu": MOE_ROWS, "parallelism": f"ep{world}" if world > 1 else "single GPU",
-                       "graph": True, "exchange": "fixed-capacity NCCL all-to-all" if world > 1 else None,
+                       "graph": True,
+                       "exchange": None if world == 1 else (
+                           "fixed-capacity plan over NVLink peer memory" if args.exchange == "p2p"
+                           else "fixed-capacity NCCL all-to-all"),
                        "mean_context": float(np.mean(lengths))},
             "algorithmic_bytes_per_step_per_gpu": {"experts": expert_bytes / world, "kv": kv_bytes},
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
-    dec.graph = None  # a graph holding NCCL calls must go before the process group
+    dec.close()  # the graph (NCCL calls) and the peer mailboxes go before the process group
     torch.cuda.synchronize(device)
     if world > 1:
         import torch.distributed as dist
@@ -909,6 +912,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-tokens", type=int, default=2)
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="moe-decode on N GPUs: expert exchange over NVLink peer memory or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
                                        *TC_CASES, *ATTN_CASES, *EXPERT_CASES],

@@ -236,6 +236,39 @@ int mrb_stable_route_reduce(const void *expert_out_bf16, const float *coef, cons
                             int64_t tokens, int64_t k, int64_t hidden, float *out_f32,
                             void *out_bf16, void *stream);
 
+/* Expert-parallel exchange over NVLink peer memory (no counterpart in the reference, which
+ * runs every expert on one device; an alternative to the NCCL all-to-all of the same
+ * fixed-capacity plan). Each rank owns one mailbox of mrb_ep_mailbox_bytes(world,
+ * capacity, hidden) bytes; mrb_ep_mailbox_create allocates and zeroes it and returns its
+ * 64-byte CUDA IPC handle, mrb_ep_mailbox_open maps a peer's handle (another process on the
+ * same node), mrb_ep_mailbox_close unmaps (owned = 0) or frees (owned = 1).
+ * mrb_ep_mailbox_offsets gives the byte offsets of its six sections: dispatch flags,
+ * return flags, counts, ids (int32 [world, capacity]), rows and back rows (bf16
+ * [world * capacity, hidden]). `mailboxes` is a device array of the world mailbox pointers
+ * (this rank's own at index rank); `state` is int32[4] of zeros owned by the caller per
+ * exchange site ([3] becomes 1 if a bounded wait timed out: outputs are then invalid).
+ * Per use: mrb_ep_pack (the plan) -> mrb_ep_p2p_dispatch (real rows into each destination's
+ * mailbox, then release flags) -> mrb_ep_p2p_wait_dispatch (acquire every source's flag;
+ * ids64 = received local expert ids, unused slots = dummy_expert) -> route + grouped MLP on
+ * the mailbox rows -> mrb_ep_p2p_return (outputs into each source's back rows, then flags)
+ * -> mrb_ep_p2p_wait_return -> mrb_stable_route_reduce on the back rows. Every rank must run
+ * the same sequence (one process per GPU); waits are bounded. */
+size_t mrb_ep_mailbox_bytes(int64_t world, int64_t capacity, int64_t hidden);
+int mrb_ep_mailbox_offsets(int64_t world, int64_t capacity, int64_t hidden, int64_t *out6);
+int mrb_ep_mailbox_create(size_t bytes, void **ptr, void *ipc_handle);
+int mrb_ep_mailbox_open(const void *ipc_handle, void **ptr);
+int mrb_ep_mailbox_close(void *ptr, int owned);
+int mrb_ep_p2p_dispatch(const void *x_bf16, int64_t hidden, const int32_t *slot_src,
+                        const int32_t *send_expert, int64_t world, int64_t rank, int64_t capacity,
+                        void *const *mailboxes, int32_t *state, void *stream);
+int mrb_ep_p2p_wait_dispatch(void *mailbox, int64_t world, int64_t capacity, int64_t hidden,
+                             int32_t dummy_expert, int64_t *ids64, int32_t *state, void *stream);
+int mrb_ep_p2p_return(const void *eo_bf16, const int64_t *inverse, int64_t hidden, int64_t world,
+                      int64_t rank, int64_t capacity, void *const *mailboxes, int32_t *state,
+                      void *stream);
+int mrb_ep_p2p_wait_return(void *mailbox, int64_t world, int64_t capacity, int64_t hidden,
+                           int32_t *state, void *stream);
+
 /* ---------------------------------------------------------------- (c) paged-KV decode attention */
 
 /* RoPE (rotate-half, fp32 products rounded separately, then bf16) for the queries and keys of

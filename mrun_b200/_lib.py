@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import c_float, c_int, c_int64, c_size_t, c_void_p
+from ctypes import c_int32, c_float, c_int, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
 import torch
@@ -62,9 +62,19 @@ SIGNATURES: dict[str, list] = {
     "mrb_decode_advance": [_P, _P, _P, _P, _I64, _P],
     "mrb_copy_pages": [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _P],
     "mrb_w8a8_linear_bf16": [_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P],
+    "mrb_ep_mailbox_bytes": [_I64, _I64, _I64],
+    "mrb_ep_mailbox_offsets": [_I64, _I64, _I64, _P],
+    "mrb_ep_mailbox_create": [c_size_t, _P, _P],
+    "mrb_ep_mailbox_open": [_P, _P],
+    "mrb_ep_mailbox_close": [_P, c_int],
+    "mrb_ep_p2p_dispatch": [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _P],
+    "mrb_ep_p2p_wait_dispatch": [_P, _I64, _I64, _I64, c_int32, _P, _P, _P],
+    "mrb_ep_p2p_return": [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _P],
+    "mrb_ep_p2p_wait_return": [_P, _I64, _I64, _I64, _P, _P],
 }
 _RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t,
-             "mrb_paged_attention_static_capacity": c_size_t, "mrb_qrow_workspace": c_size_t}
+             "mrb_paged_attention_static_capacity": c_size_t, "mrb_qrow_workspace": c_size_t,
+             "mrb_ep_mailbox_bytes": c_size_t}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

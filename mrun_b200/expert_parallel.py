@@ -178,6 +178,139 @@ class FixedCapacityExpertParallelMoE:
         return out
 
 
+class P2PExpertParallelMoE:
+    """The fixed-capacity plan exchanged over NVLink peer memory instead of NCCL: each rank owns
+    a mailbox (CUDA IPC-mapped into every peer); the dispatch kernel stores only the real rows
+    straight into their owners' mailboxes and release-publishes a per-exchange epoch flag, the
+    owner acquires every source's flag (bounded wait), runs the grouped int8 MLP on the rows
+    in place and stores the outputs straight back into the sources' mailboxes, and the source
+    combines in route-rank order once every owner's flag has arrived. Results are
+    bit-identical to one GPU and to the NCCL exchange. One instance per call site (each MoE
+    layer) and per process group; every rank must call forward in the same order. ``close()``
+    unmaps the peers' mailboxes and frees this rank's (after the last use, before the process
+    group goes away)."""
+
+    def __init__(self, shard: ExpertShard, pages: torch.Tensor, layout, *, tokens: int, k: int, hidden: int,
+                 group=None) -> None:
+        import ctypes
+
+        from . import _lib
+
+        self.shard = shard
+        self.pages = pages
+        self.layout = layout
+        self.group = group
+        self.tokens, self.k, self.hidden = int(tokens), int(k), int(hidden)
+        device = pages.device
+        self.device = device
+        world, rank = shard.world, shard.rank
+        self.cap = self.tokens * self.k
+        slots = world * self.cap
+        lib = _lib.load()
+        nbytes = int(lib.mrb_ep_mailbox_bytes(world, self.cap, self.hidden))
+        offsets = (ctypes.c_int64 * 6)()
+        _lib.call("mrb_ep_mailbox_offsets", world, self.cap, self.hidden, offsets)
+        self.offsets = list(offsets)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        _lib.call("mrb_ep_mailbox_create", nbytes, ctypes.byref(own), handle)
+        self._own = own.value
+        self._peers: list[int] = []
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+        everyone = torch.empty(world * 64, dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(everyone, mine, group=group)
+        handles = everyone.cpu().numpy().reshape(world, 64)
+        ptrs = []
+        for r in range(world):
+            if r == rank:
+                ptrs.append(self._own)
+                continue
+            peer = ctypes.c_void_p()
+            h = (ctypes.c_ubyte * 64).from_buffer_copy(handles[r].tobytes())
+            _lib.call("mrb_ep_mailbox_open", h, ctypes.byref(peer))
+            self._peers.append(peer.value)
+            ptrs.append(peer.value)
+        self.mailboxes = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.state = torch.zeros(4, dtype=torch.int32, device=device)
+        # the plan and receive-side buffers live as long as the instance (graph friendly)
+        self.send_expert = torch.empty(slots, dtype=torch.int32, device=device)
+        self.coef_slot = torch.empty(slots, dtype=torch.float32, device=device)
+        self.slot_of_assign = torch.empty(self.cap, dtype=torch.int64, device=device)
+        self.slot_src = torch.empty(slots, dtype=torch.int32, device=device)
+        self.ids64 = torch.empty((slots, 1), dtype=torch.int64, device=device)
+        self.zeros = torch.zeros((slots, 1), dtype=torch.float32, device=device)
+        dist.barrier(group=group)  # every mailbox exists and is zeroed before any dispatch
+
+    def forward(self, source: torch.Tensor, top_indices: torch.Tensor, top_weights: torch.Tensor) -> torch.Tensor:
+        from . import _lib
+        from .moe import grouped_route_tensors_with_inverse
+
+        sh = self.shard
+        t, k = (int(v) for v in top_indices.shape)
+        if t > self.tokens or k != self.k or int(source.shape[1]) != self.hidden:
+            raise ValueError("P2P expert exchange was sized for a smaller batch")
+        device = source.device
+        world, per, cap, hidden = sh.world, sh.per_rank, self.cap, self.hidden
+        slots = world * cap
+        stream = _lib.stream_handle(device)
+        idx = top_indices.to(torch.int64).contiguous()
+        w32 = top_weights.float().contiguous()
+        _lib.call("mrb_ep_pack", idx.data_ptr(), w32.data_ptr(), t, k, per, world, cap, self.send_expert.data_ptr(),
+                  self.coef_slot.data_ptr(), self.slot_of_assign.data_ptr(), self.slot_src.data_ptr(), None, stream)
+        src = source.contiguous()
+        _lib.call("mrb_ep_p2p_dispatch", src.data_ptr(), hidden, self.slot_src.data_ptr(), self.send_expert.data_ptr(),
+                  world, sh.rank, cap, self.mailboxes.data_ptr(), self.state.data_ptr(), stream)
+        _lib.call("mrb_ep_p2p_wait_dispatch", self._own, world, cap, hidden, per, self.ids64.data_ptr(),
+                  self.state.data_ptr(), stream)
+        token_ids, _, starts, counts, inverse, _ = grouped_route_tensors_with_inverse(
+            self.ids64, self.zeros, num_experts=per + 1)
+        eo = _grouped_mlp_from_pointer(self._own + self.offsets[4], token_ids, starts[:per], counts[:per],
+                                       self.pages, self.layout, hidden, device)
+        _lib.call("mrb_ep_p2p_return", eo.data_ptr(), inverse.data_ptr(), hidden, world, sh.rank, cap,
+                  self.mailboxes.data_ptr(), self.state.data_ptr(), stream)
+        _lib.call("mrb_ep_p2p_wait_return", self._own, world, cap, hidden, self.state.data_ptr(), stream)
+        out = torch.empty((t, hidden), dtype=torch.bfloat16, device=device)
+        _lib.call("mrb_stable_route_reduce", self._own + self.offsets[5], self.coef_slot.data_ptr(),
+                  self.slot_of_assign.data_ptr(), t, k, hidden, None, out.data_ptr(), stream)
+        return out
+
+    def check(self) -> None:
+        """Raise if a bounded wait of the exchange timed out (synchronises)."""
+        if int(self.state[3].item()):
+            raise RuntimeError("expert-parallel peer exchange timed out waiting for a rank")
+
+    def close(self) -> None:
+        from . import _lib
+
+        for p in self._peers:
+            _lib.call("mrb_ep_mailbox_close", p, 0)
+        self._peers = []
+        if self._own:
+            _lib.call("mrb_ep_mailbox_close", self._own, 1)
+            self._own = 0
+
+
+def _grouped_mlp_from_pointer(rows_ptr: int, token_ids, starts, counts, pages, layout, hidden: int, device):
+    """grouped_expert_mlp over activation rows given by a raw device pointer (a mailbox)."""
+    from . import _lib
+
+    ly = layout
+    f = ly.intermediate_size
+    a = int(token_ids.numel())
+    e = int(counts.numel())
+    act = torch.empty((a, f), dtype=torch.bfloat16, device=device)
+    y = torch.empty((a, hidden), dtype=torch.bfloat16, device=device)
+    base, stride = pages.data_ptr(), ly.page_stride
+    stream = _lib.stream_handle(device)
+    _lib.call("mrb_grouped_qrow", rows_ptr, token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
+              base + ly.gate_up_codes_offset, stride, base + ly.gate_up_scales_offset, stride // 4, None, f, hidden,
+              f, 1, a, act.data_ptr(), stream)
+    _lib.call("mrb_grouped_qrow", act.data_ptr(), None, starts.data_ptr(), counts.data_ptr(), e,
+              base + ly.down_codes_offset, stride, base + ly.down_scales_offset, stride // 4, None, hidden, f, 0, 0,
+              a, y.data_ptr(), stream)
+    return y
+
+
 def torch_combine(rows: torch.Tensor, coef: torch.Tensor, inverse: torch.Tensor, t: int, k: int) -> torch.Tensor:
     """out[t] = sum_r coef[p] * rows[p], p = inverse[t*k + r]: fp32 products added in rank order."""
     per = rows.index_select(0, inverse).reshape(t, k, -1).float()
@@ -215,6 +348,7 @@ def local_expert_mlp_fn(pages: torch.Tensor, layout, experts_per_rank: int):
 __all__ = [
     "ExpertParallelMoE",
     "FixedCapacityExpertParallelMoE",
+    "P2PExpertParallelMoE",
     "ExpertShard",
     "local_expert_mlp_fn",
     "native_combine",

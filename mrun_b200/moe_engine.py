@@ -10,8 +10,10 @@ head, embedding) is an int8 qrow matrix; expert weights are int8 qrow pages.
 
 The whole step is captured in a CUDA graph (no host synchronisation inside). With a process
 group of N ranks the experts are sharded (rank r owns experts [r*E/N, (r+1)*E/N)) and each
-layer's MoE runs through ``FixedCapacityExpertParallelMoE`` (fixed-size NCCL all-to-all, so
-the exchange is captured with the rest of the step); every rank decodes its own rows
+layer's MoE runs through ``P2PExpertParallelMoE`` (real rows stored straight into the owners'
+peer-mapped mailboxes over NVLink, epoch flags with bounded waits) or, with
+``exchange="nccl"``, ``FixedCapacityExpertParallelMoE`` (fixed-size NCCL all-to-all); both are
+captured with the rest of the step. Every rank decodes its own rows
 (data-parallel attention), so per-GPU work stays fixed as N grows.
 """
 from __future__ import annotations
@@ -25,7 +27,7 @@ import torch
 from . import _lib
 from .dense_engine import QRow, rope_tables
 from .dense_qstore_cuda import qrow_argmax, qrow_linear, qrow_workspace_bytes, residual_rms_norm_into, rms_norm_into
-from .expert_parallel import ExpertShard, FixedCapacityExpertParallelMoE
+from .expert_parallel import ExpertShard, FixedCapacityExpertParallelMoE, P2PExpertParallelMoE
 from .moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_topk
 from .paged_kv import PagedKVCache
 from .qstore_build import embed_rows
@@ -158,7 +160,7 @@ class MoeDecoder:
     """Ragged continuous-batch greedy decode over a paged KV cache (one token per row per step)."""
 
     def __init__(self, weights: MoeWeights, *, max_rows: int, max_seq_len: int, device: torch.device,
-                 group=None, world: int = 1) -> None:
+                 group=None, world: int = 1, exchange: str = "p2p") -> None:
         cfg = weights.cfg
         self.w = weights
         self.cfg = cfg
@@ -196,8 +198,14 @@ class MoeDecoder:
         self.group = group
         if self.world > 1:
             shard = ExpertShard(self.world, torch.distributed.get_rank(group), cfg.experts)
-            self.ep = [FixedCapacityExpertParallelMoE(shard, L.pages, weights.layout, group=group)
-                       for L in weights.layers]
+            if exchange not in ("p2p", "nccl"):
+                raise ValueError(f"unknown expert exchange {exchange!r}")
+            if exchange == "p2p":
+                self.ep = [P2PExpertParallelMoE(shard, L.pages, weights.layout, tokens=self.max_rows, k=cfg.top_k,
+                                                hidden=cfg.hidden, group=group) for L in weights.layers]
+            else:
+                self.ep = [FixedCapacityExpertParallelMoE(shard, L.pages, weights.layout, group=group)
+                           for L in weights.layers]
             self.backend = None
         else:
             self.ep = None
@@ -300,6 +308,18 @@ class MoeDecoder:
     def check_errors(self) -> None:
         if int(self.error_flag.item()):
             raise RuntimeError("KV append saw a position outside the mapped pages")
+        for ep in self.ep or []:
+            if hasattr(ep, "check"):
+                ep.check()
+
+    def close(self) -> None:
+        """Release the captured graph and the peer mailboxes of the expert exchange (call on
+        every rank before the process group is destroyed)."""
+        self.graph = None
+        for ep in self.ep or []:
+            if hasattr(ep, "close"):
+                torch.cuda.synchronize(self.device)
+                ep.close()
 
     def gather_kv(self, layer: int, row: int, length: int) -> tuple[np.ndarray, np.ndarray]:
         """Committed K/V of one row as float arrays [length, Hkv, D] (test support)."""

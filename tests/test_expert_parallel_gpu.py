@@ -1,7 +1,7 @@
-"""Expert parallelism on 2+ GPUs (NCCL all-to-all over NVLink): each rank's MoE output must
-be bit-identical to the single-GPU backend over all experts, for the host-sized exchange and
-for the fixed-capacity exchange both eagerly and replayed from a CUDA graph. Skipped with
-fewer than 2 GPUs."""
+"""Expert parallelism on 2+ GPUs: each rank's MoE output must be bit-identical to the
+single-GPU backend over all experts, for the host-sized NCCL exchange, the fixed-capacity NCCL
+exchange (eager and replayed from a CUDA graph) and the fixed-capacity exchange over NVLink
+peer memory (eager and graph-replayed, no wait timed out). Skipped with fewer than 2 GPUs."""
 from __future__ import annotations
 
 import datetime
@@ -27,8 +27,8 @@ def _worker(rank, world, port, q):
     import torch.distributed as dist
 
     from mrun_b200.expert_parallel import (
-        ExpertParallelMoE, ExpertShard, FixedCapacityExpertParallelMoE, local_expert_mlp_fn, native_combine,
-        native_planner,
+        ExpertParallelMoE, ExpertShard, FixedCapacityExpertParallelMoE, P2PExpertParallelMoE, local_expert_mlp_fn,
+        native_combine, native_planner,
     )
     from mrun_b200.moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, pack_expert_page, router_topk
     from oracle import qrow as oq
@@ -72,6 +72,26 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         ok = bool(torch.equal(out, single) and torch.equal(out_fixed, single) and torch.equal(out_graph, single))
         del graph  # before the process group goes away
+        # the same plan over NVLink peer memory (mailboxes), eager twice and graph-replayed twice
+        p2p = P2PExpertParallelMoE(shard, mine, ly, tokens=T, k=K, hidden=H)
+        outs = [p2p.forward(x, idx, w) for _ in range(2)]
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            p2p.forward(x, idx, w)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            out_p2p_graph = p2p.forward(x, idx, w)
+        for _ in range(2):
+            graph.replay()
+            torch.cuda.synchronize()
+            outs.append(out_p2p_graph.clone())
+        p2p.check()
+        ok = ok and all(bool(torch.equal(o, single)) for o in outs)
+        del graph
+        dist.barrier()
+        p2p.close()
         q.put((rank, ok, ep.last_stats))
         dist.barrier()
     finally:
