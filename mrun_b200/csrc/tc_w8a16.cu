@@ -11,11 +11,13 @@
 //  * warp 0, one thread: TMA producer of the raw int8 weight boxes ([BN x 64 B], no swizzle;
 //    the gate and up halves as two boxes when paired) into a ring of its own, running ahead
 //    of the conversion;
-//  * warps 6-13 (256 threads): converters. Per stage they wait for the stage to be free,
-//    one elected thread issues the activation TMA ([BM x 64 bf16], 128-byte swizzle), and
-//    all of them turn the raw int8 box into bf16 rows in the 128-byte-swizzled K-major
-//    layout the MMA descriptor reads (chunk c of row r at c ^ (r & 7)), fence the writes to
-//    the async proxy and arrive on the stage barrier (one arrival per warp);
+//  * warp 6, one thread: TMA producer of the activation boxes ([BM x 64 bf16], 128-byte
+//    swizzle) into the activation ring;
+//  * warps 7-14 (256 threads): converters. Per stage they wait for a raw box and a free
+//    converted-weight stage, turn the raw int8 box into bf16 rows in the 128-byte-swizzled
+//    K-major layout the MMA descriptor reads (chunk c of row r at c ^ (r & 7)), fence the
+//    writes to the async proxy and arrive on the stage barrier (one arrival per warp);
+//    the three rings (activations, raw weights, converted weights) run ahead independently;
 //  * warp 1: TMEM owner; one thread issues tcgen05.mma (M=128 per accumulator half, N=BN,
 //    K=16) and commits stages and finished tiles;
 //  * warps 2-5: epilogue, TMEM -> registers -> bf16 rows.
@@ -37,7 +39,8 @@ namespace mrb {
 constexpr int TW_HM = 128;            // MMA M (activation rows of one accumulator)
 constexpr int TW_BKE = 64;            // k elements per stage: one 128-byte bf16 swizzle row
 constexpr int TW_UK_BYTES = 32;       // k bytes per MMA (16 bf16)
-constexpr int TW_CVT_WARP0 = 6;       // first converter warp
+constexpr int TW_A_WARP = 6;          // activation TMA producer warp
+constexpr int TW_CVT_WARP0 = 7;       // first converter warp
 constexpr int TW_CVT_THREADS = 256;   // 8 converter warps
 constexpr int TW_CVT_WARPS = TW_CVT_THREADS / 32;
 constexpr int TW_EPI_THREADS = 128;
@@ -50,19 +53,19 @@ struct TwTile {
   static constexpr int A_BYTES = BM * 128;   // bf16 activations [BM x 64]
   static constexpr int B_BYTES = BN * 128;   // converted bf16 weights [BN x 64]
   static constexpr int RAW_BYTES = BN * 64;  // int8 weights [BN x 64]
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int RAW_STAGES = HALVES == 2 ? 2 : 4;
-  static constexpr size_t FIXED = 1024 + 512 + (size_t)RAW_STAGES * RAW_BYTES;
-  static constexpr int STAGES_FIT = (int)((TW_SMEM_LIMIT - FIXED) / STAGE_BYTES);
-  static constexpr int STAGES = STAGES_FIT < 6 ? STAGES_FIT : 6;
+  // ring depths: activations, converted weights, raw weights (about 224 KB in all)
+  static constexpr int A_STAGES = HALVES == 2 ? 3 : (BN == 256 ? 4 : 6);
+  static constexpr int B_STAGES = HALVES == 2 ? 2 : (BN == 256 ? 2 : 3);
+  static constexpr int RAW_STAGES = HALVES == 2 ? 4 : (BN == 256 ? 6 : 8);
+  static constexpr size_t RING_AB = (size_t)A_STAGES * A_BYTES + (size_t)B_STAGES * B_BYTES;
   static constexpr int NBUF = HALVES == 1 ? 2 : 1;
   static constexpr unsigned TMEM_COLS = HALVES * BN * NBUF <= 256 ? 256u : 512u;
-  static constexpr size_t SMEM = FIXED + (size_t)STAGES * STAGE_BYTES;
-  static_assert(STAGES >= 2, "tile does not fit in shared memory");
+  static constexpr size_t SMEM = 1024 + RING_AB + (size_t)RAW_STAGES * RAW_BYTES + 512;
   static_assert(SMEM <= TW_SMEM_LIMIT, "tile does not fit in shared memory");
   static_assert(HALVES * BN * NBUF <= 512, "accumulators exceed TMEM");
   static constexpr int PSTRIDE = BN + 4;  // fp32 row stride of a parked partial (bank spread)
-  static_assert((size_t)TW_HM * PSTRIDE * 4 <= (size_t)STAGES * STAGE_BYTES, "partial tile exceeds the ring");
+  // a split-K partial is parked over the rings (all three are idle by then)
+  static_assert((size_t)TW_HM * PSTRIDE * 4 <= RING_AB + (size_t)RAW_STAGES * RAW_BYTES, "partial exceeds the rings");
 };
 constexpr int TW_MAX_CLUSTER = 8;
 
@@ -91,14 +94,19 @@ __device__ unsigned g_tw_timeouts = 0;
 template <int HALVES, int BN>
 __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __grid_constant__ TwGemmArgs a) {
   using Tile = TwTile<HALVES, BN>;
-  constexpr int STAGES = Tile::STAGES, RAW_STAGES = Tile::RAW_STAGES, NBUF = Tile::NBUF, BM = Tile::BM;
+  constexpr int A_STAGES = Tile::A_STAGES, B_STAGES = Tile::B_STAGES, RAW_STAGES = Tile::RAW_STAGES;
+  constexpr int NBUF = Tile::NBUF, BM = Tile::BM;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* raw_base = smem + STAGES * Tile::STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(raw_base + RAW_STAGES * Tile::RAW_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* raw_full = empty + STAGES;
+  unsigned char* a_base = smem;                                         // activation ring
+  unsigned char* b_base = smem + (size_t)A_STAGES * Tile::A_BYTES;      // converted-weight ring
+  unsigned char* raw_base = smem + Tile::RING_AB;                       // raw int8 ring
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(raw_base + RAW_STAGES * Tile::RAW_BYTES);
+  uint64_t* a_empty = a_full + A_STAGES;
+  uint64_t* b_full = a_empty + A_STAGES;
+  uint64_t* b_empty = b_full + B_STAGES;
+  uint64_t* raw_full = b_empty + B_STAGES;
   uint64_t* raw_empty = raw_full + RAW_STAGES;
   uint64_t* acc_full = raw_empty + RAW_STAGES;
   uint64_t* acc_empty = acc_full + NBUF;
@@ -107,9 +115,13 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full + s, 1 + TW_CVT_WARPS);  // activation TMA (expect_tx) + one per converter warp
-      mbar_init(empty + s, 1);
+    for (int s = 0; s < A_STAGES; ++s) {
+      mbar_init(a_full + s, 1);  // the activation TMA (expect_tx)
+      mbar_init(a_empty + s, 1);
+    }
+    for (int s = 0; s < B_STAGES; ++s) {
+      mbar_init(b_full + s, TW_CVT_WARPS);  // one arrival per converter warp
+      mbar_init(b_empty + s, 1);
     }
     for (int s = 0; s < RAW_STAGES; ++s) {
       mbar_init(raw_full + s, 1);
@@ -171,8 +183,8 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
     // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(UMMA_D_F32, UMMA_BF16, UMMA_BF16, TW_HM, BN);
-      int stage = 0, buf = 0;
-      unsigned phase = 0, acc_phase = 0;
+      int as = 0, bs = 0, buf = 0;
+      unsigned aphase = 0, bphase = 0, acc_phase = 0;
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
         const int t = it / a.splits;
         const int kb0 = (it % a.splits) * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
@@ -185,14 +197,14 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
         while (halves > 1 && (int64_t)(t % a.tiles_m) * BM + (halves - 1) * TW_HM >= a.m) --halves;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait_bounded(full + stage, phase)) {
+          if (!mbar_wait_bounded(a_full + as, aphase) || !mbar_wait_bounded(b_full + bs, bphase)) {
             fail_wait();
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * Tile::STAGE_BYTES);
-          const uint32_t sb = sa + Tile::A_BYTES;
+          const uint32_t sa = smem_u32(a_base + as * Tile::A_BYTES);
+          const uint32_t sb = smem_u32(b_base + bs * Tile::B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 128 / TW_UK_BYTES; ++kk) {
             const uint64_t db = umma_desc_k_sw128(sb + kk * TW_UK_BYTES);
@@ -202,10 +214,15 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
                 umma_f16(tmem + acc_col(buf, h), umma_desc_k_sw128(sa + h * TW_HM * 128 + kk * TW_UK_BYTES), db,
                          idesc, kb > kb0 || kk > 0);
           }
-          umma_commit(empty + stage);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+          umma_commit(a_empty + as);  // both stages are free once these MMAs have read them
+          umma_commit(b_empty + bs);
+          if (++as == A_STAGES) {
+            as = 0;
+            aphase ^= 1u;
+          }
+          if (++bs == B_STAGES) {
+            bs = 0;
+            bphase ^= 1u;
           }
         }
         if (!ok) break;
@@ -216,7 +233,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
         }
       }
     }
-  } else if (warp < TW_CVT_WARP0) {
+  } else if (warp < TW_A_WARP) {
     // ---------------- epilogue
     pdl_wait();
     const int q = warp & 3;
@@ -308,32 +325,47 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
         acc_phase ^= 1u;
       }
     }
+  } else if (warp == TW_A_WARP) {
+    // ---------------- activation TMA producer
+    if (lane == 0) {
+      pdl_wait();  // the activations come from the previous kernel
+      int as = 0;
+      unsigned aphase = 0;
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+        const int tm = (it / a.splits) % a.tiles_m;
+        const int kb0 = (it % a.splits) * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(a_empty + as, aphase ^ 1u)) {
+            fail_wait();
+            break;
+          }
+          mbar_arrive_expect_tx(a_full + as, Tile::A_BYTES);
+          tma_load_2d(a_base + as * Tile::A_BYTES, &a.map_x, kb * TW_BKE, tm * BM, a_full + as);
+          if (++as == A_STAGES) {
+            as = 0;
+            aphase ^= 1u;
+          }
+        }
+      }
+    }
   } else {
     // ---------------- converters: int8 raw box -> swizzled bf16 B operand
     const int ct = tid - TW_CVT_WARP0 * 32;
-    const bool leader = ct == 0;
-    if (leader) pdl_wait();  // the activations come from the previous kernel
-    int stage = 0, rs = 0;
-    unsigned phase = 0, rphase = 0;
+    int bs = 0, rs = 0;
+    unsigned bphase = 0, rphase = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-      const int tm = (it / a.splits) % a.tiles_m;
       const int kb0 = (it % a.splits) * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
       for (int kb = kb0; kb < kb1; ++kb) {
         // waits are made warp-uniform: the warp signals with one lane after __syncwarp
-        ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait_bounded(empty + stage, phase ^ 1u));
-        if (ok && leader) {
-          unsigned char* st = smem + stage * Tile::STAGE_BYTES;
-          mbar_arrive_expect_tx(full + stage, Tile::A_BYTES);
-          tma_load_2d(st, &a.map_x, kb * TW_BKE, tm * BM, full + stage);
-        }
+        ok = __all_sync(0xffffffffu, !*abort_flag && mbar_wait_bounded(b_empty + bs, bphase ^ 1u));
         ok = __all_sync(0xffffffffu, ok && mbar_wait_bounded(raw_full + rs, rphase));
         if (!ok) {
           if (lane == 0 && !*abort_flag) fail_wait();
           break;
         }
         const unsigned char* raw = raw_base + rs * Tile::RAW_BYTES;
-        unsigned char* dst = smem + stage * Tile::STAGE_BYTES + Tile::A_BYTES;
+        unsigned char* dst = b_base + bs * Tile::B_BYTES;
 #pragma unroll
         for (int j = 0; j < BN * 4 / TW_CVT_THREADS; ++j) {
           const int i = ct + j * TW_CVT_THREADS;  // 16-byte chunk of the raw box
@@ -354,15 +386,15 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(raw_empty + rs);
-          mbar_arrive(full + stage);
+          mbar_arrive(b_full + bs);
         }
         if (++rs == RAW_STAGES) {
           rs = 0;
           rphase ^= 1u;
         }
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
+        if (++bs == B_STAGES) {
+          bs = 0;
+          bphase ^= 1u;
         }
       }
     }
@@ -372,7 +404,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1) tc_w8a16_gemm_kernel(const __gr
     // ---------------- cluster split-K reduction (every thread takes part in both barriers)
     __syncwarp();
     cluster_sync_all();  // every CTA of the cluster has parked its partial tile
-    if (warp >= 2 && warp < TW_CVT_WARP0) {
+    if (warp >= 2 && warp < TW_A_WARP) {
       const unsigned nsplit = (unsigned)a.splits, rank = cluster_ctarank();
       const int t = blockIdx.x / a.splits;
       const int tm = t % a.tiles_m, tn = t / a.tiles_m;
