@@ -295,6 +295,35 @@ int mrb_rope_kv_append(const void *q_in, const void *k_in, const void *v_in, int
                        int64_t num_pages, int32_t *error_flag, const void *q_norm,
                        const void *k_norm, float norm_eps, void *stream);
 
+/* One decode token per query row in one launch: mrb_rope_kv_append's RoPE (and optional
+ * q/k norm) of the row's query heads and key, its K/V append at position positions[r] of
+ * block-table row row_seq[r] (NULL: r), and mrb_paged_attention over tokens
+ * [0, positions[r]] -- the cached ones plus the new one -- written to out (bf16
+ * [rows, hq, head_dim]). Same rounding as the two separate calls for the rotation and the
+ * append (bit-exact cache contents); the attention splits each row over a cluster of up to
+ * 16 CTAs per KV head and merges in rank order through distributed shared memory
+ * (deterministic; no workspace). max_total_tokens bounds positions[r] + 1 and fixes the
+ * cluster size. An invalid position or new-token page sets *error_flag and writes zeros
+ * for that row; an unmapped page among the cached tokens sets *error_flag and reads as
+ * zeros. head_dim in {64, 128}; hq / hkv <= 16; rows * hkv <= 65535; K/V rows 16-byte
+ * aligned. Replaces the `_rope` + `scatter_segmented_decode_kv` + `segmented_gqa_decode`
+ * sequence of one decode layer (engine/dense_qstore_cuda.py:689-704,
+ * engine/kernels/segmented_gqa_decode.py:458-607). */
+int mrb_rope_append_attention(const void *q_in, const void *k_in, const void *v_in,
+                              int64_t in_row_stride, int64_t rows, int64_t hq, int64_t hkv,
+                              int64_t head_dim, const int32_t *positions, const int32_t *row_seq,
+                              const float *rope_cos, const float *rope_sin, int64_t rope_len,
+                              const void *q_norm, const void *k_norm, float norm_eps,
+                              void *k_cache, void *v_cache, int64_t stride_page,
+                              int64_t stride_head, int64_t stride_tok, int64_t page_size,
+                              const int32_t *block_table, int64_t block_table_stride,
+                              int64_t num_pages, int32_t *error_flag, float scale,
+                              int64_t max_total_tokens, void *out, void *stream);
+/* CTAs per (row, KV head) cluster mrb_rope_append_attention uses for these sizes (0 for an
+ * unsupported shape). Needs the current device. */
+int mrb_rope_append_attention_cluster(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
+                                      int64_t max_total_tokens);
+
 /* Workspace bytes mrb_paged_attention needs for these sizes (0 when no split is used). */
 size_t mrb_paged_attention_workspace(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
                                      int64_t max_total_tokens);

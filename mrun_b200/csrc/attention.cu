@@ -12,6 +12,7 @@
 // read once per group). Splits publish (max, sum, acc) partials; the last CTA of a
 // (row, head) group to finish merges them in split order, so results are deterministic.
 #include "qrow_common.cuh"
+#include "tc_common.cuh"
 
 #include <algorithm>
 
@@ -182,6 +183,63 @@ __device__ __forceinline__ int64_t kv_offset(const AttnArgs& a, int64_t seq, int
   return page * a.stride_page + khead + (int64_t)(t - lp * ps) * a.stride_tok;
 }
 
+// One 16-token tile of the scalar decode attention for one warp (= one query head): the
+// lane's token score (lane = token + 16 * half of the head dim, K rows XOR-swizzled by 16-byte
+// chunk), the fp32 online-softmax update of (m, l) and acc += p_t * V[t][lane's D/32 dims].
+// `valid`: this lane's token lies inside the range being attended.
+template <int D>
+__device__ __forceinline__ void attend_tile(const __nv_bfloat16 (*ks)[D], const __nv_bfloat16 (*vs)[D],
+                                            const float (&qreg)[D / 2], bool valid, int lane, float& m, float& l,
+                                            float (&acc)[D / 32]) {
+  constexpr int HALF = D / 2, VD = D / 32;
+  const int my_tok = lane & 15, half = lane >> 4;
+  float sc = 0.f;
+#pragma unroll
+  for (int c8 = 0; c8 < HALF / 8; ++c8) {
+    const int c = half * (HALF / 8) + c8;
+    const uint4 raw = reinterpret_cast<const uint4*>(&ks[my_tok][0])[c ^ (my_tok & 7)];
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h2[j]);
+      sc = fmaf(qreg[c8 * 8 + 2 * j], f.x, sc);
+      sc = fmaf(qreg[c8 * 8 + 2 * j + 1], f.y, sc);
+    }
+  }
+  sc += __shfl_xor_sync(0xffffffffu, sc, 16);
+  if (!valid) sc = -INFINITY;
+  float mx = sc;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float m_new = fmaxf(m, mx);
+  const float p = (m_new == -INFINITY) ? 0.f : expf(sc - m_new);
+  float sum = p;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float alpha = (m == -INFINITY) ? 0.f : expf(m - m_new);
+  l = l * alpha + sum;
+  m = m_new;
+#pragma unroll
+  for (int k = 0; k < VD; ++k) acc[k] *= alpha;
+#pragma unroll
+  for (int t = 0; t < AT_TILE; ++t) {
+    const float pt = __shfl_sync(0xffffffffu, p, t);
+    if (VD == 4) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(&vs[t][lane * 4]);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
+      acc[0] = fmaf(pt, f0.x, acc[0]);
+      acc[1 % VD] = fmaf(pt, f0.y, acc[1 % VD]);
+      acc[2 % VD] = fmaf(pt, f1.x, acc[2 % VD]);
+      acc[3 % VD] = fmaf(pt, f1.y, acc[3 % VD]);
+    } else {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vs[t][lane * 2]));
+      acc[0] = fmaf(pt, f.x, acc[0]);
+      acc[1 % VD] = fmaf(pt, f.y, acc[1 % VD]);
+    }
+  }
+}
+
 // Decode attention, one warp per query head of the GQA group (blockDim = 32 * group).
 // The CTA owns (query row, KV head, split) and walks the split's 16-token tiles through a
 // 4-stage cp.async ring in shared memory (K XOR-swizzled so the score reads are
@@ -277,53 +335,7 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
     issue(i + AT_STAGES - 1);  // refills the stage tile i - 1 used
     const int st = i % AT_STAGES;
     const int64_t t0 = t_begin + (int64_t)i * AT_TILE;
-    // ---- score of this lane's token for this warp's head
-    float sc = 0.f;
-#pragma unroll
-    for (int c8 = 0; c8 < HALF / 8; ++c8) {
-      const int c = half * (HALF / 8) + c8;
-      const uint4 raw = reinterpret_cast<const uint4*>(&ks[st][my_tok][0])[c ^ (my_tok & 7)];
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h2[j]);
-        sc = fmaf(qreg[c8 * 8 + 2 * j], f.x, sc);
-        sc = fmaf(qreg[c8 * 8 + 2 * j + 1], f.y, sc);
-      }
-    }
-    sc += __shfl_xor_sync(0xffffffffu, sc, 16);
-    if (t0 + my_tok >= t_end) sc = -INFINITY;
-    float mx = sc;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float m_new = fmaxf(m, mx);
-    const float p = (m_new == -INFINITY) ? 0.f : expf(sc - m_new);
-    float sum = p;
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float alpha = (m == -INFINITY) ? 0.f : expf(m - m_new);
-    l = l * alpha + sum;
-    m = m_new;
-#pragma unroll
-    for (int k = 0; k < VD; ++k) acc[k] *= alpha;
-    // ---- acc += sum_t p_t * V[t][lane dims]
-#pragma unroll
-    for (int t = 0; t < AT_TILE; ++t) {
-      const float pt = __shfl_sync(0xffffffffu, p, t);
-      if (VD == 4) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(&vs[st][t][lane * 4]);
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-        const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
-        acc[0] = fmaf(pt, f0.x, acc[0]);
-        acc[1 % VD] = fmaf(pt, f0.y, acc[1 % VD]);
-        acc[2 % VD] = fmaf(pt, f1.x, acc[2 % VD]);
-        acc[3 % VD] = fmaf(pt, f1.y, acc[3 % VD]);
-      } else {
-        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vs[st][t][lane * 2]));
-        acc[0] = fmaf(pt, f.x, acc[0]);
-        acc[1 % VD] = fmaf(pt, f.y, acc[1 % VD]);
-      }
-    }
+    attend_tile<D>(ks[st], vs[st], qreg, t0 + my_tok < t_end, lane, m, l, acc);
   }
   cp_async_wait_group<0>();
 
@@ -382,6 +394,245 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(Attn
   for (int i = 0; i < VD; ++i) out[i] = __float2bfloat16_rn(lsum > 0.f ? o[i] / lsum : 0.f);
   __syncthreads();
   if (tid == 0) a.counters[rh] = 0u;  // ready for the next launch (graph replays)
+}
+
+// ------------------------------------------------------------------ fused decode step
+
+// One new token per query row in one launch: the RoPE (and optional per-head q/k norm) of the
+// row's query heads and key, the K/V append into the paged cache, and the grouped-query
+// attention over tokens [0, pos] (the cached ones plus the new one). A cluster of S CTAs owns
+// one (row, KV head); CTA c takes an even share of the row's tiles, computed on the device
+// from the row's position, so a captured graph stays balanced as the context grows. The S
+// partials (max, sum, acc) of every query head are merged in rank order through distributed
+// shared memory -- no global scratch, no atomics.
+constexpr int FD_MAX_CLUSTER = 16;
+constexpr int FD_MIN_TILES = 2;  // fewest 16-token tiles per CTA when sizing the cluster
+
+struct FusedArgs {
+  const __nv_bfloat16* q_in;  // row r's query heads at q_in + r * in_stride, [hq, d]
+  const __nv_bfloat16* k_in;  // [hkv, d] at k_in + r * in_stride
+  const __nv_bfloat16* v_in;
+  int64_t in_stride;
+  int64_t rows, hq, hkv;
+  const int32_t* positions;  // position of row r's new token (= its committed length)
+  const int32_t* row_seq;    // block-table row per query row (null: identity)
+  const float* cos_tab;      // [rope_len, d/2] or null (no rotation)
+  const float* sin_tab;
+  int64_t rope_len;
+  const __nv_bfloat16* q_norm;  // [d] or null
+  const __nv_bfloat16* k_norm;
+  float norm_eps;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t stride_page, stride_head, stride_tok, page_size;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int64_t num_pages;
+  int32_t* error_flag;
+  float scale;
+  __nv_bfloat16* out;  // [rows, hq, d]
+};
+
+template <int D>
+__global__ void __launch_bounds__(AT_MAX_GROUP * 32) rope_append_attention_kernel(FusedArgs a) {
+  constexpr int HALF = D / 2, VD = D / 32, CH = D / 8;
+  const int group = blockDim.x >> 5;
+  const int S = (int)gridDim.x;      // the cluster spans grid x
+  const int rank = (int)blockIdx.x;  // = %cluster_ctarank
+  const int64_t rh = blockIdx.y;     // row * hkv + kv head
+  const int64_t r = rh / a.hkv;
+  const int kvh = (int)(rh - r * a.hkv);
+  const int tid = threadIdx.x, g = tid >> 5, lane = tid & 31;
+
+  __shared__ __align__(16) __nv_bfloat16 ks[AT_STAGES][AT_TILE][D];
+  __shared__ __align__(16) __nv_bfloat16 vs[AT_STAGES][AT_TILE][D];
+  __shared__ __align__(16) __nv_bfloat16 qs[AT_MAX_GROUP][D];
+  __shared__ __align__(16) __nv_bfloat16 knew[D];
+  __shared__ __align__(16) __nv_bfloat16 vnew[D];
+  __shared__ __align__(16) float pacc[AT_MAX_GROUP][D];
+  __shared__ __align__(8) float pstat[AT_MAX_GROUP][2];
+
+  pdl_launch_dependents();
+  pdl_wait();
+
+  // ---- the row's new position and its cache slot (every CTA of the cluster agrees)
+  const int64_t seq = a.row_seq ? a.row_seq[r] : r;
+  const int64_t pos = a.positions[r];
+  bool ok = pos >= 0 && (a.cos_tab == nullptr || pos < a.rope_len);
+  int64_t new_off = 0;
+  if (ok) {
+    const int64_t lp = pos / a.page_size;
+    const int64_t page = a.block_table[seq * a.bt_stride + lp];
+    ok = page >= 0 && page < a.num_pages;
+    new_off = page * a.stride_page + (int64_t)kvh * a.stride_head + (pos - lp * a.page_size) * a.stride_tok;
+  }
+  __nv_bfloat16* out_base = a.out + (r * a.hq + (int64_t)kvh * group) * D;
+  if (!ok) {  // cluster-uniform: no CTA reaches a cluster barrier
+    if (rank == 0) {
+      if (tid == 0 && a.error_flag) atomicExch(a.error_flag, 1);
+      for (int e = tid; e < group * D; e += blockDim.x) out_base[e] = __float2bfloat16_rn(0.f);
+    }
+    return;
+  }
+
+  // ---- this CTA's share of the row's 16-token tiles
+  const int64_t total = pos + 1;
+  const int64_t tiles = (total + AT_TILE - 1) / AT_TILE;
+  const int64_t per = (tiles + S - 1) / S;
+  const int64_t tb = min(tiles, (int64_t)rank * per), te = min(tiles, tb + per);
+  const int ntile = (int)(te - tb);
+  const int64_t t_begin = tb * AT_TILE, t_end = min(total, te * AT_TILE);
+  const bool owns_new = pos >= t_begin && pos < t_end;
+  const int64_t khead = (int64_t)kvh * a.stride_head;
+  bool bad_page = false;
+
+  // K/V ring as in the split kernel; the new token's slot is zero-filled here and written
+  // from shared memory once its tile has landed
+  auto issue = [&](int i) {
+    if (i < ntile) {
+      const int st = i % AT_STAGES;
+      const int64_t t0 = t_begin + (int64_t)i * AT_TILE;
+      for (int e = tid; e < AT_TILE * CH; e += blockDim.x) {
+        const int t = e / CH, c = e - t * CH;
+        const int64_t tok = t0 + t;
+        bool ld = tok < pos;
+        int64_t off = 0;
+        if (ld) {
+          const unsigned lp = (unsigned)tok / (unsigned)a.page_size;
+          const int64_t page = a.block_table[seq * a.bt_stride + lp];
+          if (page < 0 || page >= a.num_pages) {
+            ld = false;
+            bad_page = true;
+          } else {
+            off = page * a.stride_page + khead + (int64_t)((unsigned)tok - lp * (unsigned)a.page_size) * a.stride_tok;
+          }
+        }
+        cp_async16_zfill(reinterpret_cast<uint4*>(&ks[st][t][0]) + (c ^ (t & 7)),
+                         reinterpret_cast<const uint4*>(a.k_cache + off) + (ld ? c : 0), ld);
+        cp_async16_zfill(reinterpret_cast<uint4*>(&vs[st][t][0]) + c,
+                         reinterpret_cast<const uint4*>(a.v_cache + off) + (ld ? c : 0), ld);
+      }
+    }
+    cp_async_commit_group();
+  };
+#pragma unroll
+  for (int i = 0; i < AT_STAGES - 1; ++i) issue(i);
+
+  // ---- RoPE of this warp's query head (and of the new key in the CTA that owns it)
+  const float* cr = a.cos_tab ? a.cos_tab + pos * HALF : nullptr;
+  const float* sr = a.sin_tab ? a.sin_tab + pos * HALF : nullptr;
+  const __nv_bfloat16* qrow = a.q_in + r * a.in_stride;
+  rope_head(qrow + ((int64_t)kvh * group + g) * D, &qs[g][0], HALF, cr, sr, lane, a.q_norm, a.norm_eps);
+  if (owns_new) {
+    if (g == 0)
+      rope_head(a.k_in + r * a.in_stride + (int64_t)kvh * D, knew, HALF, cr, sr, lane, a.k_norm, a.norm_eps);
+    if (g == (group > 1 ? 1 : 0))
+      rope_head(a.v_in + r * a.in_stride + (int64_t)kvh * D, vnew, HALF, nullptr, nullptr, lane);
+  }
+  __syncthreads();
+  if (owns_new) {  // commit the new row to the cache (this CTA alone touches slot pos)
+    for (int e = tid; e < 2 * CH; e += blockDim.x) {
+      if (e < CH)
+        reinterpret_cast<uint4*>(a.k_cache + new_off)[e] = reinterpret_cast<const uint4*>(knew)[e];
+      else
+        reinterpret_cast<uint4*>(a.v_cache + new_off)[e - CH] = reinterpret_cast<const uint4*>(vnew)[e - CH];
+    }
+  }
+  const int half = lane >> 4, my_tok = lane & 15;
+  float qreg[HALF];
+#pragma unroll
+  for (int i = 0; i < HALF; i += 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(&qs[g][half * HALF + i]);
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h2[j]);
+      qreg[i + 2 * j] = f.x * a.scale;
+      qreg[i + 2 * j + 1] = f.y * a.scale;
+    }
+  }
+  float m = -INFINITY, l = 0.f, acc[VD];
+#pragma unroll
+  for (int i = 0; i < VD; ++i) acc[i] = 0.f;
+
+  for (int i = 0; i < ntile; ++i) {
+    cp_async_wait_group<AT_STAGES - 2>();
+    __syncthreads();  // tile i is in shared memory; every warp is done with tile i - 1
+    issue(i + AT_STAGES - 1);
+    const int st = i % AT_STAGES;
+    const int64_t t0 = t_begin + (int64_t)i * AT_TILE;
+    if (owns_new && pos < t0 + AT_TILE && pos >= t0) {  // CTA-uniform
+      const int t = (int)(pos - t0);
+      for (int c = tid; c < 2 * CH; c += blockDim.x) {
+        if (c < CH)
+          reinterpret_cast<uint4*>(&ks[st][t][0])[c ^ (t & 7)] = reinterpret_cast<const uint4*>(knew)[c];
+        else
+          reinterpret_cast<uint4*>(&vs[st][t][0])[c - CH] = reinterpret_cast<const uint4*>(vnew)[c - CH];
+      }
+      __syncthreads();
+    }
+    attend_tile<D>(ks[st], vs[st], qreg, t0 + my_tok < t_end, lane, m, l, acc);
+  }
+  cp_async_wait_group<0>();
+  if (bad_page && a.error_flag) atomicExch(a.error_flag, 1);
+
+  if (S == 1) {
+#pragma unroll
+    for (int i = 0; i < VD; ++i) out_base[g * D + lane * VD + i] = __float2bfloat16_rn(l > 0.f ? acc[i] / l : 0.f);
+    return;
+  }
+  // ---- publish this CTA's partial of every head, then merge across the cluster
+#pragma unroll
+  for (int i = 0; i < VD; ++i) pacc[g][lane * VD + i] = acc[i];
+  if (lane == 0) {
+    pstat[g][0] = m;
+    pstat[g][1] = l;
+  }
+  cluster_sync_all();
+  const int h = rank + S * g;  // heads rank, rank + S, ... are merged by this CTA's warps 0, 1, ...
+  if (h < group) {
+    float ms = -INFINITY, ls = 0.f;
+    if (lane < S) {
+      const uint32_t ra = mapa_shared(smem_u32(&pstat[h][0]), (unsigned)lane);
+      ms = ld_shared_cluster_f32(ra);
+      ls = ld_shared_cluster_f32(ra + 4);
+    }
+    const float mx = warp_max(ms);
+    const float wt = (ms == -INFINITY) ? 0.f : expf(ms - mx);
+    const float lsum = warp_sum(ls * wt);
+    const uint32_t acc_addr = smem_u32(&pacc[h][lane * VD]);
+    float o[VD];
+#pragma unroll
+    for (int i = 0; i < VD; ++i) o[i] = 0.f;
+    for (int s0 = 0; s0 < S; s0 += 8) {
+      float av[8][VD];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const bool in = s0 + j < S;
+        const uint32_t ra = mapa_shared(acc_addr, (unsigned)(in ? s0 + j : 0));
+        if (VD == 4) {
+          const float4 v = in ? ld_shared_cluster_v4f32(ra) : make_float4(0.f, 0.f, 0.f, 0.f);
+          av[j][0] = v.x;
+          av[j][1 % VD] = v.y;
+          av[j][2 % VD] = v.z;
+          av[j][3 % VD] = v.w;
+        } else {
+          const float2 v = in ? ld_shared_cluster_v2f32(ra) : make_float2(0.f, 0.f);
+          av[j][0] = v.x;
+          av[j][1 % VD] = v.y;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float w = __shfl_sync(0xffffffffu, wt, (s0 + j) & 31);
+#pragma unroll
+        for (int i = 0; i < VD; ++i) o[i] = fmaf(av[j][i], w, o[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VD; ++i) out_base[h * D + lane * VD + i] = __float2bfloat16_rn(lsum > 0.f ? o[i] / lsum : 0.f);
+  }
+  cluster_sync_all();  // peers' shared memory stays alive until every merge has read it
 }
 
 // ------------------------------------------------------------------ tensor-core decode attention
@@ -878,6 +1129,119 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
     a.part = (float*)((char*)workspace + AT_COUNTER_BYTES);
   }
   return launch_attention(a, head_dim, max_total_tokens, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------------------ fused decode step (host)
+
+// Cluster size for the fused step: about FD_MIN_TILES tiles per CTA at max_total_tokens, at
+// most 16 (a non-portable cluster; 8 where the device cannot co-schedule 16 of these CTAs),
+// and at most two CTAs per SM over all (row, KV head) clusters.
+template <int D>
+static int fused_cluster_size(int64_t rows, int64_t hkv, int64_t max_total, int group) {
+  const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
+  const int64_t groups = std::max<int64_t>(1, rows * hkv);
+  int64_t s = std::min<int64_t>(FD_MAX_CLUSTER, (tiles + FD_MIN_TILES - 1) / FD_MIN_TILES);
+  s = std::min<int64_t>(s, std::max<int64_t>(1, 2 * num_sms() / groups));
+  if (s > 8) {
+    static int fits16[AT_MAX_GROUP + 1] = {};  // 0 unknown, 1 yes, -1 no (per group size)
+    if (fits16[group] == 0) {
+      fits16[group] = -1;
+      auto kern = rope_append_attention_kernel<D>;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(FD_MAX_CLUSTER, 1);
+        cfg.blockDim = dim3(32 * group);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = FD_MAX_CLUSTER;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) fits16[group] = 1;
+      }
+      cudaGetLastError();
+    }
+    if (fits16[group] < 0) s = 8;
+  }
+  return (int)s;
+}
+
+template <int D>
+static int launch_fused(const FusedArgs& a, int64_t max_total, cudaStream_t st) {
+  const int group = (int)(a.hq / a.hkv);
+  const int s = fused_cluster_size<D>(a.rows, a.hkv, max_total, group);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)s, (unsigned)(a.rows * a.hkv));
+  cfg.blockDim = dim3((unsigned)(32 * group));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (s > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)s;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = n ? attr : nullptr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, rope_append_attention_kernel<D>, a);
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "rope_append_attention: launch: %s", cudaGetErrorString(e));
+  return launch_status("rope_append_attention");
+}
+
+extern "C" int mrb_rope_append_attention_cluster(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
+                                                 int64_t max_total_tokens) {
+  if (rows <= 0 || hq <= 0 || hkv <= 0 || hq % hkv || hq / hkv > AT_MAX_GROUP) return 0;
+  const int group = (int)(hq / hkv);
+  if (head_dim == 128) return fused_cluster_size<128>(rows, hkv, max_total_tokens, group);
+  if (head_dim == 64) return fused_cluster_size<64>(rows, hkv, max_total_tokens, group);
+  return 0;
+}
+
+extern "C" int mrb_rope_append_attention(const void* q_in, const void* k_in, const void* v_in, int64_t in_row_stride,
+                                         int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
+                                         const int32_t* positions, const int32_t* row_seq, const float* rope_cos,
+                                         const float* rope_sin, int64_t rope_len, const void* q_norm,
+                                         const void* k_norm, float norm_eps, void* k_cache, void* v_cache,
+                                         int64_t stride_page, int64_t stride_head, int64_t stride_tok,
+                                         int64_t page_size, const int32_t* block_table, int64_t block_table_stride,
+                                         int64_t num_pages, int32_t* error_flag, float scale,
+                                         int64_t max_total_tokens, void* out, void* stream) {
+  if (rows < 0 || hq <= 0 || hkv <= 0 || hq % hkv || page_size <= 0 || num_pages <= 0 || max_total_tokens < 0)
+    return fail(MRB_ERR_ARG, "rope_append_attention: bad shape");
+  if (hq / hkv > AT_MAX_GROUP)
+    return fail(MRB_ERR_UNSUPPORTED, "rope_append_attention: query group %lld exceeds %d", (long long)(hq / hkv),
+                AT_MAX_GROUP);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(MRB_ERR_UNSUPPORTED, "rope_append_attention: head_dim %lld (supported: 64, 128)",
+                (long long)head_dim);
+  if (rows == 0) return MRB_OK;
+  if (!q_in || !k_in || !v_in || !positions || !k_cache || !v_cache || !block_table || !out)
+    return fail(MRB_ERR_ARG, "rope_append_attention: null pointer");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return fail(MRB_ERR_ARG, "rope_append_attention: cos/sin mismatch");
+  if ((in_row_stride % 2) || !aligned(q_in, 4) || !aligned(k_in, 4) || !aligned(v_in, 4) ||
+      (rope_cos && (!aligned(rope_cos, 8) || !aligned(rope_sin, 8))) || (q_norm && !aligned(q_norm, 4)) ||
+      (k_norm && !aligned(k_norm, 4)))
+    return fail(MRB_ERR_ARG, "rope_append_attention: q/k/v rows and norms must be 4-byte aligned (8-byte tables)");
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || (stride_page % 8) || (stride_head % 8) || (stride_tok % 8))
+    return fail(MRB_ERR_ARG, "rope_append_attention: K/V rows must be 16-byte aligned");
+  if (rows * hkv > 65535) return fail(MRB_ERR_UNSUPPORTED, "rope_append_attention: grid too large");
+  FusedArgs a{(const __nv_bfloat16*)q_in, (const __nv_bfloat16*)k_in, (const __nv_bfloat16*)v_in, in_row_stride,
+              rows, hq, hkv, positions, row_seq, rope_cos, rope_sin, rope_len, (const __nv_bfloat16*)q_norm,
+              (const __nv_bfloat16*)k_norm, norm_eps, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, stride_page,
+              stride_head, stride_tok, page_size, block_table, block_table_stride, num_pages, error_flag, scale,
+              (__nv_bfloat16*)out};
+  return head_dim == 128 ? launch_fused<128>(a, max_total_tokens, (cudaStream_t)stream)
+                         : launch_fused<64>(a, max_total_tokens, (cudaStream_t)stream);
 }
 
 // ------------------------------------------------------------------ decode-step bookkeeping

@@ -165,6 +165,11 @@ class DenseWeights:
         return out
 
 
+# Decode batches with at most this many (row, KV head) pairs run RoPE + KV append + attention
+# as one clustered launch per layer; larger batches keep the tensor-core split-K attention.
+FUSED_DECODE_MAX_GROUPS = 32
+
+
 def rope_tables(head_dim: int, theta: float, length: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin [length, head_dim/2] computed with the reference's fp32 torch recipe
     (engine/dense_qstore_cuda.py:689-704) on the host, then uploaded."""
@@ -247,8 +252,11 @@ class DenseDecoder:
     # ------------------------------------------------------------------ body
 
     def _layers(self, rows: int, positions: torch.Tensor, token_rows: torch.Tensor, row_len: torch.Tensor,
-                max_total: int, *, last_only: bool) -> torch.Tensor:
-        """Run embeddings-to-final-norm for ``rows`` tokens already embedded in buf['hidden']."""
+                max_total: int, *, last_only: bool, fused: bool = False) -> torch.Tensor:
+        """Run embeddings-to-final-norm for ``rows`` tokens already embedded in buf['hidden'].
+
+        ``fused``: each row is the next token of a different sequence, so RoPE, the KV append
+        and the attention run as one launch per layer."""
         cfg, buf, w = self.cfg, self.buf, self.w
         hidden = buf["hidden"][:rows]
         normed = buf["normed"][:rows]
@@ -278,13 +286,20 @@ class DenseDecoder:
         rms_norm_into(hidden, w.layers[0].ln1, cfg.eps, normed)
         for i, layer in enumerate(w.layers):
             linear(layer.qkv, normed, qkv, bias=layer.qkv_bias)
-            self.kv.append(
-                i, qkv[:, qd:], qkv[:, qd + kd:], positions, token_rows, q_rows=qkv, q_out=q,
-                rope=(self.cos, self.sin), in_row_stride=cfg.qkv_rows, num_heads=cfg.heads,
-                error_flag=self.error_flag,
-            )
-            self.kv.attend(i, q, row_len, max_total_tokens=max_total, row_seq=token_rows, out=ctx,
-                           workspace=self.workspace, scale=self.scale)
+            if fused:
+                self.kv.append_attend(
+                    i, qkv, qkv[:, qd:], qkv[:, qd + kd:], positions, token_rows, num_heads=cfg.heads,
+                    max_total_tokens=max_total, in_row_stride=cfg.qkv_rows, rope=(self.cos, self.sin),
+                    error_flag=self.error_flag, scale=self.scale, out=ctx,
+                )
+            else:
+                self.kv.append(
+                    i, qkv[:, qd:], qkv[:, qd + kd:], positions, token_rows, q_rows=qkv, q_out=q,
+                    rope=(self.cos, self.sin), in_row_stride=cfg.qkv_rows, num_heads=cfg.heads,
+                    error_flag=self.error_flag,
+                )
+                self.kv.attend(i, q, row_len, max_total_tokens=max_total, row_seq=token_rows, out=ctx,
+                               workspace=self.workspace, scale=self.scale)
             linear(layer.o, ctx.view(rows, qd), proj)
             residual_rms_norm_into(hidden, proj, layer.ln2, cfg.eps, hidden, normed)
             swiglu(layer.gate, layer.up, normed, mlp)
@@ -327,7 +342,8 @@ class DenseDecoder:
         cfg = self.cfg
         embed_rows(self.w.embed.codes, self.w.embed.scales, self.in_ids[:rows], out=self.buf["hidden"][:rows])
         normed = self._layers(rows, self.positions[:rows], self.row_seq[:rows], self.row_len[:rows],
-                              self.max_seq_len, last_only=False)
+                              self.max_seq_len, last_only=False,
+                              fused=rows * self.cfg.kv_heads <= FUSED_DECODE_MAX_GROUPS)
         qrow_argmax(self.w.head.codes, self.w.head.scales, normed, out_index=self.next_ids[:rows],
                     out_value=self.next_val[:rows], store_logits=False)
         _lib.call("mrb_decode_advance", self.next_ids.data_ptr(), self.in_ids.data_ptr(),
@@ -361,9 +377,11 @@ class DenseDecoder:
             self._decode_body(rows)
         self.graph = graph
         self.graph_rows = rows
-        # kernels: embed, final norm, 8 per layer (W8A8: + 4 activation quantisers), head
-        # GEMV + argmax unpack, advance (the argmax key reset is a memset node, not a kernel)
-        per_layer = 8 + (4 if self.mode == "w8a8" else 0)
+        # kernels: embed, final norm, 8 per layer (7 with the fused RoPE/append/attention; W8A8:
+        # + 4 activation quantisers), head GEMV + argmax unpack, advance (the argmax key reset
+        # is a memset node, not a kernel)
+        fused = rows * self.cfg.kv_heads <= FUSED_DECODE_MAX_GROUPS
+        per_layer = (7 if fused else 8) + (4 if self.mode == "w8a8" else 0)
         self.launches_per_step = 2 + per_layer * self.cfg.num_layers + 2 + 1
 
     def step(self) -> None:

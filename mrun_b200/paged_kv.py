@@ -10,7 +10,8 @@ from __future__ import annotations
 
 import torch
 
-from .segmented_gqa_decode import paged_attention, paged_attention_workspace_bytes, rope_kv_append
+from .segmented_gqa_decode import (paged_attention, paged_attention_workspace_bytes, rope_append_attention,
+                                   rope_kv_append)
 
 PAGE = 16
 
@@ -107,6 +108,33 @@ class PagedKVCache:
             block_table=self.block_table, positions=positions, token_rows=token_rows, q_in=q_rows, q_out=q_out,
             rope=rope, in_row_stride=in_row_stride, num_heads=num_heads, error_flag=error_flag, qk_norm=qk_norm,
             norm_eps=norm_eps,
+        )
+
+    def append_attend(
+        self,
+        layer: int,
+        q_rows: torch.Tensor,
+        k_rows: torch.Tensor,
+        v_rows: torch.Tensor,
+        positions: torch.Tensor,
+        row_seq: torch.Tensor | None,
+        *,
+        num_heads: int,
+        max_total_tokens: int,
+        in_row_stride: int | None = None,
+        rope: tuple[torch.Tensor, torch.Tensor] | None = None,
+        qk_norm: tuple[torch.Tensor, torch.Tensor] | None = None,
+        norm_eps: float = 1e-6,
+        error_flag: torch.Tensor | None = None,
+        scale: float | None = None,
+        out: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        """``append`` then ``attend`` for one decode token per sequence, in one launch."""
+        return rope_append_attention(
+            q_rows, k_rows, v_rows, self.k[layer], self.v[layer], strides=self.strides, page_size=self.page_size,
+            block_table=self.block_table, positions=positions, row_seq=row_seq, num_heads=num_heads,
+            max_total_tokens=max_total_tokens, in_row_stride=in_row_stride, rope=rope, qk_norm=qk_norm,
+            norm_eps=norm_eps, error_flag=error_flag, scale=scale, out=out,
         )
 
     def workspace_bytes(self, rows: int, num_heads: int, max_total_tokens: int) -> int:

@@ -143,6 +143,67 @@ def rope_kv_append(
     )
 
 
+def rope_append_attention(
+    q_in: torch.Tensor,
+    k_in: torch.Tensor,
+    v_in: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    *,
+    strides: tuple[int, int, int],
+    page_size: int,
+    block_table: torch.Tensor,
+    positions: torch.Tensor,
+    row_seq: torch.Tensor | None,
+    num_heads: int,
+    max_total_tokens: int,
+    in_row_stride: int | None = None,
+    rope: tuple[torch.Tensor, torch.Tensor] | None = None,
+    qk_norm: tuple[torch.Tensor, torch.Tensor] | None = None,
+    norm_eps: float = 1e-6,
+    error_flag: torch.Tensor | None = None,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """One decode token per row in one launch: ``rope_kv_append`` of the row's new position
+    followed by ``paged_attention`` over positions ``[0, positions[r]]``.
+
+    Every row must continue a different sequence (``row_seq`` distinct): a row reads only
+    cache entries written before this call plus its own new token. Returns bf16
+    ``[rows, num_heads, head_dim]``."""
+    rows = int(positions.numel())
+    hkv, d = int(k_cache.shape[1]), int(k_cache.shape[-1])
+    device = _lib.require_cuda(q_in, k_in, v_in, k_cache, v_cache, block_table, positions,
+                               what="fused decode attention")
+    if k_cache.dtype != torch.bfloat16 or v_cache.dtype != torch.bfloat16 or q_in.dtype != torch.bfloat16:
+        raise TypeError("fused decode attention runs on bf16 rows and caches")
+    if block_table.dtype != torch.int32 or positions.dtype != torch.int32:
+        raise TypeError("block tables and positions must be int32")
+    if out is None:
+        out = torch.empty(rows, int(num_heads), d, dtype=torch.bfloat16, device=device)
+    elif out.shape != (rows, int(num_heads), d) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [rows, num_heads, head_dim] tensor")
+    stride = int(in_row_stride if in_row_stride is not None else q_in.stride(0))
+    cos, sin = rope if rope is not None else (None, None)
+    sc = (1.0 / math.sqrt(d)) if scale is None else float(scale)
+    _lib.call(
+        "mrb_rope_append_attention",
+        q_in.data_ptr(), k_in.data_ptr(), v_in.data_ptr(), stride, rows, int(num_heads), hkv, d,
+        positions.data_ptr(), _lib.ptr(row_seq), _lib.ptr(cos), _lib.ptr(sin),
+        0 if cos is None else int(cos.shape[0]), _lib.ptr(qk_norm[0] if qk_norm else None),
+        _lib.ptr(qk_norm[1] if qk_norm else None), float(norm_eps), k_cache.data_ptr(), v_cache.data_ptr(),
+        strides[0], strides[1], strides[2], page_size, block_table.data_ptr(),
+        int(block_table.stride(0)) if block_table.ndim > 1 else 1, int(k_cache.shape[0]), _lib.ptr(error_flag), sc,
+        int(max_total_tokens), out.data_ptr(), _lib.stream_handle(device),
+    )
+    return out
+
+
+def rope_append_attention_cluster(rows: int, hq: int, hkv: int, head_dim: int, max_total_tokens: int) -> int:
+    """CTAs per (row, KV head) the fused decode step uses for these sizes."""
+    return int(_lib.load().mrb_rope_append_attention_cluster(rows, hq, hkv, head_dim, max_total_tokens))
+
+
 # ------------------------------------------------------------------ reference-shaped API
 
 

@@ -145,3 +145,121 @@ def test_scatter_segmented_decode_kv(cuda):
         assert torch.equal(kc[slot, :, pos], k[row])
         assert torch.equal(vc[slot, :, pos], v[row])
     assert int((kc != 0).any(dim=-1).sum()) == 6
+
+
+def _qk_rms(x, w, eps):
+    from oracle.moe_decoder import _rms
+
+    return _rms(x, w, eps)
+
+
+@pytest.mark.parametrize("rows,hq,hkv,d,positions,max_total,use_rope,qk_norm", [
+    (1, 28, 4, 128, [520], 960, True, False),        # config-2 shape: 16-CTA clusters
+    (1, 28, 4, 128, [0], 16, True, False),           # first token: one CTA, no cluster
+    (3, 32, 4, 128, [15, 16, 255], 300, True, True),  # page edges, Qwen3 q/k norm
+    (2, 8, 8, 64, [31, 100], 128, True, False),      # head_dim 64, group 1
+    (8, 28, 4, 128, [1, 17, 300, 511, 64, 5, 1000, 47], 1024, True, False),  # 9-CTA clusters, ragged
+    (1, 64, 4, 128, [3000], 4096, True, False),      # 16-head group
+    (2, 28, 4, 128, [40, 7], 64, False, False),      # no rotation (plain append)
+])
+def test_rope_append_attention_vs_separate_and_oracle(rows, hq, hkv, d, positions, max_total, use_rope, qk_norm,
+                                                      cuda):
+    from mrun_b200.paged_kv import PagedKVCache
+    from mrun_b200.segmented_gqa_decode import rope_append_attention_cluster
+
+    rng = np.random.default_rng(sum(positions) + hq)
+    seqs = list(range(rows))[::-1]  # row r continues sequence rows-1-r
+    pages_per_seq = (max_total + 15) // 16
+    cache = PagedKVCache(num_layers=1, num_pages=rows * pages_per_seq + 2, kv_heads=hkv, head_dim=d,
+                         max_seqs=rows, max_pages_per_seq=pages_per_seq, device=cuda)
+    for r, p in enumerate(positions):
+        cache.reserve(seqs[r], p + 1)
+    # the cached prefix: random bf16 K/V in every mapped page
+    cache.k.copy_(_bf(rng.standard_normal(tuple(cache.k.shape)), cuda))
+    cache.v.copy_(_bf(rng.standard_normal(tuple(cache.v.shape)), cuda))
+    width = (hq + 2 * hkv) * d
+    qkv = bf16_round(rng.standard_normal((rows, width)).astype(np.float32))
+    qkv_dev = _bf(qkv, cuda)
+    pos_dev = torch.tensor(positions, dtype=torch.int32, device=cuda)
+    seq_dev = torch.tensor(seqs, dtype=torch.int32, device=cuda)
+    cos, sin = oatt.rope_tables(d, 1e6, np.arange(max_total))
+    rope = (torch.from_numpy(cos[:, : d // 2].copy()).to(cuda), torch.from_numpy(sin[:, : d // 2].copy()).to(cuda)) \
+        if use_rope else None
+    norms = None
+    if qk_norm:
+        qw = bf16_round(1.0 + 0.1 * rng.standard_normal(d).astype(np.float32))
+        kw = bf16_round(1.0 + 0.1 * rng.standard_normal(d).astype(np.float32))
+        norms = (_bf(qw, cuda), _bf(kw, cuda))
+    k0, v0 = cache.k.clone(), cache.v.clone()
+
+    # separate launches: rope_kv_append + paged_attention
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    q_rot = torch.empty(rows, hq, d, dtype=torch.bfloat16, device=cuda)
+    cache.append(0, qkv_dev[:, hq * d:], qkv_dev[:, (hq + hkv) * d:], pos_dev, seq_dev, q_rows=qkv_dev, q_out=q_rot,
+                 rope=rope, in_row_stride=width, num_heads=hq, error_flag=err, qk_norm=norms)
+    sep = cache.attend(0, q_rot, pos_dev + 1, max_total_tokens=max_total, row_seq=seq_dev)
+    k_sep, v_sep = cache.k.clone(), cache.v.clone()
+    # fused launch on the original cache
+    cache.k.copy_(k0)
+    cache.v.copy_(v0)
+    fused = cache.append_attend(0, qkv_dev, qkv_dev[:, hq * d:], qkv_dev[:, (hq + hkv) * d:], pos_dev, seq_dev,
+                                num_heads=hq, max_total_tokens=max_total, in_row_stride=width, rope=rope,
+                                qk_norm=norms, error_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert rope_append_attention_cluster(rows, hq, hkv, d, max_total) >= 1
+    # the append is bit-exact with the separate kernel
+    assert torch.equal(cache.k, k_sep) and torch.equal(cache.v, v_sep)
+    # attention against the oracle over the gathered cache (the new token included)
+    k_pages = cache.k[0].float().cpu().numpy()
+    v_pages = cache.v[0].float().cpu().numpy()
+    q = qkv[:, : hq * d].reshape(rows, hq, d)
+    k_new = qkv[:, hq * d:(hq + hkv) * d].reshape(rows, hkv, d)
+    if qk_norm:
+        q = _qk_rms(q, qw, 1e-6)
+        k_new = _qk_rms(k_new, kw, 1e-6)
+    if use_rope:
+        q = np.stack([oatt.rope(q[r:r + 1], cos[p:p + 1], sin[p:p + 1])[0] for r, p in enumerate(positions)])
+        k_new = np.stack([oatt.rope(k_new[r:r + 1], cos[p:p + 1], sin[p:p + 1])[0] for r, p in enumerate(positions)])
+    keys = [oatt.paged_gather(k_pages, cache.pages_of(seqs[r]), p + 1) for r, p in enumerate(positions)]
+    vals = [oatt.paged_gather(v_pages, cache.pages_of(seqs[r]), p + 1) for r, p in enumerate(positions)]
+    for r, p in enumerate(positions):
+        if qk_norm:  # fp32 rsqrt in the kernel vs float64 here: equal up to bf16 rounding ties
+            assert max_rel_err(keys[r][p], k_new[r]) < TOL
+        else:
+            np.testing.assert_array_equal(keys[r][p], k_new[r])
+        np.testing.assert_array_equal(vals[r][p], qkv[r, (hq + hkv) * d:].reshape(hkv, d))
+    ref = bf16_round(oatt.gqa_decode_rows(q, keys, vals))
+    assert max_rel_err(fused.float().cpu().numpy(), ref) < TOL
+    assert max_rel_err(fused.float().cpu().numpy(), sep.float().cpu().numpy()) < TOL
+    # deterministic: a second run on the same inputs gives identical bits
+    cache.k.copy_(k0)
+    cache.v.copy_(v0)
+    again = cache.append_attend(0, qkv_dev, qkv_dev[:, hq * d:], qkv_dev[:, (hq + hkv) * d:], pos_dev, seq_dev,
+                                num_heads=hq, max_total_tokens=max_total, in_row_stride=width, rope=rope,
+                                qk_norm=norms, error_flag=err)
+    assert torch.equal(again, fused)
+
+
+def test_rope_append_attention_bad_position_flags_and_zeroes(cuda):
+    from mrun_b200.paged_kv import PagedKVCache
+
+    rng = np.random.default_rng(11)
+    hq, hkv, d = 8, 2, 128
+    cache = PagedKVCache(num_layers=1, num_pages=8, kv_heads=hkv, head_dim=d, max_seqs=2, max_pages_per_seq=4,
+                         device=cuda)
+    cache.reserve(0, 20)
+    cache.reserve(1, 20)
+    width = (hq + 2 * hkv) * d
+    qkv = _bf(rng.standard_normal((2, width)), cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    # row 1's position lies on an unmapped page (the table row maps 2 pages = 32 tokens)
+    pos = torch.tensor([19, 40], dtype=torch.int32, device=cuda)
+    out = cache.append_attend(0, qkv, qkv[:, hq * d:], qkv[:, (hq + hkv) * d:], pos,
+                              torch.tensor([0, 1], dtype=torch.int32, device=cuda), num_heads=hq,
+                              max_total_tokens=64, in_row_stride=width, error_flag=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 1
+    assert not bool(out[1].any())
+    assert bool(out[0].any())
+    assert bool(torch.isfinite(out[0].float()).all())
