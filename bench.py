@@ -290,6 +290,8 @@ GEMV_CASES = {
     # config-2 shapes at M=1, config-4 dense projections at M=32 (as the MoE decoder calls them)
     "gemv-swiglu": (18944, 3584, True, 1, False),
     "gemv-down": (3584, 18944, False, 1, False),
+    "gemv-down-ws": (3584, 18944, False, 1, True),
+    "gemv-o": (3584, 3584, False, 1, True),
     "gemv-qkv": (4608, 3584, False, 1, False),
     "gemv-o32": (2048, 4096, False, 32, True),
     "gemv-qkv32": (5120, 2048, False, 32, True),

@@ -118,6 +118,9 @@ template <> struct io<__half> {
   static __device__ __forceinline__ void store(__half* p, float v) { *p = __float2half_rn(v); }
 };
 
+// Bring the 128-byte line holding p into L2 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 // Streaming 128-bit read-only load that does not allocate in L1 (weights are read once).
 __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
   uint4 r;
