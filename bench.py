@@ -640,6 +640,44 @@ def run_attn_case(args) -> None:
                       "kv_gbs": kv_bytes / avg_s / 1e9, "launches": args.steps}), flush=True)
 
 
+def run_fused_attn_case(args) -> None:
+    """Small case for kernel captures: the fused decode step (RoPE + KV append + attention,
+    one clustered launch) at the config-2 shape -- one row, 28 query / 4 KV heads, 600 cached
+    tokens, cluster sized for the bench's 960-token capacity -- cycling over 160 layers'
+    caches (197 MB of K/V, above L2) so every launch reads cold pages as in the decode step.
+    Prints the device-timed average and the K/V bytes read per second; not the bench metric."""
+    import torch
+
+    from mrun_b200.paged_kv import PagedKVCache
+    from mrun_b200.dense_engine import rope_tables
+    from mrun_b200.segmented_gqa_decode import rope_append_attention_cluster
+
+    hq, hkv, d, ctx, cap, layers = 28, 4, 128, 600, 960, 160
+    device = torch.device("cuda", 0)
+    kv = PagedKVCache(num_layers=layers, num_pages=(cap + 15) // 16, kv_heads=hkv, head_dim=d, max_seqs=1,
+                      max_pages_per_seq=(cap + 15) // 16, device=device)
+    kv.reserve(0, ctx + 1)
+    gen = torch.Generator(device=device).manual_seed(0)
+    kv.k.normal_(0.0, 1.0, generator=gen)
+    kv.v.normal_(0.0, 1.0, generator=gen)
+    width = (hq + 2 * hkv) * d
+    qkv = torch.randn(1, width, device=device, generator=gen).to(torch.bfloat16)
+    cos, sin = rope_tables(d, 1e6, cap, device)
+    pos = torch.tensor([ctx], dtype=torch.int32, device=device)
+    seq = torch.zeros(1, dtype=torch.int32, device=device)
+    out = torch.empty(1, hq, d, dtype=torch.bfloat16, device=device)
+
+    def launch(i):
+        kv.append_attend(i % layers, qkv, qkv[:, hq * d:], qkv[:, (hq + hkv) * d:], pos, seq, num_heads=hq,
+                         max_total_tokens=cap, in_row_stride=width, rope=(cos, sin), scale=d ** -0.5, out=out)
+
+    avg_s = _graph_avg_seconds(launch, args.steps, args.warmup, device)
+    kv_bytes = ctx * 2 * hkv * d * 2
+    print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "kv_bytes": kv_bytes,
+                      "kv_gbs": kv_bytes / avg_s / 1e9, "cluster": rope_append_attention_cluster(1, hq, hkv, d, cap),
+                      "launches": args.steps}), flush=True)
+
+
 EXPERT_CASES = {
     # name: (experts on this GPU, tokens, top-k) of one config-4 MoE layer's grouped expert
     # MLP: one GPU (32 tokens x top-8 over 128 experts, ~2 rows per expert) and an EP8 shard
@@ -918,7 +956,7 @@ def main() -> None:
                     help="moe-decode on N GPUs: expert exchange over NVLink peer memory or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
-                                       *TC_CASES, *ATTN_CASES, *EXPERT_CASES],
+                                       *TC_CASES, *ATTN_CASES, "attn-fused1", *EXPERT_CASES],
                     default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
@@ -928,6 +966,8 @@ def main() -> None:
         run_gemv_case(args)
     elif args.case in ATTN_CASES:
         run_attn_case(args)
+    elif args.case == "attn-fused1":
+        run_fused_attn_case(args)
     elif args.case in EXPERT_CASES:
         run_expert_case(args)
     elif args.case in TC_CASES:

@@ -299,15 +299,23 @@ int mrb_rope_kv_append(const void *q_in, const void *k_in, const void *v_in, int
  * q/k norm) of the row's query heads and key, its K/V append at position positions[r] of
  * block-table row row_seq[r] (NULL: r), and mrb_paged_attention over tokens
  * [0, positions[r]] -- the cached ones plus the new one -- written to out (bf16
- * [rows, hq, head_dim]). Same rounding as the two separate calls for the rotation and the
- * append (bit-exact cache contents); the attention splits each row over a cluster of up to
- * 16 CTAs per KV head and merges in rank order through distributed shared memory
- * (deterministic; no workspace). max_total_tokens bounds positions[r] + 1 and fixes the
- * cluster size. An invalid position or new-token page sets *error_flag and writes zeros
- * for that row; an unmapped page among the cached tokens sets *error_flag and reads as
- * zeros. head_dim in {64, 128}; hq / hkv <= 16; rows * hkv <= 65535; K/V rows 16-byte
- * aligned. Replaces the `_rope` + `scatter_segmented_decode_kv` + `segmented_gqa_decode`
- * sequence of one decode layer (engine/dense_qstore_cuda.py:689-704,
+ * [rows, hq, head_dim]). Every row continues a different sequence.
+ * - Same rounding as the two separate calls for the rotation and the append (bit-exact
+ *   cache contents).
+ * - The attention splits each row over a cluster of up to 16 CTAs per KV head and merges in
+ *   rank order through distributed shared memory (deterministic; no workspace): on the
+ *   tensor pipe (mma.sync, query heads as the rows) for head_dim 128 with pages of a
+ *   multiple of 16 tokens, else one warp per query head. max_total_tokens bounds
+ *   positions[r] + 1 and fixes the cluster size.
+ * - state_ready = 1: positions, row_seq, the block table and the cached K/V below
+ *   positions[r] are not written by any kernel that may still run when this one starts (a
+ *   decode step whose bookkeeping runs after its layers); the kernel reads them before
+ *   waiting on the preceding kernel (programmatic dependent launch). 0: every read waits.
+ * - An invalid position or new-token page sets *error_flag and writes zeros for that row; an
+ *   unmapped page among the cached tokens sets *error_flag and reads as zeros.
+ * - head_dim in {64, 128}; hq / hkv <= 16; rows * hkv <= 65535; K/V rows 16-byte aligned.
+ * Replaces the `_rope` + `scatter_segmented_decode_kv` + `segmented_gqa_decode` sequence of
+ * one decode layer (engine/dense_qstore_cuda.py:689-704,
  * engine/kernels/segmented_gqa_decode.py:458-607). */
 int mrb_rope_append_attention(const void *q_in, const void *k_in, const void *v_in,
                               int64_t in_row_stride, int64_t rows, int64_t hq, int64_t hkv,
@@ -318,7 +326,7 @@ int mrb_rope_append_attention(const void *q_in, const void *k_in, const void *v_
                               int64_t stride_head, int64_t stride_tok, int64_t page_size,
                               const int32_t *block_table, int64_t block_table_stride,
                               int64_t num_pages, int32_t *error_flag, float scale,
-                              int64_t max_total_tokens, void *out, void *stream);
+                              int64_t max_total_tokens, int state_ready, void *out, void *stream);
 /* CTAs per (row, KV head) cluster mrb_rope_append_attention uses for these sizes (0 for an
  * unsupported shape). Needs the current device. */
 int mrb_rope_append_attention_cluster(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,

@@ -54,7 +54,8 @@ SIGNATURES: dict[str, list] = {
     "mrb_rope_kv_append": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P, _P,
                            _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _P, c_float, _P],
     "mrb_rope_append_attention": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _I64, _P, _P, c_float,
-                                  _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, c_float, _I64, _P, _P],
+                                  _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, c_float, _I64, c_int, _P,
+                                  _P],
     "mrb_rope_append_attention_cluster": [_I64, _I64, _I64, _I64, _I64],
     "mrb_paged_attention_workspace": [_I64, _I64, _I64, _I64, _I64],
     "mrb_paged_attention": [_P, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P,

@@ -431,6 +431,7 @@ struct FusedArgs {
   int32_t* error_flag;
   float scale;
   __nv_bfloat16* out;  // [rows, hq, d]
+  int state_ready;     // positions, row_seq, block table and cached K/V may be read before the wait
 };
 
 template <int D>
@@ -979,6 +980,304 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
   if (tid == 0) a.counters[rh] = 0u;  // ready for the next launch (graph replays)
 }
 
+// The fused decode step (rope_append_attention_kernel's prologue and cluster merge) around
+// the tensor-core tile loop of paged_attention_mma_kernel, for head_dim 128: W warps per CTA
+// take the CTA's 16-token tiles in turn (one block-table lookup per tile -- the page size is
+// a multiple of 16), compute S = Q K^T for all query heads of the group with heads as the mma
+// rows, and accumulate O += P V; the warp owning the new token's tile writes its rotated K
+// and V into the staged tile. The W warp states merge in shared memory in warp order, then
+// the cluster's CTA states through distributed shared memory in rank order (deterministic).
+__global__ void __launch_bounds__(AM_MAX_WARPS * 32) rope_append_attention_mma_kernel(FusedArgs a) {
+  constexpr int D = 128, HALF = D / 2, CH = D / 8;
+  const int W = blockDim.x >> 5;
+  const int group = (int)(a.hq / a.hkv);
+  const int S = (int)gridDim.x;      // the cluster spans grid x
+  const int rank = (int)blockIdx.x;  // = %cluster_ctarank
+  const int64_t rh = blockIdx.y;     // row * hkv + kv head
+  const int64_t r = rh / a.hkv;
+  const int kvh = (int)(rh - r * a.hkv);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+
+  extern __shared__ __align__(16) unsigned char am_smem[];
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(am_smem) + (size_t)warp * AM_STAGES * AM_STAGE_ELEMS;
+  __shared__ __align__(16) __nv_bfloat16 qs[AT_MAX_GROUP][D];
+  __shared__ __align__(16) __nv_bfloat16 knew[D];
+  __shared__ __align__(16) __nv_bfloat16 vnew[D];
+  __shared__ __align__(16) float pacc[AT_MAX_GROUP][D];
+  __shared__ __align__(8) float pstat[AT_MAX_GROUP][2];
+
+  pdl_launch_dependents();
+  // With state_ready the step state and the cached K/V are not written by any kernel that may
+  // still run, so their reads (and the K/V tile loads) overlap the previous kernel; only the
+  // new token's q/k/v rows wait for it.
+  if (!a.state_ready) pdl_wait();
+
+  // ---- the row's new position and its cache slot (every CTA of the cluster agrees)
+  const int64_t seq = a.row_seq ? a.row_seq[r] : r;
+  const int64_t pos = a.positions[r];
+  bool ok = pos >= 0 && (a.cos_tab == nullptr || pos < a.rope_len);
+  int64_t new_off = 0;
+  if (ok) {
+    const int64_t lp = pos / a.page_size;
+    const int64_t page = a.block_table[seq * a.bt_stride + lp];
+    ok = page >= 0 && page < a.num_pages;
+    new_off = page * a.stride_page + (int64_t)kvh * a.stride_head + (pos - lp * a.page_size) * a.stride_tok;
+  }
+  __nv_bfloat16* out_base = a.out + (r * a.hq + (int64_t)kvh * group) * D;
+  if (!ok) {  // cluster-uniform: no CTA reaches a cluster barrier
+    if (a.state_ready) pdl_wait();  // the output may still be read by an earlier kernel
+    if (rank == 0) {
+      if (tid == 0 && a.error_flag) atomicExch(a.error_flag, 1);
+      for (int e = tid; e < group * D; e += blockDim.x) out_base[e] = __float2bfloat16_rn(0.f);
+    }
+    return;
+  }
+
+  // ---- this CTA's share of the row's tiles; warp w takes tiles w, w + W, ...
+  const int64_t total = pos + 1;
+  const int64_t tiles = (total + AT_TILE - 1) / AT_TILE;
+  const int64_t per = (tiles + S - 1) / S;
+  const int64_t tb = min(tiles, (int64_t)rank * per), te = min(tiles, tb + per);
+  const int ntile = (int)(te - tb);
+  const int64_t t_begin = tb * AT_TILE, t_end = min(total, te * AT_TILE);
+  const bool owns_new = pos >= t_begin && pos < t_end;
+  const int nmine = warp < ntile ? (ntile - warp + W - 1) / W : 0;
+  const int64_t khead = (int64_t)kvh * a.stride_head;
+  bool bad_page = false;
+
+  auto issue = [&](int j) {
+    if (j < nmine) {
+      __nv_bfloat16* kst = ring + (j % AM_STAGES) * AM_STAGE_ELEMS;
+      __nv_bfloat16* vst = kst + AM_TILE_ELEMS;
+      const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
+      const int64_t lp = t0 / a.page_size;
+      const int64_t page = a.block_table[seq * a.bt_stride + lp];
+      const bool page_ok = page >= 0 && page < a.num_pages;
+      bad_page |= !page_ok;
+      const int64_t base = page_ok ? page * a.stride_page + khead + (t0 - lp * a.page_size) * a.stride_tok : 0;
+      const int lim = (int)(t_end - t0), newt = (int)(pos - t0);  // the new token is staged below
+#pragma unroll
+      for (int i = 0; i < AT_TILE * CH / 32; ++i) {
+        const int e = lane + 32 * i;
+        const int t = e >> 4, ch = e & 15;
+        const bool ld = page_ok && t < lim && t != newt;
+        const int64_t off = ld ? base + (int64_t)t * a.stride_tok + ch * 8 : 0;
+        cp_async16_zfill(kst + t * AM_ROW + ch * 8, a.k_cache + off, ld);
+        cp_async16_zfill(vst + t * AM_ROW + ch * 8, a.v_cache + off, ld);
+      }
+    }
+    cp_async_commit_group();
+  };
+#pragma unroll
+  for (int j = 0; j < AM_STAGES - 1; ++j) issue(j);
+  if (a.state_ready) pdl_wait();
+
+  // ---- RoPE of the group's query heads into shared memory (and of the new key / value in
+  // the CTA whose range holds the new position)
+  const float* cr = a.cos_tab ? a.cos_tab + pos * HALF : nullptr;
+  const float* sr = a.sin_tab ? a.sin_tab + pos * HALF : nullptr;
+  const __nv_bfloat16* qrow = a.q_in + r * a.in_stride + (int64_t)kvh * group * D;
+  for (int h = warp; h < group; h += W) rope_head(qrow + (int64_t)h * D, &qs[h][0], HALF, cr, sr, lane, a.q_norm, a.norm_eps);
+  if (owns_new) {
+    if (warp == 0)
+      rope_head(a.k_in + r * a.in_stride + (int64_t)kvh * D, knew, HALF, cr, sr, lane, a.k_norm, a.norm_eps);
+    if (warp == (W > 1 ? 1 : 0))
+      rope_head(a.v_in + r * a.in_stride + (int64_t)kvh * D, vnew, HALF, nullptr, nullptr, lane);
+  }
+  __syncthreads();
+  if (owns_new && tid < 2 * CH) {  // commit the new row to the cache (this CTA alone touches slot pos)
+    if (tid < CH)
+      reinterpret_cast<uint4*>(a.k_cache + new_off)[tid] = reinterpret_cast<const uint4*>(knew)[tid];
+    else
+      reinterpret_cast<uint4*>(a.v_cache + new_off)[tid - CH] = reinterpret_cast<const uint4*>(vnew)[tid - CH];
+  }
+
+  // ---- Q of the group as the mma A operand (rows g and g + 8 are query heads, zero beyond)
+  const bool two_halves = group > 8;
+  uint32_t qa[D / 16][4];
+  {
+    const bool v0 = g < group, v1 = g + 8 < group;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int d0 = ks * 16 + 2 * c;
+      qa[ks][0] = v0 ? *reinterpret_cast<const uint32_t*>(&qs[g][d0]) : 0u;
+      qa[ks][1] = v1 ? *reinterpret_cast<const uint32_t*>(&qs[g + 8][d0]) : 0u;
+      qa[ks][2] = v0 ? *reinterpret_cast<const uint32_t*>(&qs[g][d0 + 8]) : 0u;
+      qa[ks][3] = v1 ? *reinterpret_cast<const uint32_t*>(&qs[g + 8][d0 + 8]) : 0u;
+    }
+  }
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  for (int j = 0; j < nmine; ++j) {
+    cp_async_wait_group<AM_STAGES - 2>();
+    __syncwarp();  // the whole tile is in shared memory; the stage of tile j - 1 is free
+    issue(j + AM_STAGES - 1);
+    __nv_bfloat16* kst = ring + (j % AM_STAGES) * AM_STAGE_ELEMS;
+    __nv_bfloat16* vst = kst + AM_TILE_ELEMS;
+    const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
+    const int64_t newt = pos - t0;
+    if (newt >= 0 && newt < AT_TILE) {  // warp-uniform: stage the new token's K and V row
+      if (lane < CH)
+        reinterpret_cast<uint4*>(kst + newt * AM_ROW)[lane] = reinterpret_cast<const uint4*>(knew)[lane];
+      else
+        reinterpret_cast<uint4*>(vst + newt * AM_ROW)[lane - CH] = reinterpret_cast<const uint4*>(vnew)[lane - CH];
+      __syncwarp();
+    }
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      const __nv_bfloat16* kr = kst + (nt * 8 + (lane & 7)) * AM_ROW + (lane >> 3) * 8;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ks += 2) {
+        uint32_t kb[4];
+        ldmatrix_x4(kb, kr + ks * 16);
+        mma_bf16_16816(s[nt], qa[ks], kb[0], kb[1]);
+        mma_bf16_16816(s[nt], qa[ks + 1], kb[2], kb[3]);
+      }
+    }
+    const int lim = (int)(t_end - t0);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[nt][i] = nt * 8 + 2 * c + (i & 1) < lim ? s[nt][i] * a.scale : -INFINITY;
+    float alpha[2] = {1.f, 1.f};
+    if (!two_halves) s[0][2] = s[0][3] = s[1][2] = s[1][3] = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h == 1 && !two_halves) break;
+      float mx = fmaxf(fmaxf(s[0][2 * h], s[0][2 * h + 1]), fmaxf(s[1][2 * h], s[1][2 * h + 1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(mrow[h], mx);
+      alpha[h] = (mrow[h] == -INFINITY) ? 0.f : expf(mrow[h] - m_new);
+      float sum = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float p = (m_new == -INFINITY) ? 0.f : expf(s[nt][2 * h + i] - m_new);
+          s[nt][2 * h + i] = p;
+          sum += p;
+        }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      lrow[h] = lrow[h] * alpha[h] + sum;
+      mrow[h] = m_new;
+    }
+    const uint32_t pa[4] = {pack_bf16x2(s[0][0], s[0][1]), pack_bf16x2(s[0][2], s[0][3]),
+                            pack_bf16x2(s[1][0], s[1][1]), pack_bf16x2(s[1][2], s[1][3])};
+    const __nv_bfloat16* vrow = vst + (lane & 15) * AM_ROW + (lane >> 4) * 8;
+    if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt) {
+        o[dt][0] *= alpha[0];
+        o[dt][1] *= alpha[0];
+        o[dt][2] *= alpha[1];
+        o[dt][3] *= alpha[1];
+      }
+    }
+#pragma unroll
+    for (int dt = 0; dt < D / 8; dt += 2) {
+      uint32_t vb[4];
+      ldmatrix_x4_trans(vb, vrow + dt * 8);
+      mma_bf16_16816(o[dt], pa, vb[0], vb[1]);
+      mma_bf16_16816(o[dt + 1], pa, vb[2], vb[3]);
+    }
+  }
+  cp_async_wait_group<0>();
+  if (bad_page && a.error_flag) atomicExch(a.error_flag, 1);
+  __syncthreads();  // every warp is done with its ring: the space becomes the merge area
+
+  // ---- merge the W warp states per head in warp order
+  float* mb = reinterpret_cast<float*>(am_smem);  // [W][16 rows][2 + D]
+  {
+    float* mine = mb + (size_t)warp * 16 * (2 + D);
+    if (c == 0) {
+      mine[g * (2 + D)] = mrow[0];
+      mine[g * (2 + D) + 1] = lrow[0];
+      mine[(g + 8) * (2 + D)] = mrow[1];
+      mine[(g + 8) * (2 + D) + 1] = lrow[1];
+    }
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt) {
+      mine[g * (2 + D) + 2 + dt * 8 + 2 * c] = o[dt][0];
+      mine[g * (2 + D) + 2 + dt * 8 + 2 * c + 1] = o[dt][1];
+      mine[(g + 8) * (2 + D) + 2 + dt * 8 + 2 * c] = o[dt][2];
+      mine[(g + 8) * (2 + D) + 2 + dt * 8 + 2 * c + 1] = o[dt][3];
+    }
+  }
+  __syncthreads();
+  float* wts = mb + (size_t)W * 16 * (2 + D);  // [W][16]
+  if (tid < group) {
+    const int h = tid;
+    float mx = -INFINITY;
+    for (int w = 0; w < W; ++w) mx = fmaxf(mx, mb[((size_t)w * 16 + h) * (2 + D)]);
+    float l = 0.f;
+    for (int w = 0; w < W; ++w) {
+      const float* st = mb + ((size_t)w * 16 + h) * (2 + D);
+      const float wt = (st[0] == -INFINITY) ? 0.f : expf(st[0] - mx);
+      wts[w * 16 + h] = wt;
+      l = fmaf(st[1], wt, l);
+    }
+    pstat[h][0] = mx;
+    pstat[h][1] = l;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < group * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx - h * D;
+    float acc = 0.f;
+    for (int w = 0; w < W; ++w) acc = fmaf(mb[((size_t)w * 16 + h) * (2 + D) + 2 + d], wts[w * 16 + h], acc);
+    if (S == 1) {
+      const float l = pstat[h][1];
+      out_base[idx] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+    } else {
+      pacc[h][d] = acc;
+    }
+  }
+  if (S == 1) return;
+
+  // ---- merge the cluster's CTA states per head in rank order
+  constexpr int VD = D / 32;
+  cluster_sync_all();
+  for (int h = rank + S * warp; h < group; h += S * W) {
+    float ms = -INFINITY, ls = 0.f;
+    if (lane < S) {
+      const uint32_t ra = mapa_shared(smem_u32(&pstat[h][0]), (unsigned)lane);
+      ms = ld_shared_cluster_f32(ra);
+      ls = ld_shared_cluster_f32(ra + 4);
+    }
+    const float mx = warp_max(ms);
+    const float wt = (ms == -INFINITY) ? 0.f : expf(ms - mx);
+    const float lsum = warp_sum(ls * wt);
+    const uint32_t acc_addr = smem_u32(&pacc[h][lane * VD]);
+    float ov[VD] = {0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < S; s0 += 8) {
+      float4 av[8];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj)
+        av[jj] = s0 + jj < S ? ld_shared_cluster_v4f32(mapa_shared(acc_addr, (unsigned)(s0 + jj)))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const float w = __shfl_sync(0xffffffffu, wt, (s0 + jj) & 31);
+        ov[0] = fmaf(av[jj].x, w, ov[0]);
+        ov[1] = fmaf(av[jj].y, w, ov[1]);
+        ov[2] = fmaf(av[jj].z, w, ov[2]);
+        ov[3] = fmaf(av[jj].w, w, ov[3]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VD; ++i)
+      out_base[h * D + lane * VD + i] = __float2bfloat16_rn(lsum > 0.f ? ov[i] / lsum : 0.f);
+  }
+  cluster_sync_all();  // peers' shared memory stays alive until every merge has read it
+}
+
 static bool use_mma(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_dim);
 
 // Launch the decode attention for a checked AttnArgs planned with plan_splits: the
@@ -1133,54 +1432,101 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
 
 // ------------------------------------------------------------------ fused decode step (host)
 
-// Cluster size for the fused step: about FD_MIN_TILES tiles per CTA at max_total_tokens, at
-// most 16 (a non-portable cluster; 8 where the device cannot co-schedule 16 of these CTAs),
-// and at most two CTAs per SM over all (row, KV head) clusters.
-template <int D>
-static int fused_cluster_size(int64_t rows, int64_t hkv, int64_t max_total, int group) {
-  const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
-  const int64_t groups = std::max<int64_t>(1, rows * hkv);
-  int64_t s = std::min<int64_t>(FD_MAX_CLUSTER, (tiles + FD_MIN_TILES - 1) / FD_MIN_TILES);
-  s = std::min<int64_t>(s, std::max<int64_t>(1, 2 * num_sms() / groups));
-  if (s > 8) {
-    static int fits16[AT_MAX_GROUP + 1] = {};  // 0 unknown, 1 yes, -1 no (per group size)
-    if (fits16[group] == 0) {
-      fits16[group] = -1;
-      auto kern = rope_append_attention_kernel<D>;
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(FD_MAX_CLUSTER, 1);
-        cfg.blockDim = dim3(32 * group);
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = FD_MAX_CLUSTER;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) fits16[group] = 1;
-      }
-      cudaGetLastError();
-    }
-    if (fits16[group] < 0) s = 8;
+// Whether the 16-CTA cluster fits for this kernel and block (non-portable size; 8 otherwise).
+template <typename Kern>
+static bool fused_cluster16_fits(Kern kern, int threads, size_t smem) {
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+      (smem > 48 * 1024 &&
+       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)) {
+    cudaGetLastError();
+    return false;
   }
-  return (int)s;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(FD_MAX_CLUSTER, 1);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = FD_MAX_CLUSTER;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  const bool ok = cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0;
+  cudaGetLastError();
+  return ok;
 }
 
-template <int D>
-static int launch_fused(const FusedArgs& a, int64_t max_total, cudaStream_t st) {
+// Launch plan of the fused step: CTAs per (row, KV head) cluster and warps per CTA.
+//  * tensor-core kernel (head_dim 128, pages of a multiple of 16 tokens): a power of two of
+//    CTAs with about FD_MMA_MIN_TILES tiles each at max_total_tokens, up to 4 warps;
+//  * scalar kernel: about FD_MIN_TILES tiles per CTA, one warp per query head.
+// At most 16 CTAs (8 where the device cannot co-schedule 16 of them) and two per SM over
+// all (row, KV head) clusters.
+#ifndef FD_MMA_MIN_TILES
+#define FD_MMA_MIN_TILES 4
+#endif
+struct FusedPlan {
+  bool mma;
+  int cluster;
+  int warps;
+};
+
+static FusedPlan fused_plan(int64_t rows, int64_t hkv, int64_t head_dim, int64_t page_size, int64_t max_total,
+                            int group) {
+  FusedPlan p{head_dim == 128 && page_size % AT_TILE == 0, 1, group};
+  const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
+  const int64_t groups = std::max<int64_t>(1, rows * hkv);
+  int64_t s = (tiles + (p.mma ? FD_MMA_MIN_TILES : FD_MIN_TILES) - 1) / (p.mma ? FD_MMA_MIN_TILES : FD_MIN_TILES);
+  s = std::min<int64_t>(s, FD_MAX_CLUSTER);
+  s = std::min<int64_t>(s, std::max<int64_t>(1, 2 * num_sms() / groups));
+  if (p.mma) {
+    int64_t pw = 1;
+    while (pw * 2 <= s) pw *= 2;
+    s = pw;
+    p.warps = (int)std::min<int64_t>(AM_MAX_WARPS, (tiles + s - 1) / s);
+  }
+  if (s > 8) {
+    static int fits[2][AT_MAX_GROUP + 1] = {};  // 0 unknown, 1 yes, -1 no
+    int& f = fits[p.mma ? 1 : 0][p.mma ? p.warps : group];
+    if (f == 0) {
+      const bool ok = p.mma ? fused_cluster16_fits(rope_append_attention_mma_kernel, 32 * p.warps,
+                                                   am_smem_bytes(AM_MAX_WARPS))
+                            : (head_dim == 128 ? fused_cluster16_fits(rope_append_attention_kernel<128>, 32 * group, 0)
+                                               : fused_cluster16_fits(rope_append_attention_kernel<64>, 32 * group, 0));
+      f = ok ? 1 : -1;
+    }
+    if (f < 0) s = 8;
+  }
+  p.cluster = (int)s;
+  return p;
+}
+
+static int launch_fused(const FusedArgs& a, int64_t head_dim, int64_t max_total, cudaStream_t st) {
   const int group = (int)(a.hq / a.hkv);
-  const int s = fused_cluster_size<D>(a.rows, a.hkv, max_total, group);
+  const FusedPlan p = fused_plan(a.rows, a.hkv, head_dim, a.page_size, max_total, group);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)s, (unsigned)(a.rows * a.hkv));
-  cfg.blockDim = dim3((unsigned)(32 * group));
+  cfg.gridDim = dim3((unsigned)p.cluster, (unsigned)(a.rows * a.hkv));
+  cfg.blockDim = dim3((unsigned)(32 * (p.mma ? p.warps : group)));
+  cfg.dynamicSmemBytes = p.mma ? am_smem_bytes(p.warps) : 0;
   cfg.stream = st;
+  if (p.mma) {
+    static size_t configured = 0;
+    if (cfg.dynamicSmemBytes > configured) {
+      const cudaError_t e = cudaFuncSetAttribute(rope_append_attention_mma_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)am_smem_bytes(AM_MAX_WARPS));
+      if (e != cudaSuccess)
+        return fail(MRB_ERR_CUDA, "rope_append_attention: smem attribute: %s", cudaGetErrorString(e));
+      configured = am_smem_bytes(AM_MAX_WARPS);
+    }
+  }
   cudaLaunchAttribute attr[2];
   int n = 0;
-  if (s > 1) {
+  if (p.cluster > 1) {
     attr[n].id = cudaLaunchAttributeClusterDimension;
-    attr[n].val.clusterDim.x = (unsigned)s;
+    attr[n].val.clusterDim.x = (unsigned)p.cluster;
     attr[n].val.clusterDim.y = 1;
     attr[n].val.clusterDim.z = 1;
     ++n;
@@ -1192,7 +1538,10 @@ static int launch_fused(const FusedArgs& a, int64_t max_total, cudaStream_t st) 
   }
   cfg.attrs = n ? attr : nullptr;
   cfg.numAttrs = n;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, rope_append_attention_kernel<D>, a);
+  const cudaError_t e =
+      p.mma ? cudaLaunchKernelEx(&cfg, rope_append_attention_mma_kernel, a)
+            : (head_dim == 128 ? cudaLaunchKernelEx(&cfg, rope_append_attention_kernel<128>, a)
+                               : cudaLaunchKernelEx(&cfg, rope_append_attention_kernel<64>, a));
   if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "rope_append_attention: launch: %s", cudaGetErrorString(e));
   return launch_status("rope_append_attention");
 }
@@ -1200,10 +1549,8 @@ static int launch_fused(const FusedArgs& a, int64_t max_total, cudaStream_t st) 
 extern "C" int mrb_rope_append_attention_cluster(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
                                                  int64_t max_total_tokens) {
   if (rows <= 0 || hq <= 0 || hkv <= 0 || hq % hkv || hq / hkv > AT_MAX_GROUP) return 0;
-  const int group = (int)(hq / hkv);
-  if (head_dim == 128) return fused_cluster_size<128>(rows, hkv, max_total_tokens, group);
-  if (head_dim == 64) return fused_cluster_size<64>(rows, hkv, max_total_tokens, group);
-  return 0;
+  if (head_dim != 128 && head_dim != 64) return 0;
+  return fused_plan(rows, hkv, head_dim, AT_TILE, max_total_tokens, (int)(hq / hkv)).cluster;
 }
 
 extern "C" int mrb_rope_append_attention(const void* q_in, const void* k_in, const void* v_in, int64_t in_row_stride,
@@ -1214,7 +1561,7 @@ extern "C" int mrb_rope_append_attention(const void* q_in, const void* k_in, con
                                          int64_t stride_page, int64_t stride_head, int64_t stride_tok,
                                          int64_t page_size, const int32_t* block_table, int64_t block_table_stride,
                                          int64_t num_pages, int32_t* error_flag, float scale,
-                                         int64_t max_total_tokens, void* out, void* stream) {
+                                         int64_t max_total_tokens, int state_ready, void* out, void* stream) {
   if (rows < 0 || hq <= 0 || hkv <= 0 || hq % hkv || page_size <= 0 || num_pages <= 0 || max_total_tokens < 0)
     return fail(MRB_ERR_ARG, "rope_append_attention: bad shape");
   if (hq / hkv > AT_MAX_GROUP)
@@ -1239,9 +1586,8 @@ extern "C" int mrb_rope_append_attention(const void* q_in, const void* k_in, con
               rows, hq, hkv, positions, row_seq, rope_cos, rope_sin, rope_len, (const __nv_bfloat16*)q_norm,
               (const __nv_bfloat16*)k_norm, norm_eps, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, stride_page,
               stride_head, stride_tok, page_size, block_table, block_table_stride, num_pages, error_flag, scale,
-              (__nv_bfloat16*)out};
-  return head_dim == 128 ? launch_fused<128>(a, max_total_tokens, (cudaStream_t)stream)
-                         : launch_fused<64>(a, max_total_tokens, (cudaStream_t)stream);
+              (__nv_bfloat16*)out, state_ready ? 1 : 0};
+  return launch_fused(a, head_dim, max_total_tokens, (cudaStream_t)stream);
 }
 
 // ------------------------------------------------------------------ decode-step bookkeeping

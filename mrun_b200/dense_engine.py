@@ -287,10 +287,12 @@ class DenseDecoder:
         for i, layer in enumerate(w.layers):
             linear(layer.qkv, normed, qkv, bias=layer.qkv_bias)
             if fused:
+                # the step's bookkeeping (decode_advance) runs after every layer: the step state
+                # and the cached K/V are settled when a layer's attention starts
                 self.kv.append_attend(
                     i, qkv, qkv[:, qd:], qkv[:, qd + kd:], positions, token_rows, num_heads=cfg.heads,
                     max_total_tokens=max_total, in_row_stride=cfg.qkv_rows, rope=(self.cos, self.sin),
-                    error_flag=self.error_flag, scale=self.scale, out=ctx,
+                    error_flag=self.error_flag, scale=self.scale, out=ctx, state_ready=True,
                 )
             else:
                 self.kv.append(

@@ -128,13 +128,14 @@ class PagedKVCache:
         error_flag: torch.Tensor | None = None,
         scale: float | None = None,
         out: torch.Tensor | None = None,
+        state_ready: bool = False,
     ) -> torch.Tensor:
         """``append`` then ``attend`` for one decode token per sequence, in one launch."""
         return rope_append_attention(
             q_rows, k_rows, v_rows, self.k[layer], self.v[layer], strides=self.strides, page_size=self.page_size,
             block_table=self.block_table, positions=positions, row_seq=row_seq, num_heads=num_heads,
             max_total_tokens=max_total_tokens, in_row_stride=in_row_stride, rope=rope, qk_norm=qk_norm,
-            norm_eps=norm_eps, error_flag=error_flag, scale=scale, out=out,
+            norm_eps=norm_eps, error_flag=error_flag, scale=scale, out=out, state_ready=state_ready,
         )
 
     def workspace_bytes(self, rows: int, num_heads: int, max_total_tokens: int) -> int:

@@ -164,12 +164,15 @@ def rope_append_attention(
     error_flag: torch.Tensor | None = None,
     scale: float | None = None,
     out: torch.Tensor | None = None,
+    state_ready: bool = False,
 ) -> torch.Tensor:
     """One decode token per row in one launch: ``rope_kv_append`` of the row's new position
     followed by ``paged_attention`` over positions ``[0, positions[r]]``.
 
     Every row must continue a different sequence (``row_seq`` distinct): a row reads only
-    cache entries written before this call plus its own new token. Returns bf16
+    cache entries written before this call plus its own new token. ``state_ready``: the
+    positions, block table and cached K/V are not written by a kernel still in flight, so the
+    kernel may read them before waiting on the previous launch. Returns bf16
     ``[rows, num_heads, head_dim]``."""
     rows = int(positions.numel())
     hkv, d = int(k_cache.shape[1]), int(k_cache.shape[-1])
@@ -194,7 +197,7 @@ def rope_append_attention(
         _lib.ptr(qk_norm[1] if qk_norm else None), float(norm_eps), k_cache.data_ptr(), v_cache.data_ptr(),
         strides[0], strides[1], strides[2], page_size, block_table.data_ptr(),
         int(block_table.stride(0)) if block_table.ndim > 1 else 1, int(k_cache.shape[0]), _lib.ptr(error_flag), sc,
-        int(max_total_tokens), out.data_ptr(), _lib.stream_handle(device),
+        int(max_total_tokens), 1 if state_ready else 0, out.data_ptr(), _lib.stream_handle(device),
     )
     return out
 

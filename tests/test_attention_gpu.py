@@ -232,13 +232,16 @@ def test_rope_append_attention_vs_separate_and_oracle(rows, hq, hkv, d, position
     ref = bf16_round(oatt.gqa_decode_rows(q, keys, vals))
     assert max_rel_err(fused.float().cpu().numpy(), ref) < TOL
     assert max_rel_err(fused.float().cpu().numpy(), sep.float().cpu().numpy()) < TOL
-    # deterministic: a second run on the same inputs gives identical bits
+    # deterministic: a second run on the same inputs gives identical bits, also when the step
+    # state is read before the dependency wait (state_ready: nothing in flight writes it)
     cache.k.copy_(k0)
     cache.v.copy_(v0)
+    torch.cuda.synchronize()
     again = cache.append_attend(0, qkv_dev, qkv_dev[:, hq * d:], qkv_dev[:, (hq + hkv) * d:], pos_dev, seq_dev,
                                 num_heads=hq, max_total_tokens=max_total, in_row_stride=width, rope=rope,
-                                qk_norm=norms, error_flag=err)
+                                qk_norm=norms, error_flag=err, state_ready=True)
     assert torch.equal(again, fused)
+    assert torch.equal(cache.k, k_sep) and torch.equal(cache.v, v_sep)
 
 
 def test_rope_append_attention_bad_position_flags_and_zeroes(cuda):
