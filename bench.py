@@ -640,6 +640,76 @@ def run_attn_case(args) -> None:
                       "kv_gbs": kv_bytes / avg_s / 1e9, "launches": args.steps}), flush=True)
 
 
+def run_qstore_ingest_case(args) -> None:
+    """On-disk QStore ingestion: 16 int8 blocks of the config-2 down-projection shape
+    (3584 x 18944, 1.09 GB) written to a temporary store, then read into HBM (a) directly, one
+    block at a time through pinned staging, (b) through the prefetch ring while a W8A16 GEMV
+    consumes every page, and (c) as the reference stages blocks (numpy memory map copied into
+    pinned memory by 3 threads, then one host-to-device copy). The files stay in the page
+    cache (reads do not drop them), so this measures host memory to HBM, not the disk. Prints
+    GB/s of store bytes per pass; not the bench metric."""
+    import shutil
+    import tempfile
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+    import torch
+
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+    from mrun_b200.qstore import QStore
+    from mrun_b200.qstore_build import write_qstore
+
+    device = torch.device("cuda", 0)
+    rows, cols, nblocks = 3584, 18944, 16
+    tmp = Path(tempfile.mkdtemp(prefix="qstore-bench-"))
+    try:
+        base = (np.arange(rows * cols, dtype=np.int64) % 251 - 125).astype(np.int8).reshape(rows, cols)
+        scales = np.full(rows, 0.01, np.float32)
+        write_qstore(tmp / "m", qrows={f"b{i}": (base, scales) for i in range(nblocks)},
+                     fp32={"n": np.ones(cols, np.float32)})
+        names = [f"b{i}" for i in range(nblocks)]
+        per_pass = nblocks * (rows * cols + rows * 4)
+        x = torch.randn(1, cols, device=device).to(torch.bfloat16)
+
+        def timed(fn, passes=3):
+            fn()  # warm-up pass (and the ring's learning pass)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(passes):
+                fn()
+            torch.cuda.synchronize()
+            return passes * per_pass / (time.perf_counter() - t0) / 1e9
+
+        with QStore("m", root=tmp, device=device, enable_prefetch_ring=False, drop_read_pages=False) as store:
+            direct = timed(lambda: [store.page(n) for n in names])
+        with QStore("m", root=tmp, device=device, enable_prefetch_ring=True, drop_read_pages=False) as store:
+            ring = timed(lambda: [qrow_linear((p := store.page(n)).codes, p.scales, x) for n in names])
+            stats = store.ring_stats()
+        # the reference's staging: memmap -> pinned (3 copy threads) -> one H2D per block
+        mm = np.memmap(tmp / "m" / "weights.i8", dtype=np.int8, mode="r")
+        pinned = torch.empty(rows * cols, dtype=torch.int8, pin_memory=True)
+        dst = pinned.numpy()
+        pool = ThreadPoolExecutor(3)
+        chunk = 8 << 20
+
+        def ref_pass():
+            for i in range(nblocks):
+                src = mm[i * rows * cols:(i + 1) * rows * cols]
+                list(pool.map(lambda a: np.copyto(dst[a:a + chunk], src[a:a + chunk]), range(0, rows * cols, chunk)))
+                dev = torch.empty(rows * cols, dtype=torch.int8, device=device)
+                dev.copy_(pinned, non_blocking=True)
+                torch.cuda.current_stream(device).synchronize()
+
+        reference_style = timed(ref_pass)
+        pool.shutdown()
+        del mm
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    print(json.dumps({"case": args.case, "store_bytes_per_pass": per_pass, "direct_gbs": direct,
+                      "ring_with_gemv_gbs": ring, "reference_style_gbs": reference_style, "ring_stats": stats,
+                      "source": "page cache (host memory)"}), flush=True)
+
+
 def run_fused_attn_case(args) -> None:
     """Small case for kernel captures: the fused decode step (RoPE + KV append + attention,
     one clustered launch) at the config-2 shape -- one row, 28 query / 4 KV heads, 600 cached
@@ -956,7 +1026,7 @@ def main() -> None:
                     help="moe-decode on N GPUs: expert exchange over NVLink peer memory or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
-                                       *TC_CASES, *ATTN_CASES, "attn-fused1", *EXPERT_CASES],
+                                       *TC_CASES, *ATTN_CASES, "attn-fused1", "qstore-ingest", *EXPERT_CASES],
                     default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
@@ -968,6 +1038,8 @@ def main() -> None:
         run_attn_case(args)
     elif args.case == "attn-fused1":
         run_fused_attn_case(args)
+    elif args.case == "qstore-ingest":
+        run_qstore_ingest_case(args)
     elif args.case in EXPERT_CASES:
         run_expert_case(args)
     elif args.case in TC_CASES:

@@ -9,14 +9,15 @@
  *   MRB_ERR_ARG (1)       an argument failed validation (the Python mirror raises ValueError)
  *   MRB_ERR_CUDA (2)      a CUDA launch or runtime call failed (RuntimeError)
  *   MRB_ERR_UNSUPPORTED (3) a valid request outside this build's kernels (RuntimeError)
+ *   MRB_ERR_IO (4)        an operating-system file call failed (OSError)
  *
  * mrb_last_error() returns the message of the last failing call on the calling thread.
  * Layouts follow the reference QStore: a "qrow" matrix is int8 codes [rows, cols] row-major
  * with one fp32 scale per row (weight = code * scale), exactly as written by
  * `_quant_row_int8` (mrun engine/kernels/qstore_build.py:496-501).
  *
- * The reference is pure Python; the ctypes binding a maintainer would add on its side is
- * shown in INTEGRATION.md. Each entry point names the reference function it replaces.
+ * The reference is pure Python; a maintainer binds these entry points on its side with
+ * ctypes. Each entry point names the reference function it replaces.
  */
 #ifndef MRUN_B200_H
 #define MRUN_B200_H
@@ -33,6 +34,7 @@ enum {
   MRB_ERR_ARG = 1,
   MRB_ERR_CUDA = 2,
   MRB_ERR_UNSUPPORTED = 3,
+  MRB_ERR_IO = 4,
 };
 
 /* Element types of activation/output buffers. */
@@ -268,6 +270,28 @@ int mrb_ep_p2p_return(const void *eo_bf16, const int64_t *inverse, int64_t hidde
                       void *stream);
 int mrb_ep_p2p_wait_return(void *mailbox, int64_t world, int64_t capacity, int64_t hidden,
                            int32_t *state, void *stream);
+
+/* ---------------------------------------------------------------- on-disk stores */
+
+/* Open a store file (a QStore's weights.i8 / scales.f32 / extras.f32, an expert page file)
+ * for reading: *handle receives the reader, *size the file's length in bytes. Host only.
+ * Replaces the numpy memory maps of `QStore.__init__` (engine/kernels/qstore.py:700-714). */
+int mrb_store_file_open(const char *path, void **handle, uint64_t *size);
+/* Close a reader from mrb_store_file_open (NULL: no-op). */
+int mrb_store_file_close(void *handle);
+/* Copy bytes [offset, offset + bytes) of the file into host memory dst (normally a pinned
+ * staging buffer), split over up to `threads` parallel pread calls of 4 MiB pieces (the
+ * calling thread is one of them; small ranges use it alone). drop_after != 0 then asks the
+ * kernel to drop the range's cached pages (POSIX_FADV_DONTNEED). A range past the end of the
+ * file is MRB_ERR_ARG; a failed or short read is MRB_ERR_IO. Safe to call from several
+ * threads at once (pread does not move a shared offset). Replaces the mmap-to-pinned copy of
+ * `_RingPrefetch._stage` (engine/kernels/qstore.py:622-660, with `_drop_mmap_pages`
+ * :402-426) and the pread warm-up of `HostPageTier.warm` (engine/qwen3_moe_cuda.py:925-951). */
+int mrb_store_file_read(void *handle, uint64_t offset, uint64_t bytes, void *dst, int threads,
+                        int drop_after);
+/* Read-ahead hint for a range the caller expects to read next (will_need != 0:
+ * POSIX_FADV_WILLNEED) or no longer needs (0: POSIX_FADV_DONTNEED); clipped to the file. */
+int mrb_store_file_advise(void *handle, uint64_t offset, uint64_t bytes, int will_need);
 
 /* ---------------------------------------------------------------- (c) paged-KV decode attention */
 

@@ -20,6 +20,7 @@ MRB_OK = 0
 MRB_ERR_ARG = 1
 MRB_ERR_CUDA = 2
 MRB_ERR_UNSUPPORTED = 3
+MRB_ERR_IO = 4
 
 MRB_F32 = 0
 MRB_BF16 = 1
@@ -57,6 +58,10 @@ SIGNATURES: dict[str, list] = {
                                   _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, c_float, _I64, c_int, _P,
                                   _P],
     "mrb_rope_append_attention_cluster": [_I64, _I64, _I64, _I64, _I64],
+    "mrb_store_file_open": [ctypes.c_char_p, ctypes.POINTER(c_void_p), ctypes.POINTER(ctypes.c_uint64)],
+    "mrb_store_file_close": [_P],
+    "mrb_store_file_read": [_P, ctypes.c_uint64, ctypes.c_uint64, _P, c_int, c_int],
+    "mrb_store_file_advise": [_P, ctypes.c_uint64, ctypes.c_uint64, c_int],
     "mrb_paged_attention_workspace": [_I64, _I64, _I64, _I64, _I64],
     "mrb_paged_attention": [_P, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P,
                             _P, _P, c_float, _I64, _P, _P, c_size_t, _P],
@@ -117,6 +122,8 @@ def check(status: int, what: str) -> None:
     text = f"{what}: {message}" if message else f"{what}: status {status}"
     if status == MRB_ERR_ARG:
         raise ValueError(text)
+    if status == MRB_ERR_IO:
+        raise OSError(text)
     raise MrbError(text)
 
 

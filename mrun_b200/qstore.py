@@ -1,0 +1,529 @@
+"""On-disk QStore reader: int8 row-quantised pages from disk to HBM through pinned staging.
+
+Reads the reference's paged store directory (engine/kernels/qstore.py:662-1128): a
+``manifest.json`` whose ``blocks`` table maps each name to a ``qrow`` block (int8 codes
+``[out, in]`` at ``w_off`` in ``weights.i8`` plus fp32 row scales at ``s_off`` in
+``scales.f32``), an ``fp32`` block (at ``e_off`` in ``extras.f32``) or an ``alias`` of another
+name. Bytes come off disk through the library's parallel ``pread`` reader
+(``mrb_store_file_read``) straight into pinned host buffers, then one asynchronous copy puts
+them in HBM, where the B200 kernels consume the codes as they are (no fp32 weight copy).
+
+``_PageRing`` is the B200 counterpart of the reference's successor-oracle ``_RingPrefetch``
+(engine/kernels/qstore.py:459-660): it learns which block follows which, stages the predicted
+next blocks into reusable pinned slots on a worker thread (the reads release the GIL) and
+issues their host-to-device copies on a dedicated stream, so a decode loop's disk and PCIe
+traffic overlaps its kernels. A hit returns the same bytes as a direct read.
+
+The manifest's content-identity and provenance digests are not verified here (the
+reference's identity layer is outside this path); the block layout is validated as the
+reference validates it (engine/kernels/qstore.py:124-219).
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import math
+import threading
+from collections import OrderedDict
+from collections.abc import Mapping
+from concurrent.futures import Future, ThreadPoolExecutor
+from pathlib import Path
+from typing import Any
+
+import numpy as np
+import torch
+
+from . import _lib
+from .dense_qstore_cuda import CompactQRowPage, qrow_linear
+
+QSTORE_FILES = ("weights.i8", "scales.f32", "extras.f32")
+DEFAULT_READ_THREADS = 8
+
+
+# ------------------------------------------------------------------ native file reader
+
+
+class StoreFile:
+    """One store file opened for parallel positional reads (``mrb_store_file_*``)."""
+
+    def __init__(self, path: str | Path) -> None:
+        self.path = Path(path)
+        handle = ctypes.c_void_p()
+        size = ctypes.c_uint64()
+        _lib.call("mrb_store_file_open", str(self.path).encode(), ctypes.byref(handle), ctypes.byref(size))
+        self._handle = handle.value
+        self.size = int(size.value)
+        self._lock = threading.Lock()
+
+    def read_into(self, offset: int, nbytes: int, dst: np.ndarray | torch.Tensor, *, threads: int = 1,
+                  drop_after: bool = False) -> None:
+        """Copy file bytes [offset, offset + nbytes) into the start of host buffer ``dst``."""
+        if isinstance(dst, torch.Tensor):
+            if dst.is_cuda or not dst.is_contiguous():
+                raise ValueError("destination must be a contiguous host tensor")
+            capacity, address = dst.numel() * dst.element_size(), dst.data_ptr()
+        else:
+            if not dst.flags["C_CONTIGUOUS"] or not dst.flags["WRITEABLE"]:
+                raise ValueError("destination must be a writable contiguous array")
+            capacity, address = dst.nbytes, dst.ctypes.data
+        if nbytes > capacity:
+            raise ValueError(f"destination holds {capacity} bytes, {nbytes} requested")
+        if self._handle is None:
+            raise ValueError(f"{self.path} is closed")
+        _lib.call("mrb_store_file_read", self._handle, int(offset), int(nbytes), address, int(threads),
+                  1 if drop_after else 0)
+
+    def advise(self, offset: int, nbytes: int, *, will_need: bool = True) -> None:
+        if self._handle is not None:
+            _lib.call("mrb_store_file_advise", self._handle, int(offset), int(nbytes), 1 if will_need else 0)
+
+    def close(self) -> None:
+        with self._lock:
+            handle, self._handle = self._handle, None
+        if handle is not None:
+            _lib.call("mrb_store_file_close", handle)
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order varies
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ manifest
+
+
+def _int_field(block: Mapping[str, Any], key: str, *, positive: bool = False) -> int:
+    value = block.get(key)
+    if isinstance(value, bool) or not isinstance(value, int):
+        raise RuntimeError(f"QStore block field {key!r} must be an integer")
+    if value < (1 if positive else 0):
+        raise RuntimeError(f"QStore block field {key!r} must be {'positive' if positive else 'non-negative'}")
+    return value
+
+
+def _shape_field(block: Mapping[str, Any], dims: int | None = None) -> tuple[int, ...]:
+    raw = block.get("shape")
+    if not isinstance(raw, list) or not raw:
+        raise RuntimeError("QStore block shape must be a non-empty list")
+    if any(isinstance(v, bool) or not isinstance(v, int) or v <= 0 for v in raw):
+        raise RuntimeError("QStore block shape dimensions must be positive integers")
+    if dims is not None and len(raw) != dims:
+        raise RuntimeError(f"QStore block shape must have {dims} dimensions")
+    return tuple(raw)
+
+
+def validate_int8_layout(directory: Path, manifest: Mapping[str, Any]) -> None:
+    """The reference's int8 layout contract (engine/kernels/qstore.py:124-219): every block
+    well formed, aliases resolve without cycles, and in each file the referenced ranges tile
+    the whole file with no gap and no overlap. Raises RuntimeError otherwise."""
+    if manifest.get("dtype") != "int8":
+        raise RuntimeError("QStore must declare dtype='int8'")
+    blocks = manifest.get("blocks")
+    if not isinstance(manifest.get("config"), Mapping) or not isinstance(blocks, Mapping) or not blocks:
+        raise RuntimeError("QStore requires config and a non-empty block table")
+    ranges: dict[str, list[tuple[int, int, str]]] = {name: [] for name in QSTORE_FILES}
+    n_qrow = n_fp32 = 0
+    for name, block in blocks.items():
+        if not isinstance(name, str) or not name or not isinstance(block, Mapping):
+            raise RuntimeError("QStore block names and descriptors must be non-empty mappings")
+        if "alias" in block:
+            if not isinstance(block.get("alias"), str) or not block["alias"]:
+                raise RuntimeError(f"QStore alias {name!r} has an invalid target")
+            continue
+        kind = block.get("kind")
+        if kind == "qrow":
+            rows, cols = _shape_field(block, 2)
+            w_off, w_len = _int_field(block, "w_off"), _int_field(block, "w_len", positive=True)
+            s_off, s_len = _int_field(block, "s_off"), _int_field(block, "s_len", positive=True)
+            if w_len != rows * cols:
+                raise RuntimeError(f"QStore qrow {name!r} weight length does not match its shape")
+            if s_len != rows * 4 or s_off % 4:
+                raise RuntimeError(f"QStore qrow {name!r} scale range does not match its shape")
+            ranges["weights.i8"].append((w_off, w_off + w_len, name))
+            ranges["scales.f32"].append((s_off, s_off + s_len, name))
+            n_qrow += 1
+        elif kind == "fp32":
+            shape = _shape_field(block)
+            e_off, e_len = _int_field(block, "e_off"), _int_field(block, "e_len", positive=True)
+            if e_len != math.prod(shape) * 4 or e_off % 4:
+                raise RuntimeError(f"QStore fp32 {name!r} range does not match its shape")
+            ranges["extras.f32"].append((e_off, e_off + e_len, name))
+            n_fp32 += 1
+        else:
+            raise RuntimeError(f"QStore block {name!r} has unsupported kind {kind!r}")
+    if not n_qrow or not n_fp32:
+        raise RuntimeError("QStore requires qrow and fp32 blocks")
+    for name, block in blocks.items():
+        if "alias" not in block:
+            continue
+        seen, target = {name}, block["alias"]
+        while True:
+            if target not in blocks:
+                raise RuntimeError(f"QStore alias {name!r} targets missing block {target!r}")
+            if target in seen:
+                raise RuntimeError(f"QStore alias cycle contains {target!r}")
+            seen.add(target)
+            if not isinstance(blocks[target], Mapping):
+                raise RuntimeError(f"QStore alias {name!r} targets an invalid block")
+            nxt = blocks[target].get("alias")
+            if nxt is None:
+                break
+            if not isinstance(nxt, str) or not nxt:
+                raise RuntimeError(f"QStore alias {target!r} has an invalid target")
+            target = nxt
+    for filename, spans in ranges.items():
+        path = directory / filename
+        if not path.is_file():
+            raise RuntimeError(f"QStore file is missing: {filename}")
+        size = path.stat().st_size
+        end = 0
+        for lo, hi, name in sorted(spans):
+            if hi > size:
+                raise RuntimeError(f"QStore {filename} range for block {name!r} exceeds file bounds")
+            if lo < end:
+                raise RuntimeError(f"QStore {filename} ranges overlap at block {name!r}")
+            if lo != end:
+                raise RuntimeError(f"QStore {filename} has an unreferenced gap before block {name!r}")
+            end = hi
+        if end != size:
+            raise RuntimeError(f"QStore {filename} block ranges do not cover the complete file")
+
+
+def _resolve_in(blocks: Mapping[str, Any], name: str) -> Mapping[str, Any]:
+    """Follow alias links (engine/kernels/qstore.py:928-942); KeyError for a missing name."""
+    key = str(name)
+    seen: set[str] = set()
+    while True:
+        if key in seen:
+            raise RuntimeError(f"QStore alias cycle contains {key!r}")
+        seen.add(key)
+        if key not in blocks:
+            raise KeyError(f"QStore has no block {key!r}")
+        block = blocks[key]
+        if not isinstance(block, Mapping):
+            raise RuntimeError(f"QStore block {key!r} is not a mapping")
+        if "alias" not in block:
+            return block
+        key = str(block["alias"])
+
+
+def load_manifest(directory: str | Path) -> dict[str, Any]:
+    directory = Path(directory)
+    manifest = json.loads((directory / "manifest.json").read_text(encoding="utf-8"))
+    if not isinstance(manifest, dict):
+        raise RuntimeError("QStore manifest must be a JSON object")
+    validate_int8_layout(directory, manifest)
+    return manifest
+
+
+# ------------------------------------------------------------------ prefetch ring
+
+
+class _RingSlot:
+    """One staging lane: pinned host buffers reused across prefetches, plus the device
+    tensors of the block in flight and the event that marks its host-to-device copy."""
+
+    __slots__ = ("pinned_q", "pinned_s", "dev_q", "dev_s", "event", "future", "name", "shape")
+
+    def __init__(self) -> None:
+        self.pinned_q: torch.Tensor | None = None
+        self.pinned_s: torch.Tensor | None = None
+        self.dev_q: torch.Tensor | None = None
+        self.dev_s: torch.Tensor | None = None
+        self.event: torch.cuda.Event | None = None  # kept across releases: the pinned
+        self.future: Future | None = None           # buffers are reused only after it
+        self.name: str | None = None
+        self.shape: tuple[int, int] | None = None
+
+    def release(self) -> None:
+        self.dev_q = self.dev_s = None
+        self.future = None
+        self.name = None
+        self.shape = None
+
+
+class _PageRing:
+    """Successor-oracle prefetch of qrow blocks (engine/kernels/qstore.py:485-660).
+
+    ``observe(name)`` records that ``name`` followed the previous access and stages the
+    ``depth`` predicted successors; ``take(name)`` hands back a staged block (waiting on its
+    copy event from the caller's stream) or None. A mispredicted block is evicted when its
+    slot is needed."""
+
+    def __init__(self, store: "QStore", *, slots: int, depth: int) -> None:
+        self.store = store
+        self.depth = max(1, int(depth))
+        self.device = store.device
+        self.stream = torch.cuda.Stream(device=self.device)
+        self.pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="qstore-ring")
+        self.slots = [_RingSlot() for _ in range(max(2, int(slots)))]
+        self.inflight: OrderedDict[str, _RingSlot] = OrderedDict()
+        self.successor: dict[str, str] = {}
+        self.last_access: str | None = None
+        self.stats = {"hits": 0, "late_hits": 0, "misses": 0, "prefetches": 0, "staged": 0, "prefetch_bytes": 0,
+                      "evicted_unused": 0, "successor_entries": 0}
+
+    def preallocate(self, max_codes: int, max_rows: int) -> None:
+        """Pinned buffers of every slot, allocated on the calling thread once."""
+        for slot in self.slots:
+            slot.pinned_q = torch.empty(max_codes, dtype=torch.int8, pin_memory=True)
+            slot.pinned_s = torch.empty(max_rows, dtype=torch.float32, pin_memory=True)
+
+    def close(self) -> None:
+        for slot in self.inflight.values():
+            if slot.future is not None:
+                slot.future.result()
+            slot.release()
+        self.inflight.clear()
+        self.pool.shutdown(wait=True)
+
+    def take(self, name: str) -> tuple[torch.Tensor, torch.Tensor] | None:
+        slot = self.inflight.pop(name, None)
+        if slot is None:
+            self.stats["misses"] += 1
+            return None
+        assert slot.future is not None
+        self.stats["hits" if slot.future.done() else "late_hits"] += 1
+        slot.future.result()  # staged and its copy issued (re-raises a staging error)
+        consumer = torch.cuda.current_stream(self.device)
+        consumer.wait_event(slot.event)
+        # allocated on the ring stream, used on the consumer's: keep the allocator from
+        # handing the memory to the next prefetch while consumer kernels still read it
+        slot.dev_q.record_stream(consumer)
+        slot.dev_s.record_stream(consumer)
+        rows, cols = slot.shape
+        codes, scales = slot.dev_q.view(rows, cols), slot.dev_s
+        slot.release()
+        return codes, scales
+
+    def observe(self, name: str) -> None:
+        if self.last_access is not None and self.last_access != name:
+            self.successor[self.last_access] = name
+            self.stats["successor_entries"] = len(self.successor)
+        self.last_access = name
+        nxt: str | None = name
+        for _ in range(self.depth):
+            nxt = self.successor.get(nxt)
+            if nxt is None:
+                return
+            self._prefetch(nxt)
+
+    def _free_slot(self) -> _RingSlot | None:
+        for slot in self.slots:
+            if slot.name is None:
+                return slot
+        for key, slot in list(self.inflight.items()):  # oldest staged, never taken
+            if slot.future is not None and slot.future.done():
+                self.inflight.pop(key)
+                slot.release()
+                self.stats["evicted_unused"] += 1
+                return slot
+        return None
+
+    def _prefetch(self, name: str) -> None:
+        if name in self.inflight:
+            return
+        try:
+            block = self.store._resolve(name)
+        except KeyError:
+            return
+        if block.get("kind") != "qrow":
+            return
+        slot = self._free_slot()
+        if slot is None:
+            return
+        rows, cols = (int(v) for v in block["shape"])
+        slot.name, slot.shape = name, (rows, cols)
+        slot.future = self.pool.submit(self._stage, slot, block)
+        self.inflight[name] = slot
+        self.stats["prefetches"] += 1
+        self.stats["prefetch_bytes"] += rows * cols + rows * 4
+
+    def _stage(self, slot: _RingSlot, block: Mapping[str, Any]) -> None:
+        if slot.event is not None:
+            slot.event.synchronize()  # the previous copy out of these pinned buffers is done
+        rows, cols = slot.shape
+        n = rows * cols
+        self.store._read_block(block, slot.pinned_q, slot.pinned_s)
+        with torch.cuda.stream(self.stream):
+            slot.dev_q = torch.empty(n, dtype=torch.int8, device=self.device)
+            slot.dev_q.copy_(slot.pinned_q[:n], non_blocking=True)
+            slot.dev_s = torch.empty(rows, dtype=torch.float32, device=self.device)
+            slot.dev_s.copy_(slot.pinned_s[:rows], non_blocking=True)
+            slot.event = torch.cuda.Event()
+            slot.event.record(self.stream)
+        self.stats["staged"] += 1
+
+
+# ------------------------------------------------------------------ store
+
+
+class QStore:
+    """Paged int8 store on disk, served to the B200 kernels as device pages.
+
+    Mirrors ``QStore`` (engine/kernels/qstore.py:662-1128) on its CUDA path: ``weight``
+    returns the dequantised fp32 matrix exactly as the reference computes it on the device
+    (``codes.float() * scales[:, None]``), while ``page`` / ``matmul`` keep the int8 codes and
+    run the W8A16 kernel (``mrb_qrow_matmul``) without materialising fp32 weights."""
+
+    def __init__(self, model_name: str, *, root: str | Path, device: str | torch.device = "cuda",
+                 enable_prefetch_ring: bool = True, ring_slots: int = 3, ring_depth: int = 2,
+                 read_threads: int = DEFAULT_READ_THREADS, drop_read_pages: bool = True) -> None:
+        self.directory = (Path(root) / model_name).resolve()
+        self.man = load_manifest(self.directory)
+        self.blocks = self.man["blocks"]
+        self.cfg = self.man["config"]
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("the B200 QStore serves CUDA devices only")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.read_threads = int(read_threads)
+        self.drop_read_pages = bool(drop_read_pages)
+        self.w = StoreFile(self.directory / "weights.i8")
+        self.s = StoreFile(self.directory / "scales.f32")
+        self.e = StoreFile(self.directory / "extras.f32")
+        self._ring: _PageRing | None = None
+        self._miss_q: torch.Tensor | None = None  # pinned staging of direct (unprefetched) reads
+        self._miss_s: torch.Tensor | None = None
+        self._miss_event: torch.cuda.Event | None = None
+        if enable_prefetch_ring:
+            self.enable_ring(slots=ring_slots, depth=ring_depth)
+
+    # ---- lifecycle
+
+    def _max_qrow(self) -> tuple[int, int]:
+        max_codes = max_rows = 1
+        for block in self.blocks.values():
+            if isinstance(block, Mapping) and block.get("kind") == "qrow":
+                rows, cols = (int(v) for v in block["shape"])
+                max_codes, max_rows = max(max_codes, rows * cols), max(max_rows, rows)
+        return max_codes, max_rows
+
+    def enable_ring(self, *, slots: int = 3, depth: int = 2) -> None:
+        if self._ring is None:
+            ring = _PageRing(self, slots=slots, depth=depth)
+            ring.preallocate(*self._max_qrow())
+            self._ring = ring
+
+    def disable_ring(self) -> None:
+        if self._ring is not None:
+            self._ring.close()
+            self._ring = None
+
+    def ring_stats(self) -> dict[str, int] | None:
+        return dict(self._ring.stats) if self._ring is not None else None
+
+    def ring_allocated_bytes(self) -> int:
+        """Pinned bytes the ring holds (device tensors are per prefetch)."""
+        if self._ring is None:
+            return 0
+        return sum(t.numel() * t.element_size() for s in self._ring.slots for t in (s.pinned_q, s.pinned_s)
+                   if t is not None)
+
+    def close(self) -> None:
+        self.disable_ring()
+        if self._miss_event is not None:
+            self._miss_event.synchronize()
+        for f in (self.w, self.s, self.e):
+            f.close()
+
+    def __enter__(self) -> "QStore":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    # ---- blocks
+
+    def _resolve(self, name: str) -> Mapping[str, Any]:
+        return _resolve_in(self.blocks, name)
+
+    def has(self, name: str) -> bool:
+        return name in self.blocks
+
+    def _read_block(self, block: Mapping[str, Any], pinned_q: torch.Tensor, pinned_s: torch.Tensor) -> None:
+        rows, cols = (int(v) for v in block["shape"])
+        self.w.read_into(int(block["w_off"]), rows * cols, pinned_q, threads=self.read_threads,
+                         drop_after=self.drop_read_pages)
+        self.s.read_into(int(block["s_off"]), rows * 4, pinned_s, drop_after=self.drop_read_pages)
+
+    def _direct(self, block: Mapping[str, Any]) -> tuple[torch.Tensor, torch.Tensor]:
+        """Read a block through the store's own pinned buffers and copy it on the current
+        stream (the previous direct copy must have left those buffers first)."""
+        rows, cols = (int(v) for v in block["shape"])
+        n = rows * cols
+        if self._miss_q is None or self._miss_q.numel() < n or self._miss_s.numel() < rows:
+            max_codes, max_rows = self._max_qrow()
+            if self._miss_event is not None:
+                self._miss_event.synchronize()
+            self._miss_q = torch.empty(max_codes, dtype=torch.int8, pin_memory=True)
+            self._miss_s = torch.empty(max_rows, dtype=torch.float32, pin_memory=True)
+        elif self._miss_event is not None:
+            self._miss_event.synchronize()
+        self._read_block(block, self._miss_q, self._miss_s)
+        codes = torch.empty((rows, cols), dtype=torch.int8, device=self.device)
+        scales = torch.empty(rows, dtype=torch.float32, device=self.device)
+        codes.view(-1).copy_(self._miss_q[:n], non_blocking=True)
+        scales.copy_(self._miss_s[:rows], non_blocking=True)
+        self._miss_event = torch.cuda.Event()
+        self._miss_event.record(torch.cuda.current_stream(self.device))
+        return codes, scales
+
+    def page(self, name: str) -> CompactQRowPage:
+        """The int8 codes [out, in] and fp32 row scales of a qrow block, in HBM (through the
+        ring when it predicted this block)."""
+        block = self._resolve(name)
+        if block.get("kind") != "qrow":
+            raise ValueError(f"QStore block {name!r} is not a qrow block")
+        rows, cols = (int(v) for v in block["shape"])
+        hit = None
+        if self._ring is not None:
+            hit = self._ring.take(name)
+            self._ring.observe(name)
+        codes, scales = hit if hit is not None else self._direct(block)
+        return CompactQRowPage(name=name, start_row=0, end_row=rows, in_features=cols, codes=codes, scales=scales)
+
+    @torch.inference_mode()
+    def weight(self, name: str) -> torch.Tensor:
+        """fp32 [out, in] = codes * row scale (engine/kernels/qstore.py:1026-1080, CUDA path)."""
+        page = self.page(name)
+        return page.codes.float() * page.scales[:, None]
+
+    def matmul(self, name: str, x: torch.Tensor) -> torch.Tensor:
+        """``x @ weight(name).T`` on the W8A16 kernel (the codes are never widened in HBM)."""
+        page = self.page(name)
+        return qrow_linear(page.codes, page.scales, x)
+
+    def fp32(self, name: str) -> torch.Tensor:
+        block = self._resolve(name)
+        if block.get("kind") != "fp32":
+            raise ValueError(f"QStore block {name!r} is not an fp32 block")
+        shape = tuple(int(v) for v in block["shape"])
+        host = np.empty(shape, dtype=np.float32)
+        self.e.read_into(int(block["e_off"]), host.nbytes, host)
+        return torch.from_numpy(host).to(self.device)
+
+    @torch.inference_mode()
+    def embed_rows(self, name: str, ids) -> torch.Tensor:
+        """fp32 rows ``codes[ids] * scales[ids]`` reading only the requested rows from disk
+        (engine/kernels/qstore.py:1099-1128). Out-of-range ids raise IndexError."""
+        block = self._resolve(name)
+        if block.get("kind") != "qrow":
+            raise ValueError(f"QStore block {name!r} is not a qrow block")
+        rows, cols = (int(v) for v in block["shape"])
+        flat = np.asarray(ids, dtype=np.int64).reshape(-1)
+        if flat.size and (flat.min() < 0 or flat.max() >= rows):
+            raise IndexError("embedding id out of range")
+        uniq, inverse = np.unique(flat, return_inverse=True)
+        q = np.empty((uniq.size, cols), dtype=np.int8)
+        sc = np.empty(uniq.size, dtype=np.float32)
+        w_off, s_off = int(block["w_off"]), int(block["s_off"])
+        for i, row in enumerate(uniq.tolist()):
+            self.w.read_into(w_off + row * cols, cols, q[i])
+            self.s.read_into(s_off + row * 4, 4, sc[i:i + 1])
+        codes = torch.from_numpy(q).to(self.device)
+        scales = torch.from_numpy(sc).to(self.device)
+        out = codes.float() * scales[:, None]
+        return out[torch.from_numpy(inverse).to(self.device)].reshape(*np.shape(ids), cols)

@@ -1,0 +1,129 @@
+"""On-disk QStore: the native positional reader, the layout validator against the
+reference's verdicts, and the read oracle against the reference's outputs (no GPU)."""
+from __future__ import annotations
+
+import json
+import shutil
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle.qstore_files import StoreOracle
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+STORE = GOLDEN / "qstore_small"
+
+
+def _norm(text: str) -> str:
+    # the reference names its current schema ("semantic QStore v3") and its provenance
+    # files ("derived"); the B200 reader validates the same layout without those words
+    return text.replace("semantic QStore v3", "QStore").replace("derived file", "file")
+
+
+def test_layout_validator_matches_reference_verdicts(tmp_path):
+    import sys
+
+    sys.path.insert(0, str(GOLDEN))
+    from make_qstore_fixtures import apply_case
+
+    from mrun_b200.qstore import validate_int8_layout
+
+    cases = json.loads((GOLDEN / "qstore_layout_cases.json").read_text())
+    assert len(cases) >= 10 and cases[0]["verdict"] == "ok"
+    for i, case in enumerate(cases):
+        directory = tmp_path / f"case{i}"
+        apply_case(STORE, directory, case)
+        manifest = json.loads((directory / "manifest.json").read_text())
+        if case["verdict"] == "ok":
+            validate_int8_layout(directory, manifest)
+            continue
+        with pytest.raises(RuntimeError) as err:
+            validate_int8_layout(directory, manifest)
+        assert _norm(f"RuntimeError: {err.value}") == _norm(case["verdict"]), case["name"]
+
+
+def test_oracle_pinned_to_reference_outputs(golden):
+    g = golden("qstore")
+    oracle = StoreOracle(STORE)
+    for name, block in oracle.blocks.items():
+        key = name.replace(".", "_")
+        if block.get("kind") == "fp32":
+            np.testing.assert_array_equal(oracle.fp32(name), g["fp32__" + key])
+        else:
+            np.testing.assert_array_equal(oracle.weight(name), g["weight__" + key])
+    np.testing.assert_array_equal(oracle.embed_rows("model.embed_tokens.weight", g["embed_ids"]), g["embed_rows"])
+
+
+def test_native_reader_bit_exact(tmp_path):
+    from mrun_b200.qstore import StoreFile
+
+    rng = np.random.default_rng(5)
+    data = rng.integers(0, 256, (37 << 20) + 4099, dtype=np.uint8)  # > 8 pieces of 4 MiB, ragged end
+    path = tmp_path / "blob.bin"
+    data.tofile(path)
+    f = StoreFile(path)
+    assert f.size == data.size
+    for offset, nbytes, threads in [(0, data.size, 1), (0, data.size, 8), (12345, 20 << 20, 3), (data.size - 7, 7, 4),
+                                    (1, 1, 16), (8 << 20, 0, 2), (3, (9 << 20) + 1, 64)]:
+        dst = np.zeros(max(nbytes, 1), dtype=np.uint8)
+        f.read_into(offset, nbytes, dst, threads=threads, drop_after=(threads % 2 == 0))
+        np.testing.assert_array_equal(dst[:nbytes], data[offset:offset + nbytes])
+    with pytest.raises(ValueError, match="beyond"):
+        f.read_into(data.size - 3, 4, np.zeros(4, np.uint8))
+    with pytest.raises(ValueError, match="destination holds"):
+        f.read_into(0, 8, np.zeros(4, np.uint8))
+    f.advise(0, 1 << 20, will_need=True)
+    f.advise(0, 1 << 20, will_need=False)
+    f.close()
+    f.close()  # idempotent
+    with pytest.raises(ValueError, match="closed"):
+        f.read_into(0, 1, np.zeros(1, np.uint8))
+    with pytest.raises(OSError, match="No such file"):
+        StoreFile(tmp_path / "missing.bin")
+    with pytest.raises(ValueError, match="regular file"):
+        StoreFile(tmp_path)
+
+
+def test_native_reader_concurrent_callers(tmp_path):
+    """Several threads read one handle at once (pread keeps no shared offset)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from mrun_b200.qstore import StoreFile
+
+    data = np.random.default_rng(6).integers(0, 256, 24 << 20, dtype=np.uint8)
+    path = tmp_path / "blob.bin"
+    data.tofile(path)
+    f = StoreFile(path)
+    spans = [(i * (3 << 20) + 11, (2 << 20) + 5) for i in range(7)]
+
+    def read(span):
+        out = np.empty(span[1], np.uint8)
+        f.read_into(span[0], span[1], out, threads=4)
+        return out
+
+    with ThreadPoolExecutor(4) as pool:
+        for (off, n), got in zip(spans, pool.map(read, spans)):
+            np.testing.assert_array_equal(got, data[off:off + n])
+    f.close()
+
+
+def test_writer_round_trip(tmp_path):
+    """write_qstore lays blocks back to back; the validator accepts it and the oracle reads
+    back exactly the arrays written."""
+    from mrun_b200.qstore import load_manifest
+    from mrun_b200.qstore_build import write_qstore
+
+    rng = np.random.default_rng(9)
+    codes = rng.integers(-127, 128, (33, 48), dtype=np.int8)
+    scales = rng.random(33).astype(np.float32)
+    norm = rng.random(48).astype(np.float32)
+    write_qstore(tmp_path / "m", qrows={"a": (codes, scales), "b": (codes[:5], scales[:5])}, fp32={"n": norm},
+                 aliases={"c": "a"}, config={"hidden_size": 48})
+    man = load_manifest(tmp_path / "m")
+    assert man["blocks"]["b"]["w_off"] == codes.nbytes
+    oracle = StoreOracle(tmp_path / "m")
+    np.testing.assert_array_equal(oracle.qrow("c")[0], codes)
+    np.testing.assert_array_equal(oracle.qrow("b")[1], scales[:5])
+    np.testing.assert_array_equal(oracle.fp32("n"), norm)
+    shutil.rmtree(tmp_path / "m")
