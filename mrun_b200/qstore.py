@@ -23,6 +23,7 @@ from __future__ import annotations
 import ctypes
 import json
 import math
+import os
 import threading
 from collections import OrderedDict
 from collections.abc import Mapping
@@ -37,7 +38,9 @@ from . import _lib
 from .dense_qstore_cuda import CompactQRowPage, qrow_linear
 
 QSTORE_FILES = ("weights.i8", "scales.f32", "extras.f32")
-DEFAULT_READ_THREADS = 8
+# parallel pread calls per block read: one per host core up to 32 (measured on a 16-core B200
+# host, page cache to pinned memory: 8.0 GB/s with 1 thread, 36.6 with 8, 45.7 with 16)
+DEFAULT_READ_THREADS = max(4, min(32, os.cpu_count() or 8))
 
 
 # ------------------------------------------------------------------ native file reader
