@@ -2,22 +2,24 @@
 fixed pool of HBM slots on a side stream, overlapped with compute.
 
 Mirrors mrun's ``HostPageTier`` / ``ExpertPageCache`` (engine/qwen3_moe_cuda.py:878-1817):
-a pinned host tier holds every expert page; an HBM slot cache (capacity from a byte budget,
-LRU) serves the experts a layer routes to; misses and predicted next-layer pages are
-copied by ``mrb_copy_pages`` (one cudaMemcpyAsync per page) on a copy stream, and the
-compute stream waits on per-slot ready events. A slot is only overwritten after the compute
-stream has passed its last use (per-slot release events), so streaming never changes a
-result: pages in HBM are byte-identical to the host tier.
+a pinned host tier holds every expert page; an HBM slot cache (capacity from a byte budget)
+serves the experts a layer routes to. Which pages stay and which slot each occupies is
+planned by ``page_policy.ExpertResidency`` (the reference's global-LRU and layer-frequency
+policies, transient-frequency prefill, route-history prefetch); this module executes the
+plans: host pages are copied by ``mrb_copy_pages`` (one cudaMemcpyAsync per page) on a copy
+stream and the compute stream waits on per-slot ready events. A slot is only overwritten
+after the compute stream has passed its last use (per-slot release events), so streaming
+never changes a result: pages in HBM are byte-identical to the host tier.
 """
 from __future__ import annotations
 
-from collections import OrderedDict
 from dataclasses import dataclass
 
 import torch
 
 from . import _lib
 from .moe import ExpertPageLayout
+from .page_policy import (CACHE_FILL_PREFILL, GLOBAL_LRU, TRANSIENT_FREQUENCY_PREFILL, ExpertResidency, PageTrace)
 
 
 @dataclass
@@ -51,103 +53,99 @@ class HostPageTier:
 
 
 class ExpertPageCache:
-    """HBM slot cache over a HostPageTier (LRU; prefetch on a side stream)."""
+    """HBM slot cache over a HostPageTier, copies on a side stream.
 
-    def __init__(self, host: HostPageTier, *, budget_bytes: int, device: torch.device) -> None:
+    cache_policy / prefill_page_policy / route_prefetch select the residency rules (see
+    ``page_policy``); page_trace records every acquisition's routed pages for offline replay
+    (``page_policy.replay``)."""
+
+    def __init__(self, host: HostPageTier, *, budget_bytes: int, device: torch.device,
+                 cache_policy: str = GLOBAL_LRU, prefill_page_policy: str = CACHE_FILL_PREFILL,
+                 route_prefetch: bool = False, page_trace: bool = False, max_active_pages: int | None = None) -> None:
         self.host = host
         self.layout = host.layout
         self.device = device
         stride = self.layout.page_stride
         self.capacity = max(1, int(budget_bytes // stride))
+        self.max_active_pages = int(max_active_pages or min(host.experts, self.capacity))
+        self.residency = ExpertResidency(layers=host.layers, experts=host.experts, capacity=self.capacity,
+                                         page_bytes=stride, max_active_pages=self.max_active_pages,
+                                         cache_policy=cache_policy, prefill_page_policy=prefill_page_policy,
+                                         route_prefetch=route_prefetch)
         self.slots = torch.empty((self.capacity, stride), dtype=torch.uint8, device=device)
-        self.where: OrderedDict[tuple[int, int], int] = OrderedDict()  # LRU order: oldest first
-        self.owner: list[tuple[int, int] | None] = [None] * self.capacity
         self.ready = [torch.cuda.Event() for _ in range(self.capacity)]
         self.released = [torch.cuda.Event() for _ in range(self.capacity)]
+        # transient prefill slab (pages a prefill layer runs from without keeping them)
+        self.slab = (torch.empty((self.max_active_pages, stride), dtype=torch.uint8, device=device)
+                     if prefill_page_policy == TRANSIENT_FREQUENCY_PREFILL else None)
+        self.slab_released = torch.cuda.Event()
+        self._slab_in_use = False
         self.prefetched: set[tuple[int, int]] = set()
         self.copy_stream = torch.cuda.Stream(device)
         self.stats = PageCacheStats()
+        self.trace = PageTrace(host.layers, stride) if page_trace else None
+        self.step = 0
         self.slot_of = torch.full((host.experts,), -1, dtype=torch.int32, device=device)
         # pinned staging for the slot map, rotated so an in-flight copy is never overwritten
         self._maps = [torch.full((host.experts,), -1, dtype=torch.int32, pin_memory=True) for _ in range(4)]
         self._map_events: list[torch.cuda.Event | None] = [None] * 4
         self._map_next = 0
+        self._pending_release: list[int] = []
 
     @property
     def device_bytes(self) -> int:
-        return self.slots.numel()
+        return self.slots.numel() + (self.slab.numel() if self.slab is not None else 0)
+
+    @property
+    def where(self):
+        """Resident pages: (layer, expert) -> slot, least recently used first."""
+        return self.residency.entries
 
     def reset(self, *, clear_pages: bool) -> None:
         self.stats = PageCacheStats()
+        self.residency.reset(clear_pages=clear_pages)
         if clear_pages:
-            self.where.clear()
-            self.owner = [None] * self.capacity
             self.prefetched.clear()
 
-    # ------------------------------------------------------------------ slot management
+    # ------------------------------------------------------------------ copies
 
-    def _victim(self, protect: set[tuple[int, int]]) -> int:
-        for slot, owner in enumerate(self.owner):
-            if owner is None:
-                return slot
-        for key in self.where:  # oldest first
-            if key not in protect:
-                slot = self.where.pop(key)
-                self.owner[slot] = None
-                self.prefetched.discard(key)
-                self.stats.evictions += 1
-                return slot
-        raise MemoryError("expert page cache has no evictable slot (capacity below one layer's working set)")
-
-    def _copy(self, keys: list[tuple[int, int]], protect: set[tuple[int, int]]) -> None:
-        """Assign slots to `keys` and copy their pages on the copy stream."""
-        if not keys:
+    def _copy_host(self, layer: int, copies: list[tuple[int, int]], dst: torch.Tensor, *, slot_events: bool) -> None:
+        """Copy host pages (expert, index) of `layer` into dst[index] on the copy stream."""
+        if not copies:
             return
-        slots, pages = [], []
-        for key in keys:
-            slot = self._victim(protect | set(keys))
-            self.owner[slot] = key
-            self.where[key] = slot
-            # the compute stream must be done with the slot's previous page
-            self.copy_stream.wait_event(self.released[slot])
-            slots.append(slot)
-            pages.append(self.host.page_index(*key))
         stride = self.layout.page_stride
-        s_arr = (torch.tensor(slots, dtype=torch.int32)).contiguous()
-        p_arr = (torch.tensor(pages, dtype=torch.int32)).contiguous()
+        if slot_events:  # the compute stream must be done with each slot's previous page
+            for _, slot in copies:
+                self.copy_stream.wait_event(self.released[slot])
+        idx = torch.tensor([i for _, i in copies], dtype=torch.int32)
+        pages = torch.tensor([self.host.page_index(layer, e) for e, _ in copies], dtype=torch.int32)
         done = torch.cuda.Event()
         with torch.cuda.stream(self.copy_stream):
-            _lib.call("mrb_copy_pages", self.slots.data_ptr(), stride, self.host.pages.data_ptr(), stride,
-                      s_arr.data_ptr(), p_arr.data_ptr(), len(slots), stride, self.copy_stream.cuda_stream, None)
+            _lib.call("mrb_copy_pages", dst.data_ptr(), stride, self.host.pages.data_ptr(), stride, idx.data_ptr(),
+                      pages.data_ptr(), len(copies), stride, self.copy_stream.cuda_stream, None)
             done.record(self.copy_stream)
-        for slot in slots:
-            self.ready[slot] = done
-        self.stats.bytes_h2d += len(slots) * stride
+        if slot_events:
+            for _, slot in copies:
+                self.ready[slot] = done
+        self.stats.bytes_h2d += len(copies) * stride
+
+    def _evictions_since(self, before: int) -> None:
+        self.stats.evictions += self.residency.stats["evictions"] - before
 
     def prefetch(self, layer: int, experts: list[int], *, protect_layer: int | None = None) -> None:
-        """Start copying `layer`'s predicted experts (no wait)."""
+        """Start copying `layer`'s predicted experts (no wait); the resident pages of
+        `protect_layer` are not evicted for them."""
         protect = {k for k in self.where if k[0] == protect_layer} if protect_layer is not None else set()
-        missing = [(layer, e) for e in experts if (layer, e) not in self.where]
-        self._copy(missing, protect)
-        self.prefetched.update(missing)
-        self.stats.prefetched += len(missing)
+        before = self.residency.stats["evictions"]
+        copies = self.residency.reserve(layer, experts, protect)
+        self._evictions_since(before)
+        self._copy_host(layer, copies, self.slots, slot_events=True)
+        self.prefetched.update((layer, e) for e, _ in copies)
+        self.stats.prefetched += len(copies)
 
-    def layer_pages(self, layer: int, top_indices: torch.Tensor, *, prefill: bool = False):
-        """(slot buffer, slot_of [E] int32) for the experts `top_indices` route to; the
-        current stream is ordered after their copies."""
-        del prefill
-        needed = sorted(int(e) for e in torch.unique(top_indices).tolist())  # host sync, as the reference
-        keys = [(layer, e) for e in needed]
-        missing = [k for k in keys if k not in self.where]
-        for k in keys:
-            if k in self.where:
-                self.where.move_to_end(k)
-                self.stats.hits += 1
-                if k in self.prefetched:
-                    self.stats.prefetch_hits += 1
-                    self.prefetched.discard(k)
-        self.stats.misses += len(missing)
-        self._copy(missing, set(keys))
+    # ------------------------------------------------------------------ acquisitions
+
+    def _publish_map(self, entries: dict[int, int], waits: list[torch.cuda.Event]) -> torch.Tensor:
         compute = torch.cuda.current_stream(self.device)
         i = self._map_next
         self._map_next = (i + 1) % len(self._maps)
@@ -155,34 +153,106 @@ class ExpertPageCache:
             self._map_events[i].synchronize()
         mapping = self._maps[i]
         mapping.fill_(-1)
-        waited = set()
-        for k in keys:
-            slot = self.where[k]
-            mapping[k[1]] = slot
-            ev = self.ready[slot]
-            if id(ev) not in waited:
+        for expert, where in entries.items():
+            mapping[expert] = where
+        seen = set()
+        for ev in waits:
+            if id(ev) not in seen:
                 compute.wait_event(ev)
-                waited.add(id(ev))
+                seen.add(id(ev))
         self.slot_of.copy_(mapping, non_blocking=True)
         ev = torch.cuda.Event()
         ev.record(compute)
         self._map_events[i] = ev
-        self._pending_release = [self.where[k] for k in keys]
-        return self.slots, self.slot_of
+        return self.slot_of
+
+    def layer_pages(self, layer: int, top_indices: torch.Tensor, *, prefill: bool = False):
+        """(page buffer, slot_of [E] int32) for the experts `top_indices` route to; the
+        current stream is ordered after their copies. Decode acquisitions (prefill False) mark
+        their pages decode-protected, as the reference's decode path does."""
+        routed = [int(e) for e in top_indices.reshape(-1).tolist()]  # host sync, as the reference
+        if self.trace is not None:
+            self.trace.record(phase="prefill" if prefill else "decode", step=self.step, layer=layer, routed=routed)
+        res = self.residency
+        before = res.stats["evictions"]
+        if prefill and res.prefill_page_policy == TRANSIENT_FREQUENCY_PREFILL:
+            return self._transient(layer, routed, before)
+        plan = res.acquire(layer, routed, protect=not prefill)
+        self._evictions_since(before)
+        missed = {e for e, _ in plan.copies}
+        for e in plan.experts:
+            if e not in missed:
+                self.stats.hits += 1
+                if (layer, e) in self.prefetched:
+                    self.stats.prefetch_hits += 1
+                    self.prefetched.discard((layer, e))
+        self.stats.misses += len(plan.copies)
+        self._copy_host(layer, plan.copies, self.slots, slot_events=True)
+        if res.route_prefetch:
+            before = res.stats["evictions"]
+            ahead = res.prefetch_next_layer(layer, {(layer, e) for e in plan.experts})
+            self._evictions_since(before)
+            self._copy_host(layer + 1, ahead, self.slots, slot_events=True)
+            self.prefetched.update((layer + 1, e) for e, _ in ahead)
+            self.stats.prefetched += len(ahead)
+        self._pending_release = list(plan.slots)
+        slot_of = self._publish_map(dict(zip(plan.experts, plan.slots)), [self.ready[s] for s in plan.slots])
+        if layer == res.layers - 1 and not prefill:
+            self.step += 1
+        return self.slots, slot_of
+
+    def _transient(self, layer: int, routed: list[int], evictions_before: int):
+        res = self.residency
+        if self._slab_in_use:
+            raise RuntimeError("release_layer() must follow each transient prefill layer")
+        plan = res.acquire_transient_prefill(layer, routed)
+        self._evictions_since(evictions_before)
+        stride = self.layout.page_stride
+        self.stats.hits += len(plan.resident_slots)
+        self.stats.misses += plan.host_count
+        # the slab is reused only after the previous transient layer's kernels
+        self.copy_stream.wait_event(self.slab_released)
+        self._copy_host(layer, [(e, i) for i, e in enumerate(plan.slab_experts[:plan.host_count])], self.slab,
+                        slot_events=False)
+        with torch.cuda.stream(self.copy_stream):
+            if plan.resident_slots:  # resident pages as they are now, before any slot is reused
+                for s in plan.resident_slots:
+                    self.copy_stream.wait_event(self.ready[s])
+                src = torch.tensor(plan.resident_slots, dtype=torch.long, device=self.device)
+                torch.index_select(self.slots, 0, src, out=self.slab[plan.host_count:len(plan.slab_experts)])
+            if plan.admissions:  # the hottest new pages stay: slab -> their cache slots
+                for _, s in plan.admissions:
+                    self.copy_stream.wait_event(self.released[s])
+                dst = torch.tensor([s for _, s in plan.admissions], dtype=torch.long, device=self.device)
+                pos = torch.tensor([p for p, _ in plan.admissions], dtype=torch.long, device=self.device)
+                self.slots.index_copy_(0, dst, self.slab.index_select(0, pos))
+            done = torch.cuda.Event()
+            done.record(self.copy_stream)
+        for _, s in plan.admissions:
+            self.ready[s] = done
+        self._slab_in_use = True
+        self._pending_release = []
+        return self.slab, self._publish_map(dict(zip(plan.experts, plan.group_slots)), [done])
 
     def release_layer(self) -> None:
-        """Mark the slots used by the last layer_pages() as free once the compute stream
+        """Mark the pages used by the last layer_pages() as free once the compute stream
         reaches this point (call after enqueuing the layer's kernels)."""
         compute = torch.cuda.current_stream(self.device)
-        for slot in getattr(self, "_pending_release", []):
+        for slot in self._pending_release:
             ev = torch.cuda.Event()
             ev.record(compute)
             self.released[slot] = ev
         self._pending_release = []
+        if self._slab_in_use:
+            self.slab_released = torch.cuda.Event()
+            self.slab_released.record(compute)
+            self._slab_in_use = False
 
     def report(self) -> dict:
         return {"kind": "streamed", "capacity_pages": self.capacity, "device_bytes": self.device_bytes,
-                "host_bytes": self.host.nbytes, **self.stats.as_dict()}
+                "host_bytes": self.host.nbytes, "cache_policy": self.residency.cache_policy,
+                "prefill_page_policy": self.residency.prefill_page_policy, **self.stats.as_dict(),
+                "residency": self.residency.stats.as_dict(), "prefetch": dict(self.residency.prefetch_stats)}
 
 
 __all__ = ["ExpertPageCache", "HostPageTier", "PageCacheStats"]

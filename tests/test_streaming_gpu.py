@@ -67,3 +67,44 @@ def test_copy_pages_validates(cuda):
 
     with pytest.raises(ValueError):
         _lib.call("mrb_copy_pages", None, 16, None, 16, None, None, 1, 16, None, None)
+
+
+@pytest.mark.parametrize("policy,prefill_policy,route_prefetch", [
+    ("global-lru-v1", "cache-fill-v1", False),
+    ("layer-frequency-lru-v1", "cache-fill-v1", True),
+    ("layer-frequency-lru-v1", "transient-frequency-v1", False),
+])
+def test_policies_bit_identical_and_trace_replays(policy, prefill_policy, route_prefetch, cuda):
+    """Every residency policy (prefill from the transient slab included) gives the resident
+    outputs bit for bit, slots hold the host pages, and replaying the recorded page trace
+    reproduces the live cache's counters (without route prefetch, which replay leaves out)."""
+    from mrun_b200.moe import PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_topk
+    from mrun_b200.page_policy import replay
+    from mrun_b200.streaming import ExpertPageCache
+
+    ly, host, resident = _build(cuda)
+    cache = ExpertPageCache(host, budget_bytes=12 * ly.page_stride, device=cuda, cache_policy=policy,
+                            prefill_page_policy=prefill_policy, route_prefetch=route_prefetch, page_trace=True)
+    streamed = PagedInt8ExpertBackend(cache, num_experts=E)
+    reference = PagedInt8ExpertBackend(ResidentInt8ExpertPages(ly, resident), num_experts=E)
+    rng = np.random.default_rng(11)
+    for step in range(4):
+        rows = T if step == 0 else 3  # a prefill pass, then decode steps
+        x = torch.from_numpy(rng.standard_normal((rows, H)).astype(np.float32)).to(cuda).to(torch.bfloat16)
+        hs, hr = x, x
+        for layer in range(L):
+            idx, w, _ = router_topk(torch.from_numpy(rng.standard_normal((rows, E)).astype(np.float32)).to(cuda), K)
+            hs = streamed.moe(layer, hs, idx, w, prefill=step == 0)
+            hr = reference.moe(layer, hr, idx, w, prefill=step == 0)
+        torch.cuda.synchronize()
+        assert torch.equal(hs, hr), f"step {step}"
+    for (layer, e), slot in cache.where.items():
+        assert torch.equal(cache.slots[slot].cpu(), host.pages[layer, e])
+    report = cache.report()
+    assert report["residency"]["page_requests"] > 0 and report["cache_policy"] == policy
+    if not route_prefetch:
+        got = replay(cache.trace, capacity_pages=cache.capacity, cache_policy=policy,
+                     prefill_page_policy=prefill_policy, max_active_pages=cache.max_active_pages)
+        live = cache.residency.stats
+        for name in ("page_hits", "page_misses", "evictions", "transient_prefill_admitted_pages"):
+            assert got[name] == live[name], name
