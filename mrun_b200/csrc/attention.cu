@@ -29,7 +29,7 @@ constexpr int AT_STAGES = 4;       // K/V tiles per CTA in shared memory (cp.asy
 #define AT_MIN_TILES 4  // split-K: fewest 16-token tiles per split
 #endif
 #ifndef AT_MMA_CTAS_PER_SM
-#define AT_MMA_CTAS_PER_SM 2  // split-K target of the tensor-core kernel
+#define AT_MMA_CTAS_PER_SM 3  // split-K target of the tensor-core kernel (its resident CTAs per SM)
 #endif
 
 // ------------------------------------------------------------------ RoPE + KV append
@@ -638,7 +638,13 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) rope_append_attention_kerne
 
 // ------------------------------------------------------------------ tensor-core decode attention
 
-constexpr int AM_STAGES = 3;                          // K/V tiles in flight per warp
+// Two stages per warp keep a CTA at 70 KB of shared memory, so 3 CTAs (12 warps) share an
+// SM: 64 rows x 28/4 heads, ctx U[128,2048] went 63.5 -> 48.2 us against 3 stages at 2 CTAs
+// per SM (32 rows x 32/4 heads, ctx U[256,4096]: 50.4 -> 48.3 us).
+#ifndef AM_RING_STAGES
+#define AM_RING_STAGES 2
+#endif
+constexpr int AM_STAGES = AM_RING_STAGES;             // K/V tiles in flight per warp
 constexpr int AM_ROW = 128 + 8;                       // padded smem row (bf16): conflict-free fragments
 constexpr int AM_TILE_ELEMS = AT_TILE * AM_ROW;       // one K or V tile
 constexpr int AM_STAGE_ELEMS = 2 * AM_TILE_ELEMS;     // K and V
@@ -1326,8 +1332,9 @@ static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total, int64
   const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
   const int64_t groups = std::max<int64_t>(1, rows * hkv);
   const bool mma = use_mma(rows, hkv, max_total, head_dim);
-  // the tensor-core kernel holds 2 CTAs per SM: aim at one resident wave, so each warp has
-  // enough tiles to amortise its prologue and merge (measured best of 2, 3, 4, 6 per SM)
+  // the tensor-core kernel holds 3 CTAs per SM (2-stage rings): aim at one resident wave, so
+  // each warp has enough tiles to amortise its prologue and merge (3 measured best of 2-4 at
+  // the config-3 and config-4 shapes together)
   const int64_t per_sm = mma ? AT_MMA_CTAS_PER_SM : AT_CTAS_PER_SM;
   const int64_t target = (per_sm * num_sms() + groups - 1) / groups;  // splits per group
   const int64_t min_tiles = mma ? 2 * AM_MAX_WARPS : (tiles <= 64 ? 2 : AT_MIN_TILES);
