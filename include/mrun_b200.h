@@ -319,6 +319,20 @@ int mrb_rope_kv_append(const void *q_in, const void *k_in, const void *v_in, int
                        int64_t num_pages, int32_t *error_flag, const void *q_norm,
                        const void *k_norm, float norm_eps, void *stream);
 
+/* Causal prefill attention for n tokens of one sequence at positions start .. start + n - 1,
+ * already appended to the paged cache (mrb_rope_kv_append): token i attends to positions
+ * [0, start + i] of the sequence whose page-table row is block_table. q/out: bf16
+ * [n, hq, 128]. Flash attention on the tensor pipe: one CTA per (16-token query block, KV
+ * head), the K/V prefix read once per block instead of once per token. An unmapped page sets
+ * *error_flag (may be NULL) and reads as zeros. head_dim 128, hq / hkv <= 16, page_size a
+ * multiple of 16. Replaces the prefill attention of the dense engine
+ * (`_stable_attention_kernel` / SDPA, engine/kernels/dense_qstore_cuda.py:747-829). */
+int mrb_paged_prefill_attention(const void *q, int64_t n, int64_t hq, int64_t hkv, int64_t head_dim,
+                                int64_t start, const void *k_cache, const void *v_cache,
+                                int64_t stride_page, int64_t stride_head, int64_t stride_tok,
+                                int64_t page_size, const int32_t *block_table, int64_t num_pages,
+                                int32_t *error_flag, float scale, void *out, void *stream);
+
 /* One decode token per query row in one launch: mrb_rope_kv_append's RoPE (and optional
  * q/k norm) of the row's query heads and key, its K/V append at position positions[r] of
  * block-table row row_seq[r] (NULL: r), and mrb_paged_attention over tokens

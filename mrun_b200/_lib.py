@@ -58,6 +58,8 @@ SIGNATURES: dict[str, list] = {
                                   _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, c_float, _I64, c_int, _P,
                                   _P],
     "mrb_rope_append_attention_cluster": [_I64, _I64, _I64, _I64, _I64],
+    "mrb_paged_prefill_attention": [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P,
+                                    c_float, _P, _P],
     "mrb_store_file_open": [ctypes.c_char_p, ctypes.POINTER(c_void_p), ctypes.POINTER(ctypes.c_uint64)],
     "mrb_store_file_close": [_P],
     "mrb_store_file_read": [_P, ctypes.c_uint64, ctypes.c_uint64, _P, c_int, c_int],

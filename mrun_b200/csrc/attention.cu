@@ -1284,6 +1284,185 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) rope_append_attention_mma_k
   cluster_sync_all();  // peers' shared memory stays alive until every merge has read it
 }
 
+// ------------------------------------------------------------------ prefill attention
+
+// Causal attention of a prefill block: n tokens of one sequence at positions start ..
+// start + n - 1, already appended to the paged cache, each attending to positions [0, its own].
+// Flash-attention on the tensor pipe for head_dim 128: a CTA owns (16-token query block, KV
+// head) with one warp per query head of the GQA group; all warps share each 16-token K/V tile,
+// staged through a cp.async ring in shared memory (rows padded to 272 B for conflict-free
+// fragments), and every warp computes S = Q K^T for its head with the block's 16 tokens as
+// the rows of mma.sync m16n8k16 (bf16 in, fp32 out), masks keys past each token's position,
+// runs the fp32 online softmax per token row and accumulates O += P V (P rounded to bf16 as
+// the A operand, V through ldmatrix.trans). The K/V prefix is read once per (query block,
+// KV head) instead of once per token. Deterministic (no atomics, fixed order).
+constexpr int PF_STAGES = 3;
+constexpr int PF_ROW = 128 + 8;                    // padded smem row (bf16)
+constexpr int PF_TILE_ELEMS = AT_TILE * PF_ROW;    // one K or V tile
+constexpr int PF_STAGE_ELEMS = 2 * PF_TILE_ELEMS;  // K and V
+constexpr size_t PF_SMEM = (size_t)PF_STAGES * PF_STAGE_ELEMS * sizeof(__nv_bfloat16);
+
+struct PrefillArgs {
+  const __nv_bfloat16* q;  // [n, hq, 128]
+  int64_t n, hq, hkv, start;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  int64_t stride_page, stride_head, stride_tok, page_size;
+  const int32_t* block_table;  // the sequence's row
+  int64_t num_pages;
+  int32_t* error_flag;
+  float scale;
+  __nv_bfloat16* out;  // [n, hq, 128]
+};
+
+__global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_prefill_attention_kernel(PrefillArgs a) {
+  constexpr int D = 128, CH = D / 8;
+  const int group = blockDim.x >> 5;
+  const int64_t q0 = (int64_t)blockIdx.x * AT_TILE;  // first token of the block
+  const int kvh = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int head = kvh * group + warp;
+  extern __shared__ __align__(16) unsigned char pf_smem[];
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(pf_smem);
+  pdl_launch_dependents();
+  pdl_wait();
+
+  const int64_t ntok = min((int64_t)AT_TILE, a.n - q0);         // tokens of this block
+  const int64_t last_pos = a.start + q0 + ntok - 1;              // the block's highest position
+  const int ntile = (int)(last_pos / AT_TILE) + 1;               // key tiles [0, last_pos]
+  const int64_t khead = (int64_t)kvh * a.stride_head;
+  bool bad_page = false;
+
+  auto issue = [&](int i) {
+    if (i < ntile) {
+      __nv_bfloat16* kst = ring + (i % PF_STAGES) * PF_STAGE_ELEMS;
+      __nv_bfloat16* vst = kst + PF_TILE_ELEMS;
+      const int64_t t0 = (int64_t)i * AT_TILE;
+      const int64_t lp = t0 / a.page_size;
+      const int64_t page = a.block_table[lp];
+      const bool page_ok = page >= 0 && page < a.num_pages;
+      bad_page |= !page_ok;
+      const int64_t base = page_ok ? page * a.stride_page + khead + (t0 - lp * a.page_size) * a.stride_tok : 0;
+      const int lim = (int)min((int64_t)AT_TILE, last_pos + 1 - t0);
+      for (int e = tid; e < AT_TILE * CH; e += blockDim.x) {
+        const int t = e / CH, ch = e - t * CH;
+        const bool ld = page_ok && t < lim;
+        const int64_t off = ld ? base + (int64_t)t * a.stride_tok + ch * 8 : 0;
+        cp_async16_zfill(kst + t * PF_ROW + ch * 8, a.k_cache + off, ld);
+        cp_async16_zfill(vst + t * PF_ROW + ch * 8, a.v_cache + off, ld);
+      }
+    }
+    cp_async_commit_group();
+  };
+#pragma unroll
+  for (int i = 0; i < PF_STAGES - 1; ++i) issue(i);
+
+  // Q of this warp's head for the block's tokens (rows g and g + 8; zero past the block)
+  uint32_t qa[D / 16][4];
+  {
+    const bool v0 = g < ntok, v1 = g + 8 < ntok;
+    const __nv_bfloat16* r0 = a.q + ((q0 + g) * a.hq + head) * D;
+    const __nv_bfloat16* r1 = a.q + ((q0 + g + 8) * a.hq + head) * D;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int d0 = ks * 16 + 2 * c;
+      qa[ks][0] = v0 ? *reinterpret_cast<const uint32_t*>(r0 + d0) : 0u;
+      qa[ks][1] = v1 ? *reinterpret_cast<const uint32_t*>(r1 + d0) : 0u;
+      qa[ks][2] = v0 ? *reinterpret_cast<const uint32_t*>(r0 + d0 + 8) : 0u;
+      qa[ks][3] = v1 ? *reinterpret_cast<const uint32_t*>(r1 + d0 + 8) : 0u;
+    }
+  }
+  const int64_t pos_row[2] = {a.start + q0 + g, a.start + q0 + g + 8};  // key limit per row
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  for (int i = 0; i < ntile; ++i) {
+    cp_async_wait_group<PF_STAGES - 2>();
+    __syncthreads();  // tile i is staged; every warp is done with tile i - 1
+    issue(i + PF_STAGES - 1);
+    const __nv_bfloat16* kst = ring + (i % PF_STAGES) * PF_STAGE_ELEMS;
+    const __nv_bfloat16* vst = kst + PF_TILE_ELEMS;
+    const int64_t t0 = (int64_t)i * AT_TILE;
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      const __nv_bfloat16* kr = kst + (nt * 8 + (lane & 7)) * PF_ROW + (lane >> 3) * 8;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ks += 2) {
+        uint32_t kb[4];
+        ldmatrix_x4(kb, kr + ks * 16);
+        mma_bf16_16816(s[nt], qa[ks], kb[0], kb[1]);
+        mma_bf16_16816(s[nt], qa[ks + 1], kb[2], kb[3]);
+      }
+    }
+    // causal mask: key position <= the row's token position
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int64_t key = t0 + nt * 8 + 2 * c + (e & 1);
+        s[nt][e] = key <= pos_row[e >> 1] ? s[nt][e] * a.scale : -INFINITY;
+      }
+    float alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float mx = fmaxf(fmaxf(s[0][2 * h], s[0][2 * h + 1]), fmaxf(s[1][2 * h], s[1][2 * h + 1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(mrow[h], mx);
+      alpha[h] = (mrow[h] == -INFINITY) ? 0.f : expf(mrow[h] - m_new);
+      float sum = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float p = (m_new == -INFINITY) ? 0.f : expf(s[nt][2 * h + e] - m_new);
+          s[nt][2 * h + e] = p;
+          sum += p;
+        }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      lrow[h] = lrow[h] * alpha[h] + sum;
+      mrow[h] = m_new;
+    }
+    const uint32_t pa[4] = {pack_bf16x2(s[0][0], s[0][1]), pack_bf16x2(s[0][2], s[0][3]),
+                            pack_bf16x2(s[1][0], s[1][1]), pack_bf16x2(s[1][2], s[1][3])};
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt) {
+      o[dt][0] *= alpha[0];
+      o[dt][1] *= alpha[0];
+      o[dt][2] *= alpha[1];
+      o[dt][3] *= alpha[1];
+    }
+    const __nv_bfloat16* vrow = vst + (lane & 15) * PF_ROW + (lane >> 4) * 8;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; dt += 2) {
+      uint32_t vb[4];
+      ldmatrix_x4_trans(vb, vrow + dt * 8);
+      mma_bf16_16816(o[dt], pa, vb[0], vb[1]);
+      mma_bf16_16816(o[dt + 1], pa, vb[2], vb[3]);
+    }
+  }
+  cp_async_wait_group<0>();
+  if (bad_page && a.error_flag) atomicExch(a.error_flag, 1);
+  // O / l for rows g and g + 8 of the block
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int64_t tok = q0 + g + 8 * h;
+    if (tok >= a.n) continue;
+    const float inv = lrow[h] > 0.f ? 1.f / lrow[h] : 0.f;
+    __nv_bfloat16* dst = a.out + (tok * a.hq + head) * D + 2 * c;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt)
+      *reinterpret_cast<__nv_bfloat162*>(dst + dt * 8) =
+          __floats2bfloat162_rn(o[dt][2 * h] * inv, o[dt][2 * h + 1] * inv);
+  }
+}
+
 static bool use_mma(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_dim);
 
 // Launch the decode attention for a checked AttnArgs planned with plan_splits: the
@@ -1435,6 +1614,45 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
     a.part = (float*)((char*)workspace + AT_COUNTER_BYTES);
   }
   return launch_attention(a, head_dim, max_total_tokens, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------------------ prefill attention (host)
+
+extern "C" int mrb_paged_prefill_attention(const void* q, int64_t n, int64_t hq, int64_t hkv, int64_t head_dim,
+                                           int64_t start, const void* k_cache, const void* v_cache,
+                                           int64_t stride_page, int64_t stride_head, int64_t stride_tok,
+                                           int64_t page_size, const int32_t* block_table, int64_t num_pages,
+                                           int32_t* error_flag, float scale, void* out, void* stream) {
+  if (n < 0 || hq <= 0 || hkv <= 0 || hq % hkv || start < 0 || page_size <= 0 || num_pages <= 0)
+    return fail(MRB_ERR_ARG, "paged_prefill_attention: bad shape");
+  if (hq / hkv > AT_MAX_GROUP)
+    return fail(MRB_ERR_UNSUPPORTED, "paged_prefill_attention: query group %lld exceeds %d",
+                (long long)(hq / hkv), AT_MAX_GROUP);
+  if (head_dim != 128 || page_size % AT_TILE)
+    return fail(MRB_ERR_UNSUPPORTED, "paged_prefill_attention: head_dim 128 and pages of a multiple of 16 tokens "
+                "(got %lld, %lld)", (long long)head_dim, (long long)page_size);
+  if (n == 0) return MRB_OK;
+  if (!q || !k_cache || !v_cache || !block_table || !out)
+    return fail(MRB_ERR_ARG, "paged_prefill_attention: null pointer");
+  if (!aligned(q, 16) || !aligned(out, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || (stride_page % 8) ||
+      (stride_head % 8) || (stride_tok % 8))
+    return fail(MRB_ERR_ARG, "paged_prefill_attention: q/out and K/V rows must be 16-byte aligned");
+  if ((n + AT_TILE - 1) / AT_TILE > 0x7fffffffLL || hkv > 65535)
+    return fail(MRB_ERR_UNSUPPORTED, "paged_prefill_attention: grid too large");
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(paged_prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
+    if (e != cudaSuccess)
+      return fail(MRB_ERR_CUDA, "paged_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  PrefillArgs a{(const __nv_bfloat16*)q, n, hq, hkv, start, (const __nv_bfloat16*)k_cache,
+                (const __nv_bfloat16*)v_cache, stride_page, stride_head, stride_tok, page_size, block_table,
+                num_pages, error_flag, scale, (__nv_bfloat16*)out};
+  launch_kernel(paged_prefill_attention_kernel, dim3((unsigned)((n + AT_TILE - 1) / AT_TILE), (unsigned)hkv),
+                dim3((unsigned)(32 * (hq / hkv))), PF_SMEM, (cudaStream_t)stream, true, a);
+  return launch_status("paged_prefill_attention");
 }
 
 // ------------------------------------------------------------------ fused decode step (host)

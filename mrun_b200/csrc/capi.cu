@@ -18,7 +18,7 @@ void clear_error() { g_last_error[0] = 0; }
 
 }  // namespace mrb
 
-extern "C" int mrb_abi_version(void) { return 12; }
+extern "C" int mrb_abi_version(void) { return 13; }
 
 extern "C" const char* mrb_last_error(void) { return mrb::g_last_error; }
 

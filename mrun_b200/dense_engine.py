@@ -252,11 +252,14 @@ class DenseDecoder:
     # ------------------------------------------------------------------ body
 
     def _layers(self, rows: int, positions: torch.Tensor, token_rows: torch.Tensor, row_len: torch.Tensor,
-                max_total: int, *, last_only: bool, fused: bool = False) -> torch.Tensor:
+                max_total: int, *, last_only: bool, fused: bool = False,
+                prefill: tuple[int, int] | None = None) -> torch.Tensor:
         """Run embeddings-to-final-norm for ``rows`` tokens already embedded in buf['hidden'].
 
         ``fused``: each row is the next token of a different sequence, so RoPE, the KV append
-        and the attention run as one launch per layer."""
+        and the attention run as one launch per layer. ``prefill`` = (sequence, first
+        position): the rows are consecutive tokens of that sequence, attended causally by the
+        flash prefill kernel."""
         cfg, buf, w = self.cfg, self.buf, self.w
         hidden = buf["hidden"][:rows]
         normed = buf["normed"][:rows]
@@ -300,8 +303,12 @@ class DenseDecoder:
                     rope=(self.cos, self.sin), in_row_stride=cfg.qkv_rows, num_heads=cfg.heads,
                     error_flag=self.error_flag,
                 )
-                self.kv.attend(i, q, row_len, max_total_tokens=max_total, row_seq=token_rows, out=ctx,
-                               workspace=self.workspace, scale=self.scale)
+                if prefill is not None and cfg.head_dim == 128:
+                    self.kv.attend_prefill(i, q, prefill[0], prefill[1], scale=self.scale, out=ctx,
+                                           error_flag=self.error_flag)
+                else:
+                    self.kv.attend(i, q, row_len, max_total_tokens=max_total, row_seq=token_rows, out=ctx,
+                                   workspace=self.workspace, scale=self.scale)
             linear(layer.o, ctx.view(rows, qd), proj)
             residual_rms_norm_into(hidden, proj, layer.ln2, cfg.eps, hidden, normed)
             swiglu(layer.gate, layer.up, normed, mlp)
@@ -330,7 +337,7 @@ class DenseDecoder:
         token_rows = torch.full((n,), seq, dtype=torch.int32, device=self.device)
         row_len = positions + 1
         embed_rows(self.w.embed.codes, self.w.embed.scales, ids, out=self.buf["hidden"][:n])
-        normed = self._layers(n, positions, token_rows, row_len, start + n, last_only=True)
+        normed = self._layers(n, positions, token_rows, row_len, start + n, last_only=True, prefill=(seq, start))
         self.kv.lengths[seq] = start + n
         idx, _, _ = qrow_argmax(self.w.head.codes, self.w.head.scales, normed[n - 1 : n],
                                 out_index=self.next_ids[seq : seq + 1], out_value=self.next_val[seq : seq + 1],

@@ -10,8 +10,8 @@ from __future__ import annotations
 
 import torch
 
-from .segmented_gqa_decode import (paged_attention, paged_attention_workspace_bytes, rope_append_attention,
-                                   rope_kv_append)
+from .segmented_gqa_decode import (paged_attention, paged_attention_workspace_bytes, paged_prefill_attention,
+                                   rope_append_attention, rope_kv_append)
 
 PAGE = 16
 
@@ -137,6 +137,14 @@ class PagedKVCache:
             max_total_tokens=max_total_tokens, in_row_stride=in_row_stride, rope=rope, qk_norm=qk_norm,
             norm_eps=norm_eps, error_flag=error_flag, scale=scale, out=out, state_ready=state_ready,
         )
+
+    def attend_prefill(self, layer: int, query: torch.Tensor, seq: int, start: int, *, scale: float | None = None,
+                       out: torch.Tensor | None = None, error_flag: torch.Tensor | None = None) -> torch.Tensor:
+        """Causal attention of a prefill block of sequence `seq` starting at position `start`
+        (its K/V already appended)."""
+        return paged_prefill_attention(query, self.k[layer], self.v[layer], strides=self.strides,
+                                       page_size=self.page_size, block_row=self.block_table[seq], start=start,
+                                       scale=scale, out=out, error_flag=error_flag)
 
     def workspace_bytes(self, rows: int, num_heads: int, max_total_tokens: int) -> int:
         return paged_attention_workspace_bytes(rows, num_heads, self.kv_heads, self.head_dim, max_total_tokens)

@@ -202,6 +202,38 @@ def rope_append_attention(
     return out
 
 
+def paged_prefill_attention(
+    query: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    *,
+    strides: tuple[int, int, int],
+    page_size: int,
+    block_row: torch.Tensor,
+    start: int,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+    error_flag: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Causal attention of ``query`` [n, hq, 128] (bf16): token i of one sequence sits at
+    position ``start + i`` and attends to positions ``[0, start + i]`` of the pages listed in
+    ``block_row`` (its int32 page-table row); the block's K/V must already be appended."""
+    n, hq, d = (int(v) for v in query.shape)
+    hkv = int(k_cache.shape[1])
+    device = _lib.require_cuda(query, k_cache, v_cache, block_row, what="prefill attention")
+    if query.dtype != torch.bfloat16 or not query.is_contiguous():
+        raise TypeError("prefill attention runs on contiguous bf16 queries")
+    if block_row.dtype != torch.int32 or not block_row.is_contiguous():
+        raise TypeError("the page-table row must be contiguous int32")
+    if out is None:
+        out = torch.empty_like(query)
+    sc = (1.0 / math.sqrt(d)) if scale is None else float(scale)
+    _lib.call("mrb_paged_prefill_attention", query.data_ptr(), n, hq, hkv, d, int(start), k_cache.data_ptr(),
+              v_cache.data_ptr(), strides[0], strides[1], strides[2], page_size, block_row.data_ptr(),
+              int(k_cache.shape[0]), _lib.ptr(error_flag), sc, out.data_ptr(), _lib.stream_handle(device))
+    return out
+
+
 def rope_append_attention_cluster(rows: int, hq: int, hkv: int, head_dim: int, max_total_tokens: int) -> int:
     """CTAs per (row, KV head) the fused decode step uses for these sizes."""
     return int(_lib.load().mrb_rope_append_attention_cluster(rows, hq, hkv, head_dim, max_total_tokens))

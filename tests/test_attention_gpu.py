@@ -266,3 +266,39 @@ def test_rope_append_attention_bad_position_flags_and_zeroes(cuda):
     assert not bool(out[1].any())
     assert bool(out[0].any())
     assert bool(torch.isfinite(out[0].float()).all())
+
+
+@pytest.mark.parametrize("n,start,hq,hkv", [(512, 0, 28, 4), (37, 0, 32, 4), (100, 250, 28, 4), (1, 77, 8, 8),
+                                            (64, 16, 64, 4), (200, 3, 16, 2)])
+def test_paged_prefill_attention_vs_oracle(n, start, hq, hkv, cuda):
+    """Causal prefill attention (query blocks of 16 tokens, the whole K/V prefix per block)
+    against the oracle's per-token attention over the gathered pages; deterministic."""
+    from mrun_b200.paged_kv import PagedKVCache
+
+    rng = np.random.default_rng(n + start + hq)
+    d = 128
+    total = start + n
+    cache = PagedKVCache(num_layers=1, num_pages=(total + 15) // 16 + 5, kv_heads=hkv, head_dim=d, max_seqs=2,
+                         max_pages_per_seq=(total + 15) // 16 + 1, device=cuda)
+    cache.reserve(0, 5)  # another sequence's pages first, so the block table is not the identity
+    cache.reserve(1, total)
+    cache.k.copy_(_bf(rng.standard_normal(tuple(cache.k.shape)), cuda))
+    cache.v.copy_(_bf(rng.standard_normal(tuple(cache.v.shape)), cuda))
+    q = bf16_round(rng.standard_normal((n, hq, d)).astype(np.float32))
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = cache.attend_prefill(0, _bf(q, cuda), 1, start, error_flag=err)
+    again = cache.attend_prefill(0, _bf(q, cuda), 1, start)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(out, again)
+    pages = cache.pages_of(1)
+    kp, vp = cache.k[0].float().cpu().numpy(), cache.v[0].float().cpu().numpy()
+    keys = [oatt.paged_gather(kp, pages, start + i + 1) for i in range(n)]
+    vals = [oatt.paged_gather(vp, pages, start + i + 1) for i in range(n)]
+    ref = bf16_round(oatt.gqa_decode_rows(q, keys, vals))
+    assert max_rel_err(out.float().cpu().numpy(), ref) < TOL
+    # the split-K decode kernel over the same rows (one query row per token) agrees
+    rows_len = torch.arange(start + 1, start + n + 1, dtype=torch.int32, device=cuda)
+    dec = cache.attend(0, _bf(q, cuda), rows_len, max_total_tokens=total,
+                       row_seq=torch.ones(n, dtype=torch.int32, device=cuda))
+    assert max_rel_err(out.float().cpu().numpy(), dec.float().cpu().numpy()) < TOL
