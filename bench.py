@@ -710,6 +710,35 @@ def run_qstore_ingest_case(args) -> None:
                       "source": "page cache (host memory)"}), flush=True)
 
 
+def run_prefill_attn_case(args) -> None:
+    """Small case for kernel captures: causal prefill attention of a 512-token prompt (the
+    config-2 prompt; 28 query / 4 KV heads) over 16 layers' caches in turn (64 MB of K/V).
+    Prints the device-timed average and the attention TFLOP/s (4 x n x ctx/2 x D per head:
+    QK^T and PV over the causal half); not the bench metric."""
+    import torch
+
+    from mrun_b200.paged_kv import PagedKVCache
+
+    n, hq, hkv, d, layers = 512, 28, 4, 128, 16
+    device = torch.device("cuda", 0)
+    kv = PagedKVCache(num_layers=layers, num_pages=n // 16 + 1, kv_heads=hkv, head_dim=d, max_seqs=1,
+                      max_pages_per_seq=n // 16 + 1, device=device)
+    kv.reserve(0, n)
+    gen = torch.Generator(device=device).manual_seed(0)
+    kv.k.normal_(0.0, 1.0, generator=gen)
+    kv.v.normal_(0.0, 1.0, generator=gen)
+    q = torch.randn(n, hq, d, device=device, generator=gen).to(torch.bfloat16)
+    out = torch.empty_like(q)
+
+    def launch(i):
+        kv.attend_prefill(i % layers, q, 0, 0, scale=d ** -0.5, out=out)
+
+    avg_s = _graph_avg_seconds(launch, args.steps, args.warmup, device)
+    flops = 4.0 * hq * d * n * (n + 1) / 2
+    print(json.dumps({"case": args.case, "avg_us": avg_s * 1e6, "tflops": flops / avg_s / 1e12,
+                      "launches": args.steps}), flush=True)
+
+
 def run_fused_attn_case(args) -> None:
     """Small case for kernel captures: the fused decode step (RoPE + KV append + attention,
     one clustered launch) at the config-2 shape -- one row, 28 query / 4 KV heads, 600 cached
@@ -1026,7 +1055,7 @@ def main() -> None:
                     help="moe-decode on N GPUs: expert exchange over NVLink peer memory or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
-                                       *TC_CASES, *ATTN_CASES, "attn-fused1", "qstore-ingest", *EXPERT_CASES],
+                                       *TC_CASES, *ATTN_CASES, "attn-fused1", "attn-prefill512", "qstore-ingest", *EXPERT_CASES],
                     default="decode",
                     help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
     args = ap.parse_args()
@@ -1038,6 +1067,8 @@ def main() -> None:
         run_attn_case(args)
     elif args.case == "attn-fused1":
         run_fused_attn_case(args)
+    elif args.case == "attn-prefill512":
+        run_prefill_attn_case(args)
     elif args.case == "qstore-ingest":
         run_qstore_ingest_case(args)
     elif args.case in EXPERT_CASES:
