@@ -288,7 +288,11 @@ class _PageRing:
             return None
         assert slot.future is not None
         self.stats["hits" if slot.future.done() else "late_hits"] += 1
-        slot.future.result()  # staged and its copy issued (re-raises a staging error)
+        try:
+            slot.future.result()  # staged and its copy issued (re-raises a staging error)
+        except BaseException:
+            slot.release()  # the slot serves the next prefetch; the error reaches the caller
+            raise
         consumer = torch.cuda.current_stream(self.device)
         consumer.wait_event(slot.event)
         # allocated on the ring stream, used on the consumer's: keep the allocator from

@@ -127,3 +127,26 @@ def test_writer_round_trip(tmp_path):
     np.testing.assert_array_equal(oracle.qrow("b")[1], scales[:5])
     np.testing.assert_array_equal(oracle.fp32("n"), norm)
     shutil.rmtree(tmp_path / "m")
+
+
+def test_ring_slot_freed_after_staging_error():
+    """A failed staging read reaches the caller of take() and frees its slot."""
+    from concurrent.futures import Future
+
+    from mrun_b200.qstore import _RingSlot
+
+    class _Ring:  # the take() path of the ring without a device: a slot whose staging failed
+        from mrun_b200.qstore import _PageRing as _cls
+        take = _cls.take
+
+    ring = _Ring()
+    slot = _RingSlot()
+    slot.name, slot.shape = "w", (2, 2)
+    fut = Future()
+    fut.set_exception(OSError("store_file_read: Input/output error"))
+    slot.future = fut
+    ring.inflight = {"w": slot}
+    ring.stats = {"hits": 0, "late_hits": 0, "misses": 0}
+    with pytest.raises(OSError, match="Input/output"):
+        ring.take("w")
+    assert slot.name is None and slot.future is None and ring.stats["hits"] == 1
