@@ -113,3 +113,27 @@ def test_rank_leaving_is_detected_by_collective_timeout():
 def test_shard_ownership(world):
     owners = [e // ExpertShard(world, 0, 128).per_rank for e in range(128)]
     assert owners == sorted(owners) and len(set(owners)) == world
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_p2p_mailbox_layout(world):
+    """The peer-memory mailbox (host-side layout, no GPU): every region 256-byte aligned and
+    disjoint, sized for world x capacity rows each way, flags for up to 64 ranks."""
+    import ctypes
+
+    from mrun_b200 import _lib
+
+    cap, hidden = 256, 2048
+    lib = _lib.load()
+    total = int(lib.mrb_ep_mailbox_bytes(world, cap, hidden))
+    offsets = (ctypes.c_int64 * 6)()
+    _lib.call("mrb_ep_mailbox_offsets", world, cap, hidden, offsets)
+    flags_d, flags_r, counts, ids, rows, back = list(offsets)
+    assert all(v % 256 == 0 for v in offsets)
+    assert flags_d == 0 and flags_r >= 64 * 4 and counts >= flags_r + 64 * 4 and ids >= counts + world * 4
+    assert rows >= ids + world * cap * 4
+    assert back >= rows + world * cap * hidden * 2
+    assert total >= back + world * cap * hidden * 2 and total % 256 == 0
+    assert int(lib.mrb_ep_mailbox_bytes(65, cap, hidden)) == 0  # above the 64-rank flag area
+    with pytest.raises(ValueError, match="bad shape"):
+        _lib.call("mrb_ep_mailbox_offsets", 0, cap, hidden, offsets)
