@@ -51,6 +51,17 @@ class DenseConfig:
         """Qwen2.5-7B shape."""
         return cls(num_layers=28, hidden=3584, heads=28, kv_heads=4, head_dim=128, ffn=18944, vocab=152064)
 
+    @classmethod
+    def from_hf_config(cls, config: dict, *, qkv_bias: bool = True) -> "DenseConfig":
+        """From the Hugging Face config a QStore manifest carries (its ``config`` entry)."""
+        heads = int(config["num_attention_heads"])
+        hidden = int(config["hidden_size"])
+        return cls(num_layers=int(config["num_hidden_layers"]), hidden=hidden, heads=heads,
+                   kv_heads=int(config.get("num_key_value_heads", heads)),
+                   head_dim=int(config.get("head_dim") or hidden // heads), ffn=int(config["intermediate_size"]),
+                   vocab=int(config["vocab_size"]), rope_theta=float(config.get("rope_theta", 1e6)),
+                   eps=float(config.get("rms_norm_eps", 1e-6)), qkv_bias=qkv_bias)
+
     @property
     def qkv_rows(self) -> int:
         return (self.heads + 2 * self.kv_heads) * self.head_dim
@@ -94,6 +105,48 @@ class DenseWeights:
     final_norm: torch.Tensor
     head: QRow
     extras: dict = field(default_factory=dict)
+
+    @staticmethod
+    @torch.inference_mode()
+    def from_blocks(cfg: DenseConfig, qrow, fp32, has) -> "DenseWeights":
+        """Assemble the decoder's weights from QStore blocks under the reference's canonical
+        names (engine/kernels/qstore_build.py:257-276, 340-360): ``L{i}.q/k/v/o/gate/up/down``
+        (qrow), ``L{i}.q.bias/k.bias/v.bias``, ``L{i}.ln1/ln2``, ``norm`` (fp32), ``embed``,
+        ``lm_head`` (qrow, often an alias of ``embed``). ``qrow(name)`` returns (int8 codes,
+        fp32 scales) and ``fp32(name)`` a float32 tensor, both on the target device; ``has``
+        tells whether a block exists. q, k and v are stacked into one [(Hq + 2 Hkv) D, H] page."""
+        layers = []
+        for i in range(cfg.num_layers):
+            parts = [qrow(f"L{i}.{p}") for p in ("q", "k", "v")]
+            qkv = QRow(torch.cat([c for c, _ in parts]).contiguous(), torch.cat([s for _, s in parts]).contiguous())
+            if qkv.codes.shape != (cfg.qkv_rows, cfg.hidden):
+                raise ValueError(f"layer {i}: q/k/v blocks give {tuple(qkv.codes.shape)}, "
+                                 f"expected {(cfg.qkv_rows, cfg.hidden)}")
+            bias = None
+            if cfg.qkv_bias and has(f"L{i}.q.bias"):
+                bias = torch.cat([fp32(f"L{i}.{p}.bias").reshape(-1) for p in ("q", "k", "v")]).contiguous()
+            layers.append(DenseLayer(qkv=qkv, qkv_bias=bias, o=QRow(*qrow(f"L{i}.o")), gate=QRow(*qrow(f"L{i}.gate")),
+                                     up=QRow(*qrow(f"L{i}.up")), down=QRow(*qrow(f"L{i}.down")),
+                                     ln1=fp32(f"L{i}.ln1").reshape(-1).contiguous(),
+                                     ln2=fp32(f"L{i}.ln2").reshape(-1).contiguous()))
+        embed = QRow(*qrow("embed"))
+        head = QRow(*qrow("lm_head" if has("lm_head") else "embed"))
+        if embed.codes.shape != (cfg.vocab, cfg.hidden) or head.codes.shape[1] != cfg.hidden:
+            raise ValueError("embedding / head blocks do not match the config")
+        return DenseWeights(cfg=cfg, embed=embed, layers=layers, final_norm=fp32("norm").reshape(-1).contiguous(),
+                            head=head)
+
+    @staticmethod
+    def from_qstore(store, cfg: DenseConfig | None = None) -> "DenseWeights":
+        """Load a dense decoder from an on-disk int8 QStore (``mrun_b200.qstore.QStore``): the
+        int8 pages go to HBM as they are (no fp32 weight copy)."""
+        cfg = cfg or DenseConfig.from_hf_config(store.cfg)
+
+        def qrow(name):
+            page = store.page(name)
+            return page.codes, page.scales
+
+        return DenseWeights.from_blocks(cfg, qrow, store.fp32, store.has)
 
     @staticmethod
     @torch.inference_mode()
