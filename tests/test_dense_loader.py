@@ -15,7 +15,8 @@ def _write_store(path, cfg, rng, *, tied=True):
     def q(rows, cols):
         return (rng.integers(-127, 128, (rows, cols), dtype=np.int8), rng.random(rows).astype(np.float32) + 0.01)
 
-    h, qd, kd = cfg["hidden_size"], cfg["num_attention_heads"] * 16, cfg["num_key_value_heads"] * 16
+    h, hd = cfg["hidden_size"], cfg["head_dim"]
+    qd, kd = cfg["num_attention_heads"] * hd, cfg["num_key_value_heads"] * hd
     qrows, fp32 = {"embed": q(cfg["vocab_size"], h)}, {"norm": rng.random(h).astype(np.float32)}
     for i in range(cfg["num_hidden_layers"]):
         for name, shape in (("q", (qd, h)), ("k", (kd, h)), ("v", (kd, h)), ("o", (h, qd)),

@@ -68,3 +68,30 @@ def test_ring_under_slot_reuse_and_compute(tmp_path, cuda):
                 assert max_rel_err(out.float().cpu().numpy(), ref) < 1e-2
         stats = store.ring_stats()
     assert stats["hits"] + stats["late_hits"] >= 12, stats
+
+
+def test_dense_decoder_from_qstore_matches_host_assembly(tmp_path, cuda):
+    """A dense model read from its on-disk QStore (pages through the ring) decodes the same
+    greedy tokens as the same blocks assembled from host tensors."""
+    import sys
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from test_dense_loader import _write_store
+
+    from mrun_b200.dense_engine import DenseConfig, DenseDecoder, DenseWeights
+    from mrun_b200.qstore import QStore
+
+    hf = {"num_hidden_layers": 2, "hidden_size": 256, "num_attention_heads": 2, "num_key_value_heads": 1,
+          "head_dim": 128, "intermediate_size": 256, "vocab_size": 200}
+    _write_store(tmp_path / "m", hf, np.random.default_rng(8))
+    oracle = StoreOracle(tmp_path / "m")
+    cfg = DenseConfig.from_hf_config(oracle.manifest["config"])
+    host = DenseWeights.from_blocks(
+        cfg, lambda n: tuple(torch.from_numpy(a.copy()).to(cuda) for a in oracle.qrow(n)),
+        lambda n: torch.from_numpy(oracle.fp32(n).copy()).to(cuda), lambda n: n in oracle.blocks)
+    prompt = torch.tensor([3, 17, 42, 5, 9], dtype=torch.int64)
+    want = DenseDecoder(host, max_batch=1, max_seq_len=64, device=cuda, max_prefill_tokens=16).generate(prompt, 6)
+    with QStore("m", root=tmp_path, device=cuda) as store:
+        loaded = DenseWeights.from_qstore(store)
+        got = DenseDecoder(loaded, max_batch=1, max_seq_len=64, device=cuda, max_prefill_tokens=16).generate(prompt, 6)
+    assert got == want and len(got) == 6
