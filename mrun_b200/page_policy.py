@@ -360,6 +360,48 @@ def replay(trace: PageTrace, *, capacity_pages: int, cache_policy: str, prefill_
     return out
 
 
+def replay_ab(trace: PageTrace, *, capacity_pages: int) -> dict:
+    """Both policy arms over one trace and budget (science/qwen3_moe_page_trace.py:548-614):
+    baseline global-LRU with cache-fill prefill, candidate layer-frequency LRU with transient
+    prefill, and the transfer bytes the candidate saves. A policy simulation, not a runtime
+    measurement."""
+    base = replay(trace, capacity_pages=capacity_pages, cache_policy=GLOBAL_LRU, prefill_page_policy=CACHE_FILL_PREFILL)
+    cand = replay(trace, capacity_pages=capacity_pages, cache_policy=LAYER_FREQUENCY_LRU,
+                  prefill_page_policy=TRANSIENT_FREQUENCY_PREFILL)
+    saved = base["host_to_device_bytes"] - cand["host_to_device_bytes"]
+    return {
+        "trace_sha256": trace.sha256(),
+        "capacity_pages": capacity_pages,
+        "arms": {"baseline": base, "candidate": cand},
+        "comparison": {
+            "candidate_minus_baseline_hits": cand["page_hits"] - base["page_hits"],
+            "candidate_minus_baseline_misses": cand["page_misses"] - base["page_misses"],
+            "candidate_minus_baseline_evictions": cand["evictions"] - base["evictions"],
+            "signed_h2d_bytes_saved": saved,
+            "transfer_reduction_fraction": max(0, saved) / base["host_to_device_bytes"]
+            if base["host_to_device_bytes"] else 0.0,
+        },
+    }
+
+
+def main(argv: Sequence[str] | None = None) -> int:
+    """``python -m mrun_b200.page_policy TRACE.json --capacity-pages N``: print the A/B replay."""
+    import argparse
+
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("trace")
+    ap.add_argument("--capacity-pages", type=int, required=True)
+    args = ap.parse_args(argv)
+    with open(args.trace, encoding="utf-8") as f:
+        trace = PageTrace.from_dict(json.load(f))
+    print(json.dumps(replay_ab(trace, capacity_pages=args.capacity_pages), indent=1, sort_keys=True))
+    return 0
+
+
 __all__ = ["AcquirePlan", "CACHE_FILL_PREFILL", "CACHE_POLICIES", "ExpertResidency", "GLOBAL_LRU",
            "LAYER_FREQUENCY_LRU", "PREFILL_POLICIES", "PageTrace", "ResidencyStats", "TRANSIENT_FREQUENCY_PREFILL",
-           "TransientPlan", "replay"]
+           "TransientPlan", "replay", "replay_ab"]
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

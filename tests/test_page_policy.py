@@ -98,3 +98,29 @@ def test_policy_arguments_and_trace_limits():
     assert trace.events[0]["pages"] == [[1, 2], [2, 1]] and len(trace.sha256()) == 64
     with pytest.raises(RuntimeError, match="exceeds"):
         trace.record(phase="decode", step=1, layer=1, routed=[0])
+
+
+def test_replay_ab_matches_reference_arms(tmp_path):
+    """The A/B replay (baseline global-LRU/cache-fill vs candidate layer-frequency/transient)
+    reproduces the reference simulator's two arms, also through the command line."""
+    import subprocess
+    import sys
+
+    from mrun_b200.page_policy import replay_ab
+
+    trace = PageTrace(FIXTURE["layers"], FIXTURE["page_bytes"])
+    for ev in FIXTURE["events"]:
+        trace.record(phase=ev["phase"], step=ev["step"], layer=ev["layer"], routed=ev["routed"])
+    report = replay_ab(trace, capacity_pages=FIXTURE["capacity"])
+    arms = {(a["cache_policy"], a["prefill_page_policy"]): a["replay"] for a in FIXTURE["arms"]}
+    base = arms[(GLOBAL_LRU, CACHE_FILL_PREFILL)]
+    cand = arms[(LAYER_FREQUENCY_LRU, TRANSIENT_FREQUENCY_PREFILL)]
+    assert report["arms"]["baseline"]["page_hits"] == base["page_hits"]
+    assert report["arms"]["candidate"]["page_hits"] == cand["page_hits"]
+    assert report["comparison"]["signed_h2d_bytes_saved"] == base["h2d_bytes"] - cand["h2d_bytes"]
+    path = tmp_path / "trace.json"
+    path.write_text(json.dumps(trace.as_dict()))
+    out = subprocess.run([sys.executable, "-m", "mrun_b200.page_policy", str(path), "--capacity-pages",
+                          str(FIXTURE["capacity"])], capture_output=True, text=True, check=True,
+                         cwd=Path(__file__).resolve().parents[1])
+    assert json.loads(out.stdout)["comparison"] == report["comparison"]
