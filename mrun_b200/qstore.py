@@ -363,6 +363,55 @@ class _PageRing:
         self.stats["staged"] += 1
 
 
+# ------------------------------------------------------------------ resident page cache
+
+
+class ResidentPageCache:
+    """Byte-budgeted set of pages kept in HBM (engine/kernels/qstore.py:948-1006). Policy
+    ``pin-fill`` (the reference's default) admits pages while they fit and never evicts: a
+    decode loop touches blocks in a fixed cycle, where LRU under a budget smaller than the model
+    evicts every block before its reuse while a static resident set keeps the budget's share.
+    ``lru`` evicts the least recently used page. Here the cached pages are the int8 codes and
+    row scales (what the kernels read), not fp32 expansions, so a budget holds 4x the weights."""
+
+    POLICIES = ("pin-fill", "lru")
+
+    def __init__(self, budget_bytes: int, policy: str = "pin-fill") -> None:
+        if policy not in self.POLICIES:
+            raise ValueError(f"unknown cache policy {policy!r}; expected one of {self.POLICIES}")
+        self.budget = max(0, int(budget_bytes))
+        self.policy = policy
+        self.pages: OrderedDict[str, Any] = OrderedDict()
+        self.bytes = 0
+        self.stats = {"hits": 0, "admitted": 0, "evicted": 0, "rejected": 0}
+
+    def get(self, name: str):
+        entry = self.pages.get(name)
+        if entry is None:
+            return None
+        self.pages.move_to_end(name)
+        self.stats["hits"] += 1
+        return entry[0]
+
+    def put(self, name: str, page, nbytes: int) -> None:
+        if self.budget <= 0 or name in self.pages:
+            return
+        if self.policy == "lru":
+            if nbytes > self.budget:
+                self.stats["rejected"] += 1
+                return
+            while self.bytes + nbytes > self.budget and self.pages:
+                _, (_, old_bytes) = self.pages.popitem(last=False)
+                self.bytes -= old_bytes
+                self.stats["evicted"] += 1
+        elif self.bytes + nbytes > self.budget:
+            self.stats["rejected"] += 1
+            return
+        self.pages[name] = (page, nbytes)
+        self.bytes += nbytes
+        self.stats["admitted"] += 1
+
+
 # ------------------------------------------------------------------ store
 
 
@@ -392,6 +441,7 @@ class QStore:
         self.s = StoreFile(self.directory / "scales.f32")
         self.e = StoreFile(self.directory / "extras.f32")
         self._ring: _PageRing | None = None
+        self._cache: ResidentPageCache | None = None  # set_cache_budget() enables it
         self._miss_q: torch.Tensor | None = None  # pinned staging of direct (unprefetched) reads
         self._miss_s: torch.Tensor | None = None
         self._miss_event: torch.cuda.Event | None = None
@@ -431,6 +481,7 @@ class QStore:
 
     def close(self) -> None:
         self.disable_ring()
+        self._cache = None
         if self._miss_event is not None:
             self._miss_event.synchronize()
         for f in (self.w, self.s, self.e):
@@ -485,12 +536,38 @@ class QStore:
         if block.get("kind") != "qrow":
             raise ValueError(f"QStore block {name!r} is not a qrow block")
         rows, cols = (int(v) for v in block["shape"])
+        cached = self._cache.get(name) if self._cache is not None else None
+        if cached is not None:
+            return cached
         hit = None
         if self._ring is not None:
             hit = self._ring.take(name)
             self._ring.observe(name)
         codes, scales = hit if hit is not None else self._direct(block)
-        return CompactQRowPage(name=name, start_row=0, end_row=rows, in_features=cols, codes=codes, scales=scales)
+        page = CompactQRowPage(name=name, start_row=0, end_row=rows, in_features=cols, codes=codes, scales=scales)
+        if self._cache is not None:
+            self._cache.put(name, page, rows * cols + rows * 4)
+        return page
+
+    def set_cache_budget(self, cache_mb: float, *, policy: str = "pin-fill") -> None:
+        """Keep up to `cache_mb` MB of pages resident in HBM (0 drops the cache); see
+        ``ResidentPageCache`` for the policies."""
+        budget = int(float(cache_mb) * 1e6)
+        self._cache = ResidentPageCache(budget, policy) if budget > 0 else None
+
+    def cache_stats(self) -> dict | None:
+        return None if self._cache is None else {**self._cache.stats, "bytes": self._cache.bytes,
+                                                 "budget": self._cache.budget, "policy": self._cache.policy}
+
+    def matmul_row_stable(self, name: str, x: torch.Tensor) -> torch.Tensor:
+        """``x @ weight(name).T`` with each row computed exactly as a one-row call would
+        (engine/kernels/qstore.py:1094-1097): the page is loaded once and every row runs the
+        M = 1 projection, so a row's bits never depend on the batch it came in."""
+        page = self.page(name)
+        flat = x.reshape(-1, x.shape[-1])
+        rows = [qrow_linear(page.codes, page.scales, flat[i:i + 1]) for i in range(flat.shape[0])]
+        out = torch.cat(rows) if rows else flat.new_empty((0, page.out_features))
+        return out.reshape(*x.shape[:-1], page.out_features)
 
     @torch.inference_mode()
     def weight(self, name: str) -> torch.Tensor:

@@ -150,3 +150,25 @@ def test_ring_slot_freed_after_staging_error():
     with pytest.raises(OSError, match="Input/output"):
         ring.take("w")
     assert slot.name is None and slot.future is None and ring.stats["hits"] == 1
+
+
+def test_resident_page_cache_policies():
+    """pin-fill admits while the budget allows and never evicts; lru evicts the oldest page."""
+    from mrun_b200.qstore import ResidentPageCache
+
+    pin = ResidentPageCache(250, "pin-fill")
+    for i in range(4):
+        pin.put(f"b{i}", f"page{i}", 100)
+    assert list(pin.pages) == ["b0", "b1"] and pin.stats["rejected"] == 2 and pin.get("b3") is None
+    assert pin.get("b0") == "page0" and pin.stats["hits"] == 1
+    lru = ResidentPageCache(250, "lru")
+    for i in range(3):
+        lru.put(f"b{i}", f"page{i}", 100)
+    assert list(lru.pages) == ["b1", "b2"] and lru.stats["evicted"] == 1
+    lru.get("b1")
+    lru.put("b3", "page3", 100)
+    assert list(lru.pages) == ["b1", "b3"] and lru.bytes == 200
+    lru.put("huge", "x", 1000)
+    assert "huge" not in lru.pages and lru.stats["rejected"] == 1
+    with pytest.raises(ValueError, match="unknown cache policy"):
+        ResidentPageCache(10, "mru")

@@ -95,3 +95,30 @@ def test_dense_decoder_from_qstore_matches_host_assembly(tmp_path, cuda):
         loaded = DenseWeights.from_qstore(store)
         got = DenseDecoder(loaded, max_batch=1, max_seq_len=64, device=cuda, max_prefill_tokens=16).generate(prompt, 6)
     assert got == want and len(got) == 6
+
+
+def test_store_resident_cache_and_row_stable_matmul(tmp_path, cuda):
+    """Pages kept resident by the cache are the same bytes; row-stable matmul equals one-row
+    calls bit for bit."""
+    from mrun_b200.dense_qstore_cuda import qrow_linear
+    from mrun_b200.qstore import QStore
+    from mrun_b200.qstore_build import write_qstore
+
+    rng = np.random.default_rng(21)
+    qrows = {f"l{i}": (rng.integers(-127, 128, (64, 256), dtype=np.int8), rng.random(64).astype(np.float32))
+             for i in range(4)}
+    write_qstore(tmp_path / "m", qrows=qrows, fp32={"n": np.ones(4, np.float32)})
+    x = torch.randn(20, 256, device=cuda).to(torch.bfloat16)
+    with QStore("m", root=tmp_path, device=cuda) as store:
+        store.set_cache_budget(0.04)  # two of the four 16.6 KB pages
+        for _ in range(3):
+            for name, (codes, scales) in qrows.items():
+                page = store.page(name)
+                assert torch.equal(page.codes.cpu(), torch.from_numpy(codes))
+                assert torch.equal(page.scales.cpu(), torch.from_numpy(scales))
+        stats = store.cache_stats()
+        assert stats["admitted"] == 2 and stats["hits"] == 4
+        y = store.matmul_row_stable("l1", x)
+        page = store.page("l1")
+        for i in range(x.shape[0]):
+            assert torch.equal(y[i:i + 1], qrow_linear(page.codes, page.scales, x[i:i + 1]))
