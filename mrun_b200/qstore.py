@@ -501,16 +501,24 @@ class QStore:
     def has(self, name: str) -> bool:
         return name in self.blocks
 
-    def _read_block(self, block: Mapping[str, Any], pinned_q: torch.Tensor, pinned_s: torch.Tensor) -> None:
-        rows, cols = (int(v) for v in block["shape"])
-        self.w.read_into(int(block["w_off"]), rows * cols, pinned_q, threads=self.read_threads,
+    def _read_block(self, block: Mapping[str, Any], pinned_q: torch.Tensor, pinned_s: torch.Tensor,
+                    start: int = 0, end: int | None = None) -> None:
+        """Rows [start, end) of a qrow block (all by default) into the pinned buffers."""
+        total, cols = (int(v) for v in block["shape"])
+        end = total if end is None else end
+        rows = end - start
+        self.w.read_into(int(block["w_off"]) + start * cols, rows * cols, pinned_q, threads=self.read_threads,
                          drop_after=self.drop_read_pages)
-        self.s.read_into(int(block["s_off"]), rows * 4, pinned_s, drop_after=self.drop_read_pages)
+        self.s.read_into(int(block["s_off"]) + start * 4, rows * 4, pinned_s, drop_after=self.drop_read_pages)
 
-    def _direct(self, block: Mapping[str, Any]) -> tuple[torch.Tensor, torch.Tensor]:
-        """Read a block through the store's own pinned buffers and copy it on the current
-        stream (the previous direct copy must have left those buffers first)."""
-        rows, cols = (int(v) for v in block["shape"])
+    def _direct(self, block: Mapping[str, Any], start: int = 0,
+                end: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Read rows [start, end) of a block (all by default) through the store's own pinned
+        buffers and copy them on the current stream (the previous direct copy must have left
+        those buffers first)."""
+        total, cols = (int(v) for v in block["shape"])
+        end = total if end is None else end
+        rows = end - start
         n = rows * cols
         if self._miss_q is None or self._miss_q.numel() < n or self._miss_s.numel() < rows:
             max_codes, max_rows = self._max_qrow()
@@ -520,7 +528,7 @@ class QStore:
             self._miss_s = torch.empty(max_rows, dtype=torch.float32, pin_memory=True)
         elif self._miss_event is not None:
             self._miss_event.synchronize()
-        self._read_block(block, self._miss_q, self._miss_s)
+        self._read_block(block, self._miss_q, self._miss_s, start, end)
         codes = torch.empty((rows, cols), dtype=torch.int8, device=self.device)
         scales = torch.empty(rows, dtype=torch.float32, device=self.device)
         codes.view(-1).copy_(self._miss_q[:n], non_blocking=True)
@@ -548,6 +556,36 @@ class QStore:
         if self._cache is not None:
             self._cache.put(name, page, rows * cols + rows * 4)
         return page
+
+    def row_pages(self, name: str, bs: int = 8192):
+        """Stream a qrow matrix in output-row chunks: yields (start, end, page of rows
+        [start, end)) read straight from disk, so a head larger than the staging buffers never
+        needs one whole-matrix copy. Chunks join the resident cache under ``name[start:end]``
+        (engine/kernels/qstore.py:1130-1186)."""
+        block = self._resolve(name)
+        if block.get("kind") != "qrow":
+            raise ValueError(f"QStore block {name!r} is not a qrow block")
+        if bs < 1:
+            raise ValueError("row block size must be positive")
+        rows, cols = (int(v) for v in block["shape"])
+        for start in range(0, rows, bs):
+            end = min(start + bs, rows)
+            key = f"{name}[{start}:{end}]"
+            page = self._cache.get(key) if self._cache is not None else None
+            if page is None:
+                codes, scales = self._direct(block, start, end)
+                page = CompactQRowPage(name=key, start_row=start, end_row=end, in_features=cols, codes=codes,
+                                       scales=scales)
+                if self._cache is not None:
+                    self._cache.put(key, page, (end - start) * (cols + 4))
+            yield start, end, page
+
+    @torch.inference_mode()
+    def row_blocks(self, name: str, bs: int = 8192):
+        """``row_pages`` with each chunk dequantised to fp32 on the device (the reference's
+        ``QStore.row_blocks`` contract, engine/kernels/qstore.py:1130-1186)."""
+        for start, end, page in self.row_pages(name, bs):
+            yield start, end, page.codes.float() * page.scales[:, None]
 
     def set_cache_budget(self, cache_mb: float, *, policy: str = "pin-fill") -> None:
         """Keep up to `cache_mb` MB of pages resident in HBM (0 drops the cache); see

@@ -122,3 +122,19 @@ def test_store_resident_cache_and_row_stable_matmul(tmp_path, cuda):
         page = store.page("l1")
         for i in range(x.shape[0]):
             assert torch.equal(y[i:i + 1], qrow_linear(page.codes, page.scales, x[i:i + 1]))
+
+
+def test_row_blocks_match_reference_weight(golden, cuda):
+    """Row-chunked streaming of a qrow block (uneven last chunk) reassembles the reference's
+    fp32 weight bit for bit, also when the chunks come from the resident cache."""
+    from mrun_b200.qstore import QStore
+
+    g = golden("qstore")
+    want = g["weight__model_embed_tokens_weight"]
+    with QStore("qstore_small", root=GOLDEN, device=cuda, enable_prefetch_ring=False) as store:
+        store.set_cache_budget(1.0)
+        for _ in range(2):
+            chunks = list(store.row_blocks("model.embed_tokens.weight", bs=32))
+            assert [(s, e) for s, e, _ in chunks] == [(0, 32), (32, 64), (64, 96), (96, 100)]
+            np.testing.assert_array_equal(torch.cat([w for _, _, w in chunks]).cpu().numpy(), want)
+        assert store.cache_stats()["hits"] == 4
