@@ -60,3 +60,40 @@ def test_operators_refuse_cpu_tensors():
     scales = torch.ones(8)
     with pytest.raises(RuntimeError, match="CUDA"):
         qrow_linear(codes, scales, torch.zeros(1, 64, dtype=torch.bfloat16))
+
+
+def test_new_attention_entry_points_validate_on_the_host():
+    """The fused decode step and the prefill attention reject bad shapes, unsupported head
+    sizes and null pointers before touching a device."""
+    from mrun_b200 import _lib
+
+    lib = _lib.load()
+    P = 256  # a non-null, 16-byte aligned stand-in address (never dereferenced: validation fails first)
+    # prefill: head_dim 64 is unsupported, pages must hold a multiple of 16 tokens
+    rc = lib.mrb_paged_prefill_attention(P, 4, 8, 2, 64, 0, P, P, 4096, 1024, 128, 16, P, 4, None, 0.1, P, None)
+    assert rc == _lib.MRB_ERR_UNSUPPORTED and b"head_dim 128" in lib.mrb_last_error()
+    rc = lib.mrb_paged_prefill_attention(P, 4, 8, 2, 128, 0, P, P, 4096, 1024, 128, 8, P, 4, None, 0.1, P, None)
+    assert rc == _lib.MRB_ERR_UNSUPPORTED
+    rc = lib.mrb_paged_prefill_attention(P, 4, 34, 2, 128, 0, P, P, 4096, 1024, 128, 16, P, 4, None, 0.1, P, None)
+    assert rc == _lib.MRB_ERR_UNSUPPORTED and b"group" in lib.mrb_last_error()
+    rc = lib.mrb_paged_prefill_attention(None, 4, 8, 2, 128, 0, P, P, 4096, 1024, 128, 16, P, 4, None, 0.1, P, None)
+    assert rc == _lib.MRB_ERR_ARG and b"null" in lib.mrb_last_error()
+    rc = lib.mrb_paged_prefill_attention(P + 2, 4, 8, 2, 128, 0, P, P, 4096, 1024, 128, 16, P, 4, None, 0.1, P, None)
+    assert rc == _lib.MRB_ERR_ARG and b"aligned" in lib.mrb_last_error()
+    assert lib.mrb_paged_prefill_attention(P, 0, 8, 2, 128, 0, P, P, 4096, 1024, 128, 16, P, 4, None, 0.1, P,
+                                           None) == _lib.MRB_OK  # no tokens: nothing to do
+    # fused decode step
+    args = dict(q=P, k=P, v=P, stride=1024, rows=2, hq=8, hkv=2, d=128)
+
+    def fused(**kw):
+        a = {**args, **kw}
+        return lib.mrb_rope_append_attention(a["q"], a["k"], a["v"], a["stride"], a["rows"], a["hq"], a["hkv"],
+                                             a["d"], P, None, None, None, 0, None, None, 1e-6, P, P, 4096, 1024,
+                                             128, 16, P, 8, 4, None, 0.1, 64, 0, P, None)
+
+    assert fused(d=96) == _lib.MRB_ERR_UNSUPPORTED
+    assert fused(hq=40, hkv=2) == _lib.MRB_ERR_UNSUPPORTED
+    assert fused(hq=7) == _lib.MRB_ERR_ARG
+    assert fused(q=None) == _lib.MRB_ERR_ARG
+    assert fused(k=P + 2) == _lib.MRB_ERR_ARG
+    assert fused(rows=0) == _lib.MRB_OK
