@@ -35,14 +35,100 @@ class PageCacheStats:
         return dict(self.__dict__)
 
 
+EXPERT_STORE_SCHEMA = "mrun-b200-int8-expert-store-v1"
+EXPERT_STORE_FILE = "expert_pages.u8"
+
+
+def write_expert_store(directory, layout: ExpertPageLayout, pages) -> dict:
+    """Write expert pages [layers, experts, page_stride] uint8 as an on-disk expert store: one
+    data file of pages in (layer, expert) order plus ``manifest.json`` (the reference's packed
+    expert-store manifest keys, engine/qwen3_moe_cuda.py:780-842, for this build's int8 page
+    layout). Returns the manifest."""
+    import json
+    from pathlib import Path
+
+    import numpy as np
+
+    directory = Path(directory)
+    directory.mkdir(parents=True, exist_ok=True)
+    data = pages.cpu().numpy() if isinstance(pages, torch.Tensor) else np.asarray(pages)
+    if data.dtype != np.uint8 or data.ndim != 3 or data.shape[2] != layout.page_stride:
+        raise ValueError("pages must be uint8 [layers, experts, page_stride]")
+    np.ascontiguousarray(data).tofile(directory / EXPERT_STORE_FILE)
+    manifest = {"schema_version": EXPERT_STORE_SCHEMA, "layout": layout.as_dict(), "layers": int(data.shape[0]),
+                "num_experts": int(data.shape[1]), "data_file": EXPERT_STORE_FILE}
+    (directory / "manifest.json").write_text(json.dumps(manifest, indent=1, sort_keys=True) + "\n")
+    return manifest
+
+
+class ExpertPageStore:
+    """On-disk expert pages read with the library's parallel positional reader (the
+    reference's ``PackedFP8ExpertStore`` role, engine/qwen3_moe_cuda.py:780-842, with the int8
+    page layout): the manifest names the layout, the layer and expert counts and the data file
+    of [layers * experts, page_stride] bytes."""
+
+    def __init__(self, store_dir) -> None:
+        import json
+        from pathlib import Path
+
+        from .qstore import StoreFile
+
+        self.store_dir = Path(store_dir)
+        manifest = json.loads((self.store_dir / "manifest.json").read_text(encoding="utf-8"))
+        if manifest.get("schema_version") != EXPERT_STORE_SCHEMA:
+            raise ValueError("unsupported expert store schema")
+        self.layout = ExpertPageLayout(**{k: int(v) for k, v in manifest["layout"].items()})
+        if self.layout != ExpertPageLayout.create(self.layout.hidden_size, self.layout.intermediate_size):
+            raise ValueError("expert store layout does not match the int8 page layout")
+        self.layers, self.experts = int(manifest["layers"]), int(manifest["num_experts"])
+        if self.layers < 1 or self.experts < 1:
+            raise ValueError("expert store must contain layers and experts")
+        self.file = StoreFile(self.store_dir / manifest["data_file"])
+        if self.file.size != self.layers * self.experts * self.layout.page_stride:
+            self.file.close()
+            raise ValueError("expert store byte length does not match its page geometry")
+
+    def global_page(self, layer: int, expert: int) -> int:
+        return layer * self.experts + expert
+
+    def gather(self, layer: int, expert_ids, target: torch.Tensor, *, threads: int = 4) -> None:
+        """Pages of `layer`'s `expert_ids` into host uint8 rows target[:len(expert_ids)]."""
+        stride = self.layout.page_stride
+        if target.is_cuda or target.dtype != torch.uint8 or target.shape[-1] != stride:
+            raise ValueError("expert page staging target must be a host uint8 [n, page_stride] tensor")
+        for i, expert in enumerate(expert_ids):
+            if not 0 <= int(expert) < self.experts or not 0 <= int(layer) < self.layers:
+                raise IndexError(f"expert page ({layer}, {expert}) outside the store")
+            self.file.read_into(self.global_page(int(layer), int(expert)) * stride, stride, target[i], threads=threads)
+
+    def close(self) -> None:
+        self.file.close()
+
+
 class HostPageTier:
     """Pinned host copy of every expert page: [layers, experts, page_stride] uint8."""
 
-    def __init__(self, layout: ExpertPageLayout, layers: int, experts: int) -> None:
+    def __init__(self, layout: ExpertPageLayout, layers: int, experts: int, *, pin: bool = True) -> None:
         self.layout = layout
         self.layers = layers
         self.experts = experts
-        self.pages = torch.empty((layers, experts, layout.page_stride), dtype=torch.uint8, pin_memory=True)
+        self.pages = torch.empty((layers, experts, layout.page_stride), dtype=torch.uint8, pin_memory=pin)
+        self.stats = {"warmed_pages": 0, "warm_seconds": 0.0, "pinned": bool(pin)}
+
+    @classmethod
+    def from_store(cls, store: ExpertPageStore, *, pin: bool = True, threads: int | None = None) -> "HostPageTier":
+        """Fill the tier from an on-disk store in one sequential pass of parallel reads
+        straight into the (pinned) tier -- the reference's pread warm-up of
+        ``HostPageTier.warm`` (engine/qwen3_moe_cuda.py:925-951), without a memory map."""
+        import time
+
+        from .qstore import DEFAULT_READ_THREADS
+
+        tier = cls(store.layout, store.layers, store.experts, pin=pin)
+        started = time.perf_counter()
+        store.file.read_into(0, tier.pages.numel(), tier.pages, threads=threads or DEFAULT_READ_THREADS)
+        tier.stats.update(warmed_pages=store.layers * store.experts, warm_seconds=time.perf_counter() - started)
+        return tier
 
     @property
     def nbytes(self) -> int:
