@@ -294,6 +294,30 @@ class ExpertResidency:
                              [where[e] for e in experts])
 
 
+def options_from_env(*, cache_policy: str | None = None, prefill_page_policy: str | None = None,
+                     route_prefetch: bool | None = None, page_trace: bool | None = None,
+                     environ=None) -> dict:
+    """Fill the options a caller left as None from the reference's environment switches
+    (engine/qwen3_moe_cuda.py:1239-1330): MRUN_QWEN3_MOE_CACHE_POLICY (default global-lru-v1),
+    MRUN_QWEN3_MOE_PREFILL_PAGE_POLICY (default cache-fill-v1), MRUN_QWEN3_MOE_ROUTE_PREFETCH
+    (on unless empty or "0") and MRUN_QWEN3_MOE_PAGE_TRACE (off for empty, 0, false, no, off).
+    Explicit arguments win."""
+    import os
+
+    env = os.environ if environ is None else environ
+    if cache_policy is None:
+        cache_policy = env.get("MRUN_QWEN3_MOE_CACHE_POLICY", GLOBAL_LRU)
+    if prefill_page_policy is None:
+        prefill_page_policy = env.get("MRUN_QWEN3_MOE_PREFILL_PAGE_POLICY", CACHE_FILL_PREFILL)
+    if route_prefetch is None:
+        route_prefetch = env.get("MRUN_QWEN3_MOE_ROUTE_PREFETCH", "").strip() not in ("", "0")
+    if page_trace is None:
+        page_trace = env.get("MRUN_QWEN3_MOE_PAGE_TRACE", "").strip().lower() not in ("", "0", "false", "no", "off")
+    return {"cache_policy": str(cache_policy).strip().lower(),
+            "prefill_page_policy": str(prefill_page_policy).strip().lower(),
+            "route_prefetch": bool(route_prefetch), "page_trace": bool(page_trace)}
+
+
 # ------------------------------------------------------------------ page trace and replay
 
 
@@ -400,7 +424,7 @@ def main(argv: Sequence[str] | None = None) -> int:
 
 __all__ = ["AcquirePlan", "CACHE_FILL_PREFILL", "CACHE_POLICIES", "ExpertResidency", "GLOBAL_LRU",
            "LAYER_FREQUENCY_LRU", "PREFILL_POLICIES", "PageTrace", "ResidencyStats", "TRANSIENT_FREQUENCY_PREFILL",
-           "TransientPlan", "replay", "replay_ab"]
+           "TransientPlan", "options_from_env", "replay", "replay_ab"]
 
 
 if __name__ == "__main__":

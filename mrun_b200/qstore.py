@@ -43,6 +43,29 @@ QSTORE_FILES = ("weights.i8", "scales.f32", "extras.f32")
 DEFAULT_READ_THREADS = max(4, min(32, os.cpu_count() or 8))
 
 
+def store_options_from_env(*, ring: bool = True, ring_slots: int = 3, cache_policy: str | None = None,
+                           environ=None) -> dict:
+    """The reference's QStore switches (engine/kernels/qstore.py:756-772, 948-973):
+    MRUN_PAGED_RING = "0" turns the prefetch ring off and an integer above 1 sets its slot
+    count; MRUN_QSTORE_CACHE_POLICY picks the resident cache policy when none is given
+    (pin-fill by default and for an unknown name, which is reported)."""
+    env = os.environ if environ is None else environ
+    ring_env = env.get("MRUN_PAGED_RING", "").strip()
+    if ring_env == "0":
+        ring = False
+    elif ring_env.isdigit() and int(ring_env) > 1:
+        ring_slots = int(ring_env)
+    policy = cache_policy
+    if policy is None:
+        policy = env.get("MRUN_QSTORE_CACHE_POLICY", "pin-fill").strip().lower() or "pin-fill"
+        if policy not in ResidentPageCache.POLICIES:
+            import warnings
+
+            warnings.warn(f"MRUN_QSTORE_CACHE_POLICY={policy!r} unknown -> pin-fill (want pin-fill|lru)")
+            policy = "pin-fill"
+    return {"ring": ring, "ring_slots": int(ring_slots), "cache_policy": policy}
+
+
 # ------------------------------------------------------------------ native file reader
 
 
@@ -445,8 +468,9 @@ class QStore:
         self._miss_q: torch.Tensor | None = None  # pinned staging of direct (unprefetched) reads
         self._miss_s: torch.Tensor | None = None
         self._miss_event: torch.cuda.Event | None = None
-        if enable_prefetch_ring:
-            self.enable_ring(slots=ring_slots, depth=ring_depth)
+        opts = store_options_from_env(ring=enable_prefetch_ring, ring_slots=ring_slots)
+        if opts["ring"]:
+            self.enable_ring(slots=opts["ring_slots"], depth=ring_depth)
 
     # ---- lifecycle
 
@@ -587,10 +611,11 @@ class QStore:
         for start, end, page in self.row_pages(name, bs):
             yield start, end, page.codes.float() * page.scales[:, None]
 
-    def set_cache_budget(self, cache_mb: float, *, policy: str = "pin-fill") -> None:
+    def set_cache_budget(self, cache_mb: float, *, policy: str | None = None) -> None:
         """Keep up to `cache_mb` MB of pages resident in HBM (0 drops the cache); see
-        ``ResidentPageCache`` for the policies."""
+        ``ResidentPageCache`` for the policies (default from MRUN_QSTORE_CACHE_POLICY)."""
         budget = int(float(cache_mb) * 1e6)
+        policy = store_options_from_env(cache_policy=policy)["cache_policy"]
         self._cache = ResidentPageCache(budget, policy) if budget > 0 else None
 
     def cache_stats(self) -> dict | None:

@@ -19,7 +19,7 @@ import torch
 
 from . import _lib
 from .moe import ExpertPageLayout
-from .page_policy import (CACHE_FILL_PREFILL, GLOBAL_LRU, TRANSIENT_FREQUENCY_PREFILL, ExpertResidency, PageTrace)
+from .page_policy import TRANSIENT_FREQUENCY_PREFILL, ExpertResidency, PageTrace, options_from_env
 
 
 @dataclass
@@ -143,11 +143,17 @@ class ExpertPageCache:
 
     cache_policy / prefill_page_policy / route_prefetch select the residency rules (see
     ``page_policy``); page_trace records every acquisition's routed pages for offline replay
-    (``page_policy.replay``)."""
+    (``page_policy.replay``). Options left as None come from the reference's environment
+    switches (``page_policy.options_from_env``)."""
 
     def __init__(self, host: HostPageTier, *, budget_bytes: int, device: torch.device,
-                 cache_policy: str = GLOBAL_LRU, prefill_page_policy: str = CACHE_FILL_PREFILL,
-                 route_prefetch: bool = False, page_trace: bool = False, max_active_pages: int | None = None) -> None:
+                 cache_policy: str | None = None, prefill_page_policy: str | None = None,
+                 route_prefetch: bool | None = None, page_trace: bool | None = None,
+                 max_active_pages: int | None = None) -> None:
+        opts = options_from_env(cache_policy=cache_policy, prefill_page_policy=prefill_page_policy,
+                                route_prefetch=route_prefetch, page_trace=page_trace)
+        cache_policy, prefill_page_policy = opts["cache_policy"], opts["prefill_page_policy"]
+        route_prefetch, page_trace = opts["route_prefetch"], opts["page_trace"]
         self.host = host
         self.layout = host.layout
         self.device = device

@@ -124,3 +124,26 @@ def test_replay_ab_matches_reference_arms(tmp_path):
                           str(FIXTURE["capacity"])], capture_output=True, text=True, check=True,
                          cwd=Path(__file__).resolve().parents[1])
     assert json.loads(out.stdout)["comparison"] == report["comparison"]
+
+
+def test_reference_environment_switches():
+    """Options left unset follow the reference's environment variables; explicit ones win."""
+    from mrun_b200.page_policy import options_from_env
+    from mrun_b200.qstore import store_options_from_env
+
+    assert options_from_env(environ={}) == {"cache_policy": GLOBAL_LRU, "prefill_page_policy": CACHE_FILL_PREFILL,
+                                            "route_prefetch": False, "page_trace": False}
+    env = {"MRUN_QWEN3_MOE_CACHE_POLICY": "Layer-Frequency-LRU-v1 ", "MRUN_QWEN3_MOE_ROUTE_PREFETCH": "1",
+           "MRUN_QWEN3_MOE_PAGE_TRACE": "yes", "MRUN_QWEN3_MOE_PREFILL_PAGE_POLICY": "cache-fill-v1"}
+    got = options_from_env(environ=env)
+    assert got == {"cache_policy": LAYER_FREQUENCY_LRU, "prefill_page_policy": CACHE_FILL_PREFILL,
+                   "route_prefetch": True, "page_trace": True}
+    assert options_from_env(route_prefetch=False, environ=env)["route_prefetch"] is False
+    assert options_from_env(environ={"MRUN_QWEN3_MOE_PAGE_TRACE": "off"})["page_trace"] is False
+    assert store_options_from_env(environ={}) == {"ring": True, "ring_slots": 3, "cache_policy": "pin-fill"}
+    assert store_options_from_env(environ={"MRUN_PAGED_RING": "0"})["ring"] is False
+    assert store_options_from_env(environ={"MRUN_PAGED_RING": "5"})["ring_slots"] == 5
+    assert store_options_from_env(environ={"MRUN_QSTORE_CACHE_POLICY": "LRU"})["cache_policy"] == "lru"
+    with pytest.warns(UserWarning, match="unknown"):
+        assert store_options_from_env(environ={"MRUN_QSTORE_CACHE_POLICY": "mru"})["cache_policy"] == "pin-fill"
+    assert store_options_from_env(cache_policy="lru", environ={"MRUN_QSTORE_CACHE_POLICY": "mru"})["cache_policy"] == "lru"
