@@ -138,6 +138,73 @@ class HostPageTier:
         return layer * self.experts + expert
 
 
+class BudgetedHostPageTier:
+    """Host-RAM tier of at most ``host_cache_mb`` of an on-disk expert store, for callers that
+    stage pages themselves (the reference's ``HostPageTier`` contract,
+    engine/qwen3_moe_cuda.py:878-980): ``warm()`` fills the tier with the first pages in one
+    sequential pass of parallel reads; ``gather`` serves pages from the tier, else from disk,
+    admitting disk pages while room remains (fill once, no eviction). Pinned when possible."""
+
+    def __init__(self, store: ExpertPageStore, *, host_cache_mb: float, try_pin: bool = True) -> None:
+        import numpy as np
+
+        self.store = store
+        stride = store.layout.page_stride
+        total = store.layers * store.experts
+        self.capacity = min(total, int(float(host_cache_mb) * 1e6) // stride)
+        if self.capacity < 1:
+            raise ValueError("host_cache_mb smaller than one expert page")
+        self.pinned = False
+        buf = None
+        if try_pin:
+            try:
+                buf = torch.empty((self.capacity, stride), dtype=torch.uint8, pin_memory=True)
+                self.pinned = True
+            except RuntimeError:
+                buf = None
+        self.buf = buf if buf is not None else torch.empty((self.capacity, stride), dtype=torch.uint8)
+        self._rows = np.full(total, -1, dtype=np.int64)
+        self._next = 0
+        self.stats = {"capacity_pages": self.capacity, "pinned": self.pinned, "warmed_pages": 0, "warm_seconds": 0.0,
+                      "served_pages": 0, "admitted_pages": 0, "disk_pages": 0}
+
+    def warm(self, *, threads: int | None = None) -> dict:
+        import time
+
+        import numpy as np
+
+        from .qstore import DEFAULT_READ_THREADS
+
+        started = time.perf_counter()
+        stride = self.store.layout.page_stride
+        if self._next < self.capacity:
+            first = self._next
+            self.store.file.read_into(first * stride, (self.capacity - first) * stride, self.buf[first:],
+                                      threads=threads or DEFAULT_READ_THREADS)
+            self._rows[first:self.capacity] = np.arange(first, self.capacity)
+            self._next = self.capacity
+        self.stats["warm_seconds"] = time.perf_counter() - started
+        self.stats["warmed_pages"] = self._next
+        return dict(self.stats)
+
+    def gather(self, layer: int, expert_ids, target: torch.Tensor) -> None:
+        """Pages of `layer`'s `expert_ids` into host uint8 rows target[:len(expert_ids)]."""
+        for i, expert in enumerate(expert_ids):
+            gid = self.store.global_page(int(layer), int(expert))
+            row = int(self._rows[gid]) if 0 <= gid < self._rows.size else -1
+            if row >= 0:
+                target[i].copy_(self.buf[row])
+                self.stats["served_pages"] += 1
+                continue
+            self.store.gather(layer, [expert], target[i:i + 1])
+            self.stats["disk_pages"] += 1
+            if self._next < self.capacity:
+                self.buf[self._next].copy_(target[i])
+                self._rows[gid] = self._next
+                self._next += 1
+                self.stats["admitted_pages"] += 1
+
+
 class ExpertPageCache:
     """HBM slot cache over a HostPageTier, copies on a side stream.
 

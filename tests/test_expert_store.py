@@ -56,3 +56,31 @@ def test_malformed_stores_refused(tmp_path):
         ExpertPageStore(tmp_path / "e")
     with pytest.raises(ValueError, match="uint8"):
         write_expert_store(tmp_path / "f", layout, np.zeros((1, 1, 8), np.float32))
+
+
+def test_budgeted_host_tier_serves_ram_then_disk(tmp_path):
+    """A tier smaller than the store: warm() holds the first pages, gathers of other pages come
+    from disk and are admitted until the budget is full; every page is bit-exact."""
+    from mrun_b200.moe import ExpertPageLayout
+    from mrun_b200.streaming import BudgetedHostPageTier, ExpertPageStore, write_expert_store
+
+    layout = ExpertPageLayout.create(128, 64)
+    data = _pages(2, 4, layout, seed=4)
+    write_expert_store(tmp_path / "e", layout, data)
+    store = ExpertPageStore(tmp_path / "e")
+    tier = BudgetedHostPageTier(store, host_cache_mb=3 * layout.page_stride / 1e6, try_pin=False)
+    assert tier.capacity == 3
+    stats = tier.warm(threads=2)
+    assert stats["warmed_pages"] == 3  # pages (0,0), (0,1), (0,2)
+    target = torch.zeros((3, layout.page_stride), dtype=torch.uint8)
+    tier.gather(0, [2, 3, 1], target)
+    np.testing.assert_array_equal(target.numpy(), data[0, [2, 3, 1]])
+    assert tier.stats["served_pages"] == 2 and tier.stats["disk_pages"] == 1 and tier.stats["admitted_pages"] == 0
+    small = BudgetedHostPageTier(store, host_cache_mb=2 * layout.page_stride / 1e6, try_pin=False)
+    small.gather(1, [3, 0], target)  # cold tier: both from disk, both admitted
+    small.gather(1, [0, 3, 2], target)
+    np.testing.assert_array_equal(target.numpy(), data[1, [0, 3, 2]])
+    assert small.stats["admitted_pages"] == 2 and small.stats["served_pages"] == 2 and small.stats["disk_pages"] == 3
+    with pytest.raises(ValueError, match="smaller than one expert page"):
+        BudgetedHostPageTier(store, host_cache_mb=0.0, try_pin=False)
+    store.close()
