@@ -48,7 +48,7 @@ class DenseConfig:
 
     @classmethod
     def qwen25_7b(cls) -> "DenseConfig":
-        """Qwen2.5-7B shape."""
+        """Qwen2.5-7B shape: 28 layers, hidden 3584, 28/4 heads, FFN 18944, vocab 152064."""
         return cls(num_layers=28, hidden=3584, heads=28, kv_heads=4, head_dim=128, ffn=18944, vocab=152064)
 
     @classmethod

@@ -50,7 +50,7 @@ class MoeConfig:
 
     @classmethod
     def qwen3_30b_a3b(cls) -> "MoeConfig":
-        """Qwen3-30B-A3B shape."""
+        """Qwen3-30B-A3B shape: 48 layers, hidden 2048, 32/4 heads, 128 experts top-8, expert FFN 768."""
         return cls(num_layers=48, hidden=2048, heads=32, kv_heads=4, head_dim=128, experts=128, top_k=8,
                    expert_ffn=768, vocab=151936)
 

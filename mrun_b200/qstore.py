@@ -119,101 +119,144 @@ class StoreFile:
 # ------------------------------------------------------------------ manifest
 
 
-def _int_field(block: Mapping[str, Any], key: str, *, positive: bool = False) -> int:
-    value = block.get(key)
-    if isinstance(value, bool) or not isinstance(value, int):
-        raise RuntimeError(f"QStore block field {key!r} must be an integer")
-    if value < (1 if positive else 0):
-        raise RuntimeError(f"QStore block field {key!r} must be {'positive' if positive else 'non-negative'}")
+class QStoreLayoutError(RuntimeError):
+    """A store directory whose block table does not describe its files.
+
+    ``reason`` names the broken rule (one of ``LAYOUT_REASONS``) and ``subject`` the block or
+    file it was found on, so callers can branch without parsing the message."""
+
+    def __init__(self, reason: str, subject: str | None, message: str) -> None:
+        super().__init__(message)
+        self.reason = reason
+        self.subject = subject
+
+
+LAYOUT_REASONS = ("header", "kinds", "field", "shape", "length", "kind", "alias-target", "alias-cycle",
+                  "missing-file", "bounds", "overlap", "gap", "tail")
+
+# For each data kind: the file ranges a block of that kind owns, as (file, offset field,
+# length field, bytes per element, element count from the shape). Aliases own no bytes.
+_KIND_SPANS = {
+    "qrow": (("weights.i8", "w_off", "w_len", 1, lambda shape: shape[0] * shape[1]),
+             ("scales.f32", "s_off", "s_len", 4, lambda shape: shape[0])),
+    "fp32": (("extras.f32", "e_off", "e_len", 4, math.prod),),
+}
+_KIND_DIMS = {"qrow": 2, "fp32": None}
+
+
+def _layout_error(reason: str, subject: str | None, text: str) -> QStoreLayoutError:
+    return QStoreLayoutError(reason, subject, f"QStore layout ({reason}): {text}")
+
+
+def _count(block: Mapping[str, Any], field: str, name: str, *, least: int) -> int:
+    """A byte offset (least 0) or length (least 1) read from a block descriptor."""
+    value = block.get(field)
+    if type(value) is not int:  # bool is an int subclass and is refused too
+        raise _layout_error("field", name, f"block {name!r} field {field!r} is {value!r}, not an integer")
+    if value < least:
+        raise _layout_error("field", name, f"block {name!r} field {field!r} = {value} is below {least}")
     return value
 
 
-def _shape_field(block: Mapping[str, Any], dims: int | None = None) -> tuple[int, ...]:
-    raw = block.get("shape")
-    if not isinstance(raw, list) or not raw:
-        raise RuntimeError("QStore block shape must be a non-empty list")
-    if any(isinstance(v, bool) or not isinstance(v, int) or v <= 0 for v in raw):
-        raise RuntimeError("QStore block shape dimensions must be positive integers")
-    if dims is not None and len(raw) != dims:
-        raise RuntimeError(f"QStore block shape must have {dims} dimensions")
-    return tuple(raw)
+def _dims(block: Mapping[str, Any], name: str, rank: int | None) -> tuple[int, ...]:
+    shape = block.get("shape")
+    ok = isinstance(shape, list) and len(shape) > 0 and all(type(v) is int and v > 0 for v in shape)
+    if not ok or (rank is not None and len(shape) != rank):
+        want = f"{rank} positive integers" if rank else "a non-empty list of positive integers"
+        raise _layout_error("shape", name, f"block {name!r} shape {shape!r} is not {want}")
+    return tuple(shape)
+
+
+def _block_spans(name: str, block: Mapping[str, Any]) -> list[tuple[str, int, int]]:
+    """The (file, start, end) byte ranges a data block occupies, checked against its shape."""
+    kind = block.get("kind")
+    if kind not in _KIND_SPANS:
+        raise _layout_error("kind", name, f"block {name!r} has kind {kind!r}; only 'qrow' and 'fp32' are stored")
+    shape = _dims(block, name, _KIND_DIMS[kind])
+    spans = []
+    for filename, off_field, len_field, width, elements in _KIND_SPANS[kind]:
+        start = _count(block, off_field, name, least=0)
+        length = _count(block, len_field, name, least=1)
+        if length != elements(shape) * width or start % width:
+            raise _layout_error("length", name, f"block {name!r} range {start}+{length} in {filename} does not "
+                                f"hold {elements(shape)} elements of {width} byte(s) for shape {list(shape)}")
+        spans.append((filename, start, start + length))
+    return spans
+
+
+def _check_aliases(aliases: dict[str, Any], blocks: Mapping[str, Any]) -> None:
+    """Every alias chain ends at a data block: targets exist, and following the links from any
+    alias never returns to a name already on the chain (three-colour walk, each name once)."""
+    done: set[str] = set()
+    for start in aliases:
+        chain: list[str] = []
+        on_chain: set[str] = set()
+        name = start
+        while name in aliases and name not in done:
+            if name in on_chain:
+                raise _layout_error("alias-cycle", name, f"alias chain {' -> '.join(chain + [name])} loops")
+            chain.append(name)
+            on_chain.add(name)
+            target = aliases[name]
+            if not isinstance(target, str) or not target:
+                raise _layout_error("alias-target", name, f"alias {name!r} has target {target!r}")
+            if target not in blocks or not isinstance(blocks[target], Mapping):
+                raise _layout_error("alias-target", name, f"alias {name!r} points at {target!r}, which is not a block")
+            name = target
+        done.update(chain)
+
+
+def _check_coverage(directory: Path, spans: dict[str, list[tuple[int, int, str]]]) -> None:
+    """Each store file is exactly the concatenation of the ranges its blocks own."""
+    for filename in QSTORE_FILES:
+        path = directory / filename
+        if not path.is_file():
+            raise _layout_error("missing-file", filename, f"{filename} is not in {directory}")
+        size = path.stat().st_size
+        cursor = 0
+        for start, end, name in sorted(spans[filename]):
+            if end > size:
+                raise _layout_error("bounds", name, f"{filename}: block {name!r} ends at byte {end}, "
+                                    f"past the file's {size} bytes")
+            if start != cursor:
+                reason = "overlap" if start < cursor else "gap"
+                raise _layout_error(reason, name, f"{filename}: block {name!r} starts at byte {start}, "
+                                    f"the previous range ends at {cursor}")
+            cursor = end
+        if cursor != size:
+            raise _layout_error("tail", filename, f"{filename}: {size - cursor} trailing byte(s) belong to no block")
 
 
 def validate_int8_layout(directory: Path, manifest: Mapping[str, Any]) -> None:
-    """The reference's int8 layout contract (engine/kernels/qstore.py:124-219): every block
-    well formed, aliases resolve without cycles, and in each file the referenced ranges tile
-    the whole file with no gap and no overlap. Raises RuntimeError otherwise."""
+    """Check that a store directory is a well-formed int8 QStore before any byte is read.
+
+    The accept/reject rules are those of the reference's loader (engine/kernels/qstore.py:
+    124-219): the manifest declares int8, carries a config and a non-empty block table with at
+    least one qrow and one fp32 block; every data block's ranges match its shape; every alias
+    chain ends at a data block; and each of the three files is covered by its blocks' ranges
+    exactly once, with nothing left over. Raises ``QStoreLayoutError`` (a RuntimeError)."""
+    directory = Path(directory)
     if manifest.get("dtype") != "int8":
-        raise RuntimeError("QStore must declare dtype='int8'")
+        raise _layout_error("header", None, f"manifest dtype is {manifest.get('dtype')!r}, not 'int8'")
     blocks = manifest.get("blocks")
     if not isinstance(manifest.get("config"), Mapping) or not isinstance(blocks, Mapping) or not blocks:
-        raise RuntimeError("QStore requires config and a non-empty block table")
-    ranges: dict[str, list[tuple[int, int, str]]] = {name: [] for name in QSTORE_FILES}
-    n_qrow = n_fp32 = 0
+        raise _layout_error("header", None, "manifest needs a config mapping and a non-empty block table")
+    spans: dict[str, list[tuple[int, int, str]]] = {f: [] for f in QSTORE_FILES}
+    aliases: dict[str, Any] = {}
+    kinds_seen: set[str] = set()
     for name, block in blocks.items():
         if not isinstance(name, str) or not name or not isinstance(block, Mapping):
-            raise RuntimeError("QStore block names and descriptors must be non-empty mappings")
+            raise _layout_error("header", None, f"block table entry {name!r} is not a named mapping")
         if "alias" in block:
-            if not isinstance(block.get("alias"), str) or not block["alias"]:
-                raise RuntimeError(f"QStore alias {name!r} has an invalid target")
+            aliases[name] = block["alias"]
             continue
-        kind = block.get("kind")
-        if kind == "qrow":
-            rows, cols = _shape_field(block, 2)
-            w_off, w_len = _int_field(block, "w_off"), _int_field(block, "w_len", positive=True)
-            s_off, s_len = _int_field(block, "s_off"), _int_field(block, "s_len", positive=True)
-            if w_len != rows * cols:
-                raise RuntimeError(f"QStore qrow {name!r} weight length does not match its shape")
-            if s_len != rows * 4 or s_off % 4:
-                raise RuntimeError(f"QStore qrow {name!r} scale range does not match its shape")
-            ranges["weights.i8"].append((w_off, w_off + w_len, name))
-            ranges["scales.f32"].append((s_off, s_off + s_len, name))
-            n_qrow += 1
-        elif kind == "fp32":
-            shape = _shape_field(block)
-            e_off, e_len = _int_field(block, "e_off"), _int_field(block, "e_len", positive=True)
-            if e_len != math.prod(shape) * 4 or e_off % 4:
-                raise RuntimeError(f"QStore fp32 {name!r} range does not match its shape")
-            ranges["extras.f32"].append((e_off, e_off + e_len, name))
-            n_fp32 += 1
-        else:
-            raise RuntimeError(f"QStore block {name!r} has unsupported kind {kind!r}")
-    if not n_qrow or not n_fp32:
-        raise RuntimeError("QStore requires qrow and fp32 blocks")
-    for name, block in blocks.items():
-        if "alias" not in block:
-            continue
-        seen, target = {name}, block["alias"]
-        while True:
-            if target not in blocks:
-                raise RuntimeError(f"QStore alias {name!r} targets missing block {target!r}")
-            if target in seen:
-                raise RuntimeError(f"QStore alias cycle contains {target!r}")
-            seen.add(target)
-            if not isinstance(blocks[target], Mapping):
-                raise RuntimeError(f"QStore alias {name!r} targets an invalid block")
-            nxt = blocks[target].get("alias")
-            if nxt is None:
-                break
-            if not isinstance(nxt, str) or not nxt:
-                raise RuntimeError(f"QStore alias {target!r} has an invalid target")
-            target = nxt
-    for filename, spans in ranges.items():
-        path = directory / filename
-        if not path.is_file():
-            raise RuntimeError(f"QStore file is missing: {filename}")
-        size = path.stat().st_size
-        end = 0
-        for lo, hi, name in sorted(spans):
-            if hi > size:
-                raise RuntimeError(f"QStore {filename} range for block {name!r} exceeds file bounds")
-            if lo < end:
-                raise RuntimeError(f"QStore {filename} ranges overlap at block {name!r}")
-            if lo != end:
-                raise RuntimeError(f"QStore {filename} has an unreferenced gap before block {name!r}")
-            end = hi
-        if end != size:
-            raise RuntimeError(f"QStore {filename} block ranges do not cover the complete file")
+        for filename, start, end in _block_spans(name, block):
+            spans[filename].append((start, end, name))
+        kinds_seen.add(block["kind"])
+    if kinds_seen != set(_KIND_SPANS):
+        raise _layout_error("kinds", None, f"block table holds kinds {sorted(kinds_seen)}; both qrow and fp32 are needed")
+    _check_aliases(aliases, blocks)
+    _check_coverage(directory, spans)
 
 
 def _resolve_in(blocks: Mapping[str, Any], name: str) -> Mapping[str, Any]:

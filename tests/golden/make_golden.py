@@ -102,7 +102,7 @@ def qrow_fixtures() -> None:
 
 
 def config1_fixture() -> None:
-    """BASELINE config 1 at full size, recorded as checksums plus the fp32 outputs."""
+    """The 8 x 2048 x 2048 W8A16 / W8A8 linear at full size, recorded as checksums plus the fp32 outputs."""
     from mrun.engine.kernels.qstore import _dequant_qrow  # noqa: PLC0415
     from mrun.engine.kernels.qstore_build import _quant_row_int8  # noqa: PLC0415
     from mrun.engine.kernels.w8a8 import _int8_gemm, w8a8_matmul  # noqa: PLC0415

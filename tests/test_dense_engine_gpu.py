@@ -121,7 +121,7 @@ def test_w8a8_batched_decode_matches_oracle(cuda):
 
 @pytest.mark.slow
 def test_qwen25_7b_shape_decode_smoke(cuda):
-    """Full BASELINE config-2 shapes: prefill 512 random ids, 32 greedy steps, twice."""
+    """Full Qwen2.5-7B shapes (28 layers, hidden 3584, vocab 152064): prefill 512 random ids, 32 greedy steps, twice."""
     from mrun_b200.dense_engine import DenseConfig, DenseDecoder, DenseWeights
 
     cfg = DenseConfig.qwen25_7b()

@@ -15,10 +15,44 @@ GOLDEN = Path(__file__).resolve().parent / "golden"
 STORE = GOLDEN / "qstore_small"
 
 
-def _norm(text: str) -> str:
-    # the reference names its current schema ("semantic QStore v3") and its provenance
-    # files ("derived"); the B200 reader validates the same layout without those words
-    return text.replace("semantic QStore v3", "QStore").replace("derived file", "file")
+# The reference validator's error text (its verdict on each corrupted store, recorded in the
+# fixture) mapped to the rule it enforces and the block or file it names. The B200 validator
+# raises QStoreLayoutError with its own wording; what must agree is accept/reject, the broken
+# rule and where it was found.
+_REFERENCE_RULES = [
+    (r"must declare dtype", "header", None),
+    (r"requires config and a non-empty block table", "header", None),
+    (r"requires qrow and fp32 blocks", "kinds", None),
+    (r"block field '\w+' must be", "field", "*"),
+    (r"block shape", "shape", "*"),
+    (r"qrow '(.+)' (weight length|scale range) does not match", "length", 1),
+    (r"fp32 '(.+)' range does not match", "length", 1),
+    (r"block '(.+)' has unsupported kind", "kind", 1),
+    (r"alias '(.+)' targets missing block", "alias-target", 1),
+    (r"alias cycle contains '(.+)'", "alias-cycle", "cycle"),
+    (r"file is missing: (\S+)", "missing-file", 1),
+    (r"(\S+) range for block '(.+)' exceeds file bounds", "bounds", 2),
+    (r"(\S+) ranges overlap at block '(.+)'", "overlap", 2),
+    (r"(\S+) has an unreferenced gap before block '(.+)'", "gap", 2),
+    (r"(\S+) block ranges do not cover the complete file", "tail", 1),
+]
+
+
+def _expected(verdict: str, case: dict):
+    import re
+
+    for pattern, reason, subject in _REFERENCE_RULES:
+        m = re.search(pattern, verdict)
+        if not m:
+            continue
+        if isinstance(subject, int):
+            return reason, m.group(subject)
+        if subject == "cycle":  # any member of the cycle the case builds
+            return reason, {edit[1] for edit in case["edit"] if edit[0] == "alias"}
+        if subject == "*":  # the block the case edited
+            return reason, {edit[1] for edit in case["edit"] if edit[0] == "set"}
+        return reason, None
+    raise AssertionError(f"no rule recognised in reference verdict {verdict!r}")
 
 
 def test_layout_validator_matches_reference_verdicts(tmp_path):
@@ -27,10 +61,11 @@ def test_layout_validator_matches_reference_verdicts(tmp_path):
     sys.path.insert(0, str(GOLDEN))
     from make_qstore_fixtures import apply_case
 
-    from mrun_b200.qstore import validate_int8_layout
+    from mrun_b200.qstore import LAYOUT_REASONS, QStoreLayoutError, validate_int8_layout
 
     cases = json.loads((GOLDEN / "qstore_layout_cases.json").read_text())
     assert len(cases) >= 10 and cases[0]["verdict"] == "ok"
+    seen = set()
     for i, case in enumerate(cases):
         directory = tmp_path / f"case{i}"
         apply_case(STORE, directory, case)
@@ -38,9 +73,19 @@ def test_layout_validator_matches_reference_verdicts(tmp_path):
         if case["verdict"] == "ok":
             validate_int8_layout(directory, manifest)
             continue
+        assert case["verdict"].startswith("RuntimeError: ")
         with pytest.raises(RuntimeError) as err:
             validate_int8_layout(directory, manifest)
-        assert _norm(f"RuntimeError: {err.value}") == _norm(case["verdict"]), case["name"]
+        assert isinstance(err.value, QStoreLayoutError), case["name"]
+        reason, subject = _expected(case["verdict"], case)
+        assert err.value.reason == reason, (case["name"], str(err.value))
+        assert err.value.reason in LAYOUT_REASONS
+        if isinstance(subject, set):
+            assert err.value.subject in subject, (case["name"], str(err.value))
+        elif subject is not None:
+            assert err.value.subject == subject, (case["name"], str(err.value))
+        seen.add(reason)
+    assert len(seen) >= 10  # the fixture exercises most rules
 
 
 def test_oracle_pinned_to_reference_outputs(golden):
