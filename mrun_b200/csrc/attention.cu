@@ -15,6 +15,7 @@
 #include "tc_common.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace mrb {
 
@@ -1472,13 +1473,9 @@ static int launch_attention(const AttnArgs& a, int64_t head_dim, int64_t max_tot
   if (use_mma(a.rows, a.hkv, max_total, head_dim)) {
     const int warps = std::min(AM_MAX_WARPS, std::max(1, a.tiles_per_split));
     const size_t smem = am_smem_bytes(warps);
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-      cudaError_t e = cudaFuncSetAttribute(paged_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)am_smem_bytes(AM_MAX_WARPS));
-      if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "paged_attention: smem attribute: %s", cudaGetErrorString(e));
-      configured = am_smem_bytes(AM_MAX_WARPS);
-    }
+    const int st = ensure_dynamic_smem((const void*)paged_attention_mma_kernel, am_smem_bytes(AM_MAX_WARPS),
+                                       "paged_attention");
+    if (st) return st;
     launch_kernel(paged_attention_mma_kernel, grid, dim3(32 * warps), smem, s, true, a);
   } else {
     launch_kernel(head_dim == 128 ? paged_attention_kernel<128> : paged_attention_kernel<64>, grid,
@@ -1639,14 +1636,9 @@ extern "C" int mrb_paged_prefill_attention(const void* q, int64_t n, int64_t hq,
     return fail(MRB_ERR_ARG, "paged_prefill_attention: q/out and K/V rows must be 16-byte aligned");
   if ((n + AT_TILE - 1) / AT_TILE > 0x7fffffffLL || hkv > 65535)
     return fail(MRB_ERR_UNSUPPORTED, "paged_prefill_attention: grid too large");
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(paged_prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM);
-    if (e != cudaSuccess)
-      return fail(MRB_ERR_CUDA, "paged_prefill_attention: smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+  const int smem_st =
+      ensure_dynamic_smem((const void*)paged_prefill_attention_kernel, PF_SMEM, "paged_prefill_attention");
+  if (smem_st) return smem_st;
   PrefillArgs a{(const __nv_bfloat16*)q, n, hq, hkv, start, (const __nv_bfloat16*)k_cache,
                 (const __nv_bfloat16*)v_cache, stride_page, stride_head, stride_tok, page_size, block_table,
                 num_pages, error_flag, scale, (__nv_bfloat16*)out};
@@ -1737,15 +1729,9 @@ static int launch_fused(const FusedArgs& a, int64_t head_dim, int64_t max_total,
   cfg.dynamicSmemBytes = p.mma ? am_smem_bytes(p.warps) : 0;
   cfg.stream = st;
   if (p.mma) {
-    static size_t configured = 0;
-    if (cfg.dynamicSmemBytes > configured) {
-      const cudaError_t e = cudaFuncSetAttribute(rope_append_attention_mma_kernel,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)am_smem_bytes(AM_MAX_WARPS));
-      if (e != cudaSuccess)
-        return fail(MRB_ERR_CUDA, "rope_append_attention: smem attribute: %s", cudaGetErrorString(e));
-      configured = am_smem_bytes(AM_MAX_WARPS);
-    }
+    const int smem_st = ensure_dynamic_smem((const void*)rope_append_attention_mma_kernel,
+                                            am_smem_bytes(AM_MAX_WARPS), "rope_append_attention");
+    if (smem_st) return smem_st;
   }
   cudaLaunchAttribute attr[2];
   int n = 0;
@@ -1858,8 +1844,50 @@ static __device__ __align__(256) unsigned char g_attn_static_scratch[MRB_ATTN_ST
 namespace mrb {
 namespace {
 constexpr int kMaxDevices = 64;
-int g_static_ready[kMaxDevices] = {0};
+// Per device: the context the address was resolved in and the array's device address there.
+// A device reset (cudaDeviceReset) makes a new primary context in which the module, and so
+// the array, is loaded again at a possibly different address; a changed context handle sends
+// the next call back through cudaGetSymbolAddress.
+std::mutex g_static_lock;
+void* g_static_ctx[kMaxDevices] = {nullptr};
 void* g_static_ptr[kMaxDevices] = {nullptr};
+
+using CtxGetCurrentFn = int (*)(void**);  // the driver's cuCtxGetCurrent(CUcontext*)
+
+CtxGetCurrentFn ctx_get_current() {
+  static const CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (CtxGetCurrentFn) nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
+// The device address of g_attn_static_scratch on the current device (nullptr on error, with
+// the message set). Looked up once per device and context, with that device current.
+void* static_scratch_address(int dev) {
+  const CtxGetCurrentFn get_ctx = ctx_get_current();
+  void* ctx = nullptr;
+  if (!get_ctx || get_ctx(&ctx) != 0 || ctx == nullptr) {
+    fail(MRB_ERR_CUDA, "paged_attention_static: no current CUDA context");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> hold(g_static_lock);
+  if (g_static_ctx[dev] != ctx || g_static_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_attn_static_scratch);
+    if (e != cudaSuccess || ptr == nullptr) {
+      fail(MRB_ERR_CUDA, "paged_attention_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_static_ctx[dev] = ctx;
+    g_static_ptr[dev] = ptr;
+  }
+  return g_static_ptr[dev];
+}
 }  // namespace
 }  // namespace mrb
 
@@ -1905,17 +1933,10 @@ extern "C" int mrb_paged_attention_static(const void* q, int64_t rows, int64_t h
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "paged_attention_static: cudaGetDevice: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return fail(MRB_ERR_UNSUPPORTED, "paged_attention_static: device %d", dev);
-    // once per device, with that device current: the device address of the static array
-    // (host code only has a host-side stand-in for it)
-    if (!__atomic_load_n(&g_static_ready[dev], __ATOMIC_ACQUIRE)) {
-      void* ptr = nullptr;
-      e = cudaGetSymbolAddress(&ptr, g_attn_static_scratch);
-      if (e != cudaSuccess || ptr == nullptr)
-        return fail(MRB_ERR_CUDA, "paged_attention_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-      g_static_ptr[dev] = ptr;
-      __atomic_store_n(&g_static_ready[dev], 1, __ATOMIC_RELEASE);
-    }
-    scratch = g_static_ptr[dev];
+    // the device address of the static array (host code only has a host-side stand-in for
+    // it), resolved once per device and context with that device current
+    scratch = static_scratch_address(dev);
+    if (!scratch) return MRB_ERR_CUDA;
   }
   AttnArgs a{(const __nv_bfloat16*)q, rows, hq, hkv, (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache,
              stride_page, stride_head, stride_tok, page_size, block_table, block_table_stride, row_seq, row_len,

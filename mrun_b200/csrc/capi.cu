@@ -3,6 +3,9 @@
 
 #include <string.h>
 
+#include <map>
+#include <mutex>
+
 namespace mrb {
 
 static thread_local char g_last_error[1024] = {0};
@@ -16,9 +19,25 @@ void set_error(const char* fmt, ...) {
 
 void clear_error() { g_last_error[0] = 0; }
 
+int ensure_dynamic_smem(const void* kernel, size_t bytes, const char* what) {
+  if (bytes <= 48 * 1024) return MRB_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  static std::mutex lock;
+  static std::map<std::pair<const void*, int>, size_t> granted;  // (kernel, device) -> bytes
+  std::lock_guard<std::mutex> hold(lock);
+  size_t& have = granted[{kernel, dev}];
+  if (bytes <= have) return MRB_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "%s: shared memory attribute: %s", what, cudaGetErrorString(e));
+  have = bytes;
+  return MRB_OK;
+}
+
 }  // namespace mrb
 
-extern "C" int mrb_abi_version(void) { return 13; }
+extern "C" int mrb_abi_version(void) { return 14; }
 
 extern "C" const char* mrb_last_error(void) { return mrb::g_last_error; }
 

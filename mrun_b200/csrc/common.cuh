@@ -43,6 +43,12 @@ inline int launch_status(const char* what) {
   return MRB_OK;
 }
 
+// Raise `kernel`'s dynamic shared-memory limit to at least `bytes` on the CURRENT device
+// (cudaFuncSetAttribute applies per device). Remembers what each (kernel, device) pair was
+// given, so repeated launches pay one locked map lookup; safe from several host threads and
+// for a process that drives several GPUs. Returns MRB_OK or an MRB_ERR_CUDA status.
+int ensure_dynamic_smem(const void* kernel, size_t bytes, const char* what);
+
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 inline int num_sms() {

@@ -612,13 +612,9 @@ extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, cons
   a.chunks = (int)((rtiles + a.chunk_tiles - 1) / a.chunk_tiles);
   const int64_t grid = std::min<int64_t>(experts * a.chunks, slots);
   cudaStream_t s = (cudaStream_t)stream;
-  static size_t configured[4] = {0, 0, 0, 0};  // per kernel instantiation
-  auto run = [&](auto kern, int which) -> int {
-    if (smem > 48 * 1024 && smem > configured[which]) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "grouped_qrow: smem attribute: %s", cudaGetErrorString(e));
-      configured[which] = smem;
-    }
+  auto run = [&](auto kern, int) -> int {
+    const int smem_st = ensure_dynamic_smem((const void*)kern, smem, "grouped_qrow");
+    if (smem_st) return smem_st;
     launch_kernel(kern, dim3((unsigned)grid), dim3(GX_THREADS), smem, s, true, a);
     return launch_status("grouped_qrow");
   };

@@ -226,12 +226,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) qrow_gemm_bf16_kernel(GemmArgs 
 
 template <bool PAIRED>
 static int launch_gemm(const GemmArgs& a, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(qrow_gemm_bf16_kernel<PAIRED>, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM);
-    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "qrow gemm: smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+  const int smem_st = ensure_dynamic_smem((const void*)qrow_gemm_bf16_kernel<PAIRED>, GM_SMEM, "qrow gemm");
+  if (smem_st) return smem_st;
   const int64_t rows_per_cta = PAIRED ? GM_BN / 2 : GM_BN;
   const int64_t gx = (a.n + rows_per_cta - 1) / rows_per_cta;
   const int64_t gy = (a.m + GM_BM - 1) / GM_BM;

@@ -632,12 +632,8 @@ static int launch_gemv(const GemvArgs& a0, GvWorkspace ws, cudaStream_t s) {
                 (long long)a0.m, (long long)a0.k);
   if (a0.n > (1LL << 27)) return fail(MRB_ERR_UNSUPPORTED, "qrow gemv: %lld output rows", (long long)a0.n);
   auto kern = qrow_gemv_kernel<XT, YT, SPLIT, NT, EPI>;
-  static size_t configured = 0;  // per instantiation
-  if (plan.smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
-    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "qrow gemv: smem attribute: %s", cudaGetErrorString(e));
-    configured = plan.smem;
-  }
+  const int smem_st = ensure_dynamic_smem((const void*)kern, plan.smem, "qrow gemv");
+  if (smem_st) return smem_st;
   GemvArgs a = a0;
   a.units = 0;
   a.stages = plan.stages;

@@ -413,12 +413,8 @@ template <int HALVES, int BN>
 static int tc_launch(TcGemmArgs& a, const int8_t* qx, const int8_t* qw, const int8_t* qw_up, cudaStream_t s) {
   using Tile = TcTile<HALVES, BN>;
   auto kern = tc_int8_gemm_kernel<HALVES, BN>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile::SMEM);
-    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc int8 gemm: smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+  const int smem_st = ensure_dynamic_smem((const void*)kern, Tile::SMEM, "tc int8 gemm");
+  if (smem_st) return smem_st;
   int st = encode_map_2d(&a.map_x, qx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.m, a.k, Tile::BM, TC_BK,
                          CU_TENSOR_MAP_SWIZZLE_128B);
   const int wrows = a.paired ? BN / 2 : BN;

@@ -469,12 +469,8 @@ static int tw_launch(TwGemmArgs& a, const __nv_bfloat16* x, const int8_t* codes,
                      cudaStream_t s) {
   using Tile = TwTile<HALVES, BN>;
   auto kern = tc_w8a16_gemm_kernel<HALVES, BN>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Tile::SMEM);
-    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "tc w8a16 gemm: smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+  const int smem_st = ensure_dynamic_smem((const void*)kern, Tile::SMEM, "tc w8a16 gemm");
+  if (smem_st) return smem_st;
   const int wrows = a.paired ? BN / 2 : BN;
   int st = encode_map_2d(&a.map_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.m, a.k, Tile::BM, TW_BKE,
                          CU_TENSOR_MAP_SWIZZLE_128B);

@@ -469,12 +469,8 @@ static int launch_int8_gemm(const I8GemmArgs& a, cudaStream_t s) {
 }
 
 [[maybe_unused]] static int launch_int8_gemm_mma_sync(const I8GemmArgs& a, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(int8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, I8_SMEM);
-    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "int8 gemm: smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
-  }
+  const int smem_st = ensure_dynamic_smem((const void*)int8_gemm_kernel, I8_SMEM, "int8 gemm");
+  if (smem_st) return smem_st;
   const int64_t gx = (a.n + I8_BN - 1) / I8_BN, gy = (a.m + I8_BM - 1) / I8_BM;
   if (gy > 65535) return fail(MRB_ERR_UNSUPPORTED, "int8 gemm: too many activation rows");
   cudaError_t e = launch_kernel(int8_gemm_kernel, dim3((unsigned)gx, (unsigned)gy), dim3(I8_THREADS), I8_SMEM, s,
@@ -490,12 +486,8 @@ static int launch_a8_gemv(const A8Args& a, cudaStream_t s) {
     return fail(MRB_ERR_UNSUPPORTED, "w8a8 gemv: activation block %lld x %lld too large", (long long)a.m,
                 (long long)a.k);
   auto kern = w8a8_gemv_kernel<XT, NT>;
-  static size_t configured = 0;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "w8a8 gemv: smem attribute: %s", cudaGetErrorString(e));
-    configured = smem;
-  }
+  const int smem_st = ensure_dynamic_smem((const void*)kern, smem, "w8a8 gemv");
+  if (smem_st) return smem_st;
   const int per_sm = 2 * (smem + 1024) <= 227 * 1024 ? 2 : 1;
   const int64_t ntiles = (a.n + A8_ROWS - 1) / A8_ROWS;
   const int64_t grid = std::min<int64_t>(ntiles, (int64_t)num_sms() * per_sm);
@@ -704,13 +696,7 @@ extern "C" int mrb_w8a8_protect_topk(const void* x, int x_dtype, int64_t m, int6
   if (smem > 200 * 1024) return fail(MRB_ERR_UNSUPPORTED, "w8a8_protect_topk: k %lld too large", (long long)k);
   cudaStream_t s = (cudaStream_t)stream;
   auto run = [&](auto kern) -> int {
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "w8a8_protect_topk: smem attribute: %s", cudaGetErrorString(e));
-      configured = smem;
-    }
-    return MRB_OK;
+    return ensure_dynamic_smem((const void*)kern, smem, "w8a8_protect_topk");
   };
   int st = MRB_OK;
   switch (x_dtype) {

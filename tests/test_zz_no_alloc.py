@@ -93,11 +93,16 @@ def test_static_scratch_rejects_oversized_plans(cuda):
     rows, hq, hkv, max_total = 8, 128, 8, 1 << 20
     need = int(_lib.load().mrb_paged_attention_workspace(rows, hq, hkv, 128, max_total))
     assert need > cap
-    c = _case(1, 16, 1, [16], 1, cuda)
+    # every row maps to one real page and holds one token, so even a launch that the size
+    # check failed to stop would stay inside these buffers
+    k = torch.zeros(1, hkv, 16, 128, dtype=torch.bfloat16, device=cuda)
+    v = torch.zeros_like(k)
+    table = torch.zeros(rows, 1, dtype=torch.int32, device=cuda)
+    row_len = torch.ones(rows, dtype=torch.int32, device=cuda)
     out = torch.empty(rows, hq, 128, dtype=torch.bfloat16, device=cuda)
     q = torch.zeros(rows, hq, 128, dtype=torch.bfloat16, device=cuda)
-    with pytest.raises(RuntimeError, match="static"):
-        _lib.call("mrb_paged_attention_static", q.data_ptr(), rows, hq, hkv, 128, c["k"].data_ptr(),
-                  c["v"].data_ptr(), hkv * 16 * 128, 16 * 128, 128, 16, c["table"].data_ptr(), 1, None,
-                  torch.ones(rows, dtype=torch.int32, device=cuda).data_ptr(), None, None, 0.088, max_total,
+    with pytest.raises(RuntimeError, match="bytes of scratch"):
+        _lib.call("mrb_paged_attention_static", q.data_ptr(), rows, hq, hkv, 128, k.data_ptr(), v.data_ptr(),
+                  hkv * 16 * 128, 16 * 128, 128, 16, table.data_ptr(), 1, None, row_len.data_ptr(), None, None,
+                  0.088, max_total,
                   out.data_ptr(), _lib.stream_handle(cuda))
