@@ -270,6 +270,11 @@ int mrb_ep_p2p_return(const void *eo_bf16, const int64_t *inverse, int64_t hidde
                       void *stream);
 int mrb_ep_p2p_wait_return(void *mailbox, int64_t world, int64_t capacity, int64_t hidden,
                            int32_t *state, void *stream);
+/* Bound (in polls, each followed by a ~64 ns sleep) of the flag waits launched from now on by
+ * mrb_ep_p2p_wait_dispatch / mrb_ep_p2p_wait_return in this process; 2^22 by default, [1, 2^30].
+ * A graph captured earlier keeps the bound it was captured with. mrb_ep_wait_limit reads it. */
+int mrb_ep_set_wait_limit(int64_t polls);
+int64_t mrb_ep_wait_limit(void);
 
 /* ---------------------------------------------------------------- on-disk stores */
 
@@ -403,7 +408,9 @@ int mrb_paged_attention(const void *q, int64_t rows, int64_t hq, int64_t hkv, in
  *   MRB_ERR_UNSUPPORTED (mrb_paged_attention_workspace gives the need; use the
  *   workspace entry point for those).
  * - The first call on a device looks up the array's device address with that device
- *   current; make that first call before any stream capture.
+ *   current; make that first call before any stream capture. The address is kept per device
+ *   and context: after cudaDeviceReset the next call looks it up again (a call made while
+ *   capturing would then fail), so repeat a first call outside capture after a reset.
  * - Every call on a device shares the array: calls that can overlap on the GPU (different
  *   streams without ordering) race and must not be issued. Each call returns the array's
  *   merge counters to zero, so consecutive calls need no clearing. */

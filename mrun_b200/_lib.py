@@ -82,10 +82,12 @@ SIGNATURES: dict[str, list] = {
     "mrb_ep_p2p_wait_dispatch": [_P, _I64, _I64, _I64, c_int32, _P, _P, _P],
     "mrb_ep_p2p_return": [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _P],
     "mrb_ep_p2p_wait_return": [_P, _I64, _I64, _I64, _P, _P],
+    "mrb_ep_set_wait_limit": [_I64],
+    "mrb_ep_wait_limit": [],
 }
 _RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t,
              "mrb_paged_attention_static_capacity": c_size_t, "mrb_qrow_workspace": c_size_t,
-             "mrb_ep_mailbox_bytes": c_size_t}
+             "mrb_ep_mailbox_bytes": c_size_t, "mrb_ep_wait_limit": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -19,7 +19,9 @@
 // CUDA graph replays the exchange with fresh flag values. Buffer reuse is safe without extra
 // barriers: a rank dispatches into layer L's mailboxes again only after its own combine of
 // layer L, which waited for every owner's return, which each owner issued after reading the
-// rows. Every wait is bounded: on a timeout the kernel sets state[3] (error) and proceeds.
+// rows. Every wait is bounded (mrb_ep_set_wait_limit polls, 2^22 by default): on a timeout
+// the kernel sets state[3] (error) and proceeds, so the step completes and the host can
+// read the error.
 // No TMA and no cluster multicast is involved; peers are reached by ordinary loads/stores.
 #include "qrow_common.cuh"
 
@@ -30,7 +32,11 @@ namespace mrb {
 
 constexpr size_t EPM_ALIGN = 256;
 constexpr int EPM_MAX_WORLD = 64;
-constexpr int EPM_SPIN = 1 << 22;  // bounded wait: polls with a short sleep between them
+constexpr int EPM_SPIN = 1 << 22;  // default bound of a wait: polls with a short sleep between them
+// Poll bound given to the wait kernels launched from now on (a captured graph keeps the value
+// it was captured with). mrb_ep_set_wait_limit changes it; tests shorten it to make a wait run
+// out quickly.
+static int g_epm_spin_limit = EPM_SPIN;
 
 struct MailboxLayout {
   size_t flags_dispatch, flags_return, counts, ids, rows, back, total;
@@ -103,12 +109,12 @@ __global__ void ep_p2p_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int6
   }
 }
 
-__device__ bool epm_wait_flags(const unsigned* flags, int world, unsigned epoch) {
+__device__ bool epm_wait_flags(const unsigned* flags, int world, unsigned epoch, int spin_limit) {
   bool ok = true;
   for (int s = threadIdx.x; s < world; s += blockDim.x) {
     int i = 0;
     while (ld_acquire_sys(flags + s) != epoch) {
-      if (++i == EPM_SPIN) {
+      if (++i >= spin_limit) {
         ok = false;
         break;
       }
@@ -119,11 +125,13 @@ __device__ bool epm_wait_flags(const unsigned* flags, int world, unsigned epoch)
 }
 
 __global__ void ep_p2p_wait_dispatch_kernel(unsigned char* __restrict__ mailbox, MailboxLayout lay, int world, int cap,
-                                            int dummy, int64_t* __restrict__ ids64, int32_t* __restrict__ state) {
+                                            int dummy, int64_t* __restrict__ ids64, int32_t* __restrict__ state,
+                                            int spin_limit) {
   pdl_launch_dependents();
   pdl_wait();
   const unsigned epoch = (unsigned)state[0];
-  const bool ok = epm_wait_flags(reinterpret_cast<const unsigned*>(mailbox + lay.flags_dispatch), world, epoch);
+  const bool ok =
+      epm_wait_flags(reinterpret_cast<const unsigned*>(mailbox + lay.flags_dispatch), world, epoch, spin_limit);
   if (!ok && threadIdx.x == 0) state[3] = 1;
   const int32_t* counts = reinterpret_cast<const int32_t*>(mailbox + lay.counts);
   const int32_t* ids = reinterpret_cast<const int32_t*>(mailbox + lay.ids);
@@ -164,11 +172,12 @@ __global__ void ep_p2p_return_kernel(const __nv_bfloat16* __restrict__ eo, const
 }
 
 __global__ void ep_p2p_wait_return_kernel(unsigned char* __restrict__ mailbox, MailboxLayout lay, int world,
-                                          int32_t* __restrict__ state) {
+                                          int32_t* __restrict__ state, int spin_limit) {
   pdl_launch_dependents();
   pdl_wait();
   const unsigned epoch = (unsigned)state[0];
-  const bool ok = epm_wait_flags(reinterpret_cast<const unsigned*>(mailbox + lay.flags_return), world, epoch);
+  const bool ok =
+      epm_wait_flags(reinterpret_cast<const unsigned*>(mailbox + lay.flags_return), world, epoch, spin_limit);
   if (!ok && threadIdx.x == 0) state[3] = 1;
 }
 
@@ -184,6 +193,15 @@ static int ep_grid(int64_t slots) { return (int)std::max<int64_t>(1, std::min<in
 }  // namespace mrb
 
 using namespace mrb;
+
+extern "C" int mrb_ep_set_wait_limit(int64_t polls) {
+  if (polls < 1 || polls > (1LL << 30)) return fail(MRB_ERR_ARG, "ep_set_wait_limit: polls must be in [1, 2^30]");
+  g_epm_spin_limit = (int)polls;
+  clear_error();
+  return MRB_OK;
+}
+
+extern "C" int64_t mrb_ep_wait_limit(void) { return g_epm_spin_limit; }
 
 extern "C" size_t mrb_ep_mailbox_bytes(int64_t world, int64_t capacity, int64_t hidden) {
   if (world < 1 || world > EPM_MAX_WORLD || capacity < 1 || hidden <= 0) return 0;
@@ -257,7 +275,8 @@ extern "C" int mrb_ep_p2p_wait_dispatch(void* mailbox, int64_t world, int64_t ca
   if (!mailbox || !ids64 || !state) return fail(MRB_ERR_ARG, "ep_p2p_wait_dispatch: null pointer");
   const MailboxLayout lay = epm_layout(world, capacity, hidden);
   launch_kernel(ep_p2p_wait_dispatch_kernel, dim3(1), dim3(256), 0, (cudaStream_t)stream, true,
-                (unsigned char*)mailbox, lay, (int)world, (int)capacity, (int)dummy_expert, ids64, state);
+                (unsigned char*)mailbox, lay, (int)world, (int)capacity, (int)dummy_expert, ids64, state,
+                g_epm_spin_limit);
   return launch_status("ep_p2p_wait_dispatch");
 }
 
@@ -282,6 +301,6 @@ extern "C" int mrb_ep_p2p_wait_return(void* mailbox, int64_t world, int64_t capa
   if (!mailbox || !state) return fail(MRB_ERR_ARG, "ep_p2p_wait_return: null pointer");
   const MailboxLayout lay = epm_layout(world, capacity, hidden);
   launch_kernel(ep_p2p_wait_return_kernel, dim3(1), dim3(64), 0, (cudaStream_t)stream, true, (unsigned char*)mailbox,
-                lay, (int)world, state);
+                lay, (int)world, state, g_epm_spin_limit);
   return launch_status("ep_p2p_wait_return");
 }

@@ -415,13 +415,27 @@ def fused_qrow_exact_argmax(
     return (index + page.start_row).reshape(shape), value.reshape(shape), IMPL_ARGMAX
 
 
+def __getattr__(name: str):
+    """``DenseQStore`` and ``load_compact_qrow_page`` live in ``mrun_b200.dense_store`` (they
+    build on ``qstore.QStore``, which imports this module) and are served from here too, where
+    the reference keeps them (engine/kernels/dense_qstore_cuda.py:963, 1857)."""
+    if name in ("DenseQStore", "DenseQStoreStats", "load_compact_qrow_page"):
+        from . import dense_store
+
+        return getattr(dense_store, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
+
+
 __all__ = [
     "CompactQRowPage",
+    "DenseQStore",
+    "DenseQStoreStats",
     "dequantized_reference_matmul",
     "fused_qrow_exact_argmax",
     "fused_qrow_matmul",
     "fused_qrow_swiglu",
     "fused_residual_rms_norm",
+    "load_compact_qrow_page",
     "qrow_argmax",
     "qrow_linear",
     "qrow_swiglu",

@@ -69,6 +69,18 @@ class ExpertPageLayout:
             page_stride=align_up(down_scales_off + down_scales),
         )
 
+    @classmethod
+    def from_dict(cls, payload: dict[str, Any]) -> "ExpertPageLayout":
+        """A layout recorded in a store manifest. The B200 kernels read every part with
+        16-byte vector loads, so each offset must be 16-byte aligned (``create`` always is,
+        and so is the reference's layout whenever H and F are multiples of 4)."""
+        layout = cls(**{name: int(payload[name]) for name in cls.__dataclass_fields__})
+        offsets = (layout.gate_up_scales_offset, layout.down_codes_offset, layout.down_scales_offset,
+                   layout.page_stride)
+        if layout.gate_up_codes_offset % 16 or any(o % 16 for o in offsets):
+            raise ValueError("expert page parts must start on 16-byte boundaries")
+        return layout
+
     def as_dict(self) -> dict[str, int]:
         return {name: int(getattr(self, name)) for name in self.__dataclass_fields__}
 
@@ -88,15 +100,38 @@ def pack_expert_page(layout: ExpertPageLayout, gate_up_codes, gate_up_scales, do
     put(ly.down_scales_offset, down_scales)
 
 
-def expert_page_views(layout: ExpertPageLayout, page: torch.Tensor):
-    """(gate_up codes, gate_up scales, down codes, down scales) views of one page."""
+@dataclass(frozen=True)
+class DeviceExpertLayer:
+    """Typed views of a block of expert pages (engine/qwen3_moe_cuda.py:765-769): for ``G``
+    pages, gate_up int8 [G, 2F, H], gate_up_scales fp32 [G, 2F], down int8 [G, H, F],
+    down_scales fp32 [G, H]. The codes are int8 here (the reference's fp8 codec stores
+    float8_e4m3fn at the same offsets)."""
+
+    gate_up: torch.Tensor
+    gate_up_scales: torch.Tensor
+    down: torch.Tensor
+    down_scales: torch.Tensor
+
+
+def expert_page_views(raw: torch.Tensor, layout: ExpertPageLayout) -> DeviceExpertLayer:
+    """Views (no copies) of every part of the pages in ``raw`` (uint8 ``[groups,
+    page_stride]``; one page ``[page_stride]`` counts as one group), with the reference's
+    argument order and result type (engine/qwen3_moe_cuda.py:1819-1853)."""
     ly = layout
-    f, h = ly.intermediate_size, ly.hidden_size
-    gu = page[ly.gate_up_codes_offset : ly.gate_up_codes_offset + ly.gate_up_codes_bytes].view(torch.int8)
-    gus = page[ly.gate_up_scales_offset : ly.gate_up_scales_offset + ly.gate_up_scales_bytes].view(torch.float32)
-    dn = page[ly.down_codes_offset : ly.down_codes_offset + ly.down_codes_bytes].view(torch.int8)
-    dns = page[ly.down_scales_offset : ly.down_scales_offset + ly.down_scales_bytes].view(torch.float32)
-    return gu.view(2 * f, h), gus, dn.view(h, f), dns
+    block = raw.unsqueeze(0) if raw.dim() == 1 else raw
+    if block.dim() != 2 or int(block.shape[1]) < ly.page_stride or block.dtype != torch.uint8:
+        raise ValueError("expert pages must be uint8 [groups, page_stride]")
+    groups, f, h = int(block.shape[0]), ly.intermediate_size, ly.hidden_size
+
+    def part(offset: int, nbytes: int, dtype: torch.dtype, *shape: int) -> torch.Tensor:
+        return block[:, offset: offset + nbytes].view(dtype).reshape(groups, *shape)
+
+    return DeviceExpertLayer(
+        gate_up=part(ly.gate_up_codes_offset, ly.gate_up_codes_bytes, torch.int8, 2 * f, h),
+        gate_up_scales=part(ly.gate_up_scales_offset, ly.gate_up_scales_bytes, torch.float32, 2 * f),
+        down=part(ly.down_codes_offset, ly.down_codes_bytes, torch.int8, h, f),
+        down_scales=part(ly.down_scales_offset, ly.down_scales_bytes, torch.float32, h),
+    )
 
 
 # ------------------------------------------------------------------ router
@@ -311,6 +346,7 @@ class PagedInt8ExpertBackend:
 
 
 __all__ = [
+    "DeviceExpertLayer",
     "ExpertPageLayout",
     "PagedInt8ExpertBackend",
     "ResidentInt8ExpertPages",

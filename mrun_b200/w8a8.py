@@ -11,6 +11,7 @@ from __future__ import annotations
 import types
 from typing import Any
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -142,13 +143,37 @@ def w8a8_linear_bf16(
 _ORIG_MATMUL: dict[int, Any] = {}
 
 
+def _raw_qrow(store: Any, name: str) -> tuple[torch.Tensor, torch.Tensor]:
+    """(int8 codes [out, in], fp32 row scales [out]) of a qrow block, never dequantised
+    (engine/kernels/w8a8.py:130-143). Reads through what the store offers: the device page of
+    a B200 ``QStore`` / ``DenseQStore`` (``page``), a ``compact_page`` of another dense store,
+    or the reference QStore's memory-mapped ``w`` / ``s`` files (then moved to the store's
+    device)."""
+    reader = getattr(store, "page", None) or getattr(store, "compact_page", None)
+    if callable(reader):
+        page = reader(name)
+        return page.codes, page.scales
+    block = store._resolve(name)
+    rows, cols = (int(v) for v in block["shape"])
+    w0, s0 = int(block["w_off"]), int(block["s_off"]) // 4
+    codes = torch.from_numpy(np.array(store.w[w0:w0 + rows * cols], dtype=np.int8).reshape(rows, cols))
+    scales = torch.from_numpy(np.array(store.s[s0:s0 + rows], dtype=np.float32))
+    device = getattr(store, "device", "cpu")
+    if str(device) != "cpu":
+        codes, scales = codes.to(device), scales.to(device)
+    return codes, scales
+
+
 def _w8a8_matmul_method(self: Any, name: str, x: torch.Tensor) -> torch.Tensor:
     b = self._resolve(name)
     if b.get("kind") != "qrow":
         return _ORIG_MATMUL[id(self)](name, x)
     cfg = self._w8a8
-    page = self.compact_page(name)
-    return w8a8_matmul(page.codes, page.scales, x, protect_idx=cfg["lists"].get(name), protect_k=cfg["k"])
+    codes, scales = _raw_qrow(self, name)
+    if codes.device != x.device:  # a host-resident store feeding device activations
+        codes, scales = codes.to(x.device), scales.to(x.device)
+    return w8a8_matmul(codes, scales, x, protect_idx=cfg["lists"].get(name), protect_k=cfg["k"],
+                       use_int_mm=cfg["use_int_mm"])
 
 
 def enable_w8a8(

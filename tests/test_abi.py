@@ -14,7 +14,7 @@ def _declared() -> list[str]:
     names = []
     for header in sorted((REPO / "include").glob("*.h")):
         text = header.read_text()
-        names += re.findall(r"^\s*(?:const\s+)?(?:int|void|size_t|char)\s*\*?\s*(mrb_\w+)\s*\(", text, re.M)
+        names += re.findall(r"^\s*(?:const\s+)?(?:int64_t|int|void|size_t|char)\s*\*?\s*(mrb_\w+)\s*\(", text, re.M)
     return names
 
 

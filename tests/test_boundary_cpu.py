@@ -1,0 +1,88 @@
+"""Host-side pieces of the drop-in boundary that need no GPU: expert page views with the
+reference's signature, the W8A8 raw-code reader on a reference-style store, and backend
+dispatch of ``open_engine``."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+
+def test_expert_page_views_reference_signature():
+    from mrun_b200.moe import DeviceExpertLayer, ExpertPageLayout, expert_page_views, pack_expert_page
+
+    ly = ExpertPageLayout.create(64, 48)
+    rng = np.random.default_rng(3)
+    raw = torch.zeros(3, ly.page_stride, dtype=torch.uint8)
+    parts = []
+    for g in range(3):
+        gu = torch.from_numpy(rng.integers(-127, 128, (96, 64), dtype=np.int8))
+        gus = torch.from_numpy(rng.random(96).astype(np.float32))
+        dn = torch.from_numpy(rng.integers(-127, 128, (64, 48), dtype=np.int8))
+        dns = torch.from_numpy(rng.random(64).astype(np.float32))
+        pack_expert_page(ly, gu, gus, dn, dns, raw[g])
+        parts.append((gu, gus, dn, dns))
+    views = expert_page_views(raw, ly)
+    assert isinstance(views, DeviceExpertLayer)
+    assert views.gate_up.shape == (3, 96, 64) and views.down.shape == (3, 64, 48)
+    assert views.gate_up_scales.shape == (3, 96) and views.down_scales.shape == (3, 64)
+    for g, (gu, gus, dn, dns) in enumerate(parts):
+        assert torch.equal(views.gate_up[g], gu) and torch.equal(views.gate_up_scales[g], gus)
+        assert torch.equal(views.down[g], dn) and torch.equal(views.down_scales[g], dns)
+    assert views.gate_up.data_ptr() == raw.data_ptr()  # views, not copies
+    one = expert_page_views(raw[1], ly)
+    assert one.gate_up.shape == (1, 96, 64) and torch.equal(one.down[0], parts[1][2])
+    with pytest.raises(ValueError):
+        expert_page_views(raw.view(torch.int8), ly)
+
+
+def test_expert_layout_round_trip_and_alignment():
+    from mrun_b200.moe import ExpertPageLayout
+
+    ly = ExpertPageLayout.create(2048, 768)
+    assert ExpertPageLayout.from_dict(ly.as_dict()) == ly
+    bad = dict(ly.as_dict(), down_codes_offset=ly.down_codes_offset + 4)
+    with pytest.raises(ValueError, match="16-byte"):
+        ExpertPageLayout.from_dict(bad)
+
+
+def test_raw_qrow_reads_reference_style_store():
+    """A store exposing the reference's memory-mapped ``w`` / ``s`` arrays and ``_resolve``
+    (no ``page`` method) is read without dequantisation."""
+    from mrun_b200.w8a8 import _raw_qrow
+
+    rng = np.random.default_rng(4)
+    codes = rng.integers(-127, 128, (6, 32), dtype=np.int8)
+    scales = rng.random(6).astype(np.float32)
+
+    class MemmapStore:
+        device = "cpu"
+        w = np.concatenate([np.zeros(64, np.int8), codes.reshape(-1)])
+        s = np.concatenate([np.zeros(3, np.float32), scales])
+
+        def _resolve(self, name):
+            assert name == "blk"
+            return {"kind": "qrow", "shape": [6, 32], "w_off": 64, "s_off": 12}
+
+    q, sc = _raw_qrow(MemmapStore(), "blk")
+    assert q.dtype == torch.int8 and torch.equal(q, torch.from_numpy(codes))
+    assert torch.equal(sc, torch.from_numpy(scales))
+
+
+def test_open_engine_rejects_other_backends(tmp_path):
+    from mrun_b200.engine import DENSE_BACKENDS, open_engine
+
+    assert "dense-qstore-cuda" in DENSE_BACKENDS
+    with pytest.raises(ValueError, match="not served"):
+        open_engine("m", backend="paged", stores_dir=tmp_path)
+    with pytest.raises(ValueError, match="stores_dir or store_path"):
+        open_engine("m", backend="dense-cuda", fresh=True)
+
+
+def test_ep_wait_limit_is_validated_on_the_host():
+    from mrun_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.mrb_ep_set_wait_limit(0) == _lib.MRB_ERR_ARG
+    assert lib.mrb_ep_set_wait_limit(1 << 31) == _lib.MRB_ERR_ARG
+    assert int(lib.mrb_ep_wait_limit()) == 1 << 22
