@@ -1,15 +1,22 @@
-"""Benchmark: greedy decode tokens/s of the Qwen2.5-7B-shape int8 QStore decoder (BASELINE
-config 2) and its int8-weight HBM bandwidth, on N GPUs (independent replicas).
+"""Benchmark of the quantized decode hot path on N B200s (one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--case ...]
 
-A step is one greedy decode token (batch 1, after a 512-token prompt), i.e. one pass of the
-hot path over all 28 layers and the head. `value` is device-timed (CUDA events around K
-CUDA-graph replays, inputs resident in HBM); `e2e` is the same loop through the public
-per-token path with the token id copied host->device and the chosen id device->host every
-step. The reference arm (`--impl reference`) times the reference's CPU decode path
-(restated in oracle/: fp32 dequantise-then-matmul, engine/kernels/paged_forward.py) on the
-host cores. Prints exactly one JSON line on rank 0.
+Default line: greedy decode of the Qwen3-30B-A3B-shape routed-MoE decoder (48 layers, hidden
+2048, 32/4 heads, 128 int8 experts top-8, expert FFN 768, vocab 151936), 32 ragged rows per
+GPU with committed contexts U[256, 4096], expert-parallel over the N GPUs (experts sharded,
+rows exchanged over NVLink peer memory). A step is one greedy token for every row on every
+GPU (weak scaling); ``value`` is the job's tokens/s from CUDA events around K CUDA-graph
+replays (inputs resident in HBM, max over ranks); ``e2e`` is the same loop with the rows'
+token ids copied in from pinned host memory and the chosen ids copied back every step. The
+line also carries the dominant kernel's roofline (grouped int8 expert SwiGLU launch), a
+bit-identity check of one expert-parallel layer against one GPU holding every expert, the
+CPU baseline (rank 0, N = 1) and the clocks seen while timing.
+
+``--impl reference`` times the reference's CPU decode of the same step (restated in
+oracle/cpu_moe_path.py: fp32 dense projections, int8 expert pages dequantised per use) on the
+host cores. ``--case decode`` is the dense Qwen2.5-7B-shape batch-1 decode line; the other
+cases are single-kernel or single-configuration measurements, one JSON line each.
 """
 from __future__ import annotations
 
@@ -21,6 +28,8 @@ import subprocess
 import sys
 import time
 from pathlib import Path
+
+import numpy as np
 
 REPO = Path(__file__).resolve().parent
 if str(REPO) not in sys.path:
@@ -490,6 +499,362 @@ def run_moe_case(args) -> None:
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+MOE_WORKLOAD = ("config4: Qwen3-30B-A3B-shape routed-MoE decoder (48 layers, hidden 2048, 32/4 heads, 128 int8 "
+                "experts top-8, expert FFN 768, vocab 151936), 32 ragged rows per GPU, contexts U[256,4096], "
+                "greedy decode, experts sharded over the GPUs")
+MOE_SEED = 0
+
+
+def _moe_config(world: int, exchange: str) -> dict:
+    """The ``config`` object of the default line (identical in both arms)."""
+    return {
+        "workload": MOE_WORKLOAD,
+        "rows_per_gpu": MOE_ROWS,
+        "global_batch": MOE_ROWS * world,
+        "contexts": "U[256,4096] per row (numpy default_rng(rank)), 16-token KV pages",
+        "parallelism": f"ep{world}" if world > 1 else "ep1 (single GPU, all experts resident)",
+        "exchange": None if world == 1 else ("NVLink peer memory (fixed-capacity plan, real rows only)"
+                                             if exchange == "p2p" else "NCCL all-to-all (fixed capacity)"),
+        "l2": "no flush: each GPU streams >= 10 GB of KV and weights per step, far above the 126 MB L2",
+    }
+
+
+def _graph_kernel_census(graph) -> dict[str, int]:
+    """Kernel nodes of a captured (keep_graph) torch CUDA graph, counted by the shared library
+    that holds each kernel's host launch stub (dladdr)."""
+    import ctypes
+
+    from cuda.bindings import runtime as rt
+
+    class DlInfo(ctypes.Structure):
+        _fields_ = [("dli_fname", ctypes.c_char_p), ("dli_fbase", ctypes.c_void_p),
+                    ("dli_sname", ctypes.c_char_p), ("dli_saddr", ctypes.c_void_p)]
+
+    libc = ctypes.CDLL(None)
+    libc.dladdr.argtypes = [ctypes.c_void_p, ctypes.POINTER(DlInfo)]
+    raw = graph.raw_cuda_graph()
+    handle = raw if not isinstance(raw, int) else rt.cudaGraph_t(init_value=raw)
+    err, _, count = rt.cudaGraphGetNodes(handle, 0)
+    err, nodes, count = rt.cudaGraphGetNodes(handle, count)
+    census: dict[str, int] = {}
+    for node in nodes[:count]:
+        err, kind = rt.cudaGraphNodeGetType(node)
+        if kind != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+            continue
+        err, params = rt.cudaGraphKernelNodeGetParams(node)
+        func = params.func
+        address = int(func) if not hasattr(func, "getPtr") else int(func.getPtr())
+        info = DlInfo()
+        lib = "unknown"
+        if address and libc.dladdr(ctypes.c_void_p(address), ctypes.byref(info)) and info.dli_fname:
+            lib = os.path.basename(info.dli_fname.decode())
+        census[lib] = census.get(lib, 0) + 1
+    return census
+
+
+def _time_grouped_swiglu(weights, top_indices_all, rank: int, world: int, device) -> dict:
+    """Roofline of the dominant kernel: the grouped int8 expert gate/up + SwiGLU launch
+    (grouped_qrow_kernel) on the rows this rank's experts receive in one layer (the routes of
+    every rank's rows), timed alone in a CUDA graph that cycles through all 48 layers' pages
+    (so every launch streams its experts from HBM)."""
+    import torch
+
+    from mrun_b200 import _lib
+    from mrun_b200.moe import grouped_route_tensors_with_inverse
+
+    cfg, ly = weights.cfg, weights.layout
+    per = weights.experts_local
+    flat = top_indices_all.reshape(-1)
+    local = flat[(flat >= weights.expert_first) & (flat < weights.expert_first + per)] - weights.expert_first
+    rows = int(local.numel())
+    token_ids, _, starts, counts, _, _ = grouped_route_tensors_with_inverse(
+        local.view(-1, 1), torch.zeros((rows, 1), device=device), num_experts=per)
+    active = int((counts > 0).sum().item())
+    gen = torch.Generator(device=device).manual_seed(11 + rank)
+    x = torch.randn(rows, cfg.hidden, device=device, generator=gen).to(torch.bfloat16)
+    act = torch.empty(rows, cfg.expert_ffn, dtype=torch.bfloat16, device=device)
+    stream = _lib.stream_handle(device)
+    f, h, stride = cfg.expert_ffn, cfg.hidden, ly.page_stride
+
+    def launch(i):
+        base = weights.layers[i % len(weights.layers)].pages.data_ptr()
+        _lib.call("mrb_grouped_qrow", x.data_ptr(), token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), per,
+                  base + ly.gate_up_codes_offset, stride, base + ly.gate_up_scales_offset, stride // 4, None, f, h,
+                  f, 1, rows, act.data_ptr(), _lib.stream_handle(device))
+
+    del stream
+    iters = 2 * len(weights.layers)
+    avg_s = _graph_avg_seconds(launch, iters, len(weights.layers), device)
+    nbytes = active * (2 * f * h + 2 * f * 4) + rows * h * 2 + rows * f * 2
+    return {"avg_s": avg_s, "bytes": nbytes, "experts": active, "rows": rows}
+
+
+def _grouped_traffic_per_expert() -> float | None:
+    """DRAM bytes per expert page of the gate/up launch, from the committed ncu summary."""
+    path = REPO / "profiles" / "grouped_qrow_config4_ep1.md"
+    if not path.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_expert:\s*([0-9.eE+]+)", path.read_text())
+    return float(m.group(1)) if m else None
+
+
+def _cpu_moe_decoder(threads: int, lengths: list[int]):
+    import torch
+
+    from oracle.cpu_moe_path import CpuMoePathDecoder
+
+    torch.set_num_threads(threads)
+    dec = CpuMoePathDecoder.qwen3_30b_a3b(seed=MOE_SEED)
+    dec.set_context(lengths)
+    return dec
+
+
+def _cpu_moe_units(dec, units, x):
+    """Seconds to run the given units (layers, or the head) of one step for every row."""
+    t0 = time.perf_counter()
+    for u in units:
+        y = dec.run_unit(u, x)
+        if u < dec.L:
+            x = y
+    return time.perf_counter() - t0, x
+
+
+def _cpu_moe_sample(threads: int, lengths: list[int], budget_s: float = 20.0) -> dict:
+    """The reference's CPU MoE decode on the host cores: layers (and the head) of one 32-row
+    step run in turn until ``budget_s`` is spent; the step time is the mean layer time x 48
+    plus the head's time."""
+    import torch
+
+    dec = _cpu_moe_decoder(threads, lengths)
+    x = dec.embed_rows(torch.from_numpy(np.random.default_rng(0).integers(0, dec.v, len(lengths))))
+    _cpu_moe_units(dec, [0], x)  # warm-up: thread pool and allocator
+    head_s, _ = _cpu_moe_units(dec, [dec.L], x)
+    layer_times = []
+    end = time.perf_counter() + budget_s
+    li = 0
+    while not layer_times or (time.perf_counter() < end and li < dec.L):
+        dt, x = _cpu_moe_units(dec, [li], x)
+        layer_times.append(dt)
+        li += 1
+    step_s = float(np.mean(layer_times)) * dec.L + head_s
+    return {"value": len(lengths) / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{len(layer_times)} of 48 layers and the head of one {len(lengths)}-row decode step "
+                      f"(fp32 dense projections, int8 expert pages dequantised per use); step time = mean layer "
+                      f"time x 48 + head = {step_s:.2f} s"}
+
+
+def run_moe_bench(args) -> None:
+    """The default line: config-4 MoE decode, expert-parallel over N GPUs (see the module doc)."""
+    import torch
+
+    from mrun_b200.expert_parallel import ExpertShard
+    from mrun_b200.moe import PagedInt8ExpertBackend, ResidentInt8ExpertPages
+    from mrun_b200.moe_engine import MoeConfig, MoeDecoder, MoeWeights
+
+    world, rank, local = _dist_setup(args.gpus)
+    device = torch.device("cuda", local)
+    cfg = MoeConfig.qwen3_30b_a3b()
+    shard = ExpertShard(world, rank, cfg.experts) if world > 1 else None
+    weights = MoeWeights.synthetic(cfg, device, seed=MOE_SEED, shard=shard)
+    rng = np.random.default_rng(rank)
+    lengths = [int(v) for v in rng.integers(256, 4097, MOE_ROWS)]
+    first = torch.from_numpy(rng.integers(0, cfg.vocab, MOE_ROWS))
+    total = 2 * (args.warmup + args.steps) + 8
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        group = dist.group.WORLD
+    dec = MoeDecoder(weights, max_rows=MOE_ROWS, max_seq_len=4096 + total + 16, device=device, group=group,
+                     world=world, exchange=args.exchange)
+    dec.load_synthetic_context(lengths, first, steps=total, seed=rank)
+    dec.capture(MOE_ROWS)
+    try:
+        census = _graph_kernel_census(dec.graph)
+    except Exception as exc:  # noqa: BLE001 - the census is evidence, not the measurement
+        census = {"error": repr(exc)[:200]}
+    stream = torch.cuda.current_stream(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    pin_in = torch.empty(MOE_ROWS, dtype=torch.int64, pin_memory=True)
+    pin_out = torch.empty(MOE_ROWS, dtype=torch.int64, pin_memory=True)
+
+    def e2e_step():
+        dec.in_ids[:MOE_ROWS].copy_(pin_in, non_blocking=True)
+        dec.step(MOE_ROWS)
+        pin_out.copy_(dec.next_ids[:MOE_ROWS], non_blocking=True)
+        stream.synchronize()
+        pin_in.copy_(pin_out)
+
+    with ClockSampler(local) as clocks:
+        for _ in range(args.warmup):
+            dec.step(MOE_ROWS)
+        _barrier(world)
+        torch.cuda.synchronize(device)
+        torch.cuda.cudart().cudaProfilerStart()
+        e0.record(stream)
+        for _ in range(args.steps):
+            dec.step(MOE_ROWS)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        torch.cuda.cudart().cudaProfilerStop()
+        _barrier(world)
+        step_s = _max_over_ranks(e0.elapsed_time(e1) / 1000.0 / args.steps, world)
+        # end to end through the public step with host buffers, same number of steps
+        pin_in.copy_(dec.next_ids[:MOE_ROWS].cpu())
+        for _ in range(min(args.warmup, 3)):
+            e2e_step()
+        _barrier(world)
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        e2e_s = _max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+    dec.check_errors()
+
+    # one layer of the expert-parallel step against one GPU holding every expert
+    probe = {"layer": 0}
+    dec.probe = probe
+    dec.step_eager(MOE_ROWS)
+    dec.probe = None
+    torch.cuda.synchronize(device)
+    dec.check_errors()
+    full = MoeWeights.synthetic_full_layer_pages(cfg, device, 0, seed=MOE_SEED)
+    single = PagedInt8ExpertBackend(ResidentInt8ExpertPages(weights.layout, [full]), num_experts=cfg.experts)
+    expect = single.moe(0, probe["source"], probe["top_indices"], probe["top_weights"])
+    identical = torch.equal(expect, probe["output"])
+    del full, single
+    flag = torch.tensor([1 if identical else 0], dtype=torch.int32, device=device)
+    routes = probe["top_indices"].contiguous()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        gathered = torch.empty((world,) + tuple(routes.shape), dtype=routes.dtype, device=device)
+        dist.all_gather_into_tensor(gathered, routes)
+        routes = gathered
+    roof = _time_grouped_swiglu(weights, routes, rank, world, device)
+    roof_s = _max_over_ranks(roof["avg_s"], world)
+    dec.close()  # the graph (NCCL calls) and the peer mailboxes go before the process group
+    torch.cuda.synchronize(device)
+
+    line = None
+    if rank == 0:
+        peaks = _peaks()
+        per = weights.experts_local
+        distinct = per * (1.0 - (1.0 - cfg.top_k / cfg.experts) ** (MOE_ROWS * world))
+        expert_bytes = distinct * weights.layout.page_stride * cfg.num_layers
+        kv_bytes = sum(lengths) * 2 * cfg.num_layers * cfg.kv_heads * cfg.head_dim * 2
+        h = cfg.hidden
+        dense = cfg.num_layers * ((cfg.qkv_rows + h + cfg.experts) * h + h * cfg.heads * cfg.head_dim) + cfg.vocab * h
+        step_bytes = expert_bytes + kv_bytes + dense
+        achieved = roof["bytes"] / roof_s / 1e9
+        per_expert = _grouped_traffic_per_expert()
+        mine = census.get("libmrun_b200.so") if isinstance(census, dict) else None
+        line = {
+            "metric": METRIC,
+            "value": MOE_ROWS * world / step_s,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": step_s * 1000.0,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "weights": "int8 per-channel (QStore qrow codes, expert pages)",
+            "data": "synthetic: random-init int8 weights (seeded), random token ids, random bf16 K/V contexts",
+            "config": _moe_config(world, args.exchange),
+            "ep_bit_identical": bool(int(flag.item())),
+            "ep_check": "layer 0 MoE output of every rank's rows (expert-parallel, eager) == one GPU holding all "
+                        "128 experts on the same inputs, bitwise; min over ranks",
+            "hbm_bytes_per_step_per_gpu": {"experts": expert_bytes / 1.0, "kv": kv_bytes, "dense_and_head": dense},
+            "step_hbm_gbs_per_gpu": step_bytes / step_s / 1e9,
+            "step_frac_of_measured_hbm": step_bytes / step_s / 1e9 / peaks["hbm_gbs"],
+            "roofline": {
+                "kernel": "grouped_qrow_kernel<SWIGLU> (int8 expert gate/up + SwiGLU, one layer's routed rows)",
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peaks["hbm_gbs"],
+                "peak_source": f"{peaks['source']} hbm_gbs (burst copy; the kernel is timed alone)",
+                "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"],
+                "traffic": None if per_expert is None else per_expert * roof["experts"],
+                "bytes_per_launch": roof["bytes"],
+                "experts_per_launch": roof["experts"],
+                "rows_per_launch": roof["rows"],
+                "avg_launch_us": roof_s * 1e6,
+            },
+            "e2e": {"value": MOE_ROWS * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": MOE_ROWS * 8,
+                    "d2h_bytes_per_step": MOE_ROWS * 8},
+            "gpu_launches": None if mine is None else mine * args.steps,
+            "graph_kernel_nodes": census,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = _cpu_moe_sample(os.cpu_count() or 1, lengths)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def run_reference_moe(args) -> None:
+    """The reference arm of the default line: the CPU MoE decode step (oracle/cpu_moe_path.py)
+    on the host cores, rank 0 only. Each bench step runs a few whole units (layers, or the head)
+    of the 32-row step, rotating through all 49, so ``ms_per_step`` is the time a step took;
+    the token rate uses the mean layer time x 48 plus the head's time."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    threads = os.cpu_count() or 1
+    lengths = [int(v) for v in np.random.default_rng(0).integers(256, 4097, MOE_ROWS)]
+    dec = _cpu_moe_decoder(threads, lengths)
+    x = dec.embed_rows(torch.from_numpy(np.random.default_rng(0).integers(0, dec.v, MOE_ROWS)))
+    first_s, _ = _cpu_moe_units(dec, [0], x)
+    # about 2 s per step, less when many steps are asked for (the arm stays within ~2 minutes)
+    target = min(2.0, 120.0 / (args.warmup + args.steps))
+    per_step = int(min(dec.units(), max(1, round(target / max(first_s, 1e-3)))))
+    cursor = 0
+    step_times, layer_times, head_times = [], [], []
+    for i in range(args.warmup + args.steps):
+        units = [(cursor + j) % dec.units() for j in range(per_step)]
+        cursor = (cursor + per_step) % dec.units()
+        t_step = 0.0
+        for u in units:
+            dt, y = _cpu_moe_units(dec, [u], x)
+            t_step += dt
+            if i >= args.warmup:
+                (head_times if u == dec.L else layer_times).append(dt)
+        if i >= args.warmup:
+            step_times.append(t_step)
+    if not head_times:
+        head_times.append(_cpu_moe_units(dec, [dec.L], x)[0])
+    token_step_s = float(np.mean(layer_times)) * dec.L + float(np.mean(head_times))
+    value = MOE_ROWS / token_step_s  # one host, one 32-row batch: the reference has no multi-GPU path
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(np.mean(step_times)) * 1000.0,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic: random int8 expert pages and fp32 dense weights (seeded), random contexts",
+        "config": _moe_config(world, args.exchange),
+        "cpu_baseline": {
+            "value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"each bench step runs {per_step} whole unit(s) of the 49 (48 layers + head) of one "
+                      f"{MOE_ROWS}-row decode step, rotating; ms_per_step is that step's measured time; tokens/s = "
+                      f"{MOE_ROWS} / (mean layer time x 48 + head time); one host runs one {MOE_ROWS}-row batch "
+                      f"at every N (rank 0 only)",
+        },
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
 
 
 def run_stream_case(args) -> None:
@@ -1054,37 +1419,36 @@ def main() -> None:
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="moe-decode on N GPUs: expert exchange over NVLink peer memory or NCCL all-to-all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", choices=["decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
-                                       *TC_CASES, *ATTN_CASES, "attn-fused1", "attn-prefill512", "qstore-ingest", *EXPERT_CASES],
-                    default="decode",
-                    help="gemv-*: a small single-kernel case for profiler captures (not the metric)")
+    ap.add_argument("--case", choices=["moe", "decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
+                                       *TC_CASES, *ATTN_CASES, "attn-fused1", "attn-prefill512", "qstore-ingest",
+                                       *EXPERT_CASES],
+                    default="moe",
+                    help="moe (default): the config-4 expert-parallel decode line; decode: the dense batch-1 line; "
+                         "the rest are single-kernel or single-configuration cases (not the metric)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.impl == "reference":
+        if args.case == "moe":
+            run_reference_moe(args)
+        elif args.case == "decode":
+            run_reference(args)
+        else:
+            raise SystemExit("--impl reference applies to the moe and decode lines")
+        return
+    cases = {"attn-fused1": run_fused_attn_case, "attn-prefill512": run_prefill_attn_case,
+             "qstore-ingest": run_qstore_ingest_case, "moe-decode": run_moe_case, "stream-decode": run_stream_case,
+             "w8a8-batch": run_batch_case, "moe": run_moe_bench, "decode": run_ours}
     if args.case in GEMV_CASES:
         run_gemv_case(args)
     elif args.case in ATTN_CASES:
         run_attn_case(args)
-    elif args.case == "attn-fused1":
-        run_fused_attn_case(args)
-    elif args.case == "attn-prefill512":
-        run_prefill_attn_case(args)
-    elif args.case == "qstore-ingest":
-        run_qstore_ingest_case(args)
     elif args.case in EXPERT_CASES:
         run_expert_case(args)
     elif args.case in TC_CASES:
         run_tc_case(args)
-    elif args.case == "moe-decode":
-        run_moe_case(args)
-    elif args.case == "stream-decode":
-        run_stream_case(args)
-    elif args.case == "w8a8-batch":
-        run_batch_case(args)
-    elif args.impl == "reference":
-        run_reference(args)
     else:
-        run_ours(args)
+        cases[args.case](args)
 
 
 if __name__ == "__main__":

@@ -111,7 +111,8 @@ class DenseWeights:
     def from_blocks(cfg: DenseConfig, qrow, fp32, has) -> "DenseWeights":
         """Assemble the decoder's weights from QStore blocks under the reference's canonical
         names (engine/kernels/qstore_build.py:257-276, 340-360): ``L{i}.q/k/v/o/gate/up/down``
-        (qrow), ``L{i}.q.bias/k.bias/v.bias``, ``L{i}.ln1/ln2``, ``norm`` (fp32), ``embed``,
+        (qrow), ``L{i}.q.bias/k.bias/v.bias``, ``L{i}.ln1/ln2``, ``norm.final`` (fp32; ``norm`` is
+        accepted too), ``embed``,
         ``lm_head`` (qrow, often an alias of ``embed``). ``qrow(name)`` returns (int8 codes,
         fp32 scales) and ``fp32(name)`` a float32 tensor, both on the target device; ``has``
         tells whether a block exists. q, k and v are stacked into one [(Hq + 2 Hkv) D, H] page."""
@@ -133,7 +134,8 @@ class DenseWeights:
         head = QRow(*qrow("lm_head" if has("lm_head") else "embed"))
         if embed.codes.shape != (cfg.vocab, cfg.hidden) or head.codes.shape[1] != cfg.hidden:
             raise ValueError("embedding / head blocks do not match the config")
-        return DenseWeights(cfg=cfg, embed=embed, layers=layers, final_norm=fp32("norm").reshape(-1).contiguous(),
+        final = "norm.final" if has("norm.final") else "norm"
+        return DenseWeights(cfg=cfg, embed=embed, layers=layers, final_norm=fp32(final).reshape(-1).contiguous(),
                             head=head)
 
     @staticmethod
@@ -434,9 +436,10 @@ class DenseDecoder:
         self.in_ids.copy_(saved[0])
         self.positions.copy_(saved[1])
         self.row_len.copy_(saved[2])
-        graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph(keep_graph=True)  # kept so tools can list its kernel nodes
         with torch.cuda.graph(graph, stream=stream):
             self._decode_body(rows)
+        graph.instantiate()
         self.graph = graph
         self.graph_rows = rows
         # kernels: embed, final norm, 8 per layer (7 with the fused RoPE/append/attention; W8A8:

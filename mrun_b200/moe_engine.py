@@ -102,20 +102,37 @@ class MoeWeights:
         gen = torch.Generator(device=device).manual_seed(seed)
         layout = ExpertPageLayout.create(cfg.hidden, cfg.expert_ffn)
         first, local = (shard.first, shard.per_rank) if shard is not None else (0, cfg.experts)
-        h, d = cfg.hidden, cfg.head_dim
-        embed = _random_qrow(cfg.vocab, h, gen, device, std=1.0)
-        layers = []
-        for _ in range(cfg.num_layers):
-            qkv = _random_qrow(cfg.qkv_rows, h, gen, device)
-            o = _random_qrow(h, cfg.heads * d, gen, device)
-            router = _random_qrow(cfg.experts, h, gen, device, std=0.05)
-            q_norm, k_norm = _random_norm(d, gen, device), _random_norm(d, gen, device)
-            ln1, ln2 = _random_norm(h, gen, device).float(), _random_norm(h, gen, device).float()
-            pages = cls._expert_pages(cfg, layout, gen, device, first, local)
-            layers.append(MoeLayer(qkv, o, router, q_norm, k_norm, ln1, ln2, pages))
-        final_norm = _random_norm(h, gen, device).float()
-        head = _random_qrow(cfg.vocab, h, gen, device)
+        embed = _random_qrow(cfg.vocab, cfg.hidden, gen, device, std=1.0)
+        layers = [cls._draw_layer(cfg, layout, gen, device, first, local) for _ in range(cfg.num_layers)]
+        final_norm = _random_norm(cfg.hidden, gen, device).float()
+        head = _random_qrow(cfg.vocab, cfg.hidden, gen, device)
         return cls(cfg, layout, embed, layers, final_norm, head, first, local)
+
+    @classmethod
+    def _draw_layer(cls, cfg: MoeConfig, layout: ExpertPageLayout, gen: torch.Generator, device: torch.device,
+                    first: int, local: int) -> MoeLayer:
+        """One layer's random weights, drawn in a fixed order from ``gen``."""
+        h, d = cfg.hidden, cfg.head_dim
+        qkv = _random_qrow(cfg.qkv_rows, h, gen, device)
+        o = _random_qrow(h, cfg.heads * d, gen, device)
+        router = _random_qrow(cfg.experts, h, gen, device, std=0.05)
+        q_norm, k_norm = _random_norm(d, gen, device), _random_norm(d, gen, device)
+        ln1, ln2 = _random_norm(h, gen, device).float(), _random_norm(h, gen, device).float()
+        pages = cls._expert_pages(cfg, layout, gen, device, first, local)
+        return MoeLayer(qkv, o, router, q_norm, k_norm, ln1, ln2, pages)
+
+    @classmethod
+    def synthetic_full_layer_pages(cls, cfg: MoeConfig, device: torch.device, layer: int,
+                                   seed: int = 0) -> torch.Tensor:
+        """Every expert page ([experts, page_stride]) of one layer of ``synthetic(cfg, device,
+        seed)``, whatever shard a rank holds: the generator replays the draws up to that layer
+        (used to check an expert-parallel layer against one GPU holding all experts)."""
+        gen = torch.Generator(device=device).manual_seed(seed)
+        layout = ExpertPageLayout.create(cfg.hidden, cfg.expert_ffn)
+        _random_qrow(cfg.vocab, cfg.hidden, gen, device, std=1.0)
+        for _ in range(layer):
+            cls._draw_layer(cfg, layout, gen, device, 0, 0)
+        return cls._draw_layer(cfg, layout, gen, device, 0, cfg.experts).pages
 
     @staticmethod
     def _expert_pages(cfg: MoeConfig, layout: ExpertPageLayout, gen: torch.Generator, device: torch.device,
@@ -215,6 +232,9 @@ class MoeDecoder:
         self.graph_rows = 0
         self.max_context = 0
         self.routes: list[torch.Tensor] | None = None  # filled when record_routes is set
+        # set to {"layer": i} before an eager step to keep that layer's MoE input, routes and
+        # output (clones) in the dict
+        self.probe: dict | None = None
 
     # ------------------------------------------------------------------ context
 
@@ -270,6 +290,9 @@ class MoeDecoder:
                 moe_out = self.ep[i].forward(normed, top_idx, top_w)
             else:
                 moe_out = self.backend.moe(i, normed, top_idx, top_w)
+            if self.probe is not None and self.probe.get("layer") == i:
+                self.probe.update(source=normed.clone(), top_indices=top_idx.clone(), top_weights=top_w.clone(),
+                                  output=moe_out.clone())
             nxt = w.layers[i + 1].ln1 if i + 1 < len(w.layers) else w.final_norm
             residual_rms_norm_into(hidden, moe_out, nxt, cfg.eps, hidden, normed)
         qrow_argmax(w.head.codes, w.head.scales, normed, out_index=self.next_ids[:rows],
@@ -291,11 +314,18 @@ class MoeDecoder:
         self.in_ids.copy_(saved[0])
         self.positions.copy_(saved[1])
         self.row_len.copy_(saved[2])
-        graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph(keep_graph=True)  # kept so tools can list its kernel nodes
         with torch.cuda.graph(graph, stream=stream):
             self._decode_body(rows)
+        graph.instantiate()
         self.graph = graph
         self.graph_rows = rows
+
+    @torch.inference_mode()
+    def step_eager(self, rows: int) -> None:
+        """One greedy token without the captured graph (same kernels, launched one by one;
+        with expert parallelism every rank must call it too)."""
+        self._decode_body(rows)
 
     @torch.inference_mode()
     def step(self, rows: int) -> None:

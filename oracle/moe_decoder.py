@@ -48,12 +48,14 @@ def _expert_tensors(layout: dict, page: np.ndarray):
     return gu, gus, dn, dns
 
 
-def moe_decode_step(w: dict, cfg, ids, positions, context_k, context_v):
+def moe_decode_step(w: dict, cfg, ids, positions, context_k, context_v, *, new_kv: list | None = None):
     """One decode token per row.
 
     w: ``MoeWeights.to_host()``; ids [R]; positions [R] (= committed lengths);
     context_k[layer][row] / context_v: [positions[row], Hkv, D] float arrays.
-    Returns (fp32 logits [R, vocab], per-layer router indices [R, k])."""
+    Returns (fp32 logits [R, vocab], per-layer router indices [R, k]). With ``new_kv`` (a
+    list), the step's own K/V rows are appended to it per layer as (k [R, Hkv, D], v), so a
+    caller can grow the context and run several steps."""
     ids = np.asarray(ids, np.int64)
     pos = np.asarray(positions, np.int64)
     rows = ids.size
@@ -70,6 +72,8 @@ def moe_decode_step(w: dict, cfg, ids, positions, context_k, context_v):
         v = qkv[:, (hq + hkv) * d:].reshape(rows, hkv, d)
         q = rope(_rms(q, L["q_norm"], cfg.eps), cos, sin)
         k = rope(_rms(k, L["k_norm"], cfg.eps), cos, sin)
+        if new_kv is not None:
+            new_kv.append((k, v))
         keys = [np.concatenate([context_k[li][r], k[r:r + 1]], 0) for r in range(rows)]
         vals = [np.concatenate([context_v[li][r], v[r:r + 1]], 0) for r in range(rows)]
         ctx = bf16_round(gqa_decode_rows(q, keys, vals)).reshape(rows, hq * d)

@@ -86,3 +86,21 @@ def test_ep_wait_limit_is_validated_on_the_host():
     assert lib.mrb_ep_set_wait_limit(0) == _lib.MRB_ERR_ARG
     assert lib.mrb_ep_set_wait_limit(1 << 31) == _lib.MRB_ERR_ARG
     assert int(lib.mrb_ep_wait_limit()) == 1 << 22
+
+
+def test_full_layer_pages_replay_every_shard():
+    """The expert-parallel check rebuilds one layer's full expert set on any rank: it equals
+    the unsharded model's pages and contains each rank's shard."""
+    from mrun_b200.expert_parallel import ExpertShard
+    from mrun_b200.moe_engine import MoeConfig, MoeWeights
+
+    cfg = MoeConfig(num_layers=3, hidden=256, heads=4, kv_heads=2, head_dim=64, experts=8, top_k=2, expert_ffn=128,
+                    vocab=300)
+    cpu = torch.device("cpu")
+    full = MoeWeights.synthetic(cfg, cpu, seed=3)
+    shards = [MoeWeights.synthetic(cfg, cpu, seed=3, shard=ExpertShard(4, r, 8)) for r in range(4)]
+    for layer in range(3):
+        pages = MoeWeights.synthetic_full_layer_pages(cfg, cpu, layer, seed=3)
+        assert torch.equal(pages, full.layers[layer].pages)
+        for r, sh in enumerate(shards):
+            assert torch.equal(pages[2 * r: 2 * r + 2], sh.layers[layer].pages)

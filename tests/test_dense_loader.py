@@ -17,7 +17,7 @@ def _write_store(path, cfg, rng, *, tied=True):
 
     h, hd = cfg["hidden_size"], cfg["head_dim"]
     qd, kd = cfg["num_attention_heads"] * hd, cfg["num_key_value_heads"] * hd
-    qrows, fp32 = {"embed": q(cfg["vocab_size"], h)}, {"norm": rng.random(h).astype(np.float32)}
+    qrows, fp32 = {"embed": q(cfg["vocab_size"], h)}, {"norm.final": rng.random(h).astype(np.float32)}
     for i in range(cfg["num_hidden_layers"]):
         for name, shape in (("q", (qd, h)), ("k", (kd, h)), ("v", (kd, h)), ("o", (h, qd)),
                             ("gate", (cfg["intermediate_size"], h)), ("up", (cfg["intermediate_size"], h)),
@@ -58,7 +58,7 @@ def test_dense_weights_from_store_blocks(tmp_path, tied):
         np.testing.assert_array_equal(layer.ln2.numpy(), oracle.fp32(f"L{i}.ln2"))
     np.testing.assert_array_equal(w.head.codes.numpy(), oracle.qrow("lm_head")[0])
     assert tied == np.array_equal(w.head.codes.numpy(), w.embed.codes.numpy())
-    np.testing.assert_array_equal(w.final_norm.numpy(), oracle.fp32("norm"))
+    np.testing.assert_array_equal(w.final_norm.numpy(), oracle.fp32("norm.final"))
     # a config that does not match the blocks is refused
     bad = DenseConfig(num_layers=2, hidden=64, heads=8, kv_heads=2, head_dim=16, ffn=96, vocab=50)
     with pytest.raises(ValueError, match="q/k/v blocks"):
