@@ -521,37 +521,40 @@ def _moe_config(world: int, exchange: str) -> dict:
     }
 
 
-def _graph_kernel_census(graph) -> dict[str, int]:
-    """Kernel nodes of a captured (keep_graph) torch CUDA graph, counted by the shared library
-    that holds each kernel's host launch stub (dladdr)."""
-    import ctypes
+def _graph_kernel_census(graph) -> dict:
+    """Kernel nodes of a captured (keep_graph) torch CUDA graph, named through the driver
+    (cuFuncGetName). Kernels of libmrun_b200 live in C++ namespace ``mrb`` (mangled
+    ``_ZN3mrb``); every other kernel node is counted as another library's."""
+    from cuda.bindings import driver as dr
 
-    from cuda.bindings import runtime as rt
-
-    class DlInfo(ctypes.Structure):
-        _fields_ = [("dli_fname", ctypes.c_char_p), ("dli_fbase", ctypes.c_void_p),
-                    ("dli_sname", ctypes.c_char_p), ("dli_saddr", ctypes.c_void_p)]
-
-    libc = ctypes.CDLL(None)
-    libc.dladdr.argtypes = [ctypes.c_void_p, ctypes.POINTER(DlInfo)]
     raw = graph.raw_cuda_graph()
-    handle = raw if not isinstance(raw, int) else rt.cudaGraph_t(init_value=raw)
-    err, _, count = rt.cudaGraphGetNodes(handle, 0)
-    err, nodes, count = rt.cudaGraphGetNodes(handle, count)
-    census: dict[str, int] = {}
+    handle = dr.CUgraph(init_value=raw) if isinstance(raw, int) else raw
+    err, _, count = dr.cuGraphGetNodes(handle, 0)
+    err, nodes, count = dr.cuGraphGetNodes(handle, count)
+    names: dict[str, int] = {}
+    mine = other = unnamed = 0
     for node in nodes[:count]:
-        err, kind = rt.cudaGraphNodeGetType(node)
-        if kind != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+        err, kind = dr.cuGraphNodeGetType(node)
+        if kind != dr.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
             continue
-        err, params = rt.cudaGraphKernelNodeGetParams(node)
-        func = params.func
-        address = int(func) if not hasattr(func, "getPtr") else int(func.getPtr())
-        info = DlInfo()
-        lib = "unknown"
-        if address and libc.dladdr(ctypes.c_void_p(address), ctypes.byref(info)) and info.dli_fname:
-            lib = os.path.basename(info.dli_fname.decode())
-        census[lib] = census.get(lib, 0) + 1
-    return census
+        err, params = dr.cuGraphKernelNodeGetParams(node)
+        name = None
+        if params is not None and params.func is not None:
+            err, raw_name = dr.cuFuncGetName(params.func)
+            if raw_name:
+                name = raw_name.decode() if isinstance(raw_name, bytes) else str(raw_name)
+        if name is None:
+            unnamed += 1
+            continue
+        if name.startswith("_ZN3mrb"):
+            mine += 1
+            short = name[7:]
+            digits = len(short) - len(short.lstrip("0123456789"))
+            base = short[digits:digits + int(short[:digits])] if digits else short
+            names[base] = names.get(base, 0) + 1
+        else:
+            other += 1
+    return {"libmrun_b200_kernels": mine, "other_kernels": other, "unnamed_kernels": unnamed, "by_kernel": names}
 
 
 def _time_grouped_swiglu(weights, top_indices_all, rank: int, world: int, device) -> dict:
@@ -752,7 +755,7 @@ def run_moe_bench(args) -> None:
         step_bytes = expert_bytes + kv_bytes + dense
         achieved = roof["bytes"] / roof_s / 1e9
         per_expert = _grouped_traffic_per_expert()
-        mine = census.get("libmrun_b200.so") if isinstance(census, dict) else None
+        mine = census.get("libmrun_b200_kernels") if isinstance(census, dict) else None
         line = {
             "metric": METRIC,
             "value": MOE_ROWS * world / step_s,

@@ -101,7 +101,7 @@ def test_enable_w8a8_on_repo_stores(kind, tmp_path, cuda):
         enable_w8a8(store, protect_k=0)
         y = store.matmul(name, x.to(cuda))
         codes, scales = oracle.qrow(name)
-        want = ow.w8a8_matmul(x.numpy(), codes, scales)
+        want = ow.w8a8_matmul(codes, scales, x.numpy())
         np.testing.assert_array_equal(y.cpu().numpy(), want)
         disable_w8a8(store)
         again = store.matmul(name, x.to(cuda).to(torch.bfloat16))
