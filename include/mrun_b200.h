@@ -185,6 +185,20 @@ int mrb_w8a8_linear_bf16(const void *x_bf16, int64_t m, int64_t k, const int8_t 
 int mrb_router_topk(const void *logits, int logits_dtype, int64_t tokens, int64_t experts, int64_t k,
                     int renorm, int64_t *top_idx, float *top_w_f32, void *top_w_bf16, void *stream);
 
+/* The whole router of one MoE layer: logits[t, e] = bf16(scale[e] * sum_k x[t, k] * code[e, k])
+ * (bf16 activations [tokens, hidden], int8 router codes [experts, hidden] with fp32 row
+ * scales: the W8A16 projection's boundary, exact products, fp32 sums in a fixed order), then
+ * the selection of mrb_router_topk on them -- two launches on `stream`, the second waiting on
+ * the first's grid. logits_bf16 [tokens, experts] receives the logits and is required.
+ * Outputs: top_idx, top_w_f32 (before bf16 rounding; may be NULL), top_w_bf16 (may be NULL)
+ * and top_w_coef = float(bf16 weight) (the route compiler's coefficients; may be NULL).
+ * hidden % 8 == 0; experts <= 256; k <= 16. Replaces the router linear and selection of
+ * `Qwen3MoeDecodeRuntime.forward` (engine/qwen3_moe_cuda.py:3700-3707, 3927-3933). */
+int mrb_router_qrow_topk(const void *x_bf16, int64_t tokens, int64_t hidden, const int8_t *codes,
+                         const float *scales, int64_t experts, int64_t k, int renorm, void *logits_bf16,
+                         int64_t *top_idx, float *top_w_f32, void *top_w_bf16, float *top_w_coef,
+                         void *stream);
+
 /* Route plan: counts/starts per expert (exclusive scan), expert-major token_ids and
  * coefficients in the stable order of the reference's CPU branch (argsort by expert,
  * stable: flat (token, rank) order inside each expert), and inverse[token*k + rank] = the

@@ -47,6 +47,7 @@ SIGNATURES: dict[str, list] = {
     "mrb_w8a8_protect_topk": [_P, c_int, _I64, _I64, c_int, _P, _P, _P],
     "mrb_w8a8_matmul": [_P, c_int, _I64, _I64, _P, _P, _I64, _P, c_int, _P, _P, _P, _P, _P, _P, _P],
     "mrb_router_topk": [_P, c_int, _I64, _I64, _I64, c_int, _P, _P, _P, _P],
+    "mrb_router_qrow_topk": [_P, _I64, _I64, _P, _P, _I64, _I64, c_int, _P, _P, _P, _P, _P, _P],
     "mrb_route_compile": [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P],
     "mrb_grouped_qrow": [_P, _P, _P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, c_int, _I64, _P, _P],
     "mrb_stable_route_reduce": [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P],

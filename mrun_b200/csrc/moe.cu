@@ -17,77 +17,203 @@ namespace mrb {
 
 // ------------------------------------------------------------------ router
 
-// One warp per token: softmax over E logits in fp32 (max-subtracted exp, divided by the
-// sum), then k rounds of arg-max (ties -> lower expert), optional renormalisation by the
+constexpr int ROUTER_MAXE = 256;
+
+// The selection shared by the router kernels, for one token held by one warp: lane l holds
+// the logits of experts l, l + 32, ... in p[]. Softmax in fp32 (max-subtracted exp, divided by
+// the sum), then k rounds of arg-max (ties -> lower expert), optional renormalisation by the
 // fp32 sum of the chosen probabilities, and the bf16 weights the reference hands on.
+// Outputs (each optional but top_idx): fp32 weights before the bf16 rounding, the bf16
+// weights, and the bf16 weights as fp32 (the coefficients the route compiler takes).
+//
+// Latency is the cost here (one warp, a few thousand cycles), so: slots past the last expert
+// are skipped by uniform branches; each lane sorts its own probabilities once (by key, then
+// expert), so its best is always at the head; and each arg-max round is two warp reductions
+// (redux.sync) over an order-preserving key -- the probability's bits + 1 (probabilities are
+// >= 0, so their bits order like the values; 0 marks an absent or taken expert) -- and then
+// the lowest expert among the lanes holding that key. The winning lane shifts its list.
+__device__ __forceinline__ uint32_t router_key(float prob) { return __float_as_uint(prob) + 1u; }
+
+// (key, expert) ordering: larger key first, then the lower expert
+__device__ __forceinline__ void router_cx(uint32_t& ka, uint32_t& ia, uint32_t& kb, uint32_t& ib) {
+  const bool swap = kb > ka || (kb == ka && ib < ia);
+  const uint32_t k0 = swap ? kb : ka, i0 = swap ? ib : ia;
+  kb = swap ? ka : kb;
+  ib = swap ? ia : ib;
+  ka = k0;
+  ia = i0;
+}
+
+template <int NS>
+__device__ __forceinline__ void router_pick(const float (&p)[ROUTER_MAXE / 32], int E, int k, int renorm, int64_t t,
+                                            int64_t* __restrict__ top_idx, float* __restrict__ top_w_f32,
+                                            __nv_bfloat16* __restrict__ top_w_bf16, float* __restrict__ top_w_coef) {
+  const int lane = threadIdx.x & 31;
+  uint32_t key[NS], idx[NS];
+#pragma unroll
+  for (int i = 0; i < NS; ++i) {
+    const int e = lane + 32 * i;
+    key[i] = e < E ? router_key(p[i]) : 0u;
+    idx[i] = e < E ? (uint32_t)e : 0xffffffffu;
+  }
+  // odd-even transposition sort of the lane's NS slots
+#pragma unroll
+  for (int r = 0; r < NS; ++r)
+#pragma unroll
+    for (int i = r & 1; i + 1 < NS; i += 2) router_cx(key[i], idx[i], key[i + 1], idx[i + 1]);
+  float chosen_sum = 0.f, my_w = 0.f;
+  uint32_t my_i = 0;
+  for (int j = 0; j < k; ++j) {
+    const uint32_t m = __reduce_max_sync(0xffffffffu, key[0]);
+    const uint32_t bi = __reduce_min_sync(0xffffffffu, key[0] == m ? idx[0] : 0xffffffffu);
+    const float best = __uint_as_float(m - 1u);
+    if (lane == j) {
+      my_w = best;
+      my_i = bi;
+    }
+    chosen_sum += best;
+    if (idx[0] == bi) {
+#pragma unroll
+      for (int i = 0; i + 1 < NS; ++i) {
+        key[i] = key[i + 1];
+        idx[i] = idx[i + 1];
+      }
+      key[NS - 1] = 0u;
+      idx[NS - 1] = 0xffffffffu;
+    }
+  }
+  if (lane < k) {
+    const float w = renorm ? my_w / chosen_sum : my_w;
+    top_idx[t * k + lane] = (int64_t)my_i;
+    if (top_w_f32) top_w_f32[t * k + lane] = w;
+    const __nv_bfloat16 wb = __float2bfloat16_rn(w);
+    if (top_w_bf16) top_w_bf16[t * k + lane] = wb;
+    if (top_w_coef) top_w_coef[t * k + lane] = __bfloat162float(wb);
+  }
+}
+
+__device__ __forceinline__ void router_select(float (&p)[ROUTER_MAXE / 32], int E, int k, int renorm, int64_t t,
+                                              int64_t* __restrict__ top_idx, float* __restrict__ top_w_f32,
+                                              __nv_bfloat16* __restrict__ top_w_bf16, float* __restrict__ top_w_coef) {
+  const int lane = threadIdx.x & 31;
+  const int slots = (E + 31) >> 5;  // slots that hold an expert in some lane (uniform)
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < ROUTER_MAXE / 32; ++i)
+    if (i < slots) mx = fmaxf(mx, p[i]);
+  // order-preserving u32 image of a float: flip all bits of negatives, the sign bit of the rest
+  const uint32_t mb = __float_as_uint(mx);
+  const uint32_t mflip = __reduce_max_sync(0xffffffffu, (mb & 0x80000000u) ? ~mb : (mb | 0x80000000u));
+  mx = __uint_as_float((mflip & 0x80000000u) ? (mflip & 0x7fffffffu) : ~mflip);
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < ROUTER_MAXE / 32; ++i)
+    if (i < slots) {
+      p[i] = (lane + 32 * i) < E ? expf(p[i] - mx) : 0.f;
+      sum += p[i];
+    }
+  sum = warp_sum(sum);
+#pragma unroll
+  for (int i = 0; i < ROUTER_MAXE / 32; ++i)
+    if (i < slots) p[i] = (lane + 32 * i) < E ? p[i] / sum : 0.f;
+  if (slots <= 1)
+    router_pick<1>(p, E, k, renorm, t, top_idx, top_w_f32, top_w_bf16, top_w_coef);
+  else if (slots <= 2)
+    router_pick<2>(p, E, k, renorm, t, top_idx, top_w_f32, top_w_bf16, top_w_coef);
+  else if (slots <= 4)
+    router_pick<4>(p, E, k, renorm, t, top_idx, top_w_f32, top_w_bf16, top_w_coef);
+  else
+    router_pick<8>(p, E, k, renorm, t, top_idx, top_w_f32, top_w_bf16, top_w_coef);
+}
+
+// One warp per token over logits already computed.
 template <typename LT>
 __global__ void router_topk_kernel(const LT* __restrict__ logits, int64_t tokens, int E, int k, int renorm,
                                    int64_t* __restrict__ top_idx, float* __restrict__ top_w_f32,
-                                   __nv_bfloat16* __restrict__ top_w_bf16) {
+                                   __nv_bfloat16* __restrict__ top_w_bf16, float* __restrict__ top_w_coef) {
   pdl_launch_dependents();
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= tokens) return;
-  constexpr int MAXE = 256;
-  float p[MAXE / 32];
+  float p[ROUTER_MAXE / 32];
   const LT* row = logits + t * E;
-  float mx = -INFINITY;
 #pragma unroll
-  for (int i = 0; i < MAXE / 32; ++i) {
+  for (int i = 0; i < ROUTER_MAXE / 32; ++i) {
     const int e = lane + 32 * i;
     p[i] = e < E ? io<LT>::load(row + e) : -INFINITY;
-    mx = fmaxf(mx, p[i]);
   }
-  mx = warp_max(mx);
-  float sum = 0.f;
+  router_select(p, E, k, renorm, t, top_idx, top_w_f32, top_w_bf16, top_w_coef);
+}
+
+// The router's logits, expert-major: CTA b computes the logits of experts b, b + grid, ...
+// for every token (exact int8 x bf16 products, fp32 sums in a fixed order, times the row
+// scale, rounded to bf16 -- the W8A16 projection's boundary). Each warp converts the expert's
+// codes to fp32 once and reuses them for its tokens, so the conversions do not scale with the
+// token count and the E x K router matrix is read from memory about once. The selection runs
+// next as router_topk_kernel (one warp per token), launched to wait on this grid.
+//
+// Conversion: 2^23 + u for the biased byte u = q + 128 is a float whose low mantissa byte is
+// u (built with one byte permute), and subtracting 2^23 + 128 gives q exactly.
+constexpr int RQ_WARPS = 16;
+constexpr int RQ_CHUNK = 8;  // 8-element vectors per lane and pass over k
+constexpr int RQ_TPW = 2;    // tokens per warp and token group (RQ_WARPS * RQ_TPW per group)
+
+__device__ __forceinline__ void rq_codes_to_f32(uint2 w, float (&f)[8]) {
+  const uint32_t lo = w.x ^ 0x80808080u, hi = w.y ^ 0x80808080u;
 #pragma unroll
-  for (int i = 0; i < MAXE / 32; ++i) {
-    const int e = lane + 32 * i;
-    p[i] = e < E ? expf(p[i] - mx) : 0.f;
-    sum += p[i];
+  for (int u = 0; u < 4; ++u) {
+    f[u] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u + u)) - 8388736.0f;
+    f[4 + u] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u + u)) - 8388736.0f;
   }
-  sum = warp_sum(sum);
+}
+
+__global__ void __launch_bounds__(RQ_WARPS * 32) router_qrow_logits_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t T, int64_t K, const int8_t* __restrict__ codes,
+    const float* __restrict__ scales, int E, __nv_bfloat16* __restrict__ logits) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = (int)(K / 8);
+  for (int e = blockIdx.x; e < E; e += gridDim.x) {
+    const uint2* wr = reinterpret_cast<const uint2*>(codes + (int64_t)e * K);
+    const float sc = scales[e];
+    for (int64_t t0 = 0; t0 < T; t0 += RQ_WARPS * RQ_TPW) {
+      float acc[RQ_TPW] = {};
+      for (int v0 = 0; v0 < nv; v0 += 32 * RQ_CHUNK) {
+        float cf[RQ_CHUNK][8];
 #pragma unroll
-  for (int i = 0; i < MAXE / 32; ++i) p[i] = (lane + 32 * i) < E ? p[i] / sum : -1.f;
-  float chosen_sum = 0.f;
-  float wsel[16];
-  int isel[16];
-  for (int j = 0; j < k; ++j) {
-    float best = -2.f;
-    int bi = 0x7fffffff;
+        for (int i = 0; i < RQ_CHUNK; ++i) {
+          const int v = v0 + lane + 32 * i;
+          rq_codes_to_f32(v < nv ? __ldg(wr + v) : make_uint2(0x80808080u, 0x80808080u) /* zeros */, cf[i]);
+        }
 #pragma unroll
-    for (int i = 0; i < MAXE / 32; ++i) {
-      const int e = lane + 32 * i;
-      if (p[i] > best || (p[i] == best && e < bi)) {
-        best = p[i];
-        bi = e;
+        for (int j = 0; j < RQ_TPW; ++j) {
+          const int64_t t = t0 + warp + RQ_WARPS * j;
+          if (t >= T) break;
+          const uint4* xr = reinterpret_cast<const uint4*>(x + t * K);
+          uint4 xv[RQ_CHUNK];
+#pragma unroll
+          for (int i = 0; i < RQ_CHUNK; ++i) {
+            const int v = v0 + lane + 32 * i;
+            xv[i] = v < nv ? __ldg(xr + v) : make_uint4(0u, 0u, 0u, 0u);
+          }
+          float a = acc[j];
+#pragma unroll
+          for (int i = 0; i < RQ_CHUNK; ++i) {
+            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&xv[i]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) a = fmaf(cf[i][u], __bfloat162float(h[u]), a);  // exact product
+          }
+          acc[j] = a;
+        }
       }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) {
-        best = ob;
-        bi = oi;
+      for (int j = 0; j < RQ_TPW; ++j) {
+        const int64_t t = t0 + warp + RQ_WARPS * j;
+        const float sum = warp_sum(acc[j]);
+        if (lane == 0 && t < T) logits[t * E + e] = __float2bfloat16_rn(round_bf16(sum * sc));
       }
-    }
-#pragma unroll
-    for (int i = 0; i < MAXE / 32; ++i)
-      if (lane + 32 * i == bi) p[i] = -2.f;  // taken
-    if (j < 16) {
-      wsel[j] = best;
-      isel[j] = bi;
-    }
-    chosen_sum += best;
-  }
-  if (lane == 0) {
-    for (int j = 0; j < k && j < 16; ++j) {
-      const float w = renorm ? wsel[j] / chosen_sum : wsel[j];
-      top_idx[t * k + j] = isel[j];
-      if (top_w_f32) top_w_f32[t * k + j] = w;
-      if (top_w_bf16) top_w_bf16[t * k + j] = __float2bfloat16_rn(w);
     }
   }
 }
@@ -544,7 +670,7 @@ extern "C" int mrb_router_topk(const void* logits, int logits_dtype, int64_t tok
                                int renorm, int64_t* top_idx, float* top_w_f32, void* top_w_bf16, void* stream) {
   if (tokens < 0 || experts <= 0 || k <= 0 || k > experts) return fail(MRB_ERR_ARG, "router_topk: bad shape");
   if (tokens == 0) return MRB_OK;
-  if (experts > 256 || k > 16) return fail(MRB_ERR_UNSUPPORTED, "router_topk: experts <= 256 and k <= 16");
+  if (experts > ROUTER_MAXE || k > 16) return fail(MRB_ERR_UNSUPPORTED, "router_topk: experts <= 256 and k <= 16");
   if (!logits || !top_idx) return fail(MRB_ERR_ARG, "router_topk: null pointer");
   const unsigned warps = 8;
   const dim3 grid((unsigned)((tokens + warps - 1) / warps));
@@ -552,17 +678,47 @@ extern "C" int mrb_router_topk(const void* logits, int logits_dtype, int64_t tok
   switch (logits_dtype) {
     case MRB_F32:
       launch_kernel(router_topk_kernel<float>, grid, dim3(32 * warps), 0, s, true, (const float*)logits, tokens,
-                    (int)experts, (int)k, renorm, top_idx, top_w_f32, (__nv_bfloat16*)top_w_bf16);
+                    (int)experts, (int)k, renorm, top_idx, top_w_f32, (__nv_bfloat16*)top_w_bf16, nullptr);
       break;
     case MRB_BF16:
       launch_kernel(router_topk_kernel<__nv_bfloat16>, grid, dim3(32 * warps), 0, s, true,
                     (const __nv_bfloat16*)logits, tokens, (int)experts, (int)k, renorm, top_idx, top_w_f32,
-                    (__nv_bfloat16*)top_w_bf16);
+                    (__nv_bfloat16*)top_w_bf16, nullptr);
       break;
     default:
       return fail(MRB_ERR_ARG, "router_topk: bad logits dtype %d", logits_dtype);
   }
   return launch_status("router_topk");
+}
+
+extern "C" int mrb_router_qrow_topk(const void* x_bf16, int64_t tokens, int64_t hidden, const int8_t* codes,
+                                    const float* scales, int64_t experts, int64_t k, int renorm, void* logits_bf16,
+                                    int64_t* top_idx, float* top_w_f32, void* top_w_bf16, float* top_w_coef,
+                                    void* stream) {
+  if (tokens < 0 || hidden <= 0 || experts <= 0 || k <= 0 || k > experts)
+    return fail(MRB_ERR_ARG, "router_qrow_topk: bad shape");
+  if (tokens == 0) return MRB_OK;
+  if (experts > ROUTER_MAXE || k > 16) return fail(MRB_ERR_UNSUPPORTED, "router_qrow_topk: experts <= 256 and k <= 16");
+  if (hidden % 8) return fail(MRB_ERR_UNSUPPORTED, "router_qrow_topk: hidden %lld is not a multiple of 8",
+                              (long long)hidden);
+  if (!x_bf16 || !codes || !scales || !logits_bf16 || !top_idx) return fail(MRB_ERR_ARG, "router_qrow_topk: null pointer");
+  if (!aligned(x_bf16, 16) || !aligned(codes, 8))
+    return fail(MRB_ERR_ARG, "router_qrow_topk: activation rows 16-byte and codes 8-byte aligned");
+  if (tokens * experts > 0x7fffffffLL) return fail(MRB_ERR_UNSUPPORTED, "router_qrow_topk: too many tokens");
+  const cudaStream_t s = (cudaStream_t)stream;
+  // one CTA per expert up to one wave, else two experts per CTA; the selection's CTAs
+  // (8 tokens each) wait for the logits on the SMs left over
+  const int grid = experts <= num_sms() ? (int)experts : (int)((experts + 1) / 2);
+  launch_kernel(router_qrow_logits_kernel, dim3((unsigned)grid), dim3(RQ_WARPS * 32), 0, s, true,
+                (const __nv_bfloat16*)x_bf16, tokens, hidden, codes, scales, (int)experts,
+                (__nv_bfloat16*)logits_bf16);
+  int rc = launch_status("router_qrow_topk");
+  if (rc) return rc;
+  const int warps = 8;
+  launch_kernel(router_topk_kernel<__nv_bfloat16>, dim3((unsigned)((tokens + warps - 1) / warps)), dim3(32 * warps), 0,
+                s, true, (const __nv_bfloat16*)logits_bf16, tokens, (int)experts, (int)k, renorm, top_idx, top_w_f32,
+                (__nv_bfloat16*)top_w_bf16, top_w_coef);
+  return launch_status("router_qrow_topk");
 }
 
 extern "C" int mrb_route_compile(const int64_t* top_idx, const float* top_w, int64_t tokens, int64_t k,

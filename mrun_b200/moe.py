@@ -155,6 +155,43 @@ def router_topk(logits: torch.Tensor, k: int, *, renorm: bool = True) -> tuple[t
     return idx, w16, w32
 
 
+def router_qrow_topk(x: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor, k: int, *, renorm: bool = True,
+                     logits: torch.Tensor | None = None, out: tuple | None = None):
+    """The router linear and selection of one MoE layer in one launch (qwen3_moe_cuda.py:
+    3700-3707): bf16 logits of x [T, H] against int8 router codes [E, H] (W8A16 boundary),
+    softmax / top-k (ties -> lower expert) / optional renorm. Returns (indices int64 [T, k],
+    weights bf16 [T, k], coefficients fp32 [T, k] = the bf16 weights as fp32).
+
+    Two launches: the logits (expert-major), then the selection waiting on them. ``logits``
+    (bf16, at least [T, E], row stride E) receives the logits; ``out`` reuses (indices,
+    weights, coefficients) buffers. A captured step passes both so their addresses stay
+    fixed."""
+    device = _lib.require_cuda(x, codes, scales, what="router")
+    xr = x.reshape(-1, x.shape[-1])
+    if xr.dtype != torch.bfloat16:
+        raise ValueError("the router takes bf16 activations")
+    if not xr.is_contiguous() or xr.data_ptr() % 16:
+        xr = xr.contiguous().clone() if xr.data_ptr() % 16 else xr.contiguous()
+    t, h = (int(v) for v in xr.shape)
+    e = int(codes.shape[0])
+    if int(codes.shape[1]) != h:
+        raise ValueError("router codes do not match the activation width")
+    if logits is None:
+        logits = torch.empty((t, e), dtype=torch.bfloat16, device=device)
+    elif (logits.dtype != torch.bfloat16 or not logits.is_contiguous() or logits.dim() != 2
+          or int(logits.shape[1]) != e or int(logits.shape[0]) < t):
+        raise ValueError("router logits must be contiguous bf16 [>= tokens, experts]")
+    if out is None:
+        out = (torch.empty((t, k), dtype=torch.int64, device=device),
+               torch.empty((t, k), dtype=torch.bfloat16, device=device),
+               torch.empty((t, k), dtype=torch.float32, device=device))
+    idx, w16, coef = (o[:t] for o in out)
+    _lib.call("mrb_router_qrow_topk", xr.data_ptr(), t, h, codes.data_ptr(), scales.data_ptr(), e, int(k),
+              int(bool(renorm)), logits.data_ptr(), idx.data_ptr(), None, w16.data_ptr(), coef.data_ptr(),
+              _lib.stream_handle(device))
+    return idx, w16, coef
+
+
 # ------------------------------------------------------------------ route compiler
 
 
@@ -355,6 +392,7 @@ __all__ = [
     "grouped_route_tensors",
     "grouped_route_tensors_with_inverse",
     "pack_expert_page",
+    "router_qrow_topk",
     "router_topk",
     "stable_route_reduce",
 ]

@@ -28,7 +28,7 @@ from . import _lib
 from .dense_engine import QRow, rope_tables
 from .dense_qstore_cuda import qrow_argmax, qrow_linear, qrow_workspace_bytes, residual_rms_norm_into, rms_norm_into
 from .expert_parallel import ExpertShard, FixedCapacityExpertParallelMoE, P2PExpertParallelMoE
-from .moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_topk
+from .moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_qrow_topk
 from .paged_kv import PagedKVCache
 from .qstore_build import embed_rows
 
@@ -203,8 +203,12 @@ class MoeDecoder:
             "q": torch.empty(r, cfg.heads, cfg.head_dim, dtype=bf, device=device),
             "ctx": torch.empty(r, cfg.heads, cfg.head_dim, dtype=bf, device=device),
             "proj": torch.empty(r, cfg.hidden, dtype=bf, device=device),
-            "logits": torch.empty(r, cfg.experts, dtype=bf, device=device),
         }
+        # router outputs: expert ids, bf16 weights and their fp32 images (route coefficients)
+        self.route_buf = (torch.empty(r, cfg.top_k, dtype=torch.int64, device=device),
+                          torch.empty(r, cfg.top_k, dtype=bf, device=device),
+                          torch.empty(r, cfg.top_k, dtype=torch.float32, device=device))
+        self.router_logits = torch.empty(r, cfg.experts, dtype=bf, device=device)
         self.in_ids = torch.zeros(r, dtype=torch.int64, device=device)
         self.positions = torch.zeros(r, dtype=torch.int32, device=device)
         self.row_len = torch.zeros(r, dtype=torch.int32, device=device)
@@ -267,7 +271,7 @@ class MoeDecoder:
         cfg, buf, w = self.cfg, self.buf, self.w
         hidden, normed = buf["hidden"][:rows], buf["normed"][:rows]
         qkv, q, ctx = buf["qkv"][:rows], buf["q"][:rows], buf["ctx"][:rows]
-        proj, logits = buf["proj"][:rows], buf["logits"][:rows]
+        proj = buf["proj"][:rows]
         qd, kd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
         ws = self.gemv_ws
         embed_rows(w.embed.codes, w.embed.scales, self.in_ids[:rows], dtype=torch.bfloat16, out=hidden)
@@ -282,10 +286,13 @@ class MoeDecoder:
                            workspace=self.attn_ws, scale=self.scale)
             qrow_linear(layer.o.codes, layer.o.scales, ctx.view(rows, qd), out=proj, workspace=ws)
             residual_rms_norm_into(hidden, proj, layer.ln2, cfg.eps, hidden, normed)
-            qrow_linear(layer.router.codes, layer.router.scales, normed, out=logits, workspace=ws)
-            top_idx, top_w, _ = router_topk(logits, cfg.top_k, renorm=cfg.norm_topk)
+            # router linear + softmax / top-k in one launch; the backends take the fp32 images
+            # of the bf16 weights (the values the reference's .float() would give)
+            top_idx, _, top_w = router_qrow_topk(normed, layer.router.codes, layer.router.scales, cfg.top_k,
+                                                 renorm=cfg.norm_topk, logits=self.router_logits,
+                                                 out=self.route_buf)
             if self.routes is not None:
-                self.routes.append(top_idx)
+                self.routes.append(top_idx.clone())  # the router buffers are reused per layer
             if self.ep is not None:
                 moe_out = self.ep[i].forward(normed, top_idx, top_w)
             else:

@@ -116,3 +116,32 @@ def test_moe_backend_vs_oracle_and_row_independence(tokens, k, experts, hidden, 
     # each token's result is independent of which other tokens share its experts
     single = torch.stack([backend.moe(0, x[i:i + 1], idx[i:i + 1], w16[i:i + 1])[0] for i in range(min(tokens, 6))])
     assert torch.equal(single, out[: single.shape[0]])
+
+
+@pytest.mark.parametrize("t,e,k,h", [(32, 128, 8, 2048), (5, 8, 2, 4096), (64, 60, 4, 512), (1, 256, 16, 256),
+                                     (97, 200, 8, 1032)])
+def test_fused_router_matches_projection_and_selection(t, e, k, h, cuda):
+    """mrb_router_qrow_topk: logits within one bf16 rounding of the exact int8 x bf16 product;
+    the selection bit-identical to router_topk on those same logits (indices, bf16 weights);
+    coefficients are the bf16 weights as fp32."""
+    from mrun_b200.moe import router_qrow_topk, router_topk
+
+    gen = torch.Generator(device="cpu").manual_seed(t * 1000 + e)
+    codes = torch.randint(-127, 128, (e, h), generator=gen, dtype=torch.int8)
+    scales = torch.rand(e, generator=gen) * 1e-3 + 1e-4
+    x = torch.randn(t, h, generator=gen).to(torch.bfloat16)
+    logits = torch.empty(t, e, dtype=torch.bfloat16, device=cuda)
+    idx, w16, coef = router_qrow_topk(x.to(cuda), codes.to(cuda), scales.to(cuda), k, logits=logits)
+    exact = (x.double() @ codes.double().T) * scales.double()[None, :]
+    got = logits.double().cpu()
+    # per element: one bf16 rounding (2^-9 relative) plus fp32 summation error, measured
+    # against the row's largest logit so that near-zero logits do not divide by ~0
+    rowmax = exact.abs().amax(dim=1, keepdim=True)
+    assert float(((got - exact).abs() / rowmax).max()) <= 2.0 ** -8
+    ridx, rw16, _ = router_topk(logits, k, renorm=True)
+    assert torch.equal(idx, ridx) and torch.equal(w16, rw16)
+    assert torch.equal(coef, w16.float())
+    # deterministic
+    for _ in range(3):
+        idx2, w2, _ = router_qrow_topk(x.to(cuda), codes.to(cuda), scales.to(cuda), k)
+        assert torch.equal(idx2, idx) and torch.equal(w2, w16)
