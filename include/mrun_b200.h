@@ -389,6 +389,12 @@ int mrb_rope_append_attention(const void *q_in, const void *k_in, const void *v_
 int mrb_rope_append_attention_cluster(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
                                       int64_t max_total_tokens);
 
+/* Waits of the TMA decode attention (canonical paged pools) that ran out on the current
+ * device since the library loaded: each stage wait is bounded, and a wait that gives up counts
+ * here and lets the kernel finish (its output is then not to be trusted). Negative on a CUDA
+ * error. */
+int64_t mrb_paged_attention_timeouts(void);
+
 /* Workspace bytes mrb_paged_attention needs for these sizes (0 when no split is used). */
 size_t mrb_paged_attention_workspace(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
                                      int64_t max_total_tokens);

@@ -66,6 +66,7 @@ SIGNATURES: dict[str, list] = {
     "mrb_store_file_read": [_P, ctypes.c_uint64, ctypes.c_uint64, _P, c_int, c_int],
     "mrb_store_file_advise": [_P, ctypes.c_uint64, ctypes.c_uint64, c_int],
     "mrb_paged_attention_workspace": [_I64, _I64, _I64, _I64, _I64],
+    "mrb_paged_attention_timeouts": [],
     "mrb_paged_attention": [_P, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P,
                             _P, _P, c_float, _I64, _P, _P, c_size_t, _P],
     "mrb_paged_attention_static_capacity": [],
@@ -88,7 +89,8 @@ SIGNATURES: dict[str, list] = {
 }
 _RESTYPES = {"mrb_last_error": ctypes.c_char_p, "mrb_abi_version": c_int, "mrb_paged_attention_workspace": c_size_t,
              "mrb_paged_attention_static_capacity": c_size_t, "mrb_qrow_workspace": c_size_t,
-             "mrb_ep_mailbox_bytes": c_size_t, "mrb_ep_wait_limit": ctypes.c_int64}
+             "mrb_ep_mailbox_bytes": c_size_t, "mrb_ep_wait_limit": ctypes.c_int64,
+             "mrb_paged_attention_timeouts": ctypes.c_int64}
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -173,8 +173,15 @@ struct AttnArgs {
   int nsplit;
   int tiles_per_split;
   __nv_bfloat16* out;  // [rows, hq, d]
-  float* part;         // [rows*hkv][nsplit][group][2 + d]
-  unsigned* counters;  // [rows*hkv]
+  float* part;         // fixed splits: [rows*hkv][nsplit][group][2 + d]; balanced: [bal_ctas + rows*hkv][group][2 + d]
+  unsigned* counters;  // [rows*hkv], zero between launches
+  unsigned* meta;      // [rows*hkv]: per group (first partial slot << 16) | partials (warp schedule)
+  int bal_ctas;        // > 0: balanced schedule over this many CTAs (tensor-core kernel)
+  int max_tiles;       // balanced: tiles per group at most (the host's context bound)
+  int tma;             // 1: the TMA kernel (canonical paged pool); kmap/vmap are set
+  int warp_sched;      // with tma and bal_ctas: one tile range per warp, then the merge kernel
+  CUtensorMap kmap;    // K pool as [rows, 128] bf16, box [16, 64], 128-byte swizzle
+  CUtensorMap vmap;
 };
 
 __device__ __forceinline__ int64_t kv_offset(const AttnArgs& a, int64_t seq, int64_t tok, int64_t khead) {
@@ -250,7 +257,7 @@ __device__ __forceinline__ void attend_tile(const __nv_bfloat16 (*ks)[D], const 
 // Splits publish (max, sum, acc) partials; the last CTA of the (row, head) group merges them
 // in split order (deterministic), each warp merging its own head.
 template <int D>
-__global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_kernel(const __grid_constant__ AttnArgs a) {
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   constexpr int HALF = D / 2;     // dims per lane in the score phase
   constexpr int VD = D / 32;      // dims per lane in the value phase
@@ -686,28 +693,28 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 // Decode attention on the tensor pipe (head_dim 128, GQA group <= 16).
 //
-// The CTA owns (query row, KV head, split) like the scalar kernel, with W <= 4 warps that
-// take the split's 16-token tiles in turn (warp w: tiles w, w + W, ...), each through its
-// own 3-stage cp.async ring of K and V tiles (rows padded to 272 B so fragment reads are
-// conflict-free). Per tile a warp computes S = Q K^T for all query heads of the group at
+// One work item: tiles [tile_lo, tile_hi) of (query row, KV head) group rh, attended by the
+// CTA's W <= 4 warps, which take the item's 16-token tiles in turn (warp w: tiles w, w + W,
+// ...), each through its own AM_STAGES-deep cp.async ring of K and V tiles (rows padded to
+// 272 B so fragment reads are conflict-free). Per tile a warp computes S = Q K^T for all query heads of the group at
 // once -- heads are the 16 rows of mma.sync m16n8k16 (bf16 inputs, fp32 accumulation), two
 // 8-token column blocks, eight 16-dim k steps -- scales it in fp32, runs the online softmax
 // per head row in fp32, and accumulates O += P V on the tensor pipe with P (rounded to
 // bf16) reused straight from the score fragments and V fragments from ldmatrix.trans. The
-// W partial states are merged through shared memory in warp order, then published and
-// merged across splits exactly as the scalar kernel does (deterministic).
-__global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(AttnArgs a) {
+// W partial states are merged through shared memory in warp order. With nparts == 1 the item
+// is the whole group and writes the output; otherwise it publishes its state in slot `slot`
+// of a.part, and the last of the group's nparts items to arrive merges slots [slot0, slot0 +
+// nparts) in slot order (deterministic). Every thread of the CTA calls it with the same
+// arguments, and the shared memory is free again when it returns.
+__device__ __forceinline__ void am_item(const AttnArgs& a, int64_t rh, int64_t tile_lo, int64_t tile_hi, int64_t slot,
+                                        int64_t slot0, int nparts) {
   constexpr int D = 128;
   const int W = blockDim.x >> 5;
   const int group = (int)(a.hq / a.hkv);
-  const int64_t rh = blockIdx.x;  // row * hkv + kv head
-  const int split = blockIdx.y;
   const int64_t r = rh / a.hkv;
   const int kvh = (int)(rh - r * a.hkv);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  pdl_launch_dependents();
-  pdl_wait();
 
   extern __shared__ __align__(16) unsigned char am_smem[];
   __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(am_smem) + (size_t)warp * AM_STAGES * AM_STAGE_ELEMS;
@@ -717,8 +724,11 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
   const int64_t len = a.row_len[r];
   const bool has_new = a.k_new != nullptr;
   const int64_t total = len + (has_new ? 1 : 0);
-  const int64_t t_begin = (int64_t)split * a.tiles_per_split * AT_TILE;
-  const int64_t t_end = min(total, t_begin + (int64_t)a.tiles_per_split * AT_TILE);
+  const int64_t t_begin = tile_lo * AT_TILE;
+  const int64_t t_end = min(total, tile_hi * AT_TILE);
+  // scores in base-2 units: exp(x * scale) = exp2(x * scale * log2(e)); running maxima and
+  // the published partial maxima are in the same units
+  const float scale2 = a.scale * 1.4426950408889634f;
   const int ntile = t_end > t_begin ? (int)((t_end - t_begin + AT_TILE - 1) / AT_TILE) : 0;
   const int nmine = warp < ntile ? (ntile - warp + W - 1) / W : 0;
   const int64_t khead = (int64_t)kvh * a.stride_head;
@@ -831,7 +841,7 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) s[nt][i] = nt * 8 + 2 * c + (i & 1) < lim ? s[nt][i] * a.scale : -INFINITY;
+      for (int i = 0; i < 4; ++i) s[nt][i] = nt * 8 + 2 * c + (i & 1) < lim ? s[nt][i] * scale2 : -INFINITY;
     // rows g + 8 hold query heads only for groups above 8; otherwise they stay empty
     float alpha[2] = {1.f, 1.f};
     if (!two_halves) s[0][2] = s[0][3] = s[1][2] = s[1][3] = 0.f;
@@ -842,13 +852,13 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       const float m_new = fmaxf(mrow[h], mx);
-      alpha[h] = (mrow[h] == -INFINITY) ? 0.f : expf(mrow[h] - m_new);
+      alpha[h] = (mrow[h] == -INFINITY) ? 0.f : exp2f(mrow[h] - m_new);
       float sum = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          const float p = (m_new == -INFINITY) ? 0.f : expf(s[nt][2 * h + i] - m_new);
+          const float p = (m_new == -INFINITY) ? 0.f : exp2f(s[nt][2 * h + i] - m_new);
           s[nt][2 * h + i] = p;
           sum += p;
         }
@@ -903,7 +913,7 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
     }
   }
   __syncthreads();
-  // per head: the combined max and sum, and one weight per warp state (expf once per (warp,
+  // per head: the combined max and sum, and one weight per warp state (exp2f once per (warp,
   // head) instead of once per element)
   float* wts = mb + (size_t)W * 16 * (2 + D);  // [W][16]
   float* hstat = wts + (size_t)W * 16;         // [16] max, [16] sum
@@ -914,7 +924,7 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
     float l = 0.f;
     for (int w = 0; w < W; ++w) {
       const float* st = mb + ((size_t)w * 16 + h) * (2 + D);
-      const float wt = (st[0] == -INFINITY) ? 0.f : expf(st[0] - mx);
+      const float wt = (st[0] == -INFINITY) ? 0.f : exp2f(st[0] - mx);
       wts[w * 16 + h] = wt;
       l = fmaf(st[1], wt, l);
     }
@@ -922,13 +932,13 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
     hstat[16 + h] = l;
   }
   __syncthreads();
-  float* part_base = a.nsplit > 1 ? a.part + (rh * a.nsplit + split) * (int64_t)group * (2 + D) : nullptr;
+  float* part_base = nparts > 1 ? a.part + slot * (int64_t)group * (2 + D) : nullptr;
   for (int idx = tid; idx < group * D; idx += blockDim.x) {
     const int h = idx / D, d = idx - h * D;
     const float mx = hstat[h], l = hstat[16 + h];
     float acc = 0.f;
     for (int w = 0; w < W; ++w) acc = fmaf(mb[((size_t)w * 16 + h) * (2 + D) + 2 + d], wts[w * 16 + h], acc);
-    if (a.nsplit == 1) {
+    if (nparts == 1) {
       a.out[(r * a.hq + (int64_t)kvh * group + h) * D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
     } else {
       float* p = part_base + (int64_t)h * (2 + D);
@@ -939,12 +949,12 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
       }
     }
   }
-  if (a.nsplit == 1) return;
+  __syncthreads();  // the merge area is read; the next item may reuse the shared memory
+  if (nparts == 1) return;
   __threadfence();
-  __syncthreads();
   if (tid == 0) {
     const unsigned prev = atomicAdd(&a.counters[rh], 1u);
-    is_last = prev == (unsigned)(a.nsplit - 1);
+    is_last = prev == (unsigned)(nparts - 1);
   }
   __syncthreads();
   if (!is_last) return;
@@ -953,18 +963,18 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
   constexpr int VD = D / 32;
   const int64_t sstride = (int64_t)group * (2 + D);
   for (int h = warp; h < group; h += W) {
-    const float* base = a.part + (rh * a.nsplit * group + h) * (2 + D);
+    const float* base = a.part + (slot0 * group + h) * (2 + D);
     float mx_all = -INFINITY;
-    for (int s0 = lane; s0 < a.nsplit; s0 += 32) mx_all = fmaxf(mx_all, __ldcg(base + s0 * sstride));
+    for (int s0 = lane; s0 < nparts; s0 += 32) mx_all = fmaxf(mx_all, __ldcg(base + s0 * sstride));
     mx_all = warp_max(mx_all);
     float lsum = 0.f, ov[VD];
 #pragma unroll
     for (int i = 0; i < VD; ++i) ov[i] = 0.f;
-    for (int s0 = 0; s0 < a.nsplit; s0 += 8) {  // 8 splits' loads in flight at a time
+    for (int s0 = 0; s0 < nparts; s0 += 8) {  // 8 partials' loads in flight at a time
       float ms[8], ls[8], av[8][VD];
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj) {
-        const bool ok = s0 + jj < a.nsplit;
+        const bool ok = s0 + jj < nparts;
         const float* p = base + (s0 + jj) * sstride;
         ms[jj] = ok ? __ldcg(p) : -INFINITY;
         ls[jj] = ok ? __ldcg(p + 1) : 0.f;
@@ -973,7 +983,7 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
       }
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj) {
-        const float wt = (ms[jj] == -INFINITY) ? 0.f : expf(ms[jj] - mx_all);
+        const float wt = (ms[jj] == -INFINITY) ? 0.f : exp2f(ms[jj] - mx_all);
         lsum = fmaf(ls[jj], wt, lsum);
 #pragma unroll
         for (int i = 0; i < VD; ++i) ov[i] = fmaf(av[jj][i], wt, ov[i]);
@@ -985,6 +995,850 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) paged_attention_mma_kernel(
   }
   __syncthreads();
   if (tid == 0) a.counters[rh] = 0u;  // ready for the next launch (graph replays)
+}
+
+
+// Tiles of one (query row, KV head) group for the balanced schedule: the row's committed
+// tokens plus the provisional one, at least one tile (an empty row still writes zeros), at
+// most the host's bound.
+__device__ __forceinline__ int am_row_tiles(const AttnArgs& a, int64_t r) {
+  const int64_t total = (int64_t)a.row_len[r] + (a.k_new != nullptr ? 1 : 0);
+  return (int)max((int64_t)1, min((int64_t)a.max_tiles, (total + AT_TILE - 1) / AT_TILE));
+}
+
+// Two schedules, one instantiation each (one copy of the item body per kernel keeps the code
+// inside the instruction cache). Fixed splits: the CTA is (group blockIdx.x, split
+// blockIdx.y) of tiles_per_split tiles. Balanced (a.bal_ctas > 0): the groups' tiles, as the
+// rows' lengths give them, are laid end to end (group-major) and CTA c of P = min(bal_ctas,
+// T) takes tiles [c*T/P, (c+1)*T/P) of the T in all, walking the groups its range touches;
+// a group cut by a range boundary is finished by the last of its CTAs, which merges their
+// partials in CTA order. Partial slot of (CTA c, group rh) = c + rh: along the tile order c
+// and rh never both decrease, so no two (c, rh) pairs of one launch share a slot, and a
+// group's slots are consecutive. The plan is recomputed from row_len by every CTA, so it
+// follows the lengths of each launch (a captured graph needs no host update).
+template <bool BALANCED, typename Item>
+__device__ __forceinline__ void attn_schedule(const AttnArgs& a, Item&& item) {
+  if constexpr (!BALANCED) {
+    const int64_t rh = blockIdx.x;
+    const int64_t split = blockIdx.y;
+    item(rh, split * a.tiles_per_split, (split + 1) * a.tiles_per_split, rh * a.nsplit + split, rh * a.nsplit,
+         a.nsplit);
+    return;
+  }
+  extern __shared__ __align__(16) unsigned char am_smem[];
+  int* pre = reinterpret_cast<int*>(am_smem);  // [rows + 1]: tiles of all groups of the rows before r
+  const int R = (int)a.rows, hkv = (int)a.hkv;
+  const int tid = threadIdx.x, lane = tid & 31;
+  for (int r = tid; r < R; r += blockDim.x) pre[r + 1] = am_row_tiles(a, r) * hkv;
+  if (tid == 0) pre[0] = 0;
+  __syncthreads();
+  if (tid < 32) {  // inclusive scan of pre[1..R], 32 rows at a time
+    int carry = 0;
+    for (int b = 1; b <= R; b += 32) {
+      int v = b + lane <= R ? pre[b + lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      if (b + lane <= R) pre[b + lane] = v + carry;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  const int64_t T = pre[R];
+  const int64_t P = min((int64_t)a.bal_ctas, T);
+  const int64_t cta = blockIdx.x;
+  const int64_t lo = cta * T / P, hi = (cta + 1) * T / P;
+  int r = 0;  // the row holding tile lo: the largest r with pre[r] <= lo
+  for (int L = 0, H = R; H - L > 1;) {
+    const int M = (L + H) >> 1;
+    if (pre[M] <= lo) L = M; else H = M;
+    r = L;
+  }
+  int64_t rowstart = pre[r];
+  int tr = (pre[r + 1] - pre[r]) / hkv;
+  __syncthreads();  // the plan is read; the shared memory becomes the K/V rings
+  if (cta >= P) return;
+  int kvh = (int)((lo - rowstart) / tr);
+  int64_t toff = lo - rowstart - (int64_t)kvh * tr;
+  for (int64_t cur = lo; cur < hi;) {
+    const int64_t gstart = rowstart + (int64_t)kvh * tr;  // the group's first tile
+    const int64_t seg = min(hi - cur, (int64_t)tr - toff);
+    const int64_t cf = ((gstart + 1) * P - 1) / T;      // the CTA holding the group's first tile
+    const int64_t cl = ((gstart + tr) * P - 1) / T;     // ... and its last
+    const int64_t rh = (int64_t)r * hkv + kvh;
+    item(rh, toff, toff + seg, cta + rh, cf + rh, (int)(cl - cf + 1));
+    cur += seg;
+    toff = 0;
+    if (++kvh == hkv && cur < hi) {
+      kvh = 0;
+      rowstart += (int64_t)hkv * tr;
+      tr = am_row_tiles(a, ++r);
+    }
+  }
+}
+
+template <bool BALANCED>
+__global__ void __launch_bounds__(AM_MAX_WARPS * 32, AT_MMA_CTAS_PER_SM) paged_attention_mma_kernel(const __grid_constant__ AttnArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  attn_schedule<BALANCED>(a, [&](int64_t rh, int64_t lo, int64_t hi, int64_t slot, int64_t slot0, int nparts) {
+    am_item(a, rh, lo, hi, slot, slot0, nparts);
+  });
+}
+
+// ------------------------------------------------------------------ TMA decode attention
+
+// Decode attention for the canonical paged pool ([pages, Hkv, page_size, 128] bf16, page
+// size a multiple of 16), head_dim 128, GQA group <= 8 * NT.
+//
+// Loads: each warp keeps an A2_STAGES-deep ring of 16-token tiles; one lane fetches a tile
+// as four TMA boxes ([16 tokens x 64 dims] of K and of V, 128-byte swizzle) completing on
+// the stage's mbarrier, so a tile costs a handful of instructions to request, and the page
+// numbers of the warp's next 32 tiles are read in one go ahead of time (no block-table load
+// on the path from one tile's request to the next).
+// Math, transposed so that tokens (not the 8 heads of a group) fill the 16 rows of
+// mma.sync m16n8k16 (bf16 inputs, fp32 accumulation): S^T = K Q^T (A = K tile by ldmatrix,
+// B = the group's queries held in registers), online softmax per head column in base 2,
+// then O^T += V^T P^T (A = V tile by ldmatrix.trans, B = P^T moved out of the score
+// fragments with movmatrix.trans). Per tile 8 + 8 MMAs per 8 heads. Row sums stay per lane
+// until the item ends. Partial states merge exactly as in am_item (same layouts, base-2
+// maxima), so the schedules and the cross-CTA merge are shared.
+#ifndef A2_RING_STAGES
+#define A2_RING_STAGES 2
+#endif
+constexpr int A2_STAGES = A2_RING_STAGES;
+constexpr int A2_BOX = AT_TILE * 64 * 2;        // [16 tokens x 64 dims] bf16: 2 KB
+constexpr int A2_STAGE_BYTES = 4 * A2_BOX;      // K dims 0-63, K 64-127, V 0-63, V 64-127
+constexpr int A2_TBL = 32;                      // page numbers fetched per batch, one per lane
+constexpr int AT_BAL_MAX_ROWS_DEV = 1024;       // rows the balanced schedules take (prefix in shared memory)
+
+__host__ __device__ inline size_t a2_smem_bytes(int warps) {
+  const size_t ring = (size_t)warps * A2_STAGES * A2_STAGE_BYTES;
+  const size_t merge = ((size_t)warps * 16 * (2 + 128) + (size_t)warps * 16 + 2 * 16) * sizeof(float);
+  return (ring > merge ? ring : merge) + 1024;  // + alignment of the rings to the 1024-byte swizzle atom
+}
+
+__device__ unsigned g_attn_timeouts = 0;
+
+__device__ __forceinline__ void movmatrix_trans(uint32_t& d, uint32_t s) {
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(s));
+}
+
+// byte offset of 16-byte chunk c (0-7) of row r inside a 128-byte-swizzled box
+__device__ __forceinline__ uint32_t a2_swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// One work item (same contract as am_item). `ring` is this warp's ring, `bars` its stage
+// barriers, `seq` the number of tiles the warp has taken through the ring so far (stage
+// and phase of its next tile), carried from item to item.
+template <int NT>
+__device__ __forceinline__ void a2_item(const AttnArgs& a, unsigned char* ring, uint64_t* bars, uint32_t& seq,
+                                        float* mb, int64_t rh, int64_t tile_lo, int64_t tile_hi, int64_t slot,
+                                        int64_t slot0, int nparts) {
+  constexpr int D = 128;
+  const int W = blockDim.x >> 5;
+  const int group = (int)(a.hq / a.hkv);
+  const int64_t r = rh / a.hkv;
+  const int kvh = (int)(rh - r * a.hkv);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = lane & 3;
+  __shared__ bool is_last;
+
+  const int64_t seq_row = a.row_seq ? a.row_seq[r] : r;
+  const int64_t len = a.row_len[r];
+  const bool has_new = a.k_new != nullptr;
+  const int64_t total = len + (has_new ? 1 : 0);
+  const int64_t t_begin = tile_lo * AT_TILE;
+  const int64_t t_end = min(total, tile_hi * AT_TILE);
+  const int ntile = t_end > t_begin ? (int)((t_end - t_begin + AT_TILE - 1) / AT_TILE) : 0;
+  const int nmine = warp < ntile ? (ntile - warp + W - 1) / W : 0;
+  const float scale2 = a.scale * 1.4426950408889634f;  // exp(x s) = exp2(x s log2(e))
+  const uint32_t seq0 = seq;
+
+  // page numbers of this warp's tiles [base, base + 32): lane i holds tile base + i's
+  int tbl = 0;
+  auto load_tbl = [&](int base) {
+    const int j = base + lane;
+    tbl = 0;
+    if (j < nmine) {
+      const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
+      if (t0 < len) tbl = a.block_table[seq_row * a.bt_stride + t0 / a.page_size];
+    }
+  };
+  load_tbl(0);
+  // request tile j of this item (whole warp; lane 0 issues)
+  auto issue = [&](int j) {
+    if (j >= nmine) return;
+    if ((j & (A2_TBL - 1)) == 0 && j) load_tbl(j);
+    const int page = __shfl_sync(0xffffffffu, tbl, j & (A2_TBL - 1));
+    if (lane == 0) {
+      const uint32_t u = seq0 + (uint32_t)j;
+      unsigned char* st = ring + (u % A2_STAGES) * A2_STAGE_BYTES;
+      uint64_t* bar = bars + (u % A2_STAGES);
+      const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
+      if (t0 < len) {
+        const int y = (int)(((int64_t)page * a.hkv + kvh) * a.page_size + (t0 % a.page_size));
+        fence_proxy_async_smem();  // this lane's earlier generic writes to the stage come first
+        mbar_arrive_expect_tx(bar, A2_STAGE_BYTES);
+        tma_load_2d(st, &a.kmap, 0, y, bar);
+        tma_load_2d(st + A2_BOX, &a.kmap, 64, y, bar);
+        tma_load_2d(st + 2 * A2_BOX, &a.vmap, 0, y, bar);
+        tma_load_2d(st + 3 * A2_BOX, &a.vmap, 64, y, bar);
+      } else {
+        mbar_arrive(bar);  // the tile holds only the provisional token: nothing to fetch
+      }
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < A2_STAGES - 1; ++j) issue(j);
+
+  // the group's queries as the B operand: head nt*8 + gq, dims ks*16 + 2cq (+1) and + 8
+  uint32_t qb[NT][D / 16][2];
+  {
+    const __nv_bfloat16* q0 = a.q + (r * a.hq + (int64_t)kvh * group) * D;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int h = nt * 8 + gq;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const int d0 = ks * 16 + 2 * cq;
+        qb[nt][ks][0] = h < group ? *reinterpret_cast<const uint32_t*>(q0 + h * D + d0) : 0u;
+        qb[nt][ks][1] = h < group ? *reinterpret_cast<const uint32_t*>(q0 + h * D + d0 + 8) : 0u;
+      }
+    }
+  }
+  // O^T accumulators: dims mt*16 + gq (+8) x heads nt*8 + 2cq (+1)
+  float o[D / 16][NT][4];
+#pragma unroll
+  for (int mt = 0; mt < D / 16; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
+  float mrow[NT][2], lrow[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) mrow[nt][0] = mrow[nt][1] = -INFINITY, lrow[nt][0] = lrow[nt][1] = 0.f;
+
+  const int mi = lane >> 3, rr = lane & 7;
+  for (int j = 0; j < nmine; ++j) {
+    const uint32_t u = seq0 + (uint32_t)j;
+    unsigned char* st = ring + (u % A2_STAGES) * A2_STAGE_BYTES;
+    if (!mbar_wait_bounded(bars + (u % A2_STAGES), (u / A2_STAGES) & 1u) && lane == 0) atomicAdd(&g_attn_timeouts, 1u);
+    __syncwarp();
+    issue(j + A2_STAGES - 1);  // into the stage the previous tile used
+    const int64_t t0 = t_begin + (int64_t)(warp + j * W) * AT_TILE;
+    const int lim = (int)min((int64_t)AT_TILE, t_end - t0);  // tokens of this tile inside the item
+    // the provisional token (not in the pool) and zeroed V rows past the item's end, so that
+    // stale rows never meet a zero probability as 0 * inf
+    bool patched = false;
+    if (has_new && len >= t0 && len < t0 + AT_TILE) {
+      const int row = (int)(len - t0), ch = lane & 15;
+      const __nv_bfloat16* src = (lane < 16 ? a.k_new : a.v_new) + (r * a.hkv + kvh) * D + ch * 8;
+      unsigned char* box = st + (lane < 16 ? 0 : 2 * A2_BOX) + (ch >> 3) * A2_BOX;
+      *reinterpret_cast<uint4*>(box + a2_swz(row, ch & 7)) = *reinterpret_cast<const uint4*>(src);
+      patched = true;
+    }
+    if (lim < AT_TILE) {
+      for (int e = lane; e < (AT_TILE - lim) * 16; e += 32) {
+        const int row = lim + (e >> 4), ch = e & 15;
+        *reinterpret_cast<uint4*>(st + 2 * A2_BOX + (ch >> 3) * A2_BOX + a2_swz(row, ch & 7)) = make_uint4(0, 0, 0, 0);
+      }
+      patched = true;
+    }
+    if (patched) fence_proxy_async_smem();  // before a later TMA overwrites the stage
+    __syncwarp();
+
+    // ---- S^T = K Q^T: two accumulator chains (even and odd 16-dim steps)
+    float sa[NT][4], sb[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sa[nt][e] = sb[nt][e] = 0.f;
+    {
+      const int tok = (mi & 1) * 8 + rr;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t ka[4];
+        ldmatrix_x4(ka, st + (ks >> 2) * A2_BOX + a2_swz(tok, ((ks & 3) * 2 + (mi >> 1))));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_bf16_16816((ks & 1) ? sb[nt] : sa[nt], ka, qb[nt][ks][0], qb[nt][ks][1]);
+      }
+    }
+    // ---- online softmax per head column (base 2); tokens gq and gq + 8 of heads 2cq, 2cq + 1
+    float alpha[NT][2];
+    uint32_t pb[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float s[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[e] = (gq + (e >> 1) * 8) < lim ? (sa[nt][e] + sb[nt][e]) * scale2 : -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        float mx = fmaxf(s[i], s[2 + i]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(mrow[nt][i], mx);
+        alpha[nt][i] = (mrow[nt][i] == -INFINITY) ? 0.f : exp2f(mrow[nt][i] - m_new);
+        const float p0 = (m_new == -INFINITY) ? 0.f : exp2f(s[i] - m_new);
+        const float p1 = (m_new == -INFINITY) ? 0.f : exp2f(s[2 + i] - m_new);
+        s[i] = p0;
+        s[2 + i] = p1;
+        lrow[nt][i] = lrow[nt][i] * alpha[nt][i] + (p0 + p1);  // this lane's tokens only
+        mrow[nt][i] = m_new;
+      }
+      // P^T as the B operand: transpose the two 8x8 (tokens x heads) blocks
+      movmatrix_trans(pb[nt][0], pack_bf16x2(s[0], s[1]));
+      movmatrix_trans(pb[nt][1], pack_bf16x2(s[2], s[3]));
+    }
+    bool moved = false;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) moved |= alpha[nt][0] != 1.f || alpha[nt][1] != 1.f;
+    if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          o[mt][nt][0] *= alpha[nt][0];
+          o[mt][nt][1] *= alpha[nt][1];
+          o[mt][nt][2] *= alpha[nt][0];
+          o[mt][nt][3] *= alpha[nt][1];
+        }
+    }
+    // ---- O^T += V^T P^T
+    {
+      const int tok = (mi >> 1) * 8 + rr;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        uint32_t va[4];
+        ldmatrix_x4_trans(va, st + 2 * A2_BOX + (mt >> 2) * A2_BOX + a2_swz(tok, ((mt & 3) * 2 + (mi & 1))));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_bf16_16816(o[mt][nt], va, pb[nt][0], pb[nt][1]);
+      }
+    }
+    __syncwarp();  // every lane is done with the stage before it is requested again
+  }
+  seq = seq0 + (uint32_t)nmine;
+  // row sums over the 8 token lanes of each head
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      lrow[nt][i] += __shfl_xor_sync(0xffffffffu, lrow[nt][i], 4);
+      lrow[nt][i] += __shfl_xor_sync(0xffffffffu, lrow[nt][i], 8);
+      lrow[nt][i] += __shfl_xor_sync(0xffffffffu, lrow[nt][i], 16);
+    }
+  __syncthreads();  // every warp is done with its ring: the space becomes the merge area
+
+  // ---- merge the W warp states per head in warp order (layout of am_item)
+  {
+    float* mine = mb + (size_t)warp * 16 * (2 + D);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int h = nt * 8 + 2 * cq + i;
+        if (gq == 0) {
+          mine[h * (2 + D)] = mrow[nt][i];
+          mine[h * (2 + D) + 1] = lrow[nt][i];
+        }
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          mine[h * (2 + D) + 2 + mt * 16 + gq] = o[mt][nt][i];
+          mine[h * (2 + D) + 2 + mt * 16 + gq + 8] = o[mt][nt][2 + i];
+        }
+      }
+  }
+  __syncthreads();
+  float* wts = mb + (size_t)W * 16 * (2 + D);  // [W][16]
+  float* hstat = wts + (size_t)W * 16;         // [16] max, [16] sum
+  if (tid < group) {
+    const int h = tid;
+    float mx = -INFINITY;
+    for (int w = 0; w < W; ++w) mx = fmaxf(mx, mb[((size_t)w * 16 + h) * (2 + D)]);
+    float l = 0.f;
+    for (int w = 0; w < W; ++w) {
+      const float* sw = mb + ((size_t)w * 16 + h) * (2 + D);
+      const float wt = (sw[0] == -INFINITY) ? 0.f : exp2f(sw[0] - mx);
+      wts[w * 16 + h] = wt;
+      l = fmaf(sw[1], wt, l);
+    }
+    hstat[h] = mx;
+    hstat[16 + h] = l;
+  }
+  __syncthreads();
+  float* part_base = nparts > 1 ? a.part + slot * (int64_t)group * (2 + D) : nullptr;
+  for (int idx = tid; idx < group * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx - h * D;
+    const float mx = hstat[h], l = hstat[16 + h];
+    float acc = 0.f;
+    for (int w = 0; w < W; ++w) acc = fmaf(mb[((size_t)w * 16 + h) * (2 + D) + 2 + d], wts[w * 16 + h], acc);
+    if (nparts == 1) {
+      a.out[(r * a.hq + (int64_t)kvh * group + h) * D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+    } else {
+      float* pp = part_base + (int64_t)h * (2 + D);
+      pp[2 + d] = acc;
+      if (d == 0) {
+        pp[0] = mx;
+        pp[1] = l;
+      }
+    }
+  }
+  fence_proxy_async_smem();  // the merge area is written generically; TMA refills it next
+  __syncthreads();
+  if (nparts == 1) return;
+  __threadfence();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&a.counters[rh], 1u);
+    is_last = prev == (unsigned)(nparts - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // ---- last of the group's items: warps merge the heads over the partials in slot order
+  constexpr int VD = D / 32;
+  const int64_t sstride = (int64_t)group * (2 + D);
+  for (int h = warp; h < group; h += W) {
+    const float* base = a.part + (slot0 * group + h) * (2 + D);
+    float mx_all = -INFINITY;
+    for (int s0 = lane; s0 < nparts; s0 += 32) mx_all = fmaxf(mx_all, __ldcg(base + s0 * sstride));
+    mx_all = warp_max(mx_all);
+    float lsum = 0.f, ov[VD];
+#pragma unroll
+    for (int i = 0; i < VD; ++i) ov[i] = 0.f;
+    for (int s0 = 0; s0 < nparts; s0 += 8) {
+      float ms[8], ls[8], av[8][VD];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const bool ok = s0 + jj < nparts;
+        const float* pp = base + (s0 + jj) * sstride;
+        ms[jj] = ok ? __ldcg(pp) : -INFINITY;
+        ls[jj] = ok ? __ldcg(pp + 1) : 0.f;
+#pragma unroll
+        for (int i = 0; i < VD; ++i) av[jj][i] = ok ? __ldcg(pp + 2 + lane * VD + i) : 0.f;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const float wt = (ms[jj] == -INFINITY) ? 0.f : exp2f(ms[jj] - mx_all);
+        lsum = fmaf(ls[jj], wt, lsum);
+#pragma unroll
+        for (int i = 0; i < VD; ++i) ov[i] = fmaf(av[jj][i], wt, ov[i]);
+      }
+    }
+    __nv_bfloat16* out = a.out + (r * a.hq + (int64_t)kvh * group + h) * D + lane * VD;
+#pragma unroll
+    for (int i = 0; i < VD; ++i) out[i] = __float2bfloat16_rn(lsum > 0.f ? ov[i] / lsum : 0.f);
+  }
+  __syncthreads();
+  if (tid == 0) a.counters[rh] = 0u;  // ready for the next launch (graph replays)
+}
+
+template <bool BALANCED, int NT>
+__global__ void __launch_bounds__(AM_MAX_WARPS * 32, AT_MMA_CTAS_PER_SM)
+    paged_attention_tma_kernel(const __grid_constant__ AttnArgs a) {
+  __shared__ __align__(8) uint64_t bars[AM_MAX_WARPS * A2_STAGES];
+  extern __shared__ __align__(16) unsigned char am_smem[];
+  const int warp = threadIdx.x >> 5;
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(am_smem) + 1023) & ~uintptr_t(1023));
+  if (threadIdx.x == 0)
+    for (int i = 0; i < AM_MAX_WARPS * A2_STAGES; ++i) mbar_init(&bars[i], 1);
+  fence_proxy_async_smem();
+  pdl_launch_dependents();
+  pdl_wait();
+  __syncthreads();
+  unsigned char* ring = base + (size_t)warp * A2_STAGES * A2_STAGE_BYTES;
+  uint32_t seq = 0;
+  attn_schedule<BALANCED>(a, [&](int64_t rh, int64_t lo, int64_t hi, int64_t slot, int64_t slot0, int nparts) {
+    a2_item<NT>(a, ring, bars + warp * A2_STAGES, seq, reinterpret_cast<float*>(base), rh, lo, hi, slot, slot0,
+                nparts);
+  });
+  // every requested tile was waited for; after a timed-out wait, wait (bounded) once more for
+  // the last tile of each stage so that no copy is still landing when the CTA exits
+  for (uint32_t u = seq >= A2_STAGES ? seq - A2_STAGES : 0; u < seq; ++u)
+    mbar_wait_bounded(bars + warp * A2_STAGES + (u % A2_STAGES), (u / A2_STAGES) & 1u);
+}
+
+// ---- warp-granular schedule of the TMA kernel
+//
+// The groups' tiles, laid end to end (group-major, as attn_schedule lays them), are cut into
+// one contiguous range per warp: warp w of NW = min(warps launched, T) takes tiles
+// [w*T/NW, (w+1)*T/NW). A warp walks its range with one ring that runs on across group
+// boundaries (no block barrier, no pipeline restart), keeps one online-softmax state per
+// group segment, and at a segment's end either writes the output (the group lies inside its
+// range) or publishes the partial in slot w + rh (the staircase argument of attn_schedule,
+// per warp). paged_attention_merge_kernel then merges each cut group's partials in warp
+// order (deterministic). Measured reason: per-CTA items paid a block-wide merge, a fence and
+// an atomic per item and restarted the ring at every item; their slowest CTAs set the time.
+
+// Tiles before each row (all kv heads) in pre[0..rows]; returns T. Whole CTA; ends synced.
+__device__ __forceinline__ int64_t attn_row_prefix(const AttnArgs& a, int* pre) {
+  const int R = (int)a.rows, hkv = (int)a.hkv;
+  const int tid = threadIdx.x, lane = tid & 31;
+  for (int r = tid; r < R; r += blockDim.x) pre[r + 1] = am_row_tiles(a, r) * hkv;
+  if (tid == 0) pre[0] = 0;
+  __syncthreads();
+  if (tid < 32) {
+    int carry = 0;
+    for (int b = 1; b <= R; b += 32) {
+      int v = b + lane <= R ? pre[b + lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+      }
+      if (b + lane <= R) pre[b + lane] = v + carry;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  return pre[R];
+}
+
+// the largest r with pre[r] <= x (pre[0] = 0 <= x < pre[R])
+__device__ __forceinline__ int attn_row_of(const int* pre, int R, int64_t x) {
+  int lo = 0, hi = R;
+  while (hi - lo > 1) {
+    const int m = (lo + hi) >> 1;
+    if (pre[m] <= x) lo = m; else hi = m;
+  }
+  return lo;
+}
+
+// Position in the flattened tile order: row r, kv head kvh, tile toff of the group; tr =
+// tiles per group of row r; rowstart = tiles before row r. Advancing moves to the next tile.
+struct AttnCursor {
+  int r, kvh, toff, tr;
+  int64_t rowstart;
+  __device__ __forceinline__ void seek(const AttnArgs& a, const int* pre, int64_t x) {
+    r = attn_row_of(pre, (int)a.rows, x);
+    rowstart = pre[r];
+    tr = (pre[r + 1] - pre[r]) / (int)a.hkv;
+    kvh = (int)((x - rowstart) / tr);
+    toff = (int)(x - rowstart - (int64_t)kvh * tr);
+  }
+  __device__ __forceinline__ void next(const AttnArgs& a, bool more) {
+    if (++toff < tr) return;
+    toff = 0;
+    if (++kvh < (int)a.hkv) return;
+    kvh = 0;
+    rowstart += (int64_t)a.hkv * tr;
+    ++r;
+    if (more) tr = am_row_tiles(a, r);
+  }
+};
+
+template <int NT>
+__global__ void __launch_bounds__(AM_MAX_WARPS * 32, AT_MMA_CTAS_PER_SM)
+    paged_attention_tma_warp_kernel(const __grid_constant__ AttnArgs a) {
+  constexpr int D = 128;
+  __shared__ __align__(8) uint64_t bars[AM_MAX_WARPS * A2_STAGES];
+  extern __shared__ __align__(16) unsigned char am_smem[];
+  const int W = blockDim.x >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, cq = lane & 3, mi = lane >> 3, rr = lane & 7;
+  const int group = (int)(a.hq / a.hkv);
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(am_smem) + 1023) & ~uintptr_t(1023));
+  if (tid == 0)
+    for (int i = 0; i < AM_MAX_WARPS * A2_STAGES; ++i) mbar_init(&bars[i], 1);
+  fence_proxy_async_smem();
+  pdl_launch_dependents();
+  pdl_wait();
+  int* pre = reinterpret_cast<int*>(am_smem);  // the rows' tile prefix, until the rings start
+  const int64_t T = attn_row_prefix(a, pre);
+  const int64_t NW = min((int64_t)gridDim.x * W, T);
+  const int64_t gw = (int64_t)blockIdx.x * W + warp;
+  const int64_t lo = gw < NW ? gw * T / NW : 0, hi = gw < NW ? (gw + 1) * T / NW : 0;
+  AttnCursor ci, cc;  // issue and consume positions
+  if (gw < NW) {
+    ci.seek(a, pre, lo);
+    cc = ci;
+  }
+  __syncthreads();  // the prefix is read: the space becomes the rings
+  if (gw >= NW) return;
+  const int n = (int)(hi - lo);
+  unsigned char* ring = base + (size_t)warp * A2_STAGES * A2_STAGE_BYTES;
+  uint64_t* wbars = bars + warp * A2_STAGES;
+  const bool has_new = a.k_new != nullptr;
+  const float scale2 = a.scale * 1.4426950408889634f;  // exp(x s) = exp2(x s log2(e))
+
+  // ---- issue side: page numbers of 32 consecutive tiles of one row, one per lane
+  int tbl = 0, tbl_row = -1, tbl_base = 0;
+  int64_t len_i = 0, seq_i = 0;
+  int len_row = -1;
+  auto issue = [&](int k) {  // the k-th tile of the range (whole warp; lane 0 requests)
+    if (k >= n) return;
+    if (len_row != ci.r) {
+      len_row = ci.r;
+      len_i = a.row_len[ci.r];
+      seq_i = a.row_seq ? a.row_seq[ci.r] : ci.r;
+    }
+    if (tbl_row != ci.r || ci.toff < tbl_base || ci.toff >= tbl_base + A2_TBL) {
+      tbl_row = ci.r;
+      tbl_base = ci.toff;
+      const int64_t t0 = (int64_t)(tbl_base + lane) * AT_TILE;
+      tbl = t0 < len_i ? a.block_table[seq_i * a.bt_stride + t0 / a.page_size] : 0;
+    }
+    const int page = __shfl_sync(0xffffffffu, tbl, ci.toff - tbl_base);
+    if (lane == 0) {
+      unsigned char* st = ring + (k % A2_STAGES) * A2_STAGE_BYTES;
+      uint64_t* bar = wbars + (k % A2_STAGES);
+      const int64_t t0 = (int64_t)ci.toff * AT_TILE;
+      if (t0 < len_i) {
+        const int y = (int)(((int64_t)page * a.hkv + ci.kvh) * a.page_size + (t0 % a.page_size));
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(bar, A2_STAGE_BYTES);
+        tma_load_2d(st, &a.kmap, 0, y, bar);
+        tma_load_2d(st + A2_BOX, &a.kmap, 64, y, bar);
+        tma_load_2d(st + 2 * A2_BOX, &a.vmap, 0, y, bar);
+        tma_load_2d(st + 3 * A2_BOX, &a.vmap, 64, y, bar);
+      } else {
+        mbar_arrive(bar);
+      }
+    }
+    ci.next(a, k + 1 < n);
+  };
+#pragma unroll
+  for (int k = 0; k < A2_STAGES - 1; ++k) issue(k);
+
+  // ---- consume side: one online-softmax state per group segment
+  uint32_t qb[NT][D / 16][2];
+  float o[D / 16][NT][4];
+  float mrow[NT][2], lrow[NT][2];
+  int64_t len_c = 0;
+  int seg_toff0 = 0;
+  unsigned* meta = a.meta;  // per group: (first partial slot << 16) | partials, for the merge
+  for (int k = 0; k < n; ++k) {
+    const bool seg_start = k == 0 || cc.toff == 0;
+    if (seg_start) {  // a new group: its queries and row length, state reset
+      seg_toff0 = cc.toff;
+      len_c = a.row_len[cc.r];
+      const __nv_bfloat16* q0 = a.q + ((int64_t)cc.r * a.hq + (int64_t)cc.kvh * group) * D;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int h = nt * 8 + gq;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const int d0 = ks * 16 + 2 * cq;
+          qb[nt][ks][0] = h < group ? *reinterpret_cast<const uint32_t*>(q0 + h * D + d0) : 0u;
+          qb[nt][ks][1] = h < group ? *reinterpret_cast<const uint32_t*>(q0 + h * D + d0 + 8) : 0u;
+        }
+        mrow[nt][0] = mrow[nt][1] = -INFINITY;
+        lrow[nt][0] = lrow[nt][1] = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.f;
+      }
+    }
+    unsigned char* st = ring + (k % A2_STAGES) * A2_STAGE_BYTES;
+    if (!mbar_wait_bounded(wbars + (k % A2_STAGES), ((uint32_t)k / A2_STAGES) & 1u) && lane == 0)
+      atomicAdd(&g_attn_timeouts, 1u);
+    __syncwarp();
+    issue(k + A2_STAGES - 1);
+    const int64_t total = len_c + (has_new ? 1 : 0);
+    const int64_t t0 = (int64_t)cc.toff * AT_TILE;
+    const int lim = (int)min((int64_t)AT_TILE, total - t0);
+    bool patched = false;
+    if (has_new && len_c >= t0 && len_c < t0 + AT_TILE) {
+      const int row = (int)(len_c - t0), ch = lane & 15;
+      const __nv_bfloat16* src = (lane < 16 ? a.k_new : a.v_new) + ((int64_t)cc.r * a.hkv + cc.kvh) * D + ch * 8;
+      unsigned char* box = st + (lane < 16 ? 0 : 2 * A2_BOX) + (ch >> 3) * A2_BOX;
+      *reinterpret_cast<uint4*>(box + a2_swz(row, ch & 7)) = *reinterpret_cast<const uint4*>(src);
+      patched = true;
+    }
+    if (lim < AT_TILE) {
+      for (int e = lane; e < (AT_TILE - lim) * 16; e += 32) {
+        const int row = lim + (e >> 4), ch = e & 15;
+        *reinterpret_cast<uint4*>(st + 2 * A2_BOX + (ch >> 3) * A2_BOX + a2_swz(row, ch & 7)) = make_uint4(0, 0, 0, 0);
+      }
+      patched = true;
+    }
+    if (patched) fence_proxy_async_smem();
+    __syncwarp();
+    // ---- S^T = K Q^T
+    float sa[NT][4], sb[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sa[nt][e] = sb[nt][e] = 0.f;
+    {
+      const int tok = (mi & 1) * 8 + rr;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t ka[4];
+        ldmatrix_x4(ka, st + (ks >> 2) * A2_BOX + a2_swz(tok, ((ks & 3) * 2 + (mi >> 1))));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_bf16_16816((ks & 1) ? sb[nt] : sa[nt], ka, qb[nt][ks][0], qb[nt][ks][1]);
+      }
+    }
+    // ---- online softmax per head column (base 2)
+    float alpha[NT][2];
+    uint32_t pb[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float sv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sv[e] = (gq + (e >> 1) * 8) < lim ? (sa[nt][e] + sb[nt][e]) * scale2 : -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        float mx = fmaxf(sv[i], sv[2 + i]);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(mrow[nt][i], mx);
+        alpha[nt][i] = (mrow[nt][i] == -INFINITY) ? 0.f : exp2f(mrow[nt][i] - m_new);
+        const float p0 = (m_new == -INFINITY) ? 0.f : exp2f(sv[i] - m_new);
+        const float p1 = (m_new == -INFINITY) ? 0.f : exp2f(sv[2 + i] - m_new);
+        sv[i] = p0;
+        sv[2 + i] = p1;
+        lrow[nt][i] = lrow[nt][i] * alpha[nt][i] + (p0 + p1);
+        mrow[nt][i] = m_new;
+      }
+      movmatrix_trans(pb[nt][0], pack_bf16x2(sv[0], sv[1]));
+      movmatrix_trans(pb[nt][1], pack_bf16x2(sv[2], sv[3]));
+    }
+    bool moved = false;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) moved |= alpha[nt][0] != 1.f || alpha[nt][1] != 1.f;
+    if (__any_sync(0xffffffffu, moved)) {
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          o[mt][nt][0] *= alpha[nt][0];
+          o[mt][nt][1] *= alpha[nt][1];
+          o[mt][nt][2] *= alpha[nt][0];
+          o[mt][nt][3] *= alpha[nt][1];
+        }
+    }
+    // ---- O^T += V^T P^T
+    {
+      const int tok = (mi >> 1) * 8 + rr;
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        uint32_t va[4];
+        ldmatrix_x4_trans(va, st + 2 * A2_BOX + (mt >> 2) * A2_BOX + a2_swz(tok, ((mt & 3) * 2 + (mi & 1))));
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_bf16_16816(o[mt][nt], va, pb[nt][0], pb[nt][1]);
+      }
+    }
+    __syncwarp();
+    // ---- segment end: the output, or this warp's partial of the group
+    if (cc.toff + 1 == cc.tr || k + 1 == n) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          lrow[nt][i] += __shfl_xor_sync(0xffffffffu, lrow[nt][i], 4);
+          lrow[nt][i] += __shfl_xor_sync(0xffffffffu, lrow[nt][i], 8);
+          lrow[nt][i] += __shfl_xor_sync(0xffffffffu, lrow[nt][i], 16);
+        }
+      const int64_t rh = (int64_t)cc.r * a.hkv + cc.kvh;
+      const int64_t gstart = cc.rowstart + (int64_t)cc.kvh * cc.tr;
+      const int64_t wf = ((gstart + 1) * NW - 1) / T, wl = ((gstart + cc.tr) * NW - 1) / T;
+      if (seg_toff0 == 0 && lane == 0) meta[rh] = (unsigned)((wf + rh) << 16) | (unsigned)(wl - wf + 1);
+      if (wf == wl) {
+        __nv_bfloat16* out = a.out + ((int64_t)cc.r * a.hq + (int64_t)cc.kvh * group) * D;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int h = nt * 8 + 2 * cq + i;
+            if (h >= group) continue;
+            const float inv = lrow[nt][i] > 0.f ? 1.f / lrow[nt][i] : 0.f;
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+              out[h * D + mt * 16 + gq] = __float2bfloat16_rn(o[mt][nt][i] * inv);
+              out[h * D + mt * 16 + gq + 8] = __float2bfloat16_rn(o[mt][nt][2 + i] * inv);
+            }
+          }
+      } else {
+        float* part = a.part + (gw + rh) * (int64_t)group * (2 + D);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int h = nt * 8 + 2 * cq + i;
+            if (h >= group) continue;
+            float* ph = part + (int64_t)h * (2 + D);
+            if (gq == 0) {
+              ph[0] = mrow[nt][i];
+              ph[1] = lrow[nt][i];
+            }
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+              ph[2 + mt * 16 + gq] = o[mt][nt][i];
+              ph[2 + mt * 16 + gq + 8] = o[mt][nt][2 + i];
+            }
+          }
+      }
+    }
+    cc.next(a, k + 1 < n);
+  }
+  // every requested tile was waited for; after a timed-out wait, wait (bounded) once more for
+  // the last tile of each stage so that no copy is still landing when the warp exits
+  for (int k = n > A2_STAGES ? n - A2_STAGES : 0; k < n; ++k)
+    mbar_wait_bounded(wbars + (k % A2_STAGES), ((uint32_t)k / A2_STAGES) & 1u);
+}
+
+// The merge after paged_attention_tma_warp_kernel: CTA rh (one warp per query head) merges
+// the partials of group rh in slot order when the attention kernel cut the group (its
+// per-group record says where they are); whole groups were written by their warp. Up to 16
+// partials' loads are in flight at once, folded into a running maximum and sum.
+__global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_attention_merge_kernel(const __grid_constant__ AttnArgs a) {
+  constexpr int D = 128, VD = D / 32, CH = 16;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t rh = blockIdx.x;
+  const unsigned meta = a.meta[rh];
+  const int nparts = (int)(meta & 0xffffu);
+  if (nparts <= 1) return;
+  const int64_t slot0 = meta >> 16;
+  const int group = (int)(a.hq / a.hkv);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = rh / a.hkv, kvh = rh - r * a.hkv;
+  const int64_t sstride = (int64_t)group * (2 + D);
+  for (int h = warp; h < group; h += blockDim.x >> 5) {
+    const float* base = a.part + (slot0 * group + h) * (2 + D);
+    float M = -INFINITY, L = 0.f, acc[VD];
+#pragma unroll
+    for (int i = 0; i < VD; ++i) acc[i] = 0.f;
+    for (int s0 = 0; s0 < nparts; s0 += CH) {
+      float ms[CH], ls[CH];
+      float2 av[CH][VD / 2];
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const bool ok = s0 + j < nparts;
+        const float* pp = base + (int64_t)(s0 + j) * sstride;
+        const float2 st = ok ? *reinterpret_cast<const float2*>(pp) : make_float2(-INFINITY, 0.f);
+        ms[j] = st.x;
+        ls[j] = st.y;
+#pragma unroll
+        for (int i = 0; i < VD / 2; ++i)
+          av[j][i] = ok ? *reinterpret_cast<const float2*>(pp + 2 + lane * VD + 2 * i) : make_float2(0.f, 0.f);
+      }
+      float cm = M;
+#pragma unroll
+      for (int j = 0; j < CH; ++j) cm = fmaxf(cm, ms[j]);
+      if (cm != M && M != -INFINITY) {  // rescale what was folded under the old maximum
+        const float f = exp2f(M - cm);
+        L *= f;
+#pragma unroll
+        for (int i = 0; i < VD; ++i) acc[i] *= f;
+      }
+      M = cm;
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        const float wt = (ms[j] == -INFINITY) ? 0.f : exp2f(ms[j] - M);
+        L = fmaf(ls[j], wt, L);
+#pragma unroll
+        for (int i = 0; i < VD / 2; ++i) {
+          acc[2 * i] = fmaf(av[j][i].x, wt, acc[2 * i]);
+          acc[2 * i + 1] = fmaf(av[j][i].y, wt, acc[2 * i + 1]);
+        }
+      }
+    }
+    __nv_bfloat16* out = a.out + (r * a.hq + kvh * group + h) * D + lane * VD;
+#pragma unroll
+    for (int i = 0; i < VD; ++i) out[i] = __float2bfloat16_rn(L > 0.f ? acc[i] / L : 0.f);
+  }
 }
 
 // The fused decode step (rope_append_attention_kernel's prologue and cluster merge) around
@@ -1466,17 +2320,55 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_prefill_attention_ker
 
 static bool use_mma(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_dim);
 
-// Launch the decode attention for a checked AttnArgs planned with plan_splits: the
-// tensor-core kernel when use_mma selects it, else the scalar kernel.
-static int launch_attention(const AttnArgs& a, int64_t head_dim, int64_t max_total, cudaStream_t s) {
-  dim3 grid((unsigned)(a.rows * a.hkv), (unsigned)a.nsplit);
-  if (use_mma(a.rows, a.hkv, max_total, head_dim)) {
-    const int warps = std::min(AM_MAX_WARPS, std::max(1, a.tiles_per_split));
-    const size_t smem = am_smem_bytes(warps);
-    const int st = ensure_dynamic_smem((const void*)paged_attention_mma_kernel, am_smem_bytes(AM_MAX_WARPS),
-                                       "paged_attention");
+// Launch the decode attention for a checked AttnArgs planned with plan_splits: the TMA
+// kernel for the canonical paged pool ([pages, Hkv, page_size, 128], page size a multiple of
+// 16) where use_mma selects the tensor pipe, the ldmatrix/cp.async tensor-core kernel for
+// other layouts there, else the scalar kernel.
+static int launch_attention(AttnArgs a, int64_t head_dim, int64_t max_total, cudaStream_t s) {
+  const bool canonical = head_dim == 128 && a.hq / a.hkv <= 16 && a.page_size % AT_TILE == 0 &&
+                         a.stride_tok == 128 && a.stride_head == a.page_size * 128 &&
+                         a.stride_page == a.hkv * a.page_size * 128;
+  if (canonical && use_mma(a.rows, a.hkv, max_total, head_dim)) {
+    // the pool as rows of 128 dims; its page count is not passed, so the map spans the
+    // largest row index a TMA coordinate can name and the block table bounds the reads (as it
+    // does for the copy-based kernels)
+    const int64_t rows = 0x7fffffffLL;
+    int st = encode_map_2d(&a.kmap, a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 128, AT_TILE, 64,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!st)
+      st = encode_map_2d(&a.vmap, a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, 128, AT_TILE, 64,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    launch_kernel(paged_attention_mma_kernel, grid, dim3(32 * warps), smem, s, true, a);
+    a.tma = 1;
+  }
+  dim3 grid((unsigned)(a.rows * a.hkv), (unsigned)a.nsplit);
+  if (a.bal_ctas > 0) grid = dim3((unsigned)a.bal_ctas);
+  if (a.tma && a.warp_sched && a.bal_ctas > 0) {
+    const bool two = a.hq / a.hkv > 8;
+    auto kern = two ? paged_attention_tma_warp_kernel<2> : paged_attention_tma_warp_kernel<1>;
+    const size_t smem = a2_smem_bytes(AM_MAX_WARPS);
+    const int st = ensure_dynamic_smem((const void*)kern, smem, "paged_attention");
+    if (st) return st;
+    launch_kernel(kern, dim3((unsigned)a.bal_ctas), dim3(32 * AM_MAX_WARPS), smem, s, true, a);
+    const int rc = launch_status("paged_attention");
+    if (rc) return rc;
+    launch_kernel(paged_attention_merge_kernel, dim3((unsigned)(a.rows * a.hkv)), dim3((unsigned)(32 * (a.hq / a.hkv))), 0,
+                  s, true, a);
+  } else if (a.tma) {
+    const bool two = a.hq / a.hkv > 8;
+    auto kern = a.bal_ctas > 0 ? (two ? paged_attention_tma_kernel<true, 2> : paged_attention_tma_kernel<true, 1>)
+                               : (two ? paged_attention_tma_kernel<false, 2> : paged_attention_tma_kernel<false, 1>);
+    const size_t smem = a2_smem_bytes(AM_MAX_WARPS);
+    const int st = ensure_dynamic_smem((const void*)kern, smem, "paged_attention");
+    if (st) return st;
+    launch_kernel(kern, grid, dim3(32 * AM_MAX_WARPS), smem, s, true, a);
+  } else if (a.bal_ctas > 0 || use_mma(a.rows, a.hkv, max_total, head_dim)) {
+    const int warps = a.bal_ctas > 0 ? AM_MAX_WARPS : std::min(AM_MAX_WARPS, std::max(1, a.tiles_per_split));
+    const size_t smem = am_smem_bytes(warps);
+    auto kern = a.bal_ctas > 0 ? paged_attention_mma_kernel<true> : paged_attention_mma_kernel<false>;
+    const int st = ensure_dynamic_smem((const void*)kern, am_smem_bytes(AM_MAX_WARPS), "paged_attention");
+    if (st) return st;
+    launch_kernel(kern, grid, dim3(32 * warps), smem, s, true, a);
   } else {
     launch_kernel(head_dim == 128 ? paged_attention_kernel<128> : paged_attention_kernel<64>, grid,
                   dim3((unsigned)(32 * (a.hq / a.hkv))), 0, s, true, a);
@@ -1487,6 +2379,9 @@ static int launch_attention(const AttnArgs& a, int64_t head_dim, int64_t max_tot
 struct SplitPlan {
   int nsplit;
   int tiles_per_split;
+  int bal_ctas;   // > 0: the balanced schedule over this many CTAs (nsplit, tiles_per_split unused)
+  int max_tiles;  // balanced: tiles per group at most
+  int warp;       // balanced: scratch for one partial slot per warp (the TMA kernel's warp schedule)
 };
 
 // Splits per (row, head): enough CTAs for about 8 per SM (the kernel is latency-bound per
@@ -1502,12 +2397,45 @@ static bool use_mma(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_d
   return head_dim == 128 && rows * hkv * tiles >= 4096;
 }
 
-// The tensor-core kernel wants at least 8 tiles per split: its 4 warps take 2 each, and
-// fewer, longer splits keep the final merge (dependent L2 round trips) short.
-static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total, int64_t head_dim) {
+// The balanced schedule (tensor-core kernel): rows up to this many (each CTA scans their
+// lengths into shared memory once).
+constexpr int64_t AT_BAL_MAX_ROWS = AT_BAL_MAX_ROWS_DEV;
+constexpr int64_t AT_MAX_COUNTERS = 4096;
+// scratch head: merge counters (kept at zero between launches), then the warp schedule's
+// per-group records, each region fixed in size so that a buffer reused across shapes and
+// schedules never finds one where the other lives; the fp32 partials follow
+constexpr size_t AT_COUNTER_BYTES = 2 * AT_MAX_COUNTERS * sizeof(unsigned);
+
+static size_t balanced_bytes(int64_t rows, int64_t hq, int64_t hkv, int64_t d, int64_t units) {
+  return AT_COUNTER_BYTES + (size_t)(units + rows * hkv) * (hq / hkv) * (2 + d) * sizeof(float);
+}
+
+// The tensor-core kernel takes the balanced schedule whenever it can: one resident wave of
+// CTAs (3 per SM) sharing the tiles the rows actually hold, so ragged contexts neither
+// leave splits empty nor add a partial second wave (32 rows x 32/4 heads, contexts
+// U[256,4096]: the fixed splits ran 512 CTAs, the longest row's splits deciding the time).
+// Scratch: counters plus (CTAs + groups) partial slots; under a scratch cap the CTA count
+// shrinks to fit, down to one per SM, else the fixed splits stay.
+// Fixed splits otherwise: the tensor-core kernel wants at least 8 tiles per split (its 4
+// warps take 2 each; fewer, longer splits keep the final merge -- dependent L2 round trips
+// -- short).
+static SplitPlan plan_splits(int64_t rows, int64_t hq, int64_t hkv, int64_t max_total, int64_t head_dim,
+                             size_t scratch_cap = SIZE_MAX) {
   const int64_t tiles = std::max<int64_t>(1, (max_total + AT_TILE - 1) / AT_TILE);
   const int64_t groups = std::max<int64_t>(1, rows * hkv);
   const bool mma = use_mma(rows, hkv, max_total, head_dim);
+  if (mma && rows <= AT_BAL_MAX_ROWS && groups <= AT_MAX_COUNTERS && groups * tiles < (1LL << 31)) {
+    const int64_t ctas = std::min<int64_t>((int64_t)AT_MMA_CTAS_PER_SM * num_sms(), groups * tiles);
+    // one partial slot per warp when the scratch allows (the warp schedule), else per CTA
+    if (balanced_bytes(rows, hq, hkv, head_dim, ctas * AM_MAX_WARPS) <= scratch_cap)
+      return SplitPlan{1, 0, (int)ctas, (int)tiles, 1};
+    const size_t slot = (size_t)(hq / hkv) * (2 + head_dim) * sizeof(float);
+    int64_t fit = ctas;
+    if (balanced_bytes(rows, hq, hkv, head_dim, ctas) > scratch_cap)
+      fit = scratch_cap > AT_COUNTER_BYTES ? (int64_t)((scratch_cap - AT_COUNTER_BYTES) / slot) - groups : 0;
+    if (fit >= std::min<int64_t>(num_sms(), groups * tiles))
+      return SplitPlan{1, 0, (int)std::min(fit, ctas), (int)tiles, 0};
+  }
   // the tensor-core kernel holds 3 CTAs per SM (2-stage rings): aim at one resident wave, so
   // each warp has enough tiles to amortise its prologue and merge (3 measured best of 2-4 at
   // the config-3 and config-4 shapes together)
@@ -1518,16 +2446,15 @@ static SplitPlan plan_splits(int64_t rows, int64_t hkv, int64_t max_total, int64
   tps = std::min<int64_t>(tps, tiles);
   tps = std::max<int64_t>(tps, (tiles + AT_MAX_SPLIT - 1) / AT_MAX_SPLIT);
   const int64_t ns = (tiles + tps - 1) / tps;
-  return SplitPlan{(int)ns, (int)tps};
+  return SplitPlan{(int)ns, (int)tps, 0, 0, 0};
 }
 
-// Workspace layout: AT_MAX_COUNTERS merge counters at offset 0 (fixed, so that a buffer
-// reused across different shapes never finds stale partials where counters live), then the
-// fp32 partials. Splitting only happens for fewer than 8 * SMs (row, head) groups.
-constexpr int64_t AT_MAX_COUNTERS = 4096;
-constexpr size_t AT_COUNTER_BYTES = AT_MAX_COUNTERS * sizeof(unsigned);
-
+// Workspace layout: AT_MAX_COUNTERS merge counters at offset 0, AT_MAX_COUNTERS per-group
+// records after them (both fixed, so that a buffer reused across different shapes never
+// finds stale partials where counters live), then the fp32 partials. Fixed splits only split
+// for fewer than 8 * SMs (row, head) groups.
 static size_t workspace_bytes(int64_t rows, int64_t hq, int64_t hkv, int64_t d, const SplitPlan& p) {
+  if (p.bal_ctas > 0) return balanced_bytes(rows, hq, hkv, d, (int64_t)p.bal_ctas * (p.warp ? AM_MAX_WARPS : 1));
   if (p.nsplit <= 1) return 0;
   const int64_t group = hq / hkv;
   return AT_COUNTER_BYTES + (size_t)rows * hkv * p.nsplit * group * (2 + d) * sizeof(float);
@@ -1568,10 +2495,17 @@ extern "C" int mrb_rope_kv_append(const void* q_in, const void* k_in, const void
   return launch_status("rope_kv_append");
 }
 
+extern "C" int64_t mrb_paged_attention_timeouts(void) {
+  unsigned v = 0;
+  const cudaError_t e = cudaMemcpyFromSymbol(&v, g_attn_timeouts, sizeof(v));
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "paged_attention_timeouts: %s", cudaGetErrorString(e));
+  return (int64_t)v;
+}
+
 extern "C" size_t mrb_paged_attention_workspace(int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
                                                 int64_t max_total_tokens) {
   if (rows <= 0 || hkv <= 0 || hq % hkv) return 0;
-  return workspace_bytes(rows, hq, hkv, head_dim, plan_splits(rows, hkv, max_total_tokens, head_dim));
+  return workspace_bytes(rows, hq, hkv, head_dim, plan_splits(rows, hq, hkv, max_total_tokens, head_dim));
 }
 
 extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int64_t hkv, int64_t head_dim,
@@ -1595,7 +2529,7 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || (stride_page % 8) || (stride_head % 8) || (stride_tok % 8) ||
       (k_new && !aligned(k_new, 16)))
     return fail(MRB_ERR_ARG, "paged_attention: K/V rows must be 16-byte aligned");
-  const SplitPlan plan = plan_splits(rows, hkv, max_total_tokens, head_dim);
+  const SplitPlan plan = plan_splits(rows, hq, hkv, max_total_tokens, head_dim);
   const size_t need = workspace_bytes(rows, hq, hkv, head_dim, plan);
   if (need > 0 && (workspace == nullptr || workspace_size < need))
     return fail(MRB_ERR_ARG, "paged_attention: workspace of %zu bytes required (got %zu)", need, workspace_size);
@@ -1604,10 +2538,12 @@ extern "C" int mrb_paged_attention(const void* q, int64_t rows, int64_t hq, int6
   AttnArgs a{(const __nv_bfloat16*)q, rows, hq, hkv, (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache,
              stride_page, stride_head, stride_tok, page_size, block_table, block_table_stride, row_seq, row_len,
              (const __nv_bfloat16*)k_new, (const __nv_bfloat16*)v_new, scale, plan.nsplit, plan.tiles_per_split,
-             (__nv_bfloat16*)out, nullptr, nullptr};
+             (__nv_bfloat16*)out, nullptr, nullptr, nullptr, plan.bal_ctas, plan.max_tiles};
+  a.warp_sched = plan.warp;
   if (need > 0) {
     if (rows * hkv > AT_MAX_COUNTERS) return fail(MRB_ERR_UNSUPPORTED, "paged_attention: too many split groups");
     a.counters = (unsigned*)workspace;
+    a.meta = (unsigned*)workspace + AT_MAX_COUNTERS;
     a.part = (float*)((char*)workspace + AT_COUNTER_BYTES);
   }
   return launch_attention(a, head_dim, max_total_tokens, (cudaStream_t)stream);
@@ -1916,7 +2852,7 @@ extern "C" int mrb_paged_attention_static(const void* q, int64_t rows, int64_t h
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || (stride_page % 8) || (stride_head % 8) || (stride_tok % 8) ||
       (k_new && !aligned(k_new, 16)))
     return fail(MRB_ERR_ARG, "paged_attention_static: K/V rows must be 16-byte aligned");
-  const SplitPlan plan = plan_splits(rows, hkv, max_total_tokens, head_dim);
+  const SplitPlan plan = plan_splits(rows, hq, hkv, max_total_tokens, head_dim, MRB_ATTN_STATIC_SCRATCH_BYTES);
   const size_t need = workspace_bytes(rows, hq, hkv, head_dim, plan);
   if (need > MRB_ATTN_STATIC_SCRATCH_BYTES)
     return fail(MRB_ERR_UNSUPPORTED,
@@ -1941,9 +2877,11 @@ extern "C" int mrb_paged_attention_static(const void* q, int64_t rows, int64_t h
   AttnArgs a{(const __nv_bfloat16*)q, rows, hq, hkv, (const __nv_bfloat16*)k_cache, (const __nv_bfloat16*)v_cache,
              stride_page, stride_head, stride_tok, page_size, block_table, block_table_stride, row_seq, row_len,
              (const __nv_bfloat16*)k_new, (const __nv_bfloat16*)v_new, scale, plan.nsplit, plan.tiles_per_split,
-             (__nv_bfloat16*)out, nullptr, nullptr};
+             (__nv_bfloat16*)out, nullptr, nullptr, nullptr, plan.bal_ctas, plan.max_tiles};
+  a.warp_sched = plan.warp;
   if (scratch) {
     a.counters = (unsigned*)scratch;
+    a.meta = (unsigned*)scratch + AT_MAX_COUNTERS;
     a.part = (float*)((char*)scratch + AT_COUNTER_BYTES);
   }
   return launch_attention(a, head_dim, max_total_tokens, (cudaStream_t)stream);

@@ -302,3 +302,111 @@ def test_paged_prefill_attention_vs_oracle(n, start, hq, hkv, cuda):
     dec = cache.attend(0, _bf(q, cuda), rows_len, max_total_tokens=total,
                        row_seq=torch.ones(n, dtype=torch.int32, device=cuda))
     assert max_rel_err(out.float().cpu().numpy(), dec.float().cpu().numpy()) < TOL
+
+
+def _paged_call(cuda, q, pk, pv, table, lengths, max_total, **kw):
+    from mrun_b200.segmented_gqa_decode import paged_attention
+
+    hkv, d = pk.shape[1], pk.shape[3]
+    return paged_attention(
+        _bf(q, cuda), _bf(pk, cuda), _bf(pv, cuda), strides=(hkv * 16 * d, 16 * d, d), page_size=16,
+        block_table=torch.from_numpy(table).to(cuda),
+        row_len=torch.tensor(lengths, dtype=torch.int32, device=cuda), max_total_tokens=max_total, **kw)
+
+
+@pytest.mark.parametrize("rows,hq,hkv,lengths,max_total", [
+    # 32 ragged rows of the routed-MoE decode shape: the tiles of all (row, head) groups
+    # shared by one wave of CTAs, groups cut across CTAs
+    (32, 32, 4, "u256-4096", None),
+    # actual lengths far below the bound: fewer tiles than CTAs (most CTAs have nothing)
+    (4, 32, 4, [1, 5, 16, 33], 8192),
+    # many short groups per CTA (whole groups written directly) next to long ones
+    (96, 32, 8, "u1-200", 4096),
+])
+def test_paged_attention_balanced_schedule(rows, hq, hkv, lengths, max_total, cuda):
+    rng = np.random.default_rng(rows + hq + hkv)
+    if lengths == "u256-4096":
+        lengths = rng.integers(256, 4097, rows).tolist()
+    elif lengths == "u1-200":
+        lengths = rng.integers(1, 201, rows).tolist()
+        lengths[5] = 4000
+    d = 128
+    max_total = max_total or max(lengths)
+    pk, pv, table = _random_paged(rng, rows, hkv, d, lengths, sum((n + 15) // 16 for n in lengths) + 3)
+    q = bf16_round(rng.standard_normal((rows, hq, d)).astype(np.float32))
+    out = _paged_call(cuda, q, pk, pv, table, lengths, max_total)
+    ref = oatt.paged_gqa_decode(q, pk, pv, table, lengths)
+    assert max_rel_err(out.float().cpu().numpy(), ref) < TOL
+    again = _paged_call(cuda, q, pk, pv, table, lengths, max_total)
+    assert torch.equal(out, again)  # merge counters were left at zero; same plan, same bits
+    from mrun_b200 import _lib
+
+    assert int(_lib.load().mrb_paged_attention_timeouts()) == 0  # every bounded stage wait completed
+
+
+def test_paged_attention_empty_row_writes_zeros(cuda):
+    rng = np.random.default_rng(11)
+    rows, hq, hkv, d = 3, 32, 4, 128
+    lengths = [0, 40, 7]
+    pk, pv, table = _random_paged(rng, rows, hkv, d, [max(n, 1) for n in lengths], 8)
+    q = bf16_round(rng.standard_normal((rows, hq, d)).astype(np.float32))
+    out = _paged_call(cuda, q, pk, pv, table, lengths, 8192).float().cpu().numpy()
+    assert not out[0].any()
+    ref = oatt.paged_gqa_decode(q[1:], pk, pv, table[1:], lengths[1:])
+    assert max_rel_err(out[1:], ref) < TOL
+
+
+def test_paged_attention_graph_follows_lengths(cuda):
+    """A captured launch re-plans from row_len on every replay: lengths changed on the device
+    between replays are attended in full, and the merge counters stay consistent."""
+    from mrun_b200.segmented_gqa_decode import paged_attention, paged_attention_workspace_bytes
+
+    rng = np.random.default_rng(5)
+    rows, hq, hkv, d, cap = 16, 32, 4, 128, 2048
+    pk, pv, table = _random_paged(rng, rows, hkv, d, [cap] * rows, rows * cap // 16 + 3)
+    q = _bf(bf16_round(rng.standard_normal((rows, hq, d)).astype(np.float32)), cuda)
+    kd, vd, td = _bf(pk, cuda), _bf(pv, cuda), torch.from_numpy(table).to(cuda)
+    row_len = torch.full((rows,), 16, dtype=torch.int32, device=cuda)
+    out = torch.empty_like(q)
+    ws = torch.zeros(paged_attention_workspace_bytes(rows, hq, hkv, d, cap), dtype=torch.uint8, device=cuda)
+    kw = dict(strides=(hkv * 16 * d, 16 * d, d), page_size=16, block_table=td, row_len=row_len, max_total_tokens=cap,
+              out=out, workspace=ws)
+    stream = torch.cuda.Stream(cuda)
+    stream.wait_stream(torch.cuda.current_stream(cuda))
+    with torch.cuda.stream(stream):
+        paged_attention(q, kd, vd, **kw)
+    torch.cuda.synchronize(cuda)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        paged_attention(q, kd, vd, **kw)
+    qn = q.float().cpu().numpy()
+    for step in range(4):
+        lengths = rng.integers(1, cap + 1, rows).tolist()
+        row_len.copy_(torch.tensor(lengths, dtype=torch.int32))
+        graph.replay()
+        torch.cuda.synchronize(cuda)
+        ref = oatt.paged_gqa_decode(qn, pk, pv, table, lengths)
+        assert max_rel_err(out.float().cpu().numpy(), ref) < TOL, step
+
+
+@pytest.mark.parametrize("lengths", [[1000, 2047, 3000, 15, 16, 31, 32, 2500], [0, 4095, 17, 1023]])
+def test_paged_attention_provisional_token(lengths, cuda):
+    """k_new / v_new: the token at position row_len, held outside the pool, is attended as the
+    last token (tiles that hold only it, tiles it ends), on the tensor-core path."""
+    from mrun_b200.segmented_gqa_decode import paged_attention
+
+    rng = np.random.default_rng(len(lengths))
+    rows, hq, hkv, d = len(lengths), 32, 4, 128
+    pk, pv, table = _random_paged(rng, rows, hkv, d, [max(n, 1) for n in lengths],
+                                  sum((max(n, 1) + 15) // 16 for n in lengths) + 3)
+    q = bf16_round(rng.standard_normal((rows, hq, d)).astype(np.float32))
+    kn = bf16_round(rng.standard_normal((rows, hkv, d)).astype(np.float32))
+    vn = bf16_round(rng.standard_normal((rows, hkv, d)).astype(np.float32))
+    out = paged_attention(
+        _bf(q, cuda), _bf(pk, cuda), _bf(pv, cuda), strides=(hkv * 16 * d, 16 * d, d), page_size=16,
+        block_table=torch.from_numpy(table).to(cuda), row_len=torch.tensor(lengths, dtype=torch.int32, device=cuda),
+        k_new=_bf(kn, cuda), v_new=_bf(vn, cuda), max_total_tokens=max(lengths) + 1)
+    keys = [np.concatenate([oatt.paged_gather(pk, table[r], n), kn[r][None]]) for r, n in enumerate(lengths)]
+    vals = [np.concatenate([oatt.paged_gather(pv, table[r], n), vn[r][None]]) for r, n in enumerate(lengths)]
+    ref = bf16_round(oatt.gqa_decode_rows(q, keys, vals, None))
+    assert max_rel_err(out.float().cpu().numpy(), ref) < TOL

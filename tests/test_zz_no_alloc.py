@@ -90,7 +90,9 @@ def test_static_scratch_rejects_oversized_plans(cuda):
 
     cap = int(_lib.load().mrb_paged_attention_static_capacity())
     # 16-way query groups over 8 KV heads and a long context need more scratch than the array
-    rows, hq, hkv, max_total = 8, 128, 8, 1 << 20
+    # in either schedule: 128 (row, head) groups leave no room for a wave of balanced CTAs
+    # (one partial slot per CTA and per group), and the fixed splits need several per group
+    rows, hq, hkv, max_total = 16, 128, 8, 1 << 20
     need = int(_lib.load().mrb_paged_attention_workspace(rows, hq, hkv, 128, max_total))
     assert need > cap
     # every row maps to one real page and holds one token, so even a launch that the size
@@ -106,3 +108,24 @@ def test_static_scratch_rejects_oversized_plans(cuda):
                   hkv * 16 * 128, 16 * 128, 128, 16, table.data_ptr(), 1, None, row_len.data_ptr(), None, None,
                   0.088, max_total,
                   out.data_ptr(), _lib.stream_handle(cuda))
+
+
+def test_static_scratch_balanced_schedule_under_the_cap(cuda):
+    """The routed-MoE decode shape (32 ragged rows, 32/4 heads): the workspace entry point
+    plans one wave of balanced CTAs whose partial slots exceed the static array; the static
+    entry point plans fewer CTAs to fit and still matches the oracle."""
+    from mrun_b200 import _lib
+
+    rng = np.random.default_rng(44)
+    rows, hq, hkv = 32, 32, 4
+    lengths = rng.integers(256, 4097, rows).tolist()
+    max_total = 4096
+    c = _case(rows, hq, hkv, lengths, 44, cuda)
+    need = int(_lib.load().mrb_paged_attention_workspace(rows, hq, hkv, c["d"], max_total))
+    assert need > int(_lib.load().mrb_paged_attention_static_capacity())
+    out = torch.empty_like(c["q"])
+    args, _ = _args(c, out, max_total)
+    _lib.call("mrb_paged_attention_static", *args, _lib.stream_handle(cuda))
+    torch.cuda.synchronize()
+    oracle = oatt.paged_gqa_decode(*c["np"][:3], c["np"][3], lengths)
+    assert max_rel_err(out.float().cpu().numpy(), oracle) < TOL
