@@ -225,6 +225,23 @@ int mrb_grouped_qrow(const void *x_bf16, const int64_t *row_ids, const int32_t *
                      const int32_t *slot_of, int64_t n, int64_t k, int64_t up_rows, int swiglu,
                      int64_t rows_hint, void *y_bf16, void *stream);
 
+/* The expert MLP of one MoE layer: the gate/up projection with the fused SwiGLU into act_bf16
+ * [A, ffn], then the down projection into y_bf16 [A, hidden], over expert pages laid out as
+ * `ExpertPageLayout` (codes and scales of each part at the given byte offsets inside a page of
+ * page_stride bytes; expert e's page at slot slot_of[e], identity when NULL). Rows as for
+ * mrb_grouped_qrow (row_ids: activation row of each expert-major assignment, NULL = identity).
+ * The down launch starts on an expert as soon as the gate/up launch has stored that expert's
+ * rows: sync is uint32 [2 * experts + 1], zeroed before the first call and left zeroed by each
+ * call (per-expert counters); its last word is set to 1 when a down wait ran out (bounded),
+ * after which the outputs are not to be trusted. Calls that may overlap need their own sync.
+ * Replaces the expert loop of `PagedFP8ExpertBackend.moe` (engine/qwen3_moe_cuda.py:2740-2761). */
+int mrb_grouped_expert_mlp(const void *x_bf16, const int64_t *row_ids, const int32_t *starts,
+                           const int32_t *counts, int64_t experts, const void *pages, int64_t page_stride,
+                           int64_t gate_up_codes_offset, int64_t gate_up_scales_offset,
+                           int64_t down_codes_offset, int64_t down_scales_offset, const int32_t *slot_of,
+                           int64_t hidden, int64_t ffn, int64_t rows_hint, void *act_bf16, void *y_bf16,
+                           uint32_t *sync, void *stream);
+
 /* Fixed-capacity expert-parallel dispatch plan (no reference counterpart: the reference
  * runs every expert on one device). Expert e lives on rank e / experts_per_rank. Each
  * (source, destination) block has `capacity` >= tokens * k slots, so the plan never

@@ -50,6 +50,8 @@ SIGNATURES: dict[str, list] = {
     "mrb_router_qrow_topk": [_P, _I64, _I64, _P, _P, _I64, _I64, c_int, _P, _P, _P, _P, _P, _P],
     "mrb_route_compile": [_P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P],
     "mrb_grouped_qrow": [_P, _P, _P, _P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, c_int, _I64, _P, _P],
+    "mrb_grouped_expert_mlp": [_P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _I64, _I64, _P, _P,
+                               _P, _P],
     "mrb_stable_route_reduce": [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P],
     "mrb_ep_pack": [_P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P],
     "mrb_ep_gather_rows": [_P, _I64, _P, _I64, _P, _P],

@@ -304,6 +304,13 @@ __global__ void __launch_bounds__(RC_THREADS) route_compile_kernel(
 
 // ------------------------------------------------------------------ grouped expert GEMV
 
+// acquire load of a counter another CTA publishes (GPU scope)
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 constexpr int GX_WARPS = 8;
 constexpr int GX_THREADS = GX_WARPS * 32;
 constexpr int GX_ROWS = 16;       // weight rows per warp tile (mma M)
@@ -329,6 +336,16 @@ struct GroupedArgs {
   int chunks;                // tile chunks per expert (work items per expert)
   int chunk_tiles;           // 16-row tiles per chunk
   int maxr;                  // activation rows per pass (<= GX_MAXR; fewer when k is large)
+  // Gate/up -> down overlap (mrb_grouped_expert_mlp): 0 = a lone launch; 1 = the gate/up
+  // launch, which counts finished items per expert in ready[]; 2 = the down launch, which
+  // starts on an expert once ready[e] == ready_target, counts its own items in done[] and,
+  // on an expert's last item, leaves both counters at zero.
+  int overlap;
+  int ready_target;
+  unsigned* ready;
+  unsigned* done;
+  int32_t* error_flag;       // overlap 2: set when a wait gave up
+  int64_t wait_polls;        // overlap 2: bound of one expert's wait
 };
 
 __host__ __device__ inline int gx_steps(int64_t k, bool halves) {
@@ -376,8 +393,17 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
   const int items = a.E * a.chunks;
   const bool k_check = (int64_t)xlen != K;
 
-  pdl_launch_dependents();
-  pdl_wait();  // routes and activations come from the previous kernels
+  if (a.overlap == 1) {
+    // the down launch may start once every CTA here has passed the wait: by then the routes
+    // exist, and it reads gate/up outputs only behind ready[]
+    pdl_wait();
+    pdl_launch_dependents();
+  } else if (a.overlap == 2) {
+    pdl_launch_dependents();  // no grid-wide wait: experts start as their gate/up items finish
+  } else {
+    pdl_launch_dependents();
+    pdl_wait();  // routes and activations come from the previous kernels
+  }
 
   auto item_expert = [&](int item) { return item / a.chunks; };
   auto item_t0 = [&](int item) { return (item - item_expert(item) * a.chunks) * a.chunk_tiles; };
@@ -455,6 +481,16 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
     const int slot = a.slot_of ? a.slot_of[e] : e;
     const float* scales = a.scales + (int64_t)slot * a.scales_stride;
     const int t0 = item_t0(item), t1 = item_t1(item);
+    if (a.overlap == 2 && tid == 0) {  // the expert's activation rows are complete
+      int64_t polls = 0;
+      while (ld_acquire_u32(a.ready + e) < (unsigned)a.ready_target) {
+        if (++polls > a.wait_polls) {
+          if (a.error_flag) atomicExch(a.error_flag, 1);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
     for (int p0 = 0; p0 < cnt; p0 += maxr) {
       const int rows = min(maxr, cnt - p0);
       // ---- stage this pass's activation rows (raw copy + row max, then exact scaled f16)
@@ -466,7 +502,9 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
         const int r = idx / vpr, v = idx - r * vpr;
         const int64_t arow = st0 + p0 + r;
         const int64_t src = a.row_ids ? a.row_ids[arow] : arow;
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(a.x + src * K) + v);
+        // rows written by the overlapping gate/up launch are read through L2 only
+        const uint4 raw = a.overlap == 2 ? __ldcg(reinterpret_cast<const uint4*>(a.x + src * K) + v)
+                                         : __ldg(reinterpret_cast<const uint4*>(a.x + src * K) + v);
         *reinterpret_cast<uint4*>(xs + r * xstride + v * 8) = raw;
         const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
         float mx = 0.f;
@@ -571,6 +609,18 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
               *out = __float2bfloat16_rn((acc[0][nt][i] + acc[1][nt][i]) * rscale[r] * scales[nrow]);
             }
           }
+        }
+      }
+    }
+    if (a.overlap) {  // the item's outputs are stored: publish (gate/up) or retire (down) it
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        if (a.overlap == 1) {
+          atomicAdd(a.ready + e, 1u);
+        } else if (atomicAdd(a.done + e, 1u) + 1u == (unsigned)a.chunks) {
+          a.ready[e] = 0u;  // every down item of this expert has finished: reset for the next call
+          a.done[e] = 0u;
         }
       }
     }
@@ -735,11 +785,14 @@ extern "C" int mrb_route_compile(const int64_t* top_idx, const float* top_w, int
   return launch_status("route_compile");
 }
 
-extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, const int32_t* starts,
-                                const int32_t* counts, int64_t experts, const int8_t* codes, int64_t codes_stride,
-                                const float* scales, int64_t scales_stride, const int32_t* slot_of, int64_t n,
-                                int64_t k, int64_t up_rows, int swiglu, int64_t rows_hint, void* y_bf16,
-                                void* stream) {
+namespace mrb {
+// Checks, plans and launches one grouped projection (see mrb_grouped_qrow); `ov` carries the
+// overlap fields of GroupedArgs (all zero for a lone launch).
+static int grouped_launch(const void* x_bf16, const int64_t* row_ids, const int32_t* starts, const int32_t* counts,
+                          int64_t experts, const int8_t* codes, int64_t codes_stride, const float* scales,
+                          int64_t scales_stride, const int32_t* slot_of, int64_t n, int64_t k, int64_t up_rows,
+                          int swiglu, int64_t rows_hint, void* y_bf16, const GroupedArgs& ov, int* chunks_out,
+                          cudaStream_t s) {
   if (experts <= 0 || n <= 0 || k <= 0) return fail(MRB_ERR_ARG, "grouped_qrow: bad shape");
   if (!x_bf16 || !starts || !counts || !codes || !scales || !y_bf16) return fail(MRB_ERR_ARG, "grouped_qrow: null pointer");
   if (k % 16) return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: in_features %lld is not a multiple of 16", (long long)k);
@@ -754,10 +807,25 @@ extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, cons
   if (smem > 227 * 1024) return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: in_features %lld too large", (long long)k);
   if (experts * ((n + GX_ROWS - 1) / GX_ROWS) > 0x7fffffffLL)
     return fail(MRB_ERR_UNSUPPORTED, "grouped_qrow: too many expert tiles");
-  GroupedArgs a{(const __nv_bfloat16*)x_bf16, row_ids, starts, counts, (int)experts, codes, codes_stride, scales,
-                scales_stride, slot_of, n, k, up_rows, (__nv_bfloat16*)y_bf16, 1, 1, maxr};
+  GroupedArgs a = ov;
+  a.x = (const __nv_bfloat16*)x_bf16;
+  a.row_ids = row_ids;
+  a.starts = starts;
+  a.counts = counts;
+  a.E = (int)experts;
+  a.codes = codes;
+  a.codes_stride = codes_stride;
+  a.scales = scales;
+  a.scales_stride = scales_stride;
+  a.slot_of = slot_of;
+  a.n = n;
+  a.k = k;
+  a.up_rows = up_rows;
+  a.y = (__nv_bfloat16*)y_bf16;
+  a.maxr = maxr;
   // two CTAs per SM when two fit; chunks of whole tiles per warp sized for about two work
-  // items per CTA
+  // items per CTA. The grid never exceeds one resident wave (the overlapped down launch
+  // relies on every gate/up CTA running).
   const int64_t slots = (int64_t)num_sms() * (2 * (smem + 1024) <= 228 * 1024 ? 2 : 1);
   const int64_t rtiles = (n + GX_ROWS - 1) / GX_ROWS;
   const int64_t per_warp = std::max<int64_t>(1, experts * rtiles / (GX_WARPS * 2 * slots));
@@ -766,16 +834,59 @@ extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, cons
   const int64_t fill = std::max<int64_t>(1, (experts * rtiles + slots - 1) / slots);
   a.chunk_tiles = (int)std::min<int64_t>(rtiles, std::min<int64_t>(per_warp * GX_WARPS, fill));
   a.chunks = (int)((rtiles + a.chunk_tiles - 1) / a.chunk_tiles);
+  if (chunks_out) *chunks_out = a.chunks;
   const int64_t grid = std::min<int64_t>(experts * a.chunks, slots);
-  cudaStream_t s = (cudaStream_t)stream;
-  auto run = [&](auto kern, int) -> int {
+  auto run = [&](auto kern) -> int {
     const int smem_st = ensure_dynamic_smem((const void*)kern, smem, "grouped_qrow");
     if (smem_st) return smem_st;
     launch_kernel(kern, dim3((unsigned)grid), dim3(GX_THREADS), smem, s, true, a);
     return launch_status("grouped_qrow");
   };
-  if (maxr > 8) return swiglu ? run(grouped_qrow_kernel<true, 2>, 3) : run(grouped_qrow_kernel<false, 2>, 2);
-  return swiglu ? run(grouped_qrow_kernel<true, 1>, 1) : run(grouped_qrow_kernel<false, 1>, 0);
+  if (maxr > 8) return swiglu ? run(grouped_qrow_kernel<true, 2>) : run(grouped_qrow_kernel<false, 2>);
+  return swiglu ? run(grouped_qrow_kernel<true, 1>) : run(grouped_qrow_kernel<false, 1>);
+}
+
+}  // namespace mrb
+
+extern "C" int mrb_grouped_qrow(const void* x_bf16, const int64_t* row_ids, const int32_t* starts,
+                                const int32_t* counts, int64_t experts, const int8_t* codes, int64_t codes_stride,
+                                const float* scales, int64_t scales_stride, const int32_t* slot_of, int64_t n,
+                                int64_t k, int64_t up_rows, int swiglu, int64_t rows_hint, void* y_bf16,
+                                void* stream) {
+  const GroupedArgs lone{};
+  return grouped_launch(x_bf16, row_ids, starts, counts, experts, codes, codes_stride, scales, scales_stride, slot_of,
+                        n, k, up_rows, swiglu, rows_hint, y_bf16, lone, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int mrb_grouped_expert_mlp(const void* x_bf16, const int64_t* row_ids, const int32_t* starts,
+                                      const int32_t* counts, int64_t experts, const void* pages, int64_t page_stride,
+                                      int64_t gate_up_codes_offset, int64_t gate_up_scales_offset,
+                                      int64_t down_codes_offset, int64_t down_scales_offset, const int32_t* slot_of,
+                                      int64_t hidden, int64_t ffn, int64_t rows_hint, void* act_bf16, void* y_bf16,
+                                      uint32_t* sync, void* stream) {
+  if (experts <= 0 || hidden <= 0 || ffn <= 0 || page_stride <= 0) return fail(MRB_ERR_ARG, "grouped_expert_mlp: bad shape");
+  if (!pages || !act_bf16 || !sync) return fail(MRB_ERR_ARG, "grouped_expert_mlp: null pointer");
+  if ((page_stride % 16) || (gate_up_codes_offset % 16) || (down_codes_offset % 16) || (gate_up_scales_offset % 4) ||
+      (down_scales_offset % 4) || !aligned(sync, 4))
+    return fail(MRB_ERR_ARG, "grouped_expert_mlp: page parts must be aligned (codes 16 B, scales and sync 4 B)");
+  const char* base = (const char*)pages;
+  const cudaStream_t s = (cudaStream_t)stream;
+  GroupedArgs ov{};
+  ov.overlap = 1;
+  ov.ready = sync;
+  ov.done = sync + experts;
+  ov.error_flag = (int32_t*)(sync + 2 * experts);
+  int gu_chunks = 0;
+  int st = grouped_launch(x_bf16, row_ids, starts, counts, experts, (const int8_t*)(base + gate_up_codes_offset),
+                          page_stride, (const float*)(base + gate_up_scales_offset), page_stride / 4, slot_of, ffn,
+                          hidden, ffn, 1, rows_hint, act_bf16, ov, &gu_chunks, s);
+  if (st) return st;
+  ov.overlap = 2;
+  ov.ready_target = gu_chunks;
+  ov.wait_polls = 1LL << 22;  // x ~64 ns: ~0.3 s, far beyond any gate/up launch
+  return grouped_launch(act_bf16, nullptr, starts, counts, experts, (const int8_t*)(base + down_codes_offset),
+                        page_stride, (const float*)(base + down_scales_offset), page_stride / 4, slot_of, hidden, ffn,
+                        0, 0, rows_hint, y_bf16, ov, nullptr, s);
 }
 
 extern "C" int mrb_stable_route_reduce(const void* expert_out_bf16, const float* coef, const int64_t* inverse,

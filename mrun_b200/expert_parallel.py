@@ -239,6 +239,7 @@ class P2PExpertParallelMoE:
         self.slot_src = torch.empty(slots, dtype=torch.int32, device=device)
         self.ids64 = torch.empty((slots, 1), dtype=torch.int64, device=device)
         self.zeros = torch.zeros((slots, 1), dtype=torch.float32, device=device)
+        self.mlp_sync = torch.zeros(2 * shard.per_rank + 1, dtype=torch.int32, device=device)
         dist.barrier(group=group)  # every mailbox exists and is zeroed before any dispatch
 
     def forward(self, source: torch.Tensor, top_indices: torch.Tensor, top_weights: torch.Tensor) -> torch.Tensor:
@@ -265,7 +266,7 @@ class P2PExpertParallelMoE:
         token_ids, _, starts, counts, inverse, _ = grouped_route_tensors_with_inverse(
             self.ids64, self.zeros, num_experts=per + 1)
         eo = _grouped_mlp_from_pointer(self._own + self.offsets[4], token_ids, starts[:per], counts[:per],
-                                       self.pages, self.layout, hidden, device)
+                                       self.pages, self.layout, hidden, device, self.mlp_sync)
         _lib.call("mrb_ep_p2p_return", eo.data_ptr(), inverse.data_ptr(), hidden, world, sh.rank, cap,
                   self.mailboxes.data_ptr(), self.state.data_ptr(), stream)
         _lib.call("mrb_ep_p2p_wait_return", self._own, world, cap, hidden, self.state.data_ptr(), stream)
@@ -275,9 +276,11 @@ class P2PExpertParallelMoE:
         return out
 
     def check(self) -> None:
-        """Raise if a bounded wait of the exchange timed out (synchronises)."""
+        """Raise if a bounded wait of the exchange or of the expert MLP timed out (synchronises)."""
         if int(self.state[3].item()):
             raise RuntimeError("expert-parallel peer exchange timed out waiting for a rank")
+        if int(self.mlp_sync[-1].item()):
+            raise RuntimeError("expert MLP: the down projection timed out waiting for the gate/up projection")
 
     def close(self) -> None:
         from . import _lib
@@ -290,9 +293,11 @@ class P2PExpertParallelMoE:
             self._own = 0
 
 
-def _grouped_mlp_from_pointer(rows_ptr: int, token_ids, starts, counts, pages, layout, hidden: int, device):
+def _grouped_mlp_from_pointer(rows_ptr: int, token_ids, starts, counts, pages, layout, hidden: int, device,
+                              sync: torch.Tensor | None = None):
     """grouped_expert_mlp over activation rows given by a raw device pointer (a mailbox)."""
     from . import _lib
+    from .moe import expert_mlp_sync
 
     ly = layout
     f = ly.intermediate_size
@@ -300,14 +305,12 @@ def _grouped_mlp_from_pointer(rows_ptr: int, token_ids, starts, counts, pages, l
     e = int(counts.numel())
     act = torch.empty((a, f), dtype=torch.bfloat16, device=device)
     y = torch.empty((a, hidden), dtype=torch.bfloat16, device=device)
-    base, stride = pages.data_ptr(), ly.page_stride
-    stream = _lib.stream_handle(device)
-    _lib.call("mrb_grouped_qrow", rows_ptr, token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
-              base + ly.gate_up_codes_offset, stride, base + ly.gate_up_scales_offset, stride // 4, None, f, hidden,
-              f, 1, a, act.data_ptr(), stream)
-    _lib.call("mrb_grouped_qrow", act.data_ptr(), None, starts.data_ptr(), counts.data_ptr(), e,
-              base + ly.down_codes_offset, stride, base + ly.down_scales_offset, stride // 4, None, hidden, f, 0, 0,
-              a, y.data_ptr(), stream)
+    if sync is None:
+        sync = expert_mlp_sync(e, device)
+    _lib.call("mrb_grouped_expert_mlp", rows_ptr, token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
+              pages.data_ptr(), ly.page_stride, ly.gate_up_codes_offset, ly.gate_up_scales_offset,
+              ly.down_codes_offset, ly.down_scales_offset, None, hidden, f, a, act.data_ptr(), y.data_ptr(),
+              sync.data_ptr(), _lib.stream_handle(device))
     return y
 
 

@@ -287,11 +287,15 @@ def grouped_expert_mlp(
     slot_of: torch.Tensor | None = None,
     act_out: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    sync: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Expert-major rows -> bf16 expert outputs [A, H]: gate/up (SwiGLU fused) then down.
 
     ``pages`` is a uint8 buffer of expert pages ``[slots, page_stride]``; expert ``e`` uses
-    slot ``slot_of[e]`` (identity when None)."""
+    slot ``slot_of[e]`` (identity when None). The down launch starts on each expert as soon
+    as its gate/up work is stored, through per-expert counters in ``sync`` (int32 ``[2E + 1]``,
+    zeroed, left zeroed by every call; the last word is set when a wait gave up). Calls that
+    may run at the same time need their own ``sync``."""
     device = _lib.require_cuda(source, token_ids, starts, counts, pages, what="grouped expert MLP")
     ly = layout
     f, h = ly.intermediate_size, ly.hidden_size
@@ -305,13 +309,20 @@ def grouped_expert_mlp(
         return y
     stream = _lib.stream_handle(device)
     src = source.contiguous()
-    _lib.call("mrb_grouped_qrow", src.data_ptr(), token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
-              base + ly.gate_up_codes_offset, stride, base + ly.gate_up_scales_offset, stride // 4,
-              _lib.ptr(slot_of), f, h, f, 1, a, act.data_ptr(), stream)
-    _lib.call("mrb_grouped_qrow", act.data_ptr(), None, starts.data_ptr(), counts.data_ptr(), e,
-              base + ly.down_codes_offset, stride, base + ly.down_scales_offset, stride // 4,
-              _lib.ptr(slot_of), h, f, 0, 0, a, y.data_ptr(), stream)
+    if sync is None:
+        sync = expert_mlp_sync(e, device)
+    elif sync.dtype != torch.int32 or sync.numel() < 2 * e + 1:
+        raise ValueError(f"the expert MLP sync buffer is int32 [2 * experts + 1] = [{2 * e + 1}]")
+    _lib.call("mrb_grouped_expert_mlp", src.data_ptr(), token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
+              base, stride, ly.gate_up_codes_offset, ly.gate_up_scales_offset, ly.down_codes_offset,
+              ly.down_scales_offset, _lib.ptr(slot_of), h, f, a, act.data_ptr(), y.data_ptr(), sync.data_ptr(),
+              stream)
     return y
+
+
+def expert_mlp_sync(experts: int, device: torch.device) -> torch.Tensor:
+    """A zeroed sync buffer for ``grouped_expert_mlp`` over ``experts`` experts."""
+    return torch.zeros(2 * int(experts) + 1, dtype=torch.int32, device=device)
 
 
 # ------------------------------------------------------------------ backends
@@ -353,6 +364,20 @@ class PagedInt8ExpertBackend:
     dtype: torch.dtype = torch.bfloat16
     num_experts: int = 0
     stats: ExpertBackendStats = field(default_factory=ExpertBackendStats)
+    _sync: dict = field(default_factory=dict, repr=False)
+
+    def _sync_for(self, experts: int, device: torch.device) -> torch.Tensor:
+        key = (device.index, experts)
+        if key not in self._sync:
+            self._sync[key] = expert_mlp_sync(experts, device)
+        return self._sync[key]
+
+    def check(self) -> None:
+        """Raise if a down launch gave up waiting for its gate/up work (its output is then not
+        to be trusted)."""
+        for buf in self._sync.values():
+            if int(buf[-1].item()):
+                raise RuntimeError("expert MLP: the down projection timed out waiting for the gate/up projection")
 
     def reset_stats(self, *, clear_pages: bool) -> None:
         self.stats = ExpertBackendStats()
@@ -364,7 +389,7 @@ class PagedInt8ExpertBackend:
         token_ids, coefficients, starts, counts, inverse, _ = grouped_route_tensors_with_inverse(
             top_indices, top_weights.float(), num_experts=self.num_experts)
         expert_output = grouped_expert_mlp(source, token_ids, starts, counts, pages, self.cache.layout,
-                                           slot_of=slot_of)
+                                           slot_of=slot_of, sync=self._sync_for(self.num_experts, source.device))
         out = torch.empty((source.shape[0], source.shape[1]), dtype=torch.bfloat16, device=source.device)
         _lib.call("mrb_stable_route_reduce", expert_output.data_ptr(), coefficients.data_ptr(), inverse.data_ptr(),
                   int(top_indices.shape[0]), int(top_indices.shape[1]), int(source.shape[1]), None, out.data_ptr(),
@@ -388,6 +413,7 @@ __all__ = [
     "PagedInt8ExpertBackend",
     "ResidentInt8ExpertPages",
     "expert_page_views",
+    "expert_mlp_sync",
     "grouped_expert_mlp",
     "grouped_route_tensors",
     "grouped_route_tensors_with_inverse",

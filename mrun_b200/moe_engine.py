@@ -348,6 +348,8 @@ class MoeDecoder:
         for ep in self.ep or []:
             if hasattr(ep, "check"):
                 ep.check()
+        if self.backend is not None:
+            self.backend.check()
 
     def close(self) -> None:
         """Release the captured graph and the peer mailboxes of the expert exchange (call on

@@ -145,3 +145,34 @@ def test_fused_router_matches_projection_and_selection(t, e, k, h, cuda):
     for _ in range(3):
         idx2, w2, _ = router_qrow_topk(x.to(cuda), codes.to(cuda), scales.to(cuda), k)
         assert torch.equal(idx2, idx) and torch.equal(w2, w16)
+
+
+@pytest.mark.parametrize("tokens,k,experts,hidden,ffn", [(64, 4, 32, 512, 384), (32, 8, 128, 2048, 768),
+                                                         (16, 2, 8, 1024, 14336)])
+def test_overlapped_expert_mlp_matches_separate_launches(tokens, k, experts, hidden, ffn, cuda):
+    """mrb_grouped_expert_mlp (the down launch starting on each expert as its gate/up work is
+    stored) gives the bits of the two lone grouped launches, and leaves its counters at zero
+    call after call."""
+    from mrun_b200 import _lib
+    from mrun_b200.moe import expert_mlp_sync, grouped_expert_mlp, grouped_route_tensors_with_inverse, router_topk
+
+    rng = np.random.default_rng(tokens * experts)
+    ly, pages, _ = _expert_pages(rng, experts, hidden, ffn, cuda)
+    x = torch.from_numpy(bf16_round(rng.standard_normal((tokens, hidden)).astype(np.float32))).to(cuda).to(torch.bfloat16)
+    idx, w16, _ = router_topk(torch.from_numpy(rng.standard_normal((tokens, experts)).astype(np.float32)).to(cuda), k)
+    token_ids, _, starts, counts, _, _ = grouped_route_tensors_with_inverse(idx, w16, num_experts=experts)
+    a = int(token_ids.numel())
+    act = torch.empty(a, ffn, dtype=torch.bfloat16, device=cuda)
+    ref = torch.empty(a, hidden, dtype=torch.bfloat16, device=cuda)
+    base, stride, stream = pages.data_ptr(), ly.page_stride, _lib.stream_handle(cuda)
+    _lib.call("mrb_grouped_qrow", x.data_ptr(), token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), experts,
+              base + ly.gate_up_codes_offset, stride, base + ly.gate_up_scales_offset, stride // 4, None, ffn, hidden,
+              ffn, 1, a, act.data_ptr(), stream)
+    _lib.call("mrb_grouped_qrow", act.data_ptr(), None, starts.data_ptr(), counts.data_ptr(), experts,
+              base + ly.down_codes_offset, stride, base + ly.down_scales_offset, stride // 4, None, hidden, ffn, 0, 0,
+              a, ref.data_ptr(), stream)
+    sync = expert_mlp_sync(experts, cuda)
+    for _ in range(3):
+        y = grouped_expert_mlp(x, token_ids, starts, counts, pages, ly, sync=sync)
+        assert torch.equal(y, ref)
+    assert not sync.any()
