@@ -357,7 +357,7 @@ __host__ __device__ inline size_t gx_xs_bytes(int64_t k, bool halves, int maxr) 
   return ((size_t)maxr * (gx_xlen(k, halves) + 8) * 2 + 15) & ~size_t(15);
 }
 __host__ inline size_t gx_smem_bytes(int64_t k, bool halves, int maxr) {
-  return (size_t)GX_STAGES * GX_STAGE_BYTES + gx_xs_bytes(k, halves, maxr) + 64 * 4;  // + rscale[32], rmax[16]
+  return (size_t)GX_STAGES * GX_STAGE_BYTES + gx_xs_bytes(k, halves, maxr) + 64 * 4;  // + rscale[32] (and spare)
 }
 
 // Grouped int8 expert projection over ragged per-expert row counts.
@@ -386,7 +386,6 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
   unsigned char* ring = smem;
   __half* xs = reinterpret_cast<__half*>(smem + (size_t)GX_STAGES * GX_STAGE_BYTES);
   float* rscale = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + gx_xs_bytes(K, HALVES, a.maxr));
-  unsigned* rmax = reinterpret_cast<unsigned*>(rscale + 32);  // [16]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int rtiles = (int)((a.n + GX_ROWS - 1) / GX_ROWS);
@@ -493,54 +492,58 @@ __global__ void __launch_bounds__(GX_THREADS, 2) grouped_qrow_kernel(GroupedArgs
     }
     for (int p0 = 0; p0 < cnt; p0 += maxr) {
       const int rows = min(maxr, cnt - p0);
-      // ---- stage this pass's activation rows (raw copy + row max, then exact scaled f16)
-      __syncthreads();  // every warp is done with the previous pass's rows
-      if (tid < GX_MAXR) rmax[tid] = 0u;
-      __syncthreads();
-      const int vpr = (int)(K / 8);
-      for (int idx = tid; idx < rows * vpr; idx += GX_THREADS) {
-        const int r = idx / vpr, v = idx - r * vpr;
-        const int64_t arow = st0 + p0 + r;
-        const int64_t src = a.row_ids ? a.row_ids[arow] : arow;
-        // rows written by the overlapping gate/up launch are read through L2 only
-        const uint4 raw = a.overlap == 2 ? __ldcg(reinterpret_cast<const uint4*>(a.x + src * K) + v)
-                                         : __ldg(reinterpret_cast<const uint4*>(a.x + src * K) + v);
-        *reinterpret_cast<uint4*>(xs + r * xstride + v * 8) = raw;
-        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
-        float mx = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(__bfloat162float(h[i])));
-        atomicMax(&rmax[r], __float_as_uint(mx));
-      }
-      __syncthreads();
-      if (tid < rows) {
-        const float mx = __uint_as_float(rmax[tid]);
-        int ex = 0, e2 = 0;
-        if (mx > 0.f && isfinite(mx)) {
-          frexpf(mx, &ex);
-          e2 = max(-100, min(100, 15 - ex));  // max * 2^e2 in [2^14, 2^15): exact in f16
-        }
-        rscale[tid] = ldexpf(1.0f, -e2);
-        rscale[16 + tid] = ldexpf(1.0f, e2);
-      }
-      __syncthreads();
-      // pass width: one n8 tile for up to 8 rows, two above (staged rows beyond `rows` are 0)
+      // ---- stage this pass's activation rows as exact power-of-two-scaled f16: one warp per
+      // row -- raw copy into shared memory and the row max by warp shuffles, the scale, then
+      // the conversion in place (each lane converts the vectors it copied); rows past `rows`
+      // and k past K are zero
       const bool two = NT == 2 && rows > 8;
       const int prow = two ? maxr : min(8, maxr);
-      for (int idx = tid; idx < prow * (xlen / 8); idx += GX_THREADS) {
-        const int r = idx / (xlen / 8), v = idx - r * (xlen / 8);
-        uint4* sp = reinterpret_cast<uint4*>(xs + r * xstride + v * 8);
-        __align__(16) __half hv[8];
-        if (r < rows && v * 8 < K) {
-          const uint4 raw = *sp;
-          const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      __syncthreads();  // every warp is done with the previous pass's rows
+      {
+        const int vpr = (int)(K / 8), vlen = xlen / 8;
+        for (int r = warp; r < prow; r += GX_WARPS) {
+          uint4* row = reinterpret_cast<uint4*>(xs + r * xstride);
+          if (r >= rows) {
+            for (int v = lane; v < vlen; v += 32) row[v] = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+          }
+          const int64_t arow = st0 + p0 + r;
+          const int64_t src = a.row_ids ? a.row_ids[arow] : arow;
+          const uint4* xrow = reinterpret_cast<const uint4*>(a.x + src * K);
+          float mx = 0.f;
+          for (int v = lane; v < vpr; v += 32) {
+            // rows written by the overlapping gate/up launch are read through L2 only
+            const uint4 raw = a.overlap == 2 ? __ldcg(xrow + v) : __ldg(xrow + v);
+            row[v] = raw;
+            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(__bfloat162float(h[i]) * rscale[16 + r]);
-        } else {
+            for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(__bfloat162float(h[i])));
+          }
+          mx = warp_max(mx);
+          int ex = 0, e2 = 0;
+          if (mx > 0.f && isfinite(mx)) {
+            frexpf(mx, &ex);
+            e2 = max(-100, min(100, 15 - ex));  // max * 2^e2 in [2^14, 2^15): exact in f16
+          }
+          const float up = ldexpf(1.0f, e2);
+          if (lane == 0) {
+            rscale[r] = ldexpf(1.0f, -e2);
+            rscale[16 + r] = up;
+          }
+          for (int v = lane; v < vlen; v += 32) {
+            __align__(16) __half hv[8];
+            if (v < vpr) {
+              const uint4 raw = row[v];
+              const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(0.f);
+              for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(__bfloat162float(h[i]) * up);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) hv[i] = __float2half_rn(0.f);
+            }
+            row[v] = *reinterpret_cast<const uint4*>(hv);
+          }
         }
-        *sp = *reinterpret_cast<const uint4*>(hv);
       }
       __syncthreads();
       // ---- this warp's tiles of the chunk
