@@ -65,7 +65,7 @@ struct RopeArgs {
 // With a norm weight the head is first RMS-normalised as the reference's per-head q/k norm
 // (engine/qwen3_moe_cuda.py:3282-3285, 3903-3904): fp32 mean of squares, normalised value
 // rounded to bf16, times the bf16 weight rounded to bf16.
-// One CTA per token, one warp per head (queries, then keys, then values). Lane j handles
+// CTAs (token, group of 8 heads), one warp per head (queries, then keys, then values). Lane j handles
 // the rotation pairs (2j, 2j+1) of the first half and their partners in the second half.
 __device__ __forceinline__ void rope_head(const __nv_bfloat16* src, __nv_bfloat16* dst, int half, const float* c,
                                           const float* s, int lane, const __nv_bfloat16* nw = nullptr,
@@ -137,7 +137,9 @@ __global__ void __launch_bounds__(256) rope_kv_append_kernel(RopeArgs a) {
   const int64_t slot = pos % a.page_size;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const int64_t nq = a.q_out ? a.hq : 0;
-  for (int64_t h = warp; h < nq + 2 * a.hkv; h += nwarps) {
+  // heads spread over the CTAs of grid y, one warp per head: each head is a short chain of
+  // dependent loads, so they run side by side instead of one after another
+  for (int64_t h = (int64_t)blockIdx.y * nwarps + warp; h < nq + 2 * a.hkv; h += (int64_t)nwarps * gridDim.y) {
     if (h < nq) {
       rope_head(a.q_in + t * a.in_stride + h * a.d, a.q_out + (t * a.hq + h) * a.d, half, c, s, lane, a.q_norm,
                 a.norm_eps);
@@ -2491,7 +2493,9 @@ extern "C" int mrb_rope_kv_append(const void* q_in, const void* k_in, const void
              (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, stride_page, stride_head,
              stride_tok, page_size, block_table, block_table_stride, num_pages, error_flag,
              (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, norm_eps};
-  launch_kernel(rope_kv_append_kernel, dim3((unsigned)tokens), dim3(256), 0, (cudaStream_t)stream, true, a);
+  const int64_t heads = (q_out ? hq : 0) + 2 * hkv;
+  const unsigned hgroups = (unsigned)std::min<int64_t>(65535, (heads + 7) / 8);
+  launch_kernel(rope_kv_append_kernel, dim3((unsigned)tokens, hgroups), dim3(256), 0, (cudaStream_t)stream, true, a);
   return launch_status("rope_kv_append");
 }
 
