@@ -352,6 +352,9 @@ TC_CASES = {
     # epilogue (n = output columns; 2n weight rows) and the down projection
     "w8a16-gemm-gateup": (512, 18944, 3584),
     "w8a16-gemm-down": (512, 3584, 18944),
+    # the config-4 decode step's dense projections at 32 rows (qkv and o of one layer)
+    "w8a16-gemm-qkv32": (32, 5120, 2048),
+    "w8a16-gemm-o32": (32, 2048, 4096),
     # W8A8 projections of the config-3 decode step (64 rows: split-K for the narrow ones,
     # paired gate/up), through mrb_w8a8_linear_bf16 with its workspace
     "w8a8-linear-o64": (64, 3584, 3584),

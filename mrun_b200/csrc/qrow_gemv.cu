@@ -706,6 +706,9 @@ int tc_w8a16_gemm(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* co
                   cudaStream_t s);
 int qrow_gemm_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
                    int64_t n, const float* bias, __nv_bfloat16* y, cudaStream_t s);
+bool qrow_skinny_supported(int64_t m, int64_t n, int64_t k);
+int qrow_skinny_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* codes, const float* scales,
+                     int64_t n, const float* bias, __nv_bfloat16* y, cudaStream_t s);
 int qrow_gemm_swiglu_bf16(const __nv_bfloat16* x, int64_t m, int64_t k, const int8_t* gate_codes,
                           const float* gate_scales, const int8_t* up_codes, const float* up_scales, int64_t n,
                           __nv_bfloat16* y, cudaStream_t s);
@@ -733,6 +736,9 @@ static int qrow_gemv_dispatch(const void* x, int x_dtype, int64_t m, int64_t k, 
   switch (x_dtype) {
     case MRB_BF16:
       if (m > GEMV_MAX_ROWS) {
+        // 17-32 rows: the skinny kernel (weights in registers, cluster split-K)
+        if (qrow_skinny_supported(m, n, k))
+          return qrow_skinny_bf16((const __nv_bfloat16*)x, m, k, codes, scales, n, bias, (__nv_bfloat16*)y, s);
         if (tc_w8a16_supported(x, k, codes, nullptr))
           return tc_w8a16_gemm((const __nv_bfloat16*)x, m, k, codes, scales, nullptr, nullptr, n, bias,
                                (__nv_bfloat16*)y, s);
