@@ -37,7 +37,7 @@ int ensure_dynamic_smem(const void* kernel, size_t bytes, const char* what) {
 
 }  // namespace mrb
 
-extern "C" int mrb_abi_version(void) { return 15; }
+extern "C" int mrb_abi_version(void) { return 16; }
 
 extern "C" const char* mrb_last_error(void) { return mrb::g_last_error; }
 
