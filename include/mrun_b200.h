@@ -301,6 +301,21 @@ int mrb_ep_p2p_return(const void *eo_bf16, const int64_t *inverse, int64_t hidde
                       void *stream);
 int mrb_ep_p2p_wait_return(void *mailbox, int64_t world, int64_t capacity, int64_t hidden,
                            int32_t *state, void *stream);
+/* The receive side of a dispatch and the route compile in one launch (one CTA): waits as
+ * mrb_ep_p2p_wait_dispatch does, writes each slot's local expert id into ids64 [world *
+ * capacity] (-1 for padding, so only the rows that arrived are ranked), then compiles their
+ * routes as mrb_route_compile(ids64, coef_in, world * capacity, 1, experts_local, ...) does:
+ * counts/starts [experts_local], token_ids/coef/inverse [world * capacity] (entries of padding
+ * slots unused). experts_local <= 512. */
+int mrb_ep_p2p_wait_route(void *mailbox, int64_t world, int64_t capacity, int64_t hidden, int64_t experts_local,
+                          int64_t *ids64, const float *coef_in, int32_t *counts, int32_t *starts, int64_t *token_ids,
+                          float *coef, int64_t *inverse, int32_t *state, void *stream);
+/* Waits for every owner's return flag (as mrb_ep_p2p_wait_return) and combines the back rows
+ * in the same launch, as mrb_stable_route_reduce(back, coef, slot_of_assign, tokens, k, hidden,
+ * NULL, out_bf16) does (bit-identical). */
+int mrb_ep_p2p_combine(void *mailbox, int64_t world, int64_t capacity, int64_t hidden, const float *coef,
+                       const int64_t *slot_of_assign, int64_t tokens, int64_t k, void *out_bf16, int32_t *state,
+                       void *stream);
 /* Bound (in polls, each followed by a ~64 ns sleep) of the flag waits launched from now on by
  * mrb_ep_p2p_wait_dispatch / mrb_ep_p2p_wait_return in this process; 2^22 by default, [1, 2^30].
  * A graph captured earlier keeps the bound it was captured with. mrb_ep_wait_limit reads it. */

@@ -86,6 +86,8 @@ SIGNATURES: dict[str, list] = {
     "mrb_ep_p2p_wait_dispatch": [_P, _I64, _I64, _I64, c_int32, _P, _P, _P],
     "mrb_ep_p2p_return": [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _P],
     "mrb_ep_p2p_wait_return": [_P, _I64, _I64, _I64, _P, _P],
+    "mrb_ep_p2p_wait_route": [_P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    "mrb_ep_p2p_combine": [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P],
     "mrb_ep_set_wait_limit": [_I64],
     "mrb_ep_wait_limit": [],
 }

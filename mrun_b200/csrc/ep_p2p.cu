@@ -24,6 +24,7 @@
 // read the error.
 // No TMA and no cluster multicast is involved; peers are reached by ordinary loads/stores.
 #include "qrow_common.cuh"
+#include "moe_route.cuh"
 
 #include <algorithm>
 #include <cstring>
@@ -181,6 +182,61 @@ __global__ void ep_p2p_wait_return_kernel(unsigned char* __restrict__ mailbox, M
   if (!ok && threadIdx.x == 0) state[3] = 1;
 }
 
+// The receive side of a dispatch and the route compile in one CTA of RC_THREADS threads (one
+// launch instead of two on every layer's critical path): wait for every source's flag, keep
+// the local expert id of each real row (padding slots get -1, so the route compiler leaves
+// them out and ranks only the rows that arrived), then compile the routes over those ids.
+__global__ void __launch_bounds__(RC_THREADS) ep_p2p_wait_route_kernel(
+    unsigned char* __restrict__ mailbox, MailboxLayout lay, int world, int cap, int experts_local,
+    int64_t* __restrict__ ids64, const float* __restrict__ coef_in, int32_t* __restrict__ counts_out,
+    int32_t* __restrict__ starts, int64_t* __restrict__ token_ids, float* __restrict__ coef,
+    int64_t* __restrict__ inverse, int32_t* __restrict__ state, int spin_limit) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const unsigned epoch = (unsigned)state[0];
+  const bool ok =
+      epm_wait_flags(reinterpret_cast<const unsigned*>(mailbox + lay.flags_dispatch), world, epoch, spin_limit);
+  if (!ok && threadIdx.x == 0) state[3] = 1;
+  const int32_t* counts = reinterpret_cast<const int32_t*>(mailbox + lay.counts);
+  const int32_t* ids = reinterpret_cast<const int32_t*>(mailbox + lay.ids);
+  for (int s = threadIdx.x; s < world * cap; s += blockDim.x) {
+    const int src = s / cap, j = s - src * cap;
+    const int id = ids[s];
+    const bool real = ok && j < counts[src] && id >= 0 && id < experts_local;
+    ids64[s] = real ? id : -1;
+  }
+  __syncthreads();  // the ids are stored (block scope) before the block ranks them
+  route_compile_block(ids64, coef_in, (int64_t)world * cap, 1, experts_local, counts_out, starts, token_ids, coef,
+                      inverse, nullptr);
+}
+
+// The source side of a return and the fixed-rank combine in one launch: every CTA waits for
+// every owner's return flag (bounded), then combines as stable_route_reduce_kernel does --
+// out[t, h] = sum over r < k, in rank order, of coef[p] * float(back[p, h]), p =
+// slot_of_assign[t*k + r], each product rounded to fp32 and added left to right.
+__global__ void ep_p2p_combine_kernel(unsigned char* __restrict__ mailbox, MailboxLayout lay, int world,
+                                      const float* __restrict__ coef, const int64_t* __restrict__ slot_of_assign,
+                                      int64_t tokens, int k, int64_t H, __nv_bfloat16* __restrict__ out,
+                                      int32_t* __restrict__ state, int spin_limit) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const unsigned epoch = (unsigned)state[0];
+  const bool ok =
+      epm_wait_flags(reinterpret_cast<const unsigned*>(mailbox + lay.flags_return), world, epoch, spin_limit);
+  if (!ok && threadIdx.x == 0) state[3] = 1;
+  const __nv_bfloat16* eo = reinterpret_cast<const __nv_bfloat16*>(mailbox + lay.back);
+  const int64_t t = blockIdx.y;
+  for (int64_t h = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; h < H; h += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < k; ++r) {
+      const int64_t p = slot_of_assign[t * k + r];
+      const float prod = __fmul_rn(__bfloat162float(__ldcg(eo + p * H + h)), coef[p]);
+      acc = r == 0 ? prod : __fadd_rn(acc, prod);
+    }
+    out[t * H + h] = __float2bfloat16_rn(acc);
+  }
+}
+
 static int ep_check(int64_t world, int64_t rank, int64_t cap, int64_t hidden, const char* what) {
   if (world < 1 || world > EPM_MAX_WORLD || rank < 0 || rank >= world || cap < 1 || hidden <= 0 || hidden % 8)
     return fail(MRB_ERR_ARG, "%s: bad shape", what);
@@ -303,4 +359,36 @@ extern "C" int mrb_ep_p2p_wait_return(void* mailbox, int64_t world, int64_t capa
   launch_kernel(ep_p2p_wait_return_kernel, dim3(1), dim3(64), 0, (cudaStream_t)stream, true, (unsigned char*)mailbox,
                 lay, (int)world, state, g_epm_spin_limit);
   return launch_status("ep_p2p_wait_return");
+}
+
+extern "C" int mrb_ep_p2p_wait_route(void* mailbox, int64_t world, int64_t capacity, int64_t hidden,
+                                     int64_t experts_local, int64_t* ids64, const float* coef_in, int32_t* counts,
+                                     int32_t* starts, int64_t* token_ids, float* coef, int64_t* inverse, int32_t* state,
+                                     void* stream) {
+  int st = ep_check(world, 0, capacity, hidden, "ep_p2p_wait_route");
+  if (st) return st;
+  if (experts_local < 1 || experts_local > RC_MAXE)
+    return fail(MRB_ERR_UNSUPPORTED, "ep_p2p_wait_route: 1 to %d local experts", RC_MAXE);
+  if (!mailbox || !ids64 || !coef_in || !counts || !starts || !token_ids || !coef || !inverse || !state)
+    return fail(MRB_ERR_ARG, "ep_p2p_wait_route: null pointer");
+  launch_kernel(ep_p2p_wait_route_kernel, dim3(1), dim3(RC_THREADS), 0, (cudaStream_t)stream, true,
+                (unsigned char*)mailbox, epm_layout(world, capacity, hidden), (int)world, (int)capacity,
+                (int)experts_local, ids64, coef_in, counts, starts, token_ids, coef, inverse, state, g_epm_spin_limit);
+  return launch_status("ep_p2p_wait_route");
+}
+
+extern "C" int mrb_ep_p2p_combine(void* mailbox, int64_t world, int64_t capacity, int64_t hidden, const float* coef,
+                                  const int64_t* slot_of_assign, int64_t tokens, int64_t k, void* out_bf16,
+                                  int32_t* state, void* stream) {
+  int st = ep_check(world, 0, capacity, hidden, "ep_p2p_combine");
+  if (st) return st;
+  if (tokens < 0 || k <= 0 || tokens * k > capacity) return fail(MRB_ERR_ARG, "ep_p2p_combine: bad shape");
+  if (tokens == 0) return MRB_OK;
+  if (tokens > 65535) return fail(MRB_ERR_UNSUPPORTED, "ep_p2p_combine: at most 65535 tokens per call");
+  if (!mailbox || !coef || !slot_of_assign || !out_bf16 || !state) return fail(MRB_ERR_ARG, "ep_p2p_combine: null pointer");
+  const unsigned bx = (unsigned)std::min<int64_t>((hidden + 255) / 256, 64);
+  launch_kernel(ep_p2p_combine_kernel, dim3(bx, (unsigned)tokens), dim3(256), 0, (cudaStream_t)stream, true,
+                (unsigned char*)mailbox, epm_layout(world, capacity, hidden), (int)world, coef, slot_of_assign, tokens,
+                (int)k, hidden, (__nv_bfloat16*)out_bf16, state, g_epm_spin_limit);
+  return launch_status("ep_p2p_combine");
 }

@@ -240,6 +240,13 @@ class P2PExpertParallelMoE:
         self.ids64 = torch.empty((slots, 1), dtype=torch.int64, device=device)
         self.zeros = torch.zeros((slots, 1), dtype=torch.float32, device=device)
         self.mlp_sync = torch.zeros(2 * shard.per_rank + 1, dtype=torch.int32, device=device)
+        # routes of the received rows, compiled by the receive kernel (real rows only)
+        per = shard.per_rank
+        self.rt_counts = torch.empty(per, dtype=torch.int32, device=device)
+        self.rt_starts = torch.empty(per, dtype=torch.int32, device=device)
+        self.rt_token_ids = torch.empty(slots, dtype=torch.int64, device=device)
+        self.rt_coef = torch.empty(slots, dtype=torch.float32, device=device)
+        self.rt_inverse = torch.empty(slots, dtype=torch.int64, device=device)
         dist.barrier(group=group)  # every mailbox exists and is zeroed before any dispatch
 
     def forward(self, source: torch.Tensor, top_indices: torch.Tensor, top_weights: torch.Tensor) -> torch.Tensor:
@@ -261,18 +268,20 @@ class P2PExpertParallelMoE:
         src = source.contiguous()
         _lib.call("mrb_ep_p2p_dispatch", src.data_ptr(), hidden, self.slot_src.data_ptr(), self.send_expert.data_ptr(),
                   world, sh.rank, cap, self.mailboxes.data_ptr(), self.state.data_ptr(), stream)
-        _lib.call("mrb_ep_p2p_wait_dispatch", self._own, world, cap, hidden, per, self.ids64.data_ptr(),
+        # receive + route compile of the rows that arrived, in one launch
+        _lib.call("mrb_ep_p2p_wait_route", self._own, world, cap, hidden, per, self.ids64.data_ptr(),
+                  self.zeros.data_ptr(), self.rt_counts.data_ptr(), self.rt_starts.data_ptr(),
+                  self.rt_token_ids.data_ptr(), self.rt_coef.data_ptr(), self.rt_inverse.data_ptr(),
                   self.state.data_ptr(), stream)
-        token_ids, _, starts, counts, inverse, _ = grouped_route_tensors_with_inverse(
-            self.ids64, self.zeros, num_experts=per + 1)
-        eo = _grouped_mlp_from_pointer(self._own + self.offsets[4], token_ids, starts[:per], counts[:per],
-                                       self.pages, self.layout, hidden, device, self.mlp_sync)
-        _lib.call("mrb_ep_p2p_return", eo.data_ptr(), inverse.data_ptr(), hidden, world, sh.rank, cap,
+        eo = _grouped_mlp_from_pointer(self._own + self.offsets[4], self.rt_token_ids, self.rt_starts,
+                                       self.rt_counts, self.pages, self.layout, hidden, device, self.mlp_sync,
+                                       rows=slots)
+        _lib.call("mrb_ep_p2p_return", eo.data_ptr(), self.rt_inverse.data_ptr(), hidden, world, sh.rank, cap,
                   self.mailboxes.data_ptr(), self.state.data_ptr(), stream)
-        _lib.call("mrb_ep_p2p_wait_return", self._own, world, cap, hidden, self.state.data_ptr(), stream)
+        # wait for every owner's return + the fixed-rank combine, in one launch
         out = torch.empty((t, hidden), dtype=torch.bfloat16, device=device)
-        _lib.call("mrb_stable_route_reduce", self._own + self.offsets[5], self.coef_slot.data_ptr(),
-                  self.slot_of_assign.data_ptr(), t, k, hidden, None, out.data_ptr(), stream)
+        _lib.call("mrb_ep_p2p_combine", self._own, world, cap, hidden, self.coef_slot.data_ptr(),
+                  self.slot_of_assign.data_ptr(), t, k, out.data_ptr(), self.state.data_ptr(), stream)
         return out
 
     def check(self) -> None:
@@ -294,14 +303,15 @@ class P2PExpertParallelMoE:
 
 
 def _grouped_mlp_from_pointer(rows_ptr: int, token_ids, starts, counts, pages, layout, hidden: int, device,
-                              sync: torch.Tensor | None = None):
-    """grouped_expert_mlp over activation rows given by a raw device pointer (a mailbox)."""
+                              sync: torch.Tensor | None = None, rows: int | None = None):
+    """grouped_expert_mlp over activation rows given by a raw device pointer (a mailbox).
+    ``rows``: the assignment slots the outputs are indexed by (default token_ids' length)."""
     from . import _lib
     from .moe import expert_mlp_sync
 
     ly = layout
     f = ly.intermediate_size
-    a = int(token_ids.numel())
+    a = int(token_ids.numel()) if rows is None else int(rows)
     e = int(counts.numel())
     act = torch.empty((a, f), dtype=torch.bfloat16, device=device)
     y = torch.empty((a, hidden), dtype=torch.bfloat16, device=device)
