@@ -286,8 +286,8 @@ class MoeDecoder:
                            workspace=self.attn_ws, scale=self.scale)
             qrow_linear(layer.o.codes, layer.o.scales, ctx.view(rows, qd), out=proj, workspace=ws)
             residual_rms_norm_into(hidden, proj, layer.ln2, cfg.eps, hidden, normed)
-            # router linear + softmax / top-k in one launch; the backends take the fp32 images
-            # of the bf16 weights (the values the reference's .float() would give)
+            # router linear, then softmax / top-k waiting on it; the backends take the fp32
+            # images of the bf16 weights (the values the reference's .float() would give)
             top_idx, _, top_w = router_qrow_topk(normed, layer.router.codes, layer.router.scales, cfg.top_k,
                                                  renorm=cfg.norm_topk, logits=self.router_logits,
                                                  out=self.route_buf)
