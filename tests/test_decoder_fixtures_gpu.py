@@ -91,3 +91,54 @@ def test_moe_decoder_free_running_matches_reference_runtime(cuda):
         dec.close()
         print(f"moe prompt {p}: {len(tokens)} tokens, near-tie steps that differed: {flips}")
         assert len(flips) <= 2
+
+
+def _agrees_until_near_tie(got, fixture):
+    """The generated tokens equal the reference's until the end or until a step whose
+    reference top-1/top-2 margin is below NEAR_TIE (after which the decodes may part)."""
+    want, margin = fixture["tokens"], fixture["margin"]
+    for i, (a, b) in enumerate(zip(got, want)):
+        if int(a) != int(b):
+            assert float(margin[i]) < fm.NEAR_TIE, f"step {i}: token {a} != reference {b} (margin {margin[i]:.4f})"
+            return i
+        if float(margin[i]) < fm.NEAR_TIE:
+            return i
+    return len(got)
+
+
+def test_moe_continuous_batcher_matches_reference_runtime(cuda):
+    """MoeContinuousBatcher over a 4-slot captured step: both fixture prompts, each twice, one
+    copy arriving while the others decode and one waiting for a retired slot; every request
+    follows the reference's greedy decode until its first near-tie step, whatever slot and
+    companions it had."""
+    from mrun_b200.continuous import MoeContinuousBatcher
+    from mrun_b200.moe_engine import MoeDecoder
+
+    g = fm.load("moe_decode")
+    weights = fm.moe_device_weights(cuda)
+    fixtures = [{k: g[f"p{p}_{k}"] for k in ("prompt", "tokens", "margin")} for p in range(2)]
+    steps = len(fixtures[0]["tokens"])
+    ctx = max(len(f["prompt"]) for f in fixtures) + steps + 1
+    dec = MoeDecoder(weights, max_rows=4, max_seq_len=ctx, device=cuda)
+    bat = MoeContinuousBatcher(dec, max_context_tokens=ctx)
+    ids = {bat.submit(fixtures[0]["prompt"], max_new_tokens=steps): 0,
+           bat.submit(fixtures[1]["prompt"], max_new_tokens=steps): 1,
+           bat.submit(fixtures[1]["prompt"], max_new_tokens=24): 1}
+    results = {}
+    for _ in range(7):
+        results.update(bat.step())
+    ids[bat.submit(fixtures[0]["prompt"], max_new_tokens=steps)] = 0  # joins mid-decode
+    ids[bat.submit(fixtures[0]["prompt"], max_new_tokens=16)] = 0     # waits for a slot
+    results.update(bat.run())
+    assert set(results) == set(ids)
+    agreed = []
+    for rid, p in ids.items():
+        assert len(results[rid]) == (steps if rid not in (2, 4) else (24 if rid == 2 else 16))
+        agreed.append(_agrees_until_near_tie(results[rid], fixtures[p]))
+    t = bat.pool.telemetry()
+    assert t.allocations == 5 and t.releases == 5 and t.peak_active_slots == 4 and t.slot_reuses >= 1
+    bat.close()
+    dec.close()
+    print(f"continuous: tokens agreeing with the reference before a near tie: {agreed}")
+    # the first near-tie steps of the two prompts are 9 and 17
+    assert min(agreed) >= 9
