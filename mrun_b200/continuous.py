@@ -176,6 +176,8 @@ class _Request:
     prompt: list[int]
     max_new_tokens: int
     eos: int | None
+    context: int = 0  # positions already committed in the slot's K/V at admission
+    prefill: Any = None
     state_id: str = ""
     slot: int = -1
     generation: int = 0
@@ -200,12 +202,13 @@ class MoeContinuousBatcher:
         self._next_id = 0
         self.steps = 0
         self.generated = 0
+        self.rows_stepped = 0
         dev = decoder.device
         # every slot starts parked: token 0 at position 0
         decoder.in_ids[: self.slots].zero_()
         decoder.positions[: self.slots].zero_()
         decoder.row_len[: self.slots].fill_(1)
-        self._graph = bool(graph) and decoder.ep is None
+        self._graph = bool(graph) and decoder.ep is None and not getattr(decoder, "streamed", False)
         if self._graph:
             decoder.capture(self.slots)
         self._dev = dev
@@ -222,6 +225,22 @@ class MoeContinuousBatcher:
         self._queue.append(req)
         return req.request_id
 
+    def submit_with_context(self, first_token: int, context_tokens: int, *, max_new_tokens: int,
+                            eos: int | None = None, prefill: Any = None) -> int:
+        """Queue a request whose first ``context_tokens`` positions are committed in its K/V
+        pages at admission and whose next input is ``first_token``: ``prefill(lease)`` is
+        called when the slot is leased and writes those pages (a prefill engine; left None,
+        the pages keep what they hold, which the synthetic benchmarks fill with random K/V)."""
+        context_tokens = _strict_positive_int(context_tokens, "context_tokens")
+        _strict_positive_int(max_new_tokens, "max_new_tokens")
+        if context_tokens + max_new_tokens + 1 > self.pool.max_context_tokens:
+            raise OverflowError("requested Qwen K/V capacity exceeds the fixed slot arena")
+        req = _Request(self._next_id, [int(first_token)], int(max_new_tokens), eos, context=context_tokens,
+                       prefill=prefill)
+        self._next_id += 1
+        self._queue.append(req)
+        return req.request_id
+
     @property
     def pending(self) -> int:
         return len(self._queue) + len(self._active)
@@ -232,32 +251,40 @@ class MoeContinuousBatcher:
             tensor.index_copy_(0, idx, torch.tensor(values, dtype=tensor.dtype, device=self._dev))
 
     def _admit(self) -> None:
-        slots, ids, zeros, ones = [], [], [], []
+        slots, ids, pos, lens = [], [], [], []
         while self._queue and len(self._active) < self.slots:
-            req = self._queue.popleft()
+            req = self._queue[0]
             req.state_id = f"moe-request-{req.request_id}"
-            req.slot, req.generation, _ = self.pool.acquire(req.state_id, len(req.prompt) + req.max_new_tokens + 1)
+            req.slot, req.generation, lease = self.pool.acquire(
+                req.state_id, req.context + len(req.prompt) + req.max_new_tokens + 1)
+            self._queue.popleft()
+            if req.prefill is not None:
+                req.prefill(lease)
             req.fed = 1
             self._active[req.slot] = req
             slots.append(req.slot)
             ids.append(req.prompt[0])
-            zeros.append(0)
-            ones.append(1)
+            pos.append(req.context)
+            lens.append(req.context + 1)
         self._write(self.decoder.in_ids, slots, ids)
-        self._write(self.decoder.positions, slots, zeros)
-        self._write(self.decoder.row_len, slots, ones)
+        self._write(self.decoder.positions, slots, pos)
+        self._write(self.decoder.row_len, slots, lens)
 
     def step(self) -> dict[int, list[int]]:
         self._admit()
         dec = self.decoder
         if not self._active and dec.ep is None:
             return {}
+        # a captured step runs every slot; an eager one only up to the highest leased slot
+        # (slots are leased lowest first, so the live rows stay packed at the front)
+        rows = self.slots if self._graph or not self._active else max(self._active) + 1
         if self._graph:
-            dec.step(self.slots)
+            dec.step(rows)
         else:
-            dec.step_eager(self.slots)
+            dec.step_eager(rows)
         self.steps += 1
-        out = dec.next_ids[: self.slots].cpu().tolist()
+        self.rows_stepped += rows
+        out = dec.next_ids[:rows].cpu().tolist()
         done: dict[int, list[int]] = {}
         feed_s, feed_v = [], []
         for slot, req in list(self._active.items()):

@@ -31,6 +31,7 @@ from .expert_parallel import ExpertShard, FixedCapacityExpertParallelMoE, P2PExp
 from .moe import ExpertPageLayout, PagedInt8ExpertBackend, ResidentInt8ExpertPages, router_qrow_topk
 from .paged_kv import PagedKVCache
 from .qstore_build import embed_rows
+from .streaming import ExpertPageCache, HostPageTier
 
 
 @dataclass(frozen=True)
@@ -47,12 +48,20 @@ class MoeConfig:
     rope_theta: float = 1e6
     eps: float = 1e-6
     norm_topk: bool = True
+    qk_norm: bool = True  # per-head q/k RMSNorm (Qwen3); Mixtral has none
 
     @classmethod
     def qwen3_30b_a3b(cls) -> "MoeConfig":
         """Qwen3-30B-A3B shape: 48 layers, hidden 2048, 32/4 heads, 128 experts top-8, expert FFN 768."""
         return cls(num_layers=48, hidden=2048, heads=32, kv_heads=4, head_dim=128, experts=128, top_k=8,
                    expert_ffn=768, vocab=151936)
+
+    @classmethod
+    def mixtral_8x7b(cls) -> "MoeConfig":
+        """Mixtral-8x7B shape: 32 layers, hidden 4096, 32/8 heads, 8 experts top-2 (softmax over
+        the two picks), expert FFN 14336 (176 MB int8 pages), vocab 32000, no q/k norm."""
+        return cls(num_layers=32, hidden=4096, heads=32, kv_heads=8, head_dim=128, experts=8, top_k=2,
+                   expert_ffn=14336, vocab=32000, eps=1e-5, qk_norm=False)
 
     @property
     def qkv_rows(self) -> int:
@@ -64,11 +73,11 @@ class MoeLayer:
     qkv: QRow
     o: QRow
     router: QRow
-    q_norm: torch.Tensor   # bf16 [head_dim]
-    k_norm: torch.Tensor
+    q_norm: torch.Tensor | None   # bf16 [head_dim]; None without q/k norm
+    k_norm: torch.Tensor | None
     ln1: torch.Tensor      # input norm, fp32 [hidden] holding bf16 values
     ln2: torch.Tensor      # post-attention norm
-    pages: torch.Tensor    # uint8 [local experts, page_stride]
+    pages: torch.Tensor | None    # uint8 [local experts, page_stride]; None when the pages live in a host tier
 
 
 def _random_qrow(rows: int, cols: int, gen: torch.Generator, device: torch.device, std: float = 0.02) -> QRow:
@@ -93,20 +102,30 @@ class MoeWeights:
     head: QRow
     expert_first: int
     experts_local: int
+    host: HostPageTier | None = None  # expert pages in pinned host memory (streamed decode)
 
     @classmethod
     def synthetic(cls, cfg: MoeConfig, device: torch.device, seed: int = 0, *,
-                  shard: ExpertShard | None = None) -> "MoeWeights":
+                  shard: ExpertShard | None = None, host_experts: bool = False) -> "MoeWeights":
         """Random-init int8 weights of the given shape (no checkpoint). With ``shard`` only the
-        rank's experts are materialised; dense weights are identical on every rank."""
+        rank's experts are materialised; dense weights are identical on every rank. With
+        ``host_experts`` every expert page goes to a pinned host tier (layer by layer, so HBM
+        never holds more than one layer's pages) and the layers carry no device pages."""
         gen = torch.Generator(device=device).manual_seed(seed)
         layout = ExpertPageLayout.create(cfg.hidden, cfg.expert_ffn)
         first, local = (shard.first, shard.per_rank) if shard is not None else (0, cfg.experts)
+        host = HostPageTier(layout, cfg.num_layers, local) if host_experts else None
         embed = _random_qrow(cfg.vocab, cfg.hidden, gen, device, std=1.0)
-        layers = [cls._draw_layer(cfg, layout, gen, device, first, local) for _ in range(cfg.num_layers)]
+        layers = []
+        for i in range(cfg.num_layers):
+            layer = cls._draw_layer(cfg, layout, gen, device, first, local)
+            if host is not None:
+                host.pages[i].copy_(layer.pages)
+                layer.pages = None
+            layers.append(layer)
         final_norm = _random_norm(cfg.hidden, gen, device).float()
         head = _random_qrow(cfg.vocab, cfg.hidden, gen, device)
-        return cls(cfg, layout, embed, layers, final_norm, head, first, local)
+        return cls(cfg, layout, embed, layers, final_norm, head, first, local, host)
 
     @classmethod
     def _draw_layer(cls, cfg: MoeConfig, layout: ExpertPageLayout, gen: torch.Generator, device: torch.device,
@@ -117,6 +136,8 @@ class MoeWeights:
         o = _random_qrow(h, cfg.heads * d, gen, device)
         router = _random_qrow(cfg.experts, h, gen, device, std=0.05)
         q_norm, k_norm = _random_norm(d, gen, device), _random_norm(d, gen, device)
+        if not cfg.qk_norm:  # drawn all the same, so the later draws do not depend on the flag
+            q_norm = k_norm = None
         ln1, ln2 = _random_norm(h, gen, device).float(), _random_norm(h, gen, device).float()
         pages = cls._expert_pages(cfg, layout, gen, device, first, local)
         return MoeLayer(qkv, o, router, q_norm, k_norm, ln1, ln2, pages)
@@ -164,9 +185,11 @@ class MoeWeights:
         return {
             "embed": q(self.embed), "final_norm": b(self.final_norm), "head": q(self.head),
             "layout": self.layout.as_dict(),
-            "layers": [{"qkv": q(L.qkv), "o": q(L.o), "router": q(L.router), "q_norm": b(L.q_norm),
-                        "k_norm": b(L.k_norm), "ln1": b(L.ln1), "ln2": b(L.ln2), "pages": L.pages.cpu().numpy()}
-                       for L in self.layers],
+            "layers": [{"qkv": q(L.qkv), "o": q(L.o), "router": q(L.router),
+                        "q_norm": None if L.q_norm is None else b(L.q_norm),
+                        "k_norm": None if L.k_norm is None else b(L.k_norm), "ln1": b(L.ln1), "ln2": b(L.ln2),
+                        "pages": (self.host.pages[i] if L.pages is None else L.pages).cpu().numpy()}
+                       for i, L in enumerate(self.layers)],
         }
 
     def expert_bytes(self) -> int:
@@ -177,7 +200,8 @@ class MoeDecoder:
     """Ragged continuous-batch greedy decode over a paged KV cache (one token per row per step)."""
 
     def __init__(self, weights: MoeWeights, *, max_rows: int, max_seq_len: int, device: torch.device,
-                 group=None, world: int = 1, exchange: str = "p2p") -> None:
+                 group=None, world: int = 1, exchange: str = "p2p", expert_cache_bytes: int | None = None,
+                 route_prefetch: bool = True, cache_policy: str | None = None) -> None:
         cfg = weights.cfg
         self.w = weights
         self.cfg = cfg
@@ -217,6 +241,9 @@ class MoeDecoder:
         self.next_val = torch.zeros(r, dtype=torch.float32, device=device)
         self.world = int(world)
         self.group = group
+        self.streamed = weights.host is not None
+        if self.streamed and self.world > 1:
+            raise ValueError("host-tier experts run on one GPU (no expert-parallel streaming)")
         if self.world > 1:
             shard = ExpertShard(self.world, torch.distributed.get_rank(group), cfg.experts)
             if exchange not in ("p2p", "nccl"):
@@ -228,6 +255,15 @@ class MoeDecoder:
                 self.ep = [FixedCapacityExpertParallelMoE(shard, L.pages, weights.layout, group=group)
                            for L in weights.layers]
             self.backend = None
+        elif self.streamed:
+            # experts stream from the pinned host tier into an HBM slot cache (25 % of the
+            # expert bytes unless told otherwise); each layer's routes are read on the host to
+            # plan its copies, as the reference's ExpertPageCache does, so the step runs eagerly
+            budget = int(expert_cache_bytes if expert_cache_bytes is not None else weights.host.nbytes // 4)
+            self.ep = None
+            self.expert_cache = ExpertPageCache(weights.host, budget_bytes=budget, device=device,
+                                                route_prefetch=route_prefetch, cache_policy=cache_policy)
+            self.backend = PagedInt8ExpertBackend(self.expert_cache, num_experts=cfg.experts)
         else:
             self.ep = None
             self.backend = PagedInt8ExpertBackend(
@@ -281,7 +317,8 @@ class MoeDecoder:
             qrow_linear(layer.qkv.codes, layer.qkv.scales, normed, out=qkv, workspace=ws)
             self.kv.append(i, qkv[:, qd:], qkv[:, qd + kd:], positions, row_seq, q_rows=qkv, q_out=q,
                            rope=(self.cos, self.sin), in_row_stride=cfg.qkv_rows, num_heads=cfg.heads,
-                           error_flag=self.error_flag, qk_norm=(layer.q_norm, layer.k_norm), norm_eps=cfg.eps)
+                           error_flag=self.error_flag,
+                           qk_norm=None if layer.q_norm is None else (layer.q_norm, layer.k_norm), norm_eps=cfg.eps)
             self.kv.attend(i, q, row_len, max_total_tokens=self.max_seq_len, row_seq=row_seq, out=ctx,
                            workspace=self.attn_ws, scale=self.scale)
             qrow_linear(layer.o.codes, layer.o.scales, ctx.view(rows, qd), out=proj, workspace=ws)
@@ -310,7 +347,10 @@ class MoeDecoder:
     @torch.inference_mode()
     def capture(self, rows: int) -> None:
         """Capture one decode step for `rows` rows in a CUDA graph (with expert parallelism the
-        NCCL exchanges are captured too; every rank must capture)."""
+        NCCL exchanges are captured too; every rank must capture). Streamed experts cannot be
+        captured: their copies are planned on the host from each layer's routes."""
+        if self.streamed:
+            raise RuntimeError("a decoder with host-tier experts steps eagerly (routes are read on the host)")
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
         saved = (self.in_ids.clone(), self.positions.clone(), self.row_len.clone())

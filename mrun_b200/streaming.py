@@ -13,6 +13,7 @@ never changes a result: pages in HBM are byte-identical to the host tier.
 """
 from __future__ import annotations
 
+import weakref
 from dataclasses import dataclass
 
 import torch
@@ -105,6 +106,13 @@ class ExpertPageStore:
         self.file.close()
 
 
+_REGISTER_BYTES = 1 << 30
+
+
+def _host_unregister(pages: torch.Tensor) -> None:
+    torch.cuda.cudart().cudaHostUnregister(pages.data_ptr())
+
+
 class HostPageTier:
     """Pinned host copy of every expert page: [layers, experts, page_stride] uint8."""
 
@@ -112,7 +120,18 @@ class HostPageTier:
         self.layout = layout
         self.layers = layers
         self.experts = experts
-        self.pages = torch.empty((layers, experts, layout.page_stride), dtype=torch.uint8, pin_memory=pin)
+        shape = (layers, experts, layout.page_stride)
+        nbytes = layers * experts * layout.page_stride
+        if pin and nbytes >= _REGISTER_BYTES:
+            # torch's pinned allocator rounds every block up to a power of two (a 45 GB tier
+            # would take 64 GB); page-locking an ordinary allocation costs exactly its size
+            self.pages = torch.empty(shape, dtype=torch.uint8)
+            rc = torch.cuda.cudart().cudaHostRegister(self.pages.data_ptr(), nbytes, 0)
+            if int(rc) != 0:
+                raise RuntimeError(f"cudaHostRegister of the {nbytes} B host tier failed ({int(rc)})")
+            weakref.finalize(self, _host_unregister, self.pages)
+        else:
+            self.pages = torch.empty(shape, dtype=torch.uint8, pin_memory=pin)
         self.stats = {"warmed_pages": 0, "warm_seconds": 0.0, "pinned": bool(pin)}
 
     @classmethod

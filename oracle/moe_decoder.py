@@ -70,8 +70,10 @@ def moe_decode_step(w: dict, cfg, ids, positions, context_k, context_v, *, new_k
         q = qkv[:, : hq * d].reshape(rows, hq, d)
         k = qkv[:, hq * d: (hq + hkv) * d].reshape(rows, hkv, d)
         v = qkv[:, (hq + hkv) * d:].reshape(rows, hkv, d)
-        q = rope(_rms(q, L["q_norm"], cfg.eps), cos, sin)
-        k = rope(_rms(k, L["k_norm"], cfg.eps), cos, sin)
+        if L["q_norm"] is not None:  # Qwen3 layers; Mixtral-family layers have no q/k norm
+            q, k = _rms(q, L["q_norm"], cfg.eps), _rms(k, L["k_norm"], cfg.eps)
+        q = rope(q, cos, sin)
+        k = rope(k, cos, sin)
         if new_kv is not None:
             new_kv.append((k, v))
         keys = [np.concatenate([context_k[li][r], k[r:r + 1]], 0) for r in range(rows)]

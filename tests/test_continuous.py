@@ -209,3 +209,43 @@ def test_batcher_eos_and_limits():
     with pytest.raises(OverflowError):
         bat.submit([1] * 60, max_new_tokens=4)
     assert bat.step() == {} and bat.pending == 0
+
+
+class _FakeStreamedDecoder(_FakeDecoder):
+    """A decoder that cannot be captured (host-tier experts): the batcher steps it eagerly
+    over the live prefix of its slots."""
+
+    streamed = True
+
+    def capture(self, rows):
+        raise AssertionError("a streamed decoder is never captured")
+
+    def step_eager(self, rows):
+        self.rows_seen.append(rows)
+        self.captured = rows
+        self.step(rows)
+
+
+def test_batcher_eager_prefix_and_prefilled_context():
+    dec = _FakeStreamedDecoder(rows=4, max_seq=128)
+    dec.rows_seen = []
+    bat = MoeContinuousBatcher(dec, max_context_tokens=128)
+    leases = []
+    # a request whose first 20 positions are committed at admission (its prefill callback sees
+    # the lease), then two plain prompts
+    r0 = bat.submit_with_context(11, 20, max_new_tokens=5, prefill=leases.append)
+    r1 = bat.submit([3, 4], max_new_tokens=3)
+    r2 = bat.submit([9], max_new_tokens=8)
+    first = bat.step()
+    assert first == {} and dec.rows_seen == [3]
+    assert len(leases) == 1 and leases[0].slot == 0 and leases[0].capacity == 27
+    assert dec.positions[0] == 21  # the prefilled row decoded its first token at position 20
+    out = {**first, **bat.run()}
+    assert out[r1] == _alone([3, 4], 3) and out[r2] == _alone([9], 8)
+    assert len(out[r0]) == 5
+    # rows stepped never exceed the highest leased slot + 1
+    assert max(dec.rows_seen) == 3
+    with pytest.raises(ValueError, match="context_tokens must be a positive integer"):
+        bat.submit_with_context(1, 0, max_new_tokens=2)
+    with pytest.raises(OverflowError):
+        bat.submit_with_context(1, 120, max_new_tokens=8)

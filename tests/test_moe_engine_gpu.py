@@ -27,16 +27,27 @@ def _tiny():
                      expert_ffn=128, vocab=500)
 
 
-@pytest.mark.parametrize("graph", [False, True])
+@pytest.mark.parametrize("graph", [False, True, "streamed"])
 def test_moe_decode_steps_match_oracle(graph, cuda):
+    """graph False / True: the Qwen3 form, eager and captured. "streamed": the Mixtral form (no
+    q/k norm) with the expert pages in a pinned host tier behind an HBM slot cache of 10 of the
+    16 pages (a layer may route to all 8 experts, so a slot cache holds at least 8; eager)."""
+    from dataclasses import replace
+
     from mrun_b200.moe_engine import MoeDecoder, MoeWeights
 
     cfg = _tiny()
-    w = MoeWeights.synthetic(cfg, cuda, seed=3)
+    streamed = graph == "streamed"
+    if streamed:
+        cfg = replace(cfg, qk_norm=False)
+        graph = False
+    w = MoeWeights.synthetic(cfg, cuda, seed=3, host_experts=streamed)
     lengths = [5, 17, 33, 1, 64]
     rows = len(lengths)
     steps = 4
-    dec = MoeDecoder(w, max_rows=8, max_seq_len=96, device=cuda)
+    dec = MoeDecoder(w, max_rows=8, max_seq_len=96, device=cuda,
+                     expert_cache_bytes=10 * w.layout.page_stride if streamed else None)
+    assert dec.streamed == streamed
     first = torch.tensor([7, 123, 42, 499, 0])
     dec.load_synthetic_context(lengths, first, steps=steps, seed=1)
     host = w.to_host()
@@ -66,6 +77,40 @@ def test_moe_decode_steps_match_oracle(graph, cuda):
         pos = pos + 1
     dec.check_errors()
     assert near_ties <= 2
+    if streamed:
+        st = dec.expert_cache.stats
+        assert st.misses > 0 and st.evictions > 0 and dec.expert_cache.capacity == 10
+
+
+def test_streamed_experts_decode_like_resident_pages(cuda):
+    """Continuous batching over the Mixtral form: the decoder whose expert pages stream from a
+    pinned host tier through an HBM slot cache of 10 of the 24 pages generates, for
+    every request, the tokens of the decoder holding every page in HBM (both eager over the
+    same rows, so every kernel sees the same inputs; the pages are the same bytes)."""
+    from mrun_b200.continuous import MoeContinuousBatcher
+    from mrun_b200.moe_engine import MoeConfig, MoeDecoder, MoeWeights
+
+    cfg = MoeConfig(num_layers=3, hidden=256, heads=4, kv_heads=2, head_dim=64, experts=8, top_k=2,
+                    expert_ffn=384, vocab=500, qk_norm=False)
+    resident = MoeWeights.synthetic(cfg, cuda, seed=5)
+    host = MoeWeights.synthetic(cfg, cuda, seed=5, host_experts=True)
+    for i, layer in enumerate(resident.layers):
+        assert torch.equal(host.host.pages[i].to(cuda), layer.pages)
+    prompts = [([1, 2, 3], 10), ([7], 20), ([9, 9, 9, 9, 9], 6), ([4, 5], 12), ([300], 8), ([11, 12], 5)]
+    outs, decs = [], []
+    for w in (resident, host):
+        dec = MoeDecoder(w, max_rows=4, max_seq_len=64, device=cuda,
+                         expert_cache_bytes=10 * w.layout.page_stride if w.host is not None else None)
+        bat = MoeContinuousBatcher(dec, max_context_tokens=64, graph=False)
+        ids = [bat.submit(p, max_new_tokens=n) for p, n in prompts]
+        out = bat.run()
+        outs.append([out[i] for i in ids])
+        decs.append(dec)
+        assert bat.pool.telemetry().slot_reuses == 2
+    assert outs[0] == outs[1]
+    assert [len(o) for o in outs[1]] == [n for _, n in prompts]
+    st = decs[1].expert_cache.stats
+    assert st.misses > 0 and st.evictions > 0 and st.bytes_h2d > 0
 
 
 def test_moe_routes_match_oracle_first_layer(cuda):
