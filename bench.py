@@ -870,8 +870,10 @@ def run_stream_case(args) -> None:
     sequences with 1024-token committed contexts (random K/V pages stand in for their
     prefill) through ``MoeContinuousBatcher``. A quarter of the first sequences end two steps
     into the timed region and queued ones take their slots, so admission and retirement run
-    under load. Each layer's copies are planned on the host from its routes (the reference's
-    ExpertPageCache, global LRU with route-history prefetch), so the step runs eagerly. The
+    under load. Each layer's copies are planned on the host from its routes, so the step runs
+    eagerly. Two residency rules are timed in turn on the same running batch: the reference's
+    global LRU with route-history prefetch (which, under the every-page-every-step scan of a
+    256-row batch, misses every page) and this build's resident-prefix rule (the `value`). The
     bound is the host link: the step's H2D bytes over the measured pinned copy bandwidth of
     the same pages. Prints one JSON line; not the headline metric."""
     import numpy as np
@@ -907,24 +909,32 @@ def run_stream_case(args) -> None:
         bat.submit_with_context(int(first[i]), context, max_new_tokens=short if i % 4 == 3 else new_tokens)
     for i in range(rows, rows + rows // 4):  # waiting for the slots the short ones free
         bat.submit_with_context(int(first[i]), context, max_new_tokens=new_tokens)
-    cache = dec.expert_cache
-    for _ in range(args.warmup):
-        bat.step()
-    torch.cuda.synchronize(device)
-    h2d0, gen0, steps0 = cache.stats.bytes_h2d, bat.generated, bat.steps
     stream = torch.cuda.current_stream(device)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clocks:
-        e0.record(stream)
-        for _ in range(args.steps):
+
+    def arm(policy: str, warmup: int):
+        dec.set_expert_cache(cache_policy=policy, route_prefetch=True)
+        for _ in range(warmup):
             bat.step()
-        e1.record(stream)
         torch.cuda.synchronize(device)
-    step_s = e0.elapsed_time(e1) / 1000.0 / args.steps
-    h2d = (cache.stats.bytes_h2d - h2d0) / args.steps
-    tokens = bat.generated - gen0
-    dec.check_errors()
+        h2d0, gen0 = dec.expert_cache.stats.bytes_h2d, bat.generated
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clocks:
+            e0.record(stream)
+            for _ in range(args.steps):
+                bat.step()
+            e1.record(stream)
+            torch.cuda.synchronize(device)
+        dec.check_errors()
+        return {"step_s": e0.elapsed_time(e1) / 1000.0 / args.steps,
+                "h2d": (dec.expert_cache.stats.bytes_h2d - h2d0) / args.steps, "tokens": bat.generated - gen0,
+                "clocks": clocks.summary(), "report": dec.expert_cache.report()}
+
+    steps0 = bat.steps
+    lru = arm("global-lru-v1", args.warmup)
+    best = arm("resident-prefix-v1", 2)  # two steps fill the resident prefix
+    cache = dec.expert_cache
+    step_s, h2d, tokens = best["step_s"], best["h2d"], best["tokens"]
     tele = bat.pool.telemetry()
     # the link's measured ceiling: the same number of page copies, back to back on one stream
     stride = weights.layout.page_stride
@@ -960,6 +970,7 @@ def run_stream_case(args) -> None:
                    "rows": rows, "context": context, "decode_tokens": new_tokens,
                    "cache_slots": cache.capacity, "page_bytes": stride, "cache_policy": cache.residency.cache_policy,
                    "route_prefetch": bool(cache.residency.route_prefetch),
+                   "resident_prefix_pages": cache.residency.prefix_pages,
                    "l2": "no flush: each step moves >= 40 GB over the host link and reads ~37 GB of K/V"},
         "tokens_generated": tokens,
         "h2d_bytes_per_step": h2d,
@@ -969,12 +980,16 @@ def run_stream_case(args) -> None:
                      "traffic": None},
         "continuous": {"allocations": tele.allocations, "releases": tele.releases, "slot_reuses": tele.slot_reuses,
                        "peak_active_slots": tele.peak_active_slots, "rows_per_step": bat.rows_stepped / bat.steps,
-                       "steps_run": bat.steps, "steps_timed": bat.steps - steps0},
-        "cache": cache.report(),
+                       "steps_run": bat.steps - steps0, "steps_timed_per_rule": args.steps},
+        "cache": best["report"],
+        "reference_policy": {"cache_policy": "global-lru-v1 + route prefetch", "tokens_per_s": lru["tokens"] / (
+            lru["step_s"] * args.steps), "ms_per_step": lru["step_s"] * 1000.0, "h2d_bytes_per_step": lru["h2d"],
+            "h2d_gbs": lru["h2d"] / lru["step_s"] / 1e9, "hit_rate": lru["report"]["residency"]["hit_rate"],
+            "clocks": lru["clocks"]},
         "host_tier_gb": weights.host.nbytes / 1e9, "build_seconds": build_s,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 8 * rows, "d2h_bytes_per_step": 8 * rows,
                 "note": "value is already measured through the batcher (token ids in, ids out each step)"},
-        "clocks": clocks.summary(),
+        "clocks": best["clocks"],
     }
     print(json.dumps(line), flush=True)
 

@@ -256,14 +256,10 @@ class MoeDecoder:
                            for L in weights.layers]
             self.backend = None
         elif self.streamed:
-            # experts stream from the pinned host tier into an HBM slot cache (25 % of the
-            # expert bytes unless told otherwise); each layer's routes are read on the host to
-            # plan its copies, as the reference's ExpertPageCache does, so the step runs eagerly
-            budget = int(expert_cache_bytes if expert_cache_bytes is not None else weights.host.nbytes // 4)
             self.ep = None
-            self.expert_cache = ExpertPageCache(weights.host, budget_bytes=budget, device=device,
-                                                route_prefetch=route_prefetch, cache_policy=cache_policy)
-            self.backend = PagedInt8ExpertBackend(self.expert_cache, num_experts=cfg.experts)
+            self.backend = None
+            self.set_expert_cache(budget_bytes=expert_cache_bytes, cache_policy=cache_policy,
+                                  route_prefetch=route_prefetch)
         else:
             self.ep = None
             self.backend = PagedInt8ExpertBackend(
@@ -275,6 +271,22 @@ class MoeDecoder:
         # set to {"layer": i} before an eager step to keep that layer's MoE input, routes and
         # output (clones) in the dict
         self.probe: dict | None = None
+
+    def set_expert_cache(self, *, budget_bytes: int | None = None, cache_policy: str | None = None,
+                         route_prefetch: bool = True) -> None:
+        """(Re)build the HBM slot cache the host-tier experts stream through: ``budget_bytes``
+        (25 % of the expert bytes when None) under ``cache_policy``. Each layer's routes are
+        read on the host to plan its copies, as the reference's ExpertPageCache does, so a
+        streamed step runs eagerly. The previous cache's slots are freed first."""
+        if not self.streamed:
+            raise RuntimeError("the decoder's experts are resident in HBM")
+        torch.cuda.synchronize(self.device)
+        host = self.w.host
+        budget = int(budget_bytes if budget_bytes is not None else host.nbytes // 4)
+        self.backend = self.expert_cache = None
+        self.expert_cache = ExpertPageCache(host, budget_bytes=budget, device=self.device,
+                                            route_prefetch=route_prefetch, cache_policy=cache_policy)
+        self.backend = PagedInt8ExpertBackend(self.expert_cache, num_experts=self.cfg.experts)
 
     # ------------------------------------------------------------------ context
 

@@ -19,6 +19,13 @@ executes the plans on a copy stream). The rules are the reference's
 * route prefetch: after layer L the pages the previous step routed at layer L+1 are reserved
   and copied ahead.
 
+One rule is this build's own, for decode steps that touch every page of every layer in
+layer order (every expert hit at large batch): under that cyclic scan any LRU rule with a
+budget below the working set evicts each page just before its next use (hit rate 0).
+``resident-prefix-v1`` keeps the first ``capacity - ring`` pages ever admitted resident for
+good and runs LRU over the remaining ``ring = 2 x max_active_pages`` slots (one layer's active
+set plus the next layer's prefetch), so a 25 % budget saves the prefix's share of the copies.
+
 Slots come from a free stack (slot 0 first; released slots are reused last-in first-out),
 so physical slot numbers match the reference's for the same sequence of acquisitions.
 """
@@ -32,7 +39,8 @@ from dataclasses import dataclass, field
 
 GLOBAL_LRU = "global-lru-v1"
 LAYER_FREQUENCY_LRU = "layer-frequency-lru-v1"
-CACHE_POLICIES = (GLOBAL_LRU, LAYER_FREQUENCY_LRU)
+RESIDENT_PREFIX = "resident-prefix-v1"
+CACHE_POLICIES = (GLOBAL_LRU, LAYER_FREQUENCY_LRU, RESIDENT_PREFIX)
 CACHE_FILL_PREFILL = "cache-fill-v1"
 TRANSIENT_FREQUENCY_PREFILL = "transient-frequency-v1"
 PREFILL_POLICIES = (CACHE_FILL_PREFILL, TRANSIENT_FREQUENCY_PREFILL)
@@ -117,6 +125,8 @@ class ExpertResidency:
         self.route_prefetch = bool(route_prefetch)
         base, extra = divmod(self.capacity, self.layers)
         self.layer_quotas = tuple(base + (1 if layer < extra else 0) for layer in range(self.layers))
+        ring = 2 * self.max_active_pages
+        self.prefix_pages = max(0, self.capacity - ring) if cache_policy == RESIDENT_PREFIX else 0
         self.reset(clear_pages=True)
 
     # ---- state
@@ -130,6 +140,7 @@ class ExpertResidency:
             self.decode_protected: set[PageKey] = set()
             self.free_slots = list(range(self.capacity - 1, -1, -1))
             self.layer_counts = [0] * self.layers
+            self.pinned: set[PageKey] = set()
 
     def slot_of(self, key: PageKey) -> int | None:
         return self.entries.get(key)
@@ -137,6 +148,9 @@ class ExpertResidency:
     def _victim(self, key: PageKey, protected: set[PageKey]) -> tuple[PageKey | None, str]:
         def first(pred) -> PageKey | None:
             return next((k for k in self.entries if k not in protected and pred(k)), None)
+
+        if self.cache_policy == RESIDENT_PREFIX:
+            return first(lambda k: k not in self.pinned), "fallback"
 
         if self.cache_policy == LAYER_FREQUENCY_LRU:
             layer = key[0]
@@ -165,6 +179,8 @@ class ExpertResidency:
             self.stats[f"{reason}_evictions"] += 1
         self.entries[key] = slot
         self.layer_counts[key[0]] += 1
+        if len(self.pinned) < self.prefix_pages:
+            self.pinned.add(key)
         return slot
 
     def _count_request(self, n: int, misses: int) -> None:
@@ -422,7 +438,7 @@ def main(argv: Sequence[str] | None = None) -> int:
     return 0
 
 
-__all__ = ["AcquirePlan", "CACHE_FILL_PREFILL", "CACHE_POLICIES", "ExpertResidency", "GLOBAL_LRU",
+__all__ = ["AcquirePlan", "CACHE_FILL_PREFILL", "CACHE_POLICIES", "ExpertResidency", "GLOBAL_LRU", "RESIDENT_PREFIX",
            "LAYER_FREQUENCY_LRU", "PREFILL_POLICIES", "PageTrace", "ResidencyStats", "TRANSIENT_FREQUENCY_PREFILL",
            "TransientPlan", "options_from_env", "replay", "replay_ab"]
 

@@ -84,7 +84,8 @@ def test_moe_decode_steps_match_oracle(graph, cuda):
 
 def test_streamed_experts_decode_like_resident_pages(cuda):
     """Continuous batching over the Mixtral form: the decoder whose expert pages stream from a
-    pinned host tier through an HBM slot cache of 10 of the 24 pages generates, for
+    pinned host tier through an HBM slot cache (10 of the 24 pages under global LRU; 20 under
+    the resident-prefix rule, 4 of them held for good) generates, for
     every request, the tokens of the decoder holding every page in HBM (both eager over the
     same rows, so every kernel sees the same inputs; the pages are the same bytes)."""
     from mrun_b200.continuous import MoeContinuousBatcher
@@ -98,19 +99,22 @@ def test_streamed_experts_decode_like_resident_pages(cuda):
         assert torch.equal(host.host.pages[i].to(cuda), layer.pages)
     prompts = [([1, 2, 3], 10), ([7], 20), ([9, 9, 9, 9, 9], 6), ([4, 5], 12), ([300], 8), ([11, 12], 5)]
     outs, decs = [], []
-    for w in (resident, host):
-        dec = MoeDecoder(w, max_rows=4, max_seq_len=64, device=cuda,
-                         expert_cache_bytes=10 * w.layout.page_stride if w.host is not None else None)
+    for w, policy in ((resident, None), (host, "global-lru-v1"), (host, "resident-prefix-v1")):
+        dec = MoeDecoder(w, max_rows=4, max_seq_len=64, device=cuda, cache_policy=policy,
+                         expert_cache_bytes=(20 if policy == "resident-prefix-v1" else 10) * w.layout.page_stride
+                         if w.host is not None else None)
         bat = MoeContinuousBatcher(dec, max_context_tokens=64, graph=False)
         ids = [bat.submit(p, max_new_tokens=n) for p, n in prompts]
         out = bat.run()
         outs.append([out[i] for i in ids])
         decs.append(dec)
         assert bat.pool.telemetry().slot_reuses == 2
-    assert outs[0] == outs[1]
+    assert outs[0] == outs[1] == outs[2]
     assert [len(o) for o in outs[1]] == [n for _, n in prompts]
-    st = decs[1].expert_cache.stats
-    assert st.misses > 0 and st.evictions > 0 and st.bytes_h2d > 0
+    for dec in decs[1:]:
+        st = dec.expert_cache.stats
+        assert st.misses > 0 and st.evictions > 0 and st.bytes_h2d > 0
+    assert decs[2].expert_cache.residency.prefix_pages == 4  # 20 slots - 2 x 8 active
 
 
 def test_moe_routes_match_oracle_first_layer(cuda):

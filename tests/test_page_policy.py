@@ -147,3 +147,31 @@ def test_reference_environment_switches():
     with pytest.warns(UserWarning, match="unknown"):
         assert store_options_from_env(environ={"MRUN_QSTORE_CACHE_POLICY": "mru"})["cache_policy"] == "pin-fill"
     assert store_options_from_env(cache_policy="lru", environ={"MRUN_QSTORE_CACHE_POLICY": "mru"})["cache_policy"] == "lru"
+
+
+def test_resident_prefix_keeps_its_pages_under_a_cyclic_scan():
+    """Decode steps that touch every page of every layer in layer order: the reference's LRU
+    rules evict each page just before its next use (no hits at a 25 % budget);
+    resident-prefix-v1 keeps the first capacity - 2 x active pages admitted for good, so every
+    step after the first hits exactly those."""
+    from mrun_b200.page_policy import RESIDENT_PREFIX
+
+    layers, experts, cap = 32, 8, 64
+    trace = PageTrace(layers, 8)
+    steps = 5
+    for step in range(steps):
+        for layer in range(layers):
+            trace.record(phase="decode", step=step, layer=layer, routed=list(range(experts)) * 4)
+    lru = replay(trace, capacity_pages=cap, cache_policy=GLOBAL_LRU, prefill_page_policy=CACHE_FILL_PREFILL,
+                 max_active_pages=experts)
+    assert lru["page_hits"] == 0
+    got = replay(trace, capacity_pages=cap, cache_policy=RESIDENT_PREFIX, prefill_page_policy=CACHE_FILL_PREFILL,
+                 max_active_pages=experts)
+    prefix = cap - 2 * experts
+    assert got["page_hits"] == (steps - 1) * prefix
+    assert sorted(map(tuple, got["resident"]))[:prefix] == [(l, e) for l in range(prefix // experts)
+                                                            for e in range(experts)]
+    # the ring alone: with no room for a prefix the rule is plain LRU
+    small = replay(trace, capacity_pages=16, cache_policy=RESIDENT_PREFIX, prefill_page_policy=CACHE_FILL_PREFILL,
+                   max_active_pages=experts)
+    assert small["page_hits"] == 0 and small["evictions"] == lru["evictions"] + (cap - 16)
