@@ -218,7 +218,7 @@ class MoeContinuousBatcher:
         if not prompt:
             raise ValueError("prompt must hold at least one token")
         _strict_positive_int(max_new_tokens, "max_new_tokens")
-        if len(prompt) + max_new_tokens + 1 > self.pool.max_context_tokens:
+        if len(prompt) + max_new_tokens > self.pool.max_context_tokens:
             raise OverflowError("requested Qwen K/V capacity exceeds the fixed slot arena")
         req = _Request(self._next_id, prompt, int(max_new_tokens), eos)
         self._next_id += 1
@@ -233,7 +233,7 @@ class MoeContinuousBatcher:
         the pages keep what they hold, which the synthetic benchmarks fill with random K/V)."""
         context_tokens = _strict_positive_int(context_tokens, "context_tokens")
         _strict_positive_int(max_new_tokens, "max_new_tokens")
-        if context_tokens + max_new_tokens + 1 > self.pool.max_context_tokens:
+        if context_tokens + 1 + max_new_tokens > self.pool.max_context_tokens:
             raise OverflowError("requested Qwen K/V capacity exceeds the fixed slot arena")
         req = _Request(self._next_id, [int(first_token)], int(max_new_tokens), eos, context=context_tokens,
                        prefill=prefill)
@@ -255,8 +255,10 @@ class MoeContinuousBatcher:
         while self._queue and len(self._active) < self.slots:
             req = self._queue[0]
             req.state_id = f"moe-request-{req.request_id}"
+            # the last generated token is never fed back: positions end at
+            # context + len(prompt) + max_new_tokens - 2
             req.slot, req.generation, lease = self.pool.acquire(
-                req.state_id, req.context + len(req.prompt) + req.max_new_tokens + 1)
+                req.state_id, req.context + len(req.prompt) + req.max_new_tokens)
             self._queue.popleft()
             if req.prefill is not None:
                 req.prefill(lease)

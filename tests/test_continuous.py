@@ -207,7 +207,7 @@ def test_batcher_eos_and_limits():
     with pytest.raises(ValueError, match="max_new_tokens must be a positive integer"):
         bat.submit([1], max_new_tokens=0)
     with pytest.raises(OverflowError):
-        bat.submit([1] * 60, max_new_tokens=4)
+        bat.submit([1] * 61, max_new_tokens=4)
     assert bat.step() == {} and bat.pending == 0
 
 
@@ -238,7 +238,7 @@ def test_batcher_eager_prefix_and_prefilled_context():
     r2 = bat.submit([9], max_new_tokens=8)
     first = bat.step()
     assert first == {} and dec.rows_seen == [3]
-    assert len(leases) == 1 and leases[0].slot == 0 and leases[0].capacity == 27
+    assert len(leases) == 1 and leases[0].slot == 0 and leases[0].capacity == 26
     assert dec.positions[0] == 21  # the prefilled row decoded its first token at position 20
     out = {**first, **bat.run()}
     assert out[r1] == _alone([3, 4], 3) and out[r2] == _alone([9], 8)
