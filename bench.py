@@ -875,34 +875,48 @@ def run_stream_case(args) -> None:
     global LRU with route-history prefetch (which, under the every-page-every-step scan of a
     256-row batch, misses every page) and this build's resident-prefix rule (the `value`). The
     bound is the host link: the step's H2D bytes over the measured pinned copy bandwidth of
-    the same pages. Prints one JSON line; not the headline metric."""
+    the same pages. Under torchrun with N GPUs the experts are sharded (each GPU owns 8/N
+    experts per layer, keeps them in its own host tier and streams them over its own link
+    under a budget of 25 % of the bytes it owns), every GPU decodes its own 256 sequences
+    (weak scaling) and the rows meet their experts over the peer-memory exchange; `value` is
+    the job's tokens over the slowest rank's time. Prints one JSON line (rank 0); not the
+    headline metric."""
     import numpy as np
     import psutil
     import torch
 
     from mrun_b200 import _lib
     from mrun_b200.continuous import MoeContinuousBatcher
+    from mrun_b200.expert_parallel import ExpertShard
     from mrun_b200.moe_engine import MoeConfig, MoeDecoder, MoeWeights
 
+    world, rank, local = _dist_setup(args.gpus)
     cfg = MoeConfig.mixtral_8x7b()
     rows, context, new_tokens = 256, 1024, 128
-    device = torch.device("cuda", 0)
+    device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     expert_bytes = cfg.num_layers * cfg.experts * (3 * cfg.hidden * cfg.expert_ffn)
-    if expert_bytes > 0.8 * psutil.virtual_memory().available:
+    if expert_bytes > 0.8 * psutil.virtual_memory().available:  # every rank's share on one host
         raise SystemExit(f"config 5 needs {expert_bytes / 1e9:.1f} GB of pinned host memory; "
                          f"{psutil.virtual_memory().available / 1e9:.1f} GB available")
+    shard = ExpertShard(world, rank, cfg.experts) if world > 1 else None
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        group = dist.group.WORLD
     t0 = time.perf_counter()
-    weights = MoeWeights.synthetic(cfg, device, host_experts=True)
+    weights = MoeWeights.synthetic(cfg, device, shard=shard, host_experts=True)
     build_s = time.perf_counter() - t0
     max_ctx = context + new_tokens + 1
-    dec = MoeDecoder(weights, max_rows=rows, max_seq_len=max_ctx, device=device)
+    dec = MoeDecoder(weights, max_rows=rows, max_seq_len=max_ctx, device=device, group=group, world=world,
+                     exchange="p2p")
     bat = MoeContinuousBatcher(dec, max_context_tokens=max_ctx)
-    gen = torch.Generator(device=device).manual_seed(0)
+    gen = torch.Generator(device=device).manual_seed(rank)
     for layer in range(cfg.num_layers):  # committed contexts: random bf16 K/V in every page
         dec.kv.k[layer].normal_(0.0, 1.0, generator=gen)
         dec.kv.v[layer].normal_(0.0, 1.0, generator=gen)
-    rng = np.random.default_rng(0)
+    rng = np.random.default_rng(rank)
     first = rng.integers(0, cfg.vocab, rows + rows // 4)
     short = args.warmup + 2
     for i in range(rows):
@@ -916,17 +930,20 @@ def run_stream_case(args) -> None:
         for _ in range(warmup):
             bat.step()
         torch.cuda.synchronize(device)
+        _barrier(world)
         h2d0, gen0 = dec.expert_cache.stats.bytes_h2d, bat.generated
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(0) as clocks:
+        with ClockSampler(local) as clocks:
             e0.record(stream)
             for _ in range(args.steps):
                 bat.step()
             e1.record(stream)
             torch.cuda.synchronize(device)
+        _barrier(world)
         dec.check_errors()
-        return {"step_s": e0.elapsed_time(e1) / 1000.0 / args.steps,
+        elapsed = _max_over_ranks(e0.elapsed_time(e1) / 1000.0, world)
+        return {"step_s": elapsed / args.steps,
                 "h2d": (dec.expert_cache.stats.bytes_h2d - h2d0) / args.steps, "tokens": bat.generated - gen0,
                 "clocks": clocks.summary(), "report": dec.expert_cache.report()}
 
@@ -940,7 +957,7 @@ def run_stream_case(args) -> None:
     stride = weights.layout.page_stride
     n_pages = max(1, int(round(h2d / stride)))
     slot_ids = torch.tensor([i % cache.capacity for i in range(n_pages)], dtype=torch.int32)
-    page_ids = torch.tensor([i % (cfg.num_layers * cfg.experts) for i in range(n_pages)], dtype=torch.int32)
+    page_ids = torch.tensor([i % (cfg.num_layers * weights.experts_local) for i in range(n_pages)], dtype=torch.int32)
 
     def copy_only():
         _lib.call("mrb_copy_pages", cache.slots.data_ptr(), stride, weights.host.pages.data_ptr(), stride,
@@ -956,10 +973,19 @@ def run_stream_case(args) -> None:
     torch.cuda.synchronize(device)
     copy_s = c0.elapsed_time(c1) / 1000.0
     link_gbs = n_pages * stride / copy_s / 1e9
-    value = tokens / (step_s * args.steps)
+    value = tokens * world / (step_s * args.steps)  # every rank generates the same count
+    if world > 1:
+        import torch.distributed as dist
+
+        _barrier(world)
+        dec.close()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
     line = {
         "case": "stream-decode", "metric": "MoE decode tokens/s with host-paged experts (config 5)",
-        "unit": "tokens/s", "value": value, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "unit": "tokens/s", "value": value, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "scaling": "weak", "parallelism": f"ep{world}" if world > 1 else "ep1",
         "ms_per_step": step_s * 1000.0, "higher_is_better": True, "dtype": "bf16",
         "weights": "int8 per-channel expert pages in pinned host memory; int8 qrow dense weights in HBM",
         "data": "synthetic: random-init int8 weights (seeded), random token ids, random bf16 K/V contexts",
@@ -967,13 +993,14 @@ def run_stream_case(args) -> None:
                                "8 int8 experts top-2 of 176 MB, vocab 32000), 256 continuously batched "
                                "sequences, 1024-token contexts, experts streamed from pinned host memory "
                                "into an HBM slot cache of 25% of the expert bytes",
-                   "rows": rows, "context": context, "decode_tokens": new_tokens,
+                   "rows_per_gpu": rows, "global_batch": rows * world, "context": context,
+                   "decode_tokens": new_tokens, "experts_per_gpu": weights.experts_local,
                    "cache_slots": cache.capacity, "page_bytes": stride, "cache_policy": cache.residency.cache_policy,
                    "route_prefetch": bool(cache.residency.route_prefetch),
                    "resident_prefix_pages": cache.residency.prefix_pages,
                    "l2": "no flush: each step moves >= 40 GB over the host link and reads ~37 GB of K/V"},
-        "tokens_generated": tokens,
-        "h2d_bytes_per_step": h2d,
+        "tokens_generated": tokens * world,
+        "h2d_bytes_per_step_per_gpu": h2d,
         "roofline": {"bound": "host link", "achieved": h2d / step_s / 1e9, "peak": link_gbs,
                      "peak_source": "measured: the same number of 176 MB page copies, pinned host -> HBM, "
                                     "back to back", "unit": "GB/s", "frac": h2d / step_s / 1e9 / link_gbs,
@@ -982,12 +1009,13 @@ def run_stream_case(args) -> None:
                        "peak_active_slots": tele.peak_active_slots, "rows_per_step": bat.rows_stepped / bat.steps,
                        "steps_run": bat.steps - steps0, "steps_timed_per_rule": args.steps},
         "cache": best["report"],
-        "reference_policy": {"cache_policy": "global-lru-v1 + route prefetch", "tokens_per_s": lru["tokens"] / (
+        "reference_policy": {"cache_policy": "global-lru-v1 + route prefetch", "tokens_per_s": lru["tokens"] * world / (
             lru["step_s"] * args.steps), "ms_per_step": lru["step_s"] * 1000.0, "h2d_bytes_per_step": lru["h2d"],
             "h2d_gbs": lru["h2d"] / lru["step_s"] / 1e9, "hit_rate": lru["report"]["residency"]["hit_rate"],
             "clocks": lru["clocks"]},
         "host_tier_gb": weights.host.nbytes / 1e9, "build_seconds": build_s,
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 8 * rows, "d2h_bytes_per_step": 8 * rows,
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 8 * rows * world,
+                "d2h_bytes_per_step": 8 * rows * world,
                 "note": "value is already measured through the batcher (token ids in, ids out each step)"},
         "clocks": best["clocks"],
     }

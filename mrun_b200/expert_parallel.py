@@ -188,20 +188,32 @@ class P2PExpertParallelMoE:
     bit-identical to one GPU and to the NCCL exchange. One instance per call site (each MoE
     layer) and per process group; every rank must call forward in the same order. ``close()``
     unmaps the peers' mailboxes and frees this rank's (after the last use, before the process
-    group goes away)."""
+    group goes away).
 
-    def __init__(self, shard: ExpertShard, pages: torch.Tensor, layout, *, tokens: int, k: int, hidden: int,
-                 group=None) -> None:
+    Without resident ``pages`` (None, with ``device`` given) the pages come from
+    ``page_cache``, a ``streaming.ExpertPageCache`` over a host tier holding this rank's
+    experts only: each call acquires every local expert page of ``layer`` before the expert
+    MLP -- a static plan, so no routes are read on the host (at large batch every local expert
+    receives rows) -- and releases the slots after it; such calls run eagerly, not in a CUDA
+    graph. The owner sets ``page_cache`` (it may swap the cache between calls)."""
+
+    def __init__(self, shard: ExpertShard, pages: torch.Tensor | None, layout, *, tokens: int, k: int, hidden: int,
+                 group=None, page_cache=None, layer: int = 0, device: torch.device | None = None) -> None:
         import ctypes
 
         from . import _lib
 
+        if pages is None and device is None:
+            raise ValueError("give the resident expert pages, or the device of a streamed layer")
         self.shard = shard
         self.pages = pages
+        self.page_cache = page_cache
+        self.layer = int(layer)
+        self._local_ids = torch.arange(shard.per_rank, dtype=torch.int64)  # on the host: no sync to plan
         self.layout = layout
         self.group = group
         self.tokens, self.k, self.hidden = int(tokens), int(k), int(hidden)
-        device = pages.device
+        device = pages.device if pages is not None else torch.device(device)
         self.device = device
         world, rank = shard.world, shard.rank
         self.cap = self.tokens * self.k
@@ -273,9 +285,17 @@ class P2PExpertParallelMoE:
                   self.zeros.data_ptr(), self.rt_counts.data_ptr(), self.rt_starts.data_ptr(),
                   self.rt_token_ids.data_ptr(), self.rt_coef.data_ptr(), self.rt_inverse.data_ptr(),
                   self.state.data_ptr(), stream)
+        if self.pages is None:
+            if self.page_cache is None or self.page_cache.host.experts != per:
+                raise ValueError("a streamed layer needs a page cache over this rank's experts")
+            pages, slot_of = self.page_cache.layer_pages(self.layer, self._local_ids)
+        else:
+            pages, slot_of = self.pages, None
         eo = _grouped_mlp_from_pointer(self._own + self.offsets[4], self.rt_token_ids, self.rt_starts,
-                                       self.rt_counts, self.pages, self.layout, hidden, device, self.mlp_sync,
-                                       rows=slots)
+                                       self.rt_counts, pages, self.layout, hidden, device, self.mlp_sync,
+                                       rows=slots, slot_of=slot_of)
+        if self.pages is None:
+            self.page_cache.release_layer()  # its slots may be refilled once these kernels are done
         _lib.call("mrb_ep_p2p_return", eo.data_ptr(), self.rt_inverse.data_ptr(), hidden, world, sh.rank, cap,
                   self.mailboxes.data_ptr(), self.state.data_ptr(), stream)
         # wait for every owner's return + the fixed-rank combine, in one launch
@@ -303,9 +323,11 @@ class P2PExpertParallelMoE:
 
 
 def _grouped_mlp_from_pointer(rows_ptr: int, token_ids, starts, counts, pages, layout, hidden: int, device,
-                              sync: torch.Tensor | None = None, rows: int | None = None):
+                              sync: torch.Tensor | None = None, rows: int | None = None,
+                              slot_of: torch.Tensor | None = None):
     """grouped_expert_mlp over activation rows given by a raw device pointer (a mailbox).
-    ``rows``: the assignment slots the outputs are indexed by (default token_ids' length)."""
+    ``rows``: the assignment slots the outputs are indexed by (default token_ids' length);
+    ``slot_of``: int32 [experts] page slot of each expert in ``pages`` (None: identity)."""
     from . import _lib
     from .moe import expert_mlp_sync
 
@@ -319,8 +341,8 @@ def _grouped_mlp_from_pointer(rows_ptr: int, token_ids, starts, counts, pages, l
         sync = expert_mlp_sync(e, device)
     _lib.call("mrb_grouped_expert_mlp", rows_ptr, token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
               pages.data_ptr(), ly.page_stride, ly.gate_up_codes_offset, ly.gate_up_scales_offset,
-              ly.down_codes_offset, ly.down_scales_offset, None, hidden, f, a, act.data_ptr(), y.data_ptr(),
-              sync.data_ptr(), _lib.stream_handle(device))
+              ly.down_codes_offset, ly.down_scales_offset, _lib.ptr(slot_of), hidden, f, a, act.data_ptr(),
+              y.data_ptr(), sync.data_ptr(), _lib.stream_handle(device))
     return y
 
 

@@ -242,15 +242,21 @@ class MoeDecoder:
         self.world = int(world)
         self.group = group
         self.streamed = weights.host is not None
-        if self.streamed and self.world > 1:
-            raise ValueError("host-tier experts run on one GPU (no expert-parallel streaming)")
+        if self.streamed and self.world > 1 and exchange != "p2p":
+            raise ValueError("host-tier experts stream only under the peer-memory exchange")
+        self.expert_cache = None
         if self.world > 1:
             shard = ExpertShard(self.world, torch.distributed.get_rank(group), cfg.experts)
             if exchange not in ("p2p", "nccl"):
                 raise ValueError(f"unknown expert exchange {exchange!r}")
             if exchange == "p2p":
                 self.ep = [P2PExpertParallelMoE(shard, L.pages, weights.layout, tokens=self.max_rows, k=cfg.top_k,
-                                                hidden=cfg.hidden, group=group) for L in weights.layers]
+                                                hidden=cfg.hidden, group=group, layer=i, device=device)
+                           for i, L in enumerate(weights.layers)]
+                if self.streamed:  # each rank streams its own experts under its own budget
+                    self.backend = None
+                    self.set_expert_cache(budget_bytes=expert_cache_bytes, cache_policy=cache_policy,
+                                          route_prefetch=route_prefetch)
             else:
                 self.ep = [FixedCapacityExpertParallelMoE(shard, L.pages, weights.layout, group=group)
                            for L in weights.layers]
@@ -275,7 +281,7 @@ class MoeDecoder:
     def set_expert_cache(self, *, budget_bytes: int | None = None, cache_policy: str | None = None,
                          route_prefetch: bool = True) -> None:
         """(Re)build the HBM slot cache the host-tier experts stream through: ``budget_bytes``
-        (25 % of the expert bytes when None) under ``cache_policy``. Each layer's routes are
+        (25 % of the expert bytes this GPU owns when None) under ``cache_policy``. Each layer's routes are
         read on the host to plan its copies, as the reference's ExpertPageCache does, so a
         streamed step runs eagerly. The previous cache's slots are freed first."""
         if not self.streamed:
@@ -283,10 +289,16 @@ class MoeDecoder:
         torch.cuda.synchronize(self.device)
         host = self.w.host
         budget = int(budget_bytes if budget_bytes is not None else host.nbytes // 4)
+        for ep in self.ep or []:
+            ep.page_cache = None
         self.backend = self.expert_cache = None
         self.expert_cache = ExpertPageCache(host, budget_bytes=budget, device=self.device,
                                             route_prefetch=route_prefetch, cache_policy=cache_policy)
-        self.backend = PagedInt8ExpertBackend(self.expert_cache, num_experts=self.cfg.experts)
+        if self.ep is not None:  # expert parallel: the cache holds this rank's experts only
+            for ep in self.ep:
+                ep.page_cache = self.expert_cache
+        else:
+            self.backend = PagedInt8ExpertBackend(self.expert_cache, num_experts=self.cfg.experts)
 
     # ------------------------------------------------------------------ context
 

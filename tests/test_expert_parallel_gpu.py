@@ -1,7 +1,8 @@
 """Expert parallelism on 2+ GPUs: each rank's MoE output must be bit-identical to the
 single-GPU backend over all experts, for the host-sized NCCL exchange, the fixed-capacity NCCL
 exchange (eager and replayed from a CUDA graph) and the fixed-capacity exchange over NVLink
-peer memory (eager and graph-replayed, no wait timed out). Skipped with fewer than 2 GPUs."""
+peer memory (eager and graph-replayed, no wait timed out), also with each rank's expert pages
+streamed from a pinned host tier through a slot cache. Skipped with fewer than 2 GPUs."""
 from __future__ import annotations
 
 import datetime
@@ -92,6 +93,27 @@ def _worker(rank, world, port, q):
         del graph
         dist.barrier()
         p2p.close()
+        # the same exchange with this rank's pages streamed from a pinned host tier: two layers
+        # holding the same pages share a slot cache of one layer's pages, so every call evicts
+        from mrun_b200.streaming import ExpertPageCache, HostPageTier
+
+        tier = HostPageTier(ly, 2, shard.per_rank)
+        tier.pages[0].copy_(mine)
+        tier.pages[1].copy_(mine)
+        cache = ExpertPageCache(tier, budget_bytes=shard.per_rank * ly.page_stride, device=dev,
+                                cache_policy="global-lru-v1", route_prefetch=False)
+        layers = [P2PExpertParallelMoE(shard, None, ly, tokens=T, k=K, hidden=H, layer=i, device=dev)
+                  for i in range(2)]
+        for layer in layers:
+            layer.page_cache = cache
+        streamed = [layers[i % 2].forward(x, idx, w) for i in range(3)]
+        torch.cuda.synchronize()
+        for layer in layers:
+            layer.check()
+        ok = ok and all(bool(torch.equal(o, single)) for o in streamed) and cache.stats.evictions > 0
+        dist.barrier()
+        for layer in layers:
+            layer.close()
         q.put((rank, ok, ep.last_stats))
         dist.barrier()
     finally:
