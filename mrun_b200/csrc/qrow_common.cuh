@@ -38,6 +38,23 @@ __device__ __forceinline__ void i8x4_to_bf16x2(uint32_t w, uint32_t& lo, uint32_
   hi = prmt(__float_as_uint(f2), __float_as_uint(f3), 0x7632u);
 }
 
+// Four signed int8 codes -> bf16x2 of bytes (0,1) and bf16x2 of bytes (2,3), exactly, in
+// integer ops: the low seven bits m of each byte go under the bf16 exponent of 128 (128 + m,
+// exact with 7 mantissa bits), and 128 (q >= 0) or 256 (q < 0, where m = q + 128) is
+// subtracted in one bf16x2 sub, whose result q is exact.
+__device__ __forceinline__ void i8x4_to_bf16x2_exact(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t mag = w & 0x7F7F7F7Fu;
+  const uint32_t sgn = w & 0x80808080u;
+  const uint32_t v01 = prmt(mag, 0x43434343u, 0x5140u), v23 = prmt(mag, 0x43434343u, 0x5342u);
+  const uint32_t s01 = prmt(sgn, 0x43434343u, 0x5140u), s23 = prmt(sgn, 0x43434343u, 0x5342u);
+  const __nv_bfloat162 d01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v01),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&s01));
+  const __nv_bfloat162 d23 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v23),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&s23));
+  lo = *reinterpret_cast<const uint32_t*>(&d01);
+  hi = *reinterpret_cast<const uint32_t*>(&d23);
+}
+
 // Four signed int8 codes -> f16x2 holding (q + 1152) for bytes (0,1) and (2,3), exactly:
 // one xor and two byte permutes; the constant 1152 is removed after the dot product as
 // 1152 * sum(x) (see the biased-code GEMV path).
@@ -51,6 +68,15 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
                                         uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));

@@ -22,15 +22,6 @@ constexpr int GM_W_STAGE = GM_BN * GM_BK;      // int8 bytes
 constexpr int GM_X_STAGE = GM_BM * GM_BK * 2;  // bf16 bytes
 constexpr int GM_SMEM = GM_STAGES * (GM_W_STAGE + GM_X_STAGE);
 
-__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
   const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
   const int bytes = valid ? 16 : 0;

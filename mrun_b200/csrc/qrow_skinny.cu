@@ -57,29 +57,6 @@ __host__ inline size_t sk_smem_bytes(int blocks) {
   return xs > part ? xs : part;
 }
 
-// four int8 codes -> two bf16 pairs, exactly: (q0, q1) and (q2, q3)
-__device__ __forceinline__ void sk_i8x4_to_bf16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t mag = w & 0x7F7F7F7Fu;  // q & 127 (= q + 128 for negative q)
-  const uint32_t sgn = w & 0x80808080u;  // 0x80 where q < 0
-  // bytes [b, 0x43] form the bf16 128 + b; the subtrahend is 128 (0x4300) or 256 (0x4380)
-  const uint32_t v01 = __byte_perm(mag, 0x43434343u, 0x5140u), v23 = __byte_perm(mag, 0x43434343u, 0x5342u);
-  const uint32_t s01 = __byte_perm(sgn, 0x43434343u, 0x5140u), s23 = __byte_perm(sgn, 0x43434343u, 0x5342u);
-  const __nv_bfloat162 d01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v01),
-                                     *reinterpret_cast<const __nv_bfloat162*>(&s01));
-  const __nv_bfloat162 d23 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v23),
-                                     *reinterpret_cast<const __nv_bfloat162*>(&s23));
-  lo = *reinterpret_cast<const uint32_t*>(&d01);
-  hi = *reinterpret_cast<const uint32_t*>(&d23);
-}
-
-__device__ __forceinline__ void sk_mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                       uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 __global__ void __launch_bounds__(SK_THREADS, 2) qrow_skinny_kernel(const __grid_constant__ SkinnyArgs a) {
   extern __shared__ __align__(16) unsigned char sk_smem[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sk_smem);
@@ -146,12 +123,12 @@ __global__ void __launch_bounds__(SK_THREADS, 2) qrow_skinny_kernel(const __grid
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           uint32_t a0, a2, a1, a3;
-          sk_i8x4_to_bf16x2(wr0[ks], a0, a2);
-          sk_i8x4_to_bf16x2(wr1[ks], a1, a3);
+          i8x4_to_bf16x2_exact(wr0[ks], a0, a2);
+          i8x4_to_bf16x2_exact(wr1[ks], a1, a3);
 #pragma unroll
           for (int nt = 0; nt < 4; ++nt) {
             const uint32_t* xw = reinterpret_cast<const uint32_t*>(&xv[nt][ks >> 1]);
-            sk_mma(acc[nt], a0, a1, a2, a3, xw[(ks & 1) * 2], xw[(ks & 1) * 2 + 1]);
+            mma_bf16(acc[nt], a0, a1, a2, a3, xw[(ks & 1) * 2], xw[(ks & 1) * 2 + 1]);
           }
         }
       }
