@@ -1,6 +1,7 @@
-"""ctypes binding of the in-tree CUDA library ``libmrun_b200.so`` (the C ABI boundary).
+"""ctypes binding of the in-tree CUDA library ``libmrun_b200.so`` (the C ABI boundary), and the
+loader of its PyTorch operator library ``libmrun_b200_torch.so`` (``torch.ops.mrun_b200``).
 
-Loading is strict: if the library is missing or lacks a declared symbol, importing any
+Loading is strict: if a library is missing or lacks a declared symbol, importing any
 operator raises instead of falling back to another implementation. Status codes follow
 ``include/mrun_b200.h``: argument errors raise ``ValueError`` (the reference's validation
 errors), CUDA and unsupported-shape errors raise ``RuntimeError``.
@@ -15,6 +16,9 @@ from pathlib import Path
 import torch
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "libmrun_b200.so"
+OPS_LIBRARY_PATH = Path(__file__).resolve().parent / "libmrun_b200_torch.so"
+OPS = ("qrow_linear", "qrow_swiglu", "quant_row_int8", "router_topk", "route_compile", "stable_route_reduce",
+       "grouped_expert_mlp")
 
 MRB_OK = 0
 MRB_ERR_ARG = 1
@@ -124,6 +128,28 @@ def load() -> ctypes.CDLL:
             fn.restype = _RESTYPES.get(name, c_int)
         _lib = lib
         return lib
+
+
+_ops = None
+
+
+def ops():
+    """``torch.ops.mrun_b200``: the operator library over the C ABI (csrc/torch_ops.cpp), loaded
+    once after the C library; raises if it is absent or lacks an operator."""
+    global _ops
+    if _ops is not None:
+        return _ops
+    load()
+    with _lock:
+        if _ops is None:
+            if not OPS_LIBRARY_PATH.exists():
+                raise ImportError(f"mrun_b200 operator library not built: {OPS_LIBRARY_PATH} is missing")
+            torch.ops.load_library(str(OPS_LIBRARY_PATH))
+            namespace = torch.ops.mrun_b200
+            for name in OPS:
+                getattr(namespace, name)  # AttributeError if an operator is not registered
+            _ops = namespace
+    return _ops
 
 
 def check(status: int, what: str) -> None:

@@ -103,6 +103,15 @@ def _gemv_workspace(device: torch.device, out_features: int, workspace: torch.Te
     return workspace.data_ptr(), workspace.numel()
 
 
+def _gemv_workspace_tensor(device: torch.device, out_features: int, workspace: torch.Tensor | None):
+    """The workspace tensor for one GEMV call: the caller's (checked), else this stream's."""
+    if workspace is None:
+        return _GEMV_SCRATCH.get(device, qrow_workspace_bytes(device, out_features))
+    if workspace.device != device or workspace.dtype != torch.uint8 or not workspace.is_contiguous():
+        raise ValueError("workspace must be a contiguous uint8 tensor on the activations' device")
+    return workspace
+
+
 def qrow_linear(
     codes: torch.Tensor,
     scales: torch.Tensor,
@@ -128,24 +137,9 @@ def qrow_linear(
         raise ValueError("out must be a contiguous [rows, out_features] tensor in the activation dtype")
     if bias is not None and (bias.dtype != torch.float32 or bias.numel() != out_features):
         raise ValueError("bias must be fp32 [out_features]")
-    code = _lib.dtype_code(flat.dtype)
-    ws_ptr, ws_bytes = _gemv_workspace(device, out_features, workspace) if rows <= 32 else (None, 0)
-    _lib.call(
-        "mrb_qrow_matmul",
-        flat.data_ptr(),
-        code,
-        rows,
-        in_features,
-        codes.data_ptr(),
-        scales.data_ptr(),
-        out_features,
-        _lib.ptr(bias),
-        out.data_ptr(),
-        code,
-        ws_ptr,
-        ws_bytes,
-        _lib.stream_handle(device),
-    )
+    _lib.dtype_code(flat.dtype)  # ValueError for an unsupported activation dtype
+    ws = _gemv_workspace_tensor(device, out_features, workspace) if rows <= 32 else None
+    _lib.ops().qrow_linear(flat, codes, scales, bias, out, ws)
     return out.reshape(*activations.shape[:-1], out_features)
 
 
@@ -216,22 +210,8 @@ def qrow_swiglu(
     rows = int(flat.shape[0])
     if out is None:
         out = torch.empty((rows, out_features), device=device, dtype=torch.bfloat16)
-    ws_ptr, ws_bytes = _gemv_workspace(device, out_features, workspace) if rows <= 32 else (None, 0)
-    _lib.call(
-        "mrb_qrow_swiglu",
-        flat.data_ptr(),
-        rows,
-        in_features,
-        gate_codes.data_ptr(),
-        gate_scales.data_ptr(),
-        up_codes.data_ptr(),
-        up_scales.data_ptr(),
-        out_features,
-        out.data_ptr(),
-        ws_ptr,
-        ws_bytes,
-        _lib.stream_handle(device),
-    )
+    ws = _gemv_workspace_tensor(device, out_features, workspace) if rows <= 32 else None
+    _lib.ops().qrow_swiglu(flat, gate_codes, gate_scales, up_codes, up_scales, out, ws)
     return out.reshape(*activations.shape[:-1], out_features)
 
 

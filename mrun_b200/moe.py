@@ -150,8 +150,7 @@ def router_topk(logits: torch.Tensor, k: int, *, renorm: bool = True) -> tuple[t
     idx = torch.empty((t, k), dtype=torch.int64, device=device)
     w32 = torch.empty((t, k), dtype=torch.float32, device=device)
     w16 = torch.empty((t, k), dtype=torch.bfloat16, device=device)
-    _lib.call("mrb_router_topk", lg.data_ptr(), _lib.dtype_code(lg.dtype), t, e, int(k), int(bool(renorm)),
-              idx.data_ptr(), w32.data_ptr(), w16.data_ptr(), _lib.stream_handle(device))
+    _lib.ops().router_topk(lg, int(k), bool(renorm), idx, w32, w16)
     return idx, w16, w32
 
 
@@ -207,9 +206,7 @@ def _grouped_route_tensors_impl(top_indices, top_weights, *, num_experts, includ
     token_ids = torch.empty(a, dtype=torch.int64, device=device)
     coefficients = torch.empty(a, dtype=torch.float32, device=device)
     inverse = torch.empty(a, dtype=torch.int64, device=device)
-    _lib.call("mrb_route_compile", idx.data_ptr(), w.data_ptr(), rows, top_k, int(num_experts), counts.data_ptr(),
-              starts.data_ptr(), token_ids.data_ptr(), coefficients.data_ptr(), inverse.data_ptr(), None,
-              _lib.stream_handle(device))
+    _lib.ops().route_compile(idx, w, int(num_experts), counts, starts, token_ids, coefficients, inverse)
     if top_weights.dtype != torch.float32:
         coefficients = coefficients.to(top_weights.dtype)
     return token_ids, coefficients, starts, counts, (inverse if include_inverse else None), time.perf_counter() - started
@@ -267,9 +264,8 @@ def stable_route_reduce(
     eo = eo.contiguous()
     hidden = int(eo.shape[1])
     out = torch.empty((rows, hidden), dtype=torch.float32, device=device)
-    _lib.call("mrb_stable_route_reduce", eo.data_ptr(), coefficients.float().contiguous().data_ptr(),
-              inverse.to(torch.int64).contiguous().data_ptr(), rows, top_k, hidden, out.data_ptr(), _lib.ptr(out_bf16),
-              _lib.stream_handle(device))
+    _lib.ops().stable_route_reduce(eo, coefficients.float().contiguous(), inverse.to(torch.int64).contiguous(), rows,
+                                   top_k, out, out_bf16)
     return out
 
 
@@ -313,10 +309,9 @@ def grouped_expert_mlp(
         sync = expert_mlp_sync(e, device)
     elif sync.dtype != torch.int32 or sync.numel() < 2 * e + 1:
         raise ValueError(f"the expert MLP sync buffer is int32 [2 * experts + 1] = [{2 * e + 1}]")
-    _lib.call("mrb_grouped_expert_mlp", src.data_ptr(), token_ids.data_ptr(), starts.data_ptr(), counts.data_ptr(), e,
-              base, stride, ly.gate_up_codes_offset, ly.gate_up_scales_offset, ly.down_codes_offset,
-              ly.down_scales_offset, _lib.ptr(slot_of), h, f, a, act.data_ptr(), y.data_ptr(), sync.data_ptr(),
-              stream)
+    _lib.ops().grouped_expert_mlp(src, token_ids, starts, counts, pages, stride, ly.gate_up_codes_offset,
+                                  ly.gate_up_scales_offset, ly.down_codes_offset, ly.down_scales_offset, slot_of, act,
+                                  y, sync)
     return y
 
 
@@ -391,9 +386,8 @@ class PagedInt8ExpertBackend:
         expert_output = grouped_expert_mlp(source, token_ids, starts, counts, pages, self.cache.layout,
                                            slot_of=slot_of, sync=self._sync_for(self.num_experts, source.device))
         out = torch.empty((source.shape[0], source.shape[1]), dtype=torch.bfloat16, device=source.device)
-        _lib.call("mrb_stable_route_reduce", expert_output.data_ptr(), coefficients.data_ptr(), inverse.data_ptr(),
-                  int(top_indices.shape[0]), int(top_indices.shape[1]), int(source.shape[1]), None, out.data_ptr(),
-                  _lib.stream_handle(source.device))
+        _lib.ops().stable_route_reduce(expert_output, coefficients, inverse, int(top_indices.shape[0]),
+                                       int(top_indices.shape[1]), None, out)
         release = getattr(self.cache, "release_layer", None)
         if release is not None:  # streamed pages: slots may be reused after these kernels
             release()

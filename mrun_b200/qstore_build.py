@@ -22,8 +22,7 @@ def quant_row_int8(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     rows, cols = (int(v) for v in w.shape)
     codes = torch.empty((rows, cols), device=device, dtype=torch.int8)
     scales = torch.empty((rows,), device=device, dtype=torch.float32)
-    _lib.call("mrb_quant_row_int8", w.data_ptr(), rows, cols, codes.data_ptr(), scales.data_ptr(),
-              _lib.stream_handle(device))
+    _lib.ops().quant_row_int8(w, codes, scales)
     return codes, scales
 
 

@@ -97,3 +97,22 @@ def test_new_attention_entry_points_validate_on_the_host():
     assert fused(q=None) == _lib.MRB_ERR_ARG
     assert fused(k=P + 2) == _lib.MRB_ERR_ARG
     assert fused(rows=0) == _lib.MRB_OK
+
+
+def test_torch_operator_library_registers_every_op():
+    """libmrun_b200_torch.so loads without a GPU and registers torch.ops.mrun_b200.* with
+    caller-allocated outputs (mutable `Tensor(a!)` arguments, no return values)."""
+    import torch
+
+    from mrun_b200 import _lib
+
+    ops = _lib.ops()
+    for name in _lib.OPS:
+        schema = getattr(ops, name).default._schema
+        assert schema.name == f"mrun_b200::{name}"
+        assert len(schema.returns) == 0
+        assert any(a.alias_info is not None and a.alias_info.is_write for a in schema.arguments), name
+    # every operator has a CUDA kernel registered and nothing else (no CPU path)
+    for name in _lib.OPS:
+        assert torch._C._dispatch_has_kernel_for_dispatch_key(f"mrun_b200::{name}", "CUDA"), name
+        assert not torch._C._dispatch_has_kernel_for_dispatch_key(f"mrun_b200::{name}", "CPU"), name
