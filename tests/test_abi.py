@@ -112,6 +112,11 @@ def test_torch_operator_library_registers_every_op():
         assert schema.name == f"mrun_b200::{name}"
         assert len(schema.returns) == 0
         assert any(a.alias_info is not None and a.alias_info.is_write for a in schema.arguments), name
+    # the built library carries the schemas the Python mirror calls with
+    args = {name: [a.name for a in getattr(ops, name).default._schema.arguments] for name in _lib.OPS}
+    assert args["stable_route_reduce"] == ["expert_out", "coef", "inverse", "tokens", "k", "out_f32", "out_bf16"]
+    assert args["qrow_linear"] == ["x", "codes", "scales", "bias", "out", "workspace"]
+    assert args["grouped_expert_mlp"][-4:] == ["slot_of", "act", "y", "sync"]
     # every operator has a CUDA kernel registered and nothing else (no CPU path)
     for name in _lib.OPS:
         assert torch._C._dispatch_has_kernel_for_dispatch_key(f"mrun_b200::{name}", "CUDA"), name
