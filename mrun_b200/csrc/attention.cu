@@ -2153,6 +2153,17 @@ __global__ void __launch_bounds__(AM_MAX_WARPS * 32) rope_append_attention_mma_k
 // runs the fp32 online softmax per token row and accumulates O += P V (P rounded to bf16 as
 // the A operand, V through ldmatrix.trans). The K/V prefix is read once per (query block,
 // KV head) instead of once per token. Deterministic (no atomics, fixed order).
+//
+// The (query block, KV head) pair is a thread-block cluster of a.cluster CTAs (up to
+// PF_MAX_CLUSTER, and only while the pairs still fit one resident wave): rank r takes a
+// contiguous share of the block's causal key tiles, so the longest serial walk is
+// ceil(tiles / cluster) tiles instead of all of them. Query blocks are laid out last block
+// first, so the longest walks start first when the grid takes several waves. Each warp then
+// leaves its online-softmax state (running max and sum per token row, the unnormalised O
+// fragments) in its CTA's shared memory, and rank 0 merges the ranks' states in rank order
+// through distributed shared memory and writes the output.
+constexpr int PF_MAX_CLUSTER = 2;
+constexpr int PF_MERGE_WORDS = 64 + 4;  // per lane: 16 x 4 O fragments, max and sum of rows g, g + 8
 constexpr int PF_STAGES = 3;
 constexpr int PF_ROW = 128 + 8;                    // padded smem row (bf16)
 constexpr int PF_TILE_ELEMS = AT_TILE * PF_ROW;    // one K or V tile
@@ -2170,12 +2181,19 @@ struct PrefillArgs {
   int32_t* error_flag;
   float scale;
   __nv_bfloat16* out;  // [n, hq, 128]
+  int cluster;         // CTAs per (query block, KV head); gridDim.x = query blocks x cluster
 };
+
+__host__ __device__ inline size_t pf_smem_bytes(int group) {
+  return PF_SMEM + (size_t)group * 32 * PF_MERGE_WORDS * sizeof(float);
+}
 
 __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_prefill_attention_kernel(PrefillArgs a) {
   constexpr int D = 128, CH = D / 8;
   const int group = blockDim.x >> 5;
-  const int64_t q0 = (int64_t)blockIdx.x * AT_TILE;  // first token of the block
+  const int rank = (int)(blockIdx.x % (unsigned)a.cluster);  // = %cluster_ctarank
+  const int64_t nblk = (a.n + AT_TILE - 1) / AT_TILE;
+  const int64_t q0 = (nblk - 1 - (int64_t)(blockIdx.x / (unsigned)a.cluster)) * AT_TILE;  // first token of the block
   const int kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -2188,11 +2206,13 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_prefill_attention_ker
   const int64_t ntok = min((int64_t)AT_TILE, a.n - q0);         // tokens of this block
   const int64_t last_pos = a.start + q0 + ntok - 1;              // the block's highest position
   const int ntile = (int)(last_pos / AT_TILE) + 1;               // key tiles [0, last_pos]
+  const int share = (ntile + a.cluster - 1) / a.cluster;         // this rank: tiles [tb, te)
+  const int tb = min(ntile, rank * share), te = min(ntile, tb + share);
   const int64_t khead = (int64_t)kvh * a.stride_head;
   bool bad_page = false;
 
   auto issue = [&](int i) {
-    if (i < ntile) {
+    if (i < te) {
       __nv_bfloat16* kst = ring + (i % PF_STAGES) * PF_STAGE_ELEMS;
       __nv_bfloat16* vst = kst + PF_TILE_ELEMS;
       const int64_t t0 = (int64_t)i * AT_TILE;
@@ -2213,7 +2233,7 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_prefill_attention_ker
     cp_async_commit_group();
   };
 #pragma unroll
-  for (int i = 0; i < PF_STAGES - 1; ++i) issue(i);
+  for (int i = 0; i < PF_STAGES - 1; ++i) issue(tb + i);
 
   // Q of this warp's head for the block's tokens (rows g and g + 8; zero past the block)
   uint32_t qa[D / 16][4];
@@ -2236,7 +2256,7 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_prefill_attention_ker
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 
-  for (int i = 0; i < ntile; ++i) {
+  for (int i = tb; i < te; ++i) {
     cp_async_wait_group<PF_STAGES - 2>();
     __syncthreads();  // tile i is staged; every warp is done with tile i - 1
     issue(i + PF_STAGES - 1);
@@ -2306,6 +2326,50 @@ __global__ void __launch_bounds__(AT_MAX_GROUP * 32) paged_prefill_attention_ker
   }
   cp_async_wait_group<0>();
   if (bad_page && a.error_flag) atomicExch(a.error_flag, 1);
+  if (a.cluster > 1) {
+    // this rank's state, lane-major (conflict-free), then rank 0 folds the ranks in order
+    float* mine = reinterpret_cast<float*>(pf_smem + PF_SMEM) + (size_t)warp * 32 * PF_MERGE_WORDS;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mine[(dt * 4 + e) * 32 + lane] = o[dt][e];
+    mine[64 * 32 + lane] = mrow[0];
+    mine[65 * 32 + lane] = mrow[1];
+    mine[66 * 32 + lane] = lrow[0];
+    mine[67 * 32 + lane] = lrow[1];
+    cluster_sync_all();
+    if (rank == 0) {
+      const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(mine));
+      float M[2] = {-INFINITY, -INFINITY};
+      for (int r = 0; r < a.cluster; ++r) {
+        const uint32_t ra = mapa_shared(base, (unsigned)r);
+        M[0] = fmaxf(M[0], ld_shared_cluster_f32(ra + (64 * 32 + lane) * 4));
+        M[1] = fmaxf(M[1], ld_shared_cluster_f32(ra + (65 * 32 + lane) * 4));
+      }
+      float L[2] = {0.f, 0.f};
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
+      for (int r = 0; r < a.cluster; ++r) {
+        const uint32_t ra = mapa_shared(base, (unsigned)r);
+        float w[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float m_r = ld_shared_cluster_f32(ra + ((64 + h) * 32 + lane) * 4);
+          w[h] = m_r == -INFINITY ? 0.f : expf(m_r - M[h]);
+          L[h] = fmaf(ld_shared_cluster_f32(ra + ((66 + h) * 32 + lane) * 4), w[h], L[h]);
+        }
+#pragma unroll
+        for (int dt = 0; dt < D / 8; ++dt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            o[dt][e] = fmaf(ld_shared_cluster_f32(ra + ((dt * 4 + e) * 32 + lane) * 4), w[e >> 1], o[dt][e]);
+      }
+      lrow[0] = L[0];
+      lrow[1] = L[1];
+    }
+    cluster_sync_all();  // the peers' shared memory stays alive until rank 0 has read it
+    if (rank != 0) return;
+  }
   // O / l for rows g and g + 8 of the block
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -2574,16 +2638,43 @@ extern "C" int mrb_paged_prefill_attention(const void* q, int64_t n, int64_t hq,
   if (!aligned(q, 16) || !aligned(out, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || (stride_page % 8) ||
       (stride_head % 8) || (stride_tok % 8))
     return fail(MRB_ERR_ARG, "paged_prefill_attention: q/out and K/V rows must be 16-byte aligned");
-  if ((n + AT_TILE - 1) / AT_TILE > 0x7fffffffLL || hkv > 65535)
+  if ((n + AT_TILE - 1) / AT_TILE * PF_MAX_CLUSTER > 0x7fffffffLL || hkv > 65535)
     return fail(MRB_ERR_UNSUPPORTED, "paged_prefill_attention: grid too large");
-  const int smem_st =
-      ensure_dynamic_smem((const void*)paged_prefill_attention_kernel, PF_SMEM, "paged_prefill_attention");
+  // CTAs per (query block, KV head): PF_MAX_CLUSTER when the longest causal walk has 8 key
+  // tiles or more and the clusters fit one resident wave (two CTAs per SM), else 1 -- a
+  // second wave costs more than the shorter walk saves (measured at a 512-token prompt:
+  // 2 CTAs 40 us, 4 CTAs 49 us, 8 CTAs 93 us, 1 CTA 59 us)
+  const int group = (int)(hq / hkv);
+  const int64_t tiles = (start + n + AT_TILE - 1) / AT_TILE;
+  const int64_t pairs = ((n + AT_TILE - 1) / AT_TILE) * hkv;
+  const int cluster = tiles >= 8 && pairs * PF_MAX_CLUSTER <= 2 * (int64_t)num_sms() ? PF_MAX_CLUSTER : 1;
+  const size_t smem = pf_smem_bytes(group);
+  const int smem_st = ensure_dynamic_smem((const void*)paged_prefill_attention_kernel, smem, "paged_prefill_attention");
   if (smem_st) return smem_st;
   PrefillArgs a{(const __nv_bfloat16*)q, n, hq, hkv, start, (const __nv_bfloat16*)k_cache,
                 (const __nv_bfloat16*)v_cache, stride_page, stride_head, stride_tok, page_size, block_table,
-                num_pages, error_flag, scale, (__nv_bfloat16*)out};
-  launch_kernel(paged_prefill_attention_kernel, dim3((unsigned)((n + AT_TILE - 1) / AT_TILE), (unsigned)hkv),
-                dim3((unsigned)(32 * (hq / hkv))), PF_SMEM, (cudaStream_t)stream, true, a);
+                num_pages, error_flag, scale, (__nv_bfloat16*)out, cluster};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(((n + AT_TILE - 1) / AT_TILE) * cluster), (unsigned)hkv);
+  cfg.blockDim = dim3((unsigned)(32 * group));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = (unsigned)cluster;
+  attr[na].val.clusterDim.y = 1;
+  attr[na].val.clusterDim.z = 1;
+  ++na;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, paged_prefill_attention_kernel, a);
+  if (e != cudaSuccess) return fail(MRB_ERR_CUDA, "paged_prefill_attention: launch: %s", cudaGetErrorString(e));
   return launch_status("paged_prefill_attention");
 }
 
