@@ -1254,6 +1254,58 @@ def run_expert_case(args) -> None:
                       "launches": 2 * args.steps}), flush=True)
 
 
+def run_expert_prefill_case(args) -> None:
+    """One MoE layer of a Mixtral-8x7B-shape prefill (H 4096, F 14336, 8 int8 experts top-2,
+    2,048 tokens: ~512 rows per expert): the grouped mma.sync kernel (16-row passes, each
+    re-streaming the expert's 176 MB page) against the same layer with every expert on the
+    tcgen05 W8A16 GEMMs (``expert_mlp_large_counts``). Both timed eagerly with CUDA events
+    over the same routes (the GEMM path reads the counts on the host each call); reports
+    ms per layer and TFLOP/s of the expert matmuls; not the bench metric."""
+    import torch
+
+    from mrun_b200.moe import (ExpertPageLayout, expert_mlp_large_counts, expert_mlp_sync, grouped_expert_mlp,
+                               grouped_route_tensors_with_inverse, router_topk)
+
+    experts, tokens, k, h, f = 8, 2048, 2, 4096, 14336
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device).manual_seed(0)
+    ly = ExpertPageLayout.create(h, f)
+    pages = torch.randint(-127, 128, (experts, ly.page_stride), dtype=torch.int8, device=device,
+                          generator=gen).view(torch.uint8)
+    pages[:, ly.gate_up_scales_offset:ly.gate_up_scales_offset + ly.gate_up_scales_bytes].copy_(
+        torch.full((experts, 2 * f), 2e-4, device=device).view(torch.uint8))
+    pages[:, ly.down_scales_offset:ly.down_scales_offset + ly.down_scales_bytes].copy_(
+        torch.full((experts, h), 2e-4, device=device).view(torch.uint8))
+    x = (torch.randn(tokens, h, device=device, generator=gen) * 0.5).to(torch.bfloat16)
+    idx, w16, _ = router_topk(torch.randn(tokens, experts, device=device, generator=gen), k)
+    token_ids, _, starts, counts, _, _ = grouped_route_tensors_with_inverse(idx, w16, num_experts=experts)
+    sync = expert_mlp_sync(experts, device)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / args.steps
+
+    grouped_ms = timed(lambda: grouped_expert_mlp(x, token_ids, starts, counts, pages, ly, sync=sync))
+    gemm_ms = timed(lambda: expert_mlp_large_counts(x, token_ids, starts, counts, pages, ly, sync=sync, min_rows=1))
+    ref = grouped_expert_mlp(x, token_ids, starts, counts, pages, ly, sync=sync).float()
+    got = expert_mlp_large_counts(x, token_ids, starts, counts, pages, ly, sync=sync, min_rows=1).float()
+    rel = float((got - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+    flops = 2.0 * tokens * k * 3 * h * f
+    print(json.dumps({"case": args.case, "rows_per_expert": counts.tolist(), "grouped_ms": grouped_ms,
+                      "gemm_ms": gemm_ms, "grouped_tflops": flops / grouped_ms / 1e9,
+                      "gemm_tflops": flops / gemm_ms / 1e9, "speedup": grouped_ms / gemm_ms,
+                      "max_rel_diff": rel}), flush=True)
+
+
 BATCH_SEQS = 64
 BATCH_NEW_TOKENS = 128
 
@@ -1485,7 +1537,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", choices=["moe", "decode", "moe-decode", "stream-decode", "w8a8-batch", *GEMV_CASES,
                                        *TC_CASES, *ATTN_CASES, "attn-fused1", "attn-prefill512", "qstore-ingest",
-                                       *EXPERT_CASES],
+                                       *EXPERT_CASES, "experts-prefill-mixtral"],
                     default="moe",
                     help="moe (default): the config-4 expert-parallel decode line; decode: the dense batch-1 line; "
                          "the rest are single-kernel or single-configuration cases (not the metric)")
@@ -1502,7 +1554,8 @@ def main() -> None:
         return
     cases = {"attn-fused1": run_fused_attn_case, "attn-prefill512": run_prefill_attn_case,
              "qstore-ingest": run_qstore_ingest_case, "moe-decode": run_moe_case, "stream-decode": run_stream_case,
-             "w8a8-batch": run_batch_case, "moe": run_moe_bench, "decode": run_ours}
+             "w8a8-batch": run_batch_case, "moe": run_moe_bench, "decode": run_ours,
+             "experts-prefill-mixtral": run_expert_prefill_case}
     if args.case in GEMV_CASES:
         run_gemv_case(args)
     elif args.case in ATTN_CASES:

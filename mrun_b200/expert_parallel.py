@@ -291,9 +291,18 @@ class P2PExpertParallelMoE:
             pages, slot_of = self.page_cache.layer_pages(self.layer, self._local_ids)
         else:
             pages, slot_of = self.pages, None
-        eo = _grouped_mlp_from_pointer(self._own + self.offsets[4], self.rt_token_ids, self.rt_starts,
-                                       self.rt_counts, pages, self.layout, hidden, device, self.mlp_sync,
-                                       rows=slots, slot_of=slot_of)
+        if self.pages is None:
+            # a streamed layer runs eagerly: experts that received many rows (a large batch
+            # over few experts per rank) go to the tensor-core GEMMs
+            from .moe import expert_mlp_large_counts
+
+            received = _device_rows(self._own + self.offsets[4], slots, hidden, device)
+            eo = expert_mlp_large_counts(received, self.rt_token_ids, self.rt_starts, self.rt_counts, pages,
+                                         self.layout, slot_of=slot_of, sync=self.mlp_sync)
+        else:
+            eo = _grouped_mlp_from_pointer(self._own + self.offsets[4], self.rt_token_ids, self.rt_starts,
+                                           self.rt_counts, pages, self.layout, hidden, device, self.mlp_sync,
+                                           rows=slots, slot_of=slot_of)
         if self.pages is None:
             self.page_cache.release_layer()  # its slots may be refilled once these kernels are done
         _lib.call("mrb_ep_p2p_return", eo.data_ptr(), self.rt_inverse.data_ptr(), hidden, world, sh.rank, cap,
@@ -320,6 +329,19 @@ class P2PExpertParallelMoE:
         if self._own:
             _lib.call("mrb_ep_mailbox_close", self._own, 1)
             self._own = 0
+
+
+class _RowsInterface:
+    """``__cuda_array_interface__`` of bf16 rows at a raw device address (read as int16)."""
+
+    def __init__(self, ptr: int, rows: int, hidden: int) -> None:
+        self.__cuda_array_interface__ = {"shape": (int(rows), int(hidden)), "typestr": "<i2",
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+def _device_rows(ptr: int, rows: int, hidden: int, device) -> torch.Tensor:
+    """A bf16 [rows, hidden] tensor viewing this rank's memory at ``ptr`` (no copy)."""
+    return torch.as_tensor(_RowsInterface(ptr, rows, hidden), device=device).view(torch.bfloat16)
 
 
 def _grouped_mlp_from_pointer(rows_ptr: int, token_ids, starts, counts, pages, layout, hidden: int, device,

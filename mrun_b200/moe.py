@@ -315,6 +315,69 @@ def grouped_expert_mlp(
     return y
 
 
+#: Routed rows from which an expert's MLP runs on the tensor-core GEMMs instead of the grouped
+#: kernel, whose 16-row passes re-stream the expert's page once per pass.
+LARGE_EXPERT_ROWS = 64
+
+
+def expert_page_matrices(pages: torch.Tensor, layout: ExpertPageLayout, slot: int):
+    """(gate codes, gate scales, up codes, up scales, down codes, down scales) views of the
+    expert page in slot ``slot`` of ``pages`` (uint8 ``[slots, page_stride]``)."""
+    ly = layout
+    f, h = ly.intermediate_size, ly.hidden_size
+    page = pages[int(slot)]
+    gu = page[ly.gate_up_codes_offset: ly.gate_up_codes_offset + ly.gate_up_codes_bytes].view(torch.int8).view(2 * f, h)
+    gus = page[ly.gate_up_scales_offset: ly.gate_up_scales_offset + ly.gate_up_scales_bytes].view(torch.float32)
+    dn = page[ly.down_codes_offset: ly.down_codes_offset + ly.down_codes_bytes].view(torch.int8).view(h, f)
+    dns = page[ly.down_scales_offset: ly.down_scales_offset + ly.down_scales_bytes].view(torch.float32)
+    return gu[:f], gus[:f], gu[f:], gus[f:], dn, dns
+
+
+def expert_mlp_large_counts(
+    source: torch.Tensor,
+    token_ids: torch.Tensor,
+    starts: torch.Tensor,
+    counts: torch.Tensor,
+    pages: torch.Tensor,
+    layout: ExpertPageLayout,
+    *,
+    slot_of: torch.Tensor | None = None,
+    sync: torch.Tensor | None = None,
+    min_rows: int = LARGE_EXPERT_ROWS,
+) -> torch.Tensor:
+    """``grouped_expert_mlp`` with every expert that received ``min_rows`` rows or more moved
+    to the tcgen05 W8A16 GEMMs: its rows are gathered, the paired gate/up GEMM applies the
+    SwiGLU boundaries (``qrow_swiglu``) and the down GEMM (``qrow_linear``) writes straight
+    into the expert's rows of the route-ordered output; the other experts run on the grouped
+    kernel. Prefill-sized groups (hundreds of rows per expert) thus read each page once
+    instead of once per 16 rows. Reads the counts on the host (one synchronisation), so it
+    serves eager calls -- prefill and host-planned streamed decode -- not captured steps.
+    Each output row agrees with the grouped kernel's within the bf16 tolerance (the two sum
+    the same exact products in a different order)."""
+    from .dense_qstore_cuda import qrow_linear, qrow_swiglu
+
+    device = _lib.require_cuda(source, token_ids, starts, counts, pages, what="expert MLP")
+    counts_h = counts.cpu().tolist()
+    big = [e for e, c in enumerate(counts_h) if c >= min_rows]
+    small = counts
+    if big:
+        small = counts.clone()
+        small[torch.tensor(big, dtype=torch.int64, device=device)] = 0
+    y = grouped_expert_mlp(source, token_ids, starts, small, pages, layout, slot_of=slot_of, sync=sync)
+    if big:
+        starts_h = starts.cpu().tolist()
+        slots_h = slot_of.cpu().tolist() if slot_of is not None else None
+        src = source.reshape(-1, layout.hidden_size)
+        for e in big:
+            s, c = starts_h[e], counts_h[e]
+            gate, gate_s, up, up_s, down, down_s = expert_page_matrices(
+                pages, layout, slots_h[e] if slots_h is not None else e)
+            rows = src.index_select(0, token_ids[s:s + c])
+            act = qrow_swiglu(gate, gate_s, up, up_s, rows)
+            qrow_linear(down, down_s, act, out=y[s:s + c])
+    return y
+
+
 def expert_mlp_sync(experts: int, device: torch.device) -> torch.Tensor:
     """A zeroed sync buffer for ``grouped_expert_mlp`` over ``experts`` experts."""
     return torch.zeros(2 * int(experts) + 1, dtype=torch.int32, device=device)
@@ -359,6 +422,9 @@ class PagedInt8ExpertBackend:
     dtype: torch.dtype = torch.bfloat16
     num_experts: int = 0
     stats: ExpertBackendStats = field(default_factory=ExpertBackendStats)
+    # experts with this many routed rows or more run on the tensor-core GEMMs in prefill calls
+    # and under a cache that plans its copies on the host (None: always the grouped kernel)
+    large_expert_rows: int | None = LARGE_EXPERT_ROWS
     _sync: dict = field(default_factory=dict, repr=False)
 
     def _sync_for(self, experts: int, device: torch.device) -> torch.Tensor:
@@ -383,8 +449,13 @@ class PagedInt8ExpertBackend:
         pages, slot_of = self.cache.layer_pages(layer, top_indices, prefill=prefill)
         token_ids, coefficients, starts, counts, inverse, _ = grouped_route_tensors_with_inverse(
             top_indices, top_weights.float(), num_experts=self.num_experts)
-        expert_output = grouped_expert_mlp(source, token_ids, starts, counts, pages, self.cache.layout,
-                                           slot_of=slot_of, sync=self._sync_for(self.num_experts, source.device))
+        sync = self._sync_for(self.num_experts, source.device)
+        if self.large_expert_rows is not None and (prefill or getattr(self.cache, "plans_on_host", False)):
+            expert_output = expert_mlp_large_counts(source, token_ids, starts, counts, pages, self.cache.layout,
+                                                    slot_of=slot_of, sync=sync, min_rows=self.large_expert_rows)
+        else:
+            expert_output = grouped_expert_mlp(source, token_ids, starts, counts, pages, self.cache.layout,
+                                               slot_of=slot_of, sync=sync)
         out = torch.empty((source.shape[0], source.shape[1]), dtype=torch.bfloat16, device=source.device)
         _lib.ops().stable_route_reduce(expert_output, coefficients, inverse, int(top_indices.shape[0]),
                                        int(top_indices.shape[1]), None, out)
@@ -407,7 +478,9 @@ __all__ = [
     "PagedInt8ExpertBackend",
     "ResidentInt8ExpertPages",
     "expert_page_views",
+    "expert_mlp_large_counts",
     "expert_mlp_sync",
+    "expert_page_matrices",
     "grouped_expert_mlp",
     "grouped_route_tensors",
     "grouped_route_tensors_with_inverse",

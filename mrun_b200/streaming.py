@@ -232,6 +232,8 @@ class ExpertPageCache:
     (``page_policy.replay``). Options left as None come from the reference's environment
     switches (``page_policy.options_from_env``)."""
 
+    plans_on_host = True  # every acquisition reads its routes on the host (no graph capture)
+
     def __init__(self, host: HostPageTier, *, budget_bytes: int, device: torch.device,
                  cache_policy: str | None = None, prefill_page_policy: str | None = None,
                  route_prefetch: bool | None = None, page_trace: bool | None = None,

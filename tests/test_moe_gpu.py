@@ -176,3 +176,32 @@ def test_overlapped_expert_mlp_matches_separate_launches(tokens, k, experts, hid
         y = grouped_expert_mlp(x, token_ids, starts, counts, pages, ly, sync=sync)
         assert torch.equal(y, ref)
     assert not sync.any()
+
+
+def test_large_expert_counts_on_the_gemms_match_the_grouped_kernel(cuda):
+    """expert_mlp_large_counts: experts with at least 64 routed rows run on the tcgen05 GEMMs
+    (rows within the bf16 tolerance of the grouped kernel's); the others stay on the grouped
+    kernel, bit-identical to it."""
+    from mrun_b200.moe import (expert_mlp_large_counts, expert_mlp_sync, grouped_expert_mlp,
+                               grouped_route_tensors_with_inverse)
+
+    tokens, k, experts, hidden, ffn = 200, 2, 8, 1024, 2048
+    rng = np.random.default_rng(9)
+    ly, pages, _ = _expert_pages(rng, experts, hidden, ffn, cuda)
+    x = torch.from_numpy(bf16_round(rng.standard_normal((tokens, hidden)).astype(np.float32))).to(cuda).to(torch.bfloat16)
+    # skewed routing: experts 0 and 1 take most rows, the rest a few each
+    logits = rng.standard_normal((tokens, experts)).astype(np.float32)
+    logits[:, :2] += 3.0
+    idx = torch.from_numpy(np.argsort(-logits, axis=1)[:, :k].copy()).to(cuda)
+    w = torch.full((tokens, k), 0.5, device=cuda)
+    token_ids, _, starts, counts, _, _ = grouped_route_tensors_with_inverse(idx, w, num_experts=experts)
+    c = counts.cpu().tolist()
+    assert c[0] >= 64 and c[1] >= 64 and min(c[2:]) < 64
+    sync = expert_mlp_sync(experts, cuda)
+    ref = grouped_expert_mlp(x, token_ids, starts, counts, pages, ly, sync=sync)
+    for _ in range(2):
+        got = expert_mlp_large_counts(x, token_ids, starts, counts, pages, ly, sync=sync)
+        big = int(starts[2].item())  # experts 0 and 1 fill rows [0, big)
+        assert max_rel_err(got[:big].float().cpu().numpy(), ref[:big].float().cpu().numpy()) < TOL
+        assert torch.equal(got[big:], ref[big:])
+    assert not sync.any()
