@@ -8,7 +8,10 @@ the ``.moe`` backend (route compiler, grouped int8 expert SwiGLU MLP, fixed-orde
 residual; then the final norm and a greedy head. Every dense projection (qkv, o, router,
 head, embedding) is an int8 qrow matrix; expert weights are int8 qrow pages.
 
-The whole step is captured in a CUDA graph (no host synchronisation inside). With a process
+The whole step is captured in a CUDA graph (no host synchronisation inside) when the expert
+pages are resident in HBM. With the pages in a pinned host tier (``MoeWeights.synthetic(...,
+host_experts=True)``, the Mixtral-shape config 5) they stream through an HBM slot cache whose
+copies are planned on the host from each layer's routes, so that step runs eagerly. With a process
 group of N ranks the experts are sharded (rank r owns experts [r*E/N, (r+1)*E/N)) and each
 layer's MoE runs through ``P2PExpertParallelMoE`` (real rows stored straight into the owners'
 peer-mapped mailboxes over NVLink, epoch flags with bounded waits) or, with
