@@ -104,3 +104,31 @@ def test_full_layer_pages_replay_every_shard():
         assert torch.equal(pages, full.layers[layer].pages)
         for r, sh in enumerate(shards):
             assert torch.equal(pages[2 * r: 2 * r + 2], sh.layers[layer].pages)
+
+
+def test_expert_page_matrices_view_the_packed_parts():
+    """moe.expert_page_matrices: the gate, up and down codes and scales of one slot, as
+    views of the packed page (no copies), in the layout pack_expert_page writes."""
+    import torch
+
+    from mrun_b200.moe import ExpertPageLayout, expert_page_matrices, pack_expert_page
+
+    h, f = 64, 48
+    ly = ExpertPageLayout.create(h, f)
+    g = torch.Generator().manual_seed(3)
+    pages = torch.zeros((3, ly.page_stride), dtype=torch.uint8)
+    parts = []
+    for slot in range(3):
+        gu = torch.randint(-127, 128, (2 * f, h), dtype=torch.int8, generator=g)
+        gus = torch.rand(2 * f, generator=g)
+        dn = torch.randint(-127, 128, (h, f), dtype=torch.int8, generator=g)
+        dns = torch.rand(h, generator=g)
+        pack_expert_page(ly, gu, gus, dn, dns, pages[slot])
+        parts.append((gu, gus, dn, dns))
+    for slot in range(3):
+        gate, gate_s, up, up_s, down, down_s = expert_page_matrices(pages, ly, slot)
+        gu, gus, dn, dns = parts[slot]
+        assert torch.equal(gate, gu[:f]) and torch.equal(up, gu[f:]) and torch.equal(down, dn)
+        assert torch.equal(gate_s, gus[:f]) and torch.equal(up_s, gus[f:]) and torch.equal(down_s, dns)
+        assert gate.is_contiguous() and up.is_contiguous() and down.is_contiguous()
+        assert gate.data_ptr() == pages[slot].data_ptr() + ly.gate_up_codes_offset  # a view
